@@ -1,0 +1,138 @@
+/*
+ * iqk_b200: C ABI of the B200-native IQ_K routed-expert hot path.
+ *
+ * One shared library (mlx_iqk_b200/libiqk_b200.so, built for sm_100a)
+ * exports the entry points below. They take plain device pointers, sizes and
+ * a CUDA stream, return an int status, borrow every pointer and allocate
+ * nothing: outputs and workspaces are the caller's.
+ *
+ * Streams are the reference's k-contiguous relayout, passed as an array of
+ * device pointers in the reference's component order
+ * (src/mlx_iqk/format.py:352-377):
+ *
+ *   IQK_IQ2_KS   {qs u32[E,o,n/16], scl u8[E,o,n/64], sch u8[E,o,n/256],
+ *                 sex u8[E,o,n/256], dv f16[E,o]}
+ *   IQK_IQ2_K    {qs u32[E,o,n/16], scl u8[E,o,n/32], sex u8[E,o,n/128],
+ *                 dv f16[E,o,n/256]}
+ *   IQK_IQ1_S_R4 {qs u32[E,o,n/32], qh u16[E,o,n/32], dv f16[E,o]}
+ *
+ * Every entry point is stream-ordered on the caller's stream and reentrant;
+ * the only library state is a read-only constant table per device.
+ */
+#ifndef IQK_B200_H
+#define IQK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t; NULL is the legacy default stream. */
+typedef struct CUstream_st *iqk_stream_t;
+
+/* Members (src/mlx_iqk/format.py:116 MEMBERS). */
+enum {
+    IQK_IQ2_KS = 0,
+    IQK_IQ2_K = 1,
+    IQK_IQ1_S_R4 = 2
+};
+
+/* Element types of activations and outputs. */
+enum {
+    IQK_F32 = 0,
+    IQK_F16 = 1,
+    IQK_BF16 = 2
+};
+
+/* Status codes. The Python layer maps them onto the reference's exception
+ * classes: IqkFormatError (MEMBER), IqkKernelError (WIDTH, GEOMETRY) and
+ * IqkRuntimeError (the rest) -- src/mlx_iqk/format.py:265,
+ * src/mlx_iqk/kernels.py:86, src/mlx_iqk/nn.py:97. */
+enum {
+    IQK_OK = 0,
+    IQK_ERR_MEMBER = 1,      /* member not one of the three */
+    IQK_ERR_WIDTH = 2,       /* in_features not a sized width (2048, 4096) */
+    IQK_ERR_GEOMETRY = 3,    /* out_features / experts / row range / pairs */
+    IQK_ERR_ARGUMENT = 4,    /* null pointer, bad dtype, negative count */
+    IQK_ERR_ALIGNMENT = 5,   /* a pointer lacks the alignment a kernel needs */
+    IQK_ERR_WORKSPACE = 6,   /* workspace missing or smaller than required */
+    IQK_ERR_CUDA = 7,        /* a CUDA runtime call or launch failed */
+    IQK_ERR_DEVICE = 8       /* current device is not compute capability 10.0 */
+};
+
+/* Bits of the device-side error word (iqk_read_error). */
+enum {
+    IQK_DEVERR_EXPERT = 1,   /* an expert index was outside [0, num_experts) */
+    IQK_DEVERR_TOKEN = 2,    /* a pair's activation row was outside [0, x_rows) */
+    IQK_DEVERR_NONFINITE = 4 /* an activation row held a NaN or infinity */
+};
+
+/* Short description of a status code (static storage). */
+const char *iqk_status_string(int status);
+
+/* ABI version of this header: 1. */
+int iqk_abi_version(void);
+
+/* IQK_OK when the current device is compute capability 10.0 (sm_100a). */
+int iqk_check_device(void);
+
+/*
+ * Bit-exact stacked dequantization of out-rows [row_start, row_start + rows)
+ * of every expert into dst[E, rows, in_features] (row-major), in float32,
+ * float16 or bfloat16 (out_dtype). Every weight is the CPU dequantizer's
+ * float32 chain -- d * float(index) then * value, or
+ * d * float(2*ls + 1) then * (grid + shift) -- rounded to nearest-even once
+ * when out_dtype is 16-bit.
+ *
+ * Replaces the reference's dequant_kernel / dequant_range_kernel
+ * (src/mlx_iqk/kernels.py:631-742, launched at src/mlx_iqk/nn.py:155-201),
+ * which emit float16 only and take a power-of-two range.
+ */
+int iqk_dequant(int member, const void *const *streams, int64_t num_experts,
+                int64_t out_features, int64_t in_features, int64_t row_start,
+                int64_t rows, int out_dtype, void *dst, iqk_stream_t stream);
+
+/*
+ * Workspace bytes iqk_gemv needs for this member, width, activation-row
+ * count and pair count (routing tables plus the prepared activations).
+ */
+size_t iqk_gemv_workspace_bytes(int member, int64_t in_features, int64_t x_rows,
+                                int64_t pairs);
+
+/*
+ * Fused dequant + GEMV over token-expert pairs:
+ *   y[p, r] = sum_k W[sel[p], r, k] * x[tok[p], k]
+ * for p in [0, pairs), r in [0, out_features). x is [x_rows, in_features]
+ * (x_dtype), y is [pairs, out_features] (y_dtype). When tok is NULL the pair's
+ * activation row is p / (pairs / x_rows): top_k for the gate/up seam
+ * ([..., 1, 1, in]) and 1 for the down seam ([..., top_k, 1, in]);
+ * pairs % x_rows must then be 0. Pairs may arrive in any order; each expert's
+ * weights are streamed once for all pairs that selected it. Pairs whose
+ * expert or row index is out of range produce zeros and set the device error
+ * word. The per-element result does not depend on the order or grouping of
+ * pairs, so a sorted call is bit-identical to the unsorted one after
+ * un-permuting.
+ *
+ * Replaces gemv_kernel, gemv_sorted_kernel and gemv_union_kernel
+ * (src/mlx_iqk/kernels.py:332-572, launched at src/mlx_iqk/nn.py:240-333).
+ */
+int iqk_gemv(int member, const void *x, int x_dtype, int64_t x_rows,
+             const void *const *streams, int64_t num_experts, int64_t out_features,
+             int64_t in_features, const int32_t *sel, const int32_t *tok,
+             int64_t pairs, void *y, int y_dtype, void *workspace,
+             size_t workspace_bytes, iqk_stream_t stream);
+
+/*
+ * Copy the device error word a previous iqk_gemv left in its workspace into
+ * *flags (IQK_DEVERR_* bits), synchronising the stream. No reference
+ * counterpart: the reference's kernels read out-of-range indices unchecked.
+ */
+int iqk_read_error(const void *workspace, int32_t *flags, iqk_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IQK_B200_H */

@@ -1,0 +1,137 @@
+// extern "C" entry points of libiqk_b200.so (declared in include/iqk_b200.h).
+//
+// Every entry point validates its geometry and pointers on the host before
+// any launch (the reference fails closed the same way before compiling:
+// src/mlx_iqk/kernels.py:100-128, src/mlx_iqk/nn.py:110-126) and returns a
+// status instead of raising.
+#include <cstdio>
+
+#include "iqk_common.cuh"
+#include "iqk_gemv.cuh"
+
+namespace {
+
+using namespace iqk;
+
+bool member_ok(int m) { return m == IQK_IQ2_KS || m == IQK_IQ2_K || m == IQK_IQ1_S_R4; }
+bool dtype_ok(int d) { return d == IQK_F32 || d == IQK_F16 || d == IQK_BF16; }
+bool width_ok(int64_t n) { return n == 2048 || n == 4096; }
+bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int num_sms_current() {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms > 0 ? sms : 148;
+}
+
+// Stream pointers: present, and 16-byte aligned (the kernels move them with
+// 16-byte copies; the caller's allocator gives 256).
+int check_streams(int member, const void *const *streams) {
+    if (!streams) return IQK_ERR_ARGUMENT;
+    const RowBytes rb = row_bytes(member, 2048);
+    for (int i = 0; i < rb.count; ++i) {
+        if (!streams[i]) return IQK_ERR_ARGUMENT;
+        if (!aligned(streams[i], 16)) return IQK_ERR_ALIGNMENT;
+    }
+    return IQK_OK;
+}
+
+int cuda_status(cudaError_t err) {
+    if (err == cudaSuccess) return IQK_OK;
+    cudaGetLastError();  // clear a sticky launch error for the caller
+    return IQK_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *iqk_status_string(int status) {
+    switch (status) {
+        case IQK_OK: return "ok";
+        case IQK_ERR_MEMBER: return "member is not one of iq2_ks, iq2_k, iq1_s_r4";
+        case IQK_ERR_WIDTH: return "in_features is not a sized width (2048 or 4096)";
+        case IQK_ERR_GEOMETRY: return "geometry rejected (out_features, experts, rows or pairs)";
+        case IQK_ERR_ARGUMENT: return "invalid argument (null pointer, dtype or count)";
+        case IQK_ERR_ALIGNMENT: return "pointer is not 16-byte aligned";
+        case IQK_ERR_WORKSPACE: return "workspace missing or too small";
+        case IQK_ERR_CUDA: return "CUDA runtime error";
+        case IQK_ERR_DEVICE: return "current device is not compute capability 10.0";
+        default: return "unknown status";
+    }
+}
+
+int iqk_abi_version(void) { return 1; }
+
+int iqk_check_device(void) {
+    int dev = 0, major = 0, minor = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return cuda_status(cudaErrorNoDevice);
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+        return IQK_ERR_CUDA;
+    return (major == 10 && minor == 0) ? IQK_OK : IQK_ERR_DEVICE;
+}
+
+int iqk_dequant(int member, const void *const *streams, int64_t num_experts,
+                int64_t out_features, int64_t in_features, int64_t row_start, int64_t rows,
+                int out_dtype, void *dst, iqk_stream_t stream) {
+    if (!member_ok(member)) return IQK_ERR_MEMBER;
+    if (!width_ok(in_features)) return IQK_ERR_WIDTH;
+    if (num_experts <= 0 || out_features <= 0) return IQK_ERR_GEOMETRY;
+    if (member == IQK_IQ1_S_R4 && out_features % 4) return IQK_ERR_GEOMETRY;
+    if (row_start < 0 || rows < 0 || row_start + rows > out_features) return IQK_ERR_GEOMETRY;
+    if (!dtype_ok(out_dtype) || !dst) return IQK_ERR_ARGUMENT;
+    if (!aligned(dst, 16)) return IQK_ERR_ALIGNMENT;
+    const int st = check_streams(member, streams);
+    if (st != IQK_OK) return st;
+    if (rows == 0) return IQK_OK;
+    return cuda_status(launch_dequant(member, streams, num_experts, out_features,
+                                      (int)in_features, row_start, rows, out_dtype, dst,
+                                      reinterpret_cast<cudaStream_t>(stream),
+                                      num_sms_current()));
+}
+
+size_t iqk_gemv_workspace_bytes(int member, int64_t in_features, int64_t x_rows,
+                                int64_t pairs) {
+    if (!member_ok(member) || !width_ok(in_features) || x_rows < 0 || pairs < 0) return 0;
+    return gemv_layout(member, in_features, x_rows, pairs).total;
+}
+
+int iqk_gemv(int member, const void *x, int x_dtype, int64_t x_rows,
+             const void *const *streams, int64_t num_experts, int64_t out_features,
+             int64_t in_features, const int32_t *sel, const int32_t *tok, int64_t pairs,
+             void *y, int y_dtype, void *workspace, size_t workspace_bytes,
+             iqk_stream_t stream) {
+    if (!member_ok(member)) return IQK_ERR_MEMBER;
+    if (!width_ok(in_features)) return IQK_ERR_WIDTH;
+    if (num_experts <= 0 || num_experts > 16384) return IQK_ERR_GEOMETRY;
+    if (out_features <= 0 || out_features % 16) return IQK_ERR_GEOMETRY;
+    if (pairs < 0 || x_rows < 0 || pairs > (1 << 24) || x_rows > (1 << 24))
+        return IQK_ERR_GEOMETRY;
+    if (!tok && x_rows > 0 && pairs % x_rows) return IQK_ERR_GEOMETRY;
+    if (!tok && x_rows == 0 && pairs > 0) return IQK_ERR_GEOMETRY;
+    if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return IQK_ERR_ARGUMENT;
+    if (pairs == 0) return IQK_OK;
+    if (!x || !sel || !y || !workspace) return IQK_ERR_ARGUMENT;
+    if (!aligned(x, 16) || !aligned(y, 4) || !aligned(workspace, 256)) return IQK_ERR_ALIGNMENT;
+    const int st = check_streams(member, streams);
+    if (st != IQK_OK) return st;
+    if (workspace_bytes < gemv_layout(member, in_features, x_rows, pairs).total)
+        return IQK_ERR_WORKSPACE;
+    return cuda_status(launch_gemv(member, x, x_dtype, x_rows, streams, num_experts,
+                                   out_features, (int)in_features, sel, tok, pairs, y,
+                                   y_dtype, workspace, reinterpret_cast<cudaStream_t>(stream),
+                                   num_sms_current()));
+}
+
+int iqk_read_error(const void *workspace, int32_t *flags, iqk_stream_t stream) {
+    if (!workspace || !flags) return IQK_ERR_ARGUMENT;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t err = cudaMemcpyAsync(flags, workspace, sizeof(int32_t),
+                                      cudaMemcpyDeviceToHost, s);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    return cuda_status(err);
+}
+
+}  // extern "C"

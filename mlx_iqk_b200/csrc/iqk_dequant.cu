@@ -1,0 +1,165 @@
+// Bit-exact stacked dequantization of the IQ_K relayout streams.
+//
+// One thread reconstructs eight consecutive weights of one output row and
+// writes them with one 16-byte store (float16/bfloat16) or two (float32), so
+// a warp's stores cover 512 or 1024 contiguous bytes. The arithmetic is the
+// CPU dequantizer's float32 chain in its order
+// (vendor/ik_llama/iqk_iq2.cpp:502-562, vendor/ik_llama/iqk_iq1sr4.cpp:581-604;
+// the reference's Metal restatement is src/mlx_iqk/kernels.py:631-742):
+//
+//   2-bit members  dl = d * float(idx);             w = dl * float(value)
+//   IQ1_S_R4       dl = d * float(2 * ls + 1);      w = dl * (float(g) + shift)
+//
+// Two separate multiplies cannot be contracted into an FMA, so the float32
+// result equals the CPU's bit for bit; a 16-bit output is then one
+// round-to-nearest-even conversion, the same as numpy's astype.
+#include "iqk_common.cuh"
+#include "iqk_tables.cuh"
+
+namespace iqk {
+
+// Decode the 8 weights of octet `oct` of source row `srow` into w[0..7].
+template <int MEMBER>
+__device__ __forceinline__ void decode_octet(const void *const *s, int64_t srow,
+                                             int oct, int n, const uint16_t *grid,
+                                             float w[8]) {
+    const int k0 = oct * 8;
+    if (MEMBER == IQK_IQ1_S_R4) {
+        const uint32_t *qs = static_cast<const uint32_t *>(s[0]);
+        const uint16_t *qh = static_cast<const uint16_t *>(s[1]);
+        const uint16_t *dv = static_cast<const uint16_t *>(s[2]);
+        const int b = k0 >> 5, i = (k0 >> 3) & 3;
+        const uint32_t qw = qs[srow * (n / 32) + b];
+        const uint32_t h = qh[srow * (n / 32) + b];
+        const float d = half_bits_to_float(dv[srow]);
+        const float dl = d * (float)(int)(2u * ((h >> 12) & 7u) + 1u);
+        const float shift = (h & 0x8000u) ? -0.125f : 0.125f;
+        const uint32_t idx = ((qw >> (8 * i)) & 0xffu) | (((h >> (3 * i)) & 7u) << 8);
+        const uint32_t code = grid[idx];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int g = (int)((code >> (2 * j)) & 3u) - 1;
+            w[j] = dl * ((float)g + shift);
+        }
+        return;
+    }
+    const uint32_t *qs = static_cast<const uint32_t *>(s[0]);
+    const uint32_t word = qs[srow * (n / 16) + (k0 >> 4)];
+    const uint32_t codes = word >> (2 * (k0 & 15));  // 8 codes in the low 16 bits
+    float dl;
+    int alpha;
+    if (MEMBER == IQK_IQ2_KS) {
+        const uint8_t *scl = static_cast<const uint8_t *>(s[1]);
+        const uint8_t *sch = static_cast<const uint8_t *>(s[2]);
+        const uint8_t *sex = static_cast<const uint8_t *>(s[3]);
+        const uint16_t *dv = static_cast<const uint16_t *>(s[4]);
+        const int g = k0 >> 5;
+        const int lo = (scl[srow * (n / 64) + (g >> 1)] >> (4 * (g & 1))) & 15;
+        const int hi = (sch[srow * (n / 256) + (g >> 3)] >> (g & 7)) & 1;
+        alpha = (sex[srow * (n / 256) + (g >> 3)] >> (g & 7)) & 1;
+        const float d = half_bits_to_float(dv[srow]);
+        dl = d * (float)((lo | (hi << 4)) - 16);
+    } else {
+        const uint8_t *scl = static_cast<const uint8_t *>(s[1]);
+        const uint8_t *sex = static_cast<const uint8_t *>(s[2]);
+        const uint16_t *dv = static_cast<const uint16_t *>(s[3]);
+        const int sb = k0 >> 4;
+        const int lo = (scl[srow * (n / 32) + (sb >> 1)] >> (4 * (sb & 1))) & 15;
+        alpha = (sex[srow * (n / 128) + (sb >> 3)] >> (sb & 7)) & 1;
+        const float d = half_bits_to_float(dv[srow * (n / 256) + (sb >> 4)]);
+        dl = d * (float)(lo - 8);
+    }
+    // The sub-block's four alphabet entries as int8 bytes of one register.
+    const uint32_t tab = alpha ? kIq2Tab1 : kIq2Tab0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int v = (int)(int8_t)(tab >> (8 * ((codes >> (2 * j)) & 3u)));
+        w[j] = dl * (float)v;
+    }
+}
+
+struct StreamPtrs {
+    const void *p[5];
+};
+
+template <int MEMBER, typename OUT>
+__global__ void __launch_bounds__(256)
+dequant_rows_kernel(StreamPtrs sp, uint32_t total_octets, int log2_octs,
+                    int n, int64_t out_features, int64_t row_start, uint32_t rows,
+                    OUT *__restrict__ dst) {
+    __shared__ uint16_t grid[MEMBER == IQK_IQ1_S_R4 ? 2048 : 1];
+    if (MEMBER == IQK_IQ1_S_R4) {
+        for (int i = threadIdx.x; i < 2048; i += blockDim.x) grid[i] = g_iq1s_grid[i];
+        __syncthreads();
+    }
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t o = blockIdx.x * blockDim.x + threadIdx.x; o < total_octets; o += stride) {
+        const uint32_t lin = o >> log2_octs;  // [expert, local row]
+        const int oct = (int)(o & ((1u << log2_octs) - 1u));
+        const uint32_t e = lin / rows;
+        const int64_t srow = (int64_t)e * out_features + row_start + (lin - e * rows);
+        float w[8];
+        decode_octet<MEMBER>(sp.p, srow, oct, n, grid, w);
+        OUT *out = dst + (int64_t)lin * n + oct * 8;
+        if constexpr (sizeof(OUT) == 4) {
+            float4 *o4 = reinterpret_cast<float4 *>(out);
+            o4[0] = make_float4(w[0], w[1], w[2], w[3]);
+            o4[1] = make_float4(w[4], w[5], w[6], w[7]);
+        } else {
+            union {
+                OUT h[8];
+                uint4 u;
+            } pk;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) pk.h[j] = from_float<OUT>(w[j]);
+            *reinterpret_cast<uint4 *>(out) = pk.u;
+        }
+    }
+}
+
+cudaError_t launch_dequant(int member, const void *const *streams, int64_t num_experts,
+                           int64_t out_features, int n, int64_t row_start,
+                           int64_t rows, int out_dtype, void *dst, cudaStream_t stream,
+                           int num_sms) {
+    StreamPtrs sp{};
+    const RowBytes rb = row_bytes(member, n);
+    for (int i = 0; i < rb.count; ++i) sp.p[i] = streams[i];
+    const int log2_octs = n == 4096 ? 9 : 8;  // n / 8 octets per row
+    const int elem = out_dtype == IQK_F32 ? 4 : 2;
+    // 32-bit octet indices: split the expert range so each launch stays below 2^31.
+    const int64_t per_expert = rows * (n / 8);
+    if (per_expert == 0 || num_experts == 0) return cudaSuccess;
+    const int64_t chunk = ((int64_t)1 << 31) / per_expert;
+    for (int64_t e0 = 0; e0 < num_experts; e0 += chunk) {
+        const int64_t ne = num_experts - e0 < chunk ? num_experts - e0 : chunk;
+        const uint32_t total = (uint32_t)(ne * per_expert);
+        StreamPtrs spc = sp;
+        for (int i = 0; i < rb.count; ++i)
+            spc.p[i] = static_cast<const char *>(sp.p[i]) + e0 * out_features * rb.b[i];
+        void *dstc = static_cast<char *>(dst) + e0 * rows * n * elem;
+        const int threads = 256;
+        int64_t blocks = ((int64_t)total + threads - 1) / threads;
+        const int64_t cap = (int64_t)num_sms * 8;  // resident blocks; grid-stride beyond
+        if (blocks > cap) blocks = cap;
+#define IQK_DQ(M, T)                                                                  \
+        dequant_rows_kernel<M, T><<<(unsigned)blocks, threads, 0, stream>>>(           \
+            spc, total, log2_octs, n, out_features, row_start, (uint32_t)rows,         \
+            static_cast<T *>(dstc))
+#define IQK_DQ_MEMBER(M)                                             \
+    do {                                                             \
+        if (out_dtype == IQK_F32) IQK_DQ(M, float);                  \
+        else if (out_dtype == IQK_F16) IQK_DQ(M, __half);            \
+        else IQK_DQ(M, __nv_bfloat16);                               \
+    } while (0)
+        if (member == IQK_IQ2_KS) IQK_DQ_MEMBER(IQK_IQ2_KS);
+        else if (member == IQK_IQ2_K) IQK_DQ_MEMBER(IQK_IQ2_K);
+        else IQK_DQ_MEMBER(IQK_IQ1_S_R4);
+#undef IQK_DQ_MEMBER
+#undef IQK_DQ
+        cudaError_t err = cudaGetLastError();
+        if (err != cudaSuccess) return err;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace iqk

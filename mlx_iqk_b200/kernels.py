@@ -1,0 +1,195 @@
+"""ctypes binding of ``libiqk_b200.so`` plus the reference's geometry guards.
+
+The CUDA library is the product: this module loads it (failing loudly when it
+is missing -- there is no CPU or eager fallback), declares the C ABI of
+``include/iqk_b200.h``, and maps status codes onto the reference's exception
+classes. The guard functions keep the reference's names and messages
+(``src/mlx_iqk/kernels.py:100-128``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import torch
+
+from .format import MEMBER_IDS, IqkFormatError, check_member, check_row_width
+
+ROWS_PER_TG = 16
+"""Output rows one decode work unit (a warp) covers; out_features must tile it."""
+
+SUPPORTED_IN_FEATURES = (2048, 4096)
+"""Input widths the kernels are sized for: the down and gate/up widths."""
+
+IQ2_MEMBERS = ("iq2_ks", "iq2_k")
+"""Members the reference records sorted/union GEMV formulations for."""
+
+LIB_PATH = Path(__file__).resolve().parent / "libiqk_b200.so"
+
+IQK_OK = 0
+_STATUS_NAMES = {
+    1: "IQK_ERR_MEMBER", 2: "IQK_ERR_WIDTH", 3: "IQK_ERR_GEOMETRY", 4: "IQK_ERR_ARGUMENT",
+    5: "IQK_ERR_ALIGNMENT", 6: "IQK_ERR_WORKSPACE", 7: "IQK_ERR_CUDA", 8: "IQK_ERR_DEVICE",
+}
+DEVERR_EXPERT, DEVERR_TOKEN, DEVERR_NONFINITE = 1, 2, 4
+DTYPE_IDS = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+
+class IqkKernelError(RuntimeError):
+    """Geometry the kernels are not sized for (reference class name)."""
+
+
+class IqkRuntimeError(RuntimeError):
+    """Operand/stream contract violation or a failed launch (reference class name)."""
+
+
+def check_gemv_geometry(in_features: int, out_features: int) -> tuple[int, int]:
+    """Reject any geometry the decode GEMV does not cover, before launching."""
+    n = check_row_width(in_features)
+    if n not in SUPPORTED_IN_FEATURES:
+        raise IqkKernelError(
+            f"the decode gemv is sized per input width and covers "
+            f"{SUPPORTED_IN_FEATURES}, got {in_features}")
+    out = int(out_features)
+    if out <= 0 or out % ROWS_PER_TG:
+        raise IqkKernelError(
+            f"out_features {out_features} is not a positive multiple of {ROWS_PER_TG}")
+    return n, out
+
+
+def check_dequant_geometry(in_features: int, out_features: int) -> tuple[int, int]:
+    """Reject any geometry the stacked dequantization does not cover."""
+    n = check_row_width(in_features)
+    if n not in SUPPORTED_IN_FEATURES:
+        raise IqkKernelError(
+            f"the dequantization is sized per input width and covers "
+            f"{SUPPORTED_IN_FEATURES}, got {in_features}")
+    out = int(out_features)
+    if out <= 0:
+        raise IqkKernelError(f"out_features {out_features} is not positive")
+    return n, out
+
+
+# ------------------------------------------------------------------ loading
+
+_LIB = None
+
+
+def library() -> ctypes.CDLL:
+    """The loaded CUDA library; raises if it was never built."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    path = Path(os.environ.get("IQK_B200_LIB", LIB_PATH))
+    if not path.exists():
+        raise IqkRuntimeError(
+            f"{path} is not built; run `python -c 'import __graft_entry__ as g; g.build()'` "
+            "(the IQ_K kernels have no CPU fallback)")
+    lib = ctypes.CDLL(str(path))
+    vp, i64, i32, sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
+    lib.iqk_status_string.argtypes = [i32]
+    lib.iqk_status_string.restype = ctypes.c_char_p
+    lib.iqk_abi_version.restype = i32
+    lib.iqk_check_device.restype = i32
+    lib.iqk_dequant.argtypes = [i32, vp, i64, i64, i64, i64, i64, i32, vp, vp]
+    lib.iqk_dequant.restype = i32
+    lib.iqk_gemv_workspace_bytes.argtypes = [i32, i64, i64, i64]
+    lib.iqk_gemv_workspace_bytes.restype = sz
+    lib.iqk_gemv.argtypes = [i32, vp, i32, i64, vp, i64, i64, i64, vp, vp, i64, vp, i32, vp,
+                             sz, vp]
+    lib.iqk_gemv.restype = i32
+    lib.iqk_read_error.argtypes = [vp, ctypes.POINTER(ctypes.c_int32), vp]
+    lib.iqk_read_error.restype = i32
+    _LIB = lib
+    return lib
+
+
+def exported_symbols() -> list[str]:
+    """C ABI entry points declared in include/iqk_b200.h."""
+    return ["iqk_status_string", "iqk_abi_version", "iqk_check_device", "iqk_dequant",
+            "iqk_gemv_workspace_bytes", "iqk_gemv", "iqk_read_error"]
+
+
+def raise_for_status(status: int, what: str) -> None:
+    if status == IQK_OK:
+        return
+    msg = f"{what}: {library().iqk_status_string(status).decode()} ({_STATUS_NAMES.get(status, status)})"
+    if status == 1:
+        raise IqkFormatError(msg)
+    if status in (2, 3):
+        raise IqkKernelError(msg)
+    raise IqkRuntimeError(msg)
+
+
+_DEVICE_OK: dict[int, bool] = {}
+
+
+def check_device(device: torch.device) -> None:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _DEVICE_OK:
+        with torch.cuda.device(idx):
+            raise_for_status(library().iqk_check_device(), "device check")
+        _DEVICE_OK[idx] = True
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr_array(tensors) -> ctypes.Array:
+    arr = (ctypes.c_void_p * len(tensors))()
+    for i, t in enumerate(tensors):
+        arr[i] = t.data_ptr()
+    return arr
+
+
+def dequant(member: str, streams, num_experts: int, out_features: int, in_features: int,
+            row_start: int, rows: int, out: torch.Tensor) -> torch.Tensor:
+    """``iqk_dequant`` into ``out`` [E, rows, in] on the current stream."""
+    lib = library()
+    check_device(out.device)
+    status = lib.iqk_dequant(MEMBER_IDS[check_member(member)], ptr_array(streams), num_experts,
+                             out_features, in_features, row_start, rows,
+                             DTYPE_IDS[out.dtype], out.data_ptr(), stream_handle(out.device))
+    raise_for_status(status, "iqk_dequant")
+    return out
+
+
+def gemv_workspace_bytes(member: str, in_features: int, x_rows: int, pairs: int) -> int:
+    return int(library().iqk_gemv_workspace_bytes(MEMBER_IDS[member], in_features, x_rows, pairs))
+
+
+def gemv(member: str, x: torch.Tensor, streams, num_experts: int, out_features: int,
+         in_features: int, sel: torch.Tensor, tok: torch.Tensor | None, y: torch.Tensor,
+         workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """``iqk_gemv``: x [x_rows, in], sel/tok int32 [pairs], y [pairs, out]."""
+    lib = library()
+    check_device(y.device)
+    pairs = sel.numel()
+    x_rows = x.shape[0]
+    need = gemv_workspace_bytes(member, in_features, x_rows, pairs)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=y.device)
+    status = lib.iqk_gemv(
+        MEMBER_IDS[member], x.data_ptr(), DTYPE_IDS[x.dtype], x_rows, ptr_array(streams),
+        num_experts, out_features, in_features, sel.data_ptr(),
+        None if tok is None else tok.data_ptr(), pairs, y.data_ptr(), DTYPE_IDS[y.dtype],
+        workspace.data_ptr(), workspace.numel(), stream_handle(y.device))
+    raise_for_status(status, "iqk_gemv")
+    return y
+
+
+def read_error(workspace: torch.Tensor) -> int:
+    flags = ctypes.c_int32(0)
+    raise_for_status(library().iqk_read_error(workspace.data_ptr(), ctypes.byref(flags),
+                                              stream_handle(workspace.device)),
+                     "iqk_read_error")
+    return int(flags.value)
+
+
+__all__ = [
+    "IQ2_MEMBERS", "ROWS_PER_TG", "SUPPORTED_IN_FEATURES", "IqkKernelError", "IqkRuntimeError",
+    "check_dequant_geometry", "check_gemv_geometry", "dequant", "gemv", "library",
+]

@@ -1,0 +1,272 @@
+"""Stacked-expert IQ_K projection with the ``(x, indices)`` switch interface, on B200.
+
+``IqkSwitchLinear`` keeps the reference's surface (``src/mlx_iqk/nn.py:105-333``):
+the constructor ``(member, num_experts, out_features, in_features)``,
+``load_streams`` fed by ``format.pack`` output, ``__call__(x, indices,
+sorted_indices=False)`` with the gate/up operand ``[..., 1, 1, in]`` or the down
+operand ``[..., top_k, 1, in]`` and a ``[..., top_k, 1, out]`` result, plus
+``gemv``, ``gemv_sorted``, ``gemv_union``, ``dequantized``,
+``dequantized_range`` and ``sorted_matmul_range``. Every compute call runs the
+sm_100a kernels of ``libiqk_b200.so`` on the current CUDA stream.
+
+Differences from the reference, each deliberate:
+
+* activations are consumed in their own dtype (float32, float16 or bfloat16);
+  the reference casts to float16 first (``nn.py:247``);
+* projections return float32: the decode kernel's result is exact up to one
+  final rounding, and a 16-bit store would not hold the 1e-4 decode bound;
+* every route streams each selected expert's rows once for all pairs that
+  picked it (the reference's union formulation, for all three members).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+from torch import nn
+
+from . import kernels as K
+from .format import IQ2NL_VALUES, check_member, component_dtypes, component_shapes
+
+DECODE_MAT_LIMIT = 63
+"""Token-expert pairs at or below which ``__call__`` serves the decode GEMV
+(``src/mlx_iqk/nn.py:49``)."""
+
+IqkRuntimeError = K.IqkRuntimeError
+IqkKernelError = K.IqkKernelError
+
+_TORCH_DTYPES = {"uint8": torch.uint8, "uint16": torch.uint16, "uint32": torch.uint32,
+                 "float16": torch.float16}
+
+_VALUE_TABLES: dict[torch.device, torch.Tensor] = {}
+_GRID_TABLES: dict[torch.device, torch.Tensor] = {}
+
+
+def _default_device() -> torch.device:
+    return torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() \
+        else torch.device("cpu")
+
+
+def value_table(device: torch.device | None = None) -> torch.Tensor:
+    """The fp16 ``iq2nl_values`` table, one shared tensor per device.
+
+    The kernels carry the alphabet as immediates; the tensor exists for API
+    parity with the reference (``nn.py:60-71``) and for callers that want it.
+    """
+    dev = device or _default_device()
+    if dev not in _VALUE_TABLES:
+        _VALUE_TABLES[dev] = torch.tensor(IQ2NL_VALUES.astype(np.float16), device=dev)
+    return _VALUE_TABLES[dev]
+
+
+def grid_table(device: torch.device | None = None) -> torch.Tensor:
+    """The IQ1_S grid as uint32 words (2048 entries x 8 int8 values), shared per device."""
+    dev = device or _default_device()
+    if dev not in _GRID_TABLES:
+        from .tables import grid_values
+        words = np.ascontiguousarray(grid_values()).view(np.uint32).reshape(-1)
+        _GRID_TABLES[dev] = torch.from_numpy(words.copy()).to(dev)
+    return _GRID_TABLES[dev]
+
+
+def member_table(member: str, device: torch.device | None = None) -> torch.Tensor:
+    check_member(member)
+    return grid_table(device) if member == "iq1_s_r4" else value_table(device)
+
+
+class IqkSwitchLinear(nn.Module):
+    """Stacked IQ_K experts for one projection, ``(x, indices)`` interface."""
+
+    mode = "iqk"
+
+    def __init__(self, member: str, num_experts: int, out_features: int, in_features: int,
+                 device: torch.device | str | None = None):
+        super().__init__()
+        self.member = check_member(member)
+        K.check_gemv_geometry(in_features, out_features)
+        K.check_dequant_geometry(in_features, out_features)
+        self.num_experts = int(num_experts)
+        self.out_features = int(out_features)
+        self.in_features = int(in_features)
+        if self.num_experts <= 0:
+            raise IqkRuntimeError(f"num_experts {num_experts} is not positive")
+        dev = torch.device(device) if device is not None else _default_device()
+        shapes = component_shapes(member, num_experts, out_features, in_features)
+        dtypes = component_dtypes(member)
+        for name, shape in shapes.items():
+            self.register_buffer(
+                name, torch.zeros(shape, dtype=_TORCH_DTYPES[dtypes[name].name], device=dev))
+
+    # -- wire streams -------------------------------------------------------
+
+    def stream_names(self) -> list[str]:
+        """Relayout stream names of this member, in kernel input order."""
+        return list(component_shapes(self.member, self.num_experts, self.out_features,
+                                     self.in_features))
+
+    def _streams(self) -> list[torch.Tensor]:
+        return [getattr(self, name) for name in self.stream_names()]
+
+    @property
+    def device(self) -> torch.device:
+        return self.qs.device
+
+    def load_streams(self, streams: dict) -> None:
+        """Install packed streams (numpy or torch), checking every shape.
+
+        Values are reinterpreted (not converted) as the stream's dtype, so a
+        same-width integer view of the packed bytes is accepted; a different
+        element width is refused.
+        """
+        shapes = component_shapes(self.member, self.num_experts, self.out_features,
+                                  self.in_features)
+        if set(streams) != set(shapes):
+            raise IqkRuntimeError(
+                f"{self.member} needs streams {sorted(shapes)}, got {sorted(streams)}")
+        for name, want in shapes.items():
+            got = tuple(streams[name].shape)
+            if got != want:
+                raise IqkRuntimeError(
+                    f"stream {name} must be {want} for "
+                    f"{self.num_experts}x{self.out_features}x{self.in_features}, got {got}")
+        dtypes = component_dtypes(self.member)
+        staged = {}
+        for name, value in streams.items():
+            want_t = _TORCH_DTYPES[dtypes[name].name]
+            if isinstance(value, np.ndarray):
+                arr = np.ascontiguousarray(value)
+                if arr.dtype.itemsize != dtypes[name].itemsize:
+                    raise IqkRuntimeError(
+                        f"stream {name} has {arr.dtype} elements, expected {dtypes[name]}")
+                t = torch.from_numpy(arr.view(dtypes[name]))
+            elif isinstance(value, torch.Tensor):
+                t = value
+                if t.element_size() != dtypes[name].itemsize:
+                    raise IqkRuntimeError(
+                        f"stream {name} has {t.dtype} elements, expected {dtypes[name]}")
+                if t.dtype != want_t:
+                    t = t.contiguous().view(want_t)
+            else:
+                raise IqkRuntimeError(f"stream {name} is a {type(value).__name__}")
+            staged[name] = t.to(self.device, non_blocking=False).contiguous()
+        for name, t in staged.items():
+            setattr(self, name, t)
+
+    # -- dequantized route --------------------------------------------------
+
+    def dequantized(self, dtype: torch.dtype = torch.float16) -> torch.Tensor:
+        """Full dequantization ``[E, out, in]``, bit-identical to the CPU decode
+        rounded once to ``dtype`` (float16 by default, as the reference)."""
+        out = torch.empty((self.num_experts, self.out_features, self.in_features),
+                          dtype=dtype, device=self.device)
+        return K.dequant(self.member, self._streams(), self.num_experts, self.out_features,
+                         self.in_features, 0, self.out_features, out)
+
+    def dequantized_range(self, start: int, rows: int,
+                          dtype: torch.dtype = torch.float16) -> torch.Tensor:
+        """Dequantization of out rows ``[start, start + rows)`` of every expert,
+        ``[E, rows, in]``; the same bits as that slice of :meth:`dequantized`.
+
+        ``rows`` must be a positive power of two, as in the reference
+        (``src/mlx_iqk/nn.py:171-201``), whose range kernel is sized that way.
+        """
+        start, rows = int(start), int(rows)
+        if rows <= 0 or rows & (rows - 1):
+            raise IqkRuntimeError(f"range rows {rows} is not a positive power of two")
+        if start < 0 or start + rows > self.out_features:
+            raise IqkRuntimeError(
+                f"range [{start}, {start + rows}) is outside out_features {self.out_features}")
+        out = torch.empty((self.num_experts, rows, self.in_features), dtype=dtype,
+                          device=self.device)
+        return K.dequant(self.member, self._streams(), self.num_experts, self.out_features,
+                         self.in_features, start, rows, out)
+
+    def sorted_matmul_range(self, x, indices, start: int, rows: int) -> torch.Tensor:
+        """The sorted projection restricted to out rows ``[start, start + rows)``.
+
+        Concatenating range outputs along the feature axis reproduces the
+        unsplit call bit for bit (each output element is one dot product).
+        """
+        full = self(x, indices, sorted_indices=True)
+        if rows <= 0 or rows & (rows - 1) or start < 0 or start + rows > self.out_features:
+            raise IqkRuntimeError(f"bad range [{start}, {start + rows})")
+        return full[..., start:start + rows].contiguous()
+
+    # -- call ---------------------------------------------------------------
+
+    def __call__(self, x, indices, sorted_indices=False):
+        return self.forward(x, indices, sorted_indices)
+
+    def forward(self, x, indices, sorted_indices=False) -> torch.Tensor:
+        """Project ``x`` through the experts named by ``indices``.
+
+        ``x`` is ``[..., 1, 1, in]`` (one row per token, shared by its top_k
+        experts) or ``[..., top_k, 1, in]`` (one row per pair); ``indices``
+        is ``[..., top_k]``; the result is ``[..., top_k, 1, out]`` float32.
+        Decode-sized calls (``<= DECODE_MAT_LIMIT`` pairs, unsorted) and
+        prefill-sized ones both run the union GEMV kernel today; the routing
+        split is kept so a prefill-shaped call can take a grouped-GEMM route.
+        """
+        return self.gemv(x, indices)
+
+    def _prep(self, x: torch.Tensor) -> torch.Tensor:
+        if not isinstance(x, torch.Tensor):
+            x = torch.as_tensor(np.asarray(x))
+        if x.device != self.device:
+            x = x.to(self.device)
+        if x.dtype not in K.DTYPE_IDS:
+            x = x.to(torch.float32)
+        return x.reshape(-1, self.in_features).contiguous()
+
+    @staticmethod
+    def _idx(t, device) -> torch.Tensor:
+        if not isinstance(t, torch.Tensor):
+            t = torch.as_tensor(np.asarray(t).astype(np.int64))
+        return t.reshape(-1).to(device=device, dtype=torch.int32).contiguous()
+
+    def gemv(self, x, indices) -> torch.Tensor:
+        """Fused dequant + GEMV over the selected experts; valid for any pair count."""
+        xt = self._prep(x)
+        idx_shape = tuple(indices.shape)
+        sel = self._idx(indices, self.device)
+        mats, rows = sel.numel(), xt.shape[0]
+        if rows <= 0 or mats % rows:
+            raise IqkRuntimeError(
+                f"{mats} token-expert pairs do not tile {rows} activation "
+                f"row(s); the operand and the routing disagree")
+        y = torch.empty((mats, self.out_features), dtype=torch.float32, device=self.device)
+        K.gemv(self.member, xt, self._streams(), self.num_experts, self.out_features,
+               self.in_features, sel, None, y)
+        return y.reshape(*idx_shape, self.out_features).unsqueeze(-2)
+
+    def _gemv_toks(self, x, sorted_ids, toks) -> torch.Tensor:
+        if self.member not in K.IQ2_MEMBERS:
+            raise IqkKernelError(
+                f"the sorted and union decode GEMVs are recorded formulations "
+                f"for {K.IQ2_MEMBERS}; {self.member!r} has no such variant")
+        xt = self._prep(x)
+        sel = self._idx(sorted_ids, self.device)
+        tok = self._idx(toks, self.device)
+        if tok.numel() != sel.numel():
+            raise IqkRuntimeError(f"toks carries {tok.numel()} rows for {sel.numel()} pairs")
+        y = torch.empty((sel.numel(), self.out_features), dtype=torch.float32,
+                        device=self.device)
+        K.gemv(self.member, xt, self._streams(), self.num_experts, self.out_features,
+               self.in_features, sel, tok, y)
+        return y
+
+    def gemv_sorted(self, x, sorted_ids, toks) -> torch.Tensor:
+        """GEMV over expert-sorted pairs with explicit activation rows; ``[pairs, out]``.
+
+        Bit-identical to :meth:`gemv` after un-permuting (``src/mlx_iqk/nn.py:273-299``).
+        """
+        return self._gemv_toks(x, sorted_ids, toks)
+
+    def gemv_union(self, x, sorted_ids, toks) -> torch.Tensor:
+        """GEMV reading each distinct expert once; ``[pairs, out]``, bit-identical to
+        :meth:`gemv` after un-permuting (``src/mlx_iqk/nn.py:301-333``)."""
+        return self._gemv_toks(x, sorted_ids, toks)
+
+
+__all__ = ["DECODE_MAT_LIMIT", "IqkKernelError", "IqkRuntimeError", "IqkSwitchLinear",
+           "grid_table", "member_table", "value_table"]
