@@ -125,11 +125,41 @@ int iqk_gemv(int member, const void *x, int x_dtype, int64_t x_rows,
              size_t workspace_bytes, iqk_stream_t stream);
 
 /*
- * Copy the device error word a previous iqk_gemv left in its workspace into
- * *flags (IQK_DEVERR_* bits), synchronising the stream. No reference
- * counterpart: the reference's kernels read out-of-range indices unchecked.
+ * The two halves of iqk_gemv, for callers that share one preparation between
+ * several projections of the same activations and routing (a SwitchGLU's
+ * gate and up) or schedule them apart.
+ *
+ * iqk_gemv_prepare: turns each activation row into the kernel's exact
+ * integer operand form (power-of-two scale + three int8 digit planes) and
+ * buckets the pairs by expert, all into `workspace` (iqk_gemv_workspace_bytes
+ * for the same in_features / x_rows / pairs). Member-independent.
+ *
+ * iqk_gemv_run: streams the selected experts' rows of one projection and
+ * writes y; reads only the prepared workspace (x and sel are not needed).
+ * Must follow an iqk_gemv_prepare of the same workspace, on the same stream
+ * or with an equivalent ordering.
+ *
+ * Together they replace the reference's single gemv launch
+ * (src/mlx_iqk/nn.py:240-271); the split has no reference counterpart.
  */
-int iqk_read_error(const void *workspace, int32_t *flags, iqk_stream_t stream);
+int iqk_gemv_prepare(const void *x, int x_dtype, int64_t x_rows, int64_t in_features,
+                     int64_t num_experts, const int32_t *sel, const int32_t *tok,
+                     int64_t pairs, void *workspace, size_t workspace_bytes,
+                     iqk_stream_t stream);
+
+int iqk_gemv_run(int member, const void *const *streams, int64_t num_experts,
+                 int64_t out_features, int64_t in_features, int64_t x_rows, int64_t pairs,
+                 void *y, int y_dtype, const void *workspace, size_t workspace_bytes,
+                 iqk_stream_t stream);
+
+/*
+ * Copy the device error bits of the last preparation in `workspace` (same
+ * in_features / x_rows / pairs) into *flags (IQK_DEVERR_* bits),
+ * synchronising the stream. No reference counterpart: the reference's
+ * kernels read out-of-range indices unchecked.
+ */
+int iqk_read_error(const void *workspace, int64_t in_features, int64_t x_rows,
+                   int64_t pairs, int32_t *flags, iqk_stream_t stream);
 
 #ifdef __cplusplus
 }

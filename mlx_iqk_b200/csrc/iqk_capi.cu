@@ -98,39 +98,102 @@ size_t iqk_gemv_workspace_bytes(int member, int64_t in_features, int64_t x_rows,
     return gemv_layout(member, in_features, x_rows, pairs).total;
 }
 
-int iqk_gemv(int member, const void *x, int x_dtype, int64_t x_rows,
-             const void *const *streams, int64_t num_experts, int64_t out_features,
-             int64_t in_features, const int32_t *sel, const int32_t *tok, int64_t pairs,
-             void *y, int y_dtype, void *workspace, size_t workspace_bytes,
-             iqk_stream_t stream) {
+static int check_prepare(int64_t in_features, int64_t num_experts, int64_t x_rows,
+                         int64_t pairs, const int32_t *tok, int x_dtype) {
+    if (!width_ok(in_features)) return IQK_ERR_WIDTH;
+    if (num_experts <= 0 || num_experts > 16384) return IQK_ERR_GEOMETRY;
+    if (pairs < 0 || x_rows < 0 || pairs > (1 << 24) || x_rows > (1 << 24))
+        return IQK_ERR_GEOMETRY;
+    if (!tok && x_rows > 0 && pairs % x_rows) return IQK_ERR_GEOMETRY;
+    if (!tok && x_rows == 0 && pairs > 0) return IQK_ERR_GEOMETRY;
+    if (!dtype_ok(x_dtype)) return IQK_ERR_ARGUMENT;
+    return IQK_OK;
+}
+
+int iqk_gemv_prepare(const void *x, int x_dtype, int64_t x_rows, int64_t in_features,
+                     int64_t num_experts, const int32_t *sel, const int32_t *tok, int64_t pairs,
+                     void *workspace, size_t workspace_bytes, iqk_stream_t stream) {
+    int st = check_prepare(in_features, num_experts, x_rows, pairs, tok, x_dtype);
+    if (st != IQK_OK) return st;
+    if (pairs == 0) return IQK_OK;
+    if (!x || !sel || !workspace) return IQK_ERR_ARGUMENT;
+    if (!aligned(x, 16) || !aligned(workspace, 256)) return IQK_ERR_ALIGNMENT;
+    if (workspace_bytes < gemv_layout(0, in_features, x_rows, pairs).total)
+        return IQK_ERR_WORKSPACE;
+    return cuda_status(launch_gemv_prepare(x, x_dtype, x_rows, (int)in_features, num_experts,
+                                           sel, tok, pairs, workspace,
+                                           reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int iqk_gemv_run(int member, const void *const *streams, int64_t num_experts,
+                 int64_t out_features, int64_t in_features, int64_t x_rows, int64_t pairs,
+                 void *y, int y_dtype, const void *workspace, size_t workspace_bytes,
+                 iqk_stream_t stream) {
     if (!member_ok(member)) return IQK_ERR_MEMBER;
     if (!width_ok(in_features)) return IQK_ERR_WIDTH;
     if (num_experts <= 0 || num_experts > 16384) return IQK_ERR_GEOMETRY;
     if (out_features <= 0 || out_features % 16) return IQK_ERR_GEOMETRY;
     if (pairs < 0 || x_rows < 0 || pairs > (1 << 24) || x_rows > (1 << 24))
         return IQK_ERR_GEOMETRY;
-    if (!tok && x_rows > 0 && pairs % x_rows) return IQK_ERR_GEOMETRY;
-    if (!tok && x_rows == 0 && pairs > 0) return IQK_ERR_GEOMETRY;
-    if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return IQK_ERR_ARGUMENT;
+    if (!dtype_ok(y_dtype)) return IQK_ERR_ARGUMENT;
     if (pairs == 0) return IQK_OK;
-    if (!x || !sel || !y || !workspace) return IQK_ERR_ARGUMENT;
-    if (!aligned(x, 16) || !aligned(y, 4) || !aligned(workspace, 256)) return IQK_ERR_ALIGNMENT;
+    if (!y || !workspace) return IQK_ERR_ARGUMENT;
+    if (!aligned(y, 4) || !aligned(workspace, 256)) return IQK_ERR_ALIGNMENT;
     const int st = check_streams(member, streams);
     if (st != IQK_OK) return st;
     if (workspace_bytes < gemv_layout(member, in_features, x_rows, pairs).total)
         return IQK_ERR_WORKSPACE;
-    return cuda_status(launch_gemv(member, x, x_dtype, x_rows, streams, num_experts,
-                                   out_features, (int)in_features, sel, tok, pairs, y,
-                                   y_dtype, workspace, reinterpret_cast<cudaStream_t>(stream),
-                                   num_sms_current()));
+    return cuda_status(launch_gemv_run(member, streams, out_features, (int)in_features, x_rows,
+                                       pairs, y, y_dtype, workspace,
+                                       reinterpret_cast<cudaStream_t>(stream),
+                                       num_sms_current()));
 }
 
-int iqk_read_error(const void *workspace, int32_t *flags, iqk_stream_t stream) {
-    if (!workspace || !flags) return IQK_ERR_ARGUMENT;
+int iqk_gemv(int member, const void *x, int x_dtype, int64_t x_rows,
+             const void *const *streams, int64_t num_experts, int64_t out_features,
+             int64_t in_features, const int32_t *sel, const int32_t *tok, int64_t pairs,
+             void *y, int y_dtype, void *workspace, size_t workspace_bytes,
+             iqk_stream_t stream) {
+    if (!member_ok(member)) return IQK_ERR_MEMBER;
+    int st = check_prepare(in_features, num_experts, x_rows, pairs, tok, x_dtype);
+    if (st != IQK_OK) return st;
+    if (out_features <= 0 || out_features % 16) return IQK_ERR_GEOMETRY;
+    if (!dtype_ok(y_dtype)) return IQK_ERR_ARGUMENT;
+    if (pairs == 0) return IQK_OK;
+    if (!y || !streams) return IQK_ERR_ARGUMENT;
+    st = check_streams(member, streams);
+    if (st != IQK_OK) return st;
+    st = iqk_gemv_prepare(x, x_dtype, x_rows, in_features, num_experts, sel, tok, pairs,
+                          workspace, workspace_bytes, stream);
+    if (st != IQK_OK) return st;
+    return iqk_gemv_run(member, streams, num_experts, out_features, in_features, x_rows, pairs,
+                        y, y_dtype, workspace, workspace_bytes, stream);
+}
+
+int iqk_read_error(const void *workspace, int64_t in_features, int64_t x_rows, int64_t pairs,
+                   int32_t *flags, iqk_stream_t stream) {
+    if (!workspace || !flags || !width_ok(in_features) || x_rows < 0 || pairs < 0)
+        return IQK_ERR_ARGUMENT;
+    *flags = 0;
+    if (pairs == 0) return IQK_OK;
+    const GemvLayout L = gemv_layout(0, in_features, x_rows, pairs);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    cudaError_t err = cudaMemcpyAsync(flags, workspace, sizeof(int32_t),
+    int32_t hdr0 = 0;
+    int32_t *scales = new int32_t[x_rows > 0 ? x_rows : 1];
+    const char *w = static_cast<const char *>(workspace);
+    cudaError_t err = cudaMemcpyAsync(&hdr0, w + L.hdr, sizeof(int32_t),
                                       cudaMemcpyDeviceToHost, s);
+    if (err == cudaSuccess && x_rows > 0)
+        err = cudaMemcpyAsync(scales, w + L.xscale, sizeof(int32_t) * x_rows,
+                              cudaMemcpyDeviceToHost, s);
     if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    if (err == cudaSuccess) {
+        int32_t f = hdr0;
+        for (int64_t r = 0; r < x_rows; ++r)
+            if (scales[r] == kScaleNonFinite) f |= IQK_DEVERR_NONFINITE;
+        *flags = f;
+    }
+    delete[] scales;
     return cuda_status(err);
 }
 

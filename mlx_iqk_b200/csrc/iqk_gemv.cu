@@ -9,27 +9,33 @@
 // * Activations are prepared once per call (prep kernel): each row x[t] is
 //   scaled by a power of two 2^S_t so max|x| < 2^22, rounded to an integer,
 //   and split into three signed 8-bit digit planes (x_int = 65536*h + 256*m
-//   + l). The planes are stored in the operand order of the MMA below.
+//   + l), stored in the B-operand order of the MMA below.
 // * Weights are never materialised. Each 2-bit code (or ternary grid value)
-//   is turned into its int8 alphabet value with a byte permute straight into
-//   an mma.sync.m16n8k32 s8 A fragment; the digit planes are the B operand.
-//   The tensor core returns exact int32 sums per 32-weight group, which are
-//   scaled by the group's integer scale index with IMAD -- so the whole
-//   reduction is exact integer arithmetic until one final double-precision
-//   multiply by the fp16 row (or super-block) scale and 2^-S_t.
-// * Consequently every output is independent of reduction order and of how
-//   pairs are grouped: a sorted or unioned call is bit-identical to the
-//   per-pair call, and the only approximation is x's 22-bit rounding.
-// * Routing is on the device: pairs are bucketed by expert, and each distinct
-//   expert's weight rows are streamed once for all pairs that selected it
-//   (the reference's "union" formulation, src/mlx_iqk/kernels.py:484-572,
-//   for every member).
+//   becomes its int8 alphabet value through a byte permute whose selector
+//   nibble is (code | 4*alphabet), straight into an mma.sync.m16n8k32 s8 A
+//   fragment; the digit planes are the B operand. The tensor core returns
+//   exact int32 sums per 32-weight group, scaled by the group's integer scale
+//   index with IMAD: the whole reduction is exact integer arithmetic until
+//   one final double-precision multiply by the fp16 row (or super-block)
+//   scale and 2^-S_t.
+// * So every output is independent of reduction order and of how pairs are
+//   grouped: a sorted or unioned call is bit-identical to the per-pair call,
+//   and the only approximation is x's 22-bit rounding.
+// * Routing is on the device: pairs are bucketed by expert and each distinct
+//   expert's rows are streamed once for all pairs that selected it (the
+//   reference's "union" formulation, src/mlx_iqk/kernels.py:484-572, for
+//   every member).
 //
-// Work unit: one warp owns a 16-row tile of one expert for one "pair tile"
-// (2 pairs for IQ2_KS / IQ1_S_R4, 1 pair for IQ2_K whose two 16-weight
-// sub-blocks per k-step occupy two operand columns each). Weight streams go
-// through a per-warp cp.async ring in shared memory; activation planes are
-// read through L1.
+// Run kernel layout. A CTA item is (expert, 32-row block, pair tile of 2
+// pairs -- 1 for IQ2_K, whose two 16-weight sub-blocks per k-step occupy two
+// operand columns each). The 8 warps split it 2 row tiles x 4 k-quarters, so
+// small decode batches still spread over every SM. Each "round" moves, for
+// every warp, one 512-weight chunk of its 16 rows plus the matching slice of
+// the activation planes into a 4-stage cp.async ring; the first round of an
+// item also brings the item's scale streams. Per round each warp expands the
+// group metadata (alphabet nibble mask, scale indices) into shared memory
+// once, then runs 16 MMA k-steps. Partials of the 4 k-quarters are summed in
+// a fixed order, so results stay deterministic.
 #include "iqk_common.cuh"
 #include "iqk_gemv.cuh"
 #include "iqk_tables.cuh"
@@ -56,23 +62,18 @@ __device__ __forceinline__ void mma_s8(int32_t d[4], const uint32_t a[4], uint32
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
 }
 
-__device__ __forceinline__ uint2 ldg_nc_u2(const void *p) {
-    uint2 v;
-    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "l"(p));
-    return v;
-}
-
 // ------------------------------------------------------------- prep kernel
 
-// One block per activation row: digit planes + block sums + exponent.
-// The last block routes the pairs.
+// One block per activation row: digit planes, block sums and the exponent.
+// Row layout in the workspace: planes [n/32 k-steps][3][4 lanes][8 bytes]
+// (bytes 0-3: the lane's even k, 4-7: odd k), then block sums [n/32][4] int32.
 template <typename XT>
 __device__ void prep_row(const XT *__restrict__ x, int n, int row, const GemvLayout &L,
                          char *ws) {
     __shared__ float red_max[32];
     __shared__ int red_bad[32];
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const int noct = n / 8;  // octets: (k-step s = q / 4, tig = q % 4)
+    const int noct = n / 8;  // octets: (k-step s = q / 4, lane-in-quad = q % 4)
     const XT *xr = x + (int64_t)row * n;
     float v[2][8];
     float amax = 0.f;
@@ -122,13 +123,12 @@ __device__ void prep_row(const XT *__restrict__ x, int n, int row, const GemvLay
     if (tid == 0) {
         int32_t *xs = reinterpret_cast<int32_t *>(ws + L.xscale);
         xs[row] = bad ? kScaleNonFinite : S;
-        if (bad) atomicOr(reinterpret_cast<int32_t *>(ws + L.hdr), IQK_DEVERR_NONFINITE);
     }
     int8_t *xb = reinterpret_cast<int8_t *>(ws + L.xbuf) + (int64_t)row * L.xrow_bytes;
 #pragma unroll
     for (int it = 0; it < 2; ++it) {
         const int q = tid + it * blockDim.x;
-        if (q >= noct) continue;  // uniform per quad: noct is a multiple of 4
+        if (q >= noct) continue;  // uniform per warp: noct is a multiple of 256
         const int s = q >> 2, tig = q & 3;
         uint32_t planes[3][2] = {{0, 0}, {0, 0}, {0, 0}};
         int bsum[3] = {0, 0, 0};
@@ -140,14 +140,13 @@ __device__ void prep_row(const XT *__restrict__ x, int n, int row, const GemvLay
             const int mid = ((r1 + 128) & 255) - 128;
             const int hi = (r1 - mid) >> 8;
             const int dig[3] = {hi, mid, lo};
-            // byte j/2 of word (j & 1): even k in word 0, odd k in word 1
 #pragma unroll
             for (int p = 0; p < 3; ++p) {
                 planes[p][j & 1] |= (uint32_t)(uint8_t)(int8_t)dig[p] << (8 * (j >> 1));
                 bsum[p] += dig[p];
             }
         }
-        int8_t *dst = xb + (int64_t)s * 128;
+        int8_t *dst = xb + (int64_t)s * 96;
 #pragma unroll
         for (int p = 0; p < 3; ++p)
             *reinterpret_cast<uint2 *>(dst + p * 32 + tig * 8) = make_uint2(planes[p][0], planes[p][1]);
@@ -158,28 +157,60 @@ __device__ void prep_row(const XT *__restrict__ x, int n, int row, const GemvLay
             bsum[p] += __shfl_xor_sync(0xffffffffu, bsum[p], 2);
         }
         if (tig == 0)
-            *reinterpret_cast<int4 *>(dst + 96) = make_int4(bsum[0], bsum[1], bsum[2], 0);
-        else if (tig == 2)
-            *reinterpret_cast<int4 *>(dst + 112) = make_int4(0, 0, 0, 0);
+            *reinterpret_cast<int4 *>(xb + 3 * (int64_t)n + (int64_t)s * 16) =
+                make_int4(bsum[0], bsum[1], bsum[2], 0);
     }
 }
 
-// Route the pairs: bucket by expert (counting sort in shared memory), list
-// distinct experts, and lay out the warp work items.
+// Block-wide exclusive scan of one int per thread (warp shuffles + one
+// shared array of warp totals). Returns the exclusive prefix; *total = sum.
+__device__ __forceinline__ int block_exclusive_scan(int v, int *warp_tot, int *total) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += t;
+    }
+    if (lane == 31) warp_tot[wid] = inc;
+    __syncthreads();
+    if (wid == 0) {
+        const int w = lane < nw ? warp_tot[lane] : 0;
+        int winc = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, winc, o);
+            if (lane >= o) winc += t;
+        }
+        if (lane < nw) warp_tot[lane] = winc - w;  // exclusive warp offsets
+        if (lane == nw - 1) warp_tot[32] = winc;
+    }
+    __syncthreads();
+    const int excl = warp_tot[wid] + inc - v;
+    *total = warp_tot[32];
+    __syncthreads();
+    return excl;
+}
+
+// Route the pairs: bucket by expert (counting sort in shared memory), then
+// lay out two tile lists -- pairs grouped two by two per expert (IQ2_KS,
+// IQ1_S_R4) and one by one (IQ2_K). Pairs whose expert or row index is out of
+// range go to the tail of `order` (the run kernel zeroes their outputs) and
+// set the device error word.
 __device__ void route_pairs(const int32_t *__restrict__ sel, const int32_t *__restrict__ tok,
-                            int pairs, int x_rows, int num_experts, int out_features,
-                            int ppt, const GemvLayout &L, char *ws, void *y, int y_elem) {
+                            int pairs, int x_rows, int num_experts, const GemvLayout &L,
+                            char *ws) {
     extern __shared__ int32_t hist[];  // [num_experts]
-    __shared__ int32_t s_part[1024];
-    __shared__ int32_t s_total[2];
+    __shared__ int32_t warp_tot[33];
+    __shared__ int32_t s_bad, s_tail;
     const int tid = threadIdx.x, nt = blockDim.x;
     int32_t *hdr = reinterpret_cast<int32_t *>(ws + L.hdr);
-    int32_t *uniq = reinterpret_cast<int32_t *>(ws + L.uniq);
-    int32_t *seg = reinterpret_cast<int32_t *>(ws + L.seg);
-    int32_t *ubase = reinterpret_cast<int32_t *>(ws + L.ubase);
     int32_t *order = reinterpret_cast<int32_t *>(ws + L.order);
     int32_t *ptok = reinterpret_cast<int32_t *>(ws + L.ptok);
+    TileRef *tiles2 = reinterpret_cast<TileRef *>(ws + L.tiles2);
+    TileRef *tiles1 = reinterpret_cast<TileRef *>(ws + L.tiles1);
     for (int e = tid; e < num_experts; e += nt) hist[e] = 0;
+    if (tid == 0) s_bad = 0;
     __syncthreads();
     const int dims = tok ? 1 : pairs / x_rows;
     int err = 0;
@@ -190,76 +221,62 @@ __device__ void route_pairs(const int32_t *__restrict__ sel, const int32_t *__re
         if (e < 0 || e >= num_experts) err |= IQK_DEVERR_EXPERT;
         else if (t < 0 || t >= x_rows) err |= IQK_DEVERR_TOKEN;
         else atomicAdd(&hist[e], 1);
-        if (e < 0 || e >= num_experts || t < 0 || t >= x_rows) {
-            // zero the output row of an unroutable pair
-            char *yr = static_cast<char *>(y) + (int64_t)p * out_features * y_elem;
-            for (int i = 0; i < out_features * y_elem; i += 4)
-                *reinterpret_cast<int32_t *>(yr + i) = 0;
-        }
     }
-    if (err) atomicOr(&hdr[0], err);
+    if (err) atomicOr(&s_bad, err);
     __syncthreads();
-    // Exclusive scans over experts of (count) and (distinct flag) and of the
-    // item count ceil(count / ppt); thread-contiguous bins, then a block scan.
+    // Thread-contiguous bins; scans of (routable pairs, tiles of 2).
     const int per = (num_experts + nt - 1) / nt;
-    const int b0 = tid * per, b1 = min(b0 + per, num_experts);
-    int c_cnt = 0, c_u = 0, c_items = 0;
+    const int b0 = min(tid * per, num_experts), b1 = min(b0 + per, num_experts);
+    int c_cnt = 0, c_t2 = 0;
     for (int e = b0; e < b1; ++e) {
         const int c = hist[e];
         c_cnt += c;
-        c_u += c > 0;
-        c_items += (c + ppt - 1) / ppt;
+        c_t2 += (c + 1) >> 1;
     }
-    // pack three sums: do the scan three times through s_part (simple, once per call)
-    int scans[3] = {c_cnt, c_u, c_items};
-    int excl[3];
-    for (int k = 0; k < 3; ++k) {
-        s_part[tid] = scans[k];
-        __syncthreads();
-        for (int off = 1; off < nt; off <<= 1) {
-            const int add = tid >= off ? s_part[tid - off] : 0;
-            __syncthreads();
-            s_part[tid] += add;
-            __syncthreads();
+    int n_valid, n_t2;
+    const int base_cnt = block_exclusive_scan(c_cnt, warp_tot, &n_valid);
+    const int base_t2 = block_exclusive_scan(c_t2, warp_tot, &n_t2);
+    // scatter cursors: first position of each expert's pairs
+    {
+        int run = base_cnt;
+        for (int e = b0; e < b1; ++e) {
+            const int c = hist[e];
+            hist[e] = run;
+            run += c;
         }
-        excl[k] = s_part[tid] - scans[k];
-        if (tid == nt - 1) {
-            if (k == 1) s_total[0] = s_part[tid];
-            if (k == 2) s_total[1] = s_part[tid];
-        }
-        __syncthreads();
     }
-    const int rtiles = out_features / 16;
-    int run_cnt = excl[0], run_u = excl[1], run_items = excl[2];
-    for (int e = b0; e < b1; ++e) {
-        const int c = hist[e];
-        if (c > 0) {
-            uniq[run_u] = e;
-            seg[run_u] = run_cnt;
-            ubase[run_u] = run_items * rtiles;
-            ++run_u;
-        }
-        hist[e] = run_cnt;  // becomes the scatter cursor
-        run_cnt += c;
-        run_items += (c + ppt - 1) / ppt;
-    }
-    __syncthreads();
-    if (tid == nt - 1) {
-        // the last thread's running count is the number of routable pairs
-        const int U = s_total[0];
-        const int items = s_total[1] * rtiles;
-        hdr[1] = U;
-        hdr[2] = items;
-        seg[U] = run_cnt;
-        ubase[U] = items;
+    if (tid == 0) {
+        hdr[0] = s_bad;
+        hdr[2] = n_t2;     // tiles of 2 pairs (IQ2_KS, IQ1_S_R4)
+        hdr[3] = n_valid;  // tiles of 1 pair (IQ2_K) == routable pairs
+        s_tail = n_valid;
     }
     __syncthreads();
     for (int p = tid; p < pairs; p += nt) {
         const int e = sel[p];
         const int t = ptok[p];
-        if (e >= 0 && e < num_experts && t >= 0 && t < x_rows) {
-            const int pos = atomicAdd(&hist[e], 1);
-            order[pos] = p;
+        const bool ok = e >= 0 && e < num_experts && t >= 0 && t < x_rows;
+        const int pos = ok ? atomicAdd(&hist[e], 1) : atomicAdd(&s_tail, 1);
+        order[pos] = p;
+    }
+    __syncthreads();
+    // Tile lists, expert by expert (each thread owns its bin range again;
+    // hist[e] now holds the end of expert e's segment).
+    {
+        int run = base_cnt, run2 = base_t2;
+        for (int e = b0; e < b1; ++e) {
+            const int end = hist[e];
+            for (int q = run; q < end; ++q) {
+                const int p = order[q];
+                tiles1[q] = TileRef{e, p, -1, ptok[p], -1, 0, 0, 1};
+            }
+            for (int q = run; q < end; q += 2) {
+                const int p0 = order[q];
+                const int p1 = q + 1 < end ? order[q + 1] : -1;
+                tiles2[run2++] = TileRef{e, p0, p1, ptok[p0], p1 >= 0 ? ptok[p1] : -1, 0, 0,
+                                         p1 >= 0 ? 2 : 1};
+            }
+            run = end;
         }
     }
 }
@@ -267,40 +284,50 @@ __device__ void route_pairs(const int32_t *__restrict__ sel, const int32_t *__re
 template <typename XT>
 __global__ void __launch_bounds__(256)
 gemv_prep_kernel(const XT *__restrict__ x, int n, int x_rows, const int32_t *__restrict__ sel,
-                 const int32_t *__restrict__ tok, int pairs, int num_experts,
-                 int out_features, int ppt, GemvLayout L, char *__restrict__ ws, void *y,
-                 int y_elem) {
+                 const int32_t *__restrict__ tok, int pairs, int num_experts, GemvLayout L,
+                 char *__restrict__ ws) {
     if ((int)blockIdx.x < x_rows) {
         prep_row<XT>(x, n, blockIdx.x, L, ws);
     } else {
-        route_pairs(sel, tok, pairs, x_rows, num_experts, out_features, ppt, L, ws, y, y_elem);
+        route_pairs(sel, tok, pairs, x_rows, num_experts, L, ws);
     }
 }
 
-// ------------------------------------------------------------- gemv kernel
+// -------------------------------------------------------------- run kernel
 
 constexpr int kWarps = 8;
+constexpr int kKSplit = 4;                    // warps sharing one row tile along k
+constexpr int kRowTiles = kWarps / kKSplit;   // 16-row tiles per CTA item
+constexpr int kItemRows = 16 * kRowTiles;     // 32
 constexpr int kStages = 4;
-constexpr int kChunkK = 512;         // weights per row per ring stage
-constexpr int kStepsPerChunk = 16;   // 32-weight k-steps per stage
+constexpr int kChunkK = 512;                  // weights per row per round and warp
+constexpr int kSteps = kChunkK / 32;          // MMA k-steps per round
+constexpr int kMaxTiles = 256;                // tile entries cached in shared memory
 
 template <int MEMBER> struct Geo {
-    // ring stage: 16 rows of the main code stream for kChunkK weights
-    static constexpr int kRowChunkBytes = MEMBER == IQK_IQ1_S_R4 ? 64 : 128;
-    static constexpr int kRowStride = MEMBER == IQK_IQ1_S_R4 ? 80 : 144;  // bank-staggered
-    static constexpr int kStageBytes = 16 * kRowStride;
+    static constexpr int kPpt = MEMBER == IQK_IQ2_K ? 1 : 2;                 // pairs per tile
+    static constexpr int kRowChunk = MEMBER == IQK_IQ1_S_R4 ? 64 : 128;      // qs bytes
+    static constexpr int kRowStride = MEMBER == IQK_IQ1_S_R4 ? 80 : 144;     // bank-staggered
+    static constexpr int kWBytes = kWarps * 16 * kRowStride;
+    static constexpr int kXPlanes = kSteps * 96;                             // 3 planes
+    static constexpr int kXSums = MEMBER == IQK_IQ1_S_R4 ? kSteps * 16 : 0;  // block sums
+    static constexpr int kXBlock = kXPlanes + kXSums;                        // per (ks, pair)
+    static constexpr int kStageBytes = kWBytes + kKSplit * kPpt * kXBlock;
+    static constexpr int kMetaEntry = MEMBER == IQK_IQ2_K ? 32 : 16;
+    static constexpr int kMetaBytes = kSteps * 8 * kMetaEntry;               // per warp
 };
 
-// Per-warp scale-stream block for one 16-row tile, all streams but qs.
-template <int MEMBER> __host__ __device__ constexpr int scale_block_bytes(int n) {
-    return MEMBER == IQK_IQ2_KS ? 16 * (n / 64 + n / 256 + n / 256) + 32
-           : MEMBER == IQK_IQ2_K ? 16 * (n / 32 + n / 128 + n / 128)
-                                 : 16 * (n / 16) + 32;
+// Scale streams of one CTA item (kItemRows rows, whole k), all but qs.
+template <int MEMBER> __host__ __device__ constexpr int slot_bytes(int n) {
+    return MEMBER == IQK_IQ2_KS ? kItemRows * (n / 64 + n / 256 + n / 256) + 2 * kItemRows
+           : MEMBER == IQK_IQ2_K ? kItemRows * (n / 32 + n / 128 + n / 128)
+                                 : kItemRows * (n / 16) + 2 * kItemRows;
 }
 
-template <int MEMBER>
-__host__ __device__ constexpr int gemv_smem_bytes(int n) {
-    return kWarps * (kStages * Geo<MEMBER>::kStageBytes + 2 * scale_block_bytes<MEMBER>(n)) +
+template <int MEMBER> __host__ __device__ constexpr int gemv_smem_bytes(int n) {
+    using G = Geo<MEMBER>;
+    return kStages * G::kStageBytes + kStages * slot_bytes<MEMBER>(n) + kWarps * G::kMetaBytes +
+           kWarps * 32 * 4 * 4 + kWarps * 32 * 2 * 8 + kMaxTiles * (int)sizeof(TileRef) +
            (MEMBER == IQK_IQ1_S_R4 ? 4096 : 0);
 }
 
@@ -308,346 +335,362 @@ struct GemvArgs {
     const void *s[5];
     int64_t out_features;
     int n;
-    int x_rows;
+    int pairs;
     GemvLayout L;
     const char *ws;
     void *y;
     int y_dtype;
 };
 
+__device__ __forceinline__ uint32_t lds_u16(const void *p) {
+    return *reinterpret_cast<const uint16_t *>(p);
+}
+
 template <int MEMBER>
 __global__ void __launch_bounds__(kWarps * 32, 1)
 gemv_kernel(GemvArgs a) {
-    extern __shared__ __align__(16) char smem[];
+    extern __shared__ __align__(128) char smem[];
     using G = Geo<MEMBER>;
+    constexpr int ppt = G::kPpt;
     const int n = a.n;
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int64_t out = a.out_features;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const int g = lane >> 2, tig = lane & 3;
-    const int sbb = scale_block_bytes<MEMBER>(n);
-    char *wsm = smem + wid * (kStages * G::kStageBytes + 2 * sbb);
-    char *ring = wsm;
-    char *scal = wsm + kStages * G::kStageBytes;
-    uint16_t *grid = reinterpret_cast<uint16_t *>(smem + kWarps * (kStages * G::kStageBytes + 2 * sbb));
-    if (MEMBER == IQK_IQ1_S_R4) {
-        for (int i = threadIdx.x; i < 2048; i += blockDim.x) grid[i] = g_iq1s_grid[i];
-        __syncthreads();
-    }
+    const int rt = wid / kKSplit, ks = wid % kKSplit;
+    const int cpw = n / (kChunkK * kKSplit);  // rounds per item: 2 (n=4096) or 1 (2048)
+    const int SB = slot_bytes<MEMBER>(n);
+
+    char *stages = smem;
+    char *slots = stages + kStages * G::kStageBytes;
+    char *metas = slots + kStages * SB;
+    int32_t *red_i = reinterpret_cast<int32_t *>(metas + kWarps * G::kMetaBytes);
+    double *red_d = reinterpret_cast<double *>(red_i + kWarps * 32 * 4);
+    TileRef *tcache = reinterpret_cast<TileRef *>(red_d + kWarps * 32 * 2);
+    uint16_t *grid = reinterpret_cast<uint16_t *>(tcache + kMaxTiles);
+    char *meta = metas + wid * G::kMetaBytes;
 
     const int32_t *hdr = reinterpret_cast<const int32_t *>(a.ws + a.L.hdr);
-    const int32_t *uniq = reinterpret_cast<const int32_t *>(a.ws + a.L.uniq);
-    const int32_t *seg = reinterpret_cast<const int32_t *>(a.ws + a.L.seg);
-    const int32_t *ubase = reinterpret_cast<const int32_t *>(a.ws + a.L.ubase);
     const int32_t *order = reinterpret_cast<const int32_t *>(a.ws + a.L.order);
-    const int32_t *ptok = reinterpret_cast<const int32_t *>(a.ws + a.L.ptok);
     const int32_t *xscale = reinterpret_cast<const int32_t *>(a.ws + a.L.xscale);
-    const int8_t *xbuf = reinterpret_cast<const int8_t *>(a.ws + a.L.xbuf);
+    const TileRef *tlist = reinterpret_cast<const TileRef *>(a.ws + (ppt == 2 ? a.L.tiles2 : a.L.tiles1));
+    const char *xbuf = a.ws + a.L.xbuf;
+    const int64_t xrow = a.L.xrow_bytes;
 
-    const int U = hdr[1];
-    const int items = hdr[2];
-    const int nwarps = gridDim.x * kWarps;
-    const int gw = blockIdx.x * kWarps + wid;
-    const int i0 = (int)((int64_t)items * gw / nwarps);
-    const int i1 = (int)((int64_t)items * (gw + 1) / nwarps);
-    if (i0 >= i1) return;
-    const int chunks = n / kChunkK;
-    const int rtiles = (int)(a.out_features / 16);
-    constexpr int ppt = MEMBER == IQK_IQ2_K ? 1 : 2;
+    const int ntiles = ppt == 2 ? hdr[2] : hdr[3];
+    const int rblocks = (int)((out + kItemRows - 1) / kItemRows);
+    const int items = ntiles * rblocks;
 
-    // Resolve an item into (expert, first row, pair tile) -------------------
-    struct Item {
-        int e, r0, pfirst, npair;
-    };
-    auto resolve = [&](int i) -> Item {
-        int lo = 0, hi = U;  // ubase[lo] <= i < ubase[hi]
-        while (hi - lo > 1) {
-            const int mid = (lo + hi) >> 1;
-            if (ubase[mid] <= i) lo = mid;
-            else hi = mid;
+    if (blockIdx.x == 0) {
+        // zero the outputs of unroutable pairs (the tail of order)
+        const int nvalid = hdr[3];
+        const int elem = a.y_dtype == IQK_F32 ? 4 : 2;
+        const int row_words = (int)(out * elem / 4);
+        for (int q = nvalid; q < a.pairs; ++q) {
+            int32_t *yr = reinterpret_cast<int32_t *>(static_cast<char *>(a.y) +
+                                                      (int64_t)order[q] * out * elem);
+            for (int i = tid; i < row_words; i += blockDim.x) yr[i] = 0;
         }
-        const int cnt = seg[lo + 1] - seg[lo];
-        const int ntile = (cnt + ppt - 1) / ppt;
-        const int local = i - ubase[lo];
-        const int rt = local / ntile, pt = local - rt * ntile;
-        Item it;
-        it.e = uniq[lo];
-        it.r0 = rt * 16;
-        it.pfirst = seg[lo] + pt * ppt;
-        it.npair = min(ppt, cnt - pt * ppt);
-        return it;
+    }
+    const int i0 = (int)((int64_t)items * blockIdx.x / gridDim.x);
+    const int i1 = (int)((int64_t)items * (blockIdx.x + 1) / gridDim.x);
+    if (i0 >= i1) return;  // uniform over the CTA
+    const int t0 = i0 / rblocks, t1 = (i1 - 1) / rblocks;
+    const bool cached = t1 - t0 < kMaxTiles;
+    auto load_tile = [&](int t) -> TileRef {
+        TileRef r = tlist[t];
+        r.sh0 = xscale[r.tok0];
+        r.sh1 = r.tok1 >= 0 ? xscale[r.tok1] : 0;
+        return r;
     };
+    if (cached)
+        for (int t = tid; t <= t1 - t0; t += blockDim.x) tcache[t] = load_tile(t0 + t);
+    if (MEMBER == IQK_IQ1_S_R4)
+        for (int i = tid; i < 2048; i += blockDim.x) grid[i] = g_iq1s_grid[i];
+    __syncthreads();
+    auto tile_of = [&](int t) -> TileRef { return cached ? tcache[t - t0] : load_tile(t); };
 
-    // Issue one ring stage (item, chunk); chunk 0 also brings the scale block.
-    auto issue = [&](int stage_idx, const Item &it, int item_ord, int c) {
-        const int64_t rowbase = (int64_t)it.e * a.out_features + it.r0;
-        char *dst = ring + (stage_idx % kStages) * G::kStageBytes;
-        const char *qs = static_cast<const char *>(a.s[0]);
-        const int qrow = MEMBER == IQK_IQ1_S_R4 ? n / 8 : n / 4;  // bytes per qs row
-        constexpr int per_row = G::kRowChunkBytes / 16;
-        for (int i = lane; i < 16 * per_row; i += 32) {
-            const int r = i / per_row, q = i - r * per_row;
-            cp_async16(dst + r * G::kRowStride + q * 16,
-                       qs + (rowbase + r) * qrow + (int64_t)c * G::kRowChunkBytes + q * 16);
+    const char *qs = static_cast<const char *>(a.s[0]);
+    const int64_t qrow = MEMBER == IQK_IQ1_S_R4 ? n / 8 : n / 4;  // qs bytes per row
+    const RowBytes rbs = row_bytes(MEMBER, n);
+
+    // Issue round j: every warp's chunk of weights, the activation slices,
+    // and (first round of an item) the item's scale streams.
+    auto issue = [&](int j) {
+        const int o = j / cpw, r = j - o * cpw, i = i0 + o;
+        const TileRef T = tile_of(i / rblocks);
+        const int64_t r0 = (int64_t)(i % rblocks) * kItemRows;
+        const int rows_valid = (int)min((int64_t)kItemRows, out - r0);
+        char *st = stages + (j % kStages) * G::kStageBytes;
+        constexpr int per_row = G::kRowChunk / 16;
+        for (int q = tid; q < kWarps * 16 * per_row; q += blockDim.x) {
+            const int w = q / (16 * per_row), rem = q - w * 16 * per_row;
+            const int row = rem / per_row, part = rem - row * per_row;
+            const int lr = 16 * (w / kKSplit) + row;
+            if (lr >= rows_valid) continue;
+            const int c = (w % kKSplit) * cpw + r;
+            cp_async16(st + (w * 16 + row) * G::kRowStride + part * 16,
+                       qs + ((int64_t)T.e * out + r0 + lr) * qrow + c * G::kRowChunk + part * 16);
         }
-        if (c == 0) {
-            char *sd = scal + (item_ord & 1) * sbb;
+        char *xs = st + G::kWBytes;
+        constexpr int xparts = G::kXBlock / 16;
+        for (int q = tid; q < kKSplit * ppt * xparts; q += blockDim.x) {
+            const int blk = q / xparts, part = q - blk * xparts;
+            const int ksx = blk / ppt, t = blk - ksx * ppt;
+            const int tk = t == 0 ? T.tok0 : T.tok1;
+            if (tk < 0) continue;
+            const int c = ksx * cpw + r;
+            const char *src = part < G::kXPlanes / 16
+                                  ? xbuf + tk * xrow + (int64_t)c * G::kXPlanes + part * 16
+                                  : xbuf + tk * xrow + 3 * (int64_t)n + (int64_t)c * kSteps * 16 +
+                                        (part - G::kXPlanes / 16) * 16;
+            cp_async16(xs + blk * G::kXBlock + part * 16, src);
+        }
+        if (r == 0) {
+            char *sd = slots + (o % kStages) * SB;
             int off = 0;
-            const RowBytes rb = row_bytes(MEMBER, n);
-            for (int si = 1; si < rb.count; ++si) {
-                const int bytes = (int)(16 * rb.b[si]);
-                const char *src = static_cast<const char *>(a.s[si]) + rowbase * rb.b[si];
-                for (int i = lane * 16; i < bytes; i += 32 * 16) cp_async16(sd + off + i, src + i);
-                off += bytes;
+            for (int si = 1; si < rbs.count; ++si) {
+                const int bytes = (int)(rows_valid * rbs.b[si]);
+                const char *src = static_cast<const char *>(a.s[si]) + ((int64_t)T.e * out + r0) * rbs.b[si];
+                for (int q = tid * 16; q < bytes; q += blockDim.x * 16) cp_async16(sd + off + q, src + q);
+                off += (int)(kItemRows * rbs.b[si]);
             }
         }
     };
 
-    const int total_stages = (i1 - i0) * chunks;
-    // stage index j -> (item ordinal j / chunks, chunk j % chunks)
-    Item it_issue = resolve(i0);
-    int issue_ord = 0;
+    const int total_rounds = (i1 - i0) * cpw;
 #pragma unroll 1
     for (int j = 0; j < kStages - 1; ++j) {
-        if (j < total_stages) {
-            const int ord = j / chunks, c = j - ord * chunks;
-            if (ord != issue_ord) {
-                issue_ord = ord;
-                it_issue = resolve(i0 + ord);
-            }
-            issue(j, it_issue, ord, c);
-        }
+        if (j < total_rounds) issue(j);
         cp_async_commit();
     }
 
-    // Per-item state
-    Item it{};
     int32_t tot[4] = {0, 0, 0, 0};
-    double acc_g[2] = {0.0, 0.0}, acc_g8[2] = {0.0, 0.0};  // IQ2_K super-block sums
-    const int8_t *xcol = nullptr;  // activation planes for this lane's B column
-    bool col_live = false;
-    int tok_t[2] = {-1, -1};
-    int pair_t[2] = {-1, -1};
+    double dacc[2] = {0.0, 0.0};  // IQ2_K: rows g, g+8 (lanes with tig == 0)
 
 #pragma unroll 1
-    for (int j = 0; j < total_stages; ++j) {
-        const int ord = j / chunks, c = j - ord * chunks;
-        if (c == 0) {
-            it = resolve(i0 + ord);
-            for (int t = 0; t < 2; ++t) {
-                pair_t[t] = t < it.npair ? order[it.pfirst + t] : -1;
-                tok_t[t] = pair_t[t] >= 0 ? ptok[pair_t[t]] : -1;
-            }
-            // B column of this lane: IQ2_KS / IQ1: col g = 4*t + plane;
-            // IQ2_K: col g = 2*plane + half (1 pair per tile).
-            int t, p;
-            if (MEMBER == IQK_IQ2_K) {
-                t = 0;
-                p = g >> 1;
-                col_live = p < 3 && (g & 1) == (tig >> 1) && tok_t[0] >= 0;
-            } else {
-                t = g >> 2;
-                p = g & 3;
-                col_live = p < 3 && tok_t[t] >= 0;
-            }
-            xcol = col_live ? xbuf + (int64_t)tok_t[t] * a.L.xrow_bytes + p * 32 + tig * 8 : nullptr;
-            tot[0] = tot[1] = tot[2] = tot[3] = 0;
-            acc_g[0] = acc_g[1] = acc_g8[0] = acc_g8[1] = 0.0;
-        }
+    for (int j = 0; j < total_rounds; ++j) {
+        const int o = j / cpw, r = j - o * cpw, i = i0 + o;
+        const TileRef T = tile_of(i / rblocks);
+        const int64_t r0 = (int64_t)(i % rblocks) * kItemRows;
         cp_async_wait<kStages - 2>();
-        __syncwarp();
-        // Refill the slot consumed in the previous iteration, S-1 stages ahead.
-        {
-            const int jn = j + kStages - 1;
-            if (jn < total_stages) {
-                const int ordn = jn / chunks, cn = jn - ordn * chunks;
-                if (ordn != issue_ord) {
-                    issue_ord = ordn;
-                    it_issue = resolve(i0 + ordn);
-                }
-                issue(jn, it_issue, ordn, cn);
-            }
-            cp_async_commit();
+        __syncthreads();
+        if (j + kStages - 1 < total_rounds) issue(j + kStages - 1);
+        cp_async_commit();
+        if (r == 0) {
+            tot[0] = tot[1] = tot[2] = tot[3] = 0;
+            dacc[0] = dacc[1] = 0.0;
         }
-
-        const char *st = ring + (j % kStages) * G::kStageBytes;
-        const char *sd = scal + (ord & 1) * sbb;
-        // B fragments for the 16 k-steps of this chunk
-        uint32_t bf[kStepsPerChunk][2];
+        const bool live = 16 * rt < out - r0;  // this warp's row tile exists
+        const char *st = stages + (j % kStages) * G::kStageBytes;
+        const char *sd = slots + (o % kStages) * SB;
+        const int c = ks * cpw + r;  // chunk of this warp
+        if (live) {
+            // ---- expand group metadata for this warp's 16 rows x 16 k-steps
+            {
+                const int mg = lane & 7, mq = lane >> 3;  // row pair, quad of k-steps
+                const int ra = 16 * rt + mg, rb = ra + 8;  // item-local rows g, g+8
 #pragma unroll
-        for (int ls = 0; ls < kStepsPerChunk; ++ls) {
-            if (col_live) {
-                const uint2 v = ldg_nc_u2(xcol + (int64_t)(c * kStepsPerChunk + ls) * 128);
-                bf[ls][0] = v.x;
-                bf[ls][1] = v.y;
-            } else {
-                bf[ls][0] = bf[ls][1] = 0;
-            }
-        }
-        // IQ1_S_R4: block sums of this lane's two C columns (token tig>>1,
-        // planes 2*(tig&1) and +1; plane 3 reads the stored zero).
-        int32_t xbs[MEMBER == IQK_IQ1_S_R4 ? kStepsPerChunk : 1][2];
-        if (MEMBER == IQK_IQ1_S_R4) {
-            const int ct = tig >> 1, cp = 2 * (tig & 1);
-#pragma unroll
-            for (int ls = 0; ls < kStepsPerChunk; ++ls) {
-                if (tok_t[ct] >= 0) {
-                    const uint2 v = ldg_nc_u2(xbuf + (int64_t)tok_t[ct] * a.L.xrow_bytes +
-                                              (int64_t)(c * kStepsPerChunk + ls) * 128 + 96 + cp * 4);
-                    xbs[ls][0] = (int32_t)v.x;
-                    xbs[ls][1] = (int32_t)v.y;
-                } else {
-                    xbs[ls][0] = xbs[ls][1] = 0;
-                }
-            }
-        }
-
-#pragma unroll
-        for (int ls = 0; ls < kStepsPerChunk; ++ls) {
-            const int s = c * kStepsPerChunk + ls;  // global k-step (32 weights)
-            uint32_t A[4];
-            if (MEMBER == IQK_IQ1_S_R4) {
-                const uint32_t qg = *reinterpret_cast<const uint32_t *>(st + g * G::kRowStride + ls * 4);
-                const uint32_t qg8 = *reinterpret_cast<const uint32_t *>(st + (g + 8) * G::kRowStride + ls * 4);
-                const uint16_t *qh = reinterpret_cast<const uint16_t *>(sd);
-                const uint32_t hg = qh[g * (n / 32) + s];
-                const uint32_t hg8 = qh[(g + 8) * (n / 32) + s];
-                const uint32_t ig = ((qg >> (8 * tig)) & 0xffu) | (((hg >> (3 * tig)) & 7u) << 8);
-                const uint32_t ig8 = ((qg8 >> (8 * tig)) & 0xffu) | (((hg8 >> (3 * tig)) & 7u) << 8);
-                const uint32_t v = (uint32_t)grid[ig] | ((uint32_t)grid[ig8] << 16);
-                const uint32_t s0 = v & 0x33333333u;
-                const uint32_t s1 = (v >> 2) & 0x33333333u;
-                A[0] = prmt(kTernTab, 0u, s0);
-                A[1] = prmt(kTernTab, 0u, s0 >> 16);
-                A[2] = prmt(kTernTab, 0u, s1);
-                A[3] = prmt(kTernTab, 0u, s1 >> 16);
-                int32_t d[4];
-                mma_s8(d, A, bf[ls][0], bf[ls][1]);
-                const int xb0 = xbs[MEMBER == IQK_IQ1_S_R4 ? ls : 0][0];
-                const int xb1 = xbs[MEMBER == IQK_IQ1_S_R4 ? ls : 0][1];
-                const int mg = 2 * (int)((hg >> 12) & 7u) + 1;
-                const int mg8 = 2 * (int)((hg8 >> 12) & 7u) + 1;
-                const int sg = (hg & 0x8000u) ? -1 : 1;
-                const int sg8 = (hg8 & 0x8000u) ? -1 : 1;
-                tot[0] += mg * (8 * d[0] + sg * xb0);
-                tot[1] += mg * (8 * d[1] + sg * xb1);
-                tot[2] += mg8 * (8 * d[2] + sg8 * xb0);
-                tot[3] += mg8 * (8 * d[3] + sg8 * xb1);
-            } else {
-                const uint32_t wg = *reinterpret_cast<const uint32_t *>(
-                    st + g * G::kRowStride + (2 * ls + (tig >> 1)) * 4);
-                const uint32_t wg8 = *reinterpret_cast<const uint32_t *>(
-                    st + (g + 8) * G::kRowStride + (2 * ls + (tig >> 1)) * 4);
-                const uint32_t v = prmt(wg, wg8, (tig & 1) ? 0x7632u : 0x5410u);
-                int alpha_g, alpha_g8, idx_g0, idx_g1, idx_g80, idx_g81;
-                if (MEMBER == IQK_IQ2_KS) {
-                    const uint8_t *scl = reinterpret_cast<const uint8_t *>(sd);
-                    const uint8_t *sch = scl + 16 * (n / 64);
-                    const uint8_t *sex = sch + 16 * (n / 256);
-                    const int sb = (s & 1) * 4;
-                    const int lo_g = (scl[g * (n / 64) + (s >> 1)] >> sb) & 15;
-                    const int lo_g8 = (scl[(g + 8) * (n / 64) + (s >> 1)] >> sb) & 15;
-                    const int hi_g = (sch[g * (n / 256) + (s >> 3)] >> (s & 7)) & 1;
-                    const int hi_g8 = (sch[(g + 8) * (n / 256) + (s >> 3)] >> (s & 7)) & 1;
-                    alpha_g = (sex[g * (n / 256) + (s >> 3)] >> (s & 7)) & 1;
-                    alpha_g8 = (sex[(g + 8) * (n / 256) + (s >> 3)] >> (s & 7)) & 1;
-                    idx_g0 = idx_g1 = (lo_g | (hi_g << 4)) - 16;
-                    idx_g80 = idx_g81 = (lo_g8 | (hi_g8 << 4)) - 16;
-                } else {
-                    const uint8_t *scl = reinterpret_cast<const uint8_t *>(sd);
-                    const uint8_t *sex = scl + 16 * (n / 32);
-                    const int sbk = 2 * s + (tig >> 1);  // sub-block of this lane's codes
-                    alpha_g = (sex[g * (n / 128) + (sbk >> 3)] >> (sbk & 7)) & 1;
-                    alpha_g8 = (sex[(g + 8) * (n / 128) + (sbk >> 3)] >> (sbk & 7)) & 1;
-                    const int bg = scl[g * (n / 32) + s];
-                    const int bg8 = scl[(g + 8) * (n / 32) + s];
-                    idx_g0 = (bg & 15) - 8;
-                    idx_g1 = (bg >> 4) - 8;
-                    idx_g80 = (bg8 & 15) - 8;
-                    idx_g81 = (bg8 >> 4) - 8;
-                }
-                const uint32_t tab_g = alpha_g ? kIq2Tab1 : kIq2Tab0;
-                const uint32_t tab_g8 = alpha_g8 ? kIq2Tab1 : kIq2Tab0;
-                const uint32_t s0 = (v & 0x33333333u) | 0x44440000u;
-                const uint32_t s1 = ((v >> 2) & 0x33333333u) | 0x44440000u;
-                A[0] = prmt(tab_g, tab_g8, s0);
-                A[1] = prmt(tab_g, tab_g8, s0 >> 16);
-                A[2] = prmt(tab_g, tab_g8, s1);
-                A[3] = prmt(tab_g, tab_g8, s1 >> 16);
-                int32_t d[4];
-                mma_s8(d, A, bf[ls][0], bf[ls][1]);
-                tot[0] += idx_g0 * d[0];
-                tot[1] += idx_g1 * d[1];
-                tot[2] += idx_g80 * d[2];
-                tot[3] += idx_g81 * d[3];
-                if (MEMBER == IQK_IQ2_K && (s & 7) == 7) {
-                    // end of a 256-weight super-block: fold in its fp16 scale
-                    const int sbi = s >> 3;
-                    const uint16_t *dvp = reinterpret_cast<const uint16_t *>(
-                        sd + 16 * (n / 32) + 16 * (n / 128));
-                    const int32_t pg = tot[0] + tot[1], pg8 = tot[2] + tot[3];
-                    const int32_t p1g = __shfl_down_sync(0xffffffffu, pg, 1);
-                    const int32_t p2g = __shfl_down_sync(0xffffffffu, pg, 2);
-                    const int32_t p1g8 = __shfl_down_sync(0xffffffffu, pg8, 1);
-                    const int32_t p2g8 = __shfl_down_sync(0xffffffffu, pg8, 2);
-                    if (tig == 0) {
-                        const double Tg = (double)pg * 65536.0 + (double)p1g * 256.0 + (double)p2g;
-                        const double Tg8 = (double)pg8 * 65536.0 + (double)p1g8 * 256.0 + (double)p2g8;
-                        acc_g[0] += (double)half_bits_to_float(dvp[g * (n / 256) + sbi]) * Tg;
-                        acc_g8[0] += (double)half_bits_to_float(dvp[(g + 8) * (n / 256) + sbi]) * Tg8;
+                for (int u = 0; u < 4; ++u) {
+                    const int ls = mq * 4 + u;
+                    const int s = c * kSteps + ls;  // global k-step
+                    if (MEMBER == IQK_IQ2_KS) {
+                        const uint8_t *scl = reinterpret_cast<const uint8_t *>(sd);
+                        const uint8_t *sch = scl + kItemRows * (n / 64);
+                        const uint8_t *sex = sch + kItemRows * (n / 256);
+                        const int sh = (s & 1) * 4, bi = s >> 3, bb = s & 7;
+                        const int ia = (((scl[ra * (n / 64) + (s >> 1)] >> sh) & 15) |
+                                        (((sch[ra * (n / 256) + bi] >> bb) & 1) << 4)) - 16;
+                        const int ib = (((scl[rb * (n / 64) + (s >> 1)] >> sh) & 15) |
+                                        (((sch[rb * (n / 256) + bi] >> bb) & 1) << 4)) - 16;
+                        const uint32_t am = (((sex[ra * (n / 256) + bi] >> bb) & 1) ? 0x4444u : 0u) |
+                                            (((sex[rb * (n / 256) + bi] >> bb) & 1) ? 0x44440000u : 0u);
+                        *reinterpret_cast<int4 *>(meta + (ls * 8 + mg) * 16) =
+                            make_int4((int)am, ia, ib, 0);
+                    } else if (MEMBER == IQK_IQ2_K) {
+                        const uint8_t *scl = reinterpret_cast<const uint8_t *>(sd);
+                        const uint8_t *sex = scl + kItemRows * (n / 32);
+                        const int ba = scl[ra * (n / 32) + s], bbv = scl[rb * (n / 32) + s];
+                        const int xa = sex[ra * (n / 128) + (s >> 2)] >> ((2 * s) & 7);
+                        const int xb = sex[rb * (n / 128) + (s >> 2)] >> ((2 * s) & 7);
+                        const uint32_t am0 = ((xa & 1) ? 0x4444u : 0u) | ((xb & 1) ? 0x44440000u : 0u);
+                        const uint32_t am1 = ((xa & 2) ? 0x4444u : 0u) | ((xb & 2) ? 0x44440000u : 0u);
+                        int4 *m = reinterpret_cast<int4 *>(meta + (ls * 8 + mg) * 32);
+                        m[0] = make_int4((int)am0, (int)am1, 0, 0);
+                        m[1] = make_int4((ba & 15) - 8, (ba >> 4) - 8, (bbv & 15) - 8, (bbv >> 4) - 8);
+                    } else {
+                        const uint16_t *qh = reinterpret_cast<const uint16_t *>(sd);
+                        const uint32_t ha = qh[ra * (n / 32) + s], hb = qh[rb * (n / 32) + s];
+                        const int ma = 2 * (int)((ha >> 12) & 7u) + 1, mb = 2 * (int)((hb >> 12) & 7u) + 1;
+                        *reinterpret_cast<int4 *>(meta + (ls * 8 + mg) * 16) =
+                            make_int4((int)(ha | (hb << 16)), ma, mb,
+                                      ((ha & 0x8000u) ? 1 : 0) | ((hb & 0x8000u) ? 2 : 0));
                     }
-                    tot[0] = tot[1] = tot[2] = tot[3] = 0;
+                }
+            }
+            __syncwarp();
+
+            // ---- 16 MMA k-steps
+            const char *wb = st + wid * 16 * G::kRowStride;
+            const char *xs = st + G::kWBytes + ks * ppt * G::kXBlock;
+            int bt, bp;
+            bool blive;
+            if (MEMBER == IQK_IQ2_K) {
+                bt = 0;
+                bp = g >> 1;
+                blive = bp < 3 && (g & 1) == (tig >> 1);
+            } else {
+                bt = g >> 2;
+                bp = g & 3;
+                blive = bp < 3 && (bt == 0 ? T.tok0 : T.tok1) >= 0;
+            }
+            const char *xl = xs + bt * G::kXBlock + bp * 32 + tig * 8;
+#pragma unroll 4
+            for (int ls = 0; ls < kSteps; ++ls) {
+                uint32_t A[4];
+                uint2 bv = make_uint2(0u, 0u);
+                if (blive) bv = *reinterpret_cast<const uint2 *>(xl + ls * 96);
+                int32_t d[4];
+                if (MEMBER == IQK_IQ1_S_R4) {
+                    const int4 m = *reinterpret_cast<const int4 *>(meta + (ls * 8 + g) * 16);
+                    const uint32_t qg = *reinterpret_cast<const uint32_t *>(wb + g * G::kRowStride + ls * 4);
+                    const uint32_t qg8 = *reinterpret_cast<const uint32_t *>(wb + (g + 8) * G::kRowStride + ls * 4);
+                    const uint32_t h = (uint32_t)m.x;
+                    const uint32_t ig = ((qg >> (8 * tig)) & 0xffu) | (((h >> (3 * tig)) & 7u) << 8);
+                    const uint32_t ig8 = ((qg8 >> (8 * tig)) & 0xffu) | (((h >> (16 + 3 * tig)) & 7u) << 8);
+                    const uint32_t v = (uint32_t)grid[ig] | ((uint32_t)grid[ig8] << 16);
+                    const uint32_t s0 = v & 0x33333333u;
+                    const uint32_t s1 = (v >> 2) & 0x33333333u;
+                    A[0] = prmt(kTernTab, 0u, s0);
+                    A[1] = prmt(kTernTab, 0u, s0 >> 16);
+                    A[2] = prmt(kTernTab, 0u, s1);
+                    A[3] = prmt(kTernTab, 0u, s1 >> 16);
+                    mma_s8(d, A, bv.x, bv.y);
+                    // block sums of this lane's C columns: token tig>>1,
+                    // planes 2*(tig&1) and +1 (plane 3 is the stored zero)
+                    const int ct = tig >> 1, cp = 2 * (tig & 1);
+                    const int2 xb = *reinterpret_cast<const int2 *>(
+                        xs + ct * G::kXBlock + G::kXPlanes + ls * 16 + cp * 4);
+                    const int sa = (m.w & 1) ? -1 : 1, sb = (m.w & 2) ? -1 : 1;
+                    tot[0] += m.y * (8 * d[0] + sa * xb.x);
+                    tot[1] += m.y * (8 * d[1] + sa * xb.y);
+                    tot[2] += m.z * (8 * d[2] + sb * xb.x);
+                    tot[3] += m.z * (8 * d[3] + sb * xb.y);
+                } else {
+                    const uint32_t hg = lds_u16(wb + g * G::kRowStride + ls * 8 + tig * 2);
+                    const uint32_t hg8 = lds_u16(wb + (g + 8) * G::kRowStride + ls * 8 + tig * 2);
+                    const uint32_t v = hg | (hg8 << 16);
+                    uint32_t am;
+                    int4 ix;
+                    if (MEMBER == IQK_IQ2_KS) {
+                        const int4 m = *reinterpret_cast<const int4 *>(meta + (ls * 8 + g) * 16);
+                        am = (uint32_t)m.x;
+                        ix = make_int4(m.y, m.y, m.z, m.z);
+                    } else {
+                        const char *mp = meta + (ls * 8 + g) * 32;
+                        am = *reinterpret_cast<const uint32_t *>(mp + 4 * (tig >> 1));
+                        ix = *reinterpret_cast<const int4 *>(mp + 16);
+                    }
+                    const uint32_t s0 = (v & 0x33333333u) | am;
+                    const uint32_t s1 = ((v >> 2) & 0x33333333u) | am;
+                    A[0] = prmt(kIq2Tab0, kIq2Tab1, s0);
+                    A[1] = prmt(kIq2Tab0, kIq2Tab1, s0 >> 16);
+                    A[2] = prmt(kIq2Tab0, kIq2Tab1, s1);
+                    A[3] = prmt(kIq2Tab0, kIq2Tab1, s1 >> 16);
+                    mma_s8(d, A, bv.x, bv.y);
+                    tot[0] += ix.x * d[0];
+                    tot[1] += ix.y * d[1];
+                    tot[2] += ix.z * d[2];
+                    tot[3] += ix.w * d[3];
+                    if (MEMBER == IQK_IQ2_K && (ls & 7) == 7) {
+                        // end of a 256-weight super-block: fold in its fp16 scale
+                        const int s = c * kSteps + ls;
+                        const uint16_t *dvp = reinterpret_cast<const uint16_t *>(
+                            sd + kItemRows * (n / 32) + kItemRows * (n / 128));
+                        const int32_t pg = tot[0] + tot[1], pg8 = tot[2] + tot[3];
+                        const int32_t p1g = __shfl_down_sync(0xffffffffu, pg, 1);
+                        const int32_t p2g = __shfl_down_sync(0xffffffffu, pg, 2);
+                        const int32_t p1g8 = __shfl_down_sync(0xffffffffu, pg8, 1);
+                        const int32_t p2g8 = __shfl_down_sync(0xffffffffu, pg8, 2);
+                        if (tig == 0) {
+                            const int ra = 16 * rt + g;
+                            const double Tg = (double)pg * 65536.0 + (double)p1g * 256.0 + (double)p2g;
+                            const double Tg8 = (double)pg8 * 65536.0 + (double)p1g8 * 256.0 + (double)p2g8;
+                            dacc[0] += (double)half_bits_to_float(dvp[ra * (n / 256) + (s >> 3)]) * Tg;
+                            dacc[1] += (double)half_bits_to_float(dvp[(ra + 8) * (n / 256) + (s >> 3)]) * Tg8;
+                        }
+                        tot[0] = tot[1] = tot[2] = tot[3] = 0;
+                    }
                 }
             }
         }
-        __syncwarp();
 
-        if (c == chunks - 1) {
-            // ---- item epilogue: combine digit planes, scale, store
-            const char *sdd = sd;
-            double yg[2], yg8[2];
-            int nt_out;
+        if (r == cpw - 1) {
+            // ---- item end: k-quarter partials -> shared, fixed-order sum, epilogue
+            *reinterpret_cast<int4 *>(red_i + (wid * 32 + lane) * 4) = make_int4(tot[0], tot[1], tot[2], tot[3]);
             if (MEMBER == IQK_IQ2_K) {
-                nt_out = 1;
-                yg[0] = acc_g[0];
-                yg8[0] = acc_g8[0];
-            } else {
-                // lanes with even tig hold planes (0,1) of token tig>>1; odd hold (2, pad)
-                const int32_t n0 = __shfl_down_sync(0xffffffffu, tot[0], 1);
-                const int32_t n2 = __shfl_down_sync(0xffffffffu, tot[2], 1);
-                nt_out = 2;
-                const double Tg = (double)tot[0] * 65536.0 + (double)tot[1] * 256.0 + (double)n0;
-                const double Tg8 = (double)tot[2] * 65536.0 + (double)tot[3] * 256.0 + (double)n2;
-                const uint16_t *dvp = reinterpret_cast<const uint16_t *>(
-                    sdd + (MEMBER == IQK_IQ2_KS ? 16 * (n / 64 + n / 256 + n / 256) : 16 * (n / 16)));
-                const double dg = half_bits_to_float(dvp[g]);
-                const double dg8 = half_bits_to_float(dvp[g + 8]);
-                yg[0] = dg * Tg;
-                yg8[0] = dg8 * Tg8;
+                red_d[(wid * 32 + lane) * 2] = dacc[0];
+                red_d[(wid * 32 + lane) * 2 + 1] = dacc[1];
             }
-            const bool writer = MEMBER == IQK_IQ2_K ? tig == 0 : (tig & 1) == 0;
-            const int t = MEMBER == IQK_IQ2_K ? 0 : tig >> 1;
-            if (writer && t < nt_out && pair_t[t] >= 0) {
-                const int S = xscale[tok_t[t]];
-                const int sh = -S - (MEMBER == IQK_IQ1_S_R4 ? 3 : 0);
-                float vg, vg8;
-                if (S == kScaleNonFinite) {
-                    vg = vg8 = __int_as_float(0x7fc00000);
+            __syncthreads();
+            if (ks == 0 && live) {
+                const int ra = 16 * rt + g;  // item-local row
+                double yg = 0.0, yg8 = 0.0;
+                int t_out;
+                bool writer;
+                if (MEMBER == IQK_IQ2_K) {
+                    for (int k = 0; k < kKSplit; ++k) {
+                        yg += red_d[((rt * kKSplit + k) * 32 + lane) * 2];
+                        yg8 += red_d[((rt * kKSplit + k) * 32 + lane) * 2 + 1];
+                    }
+                    t_out = 0;
+                    writer = tig == 0;
                 } else {
-                    vg = (float)ldexp(yg[0], sh);
-                    vg8 = (float)ldexp(yg8[0], sh);
+                    int32_t s4[4] = {0, 0, 0, 0};
+                    for (int k = 0; k < kKSplit; ++k) {
+                        const int4 pv = *reinterpret_cast<const int4 *>(red_i + ((rt * kKSplit + k) * 32 + lane) * 4);
+                        s4[0] += pv.x;
+                        s4[1] += pv.y;
+                        s4[2] += pv.z;
+                        s4[3] += pv.w;
+                    }
+                    // even-tig lanes hold planes (0,1) of token tig>>1, odd lanes (2, pad)
+                    const int32_t n0 = __shfl_down_sync(0xffffffffu, s4[0], 1);
+                    const int32_t n2 = __shfl_down_sync(0xffffffffu, s4[2], 1);
+                    const double Tg = (double)s4[0] * 65536.0 + (double)s4[1] * 256.0 + (double)n0;
+                    const double Tg8 = (double)s4[2] * 65536.0 + (double)s4[3] * 256.0 + (double)n2;
+                    const uint16_t *dvp = reinterpret_cast<const uint16_t *>(
+                        sd + (MEMBER == IQK_IQ2_KS ? kItemRows * (n / 64 + n / 256 + n / 256)
+                                                   : kItemRows * (n / 16)));
+                    yg = (double)half_bits_to_float(dvp[ra]) * Tg;
+                    yg8 = (double)half_bits_to_float(dvp[ra + 8]) * Tg8;
+                    t_out = tig >> 1;
+                    writer = (tig & 1) == 0;
                 }
-                const int64_t o0 = (int64_t)pair_t[t] * a.out_features + it.r0 + g;
-                if (a.y_dtype == IQK_F32) {
-                    float *y = static_cast<float *>(a.y);
-                    y[o0] = vg;
-                    y[o0 + 8] = vg8;
-                } else if (a.y_dtype == IQK_F16) {
-                    __half *y = static_cast<__half *>(a.y);
-                    y[o0] = __float2half_rn(vg);
-                    y[o0 + 8] = __float2half_rn(vg8);
-                } else {
-                    __nv_bfloat16 *y = static_cast<__nv_bfloat16 *>(a.y);
-                    y[o0] = __float2bfloat16_rn(vg);
-                    y[o0 + 8] = __float2bfloat16_rn(vg8);
+                const int pair = t_out == 0 ? T.pair0 : T.pair1;
+                if (writer && pair >= 0) {
+                    const int S = t_out == 0 ? T.sh0 : T.sh1;
+                    const int shift = -S - (MEMBER == IQK_IQ1_S_R4 ? 3 : 0);
+                    float vg, vg8;
+                    if (S == kScaleNonFinite) {
+                        vg = vg8 = __int_as_float(0x7fc00000);
+                    } else {
+                        vg = (float)ldexp(yg, shift);
+                        vg8 = (float)ldexp(yg8, shift);
+                    }
+                    const int64_t o0 = (int64_t)pair * out + r0 + ra;
+                    if (a.y_dtype == IQK_F32) {
+                        float *y = static_cast<float *>(a.y);
+                        y[o0] = vg;
+                        y[o0 + 8] = vg8;
+                    } else if (a.y_dtype == IQK_F16) {
+                        __half *y = static_cast<__half *>(a.y);
+                        y[o0] = __float2half_rn(vg);
+                        y[o0 + 8] = __float2half_rn(vg8);
+                    } else {
+                        __nv_bfloat16 *y = static_cast<__nv_bfloat16 *>(a.y);
+                        y[o0] = __float2bfloat16_rn(vg);
+                        y[o0 + 8] = __float2bfloat16_rn(vg8);
+                    }
                 }
             }
         }
@@ -667,13 +710,12 @@ GemvLayout gemv_layout(int member, int64_t n, int64_t x_rows, int64_t pairs) {
     };
     (void)member;
     L.hdr = take(64);
-    L.uniq = take(sizeof(int32_t) * (pairs + 1));
-    L.seg = take(sizeof(int32_t) * (pairs + 2));
-    L.ubase = take(sizeof(int32_t) * (pairs + 2));
     L.order = take(sizeof(int32_t) * (pairs + 1));
     L.ptok = take(sizeof(int32_t) * (pairs + 1));
+    L.tiles2 = take(sizeof(TileRef) * (pairs + 1));
+    L.tiles1 = take(sizeof(TileRef) * (pairs + 1));
     L.xscale = take(sizeof(int32_t) * (x_rows + 1));
-    L.xrow_bytes = 4 * n;  // (n/32 k-steps) x (4 planes) x (4 lanes) x 8 bytes
+    L.xrow_bytes = 3 * n + n / 2;  // planes [n/32][3][4][8] + block sums [n/32][4] int32
     L.xbuf = take((size_t)(x_rows * L.xrow_bytes));
     L.total = off;
     return L;
@@ -685,18 +727,13 @@ int gemv_smem_for(int member, int n) {
     return gemv_smem_bytes<IQK_IQ1_S_R4>(n);
 }
 
-cudaError_t launch_gemv(int member, const void *x, int x_dtype, int64_t x_rows,
-                        const void *const *streams, int64_t num_experts,
-                        int64_t out_features, int n, const int32_t *sel,
-                        const int32_t *tok, int64_t pairs, void *y, int y_dtype,
-                        void *ws, cudaStream_t stream, int num_sms) {
-    const GemvLayout L = gemv_layout(member, n, x_rows, pairs);
+cudaError_t launch_gemv_prepare(const void *x, int x_dtype, int64_t x_rows, int n,
+                                int64_t num_experts, const int32_t *sel, const int32_t *tok,
+                                int64_t pairs, void *ws, cudaStream_t stream) {
+    const GemvLayout L = gemv_layout(0, n, x_rows, pairs);
     char *w = static_cast<char *>(ws);
-    cudaError_t err = cudaMemsetAsync(w + L.hdr, 0, 64, stream);
-    if (err != cudaSuccess) return err;
-    const int ppt = member == IQK_IQ2_K ? 1 : 2;
-    const int y_elem = y_dtype == IQK_F32 ? 4 : 2;
     const size_t hist_bytes = sizeof(int32_t) * (size_t)num_experts;
+    cudaError_t err = cudaSuccess;
     if (hist_bytes > 48 * 1024) {
         err = cudaFuncSetAttribute(gemv_prep_kernel<float>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hist_bytes);
@@ -709,33 +746,36 @@ cudaError_t launch_gemv(int member, const void *x, int x_dtype, int64_t x_rows,
         if (err != cudaSuccess) return err;
     }
     const unsigned pblocks = (unsigned)x_rows + 1;
-#define IQK_PREP(T)                                                                       \
-    gemv_prep_kernel<T><<<pblocks, 256, hist_bytes, stream>>>(                            \
-        static_cast<const T *>(x), n, (int)x_rows, sel, tok, (int)pairs, (int)num_experts, \
-        (int)out_features, ppt, L, w, y, y_elem)
+#define IQK_PREP(T)                                                                          \
+    gemv_prep_kernel<T><<<pblocks, 256, hist_bytes, stream>>>(                               \
+        static_cast<const T *>(x), n, (int)x_rows, sel, tok, (int)pairs, (int)num_experts, L, w)
     if (x_dtype == IQK_F32) IQK_PREP(float);
     else if (x_dtype == IQK_F16) IQK_PREP(__half);
     else IQK_PREP(__nv_bfloat16);
 #undef IQK_PREP
-    err = cudaGetLastError();
-    if (err != cudaSuccess) return err;
+    return cudaGetLastError();
+}
 
+cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t out_features, int n,
+                            int64_t x_rows, int64_t pairs, void *y, int y_dtype, const void *ws,
+                            cudaStream_t stream, int num_sms) {
+    const GemvLayout L = gemv_layout(member, n, x_rows, pairs);
     GemvArgs ga{};
     const RowBytes rb = row_bytes(member, n);
     for (int i = 0; i < rb.count; ++i) ga.s[i] = streams[i];
     ga.out_features = out_features;
     ga.n = n;
-    ga.x_rows = (int)x_rows;
+    ga.pairs = (int)pairs;
     ga.L = L;
-    ga.ws = w;
+    ga.ws = static_cast<const char *>(ws);
     ga.y = y;
     ga.y_dtype = y_dtype;
     const int smem = gemv_smem_for(member, n);
-    // Upper bound on work items: every pair its own tile of every row tile.
-    const int64_t max_items = pairs * (out_features / 16);
-    int64_t blocks = (max_items + kWarps - 1) / kWarps;
-    if (blocks > num_sms) blocks = num_sms;
+    // Upper bound on CTA items: every pair its own tile of every row block.
+    const int64_t max_items = pairs * ((out_features + kItemRows - 1) / kItemRows);
+    int64_t blocks = max_items < num_sms ? max_items : num_sms;
     if (blocks < 1) blocks = 1;
+    cudaError_t err = cudaSuccess;
 #define IQK_GEMV(M)                                                                          \
     do {                                                                                     \
         err = cudaFuncSetAttribute(gemv_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, \

@@ -100,7 +100,11 @@ def library() -> ctypes.CDLL:
     lib.iqk_gemv.argtypes = [i32, vp, i32, i64, vp, i64, i64, i64, vp, vp, i64, vp, i32, vp,
                              sz, vp]
     lib.iqk_gemv.restype = i32
-    lib.iqk_read_error.argtypes = [vp, ctypes.POINTER(ctypes.c_int32), vp]
+    lib.iqk_gemv_prepare.argtypes = [vp, i32, i64, i64, i64, vp, vp, i64, vp, sz, vp]
+    lib.iqk_gemv_prepare.restype = i32
+    lib.iqk_gemv_run.argtypes = [i32, vp, i64, i64, i64, i64, i64, vp, i32, vp, sz, vp]
+    lib.iqk_gemv_run.restype = i32
+    lib.iqk_read_error.argtypes = [vp, i64, i64, i64, ctypes.POINTER(ctypes.c_int32), vp]
     lib.iqk_read_error.restype = i32
     _LIB = lib
     return lib
@@ -109,7 +113,8 @@ def library() -> ctypes.CDLL:
 def exported_symbols() -> list[str]:
     """C ABI entry points declared in include/iqk_b200.h."""
     return ["iqk_status_string", "iqk_abi_version", "iqk_check_device", "iqk_dequant",
-            "iqk_gemv_workspace_bytes", "iqk_gemv", "iqk_read_error"]
+            "iqk_gemv_workspace_bytes", "iqk_gemv", "iqk_gemv_prepare", "iqk_gemv_run",
+            "iqk_read_error"]
 
 
 def raise_for_status(status: int, what: str) -> None:
@@ -181,9 +186,35 @@ def gemv(member: str, x: torch.Tensor, streams, num_experts: int, out_features: 
     return y
 
 
-def read_error(workspace: torch.Tensor) -> int:
+def gemv_prepare(x: torch.Tensor, num_experts: int, in_features: int, sel: torch.Tensor,
+                 tok: torch.Tensor | None, workspace: torch.Tensor) -> torch.Tensor:
+    """``iqk_gemv_prepare``: activation digit planes + routing into ``workspace``."""
+    lib = library()
+    check_device(workspace.device)
+    status = lib.iqk_gemv_prepare(
+        x.data_ptr(), DTYPE_IDS[x.dtype], x.shape[0], in_features, num_experts,
+        sel.data_ptr(), None if tok is None else tok.data_ptr(), sel.numel(),
+        workspace.data_ptr(), workspace.numel(), stream_handle(workspace.device))
+    raise_for_status(status, "iqk_gemv_prepare")
+    return workspace
+
+
+def gemv_run(member: str, streams, num_experts: int, out_features: int, in_features: int,
+             x_rows: int, pairs: int, y: torch.Tensor, workspace: torch.Tensor) -> torch.Tensor:
+    """``iqk_gemv_run``: one projection over a prepared workspace into ``y``."""
+    lib = library()
+    status = lib.iqk_gemv_run(
+        MEMBER_IDS[member], ptr_array(streams), num_experts, out_features, in_features, x_rows,
+        pairs, y.data_ptr(), DTYPE_IDS[y.dtype], workspace.data_ptr(), workspace.numel(),
+        stream_handle(y.device))
+    raise_for_status(status, "iqk_gemv_run")
+    return y
+
+
+def read_error(workspace: torch.Tensor, in_features: int, x_rows: int, pairs: int) -> int:
     flags = ctypes.c_int32(0)
-    raise_for_status(library().iqk_read_error(workspace.data_ptr(), ctypes.byref(flags),
+    raise_for_status(library().iqk_read_error(workspace.data_ptr(), in_features, x_rows, pairs,
+                                              ctypes.byref(flags),
                                               stream_handle(workspace.device)),
                      "iqk_read_error")
     return int(flags.value)

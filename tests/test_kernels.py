@@ -188,7 +188,7 @@ def test_gemv_out_of_range_index_sets_the_error_word(cuda):
     y = torch.full((4, 32), 7.0, device=cuda)
     ws = torch.empty(K.gemv_workspace_bytes("iq2_ks", n, 2, 4), dtype=torch.uint8, device=cuda)
     K.gemv("iq2_ks", x, mod._streams(), 8, 32, n, sel, None, y, ws)
-    assert K.read_error(ws) & K.DEVERR_EXPERT
+    assert K.read_error(ws, n, 2, 4) & K.DEVERR_EXPERT
     yc = y.cpu().numpy()
     assert np.all(yc[1] == 0) and np.all(yc[3] == 0)
     want0 = ref[1].astype(np.float64) @ x[0].cpu().double().numpy()
@@ -202,6 +202,29 @@ def test_gemv_nonfinite_activation_row_gives_nan(cuda):
     x[1, 0, 0, 5] = float("inf")
     got = mod.gemv(x, torch.tensor([[0, 1], [2, 3]], device=cuda)).cpu().numpy()
     assert np.all(np.isfinite(got[0])) and np.all(np.isnan(got[1]))
+    ws = torch.empty(K.gemv_workspace_bytes("iq2_k", n, 2, 4), dtype=torch.uint8, device=cuda)
+    K.gemv_prepare(x.reshape(2, n), 8, n, torch.tensor([0, 1, 2, 3], dtype=torch.int32,
+                                                       device=cuda), None, ws)
+    assert K.read_error(ws, n, 2, 4) == K.DEVERR_NONFINITE
+
+
+@pytest.mark.parametrize("member", MEMBERS)
+def test_prepare_once_run_twice(cuda, member):
+    """One preparation serves two projections (gate and up) bit-identically."""
+    n = 4096
+    gate, _, _ = make_module(member, n, seed=31)
+    up, _, _ = make_module(member, n, seed=32)
+    x = torch.randn(3, n, device=cuda, dtype=torch.bfloat16)
+    idx = torch.randint(0, 8, (3, 6), device=cuda)
+    sel = idx.reshape(-1).to(torch.int32)
+    ws = torch.empty(K.gemv_workspace_bytes(member, n, 3, 18), dtype=torch.uint8, device=cuda)
+    K.gemv_prepare(x, 8, n, sel, None, ws)
+    yg = torch.empty(18, 32, device=cuda)
+    yu = torch.empty(18, 32, device=cuda)
+    K.gemv_run(member, gate._streams(), 8, 32, n, 3, 18, yg, ws)
+    K.gemv_run(member, up._streams(), 8, 32, n, 3, 18, yu, ws)
+    assert torch.equal(yg.view(-1, 32), gate.gemv(x.reshape(3, 1, 1, n), idx).reshape(18, 32))
+    assert torch.equal(yu.view(-1, 32), up.gemv(x.reshape(3, 1, 1, n), idx).reshape(18, 32))
 
 
 @pytest.mark.parametrize("member", MEMBERS)
