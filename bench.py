@@ -43,7 +43,7 @@ import numpy as np
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
-E, TOP_K = 256, 6
+E, TOP_K = 256, 6  # E can be lowered with --experts for small profiling captures
 GATE_UP = (2048, 4096)   # out, in
 DOWN = (4096, 2048)
 MEMBER = "iq2_ks"
@@ -476,12 +476,16 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--experts", type=int, default=256,
+                    help="experts per projection (256 = the benchmark; fewer for profiling)")
     ap.add_argument("--eager", action="store_true",
                     help="launch kernels one by one instead of replaying CUDA graphs (profiling)")
     ap.add_argument("--traffic", type=float, default=None,
                     help="dram bytes per GEMV launch from an ncu capture (reported as is)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    global E
+    E = args.experts
     if args.impl == "reference":
         run_reference(args)
     else:

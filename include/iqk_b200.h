@@ -66,7 +66,8 @@ enum {
 enum {
     IQK_DEVERR_EXPERT = 1,   /* an expert index was outside [0, num_experts) */
     IQK_DEVERR_TOKEN = 2,    /* a pair's activation row was outside [0, x_rows) */
-    IQK_DEVERR_NONFINITE = 4 /* an activation row held a NaN or infinity */
+    IQK_DEVERR_NONFINITE = 4, /* an activation row held a NaN or infinity */
+    IQK_DEVERR_TIMEOUT = 8    /* a kernel's bounded wait on its copy pipeline expired */
 };
 
 /* Short description of a status code (static storage). */
@@ -113,7 +114,8 @@ size_t iqk_gemv_workspace_bytes(int member, int64_t in_features, int64_t x_rows,
  * expert or row index is out of range produce zeros and set the device error
  * word. The per-element result does not depend on the order or grouping of
  * pairs, so a sorted call is bit-identical to the unsorted one after
- * un-permuting.
+ * un-permuting. num_experts is at most 4096 (the routing tables live in
+ * shared memory).
  *
  * Replaces gemv_kernel, gemv_sorted_kernel and gemv_union_kernel
  * (src/mlx_iqk/kernels.py:332-572, launched at src/mlx_iqk/nn.py:240-333).

@@ -101,7 +101,7 @@ size_t iqk_gemv_workspace_bytes(int member, int64_t in_features, int64_t x_rows,
 static int check_prepare(int64_t in_features, int64_t num_experts, int64_t x_rows,
                          int64_t pairs, const int32_t *tok, int x_dtype) {
     if (!width_ok(in_features)) return IQK_ERR_WIDTH;
-    if (num_experts <= 0 || num_experts > 16384) return IQK_ERR_GEOMETRY;
+    if (num_experts <= 0 || num_experts > 4096) return IQK_ERR_GEOMETRY;
     if (pairs < 0 || x_rows < 0 || pairs > (1 << 24) || x_rows > (1 << 24))
         return IQK_ERR_GEOMETRY;
     if (!tok && x_rows > 0 && pairs % x_rows) return IQK_ERR_GEOMETRY;
@@ -131,7 +131,7 @@ int iqk_gemv_run(int member, const void *const *streams, int64_t num_experts,
                  iqk_stream_t stream) {
     if (!member_ok(member)) return IQK_ERR_MEMBER;
     if (!width_ok(in_features)) return IQK_ERR_WIDTH;
-    if (num_experts <= 0 || num_experts > 16384) return IQK_ERR_GEOMETRY;
+    if (num_experts <= 0 || num_experts > 4096) return IQK_ERR_GEOMETRY;
     if (out_features <= 0 || out_features % 16) return IQK_ERR_GEOMETRY;
     if (pairs < 0 || x_rows < 0 || pairs > (1 << 24) || x_rows > (1 << 24))
         return IQK_ERR_GEOMETRY;
@@ -143,7 +143,7 @@ int iqk_gemv_run(int member, const void *const *streams, int64_t num_experts,
     if (st != IQK_OK) return st;
     if (workspace_bytes < gemv_layout(member, in_features, x_rows, pairs).total)
         return IQK_ERR_WORKSPACE;
-    return cuda_status(launch_gemv_run(member, streams, out_features, (int)in_features, x_rows,
+    return cuda_status(launch_gemv_run(member, streams, num_experts, out_features, (int)in_features, x_rows,
                                        pairs, y, y_dtype, workspace,
                                        reinterpret_cast<cudaStream_t>(stream),
                                        num_sms_current()));

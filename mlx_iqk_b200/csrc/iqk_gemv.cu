@@ -36,6 +36,8 @@
 // group metadata (alphabet nibble mask, scale indices) into shared memory
 // once, then runs 16 MMA k-steps. Partials of the 4 k-quarters are summed in
 // a fixed order, so results stay deterministic.
+#include <cuda.h>
+
 #include "iqk_common.cuh"
 #include "iqk_gemv.cuh"
 #include "iqk_tables.cuh"
@@ -65,8 +67,10 @@ __device__ __forceinline__ void mma_s8(int32_t d[4], const uint32_t a[4], uint32
 // ------------------------------------------------------------- prep kernel
 
 // One block per activation row: digit planes, block sums and the exponent.
-// Row layout in the workspace: planes [n/32 k-steps][3][4 lanes][8 bytes]
-// (bytes 0-3: the lane's even k, 4-7: odd k), then block sums [n/32][4] int32.
+// Row layout in the workspace: planes [n/64 pairs][4 code words][3 planes]
+// [16 bytes] -- for the 16 weights of a code word: bytes 0-3 the even k of
+// its first 8, 4-7 the odd k, 8-11 / 12-15 the same for its last 8 -- then
+// block sums [n/32][4] int32 (per 32-weight block, planes 0..2, 0).
 template <typename XT>
 __device__ void prep_row(const XT *__restrict__ x, int n, int row, const GemvLayout &L,
                          char *ws) {
@@ -82,10 +86,21 @@ __device__ void prep_row(const XT *__restrict__ x, int n, int row, const GemvLay
     for (int it = 0; it < 2; ++it) {
         const int q = tid + it * blockDim.x;
         if (q < noct) {
+            // one octet = 8 consecutive activations: 16 or 32 bytes, vector loads
+            if (sizeof(XT) == 2) {
+                const uint4 u = *reinterpret_cast<const uint4 *>(xr + q * 8);
+                const XT *h = reinterpret_cast<const XT *>(&u);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[it][j] = to_float<XT>(h[j]);
+            } else {
+                const float4 a = *reinterpret_cast<const float4 *>(xr + q * 8);
+                const float4 b = *reinterpret_cast<const float4 *>(xr + q * 8 + 4);
+                v[it][0] = a.x; v[it][1] = a.y; v[it][2] = a.z; v[it][3] = a.w;
+                v[it][4] = b.x; v[it][5] = b.y; v[it][6] = b.z; v[it][7] = b.w;
+            }
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                const float f = to_float<XT>(xr[q * 8 + j]);
-                v[it][j] = f;
+                const float f = v[it][j];
                 if (!isfinite(f)) bad = 1;
                 else amax = fmaxf(amax, fabsf(f));
             }
@@ -146,10 +161,11 @@ __device__ void prep_row(const XT *__restrict__ x, int n, int row, const GemvLay
                 bsum[p] += dig[p];
             }
         }
-        int8_t *dst = xb + (int64_t)s * 96;
+        // pair of groups (64 weights) q/8, code word (16 weights) (q/2)%4, half q%2
+        int8_t *dst = xb + (int64_t)(q >> 3) * 192 + ((q >> 1) & 3) * 48 + (q & 1) * 8;
 #pragma unroll
         for (int p = 0; p < 3; ++p)
-            *reinterpret_cast<uint2 *>(dst + p * 32 + tig * 8) = make_uint2(planes[p][0], planes[p][1]);
+            *reinterpret_cast<uint2 *>(dst + p * 16) = make_uint2(planes[p][0], planes[p][1]);
         // Block sums over the 32 weights of k-step s: reduce across the quad.
 #pragma unroll
         for (int p = 0; p < 3; ++p) {
@@ -192,24 +208,23 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int *warp_tot, int *t
     return excl;
 }
 
-// Route the pairs: bucket by expert (counting sort in shared memory), then
-// lay out two tile lists -- pairs grouped two by two per expert (IQ2_KS,
-// IQ1_S_R4) and one by one (IQ2_K). Pairs whose expert or row index is out of
-// range go to the tail of `order` (the run kernel zeroes their outputs) and
-// set the device error word.
+// Route the pairs: bucket by expert (counting sort in shared memory) and lay
+// out the work tiles -- one per routable pair, grouped by expert -- written
+// directly by the thread that places each pair. Pairs whose expert or row
+// index is out of range go to the tail of `order` (the run kernel zeroes
+// their outputs) and set the device error word.
+// Shared memory: per-expert counts, then scatter cursors (num_experts ints).
 __device__ void route_pairs(const int32_t *__restrict__ sel, const int32_t *__restrict__ tok,
                             int pairs, int x_rows, int num_experts, const GemvLayout &L,
                             char *ws) {
-    extern __shared__ int32_t hist[];  // [num_experts]
+    extern __shared__ int32_t cur[];
     __shared__ int32_t warp_tot[33];
     __shared__ int32_t s_bad, s_tail;
     const int tid = threadIdx.x, nt = blockDim.x;
     int32_t *hdr = reinterpret_cast<int32_t *>(ws + L.hdr);
     int32_t *order = reinterpret_cast<int32_t *>(ws + L.order);
-    int32_t *ptok = reinterpret_cast<int32_t *>(ws + L.ptok);
-    TileRef *tiles2 = reinterpret_cast<TileRef *>(ws + L.tiles2);
-    TileRef *tiles1 = reinterpret_cast<TileRef *>(ws + L.tiles1);
-    for (int e = tid; e < num_experts; e += nt) hist[e] = 0;
+    TileRef *tiles = reinterpret_cast<TileRef *>(ws + L.tiles1);
+    for (int e = tid; e < num_experts; e += nt) cur[e] = 0;
     if (tid == 0) s_bad = 0;
     __syncthreads();
     const int dims = tok ? 1 : pairs / x_rows;
@@ -217,67 +232,41 @@ __device__ void route_pairs(const int32_t *__restrict__ sel, const int32_t *__re
     for (int p = tid; p < pairs; p += nt) {
         const int e = sel[p];
         const int t = tok ? tok[p] : p / dims;
-        ptok[p] = t;
         if (e < 0 || e >= num_experts) err |= IQK_DEVERR_EXPERT;
         else if (t < 0 || t >= x_rows) err |= IQK_DEVERR_TOKEN;
-        else atomicAdd(&hist[e], 1);
+        else atomicAdd(&cur[e], 1);
     }
     if (err) atomicOr(&s_bad, err);
     __syncthreads();
-    // Thread-contiguous bins; scans of (routable pairs, tiles of 2).
+    // thread-contiguous bins; exclusive scan of the per-expert counts
     const int per = (num_experts + nt - 1) / nt;
     const int b0 = min(tid * per, num_experts), b1 = min(b0 + per, num_experts);
-    int c_cnt = 0, c_t2 = 0;
+    int c_cnt = 0;
+    for (int e = b0; e < b1; ++e) c_cnt += cur[e];
+    int n_valid;
+    int run = block_exclusive_scan(c_cnt, warp_tot, &n_valid);
     for (int e = b0; e < b1; ++e) {
-        const int c = hist[e];
-        c_cnt += c;
-        c_t2 += (c + 1) >> 1;
-    }
-    int n_valid, n_t2;
-    const int base_cnt = block_exclusive_scan(c_cnt, warp_tot, &n_valid);
-    const int base_t2 = block_exclusive_scan(c_t2, warp_tot, &n_t2);
-    // scatter cursors: first position of each expert's pairs
-    {
-        int run = base_cnt;
-        for (int e = b0; e < b1; ++e) {
-            const int c = hist[e];
-            hist[e] = run;
-            run += c;
-        }
+        const int c = cur[e];
+        cur[e] = run;
+        run += c;
     }
     if (tid == 0) {
         hdr[0] = s_bad;
-        hdr[2] = n_t2;     // tiles of 2 pairs (IQ2_KS, IQ1_S_R4)
-        hdr[3] = n_valid;  // tiles of 1 pair (IQ2_K) == routable pairs
+        hdr[3] = n_valid;  // work tiles == routable pairs
         s_tail = n_valid;
     }
     __syncthreads();
     for (int p = tid; p < pairs; p += nt) {
         const int e = sel[p];
-        const int t = ptok[p];
+        const int t = tok ? tok[p] : p / dims;
         const bool ok = e >= 0 && e < num_experts && t >= 0 && t < x_rows;
-        const int pos = ok ? atomicAdd(&hist[e], 1) : atomicAdd(&s_tail, 1);
-        order[pos] = p;
-    }
-    __syncthreads();
-    // Tile lists, expert by expert (each thread owns its bin range again;
-    // hist[e] now holds the end of expert e's segment).
-    {
-        int run = base_cnt, run2 = base_t2;
-        for (int e = b0; e < b1; ++e) {
-            const int end = hist[e];
-            for (int q = run; q < end; ++q) {
-                const int p = order[q];
-                tiles1[q] = TileRef{e, p, -1, ptok[p], -1, 0, 0, 1};
-            }
-            for (int q = run; q < end; q += 2) {
-                const int p0 = order[q];
-                const int p1 = q + 1 < end ? order[q + 1] : -1;
-                tiles2[run2++] = TileRef{e, p0, p1, ptok[p0], p1 >= 0 ? ptok[p1] : -1, 0, 0,
-                                         p1 >= 0 ? 2 : 1};
-            }
-            run = end;
+        if (!ok) {
+            order[atomicAdd(&s_tail, 1)] = p;
+            continue;
         }
+        const int pos = atomicAdd(&cur[e], 1);
+        order[pos] = p;
+        tiles[pos] = TileRef{e, p, -1, t, -1, 0, 0, 1};
     }
 }
 
@@ -295,26 +284,32 @@ gemv_prep_kernel(const XT *__restrict__ x, int n, int x_rows, const int32_t *__r
 
 // -------------------------------------------------------------- run kernel
 
-constexpr int kWarps = 8;
-constexpr int kKSplit = 4;                    // warps sharing one row tile along k
-constexpr int kRowTiles = kWarps / kKSplit;   // 16-row tiles per CTA item
+constexpr int kConsumers = 8;                 // compute warps
+constexpr int kThreads = (kConsumers + 1) * 32;  // + one producer warp
+constexpr int kKSplit = 4;                    // compute warps sharing one row tile along k
+constexpr int kRowTiles = kConsumers / kKSplit;  // 16-row tiles per CTA item
 constexpr int kItemRows = 16 * kRowTiles;     // 32
-constexpr int kStages = 4;
 constexpr int kChunkK = 512;                  // weights per row per round and warp
-constexpr int kSteps = kChunkK / 32;          // MMA k-steps per round
-constexpr int kMaxTiles = 256;                // tile entries cached in shared memory
+constexpr int kPairsPerRound = kChunkK / 64;  // MMA pairs (64 weights per row) per round
+constexpr int kMaxTiles = 128;                // tile entries cached in shared memory
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // bounded mbarrier waits (2 s)
 
+// One work tile is one pair (expert, activation row). A warp's 16 rows x 64
+// weights form an "MMA pair": two m16n8k32 products whose A fragments come
+// from one 32-bit code word per lane and row.
 template <int MEMBER> struct Geo {
-    static constexpr int kPpt = MEMBER == IQK_IQ2_K ? 1 : 2;                 // pairs per tile
-    static constexpr int kRowChunk = MEMBER == IQK_IQ1_S_R4 ? 64 : 128;      // qs bytes
-    static constexpr int kRowStride = MEMBER == IQK_IQ1_S_R4 ? 80 : 144;     // bank-staggered
-    static constexpr int kWBytes = kWarps * 16 * kRowStride;
-    static constexpr int kXPlanes = kSteps * 96;                             // 3 planes
-    static constexpr int kXSums = MEMBER == IQK_IQ1_S_R4 ? kSteps * 16 : 0;  // block sums
-    static constexpr int kXBlock = kXPlanes + kXSums;                        // per (ks, pair)
-    static constexpr int kStageBytes = kWBytes + kKSplit * kPpt * kXBlock;
-    static constexpr int kMetaEntry = MEMBER == IQK_IQ2_K ? 32 : 16;
-    static constexpr int kMetaBytes = kSteps * 8 * kMetaEntry;               // per warp
+    // IQ2_KS and IQ1_S_R4 run two CTAs per SM (3-stage rings); IQ2_K, whose
+    // scale streams and metadata are twice as large, one CTA with 5 stages.
+    static constexpr int kStages = MEMBER == IQK_IQ2_K ? 5 : 3;
+    static constexpr int kMinBlocks = MEMBER == IQK_IQ2_K ? 1 : 2;
+    static constexpr int kRowChunk = MEMBER == IQK_IQ1_S_R4 ? 64 : 128;   // qs bytes per round
+    static constexpr int kWBox = 16 * kRowChunk;                         // one warp's TMA box
+    static constexpr int kWBytes = kConsumers * kWBox;
+    static constexpr int kXPlanes = kPairsPerRound * 192;                  // 3 planes
+    static constexpr int kXSums = MEMBER == IQK_IQ1_S_R4 ? kPairsPerRound * 32 : 0;
+    static constexpr int kXBlock = kXPlanes + kXSums;                      // per k-quarter
+    static constexpr int kMetaSides = MEMBER == IQK_IQ2_K ? 4 : 2;
+    static constexpr int kMetaBytes = kPairsPerRound * kMetaSides * 8 * 16;  // per warp
 };
 
 // Scale streams of one CTA item (kItemRows rows, whole k), all but qs.
@@ -324,11 +319,21 @@ template <int MEMBER> __host__ __device__ constexpr int slot_bytes(int n) {
                                  : kItemRows * (n / 16) + 2 * kItemRows;
 }
 
+// Stage: [weights: kConsumers TMA boxes][activation slices][item scale streams]
+// (the scale streams only in an item's first stage; the item's stages are
+// released together when the item ends).
+template <int MEMBER> __host__ __device__ constexpr int stage_bytes(int n) {
+    return (Geo<MEMBER>::kWBytes + kKSplit * Geo<MEMBER>::kXBlock + slot_bytes<MEMBER>(n) + 1023) /
+           1024 * 1024;
+}
+
 template <int MEMBER> __host__ __device__ constexpr int gemv_smem_bytes(int n) {
     using G = Geo<MEMBER>;
-    return kStages * G::kStageBytes + kStages * slot_bytes<MEMBER>(n) + kWarps * G::kMetaBytes +
-           kWarps * 32 * 4 * 4 + kWarps * 32 * 2 * 8 + kMaxTiles * (int)sizeof(TileRef) +
-           (MEMBER == IQK_IQ1_S_R4 ? 4096 : 0);
+    constexpr int kStages = G::kStages;
+    return 1024 /* alignment slack */ + kStages * stage_bytes<MEMBER>(n) +
+           kConsumers * G::kMetaBytes + kConsumers * 32 * 4 * 4 + kConsumers * 32 * 2 * 8 +
+           kMaxTiles * (int)sizeof(TileRef) + (MEMBER == IQK_IQ1_S_R4 ? 4096 : 0) +
+           (MEMBER == IQK_IQ2_K ? 256 : 0) + 2 * kStages * 8 + 16 + kPairsPerRound * 192;
 }
 
 struct GemvArgs {
@@ -338,6 +343,7 @@ struct GemvArgs {
     int pairs;
     GemvLayout L;
     const char *ws;
+    int32_t *err;  // device error word (workspace header)
     void *y;
     int y_dtype;
 };
@@ -345,47 +351,135 @@ struct GemvArgs {
 __device__ __forceinline__ uint32_t lds_u16(const void *p) {
     return *reinterpret_cast<const uint16_t *>(p);
 }
+__device__ __forceinline__ uint32_t lds_u32(const void *p) {
+    return *reinterpret_cast<const uint32_t *>(p);
+}
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// Explicit shared-space accesses on 32-bit addresses.
+__device__ __forceinline__ uint32_t ld_s32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];\n" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 ld_s64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint4 ld_s128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void st_s128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w)
+                 : "memory");
+}
+
+// d += A * B (int8 m16n8k32, accumulating in place).
+__device__ __forceinline__ void mma_s8_acc(int32_t d[4], const uint32_t a[4], uint32_t b0,
+                                           uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// ---- mbarrier / bulk-copy primitives (PTX ISA: mbarrier, cp.async.bulk)
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)),
+                 "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+    return t;
+}
+// Wait for a phase with a wall-clock bound; false means it timed out.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (global_ns() - t0 > kWaitLimitNs) return false;
+    return true;
+}
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];\n" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+        ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
 
 template <int MEMBER>
-__global__ void __launch_bounds__(kWarps * 32, 1)
-gemv_kernel(GemvArgs a) {
-    extern __shared__ __align__(128) char smem[];
+__global__ void __launch_bounds__(kThreads, Geo<MEMBER>::kMinBlocks)
+gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
+    extern __shared__ char smem_raw[];
     using G = Geo<MEMBER>;
-    constexpr int ppt = G::kPpt;
+    constexpr int kStages = G::kStages;
+    char *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int n = a.n;
     const int64_t out = a.out_features;
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const int g = lane >> 2, tig = lane & 3;
-    const int rt = wid / kKSplit, ks = wid % kKSplit;
     const int cpw = n / (kChunkK * kKSplit);  // rounds per item: 2 (n=4096) or 1 (2048)
     const int SB = slot_bytes<MEMBER>(n);
+    const int STB = stage_bytes<MEMBER>(n);
 
     char *stages = smem;
-    char *slots = stages + kStages * G::kStageBytes;
-    char *metas = slots + kStages * SB;
-    int32_t *red_i = reinterpret_cast<int32_t *>(metas + kWarps * G::kMetaBytes);
-    double *red_d = reinterpret_cast<double *>(red_i + kWarps * 32 * 4);
-    TileRef *tcache = reinterpret_cast<TileRef *>(red_d + kWarps * 32 * 2);
-    uint16_t *grid = reinterpret_cast<uint16_t *>(tcache + kMaxTiles);
-    char *meta = metas + wid * G::kMetaBytes;
+    char *metas = stages + kStages * STB;
+    int32_t *red_i = reinterpret_cast<int32_t *>(metas + kConsumers * G::kMetaBytes);
+    double *red_d = reinterpret_cast<double *>(red_i + kConsumers * 32 * 4);
+    TileRef *tcache = reinterpret_cast<TileRef *>(red_d + kConsumers * 32 * 2);
+    char *tail = reinterpret_cast<char *>(tcache + kMaxTiles);
+    uint16_t *grid = reinterpret_cast<uint16_t *>(tail);   // IQ1_S_R4
+    uint2 *ktab = reinterpret_cast<uint2 *>(tail);         // IQ2_K: (alpha, idx) -> tables
+    uint64_t *full = reinterpret_cast<uint64_t *>(
+        tail + (MEMBER == IQK_IQ1_S_R4 ? 4096 : MEMBER == IQK_IQ2_K ? 256 : 0));
+    uint64_t *empty = full + kStages;
+    int *abort_flag = reinterpret_cast<int *>(empty + kStages);
+    char *zeros = reinterpret_cast<char *>(abort_flag) + 16;  // kPairsPerRound * 192 zero bytes
 
     const int32_t *hdr = reinterpret_cast<const int32_t *>(a.ws + a.L.hdr);
     const int32_t *order = reinterpret_cast<const int32_t *>(a.ws + a.L.order);
     const int32_t *xscale = reinterpret_cast<const int32_t *>(a.ws + a.L.xscale);
-    const TileRef *tlist = reinterpret_cast<const TileRef *>(a.ws + (ppt == 2 ? a.L.tiles2 : a.L.tiles1));
+    const TileRef *tlist = reinterpret_cast<const TileRef *>(a.ws + a.L.tiles1);
     const char *xbuf = a.ws + a.L.xbuf;
     const int64_t xrow = a.L.xrow_bytes;
 
-    const int ntiles = ppt == 2 ? hdr[2] : hdr[3];
+    const int ntiles = hdr[3];
     const int rblocks = (int)((out + kItemRows - 1) / kItemRows);
     const int items = ntiles * rblocks;
 
     if (blockIdx.x == 0) {
         // zero the outputs of unroutable pairs (the tail of order)
-        const int nvalid = hdr[3];
         const int elem = a.y_dtype == IQK_F32 ? 4 : 2;
         const int row_words = (int)(out * elem / 4);
-        for (int q = nvalid; q < a.pairs; ++q) {
+        for (int q = ntiles; q < a.pairs; ++q) {
             int32_t *yr = reinterpret_cast<int32_t *>(static_cast<char *>(a.y) +
                                                       (int64_t)order[q] * out * elem);
             for (int i = tid; i < row_words; i += blockDim.x) yr[i] = 0;
@@ -399,251 +493,346 @@ gemv_kernel(GemvArgs a) {
     auto load_tile = [&](int t) -> TileRef {
         TileRef r = tlist[t];
         r.sh0 = xscale[r.tok0];
-        r.sh1 = r.tok1 >= 0 ? xscale[r.tok1] : 0;
         return r;
     };
     if (cached)
         for (int t = tid; t <= t1 - t0; t += blockDim.x) tcache[t] = load_tile(t0 + t);
     if (MEMBER == IQK_IQ1_S_R4)
         for (int i = tid; i < 2048; i += blockDim.x) grid[i] = g_iq1s_grid[i];
+    if (MEMBER == IQK_IQ2_K && tid < 32) {
+        // IQ2_K scale index idx = 4*hi + lo (hi = idx >> 2 in [-2, 1], lo = idx & 3):
+        // per (alphabet, idx) the two int8 tables V*lo and V*hi, so a sub-block's
+        // scale folds into its A operand and all sub-blocks share one accumulator.
+        const int alpha = tid >> 4, idx = (tid & 15) - 8;
+        const uint32_t tab = alpha ? kIq2Tab1 : kIq2Tab0;
+        uint32_t tlo = 0, thi = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int v = (int)(int8_t)(tab >> (8 * c));
+            tlo |= (uint32_t)(uint8_t)(int8_t)(v * (idx & 3)) << (8 * c);
+            thi |= (uint32_t)(uint8_t)(int8_t)(v * (idx >> 2)) << (8 * c);
+        }
+        ktab[tid] = make_uint2(tlo, thi);
+    }
+    for (int i = tid; i < kPairsPerRound * 192 / 4; i += blockDim.x)
+        reinterpret_cast<uint32_t *>(zeros)[i] = 0u;
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumers);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
     __syncthreads();
     auto tile_of = [&](int t) -> TileRef { return cached ? tcache[t - t0] : load_tile(t); };
-
-    const char *qs = static_cast<const char *>(a.s[0]);
-    const int64_t qrow = MEMBER == IQK_IQ1_S_R4 ? n / 8 : n / 4;  // qs bytes per row
+    const int total_rounds = (i1 - i0) * cpw;
     const RowBytes rbs = row_bytes(MEMBER, n);
 
-    // Issue round j: every warp's chunk of weights, the activation slices,
-    // and (first round of an item) the item's scale streams.
-    auto issue = [&](int j) {
-        const int o = j / cpw, r = j - o * cpw, i = i0 + o;
-        const TileRef T = tile_of(i / rblocks);
-        const int64_t r0 = (int64_t)(i % rblocks) * kItemRows;
-        const int rows_valid = (int)min((int64_t)kItemRows, out - r0);
-        char *st = stages + (j % kStages) * G::kStageBytes;
-        constexpr int per_row = G::kRowChunk / 16;
-        for (int q = tid; q < kWarps * 16 * per_row; q += blockDim.x) {
-            const int w = q / (16 * per_row), rem = q - w * 16 * per_row;
-            const int row = rem / per_row, part = rem - row * per_row;
-            const int lr = 16 * (w / kKSplit) + row;
-            if (lr >= rows_valid) continue;
-            const int c = (w % kKSplit) * cpw + r;
-            cp_async16(st + (w * 16 + row) * G::kRowStride + part * 16,
-                       qs + ((int64_t)T.e * out + r0 + lr) * qrow + c * G::kRowChunk + part * 16);
-        }
-        char *xs = st + G::kWBytes;
-        constexpr int xparts = G::kXBlock / 16;
-        for (int q = tid; q < kKSplit * ppt * xparts; q += blockDim.x) {
-            const int blk = q / xparts, part = q - blk * xparts;
-            const int ksx = blk / ppt, t = blk - ksx * ppt;
-            const int tk = t == 0 ? T.tok0 : T.tok1;
-            if (tk < 0) continue;
-            const int c = ksx * cpw + r;
-            const char *src = part < G::kXPlanes / 16
-                                  ? xbuf + tk * xrow + (int64_t)c * G::kXPlanes + part * 16
-                                  : xbuf + tk * xrow + 3 * (int64_t)n + (int64_t)c * kSteps * 16 +
-                                        (part - G::kXPlanes / 16) * 16;
-            cp_async16(xs + blk * G::kXBlock + part * 16, src);
-        }
-        if (r == 0) {
-            char *sd = slots + (o % kStages) * SB;
-            int off = 0;
-            for (int si = 1; si < rbs.count; ++si) {
-                const int bytes = (int)(rows_valid * rbs.b[si]);
-                const char *src = static_cast<const char *>(a.s[si]) + ((int64_t)T.e * out + r0) * rbs.b[si];
-                for (int q = tid * 16; q < bytes; q += blockDim.x * 16) cp_async16(sd + off + q, src + q);
-                off += (int)(kItemRows * rbs.b[si]);
+    if (wid == kConsumers) {
+        // ================= producer warp: TMA / bulk copies into the ring
+        int o = 0, r = 0, ti = i0 / rblocks, rb = i0 % rblocks;
+        int issued = 0;
+        for (int j = 0; j < total_rounds; ++j) {
+            const int slot = j % kStages;
+            if (j >= kStages && !mbar_wait(&empty[slot], ((j / kStages) & 1) ^ 1)) {
+                if (lane == 0) {
+                    atomicOr(a.err, IQK_DEVERR_TIMEOUT);
+                    atomicExch(abort_flag, 1);
+                }
+                break;
+            }
+            const TileRef T = tile_of(ti);
+            const int64_t r0 = (int64_t)rb * kItemRows;
+            const int rows_valid = (int)min((int64_t)kItemRows, out - r0);
+            char *st = stages + slot * STB;
+            uint32_t bytes = (uint32_t)(G::kWBytes + kKSplit * G::kXBlock);
+            if (r == 0)
+                for (int si = 1; si < rbs.count; ++si) bytes += (uint32_t)(rows_valid * rbs.b[si]);
+            if (lane == 0) mbar_arrive_expect_tx(&full[slot], bytes);
+            __syncwarp();
+            if (lane < kConsumers) {
+                // weights: one 16-row x kRowChunk-byte box per compute warp
+                const int w = lane, rtw = w / kKSplit, ksw = w % kKSplit;
+                tma_load_2d(st + w * G::kWBox, &qs_map, (ksw * cpw + r) * G::kRowChunk,
+                            (int)((int64_t)T.e * out + r0 + 16 * rtw), &full[slot]);
+            } else if (lane < kConsumers + kKSplit) {
+                // activation digit planes (+ IQ1 block sums) of each k-quarter
+                const int ksx = lane - kConsumers;
+                const int c = ksx * cpw + r;
+                char *xs = st + G::kWBytes + ksx * G::kXBlock;
+                const char *xb = xbuf + T.tok0 * xrow;
+                bulk_load(xs, xb + (int64_t)c * G::kXPlanes, G::kXPlanes, &full[slot]);
+                if (G::kXSums)
+                    bulk_load(xs + G::kXPlanes, xb + 3 * (int64_t)n + (int64_t)c * G::kXSums,
+                              G::kXSums, &full[slot]);
+            } else if (r == 0 && lane < kConsumers + kKSplit + rbs.count - 1) {
+                // the item's scale streams (all rows, all k)
+                const int si = lane - kConsumers - kKSplit + 1;
+                int off = 0;
+                for (int q = 1; q < si; ++q) off += (int)(kItemRows * rbs.b[q]);
+                bulk_load(st + G::kWBytes + kKSplit * G::kXBlock + off,
+                          static_cast<const char *>(a.s[si]) + ((int64_t)T.e * out + r0) * rbs.b[si],
+                          (uint32_t)(rows_valid * rbs.b[si]), &full[slot]);
+            }
+            issued = j + 1;
+            if (++r == cpw) {
+                r = 0;
+                ++o;
+                if (++rb == rblocks) {
+                    rb = 0;
+                    ++ti;
+                }
             }
         }
-    };
-
-    const int total_rounds = (i1 - i0) * cpw;
-#pragma unroll 1
-    for (int j = 0; j < kStages - 1; ++j) {
-        if (j < total_rounds) issue(j);
-        cp_async_commit();
+        // Drain: never leave the CTA with bulk copies still in flight. In
+        // normal operation the consumers already waited on every stage; after
+        // an abort this waits (bounded) for the copies issued last.
+        for (int j = issued - 1; j >= 0 && j >= issued - kStages; --j)
+            mbar_wait(&full[j % kStages], (j / kStages) & 1);
+        return;
     }
 
-    int32_t tot[4] = {0, 0, 0, 0};
-    double dacc[2] = {0.0, 0.0};  // IQ2_K: rows g, g+8 (lanes with tig == 0)
+    // ===================== compute warps
+    const int g = lane >> 2, tig = lane & 3;
+    const int rt = wid / kKSplit, ks = wid % kKSplit;
+    char *meta = metas + wid * G::kMetaBytes;
+    const uint32_t meta_u = smem_u32(meta);
+    const int side = tig >> 1;             // which 32-weight group of an MMA pair
+    int bplane;                            // activation plane of B column g (or -1)
+    if (MEMBER == IQK_IQ2_K) bplane = g < 3 ? g : -1;
+    else bplane = ((g & 3) < 3 && (g >> 2) == side) ? (g & 3) : -1;
+    // swizzled offsets of this lane's code words (rows g and g+8 of its box)
+    uint32_t woff;
+    if (MEMBER == IQK_IQ1_S_R4) woff = g * 64 + ((((uint32_t)g >> 1) & 3u) << 4) + side * 4;
+    else woff = g * 128 + ((uint32_t)(g & 7) << 4) + tig * 4;
+    // this lane's metadata entry within a pair: [pair][row pair g][side or word]
+    const uint32_t moff = MEMBER == IQK_IQ2_K ? (g * 4 + tig) * 16 : (g * 2 + side) * 16;
+    const uint32_t zero_u = smem_u32(zeros);
 
-#pragma unroll 1
+    int32_t tot[4] = {0, 0, 0, 0};
+    int32_t acc1[4] = {0, 0, 0, 0}, acc2[4] = {0, 0, 0, 0};  // IQ2_K super-block sums
+    double dacc[2] = {0.0, 0.0};                              // IQ2_K: rows g, g+8
+
+    int o = 0, r = 0, ti = i0 / rblocks, rb = i0 % rblocks;
     for (int j = 0; j < total_rounds; ++j) {
-        const int o = j / cpw, r = j - o * cpw, i = i0 + o;
-        const TileRef T = tile_of(i / rblocks);
-        const int64_t r0 = (int64_t)(i % rblocks) * kItemRows;
-        cp_async_wait<kStages - 2>();
-        __syncthreads();
-        if (j + kStages - 1 < total_rounds) issue(j + kStages - 1);
-        cp_async_commit();
+        const int slot = j % kStages;
+        const bool ok = mbar_wait(&full[slot], (j / kStages) & 1);
+        if (!ok || *(volatile int *)abort_flag) {
+            if (lane == 0 && !ok) {
+                atomicOr(a.err, IQK_DEVERR_TIMEOUT);
+                atomicExch(abort_flag, 1);
+            }
+            break;
+        }
+        const TileRef T = tile_of(ti);
+        const int64_t r0 = (int64_t)rb * kItemRows;
         if (r == 0) {
             tot[0] = tot[1] = tot[2] = tot[3] = 0;
             dacc[0] = dacc[1] = 0.0;
         }
         const bool live = 16 * rt < out - r0;  // this warp's row tile exists
-        const char *st = stages + (j % kStages) * G::kStageBytes;
-        const char *sd = slots + (o % kStages) * SB;
-        const int c = ks * cpw + r;  // chunk of this warp
+        const char *st = stages + slot * STB;
+        // the item's scale streams arrived with its first round
+        const char *sd = stages + ((j - r) % kStages) * STB + G::kWBytes + kKSplit * G::kXBlock;
+        const int c = ks * cpw + r;  // 512-weight chunk of this warp
         if (live) {
-            // ---- expand group metadata for this warp's 16 rows x 16 k-steps
+            // ---- group metadata for this warp's 16 rows x 512 weights.
+            // Lane (mg, mq) owns row pair (mg, mg + 8) and 128 weights.
             {
-                const int mg = lane & 7, mq = lane >> 3;  // row pair, quad of k-steps
-                const int ra = 16 * rt + mg, rb = ra + 8;  // item-local rows g, g+8
+                const int mg = lane & 7, mq = lane >> 3;
+                const int ra = 16 * rt + mg, rb2 = ra + 8;  // item-local rows
+                if (MEMBER == IQK_IQ2_KS) {
+                    const int s0 = c * 16 + mq * 4;  // first of 4 groups (2 pairs)
+                    const uint8_t *scl = reinterpret_cast<const uint8_t *>(sd);
+                    const uint8_t *sch = scl + kItemRows * (n / 64);
+                    const uint8_t *sex = sch + kItemRows * (n / 256);
+                    const uint32_t la = lds_u16(scl + ra * (n / 64) + (s0 >> 1));
+                    const uint32_t lb = lds_u16(scl + rb2 * (n / 64) + (s0 >> 1));
+                    const uint32_t ha = (uint32_t)sch[ra * (n / 256) + (s0 >> 3)] >> (s0 & 7);
+                    const uint32_t hb = (uint32_t)sch[rb2 * (n / 256) + (s0 >> 3)] >> (s0 & 7);
+                    const uint32_t xa = (uint32_t)sex[ra * (n / 256) + (s0 >> 3)] >> (s0 & 7);
+                    const uint32_t xb = (uint32_t)sex[rb2 * (n / 256) + (s0 >> 3)] >> (s0 & 7);
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int ls = mq * 4 + u;
-                    const int s = c * kSteps + ls;  // global k-step
-                    if (MEMBER == IQK_IQ2_KS) {
-                        const uint8_t *scl = reinterpret_cast<const uint8_t *>(sd);
-                        const uint8_t *sch = scl + kItemRows * (n / 64);
-                        const uint8_t *sex = sch + kItemRows * (n / 256);
-                        const int sh = (s & 1) * 4, bi = s >> 3, bb = s & 7;
-                        const int ia = (((scl[ra * (n / 64) + (s >> 1)] >> sh) & 15) |
-                                        (((sch[ra * (n / 256) + bi] >> bb) & 1) << 4)) - 16;
-                        const int ib = (((scl[rb * (n / 64) + (s >> 1)] >> sh) & 15) |
-                                        (((sch[rb * (n / 256) + bi] >> bb) & 1) << 4)) - 16;
-                        const uint32_t am = (((sex[ra * (n / 256) + bi] >> bb) & 1) ? 0x4444u : 0u) |
-                                            (((sex[rb * (n / 256) + bi] >> bb) & 1) ? 0x44440000u : 0u);
-                        *reinterpret_cast<int4 *>(meta + (ls * 8 + mg) * 16) =
-                            make_int4((int)am, ia, ib, 0);
-                    } else if (MEMBER == IQK_IQ2_K) {
-                        const uint8_t *scl = reinterpret_cast<const uint8_t *>(sd);
-                        const uint8_t *sex = scl + kItemRows * (n / 32);
-                        const int ba = scl[ra * (n / 32) + s], bbv = scl[rb * (n / 32) + s];
-                        const int xa = sex[ra * (n / 128) + (s >> 2)] >> ((2 * s) & 7);
-                        const int xb = sex[rb * (n / 128) + (s >> 2)] >> ((2 * s) & 7);
-                        const uint32_t am0 = ((xa & 1) ? 0x4444u : 0u) | ((xb & 1) ? 0x44440000u : 0u);
-                        const uint32_t am1 = ((xa & 2) ? 0x4444u : 0u) | ((xb & 2) ? 0x44440000u : 0u);
-                        int4 *m = reinterpret_cast<int4 *>(meta + (ls * 8 + mg) * 32);
-                        m[0] = make_int4((int)am0, (int)am1, 0, 0);
-                        m[1] = make_int4((ba & 15) - 8, (ba >> 4) - 8, (bbv & 15) - 8, (bbv >> 4) - 8);
-                    } else {
-                        const uint16_t *qh = reinterpret_cast<const uint16_t *>(sd);
-                        const uint32_t ha = qh[ra * (n / 32) + s], hb = qh[rb * (n / 32) + s];
+                    for (int u = 0; u < 4; ++u) {
+                        const int ia = (int)(((la >> (4 * u)) & 15u) | (((ha >> u) & 1u) << 4)) - 16;
+                        const int ib = (int)(((lb >> (4 * u)) & 15u) | (((hb >> u) & 1u) << 4)) - 16;
+                        const uint32_t ama = ((xa >> u) & 1u) * 0x44444444u;
+                        const uint32_t amb = ((xb >> u) & 1u) * 0x44444444u;
+                        const int pr = mq * 2 + (u >> 1), sd2 = u & 1;  // pair, side
+                        st_s128(meta_u + pr * 256 + (mg * 2 + sd2) * 16, (uint32_t)ama, (uint32_t)amb,
+                                (uint32_t)ia, (uint32_t)ib);
+                    }
+                } else if (MEMBER == IQK_IQ2_K) {
+                    const int b0 = c * 32 + mq * 8;  // first of 8 sub-blocks (2 pairs)
+                    const uint8_t *scl = reinterpret_cast<const uint8_t *>(sd);
+                    const uint8_t *sex = scl + kItemRows * (n / 32);
+                    const uint32_t la = lds_u32(scl + ra * (n / 32) + (b0 >> 1));
+                    const uint32_t lb = lds_u32(scl + rb2 * (n / 32) + (b0 >> 1));
+                    const uint32_t xa = sex[ra * (n / 128) + (b0 >> 3)];
+                    const uint32_t xb = sex[rb2 * (n / 128) + (b0 >> 3)];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const uint2 ta = ktab[((xa >> u) & 1u) * 16 + ((la >> (4 * u)) & 15u)];
+                        const uint2 tb = ktab[((xb >> u) & 1u) * 16 + ((lb >> (4 * u)) & 15u)];
+                        const int pr = mq * 2 + (u >> 2), wd = u & 3;  // pair, word
+                        st_s128(meta_u + pr * 512 + (mg * 4 + wd) * 16, ta.x, tb.x, ta.y, tb.y);
+                    }
+                } else {
+                    const int s0 = c * 16 + mq * 4;  // first of 4 blocks (2 pairs)
+                    const uint16_t *qh = reinterpret_cast<const uint16_t *>(sd);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const uint32_t ha = qh[ra * (n / 32) + s0 + u], hb = qh[rb2 * (n / 32) + s0 + u];
                         const int ma = 2 * (int)((ha >> 12) & 7u) + 1, mb = 2 * (int)((hb >> 12) & 7u) + 1;
-                        *reinterpret_cast<int4 *>(meta + (ls * 8 + mg) * 16) =
-                            make_int4((int)(ha | (hb << 16)), ma, mb,
-                                      ((ha & 0x8000u) ? 1 : 0) | ((hb & 0x8000u) ? 2 : 0));
+                        const int pr = mq * 2 + (u >> 1), sd2 = u & 1;
+                        st_s128(meta_u + pr * 256 + (mg * 2 + sd2) * 16, ha | (hb << 16),
+                                (uint32_t)((ha & 0x8000u) ? -ma : ma), (uint32_t)((hb & 0x8000u) ? -mb : mb),
+                                (uint32_t)(ma | (mb << 16)));
                     }
                 }
             }
             __syncwarp();
 
-            // ---- 16 MMA k-steps
-            const char *wb = st + wid * 16 * G::kRowStride;
-            const char *xs = st + G::kWBytes + ks * ppt * G::kXBlock;
-            int bt, bp;
-            bool blive;
-            if (MEMBER == IQK_IQ2_K) {
-                bt = 0;
-                bp = g >> 1;
-                blive = bp < 3 && (g & 1) == (tig >> 1);
-            } else {
-                bt = g >> 2;
-                bp = g & 3;
-                blive = bp < 3 && (bt == 0 ? T.tok0 : T.tok1) >= 0;
-            }
-            const char *xl = xs + bt * G::kXBlock + bp * 32 + tig * 8;
-#pragma unroll 4
-            for (int ls = 0; ls < kSteps; ++ls) {
+            // ---- 8 MMA pairs, all shared-memory addresses 32-bit and the
+            // per-pair offsets compile-time immediates.
+            const uint32_t wb_u = smem_u32(st + wid * G::kWBox);
+            const uint32_t xs_u = smem_u32(st + G::kWBytes + ks * G::kXBlock);
+            // B: live lanes read their plane's 16 bytes; the others a zero block
+            const uint32_t xl_u = bplane >= 0 ? xs_u + tig * 48 + bplane * 16 : zero_u;
+            const uint32_t mrow = meta_u + moff;
+            const uint32_t wl = wb_u | woff;  // box is 1024-aligned, woff < 1024
+#pragma unroll
+            for (int pr = 0; pr < kPairsPerRound; ++pr) {
+                const uint4 bv = ld_s128(xl_u + pr * 192);
                 uint32_t A[4];
-                uint2 bv = make_uint2(0u, 0u);
-                if (blive) bv = *reinterpret_cast<const uint2 *>(xl + ls * 96);
-                int32_t d[4];
-                if (MEMBER == IQK_IQ1_S_R4) {
-                    const int4 m = *reinterpret_cast<const int4 *>(meta + (ls * 8 + g) * 16);
-                    const uint32_t qg = *reinterpret_cast<const uint32_t *>(wb + g * G::kRowStride + ls * 4);
-                    const uint32_t qg8 = *reinterpret_cast<const uint32_t *>(wb + (g + 8) * G::kRowStride + ls * 4);
-                    const uint32_t h = (uint32_t)m.x;
-                    const uint32_t ig = ((qg >> (8 * tig)) & 0xffu) | (((h >> (3 * tig)) & 7u) << 8);
-                    const uint32_t ig8 = ((qg8 >> (8 * tig)) & 0xffu) | (((h >> (16 + 3 * tig)) & 7u) << 8);
-                    const uint32_t v = (uint32_t)grid[ig] | ((uint32_t)grid[ig8] << 16);
-                    const uint32_t s0 = v & 0x33333333u;
-                    const uint32_t s1 = (v >> 2) & 0x33333333u;
-                    A[0] = prmt(kTernTab, 0u, s0);
-                    A[1] = prmt(kTernTab, 0u, s0 >> 16);
-                    A[2] = prmt(kTernTab, 0u, s1);
-                    A[3] = prmt(kTernTab, 0u, s1 >> 16);
+                if (MEMBER == IQK_IQ2_KS) {
+                    const uint32_t wo = wl ^ (uint32_t)(pr << 4);
+                    const uint32_t wg = ld_s32(wo);
+                    const uint32_t wg8 = ld_s32(wo + 1024);
+                    const uint4 m = ld_s128(mrow + pr * 256);
+                    const uint32_t s0g = (wg & 0x33333333u) | m.x;
+                    const uint32_t s1g = ((wg >> 2) & 0x33333333u) | m.x;
+                    const uint32_t s0h = (wg8 & 0x33333333u) | m.y;
+                    const uint32_t s1h = ((wg8 >> 2) & 0x33333333u) | m.y;
+                    int32_t d[4];
+                    A[0] = prmt(kIq2Tab0, kIq2Tab1, s0g);
+                    A[1] = prmt(kIq2Tab0, kIq2Tab1, s0h);
+                    A[2] = prmt(kIq2Tab0, kIq2Tab1, s1g);
+                    A[3] = prmt(kIq2Tab0, kIq2Tab1, s1h);
                     mma_s8(d, A, bv.x, bv.y);
-                    // block sums of this lane's C columns: token tig>>1,
-                    // planes 2*(tig&1) and +1 (plane 3 is the stored zero)
-                    const int ct = tig >> 1, cp = 2 * (tig & 1);
-                    const int2 xb = *reinterpret_cast<const int2 *>(
-                        xs + ct * G::kXBlock + G::kXPlanes + ls * 16 + cp * 4);
-                    const int sa = (m.w & 1) ? -1 : 1, sb = (m.w & 2) ? -1 : 1;
-                    tot[0] += m.y * (8 * d[0] + sa * xb.x);
-                    tot[1] += m.y * (8 * d[1] + sa * xb.y);
-                    tot[2] += m.z * (8 * d[2] + sb * xb.x);
-                    tot[3] += m.z * (8 * d[3] + sb * xb.y);
-                } else {
-                    const uint32_t hg = lds_u16(wb + g * G::kRowStride + ls * 8 + tig * 2);
-                    const uint32_t hg8 = lds_u16(wb + (g + 8) * G::kRowStride + ls * 8 + tig * 2);
-                    const uint32_t v = hg | (hg8 << 16);
-                    uint32_t am;
-                    int4 ix;
-                    if (MEMBER == IQK_IQ2_KS) {
-                        const int4 m = *reinterpret_cast<const int4 *>(meta + (ls * 8 + g) * 16);
-                        am = (uint32_t)m.x;
-                        ix = make_int4(m.y, m.y, m.z, m.z);
-                    } else {
-                        const char *mp = meta + (ls * 8 + g) * 32;
-                        am = *reinterpret_cast<const uint32_t *>(mp + 4 * (tig >> 1));
-                        ix = *reinterpret_cast<const int4 *>(mp + 16);
-                    }
-                    const uint32_t s0 = (v & 0x33333333u) | am;
-                    const uint32_t s1 = ((v >> 2) & 0x33333333u) | am;
-                    A[0] = prmt(kIq2Tab0, kIq2Tab1, s0);
-                    A[1] = prmt(kIq2Tab0, kIq2Tab1, s0 >> 16);
-                    A[2] = prmt(kIq2Tab0, kIq2Tab1, s1);
-                    A[3] = prmt(kIq2Tab0, kIq2Tab1, s1 >> 16);
-                    mma_s8(d, A, bv.x, bv.y);
-                    tot[0] += ix.x * d[0];
-                    tot[1] += ix.y * d[1];
-                    tot[2] += ix.z * d[2];
-                    tot[3] += ix.w * d[3];
-                    if (MEMBER == IQK_IQ2_K && (ls & 7) == 7) {
-                        // end of a 256-weight super-block: fold in its fp16 scale
-                        const int s = c * kSteps + ls;
+                    A[0] = prmt(kIq2Tab0, kIq2Tab1, s0g >> 16);
+                    A[1] = prmt(kIq2Tab0, kIq2Tab1, s0h >> 16);
+                    A[2] = prmt(kIq2Tab0, kIq2Tab1, s1g >> 16);
+                    A[3] = prmt(kIq2Tab0, kIq2Tab1, s1h >> 16);
+                    mma_s8_acc(d, A, bv.z, bv.w);
+                    tot[0] += (int)m.z * d[0];
+                    tot[1] += (int)m.z * d[1];
+                    tot[2] += (int)m.w * d[2];
+                    tot[3] += (int)m.w * d[3];
+                } else if (MEMBER == IQK_IQ2_K) {
+                    const uint32_t wo = wl ^ (uint32_t)(pr << 4);
+                    const uint32_t wg = ld_s32(wo);
+                    const uint32_t wg8 = ld_s32(wo + 1024);
+                    const uint4 m = ld_s128(mrow + pr * 512);
+                    const uint32_t s0g = wg & 0x33333333u, s1g = (wg >> 2) & 0x33333333u;
+                    const uint32_t s0h = wg8 & 0x33333333u, s1h = (wg8 >> 2) & 0x33333333u;
+                    A[0] = prmt(m.x, 0u, s0g);
+                    A[1] = prmt(m.y, 0u, s0h);
+                    A[2] = prmt(m.x, 0u, s1g);
+                    A[3] = prmt(m.y, 0u, s1h);
+                    mma_s8_acc(acc1, A, bv.x, bv.y);
+                    A[0] = prmt(m.x, 0u, s0g >> 16);
+                    A[1] = prmt(m.y, 0u, s0h >> 16);
+                    A[2] = prmt(m.x, 0u, s1g >> 16);
+                    A[3] = prmt(m.y, 0u, s1h >> 16);
+                    mma_s8_acc(acc1, A, bv.z, bv.w);
+                    A[0] = prmt(m.z, 0u, s0g);
+                    A[1] = prmt(m.w, 0u, s0h);
+                    A[2] = prmt(m.z, 0u, s1g);
+                    A[3] = prmt(m.w, 0u, s1h);
+                    mma_s8_acc(acc2, A, bv.x, bv.y);
+                    A[0] = prmt(m.z, 0u, s0g >> 16);
+                    A[1] = prmt(m.w, 0u, s0h >> 16);
+                    A[2] = prmt(m.z, 0u, s1g >> 16);
+                    A[3] = prmt(m.w, 0u, s1h >> 16);
+                    mma_s8_acc(acc2, A, bv.z, bv.w);
+                    if ((pr & 3) == 3) {
+                        // end of a 256-weight super-block: fold in its fp16 scale.
+                        // Lane tig 0 holds planes 0, 1 (cols 0, 1), tig 1 plane 2.
+                        const int sbi = (c * kChunkK + pr * 64) >> 8;
                         const uint16_t *dvp = reinterpret_cast<const uint16_t *>(
                             sd + kItemRows * (n / 32) + kItemRows * (n / 128));
-                        const int32_t pg = tot[0] + tot[1], pg8 = tot[2] + tot[3];
-                        const int32_t p1g = __shfl_down_sync(0xffffffffu, pg, 1);
-                        const int32_t p2g = __shfl_down_sync(0xffffffffu, pg, 2);
-                        const int32_t p1g8 = __shfl_down_sync(0xffffffffu, pg8, 1);
-                        const int32_t p2g8 = __shfl_down_sync(0xffffffffu, pg8, 2);
+                        const int32_t u0 = acc1[0] + 4 * acc2[0], u1 = acc1[1] + 4 * acc2[1];
+                        const int32_t u2 = acc1[2] + 4 * acc2[2], u3 = acc1[3] + 4 * acc2[3];
+                        const int32_t p2g = __shfl_down_sync(0xffffffffu, u0, 1);
+                        const int32_t p2h = __shfl_down_sync(0xffffffffu, u2, 1);
                         if (tig == 0) {
                             const int ra = 16 * rt + g;
-                            const double Tg = (double)pg * 65536.0 + (double)p1g * 256.0 + (double)p2g;
-                            const double Tg8 = (double)pg8 * 65536.0 + (double)p1g8 * 256.0 + (double)p2g8;
-                            dacc[0] += (double)half_bits_to_float(dvp[ra * (n / 256) + (s >> 3)]) * Tg;
-                            dacc[1] += (double)half_bits_to_float(dvp[(ra + 8) * (n / 256) + (s >> 3)]) * Tg8;
+                            const double Tg = (double)u0 * 65536.0 + (double)u1 * 256.0 + (double)p2g;
+                            const double Th = (double)u2 * 65536.0 + (double)u3 * 256.0 + (double)p2h;
+                            dacc[0] += (double)half_bits_to_float(dvp[ra * (n / 256) + sbi]) * Tg;
+                            dacc[1] += (double)half_bits_to_float(dvp[(ra + 8) * (n / 256) + sbi]) * Th;
                         }
-                        tot[0] = tot[1] = tot[2] = tot[3] = 0;
+                        acc1[0] = acc1[1] = acc1[2] = acc1[3] = 0;
+                        acc2[0] = acc2[1] = acc2[2] = acc2[3] = 0;
                     }
+                } else {
+                    // IQ1_S_R4: this lane covers sub-groups 2h, 2h+1 of block 2*pr+side
+                    const int hsel = tig & 1;
+                    const uint32_t wo = (wl ^ (uint32_t)((pr >> 1) << 4)) + (uint32_t)((pr & 1) << 3);
+                    const uint32_t qg = ld_s32(wo);
+                    const uint32_t qg8 = ld_s32(wo + 512);
+                    const uint4 m = ld_s128(mrow + pr * 256);
+                    const uint32_t hg = m.x & 0xffffu, hh = m.x >> 16;
+                    const uint32_t bg = qg >> (16 * hsel), bh = qg8 >> (16 * hsel);
+                    const uint32_t ga = grid[(bg & 0xffu) | (((hg >> (6 * hsel)) & 7u) << 8)];
+                    const uint32_t gb = grid[((bg >> 8) & 0xffu) | (((hg >> (6 * hsel + 3)) & 7u) << 8)];
+                    const uint32_t ha = grid[(bh & 0xffu) | (((hh >> (6 * hsel)) & 7u) << 8)];
+                    const uint32_t hb = grid[((bh >> 8) & 0xffu) | (((hh >> (6 * hsel + 3)) & 7u) << 8)];
+                    const uint32_t vg = ga | (gb << 16), vh = ha | (hb << 16);
+                    const uint32_t s0g = vg & 0x33333333u, s1g = (vg >> 2) & 0x33333333u;
+                    const uint32_t s0h = vh & 0x33333333u, s1h = (vh >> 2) & 0x33333333u;
+                    int32_t d[4];
+                    A[0] = prmt(kTernTab, 0u, s0g);
+                    A[1] = prmt(kTernTab, 0u, s0h);
+                    A[2] = prmt(kTernTab, 0u, s1g);
+                    A[3] = prmt(kTernTab, 0u, s1h);
+                    mma_s8(d, A, bv.x, bv.y);
+                    A[0] = prmt(kTernTab, 0u, s0g >> 16);
+                    A[1] = prmt(kTernTab, 0u, s0h >> 16);
+                    A[2] = prmt(kTernTab, 0u, s1g >> 16);
+                    A[3] = prmt(kTernTab, 0u, s1h >> 16);
+                    mma_s8_acc(d, A, bv.z, bv.w);
+                    // block sums of this lane's two C columns (block 2*pr+side,
+                    // planes 2*(tig&1) and +1; plane 3 reads the stored zero)
+                    const uint2 xsum = ld_s64(xs_u + G::kXPlanes + (pr * 2 + side) * 16 + hsel * 8);
+                    const int ma = (int)(m.w & 0xffffu), mb = (int)(m.w >> 16);
+                    tot[0] += ma * 8 * d[0] + (int)m.y * (int)xsum.x;
+                    tot[1] += ma * 8 * d[1] + (int)m.y * (int)xsum.y;
+                    tot[2] += mb * 8 * d[2] + (int)m.z * (int)xsum.x;
+                    tot[3] += mb * 8 * d[3] + (int)m.z * (int)xsum.y;
                 }
             }
         }
 
-        if (r == cpw - 1) {
-            // ---- item end: k-quarter partials -> shared, fixed-order sum, epilogue
+        if (r == cpw - 1 && live) {
+            // ---- item end: k-quarter partials -> shared, fixed-order sum, epilogue.
+            // Named barrier 1 + rt spans the 4 warps of this row tile.
             *reinterpret_cast<int4 *>(red_i + (wid * 32 + lane) * 4) = make_int4(tot[0], tot[1], tot[2], tot[3]);
             if (MEMBER == IQK_IQ2_K) {
                 red_d[(wid * 32 + lane) * 2] = dacc[0];
                 red_d[(wid * 32 + lane) * 2 + 1] = dacc[1];
             }
-            __syncthreads();
-            if (ks == 0 && live) {
+            asm volatile("bar.sync %0, %1;\n" ::"r"(1 + rt), "r"(32 * kKSplit) : "memory");
+            if (ks == 0) {
                 const int ra = 16 * rt + g;  // item-local row
                 double yg = 0.0, yg8 = 0.0;
-                int t_out;
-                bool writer;
                 if (MEMBER == IQK_IQ2_K) {
                     for (int k = 0; k < kKSplit; ++k) {
                         yg += red_d[((rt * kKSplit + k) * 32 + lane) * 2];
                         yg8 += red_d[((rt * kKSplit + k) * 32 + lane) * 2 + 1];
                     }
-                    t_out = 0;
-                    writer = tig == 0;
                 } else {
                     int32_t s4[4] = {0, 0, 0, 0};
                     for (int k = 0; k < kKSplit; ++k) {
@@ -653,7 +842,8 @@ gemv_kernel(GemvArgs a) {
                         s4[2] += pv.z;
                         s4[3] += pv.w;
                     }
-                    // even-tig lanes hold planes (0,1) of token tig>>1, odd lanes (2, pad)
+                    // lanes tig 0/2 hold planes (0,1) of the two sides, 1/3 plane 2
+                    for (int k = 0; k < 4; ++k) s4[k] += __shfl_down_sync(0xffffffffu, s4[k], 2);
                     const int32_t n0 = __shfl_down_sync(0xffffffffu, s4[0], 1);
                     const int32_t n2 = __shfl_down_sync(0xffffffffu, s4[2], 1);
                     const double Tg = (double)s4[0] * 65536.0 + (double)s4[1] * 256.0 + (double)n0;
@@ -663,12 +853,9 @@ gemv_kernel(GemvArgs a) {
                                                    : kItemRows * (n / 16)));
                     yg = (double)half_bits_to_float(dvp[ra]) * Tg;
                     yg8 = (double)half_bits_to_float(dvp[ra + 8]) * Tg8;
-                    t_out = tig >> 1;
-                    writer = (tig & 1) == 0;
                 }
-                const int pair = t_out == 0 ? T.pair0 : T.pair1;
-                if (writer && pair >= 0) {
-                    const int S = t_out == 0 ? T.sh0 : T.sh1;
+                if (tig == 0) {
+                    const int S = T.sh0;
                     const int shift = -S - (MEMBER == IQK_IQ1_S_R4 ? 3 : 0);
                     float vg, vg8;
                     if (S == kScaleNonFinite) {
@@ -677,7 +864,7 @@ gemv_kernel(GemvArgs a) {
                         vg = (float)ldexp(yg, shift);
                         vg8 = (float)ldexp(yg8, shift);
                     }
-                    const int64_t o0 = (int64_t)pair * out + r0 + ra;
+                    const int64_t o0 = (int64_t)T.pair0 * out + r0 + ra;
                     if (a.y_dtype == IQK_F32) {
                         float *y = static_cast<float *>(a.y);
                         y[o0] = vg;
@@ -693,9 +880,23 @@ gemv_kernel(GemvArgs a) {
                     }
                 }
             }
+            asm volatile("bar.sync %0, %1;\n" ::"r"(1 + rt), "r"(32 * kKSplit) : "memory");
+        }
+        __syncwarp();
+        if (r == cpw - 1 && lane == 0) {
+            // release every stage of this item at once: its first stage holds
+            // the scale streams the later rounds and the epilogue still read
+            for (int q = j - r; q <= j; ++q) mbar_arrive(&empty[q % kStages]);
+        }
+        if (++r == cpw) {
+            r = 0;
+            ++o;
+            if (++rb == rblocks) {
+                rb = 0;
+                ++ti;
+            }
         }
     }
-    cp_async_wait<0>();
 }
 
 // ------------------------------------------------------------------- host
@@ -712,10 +913,9 @@ GemvLayout gemv_layout(int member, int64_t n, int64_t x_rows, int64_t pairs) {
     L.hdr = take(64);
     L.order = take(sizeof(int32_t) * (pairs + 1));
     L.ptok = take(sizeof(int32_t) * (pairs + 1));
-    L.tiles2 = take(sizeof(TileRef) * (pairs + 1));
     L.tiles1 = take(sizeof(TileRef) * (pairs + 1));
     L.xscale = take(sizeof(int32_t) * (x_rows + 1));
-    L.xrow_bytes = 3 * n + n / 2;  // planes [n/32][3][4][8] + block sums [n/32][4] int32
+    L.xrow_bytes = 3 * n + n / 2;  // planes [n/64][4][3][16] + block sums [n/32][4] int32
     L.xbuf = take((size_t)(x_rows * L.xrow_bytes));
     L.total = off;
     return L;
@@ -756,9 +956,36 @@ cudaError_t launch_gemv_prepare(const void *x, int x_dtype, int64_t x_rows, int 
     return cudaGetLastError();
 }
 
-cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t out_features, int n,
-                            int64_t x_rows, int64_t pairs, void *y, int y_dtype, const void *ws,
-                            cudaStream_t stream, int num_sms) {
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+static cudaError_t encode_qs_map(CUtensorMap *map, const void *qs, int64_t rows, int64_t row_bytes,
+                                 int box_bytes, bool swizzle128) {
+    using EncodeFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+    static EncodeFn encode = nullptr;
+    if (!encode) {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        cudaError_t err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+        if (err != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+        encode = reinterpret_cast<EncodeFn>(fn);
+    }
+    const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t)box_bytes, 16u};
+    const cuuint32_t estr[2] = {1u, 1u};
+    const CUresult res = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(qs), dims,
+                                strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return res == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_experts,
+                            int64_t out_features, int n, int64_t x_rows, int64_t pairs, void *y,
+                            int y_dtype, const void *ws, cudaStream_t stream, int num_sms) {
     const GemvLayout L = gemv_layout(member, n, x_rows, pairs);
     GemvArgs ga{};
     const RowBytes rb = row_bytes(member, n);
@@ -768,20 +995,27 @@ cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t out_
     ga.pairs = (int)pairs;
     ga.L = L;
     ga.ws = static_cast<const char *>(ws);
+    ga.err = reinterpret_cast<int32_t *>(const_cast<char *>(ga.ws) + L.hdr);
     ga.y = y;
     ga.y_dtype = y_dtype;
+    CUtensorMap map;
+    const bool iq1 = member == IQK_IQ1_S_R4;
+    cudaError_t err = encode_qs_map(&map, streams[0], num_experts * out_features,
+                                    iq1 ? n / 8 : n / 4, iq1 ? 64 : 128, !iq1);
+    if (err != cudaSuccess) return err;
     const int smem = gemv_smem_for(member, n);
     // Upper bound on CTA items: every pair its own tile of every row block.
     const int64_t max_items = pairs * ((out_features + kItemRows - 1) / kItemRows);
-    int64_t blocks = max_items < num_sms ? max_items : num_sms;
+    const int per_sm = member == IQK_IQ2_K ? Geo<IQK_IQ2_K>::kMinBlocks : Geo<IQK_IQ2_KS>::kMinBlocks;
+    const int64_t cap = (int64_t)num_sms * per_sm;
+    int64_t blocks = max_items < cap ? max_items : cap;
     if (blocks < 1) blocks = 1;
-    cudaError_t err = cudaSuccess;
 #define IQK_GEMV(M)                                                                          \
     do {                                                                                     \
         err = cudaFuncSetAttribute(gemv_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                    smem);                                                    \
         if (err != cudaSuccess) return err;                                                  \
-        gemv_kernel<M><<<(unsigned)blocks, kWarps * 32, smem, stream>>>(ga);                 \
+        gemv_kernel<M><<<(unsigned)blocks, kThreads, smem, stream>>>(ga, map);               \
     } while (0)
     if (member == IQK_IQ2_KS) IQK_GEMV(IQK_IQ2_KS);
     else if (member == IQK_IQ2_K) IQK_GEMV(IQK_IQ2_K);
