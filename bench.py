@@ -1,12 +1,13 @@
 """Routed-decode benchmark: IQ2_KS, 256 experts, top-6.
 
-One step = one MoE layer's routed projections for a batch of B decode
-tokens: gate and up ([2048, 4096] per expert) and down ([4096, 2048] per
-expert), each through the fused dequant+GEMV kernels of libiqk_b200.so. The
-gate and up projections share one preparation (iqk_gemv_prepare), the down
-projection gets its own (one activation row per pair).
+One step = one MoE layer's routed projections for one decode step at each
+batch size of the configuration (B = 1, 4 and 8 tokens): gate and up
+([2048, 4096] per expert) and down ([4096, 2048] per expert), each through
+the fused dequant+GEMV kernels of libiqk_b200.so. The gate and up projections
+share one preparation (iqk_gemv_prepare), the down projection gets its own
+(one activation row per pair). Per-batch figures are reported under "sweep".
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batches 1,4,8] [--impl reference]
 
 Metric: achieved GB/s of algorithmic bytes = the distinct (expert,
 projection) weight rows each step must stream (the reference's byte model,
@@ -148,9 +149,10 @@ class ClockSampler:
 
 # ---------------------------------------------------------- CPU baseline
 
-def cpu_path(batch: int, steps: int, seconds: float, seed: int) -> dict:
+def cpu_path(batches, steps: int, seconds: float, seed: int) -> dict:
     """The reference's CPU path on sampled decode steps: ik's dequantizer on
-    the selected experts' wire rows, then a float32 matvec, all host cores."""
+    the selected experts' wire rows, then a float32 matvec, all host cores.
+    One step = one decode step at each batch size in `batches`."""
     sys.path.insert(0, str(REPO / "oracle"))
     import oracle
     kind = "reference" if oracle.ref_available() else "port"
@@ -166,7 +168,7 @@ def cpu_path(batch: int, steps: int, seconds: float, seed: int) -> dict:
                                             scales="serving")
         return cache[key]
 
-    sels = make_selections(min(max(steps, 1), 256), batch, 1, seed)
+    sels_by_b = {b: make_selections(min(max(steps, 1), 64), b, 1, seed + b) for b in batches}
     rng = np.random.default_rng(seed + 1)
     pool = ThreadPoolExecutor(max_workers=cores)
 
@@ -178,27 +180,29 @@ def cpu_path(batch: int, steps: int, seconds: float, seed: int) -> dict:
 
     done, total_bytes, t_all = 0, 0.0, 0.0
     for s in range(steps):
-        sel_s = sels[s % sels.shape[0]]
-        experts = sorted(set(sel_s.ravel().tolist()))
-        for proj in ("gate", "up", "down"):
-            for e in experts:
-                wire_for(proj, e)  # generation is input staging, not timed
-        x = rng.standard_normal((batch, GATE_UP[1])).astype(np.float32)
-        xd = rng.standard_normal((batch * TOP_K, DOWN[1])).astype(np.float32)
-        jobs = [(p, e, x) for p in ("gate", "up") for e in experts] + \
-               [("down", e, xd[np.nonzero(sel_s.ravel() == e)[0]]) for e in experts]
-        t0 = time.perf_counter()
-        list(pool.map(one, jobs))
-        t_all += time.perf_counter() - t0
-        total_bytes += len(experts) * (2 * GATE_UP[0] * row_bytes(MEMBER, GATE_UP[1])
-                                       + DOWN[0] * row_bytes(MEMBER, DOWN[1]))
+        for batch in batches:
+            sels = sels_by_b[batch]
+            sel_s = sels[s % sels.shape[0]]
+            experts = sorted(set(sel_s.ravel().tolist()))
+            for proj in ("gate", "up", "down"):
+                for e in experts:
+                    wire_for(proj, e)  # generation is input staging, not timed
+            x = rng.standard_normal((batch, GATE_UP[1])).astype(np.float32)
+            xd = rng.standard_normal((batch * TOP_K, DOWN[1])).astype(np.float32)
+            jobs = [(p, e, x) for p in ("gate", "up") for e in experts] + \
+                   [("down", e, xd[np.nonzero(sel_s.ravel() == e)[0]]) for e in experts]
+            t0 = time.perf_counter()
+            list(pool.map(one, jobs))
+            t_all += time.perf_counter() - t0
+            total_bytes += len(experts) * (2 * GATE_UP[0] * row_bytes(MEMBER, GATE_UP[1])
+                                           + DOWN[0] * row_bytes(MEMBER, DOWN[1]))
         done += 1
         if t_all > seconds:
             break
     pool.shutdown()
     return {"value": total_bytes / t_all / 1e9, "unit": "GB/s", "cores": cores, "kind": kind,
-            "sample": f"{done} decode steps (B={batch}, gate+up+down of the selected experts): "
-                      f"ik dequantize + float32 numpy matvec, {cores} threads",
+            "sample": f"{done} decode steps at each B in {batches} (gate+up+down of the "
+                      f"selected experts): ik dequantize + float32 numpy matvec, {cores} threads",
             "ms_per_step": 1e3 * t_all / max(done, 1)}
 
 
@@ -206,15 +210,16 @@ def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    warm = cpu_path(args.batch, max(1, min(args.warmup, 2)), 1e9, seed=99)
+    batches = [int(b) for b in args.batches.split(",")]
+    warm = cpu_path(batches, max(1, min(args.warmup, 2)), 1e9, seed=99)
     del warm
-    res = cpu_path(args.batch, args.steps, args.cpu_seconds * 6, seed=1234)
+    res = cpu_path(batches, args.steps, args.cpu_seconds * 6, seed=1234)
     line = {
-        "impl": "reference", "metric": metric_name(args.batch), "value": round(res["value"], 4),
+        "impl": "reference", "metric": metric_name(batches), "value": round(res["value"], 4),
         "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(res["ms_per_step"], 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32 dequant, f32 matvec",
-        "data": "synthetic", "config": config(args),
+        "data": "synthetic", "config": config(args, batches),
         "cpu_baseline": {"value": round(res["value"], 4), "unit": "GB/s", "cores": res["cores"],
                          "kind": res["kind"], "sample": res["sample"]},
         "e2e": {"value": round(res["value"], 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -225,14 +230,17 @@ def run_reference(args) -> None:
 
 # ----------------------------------------------------------------- GPU
 
-def metric_name(batch: int) -> str:
-    return (f"routed decode GB/s (IQ2_KS, 256 experts top-6, gate+up+down, B={batch})")
+def metric_name(batches) -> str:
+    bs = "/".join(str(b) for b in batches)
+    return (f"routed decode GB/s (IQ2_KS, 256 experts top-6, gate+up+down, "
+            f"one step at each B in {bs})")
 
 
-def config(args) -> dict:
-    return {"workload": "BASELINE configs[1]: IQ2_KS routed decode, 256 experts top-6",
+def config(args, batches) -> dict:
+    return {"workload": "BASELINE configs[1]: IQ2_KS routed decode, 256 experts top-6, "
+                        "B = 1, 4, 8 tokens",
             "member": MEMBER, "experts": E, "top_k": TOP_K, "gate_up": list(GATE_UP),
-            "down": list(DOWN), "batch": args.batch,
+            "down": list(DOWN), "batches": batches,
             "l2": "rotating selections: no expert recurs within a window of > 2x L2 bytes",
             "parallelism": f"replicas x{args.gpus}"}
 
@@ -251,6 +259,60 @@ def random_streams(torch, out: int, n: int, gen, dev):
     return s
 
 
+class DecodeCell:
+    """One batch size of the decode workload: a pool of rotating selections and
+    activations, preallocated workspaces and outputs, and the 5-launch step."""
+
+    def __init__(self, torch, K, mods, B: int, dev, gen, seed: int):
+        self.torch, self.K, self.B = torch, K, B
+        self.gate, self.up, self.down = mods
+        window = max(1, math.ceil(2 * L2_BYTES / expert_bytes_per_step(B)))
+        self.pool = 128
+        self.sels_np = make_selections(self.pool, B, window, seed=seed)
+        self.sels = torch.from_numpy(self.sels_np).to(dev, torch.int32)
+        self.xs = torch.randn((self.pool, B, GATE_UP[1]), generator=gen, device=dev).to(torch.bfloat16)
+        self.xds = torch.randn((self.pool, B * TOP_K, DOWN[1]), generator=gen, device=dev).to(torch.bfloat16)
+        rb_gu, rb_d = row_bytes(MEMBER, GATE_UP[1]), row_bytes(MEMBER, DOWN[1])
+        self.rb_gu = rb_gu
+        act = (B * GATE_UP[1] * 2 + B * TOP_K * DOWN[1] * 2          # x, x_down (bf16)
+               + B * TOP_K * (2 * GATE_UP[0] + DOWN[0]) * 4)          # y (f32)
+        self.step_bytes = [len(set(self.sels_np[s].ravel().tolist()))
+                           * (2 * GATE_UP[0] * rb_gu + DOWN[0] * rb_d) + act
+                           for s in range(self.pool)]
+        self.pairs = B * TOP_K
+        self.ws_gu = torch.empty(K.gemv_workspace_bytes(MEMBER, GATE_UP[1], B, self.pairs),
+                                 dtype=torch.uint8, device=dev)
+        self.ws_d = torch.empty(K.gemv_workspace_bytes(MEMBER, DOWN[1], self.pairs, self.pairs),
+                                dtype=torch.uint8, device=dev)
+        self.yg = torch.empty((self.pairs, GATE_UP[0]), device=dev)
+        self.yu = torch.empty((self.pairs, GATE_UP[0]), device=dev)
+        self.yd = torch.empty((self.pairs, DOWN[0]), device=dev)
+        self.sg, self.su, self.sd = self.gate._streams(), self.up._streams(), self.down._streams()
+
+    launches = 5
+
+    def step(self, s: int) -> None:
+        K, p, B, P = self.K, s % self.pool, self.B, self.pairs
+        K.gemv_prepare(self.xs[p], E, GATE_UP[1], self.sels[p].reshape(-1), None, self.ws_gu)
+        K.gemv_run(MEMBER, self.sg, E, GATE_UP[0], GATE_UP[1], B, P, self.yg, self.ws_gu)
+        K.gemv_run(MEMBER, self.su, E, GATE_UP[0], GATE_UP[1], B, P, self.yu, self.ws_gu)
+        K.gemv_prepare(self.xds[p], E, DOWN[1], self.sels[p].reshape(-1), None, self.ws_d)
+        K.gemv_run(MEMBER, self.sd, E, DOWN[0], DOWN[1], P, P, self.yd, self.ws_d)
+
+    def bytes(self, s: int) -> int:
+        return self.step_bytes[s % self.pool]
+
+
+class _Eager:
+    """Stand-in for a CUDA graph: replays the same launches one by one (profiling)."""
+
+    def __init__(self, fn):
+        self.fn = fn
+
+    def replay(self):
+        self.fn()
+
+
 def run_b200(args) -> None:
     import torch
     import torch.distributed as dist
@@ -267,70 +329,38 @@ def run_b200(args) -> None:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    B = args.batch
     gen = torch.Generator(device=dev).manual_seed(1000 + rank)
     gate = IqkSwitchLinear(MEMBER, E, *GATE_UP, device=dev)
     up = IqkSwitchLinear(MEMBER, E, *GATE_UP, device=dev)
     down = IqkSwitchLinear(MEMBER, E, *DOWN, device=dev)
     for mod in (gate, up, down):
         mod.load_streams(random_streams(torch, mod.out_features, mod.in_features, gen, dev))
+    batches = [int(b) for b in args.batches.split(",")]
+    cells = [DecodeCell(torch, K, (gate, up, down), B, dev, gen, seed=7 + 31 * rank + B)
+             for B in batches]
 
-    window = max(1, math.ceil(2 * L2_BYTES / expert_bytes_per_step(B)))
-    pool = 128
-    sels_np = make_selections(pool, B, window, seed=7 + rank)
-    sels = torch.from_numpy(sels_np).to(dev, torch.int32)
-    xs = torch.randn((pool, B, GATE_UP[1]), generator=gen, device=dev).to(torch.bfloat16)
-    xds = torch.randn((pool, B * TOP_K, DOWN[1]), generator=gen, device=dev).to(torch.bfloat16)
-    step_bytes = []
-    rb_gu, rb_d = row_bytes(MEMBER, GATE_UP[1]), row_bytes(MEMBER, DOWN[1])
-    act_bytes = (B * GATE_UP[1] * 2 + B * TOP_K * DOWN[1] * 2            # x, x_down (bf16)
-                 + B * TOP_K * (2 * GATE_UP[0] + DOWN[0]) * 4)            # y (f32)
-    for s in range(pool):
-        d = len(set(sels_np[s].ravel().tolist()))
-        step_bytes.append(d * (2 * GATE_UP[0] * rb_gu + DOWN[0] * rb_d) + act_bytes)
-    pairs = B * TOP_K
-    ws_gu = torch.empty(K.gemv_workspace_bytes(MEMBER, GATE_UP[1], B, pairs), dtype=torch.uint8,
-                        device=dev)
-    ws_d = torch.empty(K.gemv_workspace_bytes(MEMBER, DOWN[1], pairs, pairs), dtype=torch.uint8,
-                       device=dev)
-    yg = torch.empty((pairs, GATE_UP[0]), device=dev)
-    yu = torch.empty((pairs, GATE_UP[0]), device=dev)
-    yd = torch.empty((pairs, DOWN[0]), device=dev)
-    sg, su, sd = gate._streams(), up._streams(), down._streams()
+    def step(s: int) -> None:  # one decode step at every batch size of the sweep
+        for c in cells:
+            c.step(s)
 
-    def step(s: int) -> None:
-        p = s % pool
-        K.gemv_prepare(xs[p], E, GATE_UP[1], sels[p].reshape(-1), None, ws_gu)
-        K.gemv_run(MEMBER, sg, E, GATE_UP[0], GATE_UP[1], B, pairs, yg, ws_gu)
-        K.gemv_run(MEMBER, su, E, GATE_UP[0], GATE_UP[1], B, pairs, yu, ws_gu)
-        K.gemv_prepare(xds[p], E, DOWN[1], sels[p].reshape(-1), None, ws_d)
-        K.gemv_run(MEMBER, sd, E, DOWN[0], DOWN[1], pairs, pairs, yd, ws_d)
+    def step_bytes(s: int) -> int:
+        return sum(c.bytes(s) for c in cells)
 
-    launches_per_step = 5
+    launches_per_step = sum(c.launches for c in cells)
     step(0)
     torch.cuda.synchronize()
 
-    def capture(n_steps: int, first: int):
+    def graph(fn):
+        if args.eager:
+            return _Eager(fn)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            for s in range(first, first + n_steps):
-                step(s)
+            fn()
         return g
 
     W, Kst = args.warmup, args.steps
-    if args.eager:
-        # no CUDA graphs (profiler runs): the same launches, issued one by one
-        class _Eager:
-            def __init__(self, fn):
-                self.fn = fn
-
-            def replay(self):
-                self.fn()
-        g_warm = _Eager(lambda: [step(s) for s in range(W)])
-        g_time = _Eager(lambda: [step(s) for s in range(W, W + Kst)])
-    else:
-        g_warm = capture(W, 0)
-        g_time = capture(Kst, W)
+    g_warm = graph(lambda: [step(s) for s in range(W)])
+    g_time = graph(lambda: [step(s) for s in range(W, W + Kst)])
     g_warm.replay()
     torch.cuda.synchronize()
 
@@ -339,50 +369,57 @@ def run_b200(args) -> None:
             dist.barrier()
         torch.cuda.synchronize()
 
+    def max_over_ranks(ms: float) -> float:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     stream = torch.cuda.current_stream(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    with ClockSampler(local) as clk:
+
+    def timed(g) -> float:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
         e0.record(stream)
-        g_time.replay()
+        g.replay()
         e1.record(stream)
         e1.synchronize()
-    barrier()
-    ms = e0.elapsed_time(e1)
-    ms_t = torch.tensor([ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms_max = float(ms_t.item())
-    bytes_timed = sum(step_bytes[s % pool] for s in range(W, W + Kst))
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1))
+
+    with ClockSampler(local) as clk:
+        ms_max = timed(g_time)
+    bytes_timed = sum(step_bytes(s) for s in range(W, W + Kst))
     value = world * bytes_timed / (ms_max * 1e-3) / 1e9
 
-    # ---- kernel-only roofline: the gate GEMV run over pre-prepared routings
-    nr = min(pool, 64)
-    wss = [torch.empty_like(ws_gu) for _ in range(nr)]
-    for i in range(nr):
-        K.gemv_prepare(xs[i], E, GATE_UP[1], sels[i].reshape(-1), None, wss[i])
-    reps = max(2, Kst // nr)
+    # ---- per batch size (same launches, one cell at a time)
+    sweep = {}
+    for c in cells:
+        ks = max(50, Kst // 2)
+        gw = graph(lambda c=c: [c.step(s) for s in range(3)])
+        gt = graph(lambda c=c, ks=ks: [c.step(s) for s in range(3, 3 + ks)])
+        gw.replay()
+        ms_c = timed(gt)
+        by = sum(c.bytes(s) for s in range(3, 3 + ks))
+        sweep[f"B={c.B}"] = {"GB/s": round(world * by / (ms_c * 1e-3) / 1e9, 2),
+                             "us_per_step": round(1e3 * ms_c / ks, 3),
+                             "MB_per_step": round(by / ks / 1e6, 2)}
+        del gw, gt
 
-    def kernel_loop():
-        for r in range(reps):
-            for i in range(nr):
-                K.gemv_run(MEMBER, sg, E, GATE_UP[0], GATE_UP[1], B, pairs, yg, wss[i])
-    if args.eager:
-        gk = _Eager(kernel_loop)
-    else:
-        gk = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gk):
-            kernel_loop()
+    # ---- kernel-only roofline: the gate GEMV at the largest batch, run over
+    # pre-prepared routings (rotating experts), CUDA events on its stream
+    c = cells[-1]
+    nr = min(c.pool, 64)
+    wss = [torch.empty_like(c.ws_gu) for _ in range(nr)]
+    for i in range(nr):
+        K.gemv_prepare(c.xs[i], E, GATE_UP[1], c.sels[i].reshape(-1), None, wss[i])
+    reps = max(2, Kst // nr)
+    gk = graph(lambda: [K.gemv_run(MEMBER, c.sg, E, GATE_UP[0], GATE_UP[1], c.B, c.pairs, c.yg,
+                                   wss[i]) for r in range(reps) for i in range(nr)])
     gk.replay()
-    torch.cuda.synchronize()
-    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    k0.record(stream)
-    gk.replay()
-    k1.record(stream)
-    k1.synchronize()
-    kms = k0.elapsed_time(k1) / (reps * nr)
-    gate_bytes = np.mean([len(set(sels_np[i].ravel().tolist())) * GATE_UP[0] * rb_gu
-                          + B * GATE_UP[1] * 2 + pairs * GATE_UP[0] * 4 for i in range(nr)])
+    kms = timed(gk) / (reps * nr)
+    gate_bytes = np.mean([len(set(c.sels_np[i].ravel().tolist())) * GATE_UP[0] * c.rb_gu
+                          + c.B * GATE_UP[1] * 2 + c.pairs * GATE_UP[0] * 4 for i in range(nr)])
     peaks = {}
     try:
         peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
@@ -392,69 +429,64 @@ def run_b200(args) -> None:
     peak_src = "measured" if hbm else "fallback"
     hbm = hbm or 6650.0
     achieved = gate_bytes / (kms * 1e-3) / 1e9
-    roofline = {"bound": "hbm", "kernel": "gemv_kernel<IQ2_KS> (gate, 2048x4096)",
+    roofline = {"bound": "hbm", "kernel": f"gemv_kernel<IQ2_KS> (gate 2048x4096, B={c.B})",
                 "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4), "peak_source": peak_src,
-                "us_per_launch": round(kms * 1e3, 3),
-                "bytes_per_launch": int(gate_bytes),
+                "us_per_launch": round(kms * 1e3, 3), "bytes_per_launch": int(gate_bytes),
                 "traffic": args.traffic}
 
     # ---- end to end through the public module API, host buffers
-    ne = min(Kst, 200)
-    hx = torch.randn((ne, B, 1, 1, GATE_UP[1])).to(torch.bfloat16).pin_memory()
-    hxd = torch.randn((ne, B, TOP_K, 1, DOWN[1])).to(torch.bfloat16).pin_memory()
-    hidx = torch.from_numpy(sels_np[np.arange(ne) % pool]).pin_memory()
-    hyg = torch.empty((ne, B, TOP_K, 1, GATE_UP[0])).pin_memory()
-    hyu = torch.empty((ne, B, TOP_K, 1, GATE_UP[0])).pin_memory()
-    hyd = torch.empty((ne, B, TOP_K, 1, DOWN[0])).pin_memory()
-    dx = torch.empty((B, 1, 1, GATE_UP[1]), device=dev, dtype=torch.bfloat16)
-    dxd = torch.empty((B, TOP_K, 1, DOWN[1]), device=dev, dtype=torch.bfloat16)
-    didx = torch.empty((B, TOP_K), device=dev, dtype=torch.int64)
+    ne = min(Kst, 100)
+    host = []
+    for c in cells:
+        B = c.B
+        host.append({
+            "x": torch.randn((ne, B, 1, 1, GATE_UP[1])).to(torch.bfloat16).pin_memory(),
+            "xd": torch.randn((ne, B, TOP_K, 1, DOWN[1])).to(torch.bfloat16).pin_memory(),
+            "idx": torch.from_numpy(c.sels_np[np.arange(ne) % c.pool]).pin_memory(),
+            "yg": torch.empty((ne, B, TOP_K, 1, GATE_UP[0])).pin_memory(),
+            "yu": torch.empty((ne, B, TOP_K, 1, GATE_UP[0])).pin_memory(),
+            "yd": torch.empty((ne, B, TOP_K, 1, DOWN[0])).pin_memory(),
+            "dx": torch.empty((B, 1, 1, GATE_UP[1]), device=dev, dtype=torch.bfloat16),
+            "dxd": torch.empty((B, TOP_K, 1, DOWN[1]), device=dev, dtype=torch.bfloat16),
+            "didx": torch.empty((B, TOP_K), device=dev, dtype=torch.int64)})
 
     def e2e_step(i: int):
-        dx.copy_(hx[i], non_blocking=True)
-        dxd.copy_(hxd[i], non_blocking=True)
-        didx.copy_(hidx[i], non_blocking=True)
-        hyg[i].copy_(gate(dx, didx), non_blocking=True)
-        hyu[i].copy_(up(dx, didx), non_blocking=True)
-        hyd[i].copy_(down(dxd, didx), non_blocking=True)
+        for h in host:
+            h["dx"].copy_(h["x"][i], non_blocking=True)
+            h["dxd"].copy_(h["xd"][i], non_blocking=True)
+            h["didx"].copy_(h["idx"][i], non_blocking=True)
+            h["yg"][i].copy_(gate(h["dx"], h["didx"]), non_blocking=True)
+            h["yu"][i].copy_(up(h["dx"], h["didx"]), non_blocking=True)
+            h["yd"][i].copy_(down(h["dxd"], h["didx"]), non_blocking=True)
 
     for i in range(3):
         e2e_step(i)
-    barrier()
-    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    x0.record(stream)
-    for i in range(ne):
-        e2e_step(i)
-    x1.record(stream)
-    x1.synchronize()
-    ems_t = torch.tensor([x0.elapsed_time(x1)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(ems_t, op=dist.ReduceOp.MAX)
-    ems = float(ems_t.item())
-    e_bytes = sum(step_bytes[i % pool] for i in range(ne))
-    h2d = B * GATE_UP[1] * 2 + B * TOP_K * DOWN[1] * 2 + B * TOP_K * 8
-    d2h = B * TOP_K * (2 * GATE_UP[0] + DOWN[0]) * 4
+    ems = timed(_Eager(lambda: [e2e_step(i) for i in range(ne)]))
+    e_bytes = sum(c.bytes(i) for c in cells for i in range(ne))
+    h2d = sum(c.B * GATE_UP[1] * 2 + c.B * TOP_K * DOWN[1] * 2 + c.B * TOP_K * 8 for c in cells)
+    d2h = sum(c.B * TOP_K * (2 * GATE_UP[0] + DOWN[0]) * 4 for c in cells)
     e2e = {"value": round(world * e_bytes / (ems * 1e-3) / 1e9, 2), "unit": "GB/s",
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
            "ms_per_step": round(ems / ne, 4), "steps": ne,
-           "path": "IqkSwitchLinear.__call__ x3 per step, pinned host in/out"}
+           "path": "IqkSwitchLinear.__call__ (gate, up, down) per batch size, pinned host in/out"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        res = cpu_path(B, 10 ** 6, args.cpu_seconds, seed=4321)
+        res = cpu_path(batches, 10 ** 6, args.cpu_seconds, seed=4321)
         cpu = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in res.items()
                if k in ("value", "unit", "cores", "kind", "sample")}
 
     if rank == 0:
         line = {
-            "metric": metric_name(B), "value": round(value, 2), "unit": "GB/s",
+            "metric": metric_name(batches), "value": round(value, 2), "unit": "GB/s",
             "n_gpus": world, "steps": Kst, "warmup": W,
             "ms_per_step": round(ms_max / Kst, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None,
             "dtype": "s8 x s8 -> s32 MMA, f64 epilogue (bf16 activations)",
             "data": "synthetic: random IQ2_KS streams (serving scales), x~N(0,1) bf16",
-            "config": config(args),
+            "config": config(args, batches),
+            "sweep": sweep,
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": launches_per_step * Kst,
             "clocks": clk.summary(),
@@ -470,9 +502,10 @@ def run_b200(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=50)
-    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--batches", default="1,4,8",
+                    help="decode batch sizes; one step runs one decode step at each")
     ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
