@@ -163,6 +163,30 @@ int iqk_gemv_run(int member, const void *const *streams, int64_t num_experts,
 int iqk_read_error(const void *workspace, int64_t in_features, int64_t x_rows,
                    int64_t pairs, int32_t *flags, iqk_stream_t stream);
 
+/*
+ * iqk_gemv without a workspace argument, for callers that cannot allocate
+ * device memory where they launch (a runtime with a fixed memory plan, code
+ * inside an allocator's own hooks, a binding without a device allocator).
+ * No counterpart in the reference: its kernels get their buffers from MLX.
+ *
+ * Scratch is one static device array of iqk_gemv_static_max_bytes() (1 MiB)
+ * per device; a call whose iqk_gemv_workspace_bytes exceeds it returns
+ * IQK_ERR_WORKSPACE (1 MiB holds 64 activation rows with 512 pairs at
+ * in_features 4096). Nothing is allocated and no byte of the scratch has to
+ * start at zero. The first call on each device looks up the array's address
+ * (cudaGetSymbolAddress, which may load the library's device code); make that
+ * first call outside any stream capture. All calls on one device share the
+ * one array, so calls that overlap in time on that device -- different
+ * streams, threads or processes' graphs without an ordering between them --
+ * race on it; order them on one stream. Results equal iqk_gemv's.
+ */
+size_t iqk_gemv_static_max_bytes(void);
+
+int iqk_gemv_static(int member, const void *x, int x_dtype, int64_t x_rows,
+                    const void *const *streams, int64_t num_experts, int64_t out_features,
+                    int64_t in_features, const int32_t *sel, const int32_t *tok,
+                    int64_t pairs, void *y, int y_dtype, iqk_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

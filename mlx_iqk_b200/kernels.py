@@ -106,6 +106,10 @@ def library() -> ctypes.CDLL:
     lib.iqk_gemv_run.restype = i32
     lib.iqk_read_error.argtypes = [vp, i64, i64, i64, ctypes.POINTER(ctypes.c_int32), vp]
     lib.iqk_read_error.restype = i32
+    lib.iqk_gemv_static_max_bytes.restype = sz
+    lib.iqk_gemv_static.argtypes = [i32, vp, i32, i64, vp, i64, i64, i64, vp, vp, i64, vp, i32,
+                                    vp]
+    lib.iqk_gemv_static.restype = i32
     _LIB = lib
     return lib
 
@@ -114,7 +118,7 @@ def exported_symbols() -> list[str]:
     """C ABI entry points declared in include/iqk_b200.h."""
     return ["iqk_status_string", "iqk_abi_version", "iqk_check_device", "iqk_dequant",
             "iqk_gemv_workspace_bytes", "iqk_gemv", "iqk_gemv_prepare", "iqk_gemv_run",
-            "iqk_read_error"]
+            "iqk_read_error", "iqk_gemv_static_max_bytes", "iqk_gemv_static"]
 
 
 def raise_for_status(status: int, what: str) -> None:
@@ -208,6 +212,21 @@ def gemv_run(member: str, streams, num_experts: int, out_features: int, in_featu
         pairs, y.data_ptr(), DTYPE_IDS[y.dtype], workspace.data_ptr(), workspace.numel(),
         stream_handle(y.device))
     raise_for_status(status, "iqk_gemv_run")
+    return y
+
+
+def gemv_static(member: str, x: torch.Tensor, streams, num_experts: int, out_features: int,
+                in_features: int, sel: torch.Tensor, tok: torch.Tensor | None,
+                y: torch.Tensor) -> torch.Tensor:
+    """``iqk_gemv_static``: as :func:`gemv`, scratch in the library's static device array."""
+    lib = library()
+    check_device(y.device)
+    status = lib.iqk_gemv_static(
+        MEMBER_IDS[member], x.data_ptr(), DTYPE_IDS[x.dtype], x.shape[0], ptr_array(streams),
+        num_experts, out_features, in_features, sel.data_ptr(),
+        None if tok is None else tok.data_ptr(), sel.numel(), y.data_ptr(), DTYPE_IDS[y.dtype],
+        stream_handle(y.device))
+    raise_for_status(status, "iqk_gemv_static")
     return y
 
 
