@@ -49,6 +49,9 @@ GATE_UP = (2048, 4096)   # out, in
 DOWN = (4096, 2048)
 MEMBER = "iq2_ks"
 L2_BYTES = 126 * 2 ** 20
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate GEMV launch at B=8,
+# measured by ncu on this kernel build (reported as roofline.traffic).
+GATE_B8_DRAM_BYTES = 111.57e6
 
 
 def row_bytes(member: str, n: int) -> int:
@@ -513,7 +516,7 @@ def main() -> None:
                     help="experts per projection (256 = the benchmark; fewer for profiling)")
     ap.add_argument("--eager", action="store_true",
                     help="launch kernels one by one instead of replaying CUDA graphs (profiling)")
-    ap.add_argument("--traffic", type=float, default=None,
+    ap.add_argument("--traffic", type=float, default=GATE_B8_DRAM_BYTES,
                     help="dram bytes per GEMV launch from an ncu capture (reported as is)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
