@@ -164,6 +164,45 @@ int iqk_read_error(const void *workspace, int64_t in_features, int64_t x_rows,
                    int64_t pairs, int32_t *flags, iqk_stream_t stream);
 
 /*
+ * Grouped per-expert GEMM for prefill-sized calls (many pairs per expert):
+ *   y[p, r] = sum_k W[sel[p], r, k] * x[tok[p], k]
+ * with the same argument meaning as iqk_gemv. Pairs are sorted by expert on
+ * the device and each expert's weights are read once per tile of up to 128
+ * of its pairs, dequantized into tensor memory and multiplied on the tensor
+ * cores (f16 operands, f32 accumulation). Members IQK_IQ2_KS and IQK_IQ2_K;
+ * out_features a multiple of 16; num_experts at most 4096. IQ2_KS weights
+ * reach the tensor cores exactly (integer products, row scale in the
+ * epilogue); IQ2_K weights carry two f16 roundings.
+ *
+ * Replaces the prefill route of IqkSwitchLinear.__call__: dequantized() then
+ * mx.gather_mm(..., sorted_indices) (src/mlx_iqk/nn.py:221-238).
+ *
+ * iqk_grouped_workspace_bytes: workspace size (routing tables plus one f16
+ * activation row per pair). iqk_grouped_prepare / iqk_grouped_run split the
+ * call like iqk_gemv_prepare / iqk_gemv_run (the split has no reference
+ * counterpart); the error word reads back with iqk_grouped_read_error.
+ */
+size_t iqk_grouped_workspace_bytes(int64_t in_features, int64_t num_experts, int64_t pairs);
+
+int iqk_grouped_gemm(int member, const void *x, int x_dtype, int64_t x_rows,
+                     const void *const *streams, int64_t num_experts, int64_t out_features,
+                     int64_t in_features, const int32_t *sel, const int32_t *tok,
+                     int64_t pairs, void *y, int y_dtype, void *workspace,
+                     size_t workspace_bytes, iqk_stream_t stream);
+
+int iqk_grouped_prepare(const void *x, int x_dtype, int64_t x_rows, int64_t in_features,
+                        int64_t num_experts, const int32_t *sel, const int32_t *tok,
+                        int64_t pairs, void *workspace, size_t workspace_bytes,
+                        iqk_stream_t stream);
+
+int iqk_grouped_run(int member, const void *const *streams, int64_t num_experts,
+                    int64_t out_features, int64_t in_features, int64_t pairs, void *y,
+                    int y_dtype, const void *workspace, size_t workspace_bytes,
+                    iqk_stream_t stream);
+
+int iqk_grouped_read_error(const void *workspace, int32_t *flags, iqk_stream_t stream);
+
+/*
  * iqk_gemv without a workspace argument, for callers that cannot allocate
  * device memory where they launch (a runtime with a fixed memory plan, code
  * inside an allocator's own hooks, a binding without a device allocator).

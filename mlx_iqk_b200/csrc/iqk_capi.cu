@@ -8,6 +8,7 @@
 
 #include "iqk_common.cuh"
 #include "iqk_gemv.cuh"
+#include "iqk_grouped.cuh"
 
 namespace {
 
@@ -168,6 +169,85 @@ int iqk_gemv(int member, const void *x, int x_dtype, int64_t x_rows,
     if (st != IQK_OK) return st;
     return iqk_gemv_run(member, streams, num_experts, out_features, in_features, x_rows, pairs,
                         y, y_dtype, workspace, workspace_bytes, stream);
+}
+
+size_t iqk_grouped_workspace_bytes(int64_t in_features, int64_t num_experts, int64_t pairs) {
+    if (!width_ok(in_features) || num_experts <= 0 || pairs < 0) return 0;
+    return grouped_layout(in_features, num_experts, pairs).total;
+}
+
+int iqk_grouped_prepare(const void *x, int x_dtype, int64_t x_rows, int64_t in_features,
+                        int64_t num_experts, const int32_t *sel, const int32_t *tok,
+                        int64_t pairs, void *workspace, size_t workspace_bytes,
+                        iqk_stream_t stream) {
+    int st = check_prepare(in_features, num_experts, x_rows, pairs, tok, x_dtype);
+    if (st != IQK_OK) return st;
+    if (pairs == 0) return IQK_OK;
+    if (!x || !sel || !workspace) return IQK_ERR_ARGUMENT;
+    if (!aligned(x, 16) || !aligned(workspace, 256)) return IQK_ERR_ALIGNMENT;
+    if (workspace_bytes < grouped_layout(in_features, num_experts, pairs).total)
+        return IQK_ERR_WORKSPACE;
+    return cuda_status(launch_grouped_prepare(x, x_dtype, x_rows, (int)in_features, num_experts,
+                                              sel, tok, pairs, workspace,
+                                              reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int iqk_grouped_run(int member, const void *const *streams, int64_t num_experts,
+                    int64_t out_features, int64_t in_features, int64_t pairs, void *y,
+                    int y_dtype, const void *workspace, size_t workspace_bytes,
+                    iqk_stream_t stream) {
+    if (!member_ok(member)) return IQK_ERR_MEMBER;
+    if (member == IQK_IQ1_S_R4) return IQK_ERR_GEOMETRY;
+    if (!width_ok(in_features)) return IQK_ERR_WIDTH;
+    if (num_experts <= 0 || num_experts > 4096) return IQK_ERR_GEOMETRY;
+    if (out_features <= 0 || out_features % 16) return IQK_ERR_GEOMETRY;
+    if (num_experts * out_features > (int64_t)1 << 30) return IQK_ERR_GEOMETRY;
+    if (pairs < 0 || pairs > (1 << 24)) return IQK_ERR_GEOMETRY;
+    if (!dtype_ok(y_dtype)) return IQK_ERR_ARGUMENT;
+    if (pairs == 0) return IQK_OK;
+    if (!y || !workspace) return IQK_ERR_ARGUMENT;
+    if (!aligned(y, 4) || !aligned(workspace, 256)) return IQK_ERR_ALIGNMENT;
+    const int st = check_streams(member, streams);
+    if (st != IQK_OK) return st;
+    if (workspace_bytes < grouped_layout(in_features, num_experts, pairs).total)
+        return IQK_ERR_WORKSPACE;
+    return cuda_status(launch_grouped_run(member, streams, num_experts, out_features,
+                                          (int)in_features, pairs, y, y_dtype, workspace,
+                                          reinterpret_cast<cudaStream_t>(stream),
+                                          num_sms_current()));
+}
+
+int iqk_grouped_gemm(int member, const void *x, int x_dtype, int64_t x_rows,
+                     const void *const *streams, int64_t num_experts, int64_t out_features,
+                     int64_t in_features, const int32_t *sel, const int32_t *tok, int64_t pairs,
+                     void *y, int y_dtype, void *workspace, size_t workspace_bytes,
+                     iqk_stream_t stream) {
+    if (!member_ok(member)) return IQK_ERR_MEMBER;
+    if (member == IQK_IQ1_S_R4) return IQK_ERR_GEOMETRY;
+    int st = check_prepare(in_features, num_experts, x_rows, pairs, tok, x_dtype);
+    if (st != IQK_OK) return st;
+    if (out_features <= 0 || out_features % 16) return IQK_ERR_GEOMETRY;
+    if (!dtype_ok(y_dtype)) return IQK_ERR_ARGUMENT;
+    if (pairs == 0) return IQK_OK;
+    if (!y || !streams) return IQK_ERR_ARGUMENT;
+    st = check_streams(member, streams);
+    if (st != IQK_OK) return st;
+    st = iqk_grouped_prepare(x, x_dtype, x_rows, in_features, num_experts, sel, tok, pairs,
+                             workspace, workspace_bytes, stream);
+    if (st != IQK_OK) return st;
+    return iqk_grouped_run(member, streams, num_experts, out_features, in_features, pairs, y,
+                           y_dtype, workspace, workspace_bytes, stream);
+}
+
+int iqk_grouped_read_error(const void *workspace, int32_t *flags, iqk_stream_t stream) {
+    if (!workspace || !flags) return IQK_ERR_ARGUMENT;
+    *flags = 0;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    int32_t hdr0 = 0;
+    cudaError_t err = cudaMemcpyAsync(&hdr0, workspace, sizeof(int32_t), cudaMemcpyDeviceToHost, s);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    if (err == cudaSuccess) *flags = hdr0;
+    return cuda_status(err);
 }
 
 int iqk_read_error(const void *workspace, int64_t in_features, int64_t x_rows, int64_t pairs,

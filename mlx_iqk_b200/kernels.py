@@ -106,6 +106,17 @@ def library() -> ctypes.CDLL:
     lib.iqk_gemv_run.restype = i32
     lib.iqk_read_error.argtypes = [vp, i64, i64, i64, ctypes.POINTER(ctypes.c_int32), vp]
     lib.iqk_read_error.restype = i32
+    lib.iqk_grouped_workspace_bytes.argtypes = [i64, i64, i64]
+    lib.iqk_grouped_workspace_bytes.restype = sz
+    lib.iqk_grouped_gemm.argtypes = [i32, vp, i32, i64, vp, i64, i64, i64, vp, vp, i64, vp, i32,
+                                     vp, sz, vp]
+    lib.iqk_grouped_gemm.restype = i32
+    lib.iqk_grouped_prepare.argtypes = [vp, i32, i64, i64, i64, vp, vp, i64, vp, sz, vp]
+    lib.iqk_grouped_prepare.restype = i32
+    lib.iqk_grouped_run.argtypes = [i32, vp, i64, i64, i64, i64, vp, i32, vp, sz, vp]
+    lib.iqk_grouped_run.restype = i32
+    lib.iqk_grouped_read_error.argtypes = [vp, ctypes.POINTER(ctypes.c_int32), vp]
+    lib.iqk_grouped_read_error.restype = i32
     lib.iqk_gemv_static_max_bytes.restype = sz
     lib.iqk_gemv_static.argtypes = [i32, vp, i32, i64, vp, i64, i64, i64, vp, vp, i64, vp, i32,
                                     vp]
@@ -118,7 +129,9 @@ def exported_symbols() -> list[str]:
     """C ABI entry points declared in include/iqk_b200.h."""
     return ["iqk_status_string", "iqk_abi_version", "iqk_check_device", "iqk_dequant",
             "iqk_gemv_workspace_bytes", "iqk_gemv", "iqk_gemv_prepare", "iqk_gemv_run",
-            "iqk_read_error", "iqk_gemv_static_max_bytes", "iqk_gemv_static"]
+            "iqk_read_error", "iqk_grouped_workspace_bytes", "iqk_grouped_gemm",
+            "iqk_grouped_prepare", "iqk_grouped_run", "iqk_grouped_read_error",
+            "iqk_gemv_static_max_bytes", "iqk_gemv_static"]
 
 
 def raise_for_status(status: int, what: str) -> None:
@@ -228,6 +241,64 @@ def gemv_static(member: str, x: torch.Tensor, streams, num_experts: int, out_fea
         stream_handle(y.device))
     raise_for_status(status, "iqk_gemv_static")
     return y
+
+
+GROUPED_MEMBERS = ("iq2_ks", "iq2_k")
+"""Members the tensor-core grouped GEMM (prefill route) covers."""
+
+
+def grouped_workspace_bytes(in_features: int, num_experts: int, pairs: int) -> int:
+    return int(library().iqk_grouped_workspace_bytes(in_features, num_experts, pairs))
+
+
+def grouped(member: str, x: torch.Tensor, streams, num_experts: int, out_features: int,
+            in_features: int, sel: torch.Tensor, tok: torch.Tensor | None, y: torch.Tensor,
+            workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """``iqk_grouped_gemm``: x [x_rows, in], sel/tok int32 [pairs], y [pairs, out]."""
+    lib = library()
+    check_device(y.device)
+    pairs = sel.numel()
+    need = grouped_workspace_bytes(in_features, num_experts, pairs)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=y.device)
+    status = lib.iqk_grouped_gemm(
+        MEMBER_IDS[member], x.data_ptr(), DTYPE_IDS[x.dtype], x.shape[0], ptr_array(streams),
+        num_experts, out_features, in_features, sel.data_ptr(),
+        None if tok is None else tok.data_ptr(), pairs, y.data_ptr(), DTYPE_IDS[y.dtype],
+        workspace.data_ptr(), workspace.numel(), stream_handle(y.device))
+    raise_for_status(status, "iqk_grouped_gemm")
+    return y
+
+
+def grouped_prepare(x: torch.Tensor, num_experts: int, in_features: int, sel: torch.Tensor,
+                    tok: torch.Tensor | None, workspace: torch.Tensor) -> torch.Tensor:
+    lib = library()
+    check_device(workspace.device)
+    status = lib.iqk_grouped_prepare(
+        x.data_ptr(), DTYPE_IDS[x.dtype], x.shape[0], in_features, num_experts,
+        sel.data_ptr(), None if tok is None else tok.data_ptr(), sel.numel(),
+        workspace.data_ptr(), workspace.numel(), stream_handle(workspace.device))
+    raise_for_status(status, "iqk_grouped_prepare")
+    return workspace
+
+
+def grouped_run(member: str, streams, num_experts: int, out_features: int, in_features: int,
+                pairs: int, y: torch.Tensor, workspace: torch.Tensor) -> torch.Tensor:
+    lib = library()
+    status = lib.iqk_grouped_run(
+        MEMBER_IDS[member], ptr_array(streams), num_experts, out_features, in_features, pairs,
+        y.data_ptr(), DTYPE_IDS[y.dtype], workspace.data_ptr(), workspace.numel(),
+        stream_handle(y.device))
+    raise_for_status(status, "iqk_grouped_run")
+    return y
+
+
+def grouped_read_error(workspace: torch.Tensor) -> int:
+    flags = ctypes.c_int32(0)
+    raise_for_status(library().iqk_grouped_read_error(workspace.data_ptr(), ctypes.byref(flags),
+                                                      stream_handle(workspace.device)),
+                     "iqk_grouped_read_error")
+    return int(flags.value)
 
 
 def read_error(workspace: torch.Tensor, in_features: int, x_rows: int, pairs: int) -> int:

@@ -203,10 +203,16 @@ class IqkSwitchLinear(nn.Module):
         ``x`` is ``[..., 1, 1, in]`` (one row per token, shared by its top_k
         experts) or ``[..., top_k, 1, in]`` (one row per pair); ``indices``
         is ``[..., top_k]``; the result is ``[..., top_k, 1, out]`` float32.
-        Decode-sized calls (``<= DECODE_MAT_LIMIT`` pairs, unsorted) and
-        prefill-sized ones both run the union GEMV kernel today; the routing
-        split is kept so a prefill-shaped call can take a grouped-GEMM route.
+        Decode-sized calls (``<= DECODE_MAT_LIMIT`` pairs, unsorted) run the
+        fused dequant + GEMV; prefill-sized or ``sorted_indices=True`` calls
+        run the tensor-core grouped GEMM (``src/mlx_iqk/nn.py:221-238`` makes
+        the same split, with dequantize + ``gather_mm`` on the prefill side).
+        ``iq1_s_r4`` has no grouped kernel and always takes the GEMV.
         """
+        pairs = int(np.prod(tuple(indices.shape))) if hasattr(indices, "shape") else \
+            int(np.asarray(indices).size)
+        if self.member in K.GROUPED_MEMBERS and (sorted_indices or pairs > DECODE_MAT_LIMIT):
+            return self.grouped(x, indices)
         return self.gemv(x, indices)
 
     def _prep(self, x: torch.Tensor) -> torch.Tensor:
@@ -237,6 +243,25 @@ class IqkSwitchLinear(nn.Module):
         y = torch.empty((mats, self.out_features), dtype=torch.float32, device=self.device)
         K.gemv(self.member, xt, self._streams(), self.num_experts, self.out_features,
                self.in_features, sel, None, y)
+        return y.reshape(*idx_shape, self.out_features).unsqueeze(-2)
+
+    def grouped(self, x, indices) -> torch.Tensor:
+        """Tensor-core grouped GEMM over the selected experts (the prefill route);
+        same operands and result shape as :meth:`gemv`."""
+        if self.member not in K.GROUPED_MEMBERS:
+            raise IqkKernelError(
+                f"the grouped GEMM covers {K.GROUPED_MEMBERS}; {self.member!r} uses gemv")
+        xt = self._prep(x)
+        idx_shape = tuple(indices.shape)
+        sel = self._idx(indices, self.device)
+        mats, rows = sel.numel(), xt.shape[0]
+        if rows <= 0 or mats % rows:
+            raise IqkRuntimeError(
+                f"{mats} token-expert pairs do not tile {rows} activation "
+                f"row(s); the operand and the routing disagree")
+        y = torch.empty((mats, self.out_features), dtype=torch.float32, device=self.device)
+        K.grouped(self.member, xt, self._streams(), self.num_experts, self.out_features,
+                  self.in_features, sel, None, y)
         return y.reshape(*idx_shape, self.out_features).unsqueeze(-2)
 
     def _gemv_toks(self, x, sorted_ids, toks) -> torch.Tensor:
