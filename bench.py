@@ -248,18 +248,94 @@ def config(args, batches) -> dict:
             "parallelism": f"replicas x{args.gpus}"}
 
 
-def random_streams(torch, out: int, n: int, gen, dev):
-    """Uniform random IQ2_KS relayout streams on the device, serving scales."""
+def random_streams(torch, out: int, n: int, gen, dev, member: str = "iq2_ks"):
+    """Uniform random relayout streams on the device, serving scales."""
     def u8(count):
         return torch.randint(0, 256, (count,), generator=gen, device=dev, dtype=torch.uint8)
-    s = {"qs": u8(E * out * n // 4).view(torch.uint32).reshape(E, out, n // 16),
-         "scl": u8(E * out * n // 64).reshape(E, out, n // 64),
-         "sch": u8(E * out * n // 256).reshape(E, out, n // 256),
-         "sex": u8(E * out * n // 256).reshape(E, out, n // 256)}
-    mag = torch.rand((E, out), generator=gen, device=dev) * 8e-4 + 2e-5
-    sign = torch.where(torch.rand((E, out), generator=gen, device=dev) < 0.5, -1.0, 1.0)
-    s["dv"] = (mag * sign).to(torch.float16)
-    return s
+
+    def scales(shape):
+        mag = torch.rand(shape, generator=gen, device=dev) * 8e-4 + 2e-5
+        sign = torch.where(torch.rand(shape, generator=gen, device=dev) < 0.5, -1.0, 1.0)
+        return (mag * sign).to(torch.float16)
+
+    if member == "iq2_ks":
+        return {"qs": u8(E * out * n // 4).view(torch.uint32).reshape(E, out, n // 16),
+                "scl": u8(E * out * n // 64).reshape(E, out, n // 64),
+                "sch": u8(E * out * n // 256).reshape(E, out, n // 256),
+                "sex": u8(E * out * n // 256).reshape(E, out, n // 256),
+                "dv": scales((E, out))}
+    return {"qs": u8(E * out * n // 4).view(torch.uint32).reshape(E, out, n // 16),
+            "scl": u8(E * out * n // 32).reshape(E, out, n // 32),
+            "sex": u8(E * out * n // 128).reshape(E, out, n // 128),
+            "dv": scales((E, out, n // 256))}
+
+
+# ---------------------------------------------------------------- prefill
+
+PREFILL_TOKENS = 2048
+
+
+def prefill_flops(pairs: int) -> float:
+    return 2.0 * pairs * (2 * GATE_UP[0] * GATE_UP[1] + DOWN[0] * DOWN[1])
+
+
+class PrefillLayer:
+    """BASELINE config 5 on one GPU: one MoE layer, gate/up IQ2_KS and down
+    IQ2_K over all 256 experts, T tokens routed top-6 by N(0,1) logits
+    (mildly skewed load), sorted_indices=True, through the grouped GEMM.
+    Step = prepare(x) + gate + up + SiLU(gate)*up + prepare(h) + down +
+    router-weighted combine."""
+
+    def __init__(self, torch, K, dev, gen, tokens: int = PREFILL_TOKENS):
+        from mlx_iqk_b200 import IqkSwitchLinear
+        self.torch, self.K, self.T = torch, K, tokens
+        self.gate = IqkSwitchLinear("iq2_ks", E, *GATE_UP, device=dev)
+        self.up = IqkSwitchLinear("iq2_ks", E, *GATE_UP, device=dev)
+        self.down = IqkSwitchLinear("iq2_k", E, *DOWN, device=dev)
+        for mod in (self.gate, self.up, self.down):
+            mod.load_streams(random_streams(torch, mod.out_features, mod.in_features, gen, dev,
+                                            mod.member))
+        logits = torch.randn((tokens, E), generator=gen, device=dev)
+        top = torch.topk(logits, TOP_K, dim=-1)
+        self.weights = torch.softmax(top.values, dim=-1)
+        self.sel = top.indices.to(torch.int32).reshape(-1).contiguous()
+        self.pairs = self.sel.numel()
+        self.x = torch.randn((tokens, GATE_UP[1]), generator=gen, device=dev).to(torch.bfloat16)
+        self.ws_gu = torch.empty(K.grouped_workspace_bytes(GATE_UP[1], E, self.pairs),
+                                 dtype=torch.uint8, device=dev)
+        self.ws_d = torch.empty(K.grouped_workspace_bytes(DOWN[1], E, self.pairs),
+                                dtype=torch.uint8, device=dev)
+        self.yg = torch.empty((self.pairs, GATE_UP[0]), device=dev)
+        self.yu = torch.empty((self.pairs, GATE_UP[0]), device=dev)
+        self.h = torch.empty((self.pairs, DOWN[1]), device=dev, dtype=torch.bfloat16)
+        self.yd = torch.empty((self.pairs, DOWN[0]), device=dev)
+        self.out = torch.empty((tokens, DOWN[0]), device=dev)
+        counts = torch.bincount(self.sel.long(), minlength=E).cpu()
+        self.load = {"max_pairs_per_expert": int(counts.max()),
+                     "min_pairs_per_expert": int(counts.min())}
+
+    def gate_up(self):
+        K = self.K
+        K.grouped_prepare(self.x, E, GATE_UP[1], self.sel, None, self.ws_gu)
+        K.grouped_run("iq2_ks", self.gate._streams(), E, GATE_UP[0], GATE_UP[1], self.pairs,
+                      self.yg, self.ws_gu)
+        K.grouped_run("iq2_ks", self.up._streams(), E, GATE_UP[0], GATE_UP[1], self.pairs,
+                      self.yu, self.ws_gu)
+
+    def down_proj(self):
+        K = self.K
+        K.grouped_prepare(self.h, E, DOWN[1], self.sel, None, self.ws_d)
+        K.grouped_run("iq2_k", self.down._streams(), E, DOWN[0], DOWN[1], self.pairs, self.yd,
+                      self.ws_d)
+
+    def step(self):
+        torch = self.torch
+        self.gate_up()
+        torch.mul(torch.nn.functional.silu(self.yg), self.yu, out=self.yg)
+        self.h.copy_(self.yg)
+        self.down_proj()
+        torch.sum(self.yd.view(self.T, TOP_K, DOWN[0]) * self.weights.unsqueeze(-1), dim=1,
+                  out=self.out)
 
 
 class DecodeCell:
@@ -438,6 +514,55 @@ def run_b200(args) -> None:
                 "us_per_launch": round(kms * 1e3, 3), "bytes_per_launch": int(gate_bytes),
                 "traffic": args.traffic}
 
+    # ---- prefill (config 5) on this GPU: the grouped GEMM layer
+    prefill = None
+    if not args.no_prefill:
+        pl = PrefillLayer(torch, K, dev, gen)
+        pl.step()
+        torch.cuda.synchronize()
+        ps = max(5, args.prefill_steps)
+        gpw = graph(lambda: [pl.step() for _ in range(3)])
+        gpt = graph(lambda: [pl.step() for _ in range(ps)])
+        gpw.replay()
+        pms = timed(gpt) / ps
+        # kernel-level: each grouped GEMM alone, repeated (same routing)
+        reps = 10
+        gk_g = graph(lambda: [K.grouped_run("iq2_ks", pl.gate._streams(), E, GATE_UP[0],
+                                            GATE_UP[1], pl.pairs, pl.yg, pl.ws_gu)
+                              for _ in range(reps)])
+        gk_d = graph(lambda: [K.grouped_run("iq2_k", pl.down._streams(), E, DOWN[0], DOWN[1],
+                                            pl.pairs, pl.yd, pl.ws_d) for _ in range(reps)])
+        pl.gate_up()
+        pl.down_proj()
+        gk_g.replay()
+        gk_d.replay()
+        g_ms = timed(gk_g) / reps
+        d_ms = timed(gk_d) / reps
+        tf_peak = peaks.get("bf16_tflops") or 1590.0
+        g_fl = 2.0 * pl.pairs * GATE_UP[0] * GATE_UP[1]
+        d_fl = 2.0 * pl.pairs * DOWN[0] * DOWN[1]
+        layer_fl = prefill_flops(pl.pairs)
+        prefill = {
+            "metric": "prefill tokens/s (config 5 layer: gate/up IQ2_KS, down IQ2_K, "
+                      "256 experts top-6, sorted_indices=True)",
+            "value": round(world * pl.T / (pms * 1e-3), 1), "unit": "tokens/s",
+            "tokens_per_gpu": pl.T, "ms_per_step": round(pms, 4),
+            "layer_tflops": round(layer_fl / (pms * 1e-3) / 1e12, 1),
+            "load": pl.load,
+            "gemm": {
+                "gate_or_up_us": round(g_ms * 1e3, 2),
+                "gate_or_up_tflops": round(g_fl / (g_ms * 1e-3) / 1e12, 1),
+                "down_us": round(d_ms * 1e3, 2),
+                "down_tflops": round(d_fl / (d_ms * 1e-3) / 1e12, 1),
+                "bound": "tensor", "peak_tflops": tf_peak,
+                "peak_source": "measured" if peaks.get("bf16_tflops") else "fallback",
+                "frac_gate_or_up": round(g_fl / (g_ms * 1e-3) / 1e12 / tf_peak, 4),
+                "frac_down": round(d_fl / (d_ms * 1e-3) / 1e12 / tf_peak, 4),
+            },
+            "parallelism": f"replicas x{world}",
+        }
+        del gpw, gpt, gk_g, gk_d, pl
+
     # ---- end to end through the public module API, host buffers
     ne = min(Kst, 100)
     host = []
@@ -494,6 +619,7 @@ def run_b200(args) -> None:
             "gpu_launches": launches_per_step * Kst,
             "clocks": clk.summary(),
             "hbm_frac_of_step": round(value / world / hbm, 4),
+            "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     del g_warm, g_time, gk
@@ -516,6 +642,8 @@ def main() -> None:
                     help="experts per projection (256 = the benchmark; fewer for profiling)")
     ap.add_argument("--eager", action="store_true",
                     help="launch kernels one by one instead of replaying CUDA graphs (profiling)")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (config 5) leg")
+    ap.add_argument("--prefill-steps", type=int, default=20)
     ap.add_argument("--traffic", type=float, default=GATE_B8_DRAM_BYTES,
                     help="dram bytes per GEMV launch from an ncu capture (reported as is)")
     args = ap.parse_args()

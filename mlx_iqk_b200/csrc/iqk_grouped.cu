@@ -55,19 +55,40 @@ namespace {
 
 using namespace dev;
 
-constexpr int kThreadsG = 384;
-constexpr int kProducer = 0, kIssuer = 1, kDq0 = 4;
-constexpr int kStageK = 128;                        // weights per k-stage
-constexpr int kStagesG = 4;
-constexpr int kCodeTile = kGroupRows * kStageK / 4;  // 4 KB of 2-bit codes
-constexpr int kXAtom = kGroupTok * 128;             // 16 KB: 128 rows x 64 f16
-constexpr int kXTile = 2 * kXAtom;
-constexpr int kStageBytesG = kXTile + kCodeTile;     // 36 KB, 1024-aligned
+constexpr int kThreadsG = 800;                       // 25 warps
+constexpr int kProducer = 0, kTmemWarp = 1, kLoader0 = 2, kDq0 = 4, kCodeWarp = 20,
+              kIssuer0 = 21;
+constexpr int kDqGroups = 4;                         // dequant warps per TMEM lane quarter
+constexpr int kStageK = 128;                         // weights per k-stage (8 MMAs of K=16)
+constexpr int kGroups = 4;                           // dequant groups = MMA issuers = A slots
+constexpr int kMaxKS = 4096 / kStageK;               // k-stages of the widest row
+constexpr int kCodeK = 512;                          // weights per code load (4 stages)
+constexpr int kCodeSlot = kGroupRows * kCodeK / 4;   // 16 KB: 128 rows x 128 B, 128-byte swizzle
+constexpr int kMaxCodeSlots = 4;
+constexpr int kMaxXSlots = 8;
+constexpr int kMinXSlots = 4;
+// Group h dequantizes stages g = h (mod 4) into A slot h and its issuer warp
+// runs their MMAs into accumulator h. Reusing slot h waits for the stage-done
+// barrier of stage g - 4, never lapped while awaited because xslots >= 4.
 constexpr int kTmemCols = 512;
-constexpr int kDCol = 0;                             // D: columns [0, 128)
-constexpr int kACol = 128;                           // A: 4 stages x 64 columns
-constexpr int kBarBytes = 8 * (3 * kStagesG + 3) + 16;
-constexpr int kSmemG = 1024 + kStagesG * kStageBytesG + kBarBytes;
+// TMEM columns: accumulators 0-3 (64 columns each, one per group), then the
+// 4 A slots of 64 columns. Each issuer waits on shared-memory barriers only
+// for its own group's stages, so a wait never stalls another group's MMAs;
+// the epilogue sums the four accumulators in a fixed order.
+constexpr int kTok = 64;                             // tokens per work tile
+constexpr uint32_t kACol = kGroups * kTok;
+constexpr int kBarBytes = 8 * (2 * kMaxXSlots + 2 * kMaxCodeSlots + kGroups + 3 + 4) + 16;
+constexpr int kSmemCap = 227 * 1024;
+
+// Per-item scale buffer: per (stage, row) scale words, transposed so that a
+// warp's 32 rows read 32 consecutive words; then row factors and the tile's
+// column table (pair index, 2^-S).
+__host__ __device__ constexpr int scale_words(int member) { return member == IQK_IQ2_K ? 2 : 1; }
+__host__ __device__ constexpr int scale_buf_bytes(int member, int n) {
+    return scale_words(member) * (n / kStageK) * kGroupRows * 4 + 2 * kGroupRows * 4 +
+           kGroupTokMax * 4;
+}
+__host__ __device__ constexpr int x_slot_bytes(int tok_cap) { return tok_cap * 2 * 128; }
 
 // f16x2 alphabet pairs {V[4a], V[4a+1]} and {V[4a+2], V[4a+3]}, IQ2NL values
 // (-31, -13, 1, 17) and (-26, -8, 6, 22).
@@ -140,10 +161,11 @@ __device__ __forceinline__ int block_scan(int v, int *warp_tot, int *total) {
 }
 
 // One block: bucket the pairs by expert, cut each bucket into tiles of at
-// most kGroupTok tokens. Shared memory: counts, then scatter cursors.
+// most L.tok_cap tokens. Shared memory: counts, then scatter cursors.
 __global__ void __launch_bounds__(1024)
 grouped_route_kernel(const int32_t *__restrict__ sel, const int32_t *__restrict__ tok, int pairs,
                      int x_rows, int num_experts, GroupedLayout L, char *ws) {
+    const int cap = L.tok_cap;
     extern __shared__ int32_t cnt[];
     __shared__ int32_t warp_tot[33];
     __shared__ int32_t s_bad, s_tail;
@@ -170,15 +192,15 @@ grouped_route_kernel(const int32_t *__restrict__ sel, const int32_t *__restrict_
     int c_cnt = 0, c_tiles = 0;
     for (int e = b0; e < b1; ++e) {
         c_cnt += cnt[e];
-        c_tiles += (cnt[e] + kGroupTok - 1) / kGroupTok;
+        c_tiles += (cnt[e] + cap - 1) / cap;
     }
     int n_valid, n_tiles;
     int run = block_scan(c_cnt, warp_tot, &n_valid);
     int trun = block_scan(c_tiles, warp_tot, &n_tiles);
     for (int e = b0; e < b1; ++e) {
         const int c = cnt[e];
-        for (int i = 0; i * kGroupTok < c; ++i)
-            tiles[trun++] = make_int4(e, run + i * kGroupTok, min(kGroupTok, c - i * kGroupTok), 0);
+        for (int i = 0; i * cap < c; ++i)
+            tiles[trun++] = make_int4(e, run + i * cap, min(cap, c - i * cap), 0);
         cnt[e] = run;  // becomes the scatter cursor
         run += c;
     }
@@ -266,7 +288,9 @@ grouped_convert_kernel(const XT *__restrict__ x, const int32_t *__restrict__ tok
         amax = fmaxf(amax, red[w]);
         bad |= redb[w];
     }
-    const int S = (bad || amax == 0.f) ? 0 : 14 - ilogbf(amax);
+    // S <= 126 keeps 2^-S a normal float for the epilogue; only rows whose
+    // maximum is below 2^-112 are then not fully normalised.
+    const int S = (bad || amax == 0.f) ? 0 : min(14 - ilogbf(amax), 126);
     if (tid == 0) {
         reinterpret_cast<int32_t *>(ws + L.pscale)[pos] = S;
         if (bad) atomicOr(reinterpret_cast<int32_t *>(ws + L.hdr), IQK_DEVERR_NONFINITE);
@@ -290,10 +314,17 @@ grouped_convert_kernel(const XT *__restrict__ x, const int32_t *__restrict__ tok
 
 // ------------------------------------------------------------- GEMM kernel
 
+// Activation tensor maps, one per box height 16, 32, ..., 128 rows: a tile's
+// k-atom then arrives in one copy of exactly its padded token count.
+struct XMaps {
+    CUtensorMap m[kGroupTokMax / 16];
+};
+
 struct GroupedArgs {
     const void *s[5];
     int64_t out_features;
     int n, pairs, rblocks;
+    int xslots, cslots, tok_cap;  // ring depths (activation, code), token cap
     const char *ws;
     GroupedLayout L;
     int32_t *err;
@@ -306,45 +337,180 @@ __device__ __forceinline__ void store_out(void *y, int64_t i, float v) {
     static_cast<T *>(y)[i] = from_float<T>(v);
 }
 
+__device__ __forceinline__ uint4 ldg128(const void *p) {
+    return __ldg(reinterpret_cast<const uint4 *>(p));
+}
+
+// Scale loader (2 warps): one item's scale streams for its 128 rows, repacked
+// per (stage, row) into the transposed buffer, plus row factors and the
+// tile's column table. Each thread owns rows t and t + 64.
+template <int MEMBER>
+__device__ __forceinline__ void load_item_scales(const GroupedArgs &a, int4 tl, int rb, int t,
+                                                 uint32_t *sc, float *rsc, int32_t *colp,
+                                                 float *colf) {
+    const int n = a.n, KS = n / kStageK;
+    const bool wide = n == 4096;
+    const int64_t out = a.out_features;
+    // column table first: independent loads
+    const int32_t *order = reinterpret_cast<const int32_t *>(a.ws + a.L.order);
+    const int32_t *pscale = reinterpret_cast<const int32_t *>(a.ws + a.L.pscale);
+    for (int j = t; j < tl.z; j += 64) {
+        colp[j] = order[tl.y + j];
+        colf[j] = __int_as_float((127 - pscale[tl.y + j]) << 23);  // 2^-S, S <= 126
+    }
+#pragma unroll 1
+    for (int rr = 0; rr < 2; ++rr) {
+        const int r = t + 64 * rr;
+        const int64_t rl = (int64_t)rb * kGroupRows + r;
+        const int64_t row = (int64_t)tl.x * out + (rl < out ? rl : 0);
+        if (MEMBER == IQK_IQ2_KS) {
+            // every load of the row is issued before any is used
+            const uint8_t *scl = static_cast<const uint8_t *>(a.s[1]) + row * (n / 64);
+            const uint8_t *sch = static_cast<const uint8_t *>(a.s[2]) + row * (n / 256);
+            const uint8_t *sex = static_cast<const uint8_t *>(a.s[3]) + row * (n / 256);
+            uint4 v[4];
+            uint2 hb[2], xb[2];
+            v[0] = ldg128(scl);
+            v[1] = ldg128(scl + 16);
+            if (wide) {
+                v[2] = ldg128(scl + 32);
+                v[3] = ldg128(scl + 48);
+            }
+            hb[0] = __ldg(reinterpret_cast<const uint2 *>(sch));
+            xb[0] = __ldg(reinterpret_cast<const uint2 *>(sex));
+            if (wide) {
+                hb[1] = __ldg(reinterpret_cast<const uint2 *>(sch + 8));
+                xb[1] = __ldg(reinterpret_cast<const uint2 *>(sex + 8));
+            }
+            const uint16_t dvb = static_cast<const uint16_t *>(a.s[4])[row];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {  // 8 stages per 16 scl bytes
+                if (c >= n / 1024) break;
+                const uint32_t sv[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+                const uint32_t h32 = (c & 1) ? hb[c >> 1].y : hb[c >> 1].x;
+                const uint32_t x32 = (c & 1) ? xb[c >> 1].y : xb[c >> 1].x;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t lo = (sv[j >> 1] >> (16 * (j & 1))) & 0xffffu;
+                    const uint32_t hi = (h32 >> (4 * j)) & 15u, al = (x32 >> (4 * j)) & 15u;
+                    sc[(8 * c + j) * kGroupRows + r] = lo | (hi << 16) | (al << 20);
+                }
+            }
+            rsc[r] = half_bits_to_float(dvb);
+        } else {
+            const uint8_t *scl = static_cast<const uint8_t *>(a.s[1]) + row * (n / 32);
+            const uint8_t *sex = static_cast<const uint8_t *>(a.s[2]) + row * (n / 128);
+            const uint16_t *dv = static_cast<const uint16_t *>(a.s[3]) + row * (n / 256);
+            uint4 v[8], xv[2], dq[2];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (i < n / 512) v[i] = ldg128(scl + 16 * i);
+            xv[0] = ldg128(sex);
+            dq[0] = ldg128(dv);
+            if (wide) {
+                xv[1] = ldg128(sex + 16);
+                dq[1] = ldg128(dv + 8);
+            }
+            const int nd = n / 256;
+            float m = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                if (i >= nd) break;
+                const uint32_t w = reinterpret_cast<const uint32_t *>(&dq[i >> 3])[(i & 7) >> 1];
+                m = fmaxf(m, fabsf(half_bits_to_float((uint16_t)(w >> (16 * (i & 1))))));
+            }
+            const int E = m > 0.f ? ilogbf(m) + 1 : 0;
+            rsc[r] = ldexpf(1.f, E);
+            const float dn = ldexpf(1.f, -E);
+#pragma unroll
+            for (int ks = 0; ks < 32; ++ks) {
+                if (ks >= KS) break;
+                const uint32_t s32 = reinterpret_cast<const uint32_t *>(&v[ks >> 2])[ks & 3];
+                const uint32_t x32 = reinterpret_cast<const uint32_t *>(&xv[ks >> 4])[(ks & 15) >> 2];
+                const int di = ks >> 1;
+                const uint32_t dw = reinterpret_cast<const uint32_t *>(&dq[di >> 3])[(di & 7) >> 1];
+                const float d = half_bits_to_float((uint16_t)(dw >> (16 * (di & 1)))) * dn;
+                const __half dh = __float2half_rn(d);
+                const uint32_t db = (uint32_t)*reinterpret_cast<const uint16_t *>(&dh);
+                sc[ks * kGroupRows + r] = s32;
+                sc[(KS + ks) * kGroupRows + r] = ((x32 >> (8 * (ks & 3))) & 0xffu) | (db << 16);
+            }
+        }
+    }
+}
+
+// Shared-memory carve-up of the GEMM kernel (base 1024-aligned).
+struct GemmSmem {
+    uint32_t x, code, sbuf, bars;  // offsets
+    int sb;                        // bytes of one scale buffer
+};
+__host__ __device__ inline GemmSmem gemm_smem(int member, int n, int tok_cap, int xslots,
+                                              int cslots) {
+    GemmSmem g;
+    g.x = 0;
+    g.code = (uint32_t)(xslots * x_slot_bytes(tok_cap));
+    g.sbuf = g.code + cslots * kCodeSlot;
+    g.sb = (scale_buf_bytes(member, n) + 15) & ~15;
+    g.bars = g.sbuf + 2 * g.sb;
+    return g;
+}
+
 template <int MEMBER>
 __global__ void __launch_bounds__(kThreadsG, 1)
 grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_map,
-                    const __grid_constant__ CUtensorMap x_map) {
+                    const __grid_constant__ XMaps x_maps) {
     extern __shared__ char smem_raw[];
     char *smem = smem_raw + ((1024u - (saddr(smem_raw) & 1023u)) & 1023u);
-    const uint32_t stage_u = saddr(smem);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStagesG * kStageBytesG);
-    uint64_t *aready = full + kStagesG;
-    uint64_t *empty = aready + kStagesG;
-    uint64_t *dfull = empty + kStagesG;
+    const uint32_t smem_u = saddr(smem);
+    const int n = a.n, KS = n / kStageK, XS = a.xslots, CS = a.cslots;
+    const int cap = a.tok_cap;
+    const GemmSmem G = gemm_smem(MEMBER, n, cap, XS, CS);
+    const uint32_t xatom = (uint32_t)cap * 128u;  // bytes of one 64-wide k atom
+    char *sbuf = smem + G.sbuf;
+    // xfull: a stage's activations landed; sdone: the stage's MMAs finished
+    // (frees its activation slot and, four stages later, its TMEM A slot).
+    uint64_t *xfull = reinterpret_cast<uint64_t *>(smem + G.bars);
+    uint64_t *sdone = xfull + kMaxXSlots;
+    uint64_t *cfull = sdone + kMaxXSlots;
+    uint64_t *cempty = cfull + kMaxCodeSlots;
+    uint64_t *aready = cempty + kMaxCodeSlots;
+    uint64_t *dfull = aready + kGroups;
     uint64_t *dempty = dfull + 1;
     uint64_t *drain = dempty + 1;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    uint64_t *sfull = drain + 1;   // [2]
+    uint64_t *sempty = sfull + 2;  // [2]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sempty + 2);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int32_t *hdr = reinterpret_cast<const int32_t *>(a.ws + a.L.hdr);
     const int4 *tiles = reinterpret_cast<const int4 *>(a.ws + a.L.tiles);
     const int32_t *order = reinterpret_cast<const int32_t *>(a.ws + a.L.order);
-    const int32_t *pscale = reinterpret_cast<const int32_t *>(a.ws + a.L.pscale);
-    const int n = a.n, KS = n / kStageK;
     const int64_t out = a.out_features;
     const int ntiles = hdr[1], n_valid = hdr[2];
     const int64_t items = (int64_t)ntiles * a.rblocks;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kStagesG; ++i) {
-            bar_init(&full[i], 1);
-            bar_init(&aready[i], 4);
-            bar_init(&empty[i], 1);
+        for (int i = 0; i < XS; ++i) {
+            bar_init(&xfull[i], 1);
+            bar_init(&sdone[i], 1);
         }
-        bar_init(dfull, 1);
-        bar_init(dempty, 8);
-        bar_init(drain, 1);
+        for (int i = 0; i < CS; ++i) {
+            bar_init(&cfull[i], 1);
+            bar_init(&cempty[i], 4 * kDqGroups);
+        }
+        for (int i = 0; i < kGroups; ++i) bar_init(&aready[i], 4);
+        bar_init(dfull, kGroups);
+        bar_init(dempty, 4 * kDqGroups);
+        bar_init(drain, kGroups);
+        for (int i = 0; i < 2; ++i) {
+            bar_init(&sfull[i], 64);
+            bar_init(&sempty[i], 4 * kDqGroups);
+        }
         *abort_flag = 0;
         bar_fence_init();
     }
-    if (warp == kIssuer) {
+    if (warp == kTmemWarp) {
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
         tc_fence_before();
@@ -374,71 +540,96 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
     };
 
     if (warp == kProducer) {
-        if (lane == 0) {
-            int g = 0;
-            for (int64_t it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
-                const int4 tl = tiles[it / a.rblocks];
-                const int rb = (int)(it % a.rblocks);
-                const int npad = (tl.z + 15) & ~15;
-                const int row0 = (int)((int64_t)tl.x * out + (int64_t)rb * kGroupRows);
-                const uint32_t bytes = (uint32_t)(kCodeTile + 2 * npad * 128);
-                for (int ks = 0; ks < KS; ++ks, ++g) {
-                    const int slot = g % kStagesG;
-                    const uint32_t use = (uint32_t)(g / kStagesG);
-                    if (!bar_wait(&empty[slot], (use & 1u) ^ 1u, abort_flag)) {
-                        give_up();
-                        break;
-                    }
-                    const uint32_t st = stage_u + slot * kStageBytesG;
-                    bar_expect_tx(&full[slot], bytes);
-                    tma_2d(st + kXTile, &qs_map, ks * (kStageK / 4), row0, &full[slot]);
-#pragma unroll 1
-                    for (int atom = 0; atom < 2; ++atom)
-#pragma unroll 1
-                        for (int b = 0; b < npad; b += 16)
-                            tma_2d(st + atom * kXAtom + b * 128, &x_map,
-                                   ks * kStageK + atom * 64, tl.y + b, &full[slot]);
+        // Activation stages: lane 0 keeps the ring, lanes 0-1 issue the two
+        // 64-wide k atoms of a stage in one instruction.
+        int g = 0;
+        bool ok = true;
+        for (int64_t it = blockIdx.x; ok && it < items && !*abort_flag; it += gridDim.x) {
+            const int4 tl = tiles[it / a.rblocks];
+            const int npad = (tl.z + 15) & ~15;
+            const CUtensorMap *xm = &x_maps.m[npad / 16 - 1];
+            for (int ks = 0; ks < KS; ++ks, ++g) {
+                const int xs = g % XS;
+                if (lane == 0) {
+                    ok = bar_wait(&sdone[xs], ((uint32_t)(g / XS) & 1u) ^ 1u, abort_flag);
+                    if (ok) bar_expect_tx(&xfull[xs], (uint32_t)(2 * npad * 128));
                 }
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                const uint32_t st = smem_u + G.x + xs * x_slot_bytes(cap);
+                if (lane < 2)
+                    tma_2d(st + lane * xatom, xm, ks * kStageK + lane * 64, tl.y, &xfull[xs]);
             }
-            // Drain: the last stages' copies must land before the CTA exits,
-            // aborted or not (bounded by time only).
-            for (int d = 0; d < kStagesG && d < g; ++d) {
+        }
+        if (lane == 0) {
+            if (!ok) give_up();
+            // Drain: every copy issued must land before the CTA exits (bounded by time only).
+            for (int d = 0; d < XS && d < g; ++d) {
                 const int gg = g - 1 - d;
-                if (!bar_wait(&full[gg % kStagesG], (uint32_t)(gg / kStagesG) & 1u, nullptr))
-                    give_up();
+                if (!bar_wait(&xfull[gg % XS], (uint32_t)(gg / XS) & 1u, nullptr)) give_up();
             }
         }
         __syncwarp();
-    } else if (warp == kIssuer) {
+    } else if (warp == kCodeWarp) {
+        // Code chunks (512 weights of 128 rows) run ahead on their own ring.
+        if (lane == 0) {
+            int cchunk = 0;
+            bool ok = true;
+            for (int64_t it = blockIdx.x; ok && it < items && !*abort_flag; it += gridDim.x) {
+                const int4 tl = tiles[it / a.rblocks];
+                const int rb = (int)(it % a.rblocks);
+                const int row0 = (int)((int64_t)tl.x * out + (int64_t)rb * kGroupRows);
+                for (int c = 0; c < KS / 4; ++c, ++cchunk) {
+                    const int cs = cchunk % CS;
+                    if (!bar_wait(&cempty[cs], ((uint32_t)(cchunk / CS) & 1u) ^ 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    bar_expect_tx(&cfull[cs], kCodeSlot);
+                    tma_2d(smem_u + G.code + cs * kCodeSlot, &qs_map, c * (kCodeK / 4), row0,
+                           &cfull[cs]);
+                }
+            }
+            if (!ok) give_up();
+            for (int d = 0; d < CS && d < cchunk; ++d) {
+                const int cc = cchunk - 1 - d;
+                if (!bar_wait(&cfull[cc % CS], (uint32_t)(cc / CS) & 1u, nullptr)) give_up();
+            }
+        }
+        __syncwarp();
+    } else if (warp >= kIssuer0) {
+        // MMA issuer of group h: the stages g = h (mod 4), into accumulator h.
+        const int h = warp - kIssuer0;
         if (lane == 0) {
             int g = 0, item_i = 0;
             for (int64_t it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++item_i) {
                 const int4 tl = tiles[it / a.rblocks];
                 const int npad = (tl.z + 15) & ~15;
                 const uint32_t idesc = idesc_f16(kGroupRows, npad);
+                // accumulator h is free once the previous item's epilogue read it
                 if (item_i > 0 && !bar_wait(dempty, (uint32_t)(item_i - 1) & 1u, abort_flag)) {
                     give_up();
                     break;
                 }
-                tc_fence_after();
-                bool ok = true;
+                bool ok = true, first = true;
                 for (int ks = 0; ks < KS; ++ks, ++g) {
-                    const int slot = g % kStagesG;
-                    const uint32_t par = (uint32_t)(g / kStagesG) & 1u;
-                    if (!bar_wait(&full[slot], par, abort_flag) ||
-                        !bar_wait(&aready[slot], par, abort_flag)) {
+                    if ((g & 3) != h) continue;
+                    const int xs = g % XS;
+                    if (!bar_wait(&xfull[xs], (uint32_t)(g / XS) & 1u, abort_flag) ||
+                        !bar_wait(&aready[h], (uint32_t)(g >> 2) & 1u, abort_flag)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t st = stage_u + slot * kStageBytesG;
+                    const uint32_t st = smem_u + G.x + xs * x_slot_bytes(cap);
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk) {
-                        const uint64_t bdesc = sw128_desc(st + (kk >> 2) * kXAtom + (kk & 3) * 32);
-                        tc_mma_ts(tmem + kDCol, tmem + kACol + slot * 64 + kk * 8, bdesc, idesc,
-                                  (ks | kk) != 0);
+                        const uint64_t bdesc = sw128_desc(st + (kk >> 2) * xatom + (kk & 3) * 32);
+                        tc_mma_ts(tmem + h * kTok, tmem + kACol + h * 64 + kk * 8, bdesc, idesc,
+                                  (first && kk == 0) ? 0u : 1u);
                     }
-                    tc_commit(&empty[slot]);
+                    first = false;
+                    tc_commit(&sdone[xs]);
                 }
                 if (!ok) {
                     give_up();
@@ -448,16 +639,33 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
             }
             // Every MMA issued must finish before tensor memory is freed.
             tc_commit(drain);
-            if (!bar_wait(drain, 0, nullptr)) give_up();
         }
         __syncwarp();
-    } else if (warp >= kDq0) {
+    } else if (warp >= kLoader0 && warp < kDq0) {
+        const int t = threadIdx.x - 32 * kLoader0;  // 0..63
+        int item_i = 0;
+        for (int64_t it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++item_i) {
+            const int buf = item_i & 1;
+            const uint32_t use = (uint32_t)(item_i >> 1);
+            if (!bar_wait(&sempty[buf], (use & 1u) ^ 1u, abort_flag)) {
+                give_up();
+                break;
+            }
+            char *b = sbuf + buf * G.sb;
+            uint32_t *sc = reinterpret_cast<uint32_t *>(b);
+            float *rsc = reinterpret_cast<float *>(b + scale_words(MEMBER) * KS * kGroupRows * 4);
+            load_item_scales<MEMBER>(a, tiles[it / a.rblocks], (int)(it % a.rblocks), t, sc, rsc,
+                                     reinterpret_cast<int32_t *>(rsc + kGroupRows),
+                                     rsc + 2 * kGroupRows);
+            bar_arrive(&sfull[buf]);
+        }
+    } else if (warp >= kDq0 && warp < kCodeWarp) {
         const int dq = warp - kDq0;
         const int q = warp & 3;        // TMEM lane quarter this warp may access
-        const int h = dq >> 2;         // stage parity this warp dequantizes
+        const int h = dq >> 2;         // stages g with g % 4 == h (TMEM slot h)
         const int rloc = 32 * q + lane;
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
-        const uint32_t sw = (uint32_t)((rloc >> 2) & 1);  // 32-byte swizzle of this row
+        const uint32_t rsw = (uint32_t)(rloc & 7);  // 128-byte swizzle of this code row
         int g = 0, item_i = 0;
         for (int64_t it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++item_i) {
             const int4 tl = tiles[it / a.rblocks];
@@ -465,83 +673,72 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
             const int npad = (tl.z + 15) & ~15;
             const int64_t rlocal = (int64_t)rb * kGroupRows + rloc;
             const bool row_ok = rlocal < out;
-            const int64_t row = (int64_t)tl.x * out + (row_ok ? rlocal : 0);
-            float rscale;  // epilogue factor of this row (before 2^-S)
-            float dnorm = 1.f;  // IQ2_K: 2^-E applied to the super-block scales
-            if (MEMBER == IQK_IQ2_KS) {
-                rscale = half_bits_to_float(static_cast<const uint16_t *>(a.s[4])[row]);
-            } else {
-                const uint16_t *dv = static_cast<const uint16_t *>(a.s[3]) + row * (n / 256);
-                float m = 0.f;
-                for (int i = 0; i < n / 256; ++i) m = fmaxf(m, fabsf(half_bits_to_float(dv[i])));
-                const int E = m > 0.f ? ilogbf(m) + 1 : 0;
-                dnorm = ldexpf(1.f, -E);
-                rscale = ldexpf(1.f, E);
+            const int buf = item_i & 1;
+            if (!bar_wait(&sfull[buf], (uint32_t)(item_i >> 1) & 1u, abort_flag)) {
+                give_up();
+                break;
             }
+            const char *b = sbuf + buf * G.sb;
+            const uint32_t *sc = reinterpret_cast<const uint32_t *>(b);
+            const float *rsc =
+                reinterpret_cast<const float *>(b + scale_words(MEMBER) * KS * kGroupRows * 4);
+            const int32_t *colp = reinterpret_cast<const int32_t *>(rsc + kGroupRows);
+            const float *colf = rsc + 2 * kGroupRows;
+            const float rscale = rsc[rloc];
             for (int ks = 0; ks < KS; ++ks, ++g) {
-                if ((g & 1) != h) continue;
-                const int slot = g % kStagesG;
-                const uint32_t par = (uint32_t)(g / kStagesG) & 1u;
-                // Scale bytes of this stage (global, cached in L1 across stages).
-                uint32_t sc0, sc1;
-                if (MEMBER == IQK_IQ2_KS) {
-                    const uint8_t *scl = static_cast<const uint8_t *>(a.s[1]);
-                    const uint8_t *sch = static_cast<const uint8_t *>(a.s[2]);
-                    const uint8_t *sex = static_cast<const uint8_t *>(a.s[3]);
-                    const int sh = 4 * (ks & 1);
-                    sc0 = *reinterpret_cast<const uint16_t *>(scl + row * (n / 64) + 2 * ks);
-                    sc1 = ((uint32_t)(sch[row * (n / 256) + (ks >> 1)] >> sh) & 15u) |
-                          (((uint32_t)(sex[row * (n / 256) + (ks >> 1)] >> sh) & 15u) << 4);
-                } else {
-                    const uint8_t *scl = static_cast<const uint8_t *>(a.s[1]);
-                    const uint8_t *sex = static_cast<const uint8_t *>(a.s[2]);
-                    const uint16_t *dv = static_cast<const uint16_t *>(a.s[3]);
-                    sc0 = *reinterpret_cast<const uint32_t *>(scl + row * (n / 32) + 4 * ks);
-                    sc1 = (uint32_t)sex[row * (n / 128) + ks] |
-                          ((uint32_t)dv[row * (n / 256) + (ks >> 1)] << 16);
+                if ((g & 3) != h) continue;
+                const int chunk = g >> 2, cs = chunk % CS;
+                const uint32_t s0 = sc[ks * kGroupRows + rloc];
+                const uint32_t s1 = scale_words(MEMBER) == 2 ? sc[(KS + ks) * kGroupRows + rloc] : 0u;
+                if (!bar_wait(&cfull[cs], (uint32_t)(chunk / CS) & 1u, abort_flag)) {
+                    give_up();
+                    break;
                 }
-                if (!bar_wait(&full[slot], par, abort_flag) ||
-                    !bar_wait(&empty[slot], par ^ 1u, abort_flag)) {
+                // this stage's 32 code bytes: 16-byte chunks 2h, 2h+1 of the row
+                const uint32_t code_u = smem_u + G.code + cs * kCodeSlot + rloc * 128;
+                const uint4 c0 = lds128(code_u + (((uint32_t)(2 * h) ^ rsw) << 4));
+                const uint4 c1 = lds128(code_u + (((uint32_t)(2 * h + 1) ^ rsw) << 4));
+                __syncwarp();
+                if (lane == 0) bar_arrive(&cempty[cs]);
+                // A slot h was last read by stage g - 4
+                if (g >= kGroups && !bar_wait(&sdone[(g - kGroups) % XS],
+                                              (uint32_t)((g - kGroups) / XS) & 1u, abort_flag)) {
                     give_up();
                     break;
                 }
                 tc_fence_after();
-                const uint32_t code_u = stage_u + slot * kStageBytesG + kXTile + rloc * 32;
-                const uint4 c0 = lds128(code_u + ((0u ^ sw) << 4));
-                const uint4 c1 = lds128(code_u + ((1u ^ sw) << 4));
                 const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                const uint32_t taddr = tmem + lane_base + kACol + h * 64;
                 float dsb = 0.f;
-                if (MEMBER == IQK_IQ2_K) dsb = half_bits_to_float((uint16_t)(sc1 >> 16)) * dnorm;
+                if (MEMBER == IQK_IQ2_K) dsb = __half2float(__ushort_as_half((uint16_t)(s1 >> 16)));
+                uint32_t t01 = 0, t23 = 0;
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    uint32_t r[32];
-#pragma unroll
-                    for (int wi = 0; wi < 4; ++wi) {
-                        const int wd = 4 * half + wi;  // word within the stage
-                        uint32_t t01, t23;
-                        if (MEMBER == IQK_IQ2_KS) {
-                            const int gq = wd >> 1;    // 32-weight group within the stage
-                            const int idx = (int)(((sc0 >> (4 * gq)) & 15u) |
-                                                  (((sc1 >> gq) & 1u) << 4)) - 16;
-                            const int alpha = (int)((sc1 >> (4 + gq)) & 1u);
-                            const uint32_t hi = h2_bcast((float)idx);
-                            t01 = hmul2_bits(hi, alpha ? kV01a1 : kV01a0);
-                            t23 = hmul2_bits(hi, alpha ? kV23a1 : kV23a0);
-                        } else {
-                            const int idx = (int)((sc0 >> (4 * wd)) & 15u) - 8;
-                            const int alpha = (int)((sc1 >> wd) & 1u);
-                            const uint32_t hi = h2_bcast(dsb * (float)idx);
-                            t01 = hmul2_bits(hi, alpha ? kV01a1 : kV01a0);
-                            t23 = hmul2_bits(hi, alpha ? kV23a1 : kV23a0);
+                for (int wd = 0; wd < 8; ++wd) {
+                    if (MEMBER == IQK_IQ2_KS) {
+                        if ((wd & 1) == 0) {  // one 32-weight group per two words
+                            const int gq = wd >> 1;
+                            const int idx = (int)(((s0 >> (4 * gq)) & 15u) |
+                                                  (((s0 >> (16 + gq)) & 1u) << 4)) - 16;
+                            const bool alpha = (s0 >> (20 + gq)) & 1u;
+                            const uint32_t hv = h2_bcast((float)idx);
+                            t01 = hmul2_bits(hv, alpha ? kV01a1 : kV01a0);
+                            t23 = hmul2_bits(hv, alpha ? kV23a1 : kV23a0);
                         }
-                        expand_word(words[wd], t01, t23, &r[8 * wi]);
+                    } else {
+                        const int idx = (int)((s0 >> (4 * wd)) & 15u) - 8;
+                        const bool alpha = (s1 >> wd) & 1u;
+                        const uint32_t hv = h2_bcast(dsb * (float)idx);
+                        t01 = hmul2_bits(hv, alpha ? kV01a1 : kV01a0);
+                        t23 = hmul2_bits(hv, alpha ? kV23a1 : kV23a0);
                     }
-                    tmem_st32(tmem + lane_base + kACol + slot * 64 + half * 32, r);
+                    uint32_t r[8];
+                    expand_word(words[wd], t01, t23, r);
+                    tmem_st8(taddr + wd * 8, r);
                 }
                 tc_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) bar_arrive(&aready[slot]);
+                if (lane == 0) bar_arrive(&aready[h]);
             }
             if (*abort_flag) break;
             // Epilogue: D rows are this thread's output row, columns the tile's tokens.
@@ -550,18 +747,26 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
                 break;
             }
             tc_fence_after();
-            for (int c = 8 * h; c < npad; c += 16) {
-                uint32_t d[8];
-                tmem_ld8(tmem + lane_base + kDCol + c, d);
-                tc_wait_ld();
+            for (int c = 8 * h; c < npad; c += 8 * kDqGroups) {
+                float sum[8];
+                {
+                    uint32_t d0[8], d1[8], d2[8], d3[8];
+                    tmem_ld8(tmem + lane_base + c, d0);
+                    tmem_ld8(tmem + lane_base + kTok + c, d1);
+                    tmem_ld8(tmem + lane_base + 2 * kTok + c, d2);
+                    tmem_ld8(tmem + lane_base + 3 * kTok + c, d3);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        sum[j] = ((__uint_as_float(d0[j]) + __uint_as_float(d1[j])) +
+                                  __uint_as_float(d2[j])) + __uint_as_float(d3[j]);
+                }
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     const int col = c + j;
                     if (col < tl.z && row_ok) {
-                        const int64_t p = order[tl.y + col];
-                        const int S = pscale[tl.y + col];
-                        const float v = ldexpf(__uint_as_float(d[j]) * rscale, -S);
-                        const int64_t o = p * out + rlocal;
+                        const int64_t o = (int64_t)colp[col] * out + rlocal;
+                        const float v = sum[j] * rscale * colf[col];
                         if (a.y_dtype == IQK_F32) store_out<float>(a.y, o, v);
                         else if (a.y_dtype == IQK_F16) store_out<__half>(a.y, o, v);
                         else store_out<__nv_bfloat16>(a.y, o, v);
@@ -570,11 +775,16 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) bar_arrive(dempty);
+            if (lane == 0) {
+                bar_arrive(dempty);
+                bar_arrive(&sempty[buf]);
+            }
         }
     }
     __syncthreads();
-    if (warp == kIssuer) {
+    if (warp == kTmemWarp) {
+        if (lane == 0 && !bar_wait(drain, 0, nullptr)) give_up();
+        __syncwarp();
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
@@ -616,7 +826,9 @@ GroupedLayout grouped_layout(int64_t n, int64_t num_experts, int64_t pairs) {
         off += (bytes + 255) & ~size_t(255);
         return at;
     };
-    L.max_tiles = (num_experts < pairs ? num_experts : pairs) + pairs / kGroupTok + 1;
+    // 64-token tiles: the four per-group accumulators and A slots fill TMEM.
+    L.tok_cap = kTok;
+    L.max_tiles = (num_experts < pairs ? num_experts : pairs) + pairs / L.tok_cap + 1;
     L.hdr = take(64);
     L.order = take(sizeof(int32_t) * (size_t)(pairs + 1));
     L.pscale = take(sizeof(int32_t) * (size_t)(pairs + 1));
@@ -668,25 +880,44 @@ cudaError_t launch_grouped_run(int member, const void *const *streams, int64_t n
     ga.err = reinterpret_cast<int32_t *>(const_cast<char *>(ga.ws) + L.hdr);
     ga.y = y;
     ga.y_dtype = y_dtype;
-    CUtensorMap qmap, xmap;
-    // codes: [E * out rows, n / 4 bytes], 128 rows x 32 B boxes, 32-byte swizzle
+    ga.tok_cap = L.tok_cap;
+    // Two code slots and up to eight activation slots; give up a code slot
+    // before going below four activation slots.
+    int cslots = kMaxCodeSlots, xslots = 0, fixed = 0;
+    for (; cslots >= 1; --cslots) {
+        fixed = 1024 + (int)gemm_smem(member, n, L.tok_cap, 0, cslots).bars + kBarBytes;
+        xslots = (kSmemCap - fixed) / x_slot_bytes(L.tok_cap);
+        if (xslots >= kMinXSlots) break;
+    }
+    if (xslots > kMaxXSlots) xslots = kMaxXSlots;
+    if (xslots < kMinXSlots) return cudaErrorInvalidConfiguration;
+    ga.xslots = xslots;
+    ga.cslots = cslots;
+    const int smem = fixed + xslots * x_slot_bytes(L.tok_cap);
+    CUtensorMap qmap;
+    XMaps xmap{};
+    // codes: [E * out rows, n / 4 bytes], 128 rows x 128 B boxes (512 weights), 128-byte swizzle
     cudaError_t err = encode_map(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, streams[0], (uint64_t)n / 4,
                                  (uint64_t)(num_experts * out_features), (uint64_t)n / 4,
-                                 kStageK / 4, kGroupRows, CU_TENSOR_MAP_SWIZZLE_32B);
+                                 kCodeK / 4, kGroupRows, CU_TENSOR_MAP_SWIZZLE_128B);
     if (err != cudaSuccess) return err;
-    // activations: [pairs rows, n] f16, 16 rows x 64 elements, 128-byte swizzle
-    err = encode_map(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ga.ws + L.xs, (uint64_t)n,
-                     (uint64_t)pairs, (uint64_t)n * 2, 64, 16, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (err != cudaSuccess) return err;
+    // activations: [pairs rows, n] f16, boxes of 64 elements x (16 .. tok_cap) rows,
+    // 128-byte swizzle
+    for (int i = 0; i < L.tok_cap / 16; ++i) {
+        err = encode_map(&xmap.m[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ga.ws + L.xs, (uint64_t)n,
+                         (uint64_t)pairs, (uint64_t)n * 2, 64, 16 * (i + 1),
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+        if (err != cudaSuccess) return err;
+    }
     const int64_t max_items = L.max_tiles * ga.rblocks;
     int64_t blocks = max_items < num_sms ? max_items : num_sms;
     if (blocks < 1) blocks = 1;
 #define IQK_GG(M)                                                                              \
     do {                                                                                       \
         err = cudaFuncSetAttribute(grouped_gemm_kernel<M>,                                     \
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemG);       \
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, smem);         \
         if (err != cudaSuccess) return err;                                                    \
-        grouped_gemm_kernel<M><<<(unsigned)blocks, kThreadsG, kSmemG, stream>>>(ga, qmap, xmap); \
+        grouped_gemm_kernel<M><<<(unsigned)blocks, kThreadsG, smem, stream>>>(ga, qmap, xmap); \
     } while (0)
     if (member == IQK_IQ2_KS) IQK_GG(IQK_IQ2_KS);
     else if (member == IQK_IQ2_K) IQK_GG(IQK_IQ2_K);

@@ -9,17 +9,18 @@ namespace iqk {
 //   hdr     [16] int32: [0] device error bits, [1] work tiles, [2] routable pairs
 //   order   [pairs] int32: sorted position -> pair (unroutable pairs at the tail)
 //   pscale  [pairs] int32: power-of-two exponent S of each position's activation row
-//   tiles   [max_tiles] int4: {expert, first position, tokens (<= 128), 0}
+//   tiles   [max_tiles] int4: {expert, first position, tokens (<= tok_cap), 0}
 //   xs      [pairs, n] f16: activation rows in sorted order, scaled by 2^S and
 //           permuted inside every 16-element block to the weight operand's order
 struct GroupedLayout {
     size_t hdr, order, pscale, tiles, xs;
     int64_t max_tiles;
+    int tok_cap;  // tokens per work tile: 64 when experts average <= 80 pairs, else 128
     size_t total;
 };
 
-constexpr int kGroupTok = 128;    // tokens per work tile (the MMA's N, padded to 16)
-constexpr int kGroupRows = 128;   // output rows per work item (the MMA's M)
+constexpr int kGroupTokMax = 128;  // largest work tile (the MMA's N, padded to 16)
+constexpr int kGroupRows = 128;    // output rows per work item (the MMA's M)
 
 GroupedLayout grouped_layout(int64_t n, int64_t num_experts, int64_t pairs);
 

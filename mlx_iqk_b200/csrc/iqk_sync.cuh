@@ -43,10 +43,41 @@ __device__ __forceinline__ bool bar_test(uint64_t *b, uint32_t parity) {
         : "=r"(ok) : "r"(saddr(b)), "r"(parity) : "memory");
     return ok != 0;
 }
+// Like bar_test, but the thread may sleep in hardware (up to `hint_ns`) until
+// the phase completes, instead of spinning and taking issue slots from the
+// warps that do the work.
+__device__ __forceinline__ bool bar_test_sleep(uint64_t *b, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok) : "r"(saddr(b)), "r"(parity), "r"(hint_ns) : "memory");
+    return ok != 0;
+}
 // Wait for the phase with the given parity. Gives up (returns false) after
 // kWaitNs, or -- when `abort` is not null -- as soon as *abort is set by
 // another warp that gave up. Drains of copies in flight pass null.
 __device__ __forceinline__ bool bar_wait(uint64_t *b, uint32_t parity, volatile int *abort) {
+    if (bar_test(b, parity)) return true;
+    const unsigned long long t0 = now_ns();
+    while (!bar_test_sleep(b, parity, 20000u)) {
+        if (abort && *abort) return false;
+        if (now_ns() - t0 > kWaitNs) return false;
+    }
+    return true;
+}
+
+// One lane of a converged warp (elect.sync); the others get false.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile("{\n .reg .pred P;\n elect.sync _|P, 0xffffffff;\n selp.b32 %0, 1, 0, P;\n}\n"
+                 : "=r"(pred));
+    return pred != 0;
+}
+
+// bar_wait without the hardware sleep: for warps whose lanes must stay
+// converged (the MMA issuers).
+__device__ __forceinline__ bool bar_wait_spin(uint64_t *b, uint32_t parity, volatile int *abort) {
     if (bar_test(b, parity)) return true;
     const unsigned long long t0 = now_ns();
     while (!bar_test(b, parity)) {
@@ -119,6 +150,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
         "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
         "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
+}
+// 32 lanes x 32-bit, 8 consecutive columns per thread (its own lane).
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(
+                     taddr),
+                 "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+                 "r"(r[7])
+                 : "memory");
 }
 // 32 lanes x 32-bit, 8 consecutive columns per thread.
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
