@@ -248,8 +248,10 @@ def config(args, batches) -> dict:
             "parallelism": f"replicas x{args.gpus}"}
 
 
-def random_streams(torch, out: int, n: int, gen, dev, member: str = "iq2_ks"):
+def random_streams(torch, out: int, n: int, gen, dev, member: str = "iq2_ks",
+                   experts: int | None = None):
     """Uniform random relayout streams on the device, serving scales."""
+    E = experts or globals()["E"]
     def u8(count):
         return torch.randint(0, 256, (count,), generator=gen, device=dev, dtype=torch.uint8)
 
@@ -277,6 +279,34 @@ PREFILL_TOKENS = 2048
 
 def prefill_flops(pairs: int) -> float:
     return 2.0 * pairs * (2 * GATE_UP[0] * GATE_UP[1] + DOWN[0] * DOWN[1])
+
+
+def measure_ep_prefill(torch, dist, K, dev, world, rank, barrier, max_over_ranks, steps):
+    """Config 5 through ExpertParallelMoE: ms per layer step, max over ranks."""
+    from mlx_iqk_b200.ep import ExpertParallelMoE
+    gen = torch.Generator(device=dev).manual_seed(2000 + rank)
+    layer = ExpertParallelMoE(E, GATE_UP[1], GATE_UP[0], members=("iq2_ks", "iq2_ks", "iq2_k"),
+                              device=dev)
+    for mod in (layer.gate, layer.up, layer.down):
+        mod.load_streams(random_streams(torch, mod.out_features, mod.in_features, gen, dev,
+                                        mod.member, experts=layer.local_experts))
+    T = PREFILL_TOKENS // world
+    x = torch.randn((T, GATE_UP[1]), generator=gen, device=dev).to(torch.bfloat16)
+    logits = torch.randn((T, E), generator=gen, device=dev)
+    top = torch.topk(logits, TOP_K, dim=-1)
+    w = torch.softmax(top.values, dim=-1)
+    for _ in range(3):
+        layer(x, top.indices, w)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for _ in range(steps):
+        layer(x, top.indices, w)
+    e1.record(stream)
+    e1.synchronize()
+    barrier()
+    return max_over_ranks(e0.elapsed_time(e1) / steps)
 
 
 class PrefillLayer:
@@ -514,9 +544,20 @@ def run_b200(args) -> None:
                 "us_per_launch": round(kms * 1e3, 3), "bytes_per_launch": int(gate_bytes),
                 "traffic": args.traffic}
 
-    # ---- prefill (config 5) on this GPU: the grouped GEMM layer
+    # ---- prefill (config 5): the expert-parallel layer over all ranks
+    # (experts sharded E/N per rank, the 2048 tokens sharded N ways: strong
+    # scaling), then at N=1 the grouped GEMMs timed alone.
     prefill = None
     if not args.no_prefill:
+        ep_ms = measure_ep_prefill(torch, dist, K, dev, world, rank, barrier, max_over_ranks,
+                                   steps=max(5, args.prefill_steps // 2))
+    if not args.no_prefill and world > 1:
+        prefill = {"metric": "prefill tokens/s (config 5 layer, expert-parallel)",
+                   "value": round(PREFILL_TOKENS / (ep_ms * 1e-3), 1), "unit": "tokens/s",
+                   "ms_per_step": round(ep_ms, 4), "tokens": PREFILL_TOKENS,
+                   "scaling": "strong", "parallelism": f"ep{world}: {E // world} experts/rank, "
+                   "NCCL all_to_all dispatch/combine"}
+    if not args.no_prefill and world == 1:
         pl = PrefillLayer(torch, K, dev, gen)
         pl.step()
         torch.cuda.synchronize()
@@ -547,6 +588,9 @@ def run_b200(args) -> None:
                       "256 experts top-6, sorted_indices=True)",
             "value": round(world * pl.T / (pms * 1e-3), 1), "unit": "tokens/s",
             "tokens_per_gpu": pl.T, "ms_per_step": round(pms, 4),
+            "ep_layer": {"value": round(PREFILL_TOKENS / (ep_ms * 1e-3), 1), "unit": "tokens/s",
+                         "ms_per_step": round(ep_ms, 4),
+                         "path": "ExpertParallelMoE.forward (dispatch, SwitchGLU, combine)"},
             "layer_tflops": round(layer_fl / (pms * 1e-3) / 1e12, 1),
             "load": pl.load,
             "gemm": {
