@@ -82,6 +82,105 @@ struct StreamPtrs {
     const void *p[5];
 };
 
+#ifndef IQK_DQ_ST
+#define IQK_DQ_ST(p, v) __stcs(p, v)  // streaming stores: the output is not re-read here
+#endif
+
+__device__ __forceinline__ uint32_t prmt_dq(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+template <typename OUT> __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    const OUT a = from_float<OUT>(lo), b = from_float<OUT>(hi);
+    return (uint32_t)*reinterpret_cast<const uint16_t *>(&a) |
+           ((uint32_t)*reinterpret_cast<const uint16_t *>(&b) << 16);
+}
+
+// 2-bit members, one 16-weight code word per thread. A group's four
+// float32 products dl * value are computed once with the CPU's
+// chain; every weight is then one of them, so the result is the same bit for
+// bit. 16-bit outputs place them with byte permutes (selector bytes 2c, 2c+1
+// pick entry c of the {T0,T1,T2,T3} table; pairs come out as (k, k+4) and
+// one more permute restores k order).
+template <typename OUT>
+__device__ __forceinline__ void store_word(OUT *out, uint32_t word, const float t[4]) {
+    if constexpr (sizeof(OUT) == 4) {
+        float w[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const uint32_t c = (word >> (2 * k)) & 3u;
+            const float lo2 = (c & 1u) ? t[1] : t[0], hi2 = (c & 1u) ? t[3] : t[2];
+            w[k] = (c & 2u) ? hi2 : lo2;
+        }
+        float4 *o4 = reinterpret_cast<float4 *>(out);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            IQK_DQ_ST(o4 + q, make_float4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]));
+    } else {
+        const uint32_t t01 = pack2<OUT>(t[0], t[1]), t23 = pack2<OUT>(t[2], t[3]);
+        uint32_t r[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t m = (word >> (2 * j)) & 0x03030303u;  // codes j, 4+j, 8+j, 12+j
+            const uint32_t sel = m * 0x22u + 0x10101010u;
+            r[j] = prmt_dq(t01, t23, sel);
+            r[4 + j] = prmt_dq(t01, t23, sel >> 16);
+        }
+        uint4 *o4 = reinterpret_cast<uint4 *>(out);
+        IQK_DQ_ST(o4, make_uint4(prmt_dq(r[0], r[1], 0x5410u), prmt_dq(r[2], r[3], 0x5410u),
+                              prmt_dq(r[0], r[1], 0x7632u), prmt_dq(r[2], r[3], 0x7632u)));
+        IQK_DQ_ST(o4 + 1, make_uint4(prmt_dq(r[4], r[5], 0x5410u), prmt_dq(r[6], r[7], 0x5410u),
+                                  prmt_dq(r[4], r[5], 0x7632u), prmt_dq(r[6], r[7], 0x7632u)));
+    }
+}
+
+__device__ __forceinline__ void group_table(float dl, int alpha, float t[4]) {
+    const uint32_t tab = alpha ? kIq2Tab1 : kIq2Tab0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) t[c] = dl * (float)(int)(int8_t)(tab >> (8 * c));
+}
+
+template <int MEMBER, typename OUT>
+__global__ void __launch_bounds__(256)
+dequant_words_kernel(StreamPtrs sp, uint32_t total_words, int log2_words, int n,
+                     int64_t out_features, int64_t row_start, uint32_t rows,
+                     OUT *__restrict__ dst) {
+    const uint32_t stride = gridDim.x * blockDim.x;
+    const uint32_t *qs = static_cast<const uint32_t *>(sp.p[0]);
+    for (uint32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < total_words; u += stride) {
+        const uint32_t lin = u >> log2_words;  // [expert, local row]
+        const int wi = (int)(u & ((1u << log2_words) - 1u));
+        const uint32_t e = lin / rows;
+        const int64_t srow = (int64_t)e * out_features + row_start + (lin - e * rows);
+        const uint32_t word = __ldg(qs + srow * (n / 16) + wi);
+        float t[4];
+        if (MEMBER == IQK_IQ2_KS) {
+            const uint8_t *scl = static_cast<const uint8_t *>(sp.p[1]);
+            const uint8_t *sch = static_cast<const uint8_t *>(sp.p[2]);
+            const uint8_t *sex = static_cast<const uint8_t *>(sp.p[3]);
+            const uint16_t *dv = static_cast<const uint16_t *>(sp.p[4]);
+            const int g = wi >> 1;
+            const int lo = (__ldg(scl + srow * (n / 64) + (g >> 1)) >> (4 * (g & 1))) & 15;
+            const int hi = (__ldg(sch + srow * (n / 256) + (g >> 3)) >> (g & 7)) & 1;
+            const int alpha = (__ldg(sex + srow * (n / 256) + (g >> 3)) >> (g & 7)) & 1;
+            group_table(half_bits_to_float(__ldg(dv + srow)) * (float)((lo | (hi << 4)) - 16),
+                        alpha, t);
+        } else {
+            const uint8_t *scl = static_cast<const uint8_t *>(sp.p[1]);
+            const uint8_t *sex = static_cast<const uint8_t *>(sp.p[2]);
+            const uint16_t *dv = static_cast<const uint16_t *>(sp.p[3]);
+            const int sb = wi;
+            const int lo = (__ldg(scl + srow * (n / 32) + (sb >> 1)) >> (4 * (sb & 1))) & 15;
+            const int alpha = (__ldg(sex + srow * (n / 128) + (sb >> 3)) >> (sb & 7)) & 1;
+            group_table(half_bits_to_float(__ldg(dv + srow * (n / 256) + (sb >> 4))) *
+                            (float)(lo - 8), alpha, t);
+        }
+        store_word<OUT>(dst + (int64_t)lin * n + wi * 16, word, t);
+    }
+}
+
 template <int MEMBER, typename OUT>
 __global__ void __launch_bounds__(256)
 dequant_rows_kernel(StreamPtrs sp, uint32_t total_octets, int log2_octs,
@@ -125,9 +224,10 @@ cudaError_t launch_dequant(int member, const void *const *streams, int64_t num_e
     const RowBytes rb = row_bytes(member, n);
     for (int i = 0; i < rb.count; ++i) sp.p[i] = streams[i];
     const int log2_octs = n == 4096 ? 9 : 8;  // n / 8 octets per row
+    const bool words = member != IQK_IQ1_S_R4;  // 2-bit members: one code word per thread
     const int elem = out_dtype == IQK_F32 ? 4 : 2;
     // 32-bit octet indices: split the expert range so each launch stays below 2^31.
-    const int64_t per_expert = rows * (n / 8);
+    const int64_t per_expert = rows * (words ? n / 16 : n / 8);
     if (per_expert == 0 || num_experts == 0) return cudaSuccess;
     const int64_t chunk = ((int64_t)1 << 31) / per_expert;
     for (int64_t e0 = 0; e0 < num_experts; e0 += chunk) {
@@ -142,9 +242,14 @@ cudaError_t launch_dequant(int member, const void *const *streams, int64_t num_e
         const int64_t cap = (int64_t)num_sms * 8;  // resident blocks; grid-stride beyond
         if (blocks > cap) blocks = cap;
 #define IQK_DQ(M, T)                                                                  \
-        dequant_rows_kernel<M, T><<<(unsigned)blocks, threads, 0, stream>>>(           \
-            spc, total, log2_octs, n, out_features, row_start, (uint32_t)rows,         \
-            static_cast<T *>(dstc))
+        if (M != IQK_IQ1_S_R4)                                                        \
+            dequant_words_kernel<M, T><<<(unsigned)blocks, threads, 0, stream>>>(      \
+                spc, total, log2_octs - 1, n, out_features, row_start, (uint32_t)rows, \
+                static_cast<T *>(dstc));                                              \
+        else                                                                          \
+            dequant_rows_kernel<M, T><<<(unsigned)blocks, threads, 0, stream>>>(       \
+                spc, total, log2_octs, n, out_features, row_start, (uint32_t)rows,     \
+                static_cast<T *>(dstc))
 #define IQK_DQ_MEMBER(M)                                             \
     do {                                                             \
         if (out_dtype == IQK_F32) IQK_DQ(M, float);                  \

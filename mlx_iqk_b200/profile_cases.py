@@ -1,0 +1,124 @@
+"""Run one kernel case repeatedly on ``cuda:0``, for timing and for profilers.
+
+    python -m mlx_iqk_b200.profile_cases gemv    --member iq2_ks --batch 8   [--reps 20]
+    python -m mlx_iqk_b200.profile_cases grouped --member iq2_ks --tokens 2048
+    python -m mlx_iqk_b200.profile_cases dequant --member iq2_ks [--experts 64]
+
+Each case builds random relayout streams for 256 experts (the benchmark
+geometry: [2048, 4096] for gate-shaped, [4096, 2048] for down-shaped
+projections), runs two untimed calls, then ``--reps`` timed calls, and prints
+one line with the mean time per call (CUDA events) and the case's
+algorithmic bytes or flops. Inputs are larger than L2 unless a case says
+otherwise. Nothing here is on the product path.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import kernels as K
+from .format import component_shapes
+from .nn import IqkSwitchLinear
+
+E_DEFAULT = 256
+ROW_BYTES = {"iq2_ks": lambda n: 2 + 70 * (n // 256), "iq2_k": lambda n: 76 * (n // 256),
+             "iq1_s_r4": lambda n: 2 + 6 * (n // 32)}
+
+
+def random_module(member: str, experts: int, out: int, n: int, dev, gen) -> IqkSwitchLinear:
+    mod = IqkSwitchLinear(member, experts, out, n, device=dev)
+    streams = {}
+    for name, shape in component_shapes(member, experts, out, n).items():
+        if name == "dv":
+            mag = torch.rand(shape, generator=gen, device=dev) * 8e-4 + 2e-5
+            sign = torch.where(torch.rand(shape, generator=gen, device=dev) < 0.5, -1.0, 1.0)
+            streams[name] = (mag * sign).to(torch.float16)
+            continue
+        dt = getattr(mod, name).dtype
+        count = 1
+        for s in shape:
+            count *= s
+        raw = torch.randint(0, 256, (count * dt.itemsize,), generator=gen, device=dev,
+                            dtype=torch.uint8)
+        streams[name] = raw.view(dt).reshape(shape)
+    mod.load_streams(streams)
+    return mod
+
+
+def timed(fn, reps: int) -> float:
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    e1.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=("gemv", "grouped", "dequant"))
+    ap.add_argument("--member", default="iq2_ks")
+    ap.add_argument("--batch", type=int, default=8, help="gemv: tokens (top-6 each)")
+    ap.add_argument("--tokens", type=int, default=2048, help="grouped: tokens (top-6 each)")
+    ap.add_argument("--experts", type=int, default=E_DEFAULT)
+    ap.add_argument("--width", type=int, default=4096, help="in_features (2048 or 4096)")
+    ap.add_argument("--reps", type=int, default=20)
+    args = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(11)
+    n = args.width
+    out = 2048 if n == 4096 else 4096
+    E = args.experts
+    mod = random_module(args.member, E, out, n, dev, gen)
+    rb = ROW_BYTES[args.member](n)
+    line = {"case": args.case, "member": args.member, "experts": E, "out": out, "in": n}
+    if args.case == "gemv":
+        B = args.batch
+        x = torch.randn((B, n), generator=gen, device=dev).to(torch.bfloat16)
+        sel = torch.stack([torch.randperm(E, generator=gen, device=dev)[:6] for _ in range(B)])
+        sel = sel.reshape(-1).to(torch.int32)
+        y = torch.empty((B * 6, out), device=dev)
+        ws = torch.empty(K.gemv_workspace_bytes(args.member, n, B, B * 6), dtype=torch.uint8,
+                         device=dev)
+        K.gemv_prepare(x, E, n, sel, None, ws)
+        ms = timed(lambda: K.gemv_run(args.member, mod._streams(), E, out, n, B, B * 6, y, ws),
+                   args.reps)
+        distinct = len(set(sel.tolist()))
+        nbytes = distinct * out * rb + B * n * 2 + B * 6 * out * 4
+        line.update(batch=B, distinct_experts=distinct, us=round(ms * 1e3, 2),
+                    bytes=nbytes, GBps=round(nbytes / (ms * 1e-3) / 1e9, 1),
+                    note="run kernel only (prepared once); weights are L2-hot across reps "
+                         "when distinct experts x rows x row bytes < 126 MB")
+    elif args.case == "grouped":
+        T = args.tokens
+        x = torch.randn((T, n), generator=gen, device=dev).to(torch.bfloat16)
+        logits = torch.randn((T, E), generator=gen, device=dev)
+        sel = torch.topk(logits, 6, dim=-1).indices.to(torch.int32).reshape(-1).contiguous()
+        P = sel.numel()
+        y = torch.empty((P, out), device=dev)
+        ws = torch.empty(K.grouped_workspace_bytes(n, E, P), dtype=torch.uint8, device=dev)
+        K.grouped_prepare(x, E, n, sel, None, ws)
+        ms = timed(lambda: K.grouped_run(args.member, mod._streams(), E, out, n, P, y, ws),
+                   args.reps)
+        flops = 2.0 * P * out * n
+        line.update(tokens=T, pairs=P, us=round(ms * 1e3, 2),
+                    tflops=round(flops / (ms * 1e-3) / 1e12, 1))
+    else:
+        y = torch.empty((E, out, n), dtype=torch.float16, device=dev)
+        ms = timed(lambda: K.dequant(args.member, mod._streams(), E, out, n, 0, out, y),
+                   args.reps)
+        nbytes = E * out * rb + E * out * n * 2
+        line.update(us=round(ms * 1e3, 2), bytes=nbytes,
+                    GBps=round(nbytes / (ms * 1e-3) / 1e9, 1))
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()
