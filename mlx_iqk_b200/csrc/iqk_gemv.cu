@@ -284,11 +284,9 @@ gemv_prep_kernel(const XT *__restrict__ x, int n, int x_rows, const int32_t *__r
 
 // -------------------------------------------------------------- run kernel
 
-constexpr int kConsumers = 8;                 // compute warps
+constexpr int kConsumers = 4;                 // compute warps: 16 rows x all of k each
 constexpr int kThreads = (kConsumers + 1) * 32;  // + one producer warp
-constexpr int kKSplit = 4;                    // compute warps sharing one row tile along k
-constexpr int kRowTiles = kConsumers / kKSplit;  // 16-row tiles per CTA item
-constexpr int kItemRows = 16 * kRowTiles;     // 32
+constexpr int kItemRows = 16 * kConsumers;    // 64 rows per CTA item
 constexpr int kChunkK = 512;                  // weights per row per round and warp
 constexpr int kPairsPerRound = kChunkK / 64;  // MMA pairs (64 weights per row) per round
 constexpr int kMaxTiles = 128;                // tile entries cached in shared memory
@@ -298,16 +296,16 @@ constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // bounded mbarrier 
 // weights form an "MMA pair": two m16n8k32 products whose A fragments come
 // from one 32-bit code word per lane and row.
 template <int MEMBER> struct Geo {
-    // IQ2_KS and IQ1_S_R4 run two CTAs per SM (3-stage rings); IQ2_K, whose
-    // scale streams and metadata are twice as large, one CTA with 5 stages.
-    static constexpr int kStages = MEMBER == IQK_IQ2_K ? 5 : 3;
-    static constexpr int kMinBlocks = MEMBER == IQK_IQ2_K ? 1 : 2;
+    // Four-stage rings; three CTAs per SM (two for IQ2_K, whose scale
+    // streams and metadata are twice as large).
+    static constexpr int kStages = 4;
+    static constexpr int kMinBlocks = MEMBER == IQK_IQ2_K ? 2 : 3;
     static constexpr int kRowChunk = MEMBER == IQK_IQ1_S_R4 ? 64 : 128;   // qs bytes per round
     static constexpr int kWBox = 16 * kRowChunk;                         // one warp's TMA box
     static constexpr int kWBytes = kConsumers * kWBox;
     static constexpr int kXPlanes = kPairsPerRound * 192;                  // 3 planes
     static constexpr int kXSums = MEMBER == IQK_IQ1_S_R4 ? kPairsPerRound * 32 : 0;
-    static constexpr int kXBlock = kXPlanes + kXSums;                      // per k-quarter
+    static constexpr int kXBlock = kXPlanes + kXSums;                      // per round
     static constexpr int kMetaSides = MEMBER == IQK_IQ2_K ? 4 : 2;
     static constexpr int kMetaBytes = kPairsPerRound * kMetaSides * 8 * 16;  // per warp
 };
@@ -319,21 +317,24 @@ template <int MEMBER> __host__ __device__ constexpr int slot_bytes(int n) {
                                  : kItemRows * (n / 16) + 2 * kItemRows;
 }
 
-// Stage: [weights: kConsumers TMA boxes][activation slices][item scale streams]
-// (the scale streams only in an item's first stage; the item's stages are
-// released together when the item ends).
+// Stage: [weights: kConsumers TMA boxes][activation slice], released every
+// round. An item's scale streams sit in one of two scale slots for the whole
+// item.
 template <int MEMBER> __host__ __device__ constexpr int stage_bytes(int n) {
-    return (Geo<MEMBER>::kWBytes + kKSplit * Geo<MEMBER>::kXBlock + slot_bytes<MEMBER>(n) + 1023) /
-           1024 * 1024;
+    return (Geo<MEMBER>::kWBytes + Geo<MEMBER>::kXBlock + 1023) / 1024 * 1024;
+}
+template <int MEMBER> __host__ __device__ constexpr int sslot_bytes(int n) {
+    return (slot_bytes<MEMBER>(n) + 127) / 128 * 128;
 }
 
 template <int MEMBER> __host__ __device__ constexpr int gemv_smem_bytes(int n) {
     using G = Geo<MEMBER>;
     constexpr int kStages = G::kStages;
     return 1024 /* alignment slack */ + kStages * stage_bytes<MEMBER>(n) +
-           kConsumers * G::kMetaBytes + kConsumers * 32 * 4 * 4 + kConsumers * 32 * 2 * 8 +
+           2 * sslot_bytes<MEMBER>(n) + kConsumers * G::kMetaBytes +
            kMaxTiles * (int)sizeof(TileRef) + (MEMBER == IQK_IQ1_S_R4 ? 4096 : 0) +
-           (MEMBER == IQK_IQ2_K ? 256 : 0) + 2 * kStages * 8 + 16 + kPairsPerRound * 192;
+           (MEMBER == IQK_IQ2_K ? 256 : 0) + 2 * kStages * 8 + 4 * 8 + 16 +
+           kPairsPerRound * 192;
 }
 
 struct GemvArgs {
@@ -446,22 +447,23 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     const int n = a.n;
     const int64_t out = a.out_features;
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const int cpw = n / (kChunkK * kKSplit);  // rounds per item: 2 (n=4096) or 1 (2048)
-    const int SB = slot_bytes<MEMBER>(n);
+    const int cpw = n / kChunkK;  // rounds per item: 8 (n=4096) or 4 (2048)
+    const int SSB = sslot_bytes<MEMBER>(n);
     const int STB = stage_bytes<MEMBER>(n);
 
     char *stages = smem;
-    char *metas = stages + kStages * STB;
-    int32_t *red_i = reinterpret_cast<int32_t *>(metas + kConsumers * G::kMetaBytes);
-    double *red_d = reinterpret_cast<double *>(red_i + kConsumers * 32 * 4);
-    TileRef *tcache = reinterpret_cast<TileRef *>(red_d + kConsumers * 32 * 2);
+    char *sslots = stages + kStages * STB;  // two item scale slots
+    char *metas = sslots + 2 * SSB;
+    TileRef *tcache = reinterpret_cast<TileRef *>(metas + kConsumers * G::kMetaBytes);
     char *tail = reinterpret_cast<char *>(tcache + kMaxTiles);
     uint16_t *grid = reinterpret_cast<uint16_t *>(tail);   // IQ1_S_R4
     uint2 *ktab = reinterpret_cast<uint2 *>(tail);         // IQ2_K: (alpha, idx) -> tables
     uint64_t *full = reinterpret_cast<uint64_t *>(
         tail + (MEMBER == IQK_IQ1_S_R4 ? 4096 : MEMBER == IQK_IQ2_K ? 256 : 0));
     uint64_t *empty = full + kStages;
-    int *abort_flag = reinterpret_cast<int *>(empty + kStages);
+    uint64_t *sfull = empty + kStages;  // [2] item scale slots
+    uint64_t *sempty = sfull + 2;       // [2]
+    int *abort_flag = reinterpret_cast<int *>(sempty + 2);
     char *zeros = reinterpret_cast<char *>(abort_flag) + 16;  // kPairsPerRound * 192 zero bytes
 
     const int32_t *hdr = reinterpret_cast<const int32_t *>(a.ws + a.L.hdr);
@@ -521,6 +523,10 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumers);
         }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&sfull[s], 1);
+            mbar_init(&sempty[s], kConsumers);
+        }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
@@ -532,48 +538,54 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     if (wid == kConsumers) {
         // ================= producer warp: TMA / bulk copies into the ring
         int o = 0, r = 0, ti = i0 / rblocks, rb = i0 % rblocks;
-        int issued = 0;
-        for (int j = 0; j < total_rounds; ++j) {
+        int issued = 0, sissued = 0;
+        bool ok = true;
+        for (int j = 0; j < total_rounds && ok; ++j) {
             const int slot = j % kStages;
-            if (j >= kStages && !mbar_wait(&empty[slot], ((j / kStages) & 1) ^ 1)) {
-                if (lane == 0) {
-                    atomicOr(a.err, IQK_DEVERR_TIMEOUT);
-                    atomicExch(abort_flag, 1);
-                }
-                break;
-            }
             const TileRef T = tile_of(ti);
             const int64_t r0 = (int64_t)rb * kItemRows;
             const int rows_valid = (int)min((int64_t)kItemRows, out - r0);
+            if (r == 0) {
+                // the item's scale streams (all rows, all of k) into scale slot o % 2
+                const int ss = o & 1;
+                if (o >= 2 && !mbar_wait(&sempty[ss], ((o >> 1) & 1) ^ 1)) {
+                    ok = false;
+                    break;
+                }
+                uint32_t sbytes = 0;
+                for (int si = 1; si < rbs.count; ++si) sbytes += (uint32_t)(rows_valid * rbs.b[si]);
+                if (lane == 0) mbar_arrive_expect_tx(&sfull[ss], sbytes);
+                __syncwarp();
+                if (lane >= 1 && lane < rbs.count) {
+                    const int si = lane;
+                    int off = 0;
+                    for (int q = 1; q < si; ++q) off += (int)(kItemRows * rbs.b[q]);
+                    bulk_load(sslots + ss * SSB + off,
+                              static_cast<const char *>(a.s[si]) + ((int64_t)T.e * out + r0) * rbs.b[si],
+                              (uint32_t)(rows_valid * rbs.b[si]), &sfull[ss]);
+                }
+                sissued = o + 1;
+            }
+            if (j >= kStages && !mbar_wait(&empty[slot], ((j / kStages) & 1) ^ 1)) {
+                ok = false;
+                break;
+            }
             char *st = stages + slot * STB;
-            uint32_t bytes = (uint32_t)(G::kWBytes + kKSplit * G::kXBlock);
-            if (r == 0)
-                for (int si = 1; si < rbs.count; ++si) bytes += (uint32_t)(rows_valid * rbs.b[si]);
+            const uint32_t bytes = (uint32_t)(G::kWBytes + G::kXBlock);
             if (lane == 0) mbar_arrive_expect_tx(&full[slot], bytes);
             __syncwarp();
             if (lane < kConsumers) {
                 // weights: one 16-row x kRowChunk-byte box per compute warp
-                const int w = lane, rtw = w / kKSplit, ksw = w % kKSplit;
-                tma_load_2d(st + w * G::kWBox, &qs_map, (ksw * cpw + r) * G::kRowChunk,
-                            (int)((int64_t)T.e * out + r0 + 16 * rtw), &full[slot]);
-            } else if (lane < kConsumers + kKSplit) {
-                // activation digit planes (+ IQ1 block sums) of each k-quarter
-                const int ksx = lane - kConsumers;
-                const int c = ksx * cpw + r;
-                char *xs = st + G::kWBytes + ksx * G::kXBlock;
+                tma_load_2d(st + lane * G::kWBox, &qs_map, r * G::kRowChunk,
+                            (int)((int64_t)T.e * out + r0 + 16 * lane), &full[slot]);
+            } else if (lane == kConsumers) {
+                // activation digit planes (+ IQ1 block sums) of this round's k range
+                char *xs = st + G::kWBytes;
                 const char *xb = xbuf + T.tok0 * xrow;
-                bulk_load(xs, xb + (int64_t)c * G::kXPlanes, G::kXPlanes, &full[slot]);
+                bulk_load(xs, xb + (int64_t)r * G::kXPlanes, G::kXPlanes, &full[slot]);
                 if (G::kXSums)
-                    bulk_load(xs + G::kXPlanes, xb + 3 * (int64_t)n + (int64_t)c * G::kXSums,
+                    bulk_load(xs + G::kXPlanes, xb + 3 * (int64_t)n + (int64_t)r * G::kXSums,
                               G::kXSums, &full[slot]);
-            } else if (r == 0 && lane < kConsumers + kKSplit + rbs.count - 1) {
-                // the item's scale streams (all rows, all k)
-                const int si = lane - kConsumers - kKSplit + 1;
-                int off = 0;
-                for (int q = 1; q < si; ++q) off += (int)(kItemRows * rbs.b[q]);
-                bulk_load(st + G::kWBytes + kKSplit * G::kXBlock + off,
-                          static_cast<const char *>(a.s[si]) + ((int64_t)T.e * out + r0) * rbs.b[si],
-                          (uint32_t)(rows_valid * rbs.b[si]), &full[slot]);
             }
             issued = j + 1;
             if (++r == cpw) {
@@ -585,17 +597,23 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                 }
             }
         }
+        if (!ok && lane == 0) {
+            atomicOr(a.err, IQK_DEVERR_TIMEOUT);
+            atomicExch(abort_flag, 1);
+        }
         // Drain: never leave the CTA with bulk copies still in flight. In
         // normal operation the consumers already waited on every stage; after
         // an abort this waits (bounded) for the copies issued last.
         for (int j = issued - 1; j >= 0 && j >= issued - kStages; --j)
             mbar_wait(&full[j % kStages], (j / kStages) & 1);
+        for (int q = sissued - 1; q >= 0 && q >= sissued - 2; --q)
+            mbar_wait(&sfull[q & 1], (q >> 1) & 1);
         return;
     }
 
     // ===================== compute warps
     const int g = lane >> 2, tig = lane & 3;
-    const int rt = wid / kKSplit, ks = wid % kKSplit;
+    const int rt = wid;  // this warp's 16-row tile of the item
     char *meta = metas + wid * G::kMetaBytes;
     const uint32_t meta_u = smem_u32(meta);
     const int side = tig >> 1;             // which 32-weight group of an MMA pair
@@ -630,12 +648,19 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
         if (r == 0) {
             tot[0] = tot[1] = tot[2] = tot[3] = 0;
             dacc[0] = dacc[1] = 0.0;
+            // the item's scale streams
+            if (!mbar_wait(&sfull[o & 1], (o >> 1) & 1)) {
+                if (lane == 0) {
+                    atomicOr(a.err, IQK_DEVERR_TIMEOUT);
+                    atomicExch(abort_flag, 1);
+                }
+                break;
+            }
         }
         const bool live = 16 * rt < out - r0;  // this warp's row tile exists
         const char *st = stages + slot * STB;
-        // the item's scale streams arrived with its first round
-        const char *sd = stages + ((j - r) % kStages) * STB + G::kWBytes + kKSplit * G::kXBlock;
-        const int c = ks * cpw + r;  // 512-weight chunk of this warp
+        const char *sd = sslots + (o & 1) * SSB;
+        const int c = r;  // 512-weight chunk of this round
         if (live) {
             // ---- group metadata for this warp's 16 rows x 512 weights.
             // Lane (mg, mq) owns row pair (mg, mg + 8) and 128 weights.
@@ -697,7 +722,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
             // ---- 8 MMA pairs, all shared-memory addresses 32-bit and the
             // per-pair offsets compile-time immediates.
             const uint32_t wb_u = smem_u32(st + wid * G::kWBox);
-            const uint32_t xs_u = smem_u32(st + G::kWBytes + ks * G::kXBlock);
+            const uint32_t xs_u = smem_u32(st + G::kWBytes);
             // B: live lanes read their plane's 16 bytes; the others a zero block
             const uint32_t xl_u = bplane >= 0 ? xs_u + tig * 48 + bplane * 16 : zero_u;
             const uint32_t mrow = meta_u + moff;
@@ -817,76 +842,58 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
         }
 
         if (r == cpw - 1 && live) {
-            // ---- item end: k-quarter partials -> shared, fixed-order sum, epilogue.
-            // Named barrier 1 + rt spans the 4 warps of this row tile.
-            *reinterpret_cast<int4 *>(red_i + (wid * 32 + lane) * 4) = make_int4(tot[0], tot[1], tot[2], tot[3]);
+            // ---- item end: this warp holds the whole k range of its 16 rows.
+            const int ra = 16 * rt + g;  // item-local row
+            double yg, yg8;
             if (MEMBER == IQK_IQ2_K) {
-                red_d[(wid * 32 + lane) * 2] = dacc[0];
-                red_d[(wid * 32 + lane) * 2 + 1] = dacc[1];
+                yg = dacc[0];
+                yg8 = dacc[1];
+            } else {
+                int32_t s4[4] = {tot[0], tot[1], tot[2], tot[3]};
+                // lanes tig 0/2 hold planes (0,1) of the two sides, 1/3 plane 2
+#pragma unroll
+                for (int k = 0; k < 4; ++k) s4[k] += __shfl_down_sync(0xffffffffu, s4[k], 2);
+                const int32_t n0 = __shfl_down_sync(0xffffffffu, s4[0], 1);
+                const int32_t n2 = __shfl_down_sync(0xffffffffu, s4[2], 1);
+                const double Tg = (double)s4[0] * 65536.0 + (double)s4[1] * 256.0 + (double)n0;
+                const double Tg8 = (double)s4[2] * 65536.0 + (double)s4[3] * 256.0 + (double)n2;
+                const uint16_t *dvp = reinterpret_cast<const uint16_t *>(
+                    sd + (MEMBER == IQK_IQ2_KS ? kItemRows * (n / 64 + n / 256 + n / 256)
+                                               : kItemRows * (n / 16)));
+                yg = (double)half_bits_to_float(dvp[ra]) * Tg;
+                yg8 = (double)half_bits_to_float(dvp[ra + 8]) * Tg8;
             }
-            asm volatile("bar.sync %0, %1;\n" ::"r"(1 + rt), "r"(32 * kKSplit) : "memory");
-            if (ks == 0) {
-                const int ra = 16 * rt + g;  // item-local row
-                double yg = 0.0, yg8 = 0.0;
-                if (MEMBER == IQK_IQ2_K) {
-                    for (int k = 0; k < kKSplit; ++k) {
-                        yg += red_d[((rt * kKSplit + k) * 32 + lane) * 2];
-                        yg8 += red_d[((rt * kKSplit + k) * 32 + lane) * 2 + 1];
-                    }
+            if (tig == 0) {
+                const int S = T.sh0;
+                const int shift = -S - (MEMBER == IQK_IQ1_S_R4 ? 3 : 0);
+                float vg, vg8;
+                if (S == kScaleNonFinite) {
+                    vg = vg8 = __int_as_float(0x7fc00000);
                 } else {
-                    int32_t s4[4] = {0, 0, 0, 0};
-                    for (int k = 0; k < kKSplit; ++k) {
-                        const int4 pv = *reinterpret_cast<const int4 *>(red_i + ((rt * kKSplit + k) * 32 + lane) * 4);
-                        s4[0] += pv.x;
-                        s4[1] += pv.y;
-                        s4[2] += pv.z;
-                        s4[3] += pv.w;
-                    }
-                    // lanes tig 0/2 hold planes (0,1) of the two sides, 1/3 plane 2
-                    for (int k = 0; k < 4; ++k) s4[k] += __shfl_down_sync(0xffffffffu, s4[k], 2);
-                    const int32_t n0 = __shfl_down_sync(0xffffffffu, s4[0], 1);
-                    const int32_t n2 = __shfl_down_sync(0xffffffffu, s4[2], 1);
-                    const double Tg = (double)s4[0] * 65536.0 + (double)s4[1] * 256.0 + (double)n0;
-                    const double Tg8 = (double)s4[2] * 65536.0 + (double)s4[3] * 256.0 + (double)n2;
-                    const uint16_t *dvp = reinterpret_cast<const uint16_t *>(
-                        sd + (MEMBER == IQK_IQ2_KS ? kItemRows * (n / 64 + n / 256 + n / 256)
-                                                   : kItemRows * (n / 16)));
-                    yg = (double)half_bits_to_float(dvp[ra]) * Tg;
-                    yg8 = (double)half_bits_to_float(dvp[ra + 8]) * Tg8;
+                    vg = (float)ldexp(yg, shift);
+                    vg8 = (float)ldexp(yg8, shift);
                 }
-                if (tig == 0) {
-                    const int S = T.sh0;
-                    const int shift = -S - (MEMBER == IQK_IQ1_S_R4 ? 3 : 0);
-                    float vg, vg8;
-                    if (S == kScaleNonFinite) {
-                        vg = vg8 = __int_as_float(0x7fc00000);
-                    } else {
-                        vg = (float)ldexp(yg, shift);
-                        vg8 = (float)ldexp(yg8, shift);
-                    }
-                    const int64_t o0 = (int64_t)T.pair0 * out + r0 + ra;
-                    if (a.y_dtype == IQK_F32) {
-                        float *y = static_cast<float *>(a.y);
-                        y[o0] = vg;
-                        y[o0 + 8] = vg8;
-                    } else if (a.y_dtype == IQK_F16) {
-                        __half *y = static_cast<__half *>(a.y);
-                        y[o0] = __float2half_rn(vg);
-                        y[o0 + 8] = __float2half_rn(vg8);
-                    } else {
-                        __nv_bfloat16 *y = static_cast<__nv_bfloat16 *>(a.y);
-                        y[o0] = __float2bfloat16_rn(vg);
-                        y[o0 + 8] = __float2bfloat16_rn(vg8);
-                    }
+                const int64_t o0 = (int64_t)T.pair0 * out + r0 + ra;
+                const bool ok8 = r0 + ra + 8 < out;
+                if (a.y_dtype == IQK_F32) {
+                    float *y = static_cast<float *>(a.y);
+                    y[o0] = vg;
+                    if (ok8) y[o0 + 8] = vg8;
+                } else if (a.y_dtype == IQK_F16) {
+                    __half *y = static_cast<__half *>(a.y);
+                    y[o0] = __float2half_rn(vg);
+                    if (ok8) y[o0 + 8] = __float2half_rn(vg8);
+                } else {
+                    __nv_bfloat16 *y = static_cast<__nv_bfloat16 *>(a.y);
+                    y[o0] = __float2bfloat16_rn(vg);
+                    if (ok8) y[o0 + 8] = __float2bfloat16_rn(vg8);
                 }
             }
-            asm volatile("bar.sync %0, %1;\n" ::"r"(1 + rt), "r"(32 * kKSplit) : "memory");
         }
         __syncwarp();
-        if (r == cpw - 1 && lane == 0) {
-            // release every stage of this item at once: its first stage holds
-            // the scale streams the later rounds and the epilogue still read
-            for (int q = j - r; q <= j; ++q) mbar_arrive(&empty[q % kStages]);
+        if (lane == 0) {
+            mbar_arrive(&empty[slot]);                         // this round's stage
+            if (r == cpw - 1) mbar_arrive(&sempty[o & 1]);     // the item's scale slot
         }
         if (++r == cpw) {
             r = 0;
