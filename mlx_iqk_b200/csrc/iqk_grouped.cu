@@ -68,8 +68,11 @@ constexpr int kMaxCodeSlots = 4;
 constexpr int kMaxXSlots = 8;
 constexpr int kMinXSlots = 4;
 // Group h dequantizes stages g = h (mod 4) into A slot h and its issuer warp
-// runs their MMAs into accumulator h. Reusing slot h waits for the stage-done
-// barrier of stage g - 4, never lapped while awaited because xslots >= 4.
+// runs their MMAs into accumulator h. Reusing slot h waits on tfree[h], which
+// issuer h commits after each of the group's stages: its next phase needs
+// group h's own next stage, so it is never lapped while awaited. (A stage-done
+// barrier of the activation ring can be lapped by another group's later stage
+// when the ring is deeper than four.)
 constexpr int kTmemCols = 512;
 // TMEM columns: accumulators 0-3 (64 columns each, one per group), then the
 // 4 A slots of 64 columns. Each issuer waits on shared-memory barriers only
@@ -77,7 +80,7 @@ constexpr int kTmemCols = 512;
 // the epilogue sums the four accumulators in a fixed order.
 constexpr int kTok = 64;                             // tokens per work tile
 constexpr uint32_t kACol = kGroups * kTok;
-constexpr int kBarBytes = 8 * (2 * kMaxXSlots + 2 * kMaxCodeSlots + kGroups + 3 + 4) + 16;
+constexpr int kBarBytes = 8 * (2 * kMaxXSlots + 2 * kMaxCodeSlots + 2 * kGroups + 3 + 4) + 16;
 constexpr int kSmemCap = 227 * 1024;
 
 // Per-item scale buffer: per (stage, row) scale words, transposed so that a
@@ -474,7 +477,8 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
     uint64_t *cfull = sdone + kMaxXSlots;
     uint64_t *cempty = cfull + kMaxCodeSlots;
     uint64_t *aready = cempty + kMaxCodeSlots;
-    uint64_t *dfull = aready + kGroups;
+    uint64_t *tfree = aready + kGroups;  // [4] A slot h free again
+    uint64_t *dfull = tfree + kGroups;
     uint64_t *dempty = dfull + 1;
     uint64_t *drain = dempty + 1;
     uint64_t *sfull = drain + 1;   // [2]
@@ -499,7 +503,10 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
             bar_init(&cfull[i], 1);
             bar_init(&cempty[i], 4 * kDqGroups);
         }
-        for (int i = 0; i < kGroups; ++i) bar_init(&aready[i], 4);
+        for (int i = 0; i < kGroups; ++i) {
+            bar_init(&aready[i], 4);
+            bar_init(&tfree[i], 1);
+        }
         bar_init(dfull, kGroups);
         bar_init(dempty, 4 * kDqGroups);
         bar_init(drain, kGroups);
@@ -630,6 +637,7 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
                     }
                     first = false;
                     tc_commit(&sdone[xs]);
+                    tc_commit(&tfree[h]);
                 }
                 if (!ok) {
                     give_up();
@@ -700,9 +708,9 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
                 const uint4 c1 = lds128(code_u + (((uint32_t)(2 * h + 1) ^ rsw) << 4));
                 __syncwarp();
                 if (lane == 0) bar_arrive(&cempty[cs]);
-                // A slot h was last read by stage g - 4
-                if (g >= kGroups && !bar_wait(&sdone[(g - kGroups) % XS],
-                                              (uint32_t)((g - kGroups) / XS) & 1u, abort_flag)) {
+                // A slot h was last read by the group's previous stage (g - 4)
+                if (g >= kGroups &&
+                    !bar_wait(&tfree[h], ((uint32_t)(g >> 2) & 1u) ^ 1u, abort_flag)) {
                     give_up();
                     break;
                 }

@@ -184,3 +184,21 @@ def test_grouped_full_geometry_sampled(cuda):
             w = oracle.decode(member, st, n)
             want = w.astype(np.float64) @ xs[t]
             assert rel_err(got[t, k], want) < GROUPED_TOL, (t, k)
+
+
+def test_grouped_repeated_calls_never_time_out(cuda):
+    """Config-5 gate geometry, 40 calls in a row: the bounded waits inside the
+    kernel must never expire (the device error word stays free of TIMEOUT)."""
+    from mlx_iqk_b200.profile_cases import random_module
+    gen = torch.Generator(device=cuda).manual_seed(23)
+    E, out, n, T = 256, 2048, 4096, 2048
+    mod = random_module("iq2_ks", E, out, n, cuda, gen)
+    x = torch.randn((T, n), generator=gen, device=cuda).to(torch.bfloat16)
+    logits = torch.randn((T, E), generator=gen, device=cuda)
+    sel = torch.topk(logits, 6, dim=-1).indices.to(torch.int32).reshape(-1).contiguous()
+    y = torch.empty((sel.numel(), out), device=cuda)
+    ws = torch.empty(K.grouped_workspace_bytes(n, E, sel.numel()), dtype=torch.uint8, device=cuda)
+    K.grouped_prepare(x, E, n, sel, None, ws)
+    for _ in range(40):
+        K.grouped_run("iq2_ks", mod._streams(), E, out, n, sel.numel(), y, ws)
+    assert K.grouped_read_error(ws) & 8 == 0  # IQK_DEVERR_TIMEOUT
