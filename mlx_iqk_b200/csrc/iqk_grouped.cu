@@ -606,48 +606,51 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
         __syncwarp();
     } else if (warp >= kIssuer0) {
         // MMA issuer of group h: the stages g = h (mod 4), into accumulator h.
+        // The whole warp runs the loop converged; one elected lane issues.
         const int h = warp - kIssuer0;
-        if (lane == 0) {
-            int g = 0, item_i = 0;
-            for (int64_t it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++item_i) {
-                const int4 tl = tiles[it / a.rblocks];
-                const int npad = (tl.z + 15) & ~15;
-                const uint32_t idesc = idesc_f16(kGroupRows, npad);
-                // accumulator h is free once the previous item's epilogue read it
-                if (item_i > 0 && !bar_wait(dempty, (uint32_t)(item_i - 1) & 1u, abort_flag)) {
-                    give_up();
+        int g = 0, item_i = 0;
+        bool ok = true;
+        for (int64_t it = blockIdx.x; ok && it < items && !*abort_flag; it += gridDim.x, ++item_i) {
+            const int4 tl = tiles[it / a.rblocks];
+            const int npad = (tl.z + 15) & ~15;
+            const uint32_t idesc = idesc_f16(kGroupRows, npad);
+            // accumulator h is free once the previous item's epilogue read it
+            if (item_i > 0 && !bar_wait(dempty, (uint32_t)(item_i - 1) & 1u, abort_flag)) {
+                ok = false;
+                break;
+            }
+            bool first = true;
+            for (int ks = 0; ks < KS; ++ks, ++g) {
+                if ((g & 3) != h) continue;
+                const int xs = g % XS;
+                if (!bar_wait(&xfull[xs], (uint32_t)(g / XS) & 1u, abort_flag) ||
+                    !bar_wait(&aready[h], (uint32_t)(g >> 2) & 1u, abort_flag)) {
+                    ok = false;
                     break;
                 }
-                bool ok = true, first = true;
-                for (int ks = 0; ks < KS; ++ks, ++g) {
-                    if ((g & 3) != h) continue;
-                    const int xs = g % XS;
-                    if (!bar_wait(&xfull[xs], (uint32_t)(g / XS) & 1u, abort_flag) ||
-                        !bar_wait(&aready[h], (uint32_t)(g >> 2) & 1u, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t st = smem_u + G.x + xs * x_slot_bytes(cap);
+                tc_fence_after();
+                const uint32_t st = smem_u + G.x + xs * x_slot_bytes(cap);
+                if (elect_one()) {
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk) {
                         const uint64_t bdesc = sw128_desc(st + (kk >> 2) * xatom + (kk & 3) * 32);
                         tc_mma_ts(tmem + h * kTok, tmem + kACol + h * 64 + kk * 8, bdesc, idesc,
                                   (first && kk == 0) ? 0u : 1u);
                     }
-                    first = false;
                     tc_commit(&sdone[xs]);
                     tc_commit(&tfree[h]);
                 }
-                if (!ok) {
-                    give_up();
-                    break;
-                }
-                tc_commit(dfull);
+                __syncwarp();
+                first = false;
             }
-            // Every MMA issued must finish before tensor memory is freed.
-            tc_commit(drain);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            if (elect_one()) tc_commit(dfull);
+            __syncwarp();
         }
+        if (!ok && lane == 0) give_up();
+        // Every MMA issued must finish before tensor memory is freed.
+        if (elect_one()) tc_commit(drain);
         __syncwarp();
     } else if (warp >= kLoader0 && warp < kDq0) {
         const int t = threadIdx.x - 32 * kLoader0;  // 0..63
