@@ -58,38 +58,35 @@ using namespace dev;
 constexpr int kThreadsG = 800;                       // 25 warps
 constexpr int kProducer = 0, kTmemWarp = 1, kLoader0 = 2, kDq0 = 4, kCodeWarp = 20,
               kIssuer0 = 21;
-constexpr int kDqGroups = 4;                         // dequant warps per TMEM lane quarter
 constexpr int kStageK = 128;                         // weights per k-stage (8 MMAs of K=16)
-constexpr int kGroups = 4;                           // dequant groups = MMA issuers = A slots
 constexpr int kMaxKS = 4096 / kStageK;               // k-stages of the widest row
 constexpr int kCodeK = 512;                          // weights per code load (4 stages)
-constexpr int kCodeSlot = kGroupRows * kCodeK / 4;   // 16 KB: 128 rows x 128 B, 128-byte swizzle
+constexpr int kCodeBox = kGroupRows * kCodeK / 4;    // 16 KB: 128 rows x 128 B, 128-byte swizzle
 constexpr int kMaxCodeSlots = 4;
 constexpr int kMaxXSlots = 8;
 constexpr int kMinXSlots = 4;
-// Group h dequantizes stages g = h (mod 4) into A slot h and its issuer warp
-// runs their MMAs into accumulator h. Reusing slot h waits on tfree[h], which
+constexpr int kMaxGroups = 4;
+// Work item = one token tile x RB*128 output rows (RB "halves" of 128 rows,
+// RB = 1 or 2). There are 4/RB dequant groups; group h takes the k-stages
+// g = h (mod 4/RB) for all RB halves, and its issuer warp runs their MMAs
+// (RB x 8 per stage, sharing one activation stage) into the group's RB
+// accumulators. TMEM columns, 64 each: accumulators (group h, half j) at
+// 64*(h*RB + j), then the A slots in the same order from column 256 -- 512
+// columns for either RB. Reusing a group's A slots waits on tfree[h], which
 // issuer h commits after each of the group's stages: its next phase needs
-// group h's own next stage, so it is never lapped while awaited. (A stage-done
-// barrier of the activation ring can be lapped by another group's later stage
-// when the ring is deeper than four.)
+// group h's own next stage, so it is never lapped while awaited.
 constexpr int kTmemCols = 512;
-// TMEM columns: accumulators 0-3 (64 columns each, one per group), then the
-// 4 A slots of 64 columns. Each issuer waits on shared-memory barriers only
-// for its own group's stages, so a wait never stalls another group's MMAs;
-// the epilogue sums the four accumulators in a fixed order.
 constexpr int kTok = 64;                             // tokens per work tile
-constexpr uint32_t kACol = kGroups * kTok;
-constexpr int kBarBytes = 8 * (2 * kMaxXSlots + 2 * kMaxCodeSlots + 2 * kGroups + 3 + 4) + 16;
+constexpr uint32_t kACol = 256;
+constexpr int kBarBytes = 8 * (2 * kMaxXSlots + 2 * kMaxCodeSlots + 2 * kMaxGroups + 3 + 4) + 16;
 constexpr int kSmemCap = 227 * 1024;
 
 // Per-item scale buffer: per (stage, row) scale words, transposed so that a
 // warp's 32 rows read 32 consecutive words; then row factors and the tile's
 // column table (pair index, 2^-S).
 __host__ __device__ constexpr int scale_words(int member) { return member == IQK_IQ2_K ? 2 : 1; }
-__host__ __device__ constexpr int scale_buf_bytes(int member, int n) {
-    return scale_words(member) * (n / kStageK) * kGroupRows * 4 + 2 * kGroupRows * 4 +
-           kGroupTokMax * 4;
+__host__ __device__ constexpr int scale_buf_bytes(int member, int n, int rows) {
+    return scale_words(member) * (n / kStageK) * rows * 4 + rows * 4 + 2 * kTok * 4;
 }
 __host__ __device__ constexpr int x_slot_bytes(int tok_cap) { return tok_cap * 2 * 128; }
 
@@ -348,8 +345,8 @@ __device__ __forceinline__ uint4 ldg128(const void *p) {
 // per (stage, row) into the transposed buffer, plus row factors and the
 // tile's column table. Each thread owns rows t and t + 64.
 template <int MEMBER>
-__device__ __forceinline__ void load_item_scales(const GroupedArgs &a, int4 tl, int rb, int t,
-                                                 uint32_t *sc, float *rsc, int32_t *colp,
+__device__ __forceinline__ void load_item_scales(const GroupedArgs &a, int4 tl, int rb, int rows,
+                                                 int t, uint32_t *sc, float *rsc, int32_t *colp,
                                                  float *colf) {
     const int n = a.n, KS = n / kStageK;
     const bool wide = n == 4096;
@@ -362,9 +359,8 @@ __device__ __forceinline__ void load_item_scales(const GroupedArgs &a, int4 tl, 
         colf[j] = __int_as_float((127 - pscale[tl.y + j]) << 23);  // 2^-S, S <= 126
     }
 #pragma unroll 1
-    for (int rr = 0; rr < 2; ++rr) {
-        const int r = t + 64 * rr;
-        const int64_t rl = (int64_t)rb * kGroupRows + r;
+    for (int r = t; r < rows; r += 64) {
+        const int64_t rl = (int64_t)rb * rows + r;
         const int64_t row = (int64_t)tl.x * out + (rl < out ? rl : 0);
         if (MEMBER == IQK_IQ2_KS) {
             // every load of the row is issued before any is used
@@ -396,7 +392,7 @@ __device__ __forceinline__ void load_item_scales(const GroupedArgs &a, int4 tl, 
                 for (int j = 0; j < 8; ++j) {
                     const uint32_t lo = (sv[j >> 1] >> (16 * (j & 1))) & 0xffffu;
                     const uint32_t hi = (h32 >> (4 * j)) & 15u, al = (x32 >> (4 * j)) & 15u;
-                    sc[(8 * c + j) * kGroupRows + r] = lo | (hi << 16) | (al << 20);
+                    sc[(8 * c + j) * rows + r] = lo | (hi << 16) | (al << 20);
                 }
             }
             rsc[r] = half_bits_to_float(dvb);
@@ -435,8 +431,8 @@ __device__ __forceinline__ void load_item_scales(const GroupedArgs &a, int4 tl, 
                 const float d = half_bits_to_float((uint16_t)(dw >> (16 * (di & 1)))) * dn;
                 const __half dh = __float2half_rn(d);
                 const uint32_t db = (uint32_t)*reinterpret_cast<const uint16_t *>(&dh);
-                sc[ks * kGroupRows + r] = s32;
-                sc[(KS + ks) * kGroupRows + r] = ((x32 >> (8 * (ks & 3))) & 0xffu) | (db << 16);
+                sc[ks * rows + r] = s32;
+                sc[(KS + ks) * rows + r] = ((x32 >> (8 * (ks & 3))) & 0xffu) | (db << 16);
             }
         }
     }
@@ -447,38 +443,41 @@ struct GemmSmem {
     uint32_t x, code, sbuf, bars;  // offsets
     int sb;                        // bytes of one scale buffer
 };
-__host__ __device__ inline GemmSmem gemm_smem(int member, int n, int tok_cap, int xslots,
+__host__ __device__ inline GemmSmem gemm_smem(int member, int n, int rb_rows, int xslots,
                                               int cslots) {
     GemmSmem g;
     g.x = 0;
-    g.code = (uint32_t)(xslots * x_slot_bytes(tok_cap));
-    g.sbuf = g.code + cslots * kCodeSlot;
-    g.sb = (scale_buf_bytes(member, n) + 15) & ~15;
+    g.code = (uint32_t)(xslots * x_slot_bytes(kTok));
+    g.sbuf = g.code + cslots * (rb_rows / kGroupRows) * kCodeBox;
+    g.sb = (scale_buf_bytes(member, n, rb_rows) + 15) & ~15;
     g.bars = g.sbuf + 2 * g.sb;
     return g;
 }
 
-template <int MEMBER>
+template <int MEMBER, int RB>
 __global__ void __launch_bounds__(kThreadsG, 1)
 grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_map,
                     const __grid_constant__ XMaps x_maps) {
+    constexpr int kRows = RB * kGroupRows;    // output rows per work item
+    constexpr int kNG = kMaxGroups / RB;      // dequant groups = issuers
+    constexpr int kCodeSlot = RB * kCodeBox;  // codes of one 512-weight chunk, all rows
     extern __shared__ char smem_raw[];
     char *smem = smem_raw + ((1024u - (saddr(smem_raw) & 1023u)) & 1023u);
     const uint32_t smem_u = saddr(smem);
     const int n = a.n, KS = n / kStageK, XS = a.xslots, CS = a.cslots;
     const int cap = a.tok_cap;
-    const GemmSmem G = gemm_smem(MEMBER, n, cap, XS, CS);
+    const GemmSmem G = gemm_smem(MEMBER, n, kRows, XS, CS);
     const uint32_t xatom = (uint32_t)cap * 128u;  // bytes of one 64-wide k atom
     char *sbuf = smem + G.sbuf;
     // xfull: a stage's activations landed; sdone: the stage's MMAs finished
-    // (frees its activation slot and, four stages later, its TMEM A slot).
+    // (frees its activation slot).
     uint64_t *xfull = reinterpret_cast<uint64_t *>(smem + G.bars);
     uint64_t *sdone = xfull + kMaxXSlots;
     uint64_t *cfull = sdone + kMaxXSlots;
     uint64_t *cempty = cfull + kMaxCodeSlots;
     uint64_t *aready = cempty + kMaxCodeSlots;
-    uint64_t *tfree = aready + kGroups;  // [4] A slot h free again
-    uint64_t *dfull = tfree + kGroups;
+    uint64_t *tfree = aready + kMaxGroups;  // group h's A slots free again
+    uint64_t *dfull = tfree + kMaxGroups;
     uint64_t *dempty = dfull + 1;
     uint64_t *drain = dempty + 1;
     uint64_t *sfull = drain + 1;   // [2]
@@ -501,18 +500,18 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
         }
         for (int i = 0; i < CS; ++i) {
             bar_init(&cfull[i], 1);
-            bar_init(&cempty[i], 4 * kDqGroups);
+            bar_init(&cempty[i], 16);
         }
-        for (int i = 0; i < kGroups; ++i) {
-            bar_init(&aready[i], 4);
+        for (int i = 0; i < kNG; ++i) {
+            bar_init(&aready[i], 4 * RB);
             bar_init(&tfree[i], 1);
         }
-        bar_init(dfull, kGroups);
-        bar_init(dempty, 4 * kDqGroups);
-        bar_init(drain, kGroups);
+        bar_init(dfull, kNG);
+        bar_init(dempty, 16);
+        bar_init(drain, kNG);
         for (int i = 0; i < 2; ++i) {
             bar_init(&sfull[i], 64);
-            bar_init(&sempty[i], 4 * kDqGroups);
+            bar_init(&sempty[i], 16);
         }
         *abort_flag = 0;
         bar_fence_init();
@@ -578,14 +577,14 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
         }
         __syncwarp();
     } else if (warp == kCodeWarp) {
-        // Code chunks (512 weights of 128 rows) run ahead on their own ring.
+        // Code chunks (512 weights of all the item's rows) run ahead on their own ring.
         if (lane == 0) {
             int cchunk = 0;
             bool ok = true;
             for (int64_t it = blockIdx.x; ok && it < items && !*abort_flag; it += gridDim.x) {
                 const int4 tl = tiles[it / a.rblocks];
                 const int rb = (int)(it % a.rblocks);
-                const int row0 = (int)((int64_t)tl.x * out + (int64_t)rb * kGroupRows);
+                const int row0 = (int)((int64_t)tl.x * out + (int64_t)rb * kRows);
                 for (int c = 0; c < KS / 4; ++c, ++cchunk) {
                     const int cs = cchunk % CS;
                     if (!bar_wait(&cempty[cs], ((uint32_t)(cchunk / CS) & 1u) ^ 1u, abort_flag)) {
@@ -593,8 +592,10 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
                         break;
                     }
                     bar_expect_tx(&cfull[cs], kCodeSlot);
-                    tma_2d(smem_u + G.code + cs * kCodeSlot, &qs_map, c * (kCodeK / 4), row0,
-                           &cfull[cs]);
+#pragma unroll
+                    for (int j = 0; j < RB; ++j)
+                        tma_2d(smem_u + G.code + cs * kCodeSlot + j * kCodeBox, &qs_map,
+                               c * (kCodeK / 4), row0 + j * kGroupRows, &cfull[cs]);
                 }
             }
             if (!ok) give_up();
@@ -605,53 +606,60 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
         }
         __syncwarp();
     } else if (warp >= kIssuer0) {
-        // MMA issuer of group h: the stages g = h (mod 4), into accumulator h.
+        // MMA issuer of group h: the stages g = h (mod kNG), RB x 8 MMAs each.
         // The whole warp runs the loop converged; one elected lane issues.
         const int h = warp - kIssuer0;
-        int g = 0, item_i = 0;
-        bool ok = true;
-        for (int64_t it = blockIdx.x; ok && it < items && !*abort_flag; it += gridDim.x, ++item_i) {
-            const int4 tl = tiles[it / a.rblocks];
-            const int npad = (tl.z + 15) & ~15;
-            const uint32_t idesc = idesc_f16(kGroupRows, npad);
-            // accumulator h is free once the previous item's epilogue read it
-            if (item_i > 0 && !bar_wait(dempty, (uint32_t)(item_i - 1) & 1u, abort_flag)) {
-                ok = false;
-                break;
-            }
-            bool first = true;
-            for (int ks = 0; ks < KS; ++ks, ++g) {
-                if ((g & 3) != h) continue;
-                const int xs = g % XS;
-                if (!bar_wait(&xfull[xs], (uint32_t)(g / XS) & 1u, abort_flag) ||
-                    !bar_wait(&aready[h], (uint32_t)(g >> 2) & 1u, abort_flag)) {
+        if (h < kNG) {
+            int g = 0, item_i = 0;
+            bool ok = true;
+            for (int64_t it = blockIdx.x; ok && it < items && !*abort_flag;
+                 it += gridDim.x, ++item_i) {
+                const int4 tl = tiles[it / a.rblocks];
+                const int npad = (tl.z + 15) & ~15;
+                const uint32_t idesc = idesc_f16(kGroupRows, npad);
+                // the accumulators are free once the previous item's epilogue read them
+                if (item_i > 0 && !bar_wait(dempty, (uint32_t)(item_i - 1) & 1u, abort_flag)) {
                     ok = false;
                     break;
                 }
-                tc_fence_after();
-                const uint32_t st = smem_u + G.x + xs * x_slot_bytes(cap);
-                if (elect_one()) {
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const uint64_t bdesc = sw128_desc(st + (kk >> 2) * xatom + (kk & 3) * 32);
-                        tc_mma_ts(tmem + h * kTok, tmem + kACol + h * 64 + kk * 8, bdesc, idesc,
-                                  (first && kk == 0) ? 0u : 1u);
+                bool first = true;
+                for (int ks = 0; ks < KS; ++ks, ++g) {
+                    if (g % kNG != h) continue;
+                    const int xs = g % XS;
+                    if (!bar_wait(&xfull[xs], (uint32_t)(g / XS) & 1u, abort_flag) ||
+                        !bar_wait(&aready[h], (uint32_t)(g / kNG) & 1u, abort_flag)) {
+                        ok = false;
+                        break;
                     }
-                    tc_commit(&sdone[xs]);
-                    tc_commit(&tfree[h]);
+                    tc_fence_after();
+                    const uint32_t st = smem_u + G.x + xs * x_slot_bytes(cap);
+                    if (elect_one()) {
+#pragma unroll
+                        for (int kk = 0; kk < 8; ++kk) {
+                            const uint64_t bdesc = sw128_desc(st + (kk >> 2) * xatom + (kk & 3) * 32);
+#pragma unroll
+                            for (int j = 0; j < RB; ++j) {
+                                const uint32_t slot = (uint32_t)(h * RB + j) * 64u;
+                                tc_mma_ts(tmem + slot, tmem + kACol + slot + kk * 8, bdesc, idesc,
+                                          (first && kk == 0) ? 0u : 1u);
+                            }
+                        }
+                        tc_commit(&sdone[xs]);
+                        tc_commit(&tfree[h]);
+                    }
+                    __syncwarp();
+                    first = false;
                 }
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+                if (elect_one()) tc_commit(dfull);
                 __syncwarp();
-                first = false;
             }
-            ok = __all_sync(0xffffffffu, ok);
-            if (!ok) break;
-            if (elect_one()) tc_commit(dfull);
+            if (!ok && lane == 0) give_up();
+            // Every MMA issued must finish before tensor memory is freed.
+            if (elect_one()) tc_commit(drain);
             __syncwarp();
         }
-        if (!ok && lane == 0) give_up();
-        // Every MMA issued must finish before tensor memory is freed.
-        if (elect_one()) tc_commit(drain);
-        __syncwarp();
     } else if (warp >= kLoader0 && warp < kDq0) {
         const int t = threadIdx.x - 32 * kLoader0;  // 0..63
         int item_i = 0;
@@ -664,25 +672,27 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
             }
             char *b = sbuf + buf * G.sb;
             uint32_t *sc = reinterpret_cast<uint32_t *>(b);
-            float *rsc = reinterpret_cast<float *>(b + scale_words(MEMBER) * KS * kGroupRows * 4);
-            load_item_scales<MEMBER>(a, tiles[it / a.rblocks], (int)(it % a.rblocks), t, sc, rsc,
-                                     reinterpret_cast<int32_t *>(rsc + kGroupRows),
-                                     rsc + 2 * kGroupRows);
+            float *rsc = reinterpret_cast<float *>(b + scale_words(MEMBER) * KS * kRows * 4);
+            load_item_scales<MEMBER>(a, tiles[it / a.rblocks], (int)(it % a.rblocks), kRows, t,
+                                     sc, rsc, reinterpret_cast<int32_t *>(rsc + kRows),
+                                     rsc + kRows + kTok);
             bar_arrive(&sfull[buf]);
         }
     } else if (warp >= kDq0 && warp < kCodeWarp) {
+        // dequant warp: TMEM lane quarter q, group h, row half j
         const int dq = warp - kDq0;
-        const int q = warp & 3;        // TMEM lane quarter this warp may access
-        const int h = dq >> 2;         // stages g with g % 4 == h (TMEM slot h)
-        const int rloc = 32 * q + lane;
+        const int q = warp & 3;
+        const int h = (dq >> 2) % kNG, j = (dq >> 2) / kNG;
+        const int rloc = kGroupRows * j + 32 * q + lane;  // item-local row
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         const uint32_t rsw = (uint32_t)(rloc & 7);  // 128-byte swizzle of this code row
+        const uint32_t aslot = (uint32_t)(h * RB + j) * 64u;
         int g = 0, item_i = 0;
         for (int64_t it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++item_i) {
             const int4 tl = tiles[it / a.rblocks];
             const int rb = (int)(it % a.rblocks);
             const int npad = (tl.z + 15) & ~15;
-            const int64_t rlocal = (int64_t)rb * kGroupRows + rloc;
+            const int64_t rlocal = (int64_t)rb * kRows + rloc;
             const bool row_ok = rlocal < out;
             const int buf = item_i & 1;
             if (!bar_wait(&sfull[buf], (uint32_t)(item_i >> 1) & 1u, abort_flag)) {
@@ -692,34 +702,39 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
             const char *b = sbuf + buf * G.sb;
             const uint32_t *sc = reinterpret_cast<const uint32_t *>(b);
             const float *rsc =
-                reinterpret_cast<const float *>(b + scale_words(MEMBER) * KS * kGroupRows * 4);
-            const int32_t *colp = reinterpret_cast<const int32_t *>(rsc + kGroupRows);
-            const float *colf = rsc + 2 * kGroupRows;
+                reinterpret_cast<const float *>(b + scale_words(MEMBER) * KS * kRows * 4);
+            const int32_t *colp = reinterpret_cast<const int32_t *>(rsc + kRows);
+            const float *colf = rsc + kRows + kTok;
             const float rscale = rsc[rloc];
             for (int ks = 0; ks < KS; ++ks, ++g) {
-                if ((g & 3) != h) continue;
-                const int chunk = g >> 2, cs = chunk % CS;
-                const uint32_t s0 = sc[ks * kGroupRows + rloc];
-                const uint32_t s1 = scale_words(MEMBER) == 2 ? sc[(KS + ks) * kGroupRows + rloc] : 0u;
+                const int chunk = g >> 2, cs = chunk % CS, sub = g & 3;
+                if (g % kNG != h) {
+                    // still release the code chunk once this warp's stages in it are done
+                    continue;
+                }
+                const uint32_t s0 = sc[ks * kRows + rloc];
+                const uint32_t s1 = scale_words(MEMBER) == 2 ? sc[(KS + ks) * kRows + rloc] : 0u;
                 if (!bar_wait(&cfull[cs], (uint32_t)(chunk / CS) & 1u, abort_flag)) {
                     give_up();
                     break;
                 }
-                // this stage's 32 code bytes: 16-byte chunks 2h, 2h+1 of the row
+                // this stage's 32 code bytes: 16-byte chunks 2*sub, 2*sub+1 of the row
                 const uint32_t code_u = smem_u + G.code + cs * kCodeSlot + rloc * 128;
-                const uint4 c0 = lds128(code_u + (((uint32_t)(2 * h) ^ rsw) << 4));
-                const uint4 c1 = lds128(code_u + (((uint32_t)(2 * h + 1) ^ rsw) << 4));
+                const uint4 c0 = lds128(code_u + (((uint32_t)(2 * sub) ^ rsw) << 4));
+                const uint4 c1 = lds128(code_u + (((uint32_t)(2 * sub + 1) ^ rsw) << 4));
                 __syncwarp();
-                if (lane == 0) bar_arrive(&cempty[cs]);
-                // A slot h was last read by the group's previous stage (g - 4)
-                if (g >= kGroups &&
-                    !bar_wait(&tfree[h], ((uint32_t)(g >> 2) & 1u) ^ 1u, abort_flag)) {
+                // the warp's last stage of this chunk releases it (RB = 1: one
+                // stage per chunk; RB = 2: stages sub = h and h + 2)
+                if (lane == 0 && sub + kNG >= 4) bar_arrive(&cempty[cs]);
+                // the group's A slots were last read by its previous stage
+                if (g >= kNG &&
+                    !bar_wait(&tfree[h], ((uint32_t)(g / kNG) & 1u) ^ 1u, abort_flag)) {
                     give_up();
                     break;
                 }
                 tc_fence_after();
                 const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-                const uint32_t taddr = tmem + lane_base + kACol + h * 64;
+                const uint32_t taddr = tmem + lane_base + kACol + aslot;
                 float dsb = 0.f;
                 if (MEMBER == IQK_IQ2_K) dsb = __half2float(__ushort_as_half((uint16_t)(s1 >> 16)));
                 uint32_t t01 = 0, t23 = 0;
@@ -752,32 +767,31 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
                 if (lane == 0) bar_arrive(&aready[h]);
             }
             if (*abort_flag) break;
-            // Epilogue: D rows are this thread's output row, columns the tile's tokens.
+            // Epilogue: D rows are this thread's output row, columns the tile's
+            // tokens; the kNG groups' accumulators of this half are summed in order.
             if (!bar_wait(dfull, (uint32_t)item_i & 1u, abort_flag)) {
                 give_up();
                 break;
             }
             tc_fence_after();
-            for (int c = 8 * h; c < npad; c += 8 * kDqGroups) {
+            for (int c = 8 * h; c < npad; c += 8 * kNG) {
                 float sum[8];
-                {
-                    uint32_t d0[8], d1[8], d2[8], d3[8];
-                    tmem_ld8(tmem + lane_base + c, d0);
-                    tmem_ld8(tmem + lane_base + kTok + c, d1);
-                    tmem_ld8(tmem + lane_base + 2 * kTok + c, d2);
-                    tmem_ld8(tmem + lane_base + 3 * kTok + c, d3);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) sum[k] = 0.f;
+#pragma unroll
+                for (int hh = 0; hh < kNG; ++hh) {
+                    uint32_t d[8];
+                    tmem_ld8(tmem + lane_base + (uint32_t)(hh * RB + j) * 64u + c, d);
                     tc_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        sum[j] = ((__uint_as_float(d0[j]) + __uint_as_float(d1[j])) +
-                                  __uint_as_float(d2[j])) + __uint_as_float(d3[j]);
+                    for (int k = 0; k < 8; ++k) sum[k] += __uint_as_float(d[k]);
                 }
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int col = c + j;
+                for (int k = 0; k < 8; ++k) {
+                    const int col = c + k;
                     if (col < tl.z && row_ok) {
                         const int64_t o = (int64_t)colp[col] * out + rlocal;
-                        const float v = sum[j] * rscale * colf[col];
+                        const float v = sum[k] * rscale * colf[col];
                         if (a.y_dtype == IQK_F32) store_out<float>(a.y, o, v);
                         else if (a.y_dtype == IQK_F16) store_out<__half>(a.y, o, v);
                         else store_out<__nv_bfloat16>(a.y, o, v);
@@ -885,23 +899,31 @@ cudaError_t launch_grouped_run(int member, const void *const *streams, int64_t n
     ga.out_features = out_features;
     ga.n = n;
     ga.pairs = (int)pairs;
-    ga.rblocks = (int)((out_features + kGroupRows - 1) / kGroupRows);
     ga.ws = static_cast<const char *>(ws);
     ga.L = L;
     ga.err = reinterpret_cast<int32_t *>(const_cast<char *>(ga.ws) + L.hdr);
     ga.y = y;
     ga.y_dtype = y_dtype;
     ga.tok_cap = L.tok_cap;
-    // Two code slots and up to eight activation slots; give up a code slot
-    // before going below four activation slots.
-    int cslots = kMaxCodeSlots, xslots = 0, fixed = 0;
-    for (; cslots >= 1; --cslots) {
-        fixed = 1024 + (int)gemm_smem(member, n, L.tok_cap, 0, cslots).bars + kBarBytes;
-        xslots = (kSmemCap - fixed) / x_slot_bytes(L.tok_cap);
-        if (xslots >= kMinXSlots) break;
+    // Items of 256 rows (two halves sharing each activation stage) when both
+    // scale buffers fit beside two 32 KB code slots and four activation
+    // slots; otherwise 128 rows.
+    auto plan = [&](int rows, int &cslots, int &xslots, int &fixed) {
+        for (cslots = kMaxCodeSlots; cslots >= 1; --cslots) {
+            if (rows == 256 && cslots > 2) continue;
+            fixed = 1024 + (int)gemm_smem(member, n, rows, 0, cslots).bars + kBarBytes;
+            xslots = (kSmemCap - fixed) / x_slot_bytes(L.tok_cap);
+            if (xslots >= kMinXSlots) break;
+        }
+        if (xslots > kMaxXSlots) xslots = kMaxXSlots;
+        return cslots >= 1 && xslots >= kMinXSlots;
+    };
+    int cslots = 0, xslots = 0, fixed = 0, rows = 256;
+    if (!plan(256, cslots, xslots, fixed)) {
+        rows = 128;
+        if (!plan(128, cslots, xslots, fixed)) return cudaErrorInvalidConfiguration;
     }
-    if (xslots > kMaxXSlots) xslots = kMaxXSlots;
-    if (xslots < kMinXSlots) return cudaErrorInvalidConfiguration;
+    ga.rblocks = (int)((out_features + rows - 1) / rows);
     ga.xslots = xslots;
     ga.cslots = cslots;
     const int smem = fixed + xslots * x_slot_bytes(L.tok_cap);
@@ -923,16 +945,23 @@ cudaError_t launch_grouped_run(int member, const void *const *streams, int64_t n
     const int64_t max_items = L.max_tiles * ga.rblocks;
     int64_t blocks = max_items < num_sms ? max_items : num_sms;
     if (blocks < 1) blocks = 1;
-#define IQK_GG(M)                                                                              \
+#define IQK_GG(M, R)                                                                           \
     do {                                                                                       \
-        err = cudaFuncSetAttribute(grouped_gemm_kernel<M>,                                     \
+        err = cudaFuncSetAttribute(grouped_gemm_kernel<M, R>,                                  \
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, smem);         \
         if (err != cudaSuccess) return err;                                                    \
-        grouped_gemm_kernel<M><<<(unsigned)blocks, kThreadsG, smem, stream>>>(ga, qmap, xmap); \
+        grouped_gemm_kernel<M, R><<<(unsigned)blocks, kThreadsG, smem, stream>>>(ga, qmap,     \
+                                                                                 xmap);        \
     } while (0)
-    if (member == IQK_IQ2_KS) IQK_GG(IQK_IQ2_KS);
-    else if (member == IQK_IQ2_K) IQK_GG(IQK_IQ2_K);
-    else return cudaErrorInvalidValue;
+    if (member == IQK_IQ2_KS) {
+        if (rows == 256) IQK_GG(IQK_IQ2_KS, 2);
+        else IQK_GG(IQK_IQ2_KS, 1);
+    } else if (member == IQK_IQ2_K) {
+        if (rows == 256) IQK_GG(IQK_IQ2_K, 2);
+        else IQK_GG(IQK_IQ2_K, 1);
+    } else {
+        return cudaErrorInvalidValue;
+    }
 #undef IQK_GG
     return cudaGetLastError();
 }
