@@ -1,6 +1,6 @@
 """Run one kernel case repeatedly on ``cuda:0``, for timing and for profilers.
 
-    python -m mlx_iqk_b200.profile_cases gemv    --member iq2_ks --batch 8   [--reps 20]
+    python -m mlx_iqk_b200.profile_cases gemv    --member iq2_ks --batch 8   [--reps 20] [--graph]
     python -m mlx_iqk_b200.profile_cases grouped --member iq2_ks --tokens 2048
     python -m mlx_iqk_b200.profile_cases dequant --member iq2_ks [--experts 64]
 
@@ -48,14 +48,31 @@ def random_module(member: str, experts: int, out: int, n: int, dev, gen) -> IqkS
     return mod
 
 
-def timed(fn, reps: int) -> float:
+def timed(fn, reps: int, graph: bool = False) -> float:
+    """Mean ms per call. With ``graph`` the ``reps`` calls are captured in one
+    CUDA graph first, so host launch cost does not hide short kernels."""
     for _ in range(2):
         fn()
     torch.cuda.synchronize()
+    run = fn
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s), torch.cuda.graph(g, stream=s):
+            for _ in range(reps):
+                fn()
+        torch.cuda.current_stream().wait_stream(s)
+        g.replay()
+        torch.cuda.synchronize()
+        run = g.replay
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(reps):
-        fn()
+    if graph:
+        run()
+    else:
+        for _ in range(reps):
+            run()
     e1.record()
     e1.synchronize()
     return e0.elapsed_time(e1) / reps
@@ -70,6 +87,8 @@ def main() -> None:
     ap.add_argument("--experts", type=int, default=E_DEFAULT)
     ap.add_argument("--width", type=int, default=4096, help="in_features (2048 or 4096)")
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--graph", action="store_true",
+                    help="time the calls replayed from one CUDA graph (no host launch cost)")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     gen = torch.Generator(device=dev).manual_seed(11)
@@ -89,7 +108,7 @@ def main() -> None:
                          device=dev)
         K.gemv_prepare(x, E, n, sel, None, ws)
         ms = timed(lambda: K.gemv_run(args.member, mod._streams(), E, out, n, B, B * 6, y, ws),
-                   args.reps)
+                   args.reps, args.graph)
         distinct = len(set(sel.tolist()))
         nbytes = distinct * out * rb + B * n * 2 + B * 6 * out * 4
         line.update(batch=B, distinct_experts=distinct, us=round(ms * 1e3, 2),
@@ -106,14 +125,14 @@ def main() -> None:
         ws = torch.empty(K.grouped_workspace_bytes(n, E, P), dtype=torch.uint8, device=dev)
         K.grouped_prepare(x, E, n, sel, None, ws)
         ms = timed(lambda: K.grouped_run(args.member, mod._streams(), E, out, n, P, y, ws),
-                   args.reps)
+                   args.reps, args.graph)
         flops = 2.0 * P * out * n
         line.update(tokens=T, pairs=P, us=round(ms * 1e3, 2),
                     tflops=round(flops / (ms * 1e-3) / 1e12, 1))
     else:
         y = torch.empty((E, out, n), dtype=torch.float16, device=dev)
         ms = timed(lambda: K.dequant(args.member, mod._streams(), E, out, n, 0, out, y),
-                   args.reps)
+                   args.reps, args.graph)
         nbytes = E * out * rb + E * out * n * 2
         line.update(us=round(ms * 1e3, 2), bytes=nbytes,
                     GBps=round(nbytes / (ms * 1e-3) / 1e9, 1))
