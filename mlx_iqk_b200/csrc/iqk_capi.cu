@@ -99,6 +99,14 @@ size_t iqk_gemv_workspace_bytes(int member, int64_t in_features, int64_t x_rows,
     return gemv_layout(member, in_features, x_rows, pairs).total;
 }
 
+// The GEMV addresses weight rows (expert * out_features + row) with 32-bit
+// tensor-map coordinates and counts its work items (pair x 64-row block) in
+// 32 bits.
+static bool gemv_rows_ok(int64_t num_experts, int64_t out_features, int64_t pairs) {
+    return num_experts * out_features <= (int64_t)1 << 30 &&
+           pairs * ((out_features + 63) / 64) < (int64_t)1 << 31;
+}
+
 static int check_prepare(int64_t in_features, int64_t num_experts, int64_t x_rows,
                          int64_t pairs, const int32_t *tok, int x_dtype) {
     if (!width_ok(in_features)) return IQK_ERR_WIDTH;
@@ -134,6 +142,7 @@ int iqk_gemv_run(int member, const void *const *streams, int64_t num_experts,
     if (!width_ok(in_features)) return IQK_ERR_WIDTH;
     if (num_experts <= 0 || num_experts > 4096) return IQK_ERR_GEOMETRY;
     if (out_features <= 0 || out_features % 16) return IQK_ERR_GEOMETRY;
+    if (!gemv_rows_ok(num_experts, out_features, pairs)) return IQK_ERR_GEOMETRY;
     if (pairs < 0 || x_rows < 0 || pairs > (1 << 24) || x_rows > (1 << 24))
         return IQK_ERR_GEOMETRY;
     if (!dtype_ok(y_dtype)) return IQK_ERR_ARGUMENT;
@@ -159,6 +168,7 @@ int iqk_gemv(int member, const void *x, int x_dtype, int64_t x_rows,
     int st = check_prepare(in_features, num_experts, x_rows, pairs, tok, x_dtype);
     if (st != IQK_OK) return st;
     if (out_features <= 0 || out_features % 16) return IQK_ERR_GEOMETRY;
+    if (!gemv_rows_ok(num_experts, out_features, pairs)) return IQK_ERR_GEOMETRY;
     if (!dtype_ok(y_dtype)) return IQK_ERR_ARGUMENT;
     if (pairs == 0) return IQK_OK;
     if (!y || !streams) return IQK_ERR_ARGUMENT;

@@ -21,21 +21,24 @@
 // * So every output is independent of reduction order and of how pairs are
 //   grouped: a sorted or unioned call is bit-identical to the per-pair call,
 //   and the only approximation is x's 22-bit rounding.
-// * Routing is on the device: pairs are bucketed by expert and each distinct
-//   expert's rows are streamed once for all pairs that selected it (the
-//   reference's "union" formulation, src/mlx_iqk/kernels.py:484-572, for
-//   every member).
+// * Routing is on the device: pairs are bucketed by expert, so the work tiles
+//   of one expert are adjacent and the CTAs that run them at the same time
+//   read the expert's rows from DRAM once (the later reads hit L2). This
+//   covers the reference's sorted and "union" formulations
+//   (src/mlx_iqk/kernels.py:404-572) for every member.
 //
-// Run kernel layout. A CTA item is (expert, 32-row block, pair tile of 2
-// pairs -- 1 for IQ2_K, whose two 16-weight sub-blocks per k-step occupy two
-// operand columns each). The 8 warps split it 2 row tiles x 4 k-quarters, so
-// small decode batches still spread over every SM. Each "round" moves, for
-// every warp, one 512-weight chunk of its 16 rows plus the matching slice of
-// the activation planes into a 4-stage cp.async ring; the first round of an
-// item also brings the item's scale streams. Per round each warp expands the
-// group metadata (alphabet nibble mask, scale indices) into shared memory
-// once, then runs 16 MMA k-steps. Partials of the 4 k-quarters are summed in
-// a fixed order, so results stay deterministic.
+// Run kernel layout. A CTA item is (pair, 64-row block): four compute warps
+// each own 16 rows for all of k, one producer warp streams the item through
+// a four-stage ring of TMA boxes (16 rows x 128 code bytes per warp and
+// round) plus the round's slice of activation planes, and the item's scale
+// streams arrive in one of two double-buffered scale slots. Per round each
+// warp expands its rows' group metadata (alphabet mask, integer scale) into
+// shared memory, then runs 8 MMA pairs of 64 weights. The operand build is
+// bound by the integer ALU pipe (byte permutes and logic ops, issued every
+// other cycle per scheduler), so right shifts go through mul.hi on the FMA
+// pipe and the metadata is expanded four groups at a time with byte-SIMD
+// multiplies. Items are split evenly over a persistent grid of three CTAs
+// per SM (two for IQ2_K).
 #include <cuda.h>
 
 #include "iqk_common.cuh"
@@ -310,28 +313,37 @@ template <int MEMBER> struct Geo {
     static constexpr int kMetaBytes = kPairsPerRound * kMetaSides * 8 * 16;  // per warp
 };
 
-// Scale streams of one CTA item (kItemRows rows, whole k), all but qs.
-template <int MEMBER> __host__ __device__ constexpr int slot_bytes(int n) {
-    return MEMBER == IQK_IQ2_KS ? kItemRows * (n / 64 + n / 256 + n / 256) + 2 * kItemRows
-           : MEMBER == IQK_IQ2_K ? kItemRows * (n / 32 + n / 128 + n / 128)
-                                 : kItemRows * (n / 16) + 2 * kItemRows;
-}
+// The scale streams of one member at width N: bytes per row of stream si
+// (1 .. kCount-1, component order after qs) and each stream's offset inside
+// an item's scale slot (kItemRows rows of every stream, back to back).
+template <int MEMBER, int N> struct Streams {
+    static constexpr int kCount = MEMBER == IQK_IQ2_KS ? 5 : MEMBER == IQK_IQ2_K ? 4 : 3;
+    static constexpr __host__ __device__ int b(int si) {
+        return MEMBER == IQK_IQ2_KS ? (si == 1 ? N / 64 : si == 4 ? 2 : N / 256)
+               : MEMBER == IQK_IQ2_K ? (si == 1 ? N / 32 : si == 2 ? N / 128 : 2 * (N / 256))
+                                     : (si == 1 ? N / 16 : 2);
+    }
+    static constexpr __host__ __device__ int off(int si) {
+        return si <= 1 ? 0 : off(si - 1) + kItemRows * b(si - 1);
+    }
+    static constexpr int kSlot = off(kCount);
+};
 
 // Stage: [weights: kConsumers TMA boxes][activation slice], released every
 // round. An item's scale streams sit in one of two scale slots for the whole
 // item.
-template <int MEMBER> __host__ __device__ constexpr int stage_bytes(int n) {
+template <int MEMBER> __host__ __device__ constexpr int stage_bytes() {
     return (Geo<MEMBER>::kWBytes + Geo<MEMBER>::kXBlock + 1023) / 1024 * 1024;
 }
-template <int MEMBER> __host__ __device__ constexpr int sslot_bytes(int n) {
-    return (slot_bytes<MEMBER>(n) + 127) / 128 * 128;
+template <int MEMBER, int N> __host__ __device__ constexpr int sslot_bytes() {
+    return (Streams<MEMBER, N>::kSlot + 127) / 128 * 128;
 }
 
-template <int MEMBER> __host__ __device__ constexpr int gemv_smem_bytes(int n) {
+template <int MEMBER, int N> __host__ __device__ constexpr int gemv_smem_bytes() {
     using G = Geo<MEMBER>;
     constexpr int kStages = G::kStages;
-    return 1024 /* alignment slack */ + kStages * stage_bytes<MEMBER>(n) +
-           2 * sslot_bytes<MEMBER>(n) + kConsumers * G::kMetaBytes +
+    return 1024 /* alignment slack */ + kStages * stage_bytes<MEMBER>() +
+           2 * sslot_bytes<MEMBER, N>() + kConsumers * G::kMetaBytes +
            kMaxTiles * (int)sizeof(TileRef) + (MEMBER == IQK_IQ1_S_R4 ? 4096 : 0) +
            (MEMBER == IQK_IQ2_K ? 256 : 0) + 2 * kStages * 8 + 4 * 8 + 16 +
            kPairsPerRound * 192;
@@ -339,9 +351,9 @@ template <int MEMBER> __host__ __device__ constexpr int gemv_smem_bytes(int n) {
 
 struct GemvArgs {
     const void *s[5];
-    int64_t out_features;
-    int n;
+    int out_features;  // experts x out_features <= 2^30 (checked by the C ABI)
     int pairs;
+    uint32_t one;      // 1: source of the mul.hi shift multipliers (see below)
     GemvLayout L;
     const char *ws;
     int32_t *err;  // device error word (workspace header)
@@ -379,6 +391,25 @@ __device__ __forceinline__ uint4 ld_s128(uint32_t a) {
 __device__ __forceinline__ void st_s128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
     asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w)
                  : "memory");
+}
+
+// Right shift by a power-of-two multiply-high, x >> s == mulhi(x, 2^(32-s)).
+// The operand-build loop is bound by the integer ALU pipe (byte permutes,
+// logic ops); a multiply-high issues on the FMA pipe instead. The multiplier
+// is derived from a kernel argument so that it stays a multiply.
+__device__ __forceinline__ uint32_t mulhi(uint32_t x, uint32_t m) { return __umulhi(x, m); }
+#ifndef IQK_SHR16_FMA
+#define IQK_SHR16_FMA 1
+#endif
+#ifndef IQK_SHR2_FMA
+#define IQK_SHR2_FMA 1
+#endif
+// x >> 16 and x >> 2 of the operand build (m16 = 2^16, m30 = 2^30).
+__device__ __forceinline__ uint32_t shr16(uint32_t x, uint32_t m16) {
+    return IQK_SHR16_FMA ? shr16(x, m16) : x >> 16;
+}
+__device__ __forceinline__ uint32_t shr2(uint32_t x, uint32_t m30) {
+    return IQK_SHR2_FMA ? shr2(x, m30) : x >> 2;
 }
 
 // d += A * B (int8 m16n8k32, accumulating in place).
@@ -437,19 +468,24 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
         ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 
-template <int MEMBER>
+// 2^k as a double, for |k| < 1000 (exact scaling, same result as ldexp).
+__device__ __forceinline__ double pow2(int k) {
+    return __longlong_as_double((long long)(k + 1023) << 52);
+}
+
+template <int MEMBER, int N>
 __global__ void __launch_bounds__(kThreads, Geo<MEMBER>::kMinBlocks)
 gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     extern __shared__ char smem_raw[];
     using G = Geo<MEMBER>;
+    using SS = Streams<MEMBER, N>;
     constexpr int kStages = G::kStages;
+    constexpr int CPW = N / kChunkK;  // rounds per item: 8 (n=4096) or 4 (2048)
+    constexpr int SSB = sslot_bytes<MEMBER, N>();
+    constexpr int STB = stage_bytes<MEMBER>();
     char *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    const int n = a.n;
-    const int64_t out = a.out_features;
+    const int out = a.out_features;
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const int cpw = n / kChunkK;  // rounds per item: 8 (n=4096) or 4 (2048)
-    const int SSB = sslot_bytes<MEMBER>(n);
-    const int STB = stage_bytes<MEMBER>(n);
 
     char *stages = smem;
     char *sslots = stages + kStages * STB;  // two item scale slots
@@ -474,13 +510,13 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     const int64_t xrow = a.L.xrow_bytes;
 
     const int ntiles = hdr[3];
-    const int rblocks = (int)((out + kItemRows - 1) / kItemRows);
-    const int items = ntiles * rblocks;
+    const int rblocks = (out + kItemRows - 1) / kItemRows;
+    const int items = ntiles * rblocks;  // < 2^31 (checked by the C ABI)
 
     if (blockIdx.x == 0) {
         // zero the outputs of unroutable pairs (the tail of order)
         const int elem = a.y_dtype == IQK_F32 ? 4 : 2;
-        const int row_words = (int)(out * elem / 4);
+        const int row_words = out * elem / 4;
         for (int q = ntiles; q < a.pairs; ++q) {
             int32_t *yr = reinterpret_cast<int32_t *>(static_cast<char *>(a.y) +
                                                       (int64_t)order[q] * out * elem);
@@ -532,69 +568,61 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     }
     __syncthreads();
     auto tile_of = [&](int t) -> TileRef { return cached ? tcache[t - t0] : load_tile(t); };
-    const int total_rounds = (i1 - i0) * cpw;
-    const RowBytes rbs = row_bytes(MEMBER, n);
+    const int n_items = i1 - i0;
 
     if (wid == kConsumers) {
         // ================= producer warp: TMA / bulk copies into the ring
-        int o = 0, r = 0, ti = i0 / rblocks, rb = i0 % rblocks;
+        int ti = i0 / rblocks, rb = i0 % rblocks;
         int issued = 0, sissued = 0;
         bool ok = true;
-        for (int j = 0; j < total_rounds && ok; ++j) {
-            const int slot = j % kStages;
+        // this lane's scale stream (lanes 1 .. kCount-1): bytes per row, slot offset
+        const int si = lane >= 1 && lane < SS::kCount ? lane : 0;
+        const int s_rowb = si ? SS::b(si) : 0, s_off = si ? SS::off(si) : 0;
+        for (int o = 0; o < n_items && ok; ++o) {
             const TileRef T = tile_of(ti);
-            const int64_t r0 = (int64_t)rb * kItemRows;
-            const int rows_valid = (int)min((int64_t)kItemRows, out - r0);
-            if (r == 0) {
-                // the item's scale streams (all rows, all of k) into scale slot o % 2
-                const int ss = o & 1;
-                if (o >= 2 && !mbar_wait(&sempty[ss], ((o >> 1) & 1) ^ 1)) {
-                    ok = false;
-                    break;
-                }
-                uint32_t sbytes = 0;
-                for (int si = 1; si < rbs.count; ++si) sbytes += (uint32_t)(rows_valid * rbs.b[si]);
-                if (lane == 0) mbar_arrive_expect_tx(&sfull[ss], sbytes);
-                __syncwarp();
-                if (lane >= 1 && lane < rbs.count) {
-                    const int si = lane;
-                    int off = 0;
-                    for (int q = 1; q < si; ++q) off += (int)(kItemRows * rbs.b[q]);
-                    bulk_load(sslots + ss * SSB + off,
-                              static_cast<const char *>(a.s[si]) + ((int64_t)T.e * out + r0) * rbs.b[si],
-                              (uint32_t)(rows_valid * rbs.b[si]), &sfull[ss]);
-                }
-                sissued = o + 1;
-            }
-            if (j >= kStages && !mbar_wait(&empty[slot], ((j / kStages) & 1) ^ 1)) {
+            const int r0 = rb * kItemRows;
+            const int rows_valid = min(kItemRows, out - r0);
+            // the item's scale streams (all rows, all of k) into scale slot o % 2
+            const int ss = o & 1;
+            if (o >= 2 && !mbar_wait(&sempty[ss], ((o >> 1) & 1) ^ 1)) {
                 ok = false;
                 break;
             }
-            char *st = stages + slot * STB;
-            const uint32_t bytes = (uint32_t)(G::kWBytes + G::kXBlock);
-            if (lane == 0) mbar_arrive_expect_tx(&full[slot], bytes);
+            if (lane == 0) mbar_arrive_expect_tx(&sfull[ss], (uint32_t)(rows_valid * (SS::kSlot / kItemRows)));
             __syncwarp();
-            if (lane < kConsumers) {
-                // weights: one 16-row x kRowChunk-byte box per compute warp
-                tma_load_2d(st + lane * G::kWBox, &qs_map, r * G::kRowChunk,
-                            (int)((int64_t)T.e * out + r0 + 16 * lane), &full[slot]);
-            } else if (lane == kConsumers) {
-                // activation digit planes (+ IQ1 block sums) of this round's k range
-                char *xs = st + G::kWBytes;
-                const char *xb = xbuf + T.tok0 * xrow;
-                bulk_load(xs, xb + (int64_t)r * G::kXPlanes, G::kXPlanes, &full[slot]);
-                if (G::kXSums)
-                    bulk_load(xs + G::kXPlanes, xb + 3 * (int64_t)n + (int64_t)r * G::kXSums,
-                              G::kXSums, &full[slot]);
-            }
-            issued = j + 1;
-            if (++r == cpw) {
-                r = 0;
-                ++o;
-                if (++rb == rblocks) {
-                    rb = 0;
-                    ++ti;
+            if (si)
+                bulk_load(sslots + ss * SSB + s_off,
+                          static_cast<const char *>(a.s[si]) + ((int64_t)T.e * out + r0) * s_rowb,
+                          (uint32_t)(rows_valid * s_rowb), &sfull[ss]);
+            sissued = o + 1;
+            const int wrow = T.e * out + r0 + 16 * lane;
+            const char *xb = xbuf + T.tok0 * xrow;
+            for (int r = 0; r < CPW; ++r) {
+                const int j = o * CPW + r;
+                const int slot = j % kStages;
+                if (j >= kStages && !mbar_wait(&empty[slot], ((j / kStages) & 1) ^ 1)) {
+                    ok = false;
+                    break;
                 }
+                char *st = stages + slot * STB;
+                if (lane == 0) mbar_arrive_expect_tx(&full[slot], (uint32_t)(G::kWBytes + G::kXBlock));
+                __syncwarp();
+                if (lane < kConsumers) {
+                    // weights: one 16-row x kRowChunk-byte box per compute warp
+                    tma_load_2d(st + lane * G::kWBox, &qs_map, r * G::kRowChunk, wrow, &full[slot]);
+                } else if (lane == kConsumers) {
+                    // activation digit planes (+ IQ1 block sums) of this round's k range
+                    char *xs = st + G::kWBytes;
+                    bulk_load(xs, xb + (int64_t)r * G::kXPlanes, G::kXPlanes, &full[slot]);
+                    if (G::kXSums)
+                        bulk_load(xs + G::kXPlanes, xb + 3 * (int64_t)N + (int64_t)r * G::kXSums,
+                                  G::kXSums, &full[slot]);
+                }
+                issued = j + 1;
+            }
+            if (++rb == rblocks) {
+                rb = 0;
+                ++ti;
             }
         }
         if (!ok && lane == 0) {
@@ -614,8 +642,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     // ===================== compute warps
     const int g = lane >> 2, tig = lane & 3;
     const int rt = wid;  // this warp's 16-row tile of the item
-    char *meta = metas + wid * G::kMetaBytes;
-    const uint32_t meta_u = smem_u32(meta);
+    const uint32_t meta_u = smem_u32(metas + wid * G::kMetaBytes);
     const int side = tig >> 1;             // which 32-weight group of an MMA pair
     int bplane;                            // activation plane of B column g (or -1)
     if (MEMBER == IQK_IQ2_K) bplane = g < 3 ? g : -1;
@@ -627,75 +654,84 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     // this lane's metadata entry within a pair: [pair][row pair g][side or word]
     const uint32_t moff = MEMBER == IQK_IQ2_K ? (g * 4 + tig) * 16 : (g * 2 + side) * 16;
     const uint32_t zero_u = smem_u32(zeros);
+    const uint32_t m16 = a.one << 16, m30 = a.one << 30;  // mulhi: >> 16, >> 2
+    // metadata lanes: (mg, mq) owns row pair (mg, mg + 8) and 128 weights a round
+    const int mg = lane & 7, mq = lane >> 3;
+    const int mra = 16 * rt + mg;  // item-local row (and mra + 8)
+    // IQ2_KS group bits of (mg, mq) sit at bit msh of the sch / sex bytes
+    const uint32_t msh = (uint32_t)(mq & 1) * 4u;
+    const uint32_t hmask = 0xFu << msh;
+    const uint32_t hmul = 0x02040810u >> msh;                 // bit msh+u -> bit 8u+4
+    const uint32_t amul = msh ? 0x01020408u : 0x10204080u;    // bit msh+u -> bit 8u+7
+    const uint32_t a44 = a.one * 0x88000000u;                 // mulhi: t>>1 | t>>5
 
-    int32_t tot[4] = {0, 0, 0, 0};
-    int32_t acc1[4] = {0, 0, 0, 0}, acc2[4] = {0, 0, 0, 0};  // IQ2_K super-block sums
-    double dacc[2] = {0.0, 0.0};                              // IQ2_K: rows g, g+8
-
-    int o = 0, r = 0, ti = i0 / rblocks, rb = i0 % rblocks;
-    for (int j = 0; j < total_rounds; ++j) {
-        const int slot = j % kStages;
-        const bool ok = mbar_wait(&full[slot], (j / kStages) & 1);
-        if (!ok || *(volatile int *)abort_flag) {
-            if (lane == 0 && !ok) {
+    int ti = i0 / rblocks, rb = i0 % rblocks;
+    for (int o = 0; o < n_items; ++o) {
+        const TileRef T = tile_of(ti);
+        const int r0 = rb * kItemRows;
+        const bool live = 16 * rt < out - r0;  // this warp's row tile exists
+        const char *sd = sslots + (o & 1) * SSB;
+        // the item's scale streams
+        if (!mbar_wait(&sfull[o & 1], (o >> 1) & 1)) {
+            if (lane == 0) {
                 atomicOr(a.err, IQK_DEVERR_TIMEOUT);
                 atomicExch(abort_flag, 1);
             }
             break;
         }
-        const TileRef T = tile_of(ti);
-        const int64_t r0 = (int64_t)rb * kItemRows;
-        if (r == 0) {
-            tot[0] = tot[1] = tot[2] = tot[3] = 0;
-            dacc[0] = dacc[1] = 0.0;
-            // the item's scale streams
-            if (!mbar_wait(&sfull[o & 1], (o >> 1) & 1)) {
-                if (lane == 0) {
-                    atomicOr(a.err, IQK_DEVERR_TIMEOUT);
-                    atomicExch(abort_flag, 1);
-                }
+        if (*(volatile int *)abort_flag) break;
+        int32_t tot[4] = {0, 0, 0, 0};
+        int32_t acc1[4] = {0, 0, 0, 0}, acc2[4] = {0, 0, 0, 0};  // IQ2_K super-block sums
+        double dacc[2] = {0.0, 0.0};                              // IQ2_K: rows g, g+8
+        bool ok = true;
+#pragma unroll 1
+        for (int r = 0; r < CPW; ++r) {
+            const int j = o * CPW + r;
+            const int slot = j % kStages;
+            if (!mbar_wait(&full[slot], (j / kStages) & 1)) {
+                ok = false;
                 break;
             }
-        }
-        const bool live = 16 * rt < out - r0;  // this warp's row tile exists
-        const char *st = stages + slot * STB;
-        const char *sd = sslots + (o & 1) * SSB;
-        const int c = r;  // 512-weight chunk of this round
-        if (live) {
-            // ---- group metadata for this warp's 16 rows x 512 weights.
-            // Lane (mg, mq) owns row pair (mg, mg + 8) and 128 weights.
-            {
-                const int mg = lane & 7, mq = lane >> 3;
-                const int ra = 16 * rt + mg, rb2 = ra + 8;  // item-local rows
+            const char *st = stages + slot * STB;
+            if (live) {
+                // ---- group metadata for this warp's 16 rows x 512 weights.
                 if (MEMBER == IQK_IQ2_KS) {
-                    const int s0 = c * 16 + mq * 4;  // first of 4 groups (2 pairs)
+                    // Four groups of rows mra and mra + 8 at once, one byte per
+                    // group: scale index (low nibble | high bit << 4) and the
+                    // alphabet mask (0x44 when the group uses the second one).
+                    const int s0 = r * 16 + mq * 4;  // first of 4 groups (2 pairs)
                     const uint8_t *scl = reinterpret_cast<const uint8_t *>(sd);
-                    const uint8_t *sch = scl + kItemRows * (n / 64);
-                    const uint8_t *sex = sch + kItemRows * (n / 256);
-                    const uint32_t la = lds_u16(scl + ra * (n / 64) + (s0 >> 1));
-                    const uint32_t lb = lds_u16(scl + rb2 * (n / 64) + (s0 >> 1));
-                    const uint32_t ha = (uint32_t)sch[ra * (n / 256) + (s0 >> 3)] >> (s0 & 7);
-                    const uint32_t hb = (uint32_t)sch[rb2 * (n / 256) + (s0 >> 3)] >> (s0 & 7);
-                    const uint32_t xa = (uint32_t)sex[ra * (n / 256) + (s0 >> 3)] >> (s0 & 7);
-                    const uint32_t xb = (uint32_t)sex[rb2 * (n / 256) + (s0 >> 3)] >> (s0 & 7);
+                    const uint8_t *sch = scl + SS::off(2) + (s0 >> 3);
+                    const uint8_t *sex = scl + SS::off(3) + (s0 >> 3);
+                    scl += s0 >> 1;
+                    const uint32_t la = lds_u16(scl + mra * (N / 64));
+                    const uint32_t lb = lds_u16(scl + (mra + 8) * (N / 64));
+                    const uint32_t ha = sch[mra * (N / 256)], hb = sch[(mra + 8) * (N / 256)];
+                    const uint32_t xa = sex[mra * (N / 256)], xb = sex[(mra + 8) * (N / 256)];
+                    const uint32_t pa = prmt(la, 0u, 0x4140u), pb = prmt(lb, 0u, 0x4140u);
+                    const uint32_t va = ((pa | (pa << 4)) & 0x0F0F0F0Fu) | (((ha & hmask) * hmul) & 0x10101010u);
+                    const uint32_t vb = ((pb | (pb << 4)) & 0x0F0F0F0Fu) | (((hb & hmask) * hmul) & 0x10101010u);
+                    const uint32_t aa = mulhi(((xa & hmask) * amul) & 0x80808080u, a44);
+                    const uint32_t ab = mulhi(((xb & hmask) * amul) & 0x80808080u, a44);
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        const int ia = (int)(((la >> (4 * u)) & 15u) | (((ha >> u) & 1u) << 4)) - 16;
-                        const int ib = (int)(((lb >> (4 * u)) & 15u) | (((hb >> u) & 1u) << 4)) - 16;
-                        const uint32_t ama = ((xa >> u) & 1u) * 0x44444444u;
-                        const uint32_t amb = ((xb >> u) & 1u) * 0x44444444u;
+                        const int ia = (int)prmt(va, 0u, 0x4440u + u) - 16;
+                        const int ib = (int)prmt(vb, 0u, 0x4440u + u) - 16;
+                        const uint32_t ama = prmt(aa, 0u, 0x1111u * u);
+                        const uint32_t amb = prmt(ab, 0u, 0x1111u * u);
                         const int pr = mq * 2 + (u >> 1), sd2 = u & 1;  // pair, side
-                        st_s128(meta_u + pr * 256 + (mg * 2 + sd2) * 16, (uint32_t)ama, (uint32_t)amb,
-                                (uint32_t)ia, (uint32_t)ib);
+                        st_s128(meta_u + pr * 256 + (mg * 2 + sd2) * 16, ama, amb, (uint32_t)ia,
+                                (uint32_t)ib);
                     }
                 } else if (MEMBER == IQK_IQ2_K) {
-                    const int b0 = c * 32 + mq * 8;  // first of 8 sub-blocks (2 pairs)
+                    const int b0 = r * 32 + mq * 8;  // first of 8 sub-blocks (2 pairs)
                     const uint8_t *scl = reinterpret_cast<const uint8_t *>(sd);
-                    const uint8_t *sex = scl + kItemRows * (n / 32);
-                    const uint32_t la = lds_u32(scl + ra * (n / 32) + (b0 >> 1));
-                    const uint32_t lb = lds_u32(scl + rb2 * (n / 32) + (b0 >> 1));
-                    const uint32_t xa = sex[ra * (n / 128) + (b0 >> 3)];
-                    const uint32_t xb = sex[rb2 * (n / 128) + (b0 >> 3)];
+                    const uint8_t *sex = scl + SS::off(2) + (b0 >> 3);
+                    scl += b0 >> 1;
+                    const uint32_t la = lds_u32(scl + mra * (N / 32));
+                    const uint32_t lb = lds_u32(scl + (mra + 8) * (N / 32));
+                    const uint32_t xa = sex[mra * (N / 128)];
+                    const uint32_t xb = sex[(mra + 8) * (N / 128)];
 #pragma unroll
                     for (int u = 0; u < 8; ++u) {
                         const uint2 ta = ktab[((xa >> u) & 1u) * 16 + ((la >> (4 * u)) & 15u)];
@@ -704,11 +740,11 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                         st_s128(meta_u + pr * 512 + (mg * 4 + wd) * 16, ta.x, tb.x, ta.y, tb.y);
                     }
                 } else {
-                    const int s0 = c * 16 + mq * 4;  // first of 4 blocks (2 pairs)
-                    const uint16_t *qh = reinterpret_cast<const uint16_t *>(sd);
+                    const int s0 = r * 16 + mq * 4;  // first of 4 blocks (2 pairs)
+                    const uint16_t *qh = reinterpret_cast<const uint16_t *>(sd) + s0;
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        const uint32_t ha = qh[ra * (n / 32) + s0 + u], hb = qh[rb2 * (n / 32) + s0 + u];
+                        const uint32_t ha = qh[mra * (N / 32) + u], hb = qh[(mra + 8) * (N / 32) + u];
                         const int ma = 2 * (int)((ha >> 12) & 7u) + 1, mb = 2 * (int)((hb >> 12) & 7u) + 1;
                         const int pr = mq * 2 + (u >> 1), sd2 = u & 1;
                         st_s128(meta_u + pr * 256 + (mg * 2 + sd2) * 16, ha | (hb << 16),
@@ -716,132 +752,142 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                                 (uint32_t)(ma | (mb << 16)));
                     }
                 }
-            }
-            __syncwarp();
+                __syncwarp();
 
-            // ---- 8 MMA pairs, all shared-memory addresses 32-bit and the
-            // per-pair offsets compile-time immediates.
-            const uint32_t wb_u = smem_u32(st + wid * G::kWBox);
-            const uint32_t xs_u = smem_u32(st + G::kWBytes);
-            // B: live lanes read their plane's 16 bytes; the others a zero block
-            const uint32_t xl_u = bplane >= 0 ? xs_u + tig * 48 + bplane * 16 : zero_u;
-            const uint32_t mrow = meta_u + moff;
-            const uint32_t wl = wb_u | woff;  // box is 1024-aligned, woff < 1024
+                // ---- 8 MMA pairs, all shared-memory addresses 32-bit and the
+                // per-pair offsets compile-time immediates.
+                const uint32_t wb_u = smem_u32(st + wid * G::kWBox);
+                const uint32_t xs_u = smem_u32(st + G::kWBytes);
+                // B: live lanes read their plane's 16 bytes; the others a zero block
+                const uint32_t xl_u = bplane >= 0 ? xs_u + tig * 48 + bplane * 16 : zero_u;
+                const uint32_t mrow = meta_u + moff;
+                const uint32_t wl = wb_u | woff;  // box is 1024-aligned, woff < 1024
 #pragma unroll
-            for (int pr = 0; pr < kPairsPerRound; ++pr) {
-                const uint4 bv = ld_s128(xl_u + pr * 192);
-                uint32_t A[4];
-                if (MEMBER == IQK_IQ2_KS) {
-                    const uint32_t wo = wl ^ (uint32_t)(pr << 4);
-                    const uint32_t wg = ld_s32(wo);
-                    const uint32_t wg8 = ld_s32(wo + 1024);
-                    const uint4 m = ld_s128(mrow + pr * 256);
-                    const uint32_t s0g = (wg & 0x33333333u) | m.x;
-                    const uint32_t s1g = ((wg >> 2) & 0x33333333u) | m.x;
-                    const uint32_t s0h = (wg8 & 0x33333333u) | m.y;
-                    const uint32_t s1h = ((wg8 >> 2) & 0x33333333u) | m.y;
-                    int32_t d[4];
-                    A[0] = prmt(kIq2Tab0, kIq2Tab1, s0g);
-                    A[1] = prmt(kIq2Tab0, kIq2Tab1, s0h);
-                    A[2] = prmt(kIq2Tab0, kIq2Tab1, s1g);
-                    A[3] = prmt(kIq2Tab0, kIq2Tab1, s1h);
-                    mma_s8(d, A, bv.x, bv.y);
-                    A[0] = prmt(kIq2Tab0, kIq2Tab1, s0g >> 16);
-                    A[1] = prmt(kIq2Tab0, kIq2Tab1, s0h >> 16);
-                    A[2] = prmt(kIq2Tab0, kIq2Tab1, s1g >> 16);
-                    A[3] = prmt(kIq2Tab0, kIq2Tab1, s1h >> 16);
-                    mma_s8_acc(d, A, bv.z, bv.w);
-                    tot[0] += (int)m.z * d[0];
-                    tot[1] += (int)m.z * d[1];
-                    tot[2] += (int)m.w * d[2];
-                    tot[3] += (int)m.w * d[3];
-                } else if (MEMBER == IQK_IQ2_K) {
-                    const uint32_t wo = wl ^ (uint32_t)(pr << 4);
-                    const uint32_t wg = ld_s32(wo);
-                    const uint32_t wg8 = ld_s32(wo + 1024);
-                    const uint4 m = ld_s128(mrow + pr * 512);
-                    const uint32_t s0g = wg & 0x33333333u, s1g = (wg >> 2) & 0x33333333u;
-                    const uint32_t s0h = wg8 & 0x33333333u, s1h = (wg8 >> 2) & 0x33333333u;
-                    A[0] = prmt(m.x, 0u, s0g);
-                    A[1] = prmt(m.y, 0u, s0h);
-                    A[2] = prmt(m.x, 0u, s1g);
-                    A[3] = prmt(m.y, 0u, s1h);
-                    mma_s8_acc(acc1, A, bv.x, bv.y);
-                    A[0] = prmt(m.x, 0u, s0g >> 16);
-                    A[1] = prmt(m.y, 0u, s0h >> 16);
-                    A[2] = prmt(m.x, 0u, s1g >> 16);
-                    A[3] = prmt(m.y, 0u, s1h >> 16);
-                    mma_s8_acc(acc1, A, bv.z, bv.w);
-                    A[0] = prmt(m.z, 0u, s0g);
-                    A[1] = prmt(m.w, 0u, s0h);
-                    A[2] = prmt(m.z, 0u, s1g);
-                    A[3] = prmt(m.w, 0u, s1h);
-                    mma_s8_acc(acc2, A, bv.x, bv.y);
-                    A[0] = prmt(m.z, 0u, s0g >> 16);
-                    A[1] = prmt(m.w, 0u, s0h >> 16);
-                    A[2] = prmt(m.z, 0u, s1g >> 16);
-                    A[3] = prmt(m.w, 0u, s1h >> 16);
-                    mma_s8_acc(acc2, A, bv.z, bv.w);
-                    if ((pr & 3) == 3) {
-                        // end of a 256-weight super-block: fold in its fp16 scale.
-                        // Lane tig 0 holds planes 0, 1 (cols 0, 1), tig 1 plane 2.
-                        const int sbi = (c * kChunkK + pr * 64) >> 8;
-                        const uint16_t *dvp = reinterpret_cast<const uint16_t *>(
-                            sd + kItemRows * (n / 32) + kItemRows * (n / 128));
-                        const int32_t u0 = acc1[0] + 4 * acc2[0], u1 = acc1[1] + 4 * acc2[1];
-                        const int32_t u2 = acc1[2] + 4 * acc2[2], u3 = acc1[3] + 4 * acc2[3];
-                        const int32_t p2g = __shfl_down_sync(0xffffffffu, u0, 1);
-                        const int32_t p2h = __shfl_down_sync(0xffffffffu, u2, 1);
-                        if (tig == 0) {
-                            const int ra = 16 * rt + g;
-                            const double Tg = (double)u0 * 65536.0 + (double)u1 * 256.0 + (double)p2g;
-                            const double Th = (double)u2 * 65536.0 + (double)u3 * 256.0 + (double)p2h;
-                            dacc[0] += (double)half_bits_to_float(dvp[ra * (n / 256) + sbi]) * Tg;
-                            dacc[1] += (double)half_bits_to_float(dvp[(ra + 8) * (n / 256) + sbi]) * Th;
+                for (int pr = 0; pr < kPairsPerRound; ++pr) {
+                    const uint4 bv = ld_s128(xl_u + pr * 192);
+                    uint32_t A[4];
+                    if (MEMBER == IQK_IQ2_KS) {
+                        const uint32_t wo = wl ^ (uint32_t)(pr << 4);
+                        const uint32_t wg = ld_s32(wo);
+                        const uint32_t wg8 = ld_s32(wo + 1024);
+                        const uint4 m = ld_s128(mrow + pr * 256);
+                        const uint32_t s0g = (wg & 0x33333333u) | m.x;
+                        const uint32_t s1g = (shr2(wg, m30) & 0x33333333u) | m.x;
+                        const uint32_t s0h = (wg8 & 0x33333333u) | m.y;
+                        const uint32_t s1h = (shr2(wg8, m30) & 0x33333333u) | m.y;
+                        int32_t d[4];
+                        A[0] = prmt(kIq2Tab0, kIq2Tab1, s0g);
+                        A[1] = prmt(kIq2Tab0, kIq2Tab1, s0h);
+                        A[2] = prmt(kIq2Tab0, kIq2Tab1, s1g);
+                        A[3] = prmt(kIq2Tab0, kIq2Tab1, s1h);
+                        mma_s8(d, A, bv.x, bv.y);
+                        A[0] = prmt(kIq2Tab0, kIq2Tab1, shr16(s0g, m16));
+                        A[1] = prmt(kIq2Tab0, kIq2Tab1, shr16(s0h, m16));
+                        A[2] = prmt(kIq2Tab0, kIq2Tab1, shr16(s1g, m16));
+                        A[3] = prmt(kIq2Tab0, kIq2Tab1, shr16(s1h, m16));
+                        mma_s8_acc(d, A, bv.z, bv.w);
+                        tot[0] += (int)m.z * d[0];
+                        tot[1] += (int)m.z * d[1];
+                        tot[2] += (int)m.w * d[2];
+                        tot[3] += (int)m.w * d[3];
+                    } else if (MEMBER == IQK_IQ2_K) {
+                        const uint32_t wo = wl ^ (uint32_t)(pr << 4);
+                        const uint32_t wg = ld_s32(wo);
+                        const uint32_t wg8 = ld_s32(wo + 1024);
+                        const uint4 m = ld_s128(mrow + pr * 512);
+                        const uint32_t s0g = wg & 0x33333333u, s1g = shr2(wg, m30) & 0x33333333u;
+                        const uint32_t s0h = wg8 & 0x33333333u, s1h = shr2(wg8, m30) & 0x33333333u;
+                        const uint32_t s0gh = shr16(s0g, m16), s1gh = shr16(s1g, m16);
+                        const uint32_t s0hh = shr16(s0h, m16), s1hh = shr16(s1h, m16);
+                        A[0] = prmt(m.x, 0u, s0g);
+                        A[1] = prmt(m.y, 0u, s0h);
+                        A[2] = prmt(m.x, 0u, s1g);
+                        A[3] = prmt(m.y, 0u, s1h);
+                        mma_s8_acc(acc1, A, bv.x, bv.y);
+                        A[0] = prmt(m.x, 0u, s0gh);
+                        A[1] = prmt(m.y, 0u, s0hh);
+                        A[2] = prmt(m.x, 0u, s1gh);
+                        A[3] = prmt(m.y, 0u, s1hh);
+                        mma_s8_acc(acc1, A, bv.z, bv.w);
+                        A[0] = prmt(m.z, 0u, s0g);
+                        A[1] = prmt(m.w, 0u, s0h);
+                        A[2] = prmt(m.z, 0u, s1g);
+                        A[3] = prmt(m.w, 0u, s1h);
+                        mma_s8_acc(acc2, A, bv.x, bv.y);
+                        A[0] = prmt(m.z, 0u, s0gh);
+                        A[1] = prmt(m.w, 0u, s0hh);
+                        A[2] = prmt(m.z, 0u, s1gh);
+                        A[3] = prmt(m.w, 0u, s1hh);
+                        mma_s8_acc(acc2, A, bv.z, bv.w);
+                        if ((pr & 3) == 3) {
+                            // end of a 256-weight super-block: fold in its fp16 scale.
+                            // Lane tig 0 holds planes 0, 1 (cols 0, 1), tig 1 plane 2.
+                            const int sbi = (r * kChunkK + pr * 64) >> 8;
+                            const uint16_t *dvp = reinterpret_cast<const uint16_t *>(sd + SS::off(3));
+                            const int32_t u0 = acc1[0] + 4 * acc2[0], u1 = acc1[1] + 4 * acc2[1];
+                            const int32_t u2 = acc1[2] + 4 * acc2[2], u3 = acc1[3] + 4 * acc2[3];
+                            const int32_t p2g = __shfl_down_sync(0xffffffffu, u0, 1);
+                            const int32_t p2h = __shfl_down_sync(0xffffffffu, u2, 1);
+                            if (tig == 0) {
+                                const int ra = 16 * rt + g;
+                                const double Tg = (double)u0 * 65536.0 + (double)u1 * 256.0 + (double)p2g;
+                                const double Th = (double)u2 * 65536.0 + (double)u3 * 256.0 + (double)p2h;
+                                dacc[0] += (double)half_bits_to_float(dvp[ra * (N / 256) + sbi]) * Tg;
+                                dacc[1] += (double)half_bits_to_float(dvp[(ra + 8) * (N / 256) + sbi]) * Th;
+                            }
+                            acc1[0] = acc1[1] = acc1[2] = acc1[3] = 0;
+                            acc2[0] = acc2[1] = acc2[2] = acc2[3] = 0;
                         }
-                        acc1[0] = acc1[1] = acc1[2] = acc1[3] = 0;
-                        acc2[0] = acc2[1] = acc2[2] = acc2[3] = 0;
+                    } else {
+                        // IQ1_S_R4: this lane covers sub-groups 2h, 2h+1 of block 2*pr+side
+                        const int hsel = tig & 1;
+                        const uint32_t wo = (wl ^ (uint32_t)((pr >> 1) << 4)) + (uint32_t)((pr & 1) << 3);
+                        const uint32_t qg = ld_s32(wo);
+                        const uint32_t qg8 = ld_s32(wo + 512);
+                        const uint4 m = ld_s128(mrow + pr * 256);
+                        const uint32_t hg = m.x & 0xffffu, hh = m.x >> 16;
+                        const uint32_t bg = qg >> (16 * hsel), bh = qg8 >> (16 * hsel);
+                        const uint32_t ga = grid[(bg & 0xffu) | (((hg >> (6 * hsel)) & 7u) << 8)];
+                        const uint32_t gb = grid[((bg >> 8) & 0xffu) | (((hg >> (6 * hsel + 3)) & 7u) << 8)];
+                        const uint32_t ha = grid[(bh & 0xffu) | (((hh >> (6 * hsel)) & 7u) << 8)];
+                        const uint32_t hb = grid[((bh >> 8) & 0xffu) | (((hh >> (6 * hsel + 3)) & 7u) << 8)];
+                        const uint32_t vg = ga | (gb << 16), vh = ha | (hb << 16);
+                        const uint32_t s0g = vg & 0x33333333u, s1g = shr2(vg, m30) & 0x33333333u;
+                        const uint32_t s0h = vh & 0x33333333u, s1h = shr2(vh, m30) & 0x33333333u;
+                        int32_t d[4];
+                        A[0] = prmt(kTernTab, 0u, s0g);
+                        A[1] = prmt(kTernTab, 0u, s0h);
+                        A[2] = prmt(kTernTab, 0u, s1g);
+                        A[3] = prmt(kTernTab, 0u, s1h);
+                        mma_s8(d, A, bv.x, bv.y);
+                        A[0] = prmt(kTernTab, 0u, shr16(s0g, m16));
+                        A[1] = prmt(kTernTab, 0u, shr16(s0h, m16));
+                        A[2] = prmt(kTernTab, 0u, shr16(s1g, m16));
+                        A[3] = prmt(kTernTab, 0u, shr16(s1h, m16));
+                        mma_s8_acc(d, A, bv.z, bv.w);
+                        // block sums of this lane's two C columns (block 2*pr+side,
+                        // planes 2*(tig&1) and +1; plane 3 reads the stored zero)
+                        const uint2 xsum = ld_s64(xs_u + G::kXPlanes + (pr * 2 + side) * 16 + hsel * 8);
+                        const int ma = (int)(m.w & 0xffffu), mb = (int)(m.w >> 16);
+                        tot[0] += ma * 8 * d[0] + (int)m.y * (int)xsum.x;
+                        tot[1] += ma * 8 * d[1] + (int)m.y * (int)xsum.y;
+                        tot[2] += mb * 8 * d[2] + (int)m.z * (int)xsum.x;
+                        tot[3] += mb * 8 * d[3] + (int)m.z * (int)xsum.y;
                     }
-                } else {
-                    // IQ1_S_R4: this lane covers sub-groups 2h, 2h+1 of block 2*pr+side
-                    const int hsel = tig & 1;
-                    const uint32_t wo = (wl ^ (uint32_t)((pr >> 1) << 4)) + (uint32_t)((pr & 1) << 3);
-                    const uint32_t qg = ld_s32(wo);
-                    const uint32_t qg8 = ld_s32(wo + 512);
-                    const uint4 m = ld_s128(mrow + pr * 256);
-                    const uint32_t hg = m.x & 0xffffu, hh = m.x >> 16;
-                    const uint32_t bg = qg >> (16 * hsel), bh = qg8 >> (16 * hsel);
-                    const uint32_t ga = grid[(bg & 0xffu) | (((hg >> (6 * hsel)) & 7u) << 8)];
-                    const uint32_t gb = grid[((bg >> 8) & 0xffu) | (((hg >> (6 * hsel + 3)) & 7u) << 8)];
-                    const uint32_t ha = grid[(bh & 0xffu) | (((hh >> (6 * hsel)) & 7u) << 8)];
-                    const uint32_t hb = grid[((bh >> 8) & 0xffu) | (((hh >> (6 * hsel + 3)) & 7u) << 8)];
-                    const uint32_t vg = ga | (gb << 16), vh = ha | (hb << 16);
-                    const uint32_t s0g = vg & 0x33333333u, s1g = (vg >> 2) & 0x33333333u;
-                    const uint32_t s0h = vh & 0x33333333u, s1h = (vh >> 2) & 0x33333333u;
-                    int32_t d[4];
-                    A[0] = prmt(kTernTab, 0u, s0g);
-                    A[1] = prmt(kTernTab, 0u, s0h);
-                    A[2] = prmt(kTernTab, 0u, s1g);
-                    A[3] = prmt(kTernTab, 0u, s1h);
-                    mma_s8(d, A, bv.x, bv.y);
-                    A[0] = prmt(kTernTab, 0u, s0g >> 16);
-                    A[1] = prmt(kTernTab, 0u, s0h >> 16);
-                    A[2] = prmt(kTernTab, 0u, s1g >> 16);
-                    A[3] = prmt(kTernTab, 0u, s1h >> 16);
-                    mma_s8_acc(d, A, bv.z, bv.w);
-                    // block sums of this lane's two C columns (block 2*pr+side,
-                    // planes 2*(tig&1) and +1; plane 3 reads the stored zero)
-                    const uint2 xsum = ld_s64(xs_u + G::kXPlanes + (pr * 2 + side) * 16 + hsel * 8);
-                    const int ma = (int)(m.w & 0xffffu), mb = (int)(m.w >> 16);
-                    tot[0] += ma * 8 * d[0] + (int)m.y * (int)xsum.x;
-                    tot[1] += ma * 8 * d[1] + (int)m.y * (int)xsum.y;
-                    tot[2] += mb * 8 * d[2] + (int)m.z * (int)xsum.x;
-                    tot[3] += mb * 8 * d[3] + (int)m.z * (int)xsum.y;
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);  // this round's stage
+        }
+        if (!ok) {
+            if (lane == 0) {
+                atomicOr(a.err, IQK_DEVERR_TIMEOUT);
+                atomicExch(abort_flag, 1);
+            }
+            break;
         }
 
-        if (r == cpw - 1 && live) {
+        if (live) {
             // ---- item end: this warp holds the whole k range of its 16 rows.
             const int ra = 16 * rt + g;  // item-local row
             double yg, yg8;
@@ -857,21 +903,19 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                 const int32_t n2 = __shfl_down_sync(0xffffffffu, s4[2], 1);
                 const double Tg = (double)s4[0] * 65536.0 + (double)s4[1] * 256.0 + (double)n0;
                 const double Tg8 = (double)s4[2] * 65536.0 + (double)s4[3] * 256.0 + (double)n2;
-                const uint16_t *dvp = reinterpret_cast<const uint16_t *>(
-                    sd + (MEMBER == IQK_IQ2_KS ? kItemRows * (n / 64 + n / 256 + n / 256)
-                                               : kItemRows * (n / 16)));
+                const uint16_t *dvp = reinterpret_cast<const uint16_t *>(sd + SS::off(SS::kCount - 1));
                 yg = (double)half_bits_to_float(dvp[ra]) * Tg;
                 yg8 = (double)half_bits_to_float(dvp[ra + 8]) * Tg8;
             }
             if (tig == 0) {
                 const int S = T.sh0;
-                const int shift = -S - (MEMBER == IQK_IQ1_S_R4 ? 3 : 0);
                 float vg, vg8;
                 if (S == kScaleNonFinite) {
                     vg = vg8 = __int_as_float(0x7fc00000);
                 } else {
-                    vg = (float)ldexp(yg, shift);
-                    vg8 = (float)ldexp(yg8, shift);
+                    const double sc = pow2(-S - (MEMBER == IQK_IQ1_S_R4 ? 3 : 0));
+                    vg = (float)(yg * sc);
+                    vg8 = (float)(yg8 * sc);
                 }
                 const int64_t o0 = (int64_t)T.pair0 * out + r0 + ra;
                 const bool ok8 = r0 + ra + 8 < out;
@@ -891,20 +935,14 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
             }
         }
         __syncwarp();
-        if (lane == 0) {
-            mbar_arrive(&empty[slot]);                         // this round's stage
-            if (r == cpw - 1) mbar_arrive(&sempty[o & 1]);     // the item's scale slot
-        }
-        if (++r == cpw) {
-            r = 0;
-            ++o;
-            if (++rb == rblocks) {
-                rb = 0;
-                ++ti;
-            }
+        if (lane == 0) mbar_arrive(&sempty[o & 1]);  // the item's scale slot
+        if (++rb == rblocks) {
+            rb = 0;
+            ++ti;
         }
     }
 }
+
 
 // ------------------------------------------------------------------- host
 
@@ -929,9 +967,14 @@ GemvLayout gemv_layout(int member, int64_t n, int64_t x_rows, int64_t pairs) {
 }
 
 int gemv_smem_for(int member, int n) {
-    if (member == IQK_IQ2_KS) return gemv_smem_bytes<IQK_IQ2_KS>(n);
-    if (member == IQK_IQ2_K) return gemv_smem_bytes<IQK_IQ2_K>(n);
-    return gemv_smem_bytes<IQK_IQ1_S_R4>(n);
+    if (n == 2048) {
+        if (member == IQK_IQ2_KS) return gemv_smem_bytes<IQK_IQ2_KS, 2048>();
+        if (member == IQK_IQ2_K) return gemv_smem_bytes<IQK_IQ2_K, 2048>();
+        return gemv_smem_bytes<IQK_IQ1_S_R4, 2048>();
+    }
+    if (member == IQK_IQ2_KS) return gemv_smem_bytes<IQK_IQ2_KS, 4096>();
+    if (member == IQK_IQ2_K) return gemv_smem_bytes<IQK_IQ2_K, 4096>();
+    return gemv_smem_bytes<IQK_IQ1_S_R4, 4096>();
 }
 
 cudaError_t launch_gemv_prepare(const void *x, int x_dtype, int64_t x_rows, int n,
@@ -997,9 +1040,9 @@ cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_
     GemvArgs ga{};
     const RowBytes rb = row_bytes(member, n);
     for (int i = 0; i < rb.count; ++i) ga.s[i] = streams[i];
-    ga.out_features = out_features;
-    ga.n = n;
+    ga.out_features = (int)out_features;
     ga.pairs = (int)pairs;
+    ga.one = 1u;
     ga.L = L;
     ga.ws = static_cast<const char *>(ws);
     ga.err = reinterpret_cast<int32_t *>(const_cast<char *>(ga.ws) + L.hdr);
@@ -1017,16 +1060,22 @@ cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_
     const int64_t cap = (int64_t)num_sms * per_sm;
     int64_t blocks = max_items < cap ? max_items : cap;
     if (blocks < 1) blocks = 1;
-#define IQK_GEMV(M)                                                                          \
-    do {                                                                                     \
-        err = cudaFuncSetAttribute(gemv_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                   smem);                                                    \
-        if (err != cudaSuccess) return err;                                                  \
-        gemv_kernel<M><<<(unsigned)blocks, kThreads, smem, stream>>>(ga, map);               \
+#define IQK_GEMV(M, N)                                                                          \
+    do {                                                                                        \
+        err = cudaFuncSetAttribute(gemv_kernel<M, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                   smem);                                                       \
+        if (err != cudaSuccess) return err;                                                     \
+        gemv_kernel<M, N><<<(unsigned)blocks, kThreads, smem, stream>>>(ga, map);               \
     } while (0)
-    if (member == IQK_IQ2_KS) IQK_GEMV(IQK_IQ2_KS);
-    else if (member == IQK_IQ2_K) IQK_GEMV(IQK_IQ2_K);
-    else IQK_GEMV(IQK_IQ1_S_R4);
+    if (n == 2048) {
+        if (member == IQK_IQ2_KS) IQK_GEMV(IQK_IQ2_KS, 2048);
+        else if (member == IQK_IQ2_K) IQK_GEMV(IQK_IQ2_K, 2048);
+        else IQK_GEMV(IQK_IQ1_S_R4, 2048);
+    } else {
+        if (member == IQK_IQ2_KS) IQK_GEMV(IQK_IQ2_KS, 4096);
+        else if (member == IQK_IQ2_K) IQK_GEMV(IQK_IQ2_K, 4096);
+        else IQK_GEMV(IQK_IQ1_S_R4, 4096);
+    }
 #undef IQK_GEMV
     return cudaGetLastError();
 }
