@@ -33,13 +33,17 @@
 // round) plus the round's slice of activation planes, and the item's scale
 // streams arrive in one of two double-buffered scale slots. Per round each
 // warp expands its rows' group metadata (alphabet mask, integer scale) into
-// shared memory, then runs 8 MMA pairs of 64 weights. The operand build is
-// bound by the integer ALU pipe (byte permutes and logic ops, issued every
-// other cycle per scheduler), so right shifts go through mul.hi on the FMA
-// pipe and the metadata is expanded four groups at a time with byte-SIMD
-// multiplies. Items are split evenly over a persistent grid of three CTAs
-// per SM (two for IQ2_K).
+// shared memory, then runs 8 MMA pairs of 64 weights; the metadata of round
+// r+1 is built during round r (two buffers per warp) so its shared-memory
+// latency overlaps the MMA work. The operand build is bound by the integer
+// ALU pipe (byte permutes and logic ops, issued every other cycle per
+// scheduler), so the shift by two of each code word goes through mul.hi on
+// the FMA pipe and the metadata is expanded four groups at a time with
+// byte-SIMD multiplies. Items are split evenly over one persistent wave of
+// CTAs (as many per SM as shared memory and registers allow).
 #include <cuda.h>
+
+#include <atomic>
 
 #include "iqk_common.cuh"
 #include "iqk_gemv.cuh"
@@ -292,7 +296,7 @@ constexpr int kThreads = (kConsumers + 1) * 32;  // + one producer warp
 constexpr int kItemRows = 16 * kConsumers;    // 64 rows per CTA item
 constexpr int kChunkK = 512;                  // weights per row per round and warp
 constexpr int kPairsPerRound = kChunkK / 64;  // MMA pairs (64 weights per row) per round
-constexpr int kMaxTiles = 128;                // tile entries cached in shared memory
+constexpr int kMaxTiles = 64;                 // tile entries cached in shared memory
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // bounded mbarrier waits (2 s)
 
 // One work tile is one pair (expert, activation row). A warp's 16 rows x 64
@@ -343,7 +347,7 @@ template <int MEMBER, int N> __host__ __device__ constexpr int gemv_smem_bytes()
     using G = Geo<MEMBER>;
     constexpr int kStages = G::kStages;
     return 1024 /* alignment slack */ + kStages * stage_bytes<MEMBER>() +
-           2 * sslot_bytes<MEMBER, N>() + kConsumers * G::kMetaBytes +
+           2 * sslot_bytes<MEMBER, N>() + 2 * kConsumers * G::kMetaBytes +
            kMaxTiles * (int)sizeof(TileRef) + (MEMBER == IQK_IQ1_S_R4 ? 4096 : 0) +
            (MEMBER == IQK_IQ2_K ? 256 : 0) + 2 * kStages * 8 + 4 * 8 + 16 +
            kPairsPerRound * 192;
@@ -393,24 +397,14 @@ __device__ __forceinline__ void st_s128(uint32_t a, uint32_t x, uint32_t y, uint
                  : "memory");
 }
 
-// Right shift by a power-of-two multiply-high, x >> s == mulhi(x, 2^(32-s)).
-// The operand-build loop is bound by the integer ALU pipe (byte permutes,
-// logic ops); a multiply-high issues on the FMA pipe instead. The multiplier
-// is derived from a kernel argument so that it stays a multiply.
+// The operand build is bound by the integer ALU pipe (byte permutes, logic
+// ops). x >> 2 of a code word goes through a multiply-high on the FMA pipe
+// instead, x >> 2 == mulhi(x, 2^30), with the multiplier taken from a kernel
+// argument so it stays a multiply; measured on B200 this beats both the plain
+// shift and moving the >> 16 selector shifts as well.
 __device__ __forceinline__ uint32_t mulhi(uint32_t x, uint32_t m) { return __umulhi(x, m); }
-#ifndef IQK_SHR16_FMA
-#define IQK_SHR16_FMA 1
-#endif
-#ifndef IQK_SHR2_FMA
-#define IQK_SHR2_FMA 1
-#endif
-// x >> 16 and x >> 2 of the operand build (m16 = 2^16, m30 = 2^30).
-__device__ __forceinline__ uint32_t shr16(uint32_t x, uint32_t m16) {
-    return IQK_SHR16_FMA ? shr16(x, m16) : x >> 16;
-}
-__device__ __forceinline__ uint32_t shr2(uint32_t x, uint32_t m30) {
-    return IQK_SHR2_FMA ? shr2(x, m30) : x >> 2;
-}
+__device__ __forceinline__ uint32_t shr2(uint32_t x, uint32_t m30) { return mulhi(x, m30); }
+__device__ __forceinline__ uint32_t shr16(uint32_t x) { return x >> 16; }
 
 // d += A * B (int8 m16n8k32, accumulating in place).
 __device__ __forceinline__ void mma_s8_acc(int32_t d[4], const uint32_t a[4], uint32_t b0,
@@ -490,7 +484,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     char *stages = smem;
     char *sslots = stages + kStages * STB;  // two item scale slots
     char *metas = sslots + 2 * SSB;
-    TileRef *tcache = reinterpret_cast<TileRef *>(metas + kConsumers * G::kMetaBytes);
+    TileRef *tcache = reinterpret_cast<TileRef *>(metas + 2 * kConsumers * G::kMetaBytes);
     char *tail = reinterpret_cast<char *>(tcache + kMaxTiles);
     uint16_t *grid = reinterpret_cast<uint16_t *>(tail);   // IQ1_S_R4
     uint2 *ktab = reinterpret_cast<uint2 *>(tail);         // IQ2_K: (alpha, idx) -> tables
@@ -642,7 +636,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     // ===================== compute warps
     const int g = lane >> 2, tig = lane & 3;
     const int rt = wid;  // this warp's 16-row tile of the item
-    const uint32_t meta_u = smem_u32(metas + wid * G::kMetaBytes);
+    const uint32_t meta_u = smem_u32(metas + wid * 2 * G::kMetaBytes);  // two round buffers
     const int side = tig >> 1;             // which 32-weight group of an MMA pair
     int bplane;                            // activation plane of B column g (or -1)
     if (MEMBER == IQK_IQ2_K) bplane = g < 3 ? g : -1;
@@ -654,7 +648,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     // this lane's metadata entry within a pair: [pair][row pair g][side or word]
     const uint32_t moff = MEMBER == IQK_IQ2_K ? (g * 4 + tig) * 16 : (g * 2 + side) * 16;
     const uint32_t zero_u = smem_u32(zeros);
-    const uint32_t m16 = a.one << 16, m30 = a.one << 30;  // mulhi: >> 16, >> 2
+    const uint32_t m30 = a.one << 30;  // mulhi(x, m30) == x >> 2
     // metadata lanes: (mg, mq) owns row pair (mg, mg + 8) and 128 weights a round
     const int mg = lane & 7, mq = lane >> 3;
     const int mra = 16 * rt + mg;  // item-local row (and mra + 8)
@@ -664,6 +658,68 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     const uint32_t hmul = 0x02040810u >> msh;                 // bit msh+u -> bit 8u+4
     const uint32_t amul = msh ? 0x01020408u : 0x10204080u;    // bit msh+u -> bit 8u+7
     const uint32_t a44 = a.one * 0x88000000u;                 // mulhi: t>>1 | t>>5
+
+    // Group metadata of round r (this warp's 16 rows x 512 weights) into the
+    // metadata buffer at mb.
+    auto build_meta = [&](const char *sd, int r, uint32_t mb) {
+        if (MEMBER == IQK_IQ2_KS) {
+            // Four groups of rows mra and mra + 8 at once, one byte per
+            // group: scale index (low nibble | high bit << 4) and the
+            // alphabet mask (0x44 when the group uses the second one).
+            const int s0 = r * 16 + mq * 4;  // first of 4 groups (2 pairs)
+            const uint8_t *scl = reinterpret_cast<const uint8_t *>(sd);
+            const uint8_t *sch = scl + SS::off(2) + (s0 >> 3);
+            const uint8_t *sex = scl + SS::off(3) + (s0 >> 3);
+            scl += s0 >> 1;
+            const uint32_t la = lds_u16(scl + mra * (N / 64));
+            const uint32_t lb = lds_u16(scl + (mra + 8) * (N / 64));
+            const uint32_t ha = sch[mra * (N / 256)], hb = sch[(mra + 8) * (N / 256)];
+            const uint32_t xa = sex[mra * (N / 256)], xb = sex[(mra + 8) * (N / 256)];
+            const uint32_t pa = prmt(la, 0u, 0x4140u), pb = prmt(lb, 0u, 0x4140u);
+            const uint32_t va = ((pa | (pa << 4)) & 0x0F0F0F0Fu) | (((ha & hmask) * hmul) & 0x10101010u);
+            const uint32_t vb = ((pb | (pb << 4)) & 0x0F0F0F0Fu) | (((hb & hmask) * hmul) & 0x10101010u);
+            const uint32_t aa = mulhi(((xa & hmask) * amul) & 0x80808080u, a44);
+            const uint32_t ab = mulhi(((xb & hmask) * amul) & 0x80808080u, a44);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int ia = (int)prmt(va, 0u, 0x4440u + u) - 16;
+                const int ib = (int)prmt(vb, 0u, 0x4440u + u) - 16;
+                const uint32_t ama = prmt(aa, 0u, 0x1111u * u);
+                const uint32_t amb = prmt(ab, 0u, 0x1111u * u);
+                const int pr = mq * 2 + (u >> 1), sd2 = u & 1;  // pair, side
+                st_s128(mb + pr * 256 + (mg * 2 + sd2) * 16, ama, amb, (uint32_t)ia,
+                        (uint32_t)ib);
+            }
+        } else if (MEMBER == IQK_IQ2_K) {
+            const int b0 = r * 32 + mq * 8;  // first of 8 sub-blocks (2 pairs)
+            const uint8_t *scl = reinterpret_cast<const uint8_t *>(sd);
+            const uint8_t *sex = scl + SS::off(2) + (b0 >> 3);
+            scl += b0 >> 1;
+            const uint32_t la = lds_u32(scl + mra * (N / 32));
+            const uint32_t lb = lds_u32(scl + (mra + 8) * (N / 32));
+            const uint32_t xa = sex[mra * (N / 128)];
+            const uint32_t xb = sex[(mra + 8) * (N / 128)];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const uint2 ta = ktab[((xa >> u) & 1u) * 16 + ((la >> (4 * u)) & 15u)];
+                const uint2 tb = ktab[((xb >> u) & 1u) * 16 + ((lb >> (4 * u)) & 15u)];
+                const int pr = mq * 2 + (u >> 2), wd = u & 3;  // pair, word
+                st_s128(mb + pr * 512 + (mg * 4 + wd) * 16, ta.x, tb.x, ta.y, tb.y);
+            }
+        } else {
+            const int s0 = r * 16 + mq * 4;  // first of 4 blocks (2 pairs)
+            const uint16_t *qh = reinterpret_cast<const uint16_t *>(sd) + s0;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t ha = qh[mra * (N / 32) + u], hb = qh[(mra + 8) * (N / 32) + u];
+                const int sa = 2 * (int)((ha >> 12) & 7u) + 1, sb = 2 * (int)((hb >> 12) & 7u) + 1;
+                const int pr = mq * 2 + (u >> 1), sd2 = u & 1;
+                st_s128(mb + pr * 256 + (mg * 2 + sd2) * 16, ha | (hb << 16),
+                        (uint32_t)((ha & 0x8000u) ? -sa : sa), (uint32_t)((hb & 0x8000u) ? -sb : sb),
+                        (uint32_t)(sa | (sb << 16)));
+            }
+        }
+    };
 
     int ti = i0 / rblocks, rb = i0 % rblocks;
     for (int o = 0; o < n_items; ++o) {
@@ -680,6 +736,8 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
             break;
         }
         if (*(volatile int *)abort_flag) break;
+        if (live) build_meta(sd, 0, meta_u);
+        __syncwarp();
         int32_t tot[4] = {0, 0, 0, 0};
         int32_t acc1[4] = {0, 0, 0, 0}, acc2[4] = {0, 0, 0, 0};  // IQ2_K super-block sums
         double dacc[2] = {0.0, 0.0};                              // IQ2_K: rows g, g+8
@@ -694,73 +752,13 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
             }
             const char *st = stages + slot * STB;
             if (live) {
-                // ---- group metadata for this warp's 16 rows x 512 weights.
-                if (MEMBER == IQK_IQ2_KS) {
-                    // Four groups of rows mra and mra + 8 at once, one byte per
-                    // group: scale index (low nibble | high bit << 4) and the
-                    // alphabet mask (0x44 when the group uses the second one).
-                    const int s0 = r * 16 + mq * 4;  // first of 4 groups (2 pairs)
-                    const uint8_t *scl = reinterpret_cast<const uint8_t *>(sd);
-                    const uint8_t *sch = scl + SS::off(2) + (s0 >> 3);
-                    const uint8_t *sex = scl + SS::off(3) + (s0 >> 3);
-                    scl += s0 >> 1;
-                    const uint32_t la = lds_u16(scl + mra * (N / 64));
-                    const uint32_t lb = lds_u16(scl + (mra + 8) * (N / 64));
-                    const uint32_t ha = sch[mra * (N / 256)], hb = sch[(mra + 8) * (N / 256)];
-                    const uint32_t xa = sex[mra * (N / 256)], xb = sex[(mra + 8) * (N / 256)];
-                    const uint32_t pa = prmt(la, 0u, 0x4140u), pb = prmt(lb, 0u, 0x4140u);
-                    const uint32_t va = ((pa | (pa << 4)) & 0x0F0F0F0Fu) | (((ha & hmask) * hmul) & 0x10101010u);
-                    const uint32_t vb = ((pb | (pb << 4)) & 0x0F0F0F0Fu) | (((hb & hmask) * hmul) & 0x10101010u);
-                    const uint32_t aa = mulhi(((xa & hmask) * amul) & 0x80808080u, a44);
-                    const uint32_t ab = mulhi(((xb & hmask) * amul) & 0x80808080u, a44);
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int ia = (int)prmt(va, 0u, 0x4440u + u) - 16;
-                        const int ib = (int)prmt(vb, 0u, 0x4440u + u) - 16;
-                        const uint32_t ama = prmt(aa, 0u, 0x1111u * u);
-                        const uint32_t amb = prmt(ab, 0u, 0x1111u * u);
-                        const int pr = mq * 2 + (u >> 1), sd2 = u & 1;  // pair, side
-                        st_s128(meta_u + pr * 256 + (mg * 2 + sd2) * 16, ama, amb, (uint32_t)ia,
-                                (uint32_t)ib);
-                    }
-                } else if (MEMBER == IQK_IQ2_K) {
-                    const int b0 = r * 32 + mq * 8;  // first of 8 sub-blocks (2 pairs)
-                    const uint8_t *scl = reinterpret_cast<const uint8_t *>(sd);
-                    const uint8_t *sex = scl + SS::off(2) + (b0 >> 3);
-                    scl += b0 >> 1;
-                    const uint32_t la = lds_u32(scl + mra * (N / 32));
-                    const uint32_t lb = lds_u32(scl + (mra + 8) * (N / 32));
-                    const uint32_t xa = sex[mra * (N / 128)];
-                    const uint32_t xb = sex[(mra + 8) * (N / 128)];
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) {
-                        const uint2 ta = ktab[((xa >> u) & 1u) * 16 + ((la >> (4 * u)) & 15u)];
-                        const uint2 tb = ktab[((xb >> u) & 1u) * 16 + ((lb >> (4 * u)) & 15u)];
-                        const int pr = mq * 2 + (u >> 2), wd = u & 3;  // pair, word
-                        st_s128(meta_u + pr * 512 + (mg * 4 + wd) * 16, ta.x, tb.x, ta.y, tb.y);
-                    }
-                } else {
-                    const int s0 = r * 16 + mq * 4;  // first of 4 blocks (2 pairs)
-                    const uint16_t *qh = reinterpret_cast<const uint16_t *>(sd) + s0;
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const uint32_t ha = qh[mra * (N / 32) + u], hb = qh[(mra + 8) * (N / 32) + u];
-                        const int ma = 2 * (int)((ha >> 12) & 7u) + 1, mb = 2 * (int)((hb >> 12) & 7u) + 1;
-                        const int pr = mq * 2 + (u >> 1), sd2 = u & 1;
-                        st_s128(meta_u + pr * 256 + (mg * 2 + sd2) * 16, ha | (hb << 16),
-                                (uint32_t)((ha & 0x8000u) ? -ma : ma), (uint32_t)((hb & 0x8000u) ? -mb : mb),
-                                (uint32_t)(ma | (mb << 16)));
-                    }
-                }
-                __syncwarp();
-
                 // ---- 8 MMA pairs, all shared-memory addresses 32-bit and the
                 // per-pair offsets compile-time immediates.
                 const uint32_t wb_u = smem_u32(st + wid * G::kWBox);
                 const uint32_t xs_u = smem_u32(st + G::kWBytes);
                 // B: live lanes read their plane's 16 bytes; the others a zero block
                 const uint32_t xl_u = bplane >= 0 ? xs_u + tig * 48 + bplane * 16 : zero_u;
-                const uint32_t mrow = meta_u + moff;
+                const uint32_t mrow = meta_u + (r & 1) * G::kMetaBytes + moff;
                 const uint32_t wl = wb_u | woff;  // box is 1024-aligned, woff < 1024
 #pragma unroll
                 for (int pr = 0; pr < kPairsPerRound; ++pr) {
@@ -781,10 +779,10 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                         A[2] = prmt(kIq2Tab0, kIq2Tab1, s1g);
                         A[3] = prmt(kIq2Tab0, kIq2Tab1, s1h);
                         mma_s8(d, A, bv.x, bv.y);
-                        A[0] = prmt(kIq2Tab0, kIq2Tab1, shr16(s0g, m16));
-                        A[1] = prmt(kIq2Tab0, kIq2Tab1, shr16(s0h, m16));
-                        A[2] = prmt(kIq2Tab0, kIq2Tab1, shr16(s1g, m16));
-                        A[3] = prmt(kIq2Tab0, kIq2Tab1, shr16(s1h, m16));
+                        A[0] = prmt(kIq2Tab0, kIq2Tab1, shr16(s0g));
+                        A[1] = prmt(kIq2Tab0, kIq2Tab1, shr16(s0h));
+                        A[2] = prmt(kIq2Tab0, kIq2Tab1, shr16(s1g));
+                        A[3] = prmt(kIq2Tab0, kIq2Tab1, shr16(s1h));
                         mma_s8_acc(d, A, bv.z, bv.w);
                         tot[0] += (int)m.z * d[0];
                         tot[1] += (int)m.z * d[1];
@@ -797,8 +795,8 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                         const uint4 m = ld_s128(mrow + pr * 512);
                         const uint32_t s0g = wg & 0x33333333u, s1g = shr2(wg, m30) & 0x33333333u;
                         const uint32_t s0h = wg8 & 0x33333333u, s1h = shr2(wg8, m30) & 0x33333333u;
-                        const uint32_t s0gh = shr16(s0g, m16), s1gh = shr16(s1g, m16);
-                        const uint32_t s0hh = shr16(s0h, m16), s1hh = shr16(s1h, m16);
+                        const uint32_t s0gh = shr16(s0g), s1gh = shr16(s1g);
+                        const uint32_t s0hh = shr16(s0h), s1hh = shr16(s1h);
                         A[0] = prmt(m.x, 0u, s0g);
                         A[1] = prmt(m.y, 0u, s0h);
                         A[2] = prmt(m.x, 0u, s1g);
@@ -860,10 +858,10 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                         A[2] = prmt(kTernTab, 0u, s1g);
                         A[3] = prmt(kTernTab, 0u, s1h);
                         mma_s8(d, A, bv.x, bv.y);
-                        A[0] = prmt(kTernTab, 0u, shr16(s0g, m16));
-                        A[1] = prmt(kTernTab, 0u, shr16(s0h, m16));
-                        A[2] = prmt(kTernTab, 0u, shr16(s1g, m16));
-                        A[3] = prmt(kTernTab, 0u, shr16(s1h, m16));
+                        A[0] = prmt(kTernTab, 0u, shr16(s0g));
+                        A[1] = prmt(kTernTab, 0u, shr16(s0h));
+                        A[2] = prmt(kTernTab, 0u, shr16(s1g));
+                        A[3] = prmt(kTernTab, 0u, shr16(s1h));
                         mma_s8_acc(d, A, bv.z, bv.w);
                         // block sums of this lane's two C columns (block 2*pr+side,
                         // planes 2*(tig&1) and +1; plane 3 reads the stored zero)
@@ -875,6 +873,11 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                         tot[3] += mb * 8 * d[3] + (int)m.z * (int)xsum.y;
                     }
                 }
+                // Next round's metadata into the other buffer, after the pair
+                // loop in program order so its loads and arithmetic can fill
+                // the loop's latency gaps. (After an item's last round it reads
+                // other rows' bytes of the scale slot and is never used.)
+                build_meta(sd, r + 1, meta_u + ((r + 1) & 1) * G::kMetaBytes);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);  // this round's stage
@@ -1056,15 +1059,26 @@ cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_
     const int smem = gemv_smem_for(member, n);
     // Upper bound on CTA items: every pair its own tile of every row block.
     const int64_t max_items = pairs * ((out_features + kItemRows - 1) / kItemRows);
-    const int per_sm = member == IQK_IQ2_K ? Geo<IQK_IQ2_K>::kMinBlocks : Geo<IQK_IQ2_KS>::kMinBlocks;
-    const int64_t cap = (int64_t)num_sms * per_sm;
-    int64_t blocks = max_items < cap ? max_items : cap;
-    if (blocks < 1) blocks = 1;
+    // One persistent wave: as many CTAs as fit on every SM at once (shared
+    // memory and registers decide; cached per member and width).
+    static std::atomic<int> resident[3][2];
+    int64_t blocks = 1;
 #define IQK_GEMV(M, N)                                                                          \
     do {                                                                                        \
         err = cudaFuncSetAttribute(gemv_kernel<M, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                    smem);                                                       \
         if (err != cudaSuccess) return err;                                                     \
+        std::atomic<int> &per_sm = resident[M][N == 4096];                                      \
+        if (per_sm.load() == 0) {                                                               \
+            int nb = 0;                                                                         \
+            err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, gemv_kernel<M, N>, kThreads, \
+                                                                smem);                          \
+            if (err != cudaSuccess) return err;                                                 \
+            per_sm.store(nb > 0 ? nb : 1);                                                      \
+        }                                                                                       \
+        const int64_t cap = (int64_t)num_sms * per_sm.load();                                   \
+        blocks = max_items < cap ? max_items : cap;                                             \
+        if (blocks < 1) blocks = 1;                                                             \
         gemv_kernel<M, N><<<(unsigned)blocks, kThreads, smem, stream>>>(ga, map);               \
     } while (0)
     if (n == 2048) {
