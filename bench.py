@@ -615,13 +615,14 @@ def run_b200(args) -> None:
         host.append({
             "x": torch.randn((ne, B, 1, 1, GATE_UP[1])).to(torch.bfloat16).pin_memory(),
             "xd": torch.randn((ne, B, TOP_K, 1, DOWN[1])).to(torch.bfloat16).pin_memory(),
-            "idx": torch.from_numpy(c.sels_np[np.arange(ne) % c.pool]).pin_memory(),
+            # int32 routing indices, as the reference's router emits 32-bit ids
+            "idx": torch.from_numpy(c.sels_np[np.arange(ne) % c.pool].astype(np.int32)).pin_memory(),
             "yg": torch.empty((ne, B, TOP_K, 1, GATE_UP[0])).pin_memory(),
             "yu": torch.empty((ne, B, TOP_K, 1, GATE_UP[0])).pin_memory(),
             "yd": torch.empty((ne, B, TOP_K, 1, DOWN[0])).pin_memory(),
             "dx": torch.empty((B, 1, 1, GATE_UP[1]), device=dev, dtype=torch.bfloat16),
             "dxd": torch.empty((B, TOP_K, 1, DOWN[1]), device=dev, dtype=torch.bfloat16),
-            "didx": torch.empty((B, TOP_K), device=dev, dtype=torch.int64)})
+            "didx": torch.empty((B, TOP_K), device=dev, dtype=torch.int32)})
 
     def e2e_step(i: int):
         for h in host:
@@ -636,7 +637,7 @@ def run_b200(args) -> None:
         e2e_step(i)
     ems = timed(_Eager(lambda: [e2e_step(i) for i in range(ne)]))
     e_bytes = sum(c.bytes(i) for c in cells for i in range(ne))
-    h2d = sum(c.B * GATE_UP[1] * 2 + c.B * TOP_K * DOWN[1] * 2 + c.B * TOP_K * 8 for c in cells)
+    h2d = sum(c.B * GATE_UP[1] * 2 + c.B * TOP_K * DOWN[1] * 2 + c.B * TOP_K * 4 for c in cells)
     d2h = sum(c.B * TOP_K * (2 * GATE_UP[0] + DOWN[0]) * 4 for c in cells)
     e2e = {"value": round(world * e_bytes / (ems * 1e-3) / 1e9, 2), "unit": "GB/s",
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

@@ -4,6 +4,7 @@
 // any launch (the reference fails closed the same way before compiling:
 // src/mlx_iqk/kernels.py:100-128, src/mlx_iqk/nn.py:110-126) and returns a
 // status instead of raising.
+#include <atomic>
 #include <cstdio>
 
 #include "iqk_common.cuh"
@@ -19,11 +20,16 @@ bool dtype_ok(int d) { return d == IQK_F32 || d == IQK_F16 || d == IQK_BF16; }
 bool width_ok(int64_t n) { return n == 2048 || n == 4096; }
 bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// SM count of the current device, queried once per device.
 int num_sms_current() {
-    int dev = 0, sms = 148;
-    if (cudaGetDevice(&dev) == cudaSuccess)
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    return sms > 0 ? sms : 148;
+    static std::atomic<int> cached[64];
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (dev >= 0 && dev < 64 && (sms = cached[dev].load()) > 0) return sms;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+        sms = 148;
+    if (dev >= 0 && dev < 64) cached[dev].store(sms);
+    return sms;
 }
 
 // Stream pointers: present, and 16-byte aligned (the kernels move them with

@@ -1062,12 +1062,20 @@ cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_
     // One persistent wave: as many CTAs as fit on every SM at once (shared
     // memory and registers decide; cached per member and width).
     static std::atomic<int> resident[3][2];
+    // The shared-memory opt-in is a per-device function attribute: set once.
+    static std::atomic<unsigned> attr_done[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = -1;
     int64_t blocks = 1;
 #define IQK_GEMV(M, N)                                                                          \
     do {                                                                                        \
-        err = cudaFuncSetAttribute(gemv_kernel<M, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                   smem);                                                       \
-        if (err != cudaSuccess) return err;                                                     \
+        const unsigned bit = 1u << ((M) * 2 + ((N) == 4096));                                   \
+        if (dev < 0 || !(attr_done[dev].load() & bit)) {                                        \
+            err = cudaFuncSetAttribute(gemv_kernel<M, N>,                                       \
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);      \
+            if (err != cudaSuccess) return err;                                                 \
+            if (dev >= 0) attr_done[dev].fetch_or(bit);                                         \
+        }                                                                                       \
         std::atomic<int> &per_sm = resident[M][N == 4096];                                      \
         if (per_sm.load() == 0) {                                                               \
             int nb = 0;                                                                         \

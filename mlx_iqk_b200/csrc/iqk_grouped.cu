@@ -46,6 +46,8 @@
 // drained, and tensor memory is freed before the CTA exits.
 #include <cuda.h>
 
+#include <atomic>
+
 #include "iqk_common.cuh"
 #include "iqk_grouped.cuh"
 #include "iqk_sync.cuh"
@@ -945,11 +947,20 @@ cudaError_t launch_grouped_run(int member, const void *const *streams, int64_t n
     const int64_t max_items = L.max_tiles * ga.rblocks;
     int64_t blocks = max_items < num_sms ? max_items : num_sms;
     if (blocks < 1) blocks = 1;
+    // The shared-memory opt-in (to the largest plan) is a per-device
+    // function attribute: set once.
+    static std::atomic<unsigned> attr_done[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = -1;
 #define IQK_GG(M, R)                                                                           \
     do {                                                                                       \
-        err = cudaFuncSetAttribute(grouped_gemm_kernel<M, R>,                                  \
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, smem);         \
-        if (err != cudaSuccess) return err;                                                    \
+        const unsigned bit = 1u << ((M) * 2 + (R) - 1);                                        \
+        if (dev < 0 || !(attr_done[dev].load() & bit)) {                                       \
+            err = cudaFuncSetAttribute(grouped_gemm_kernel<M, R>,                              \
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap); \
+            if (err != cudaSuccess) return err;                                                \
+            if (dev >= 0) attr_done[dev].fetch_or(bit);                                        \
+        }                                                                                      \
         grouped_gemm_kernel<M, R><<<(unsigned)blocks, kThreadsG, smem, stream>>>(ga, qmap,     \
                                                                                  xmap);        \
     } while (0)

@@ -160,10 +160,19 @@ def stream_handle(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+_PTR_ARRAYS: dict[tuple, ctypes.Array] = {}
+
+
 def ptr_array(tensors) -> ctypes.Array:
-    arr = (ctypes.c_void_p * len(tensors))()
-    for i, t in enumerate(tensors):
-        arr[i] = t.data_ptr()
+    """The streams' device pointers as a C array (cached per pointer tuple:
+    a module's streams keep their storage between calls)."""
+    key = tuple(t.data_ptr() for t in tensors)
+    arr = _PTR_ARRAYS.get(key)
+    if arr is None:
+        if len(_PTR_ARRAYS) > 256:
+            _PTR_ARRAYS.clear()
+        arr = (ctypes.c_void_p * len(key))(*key)
+        _PTR_ARRAYS[key] = arr
     return arr
 
 

@@ -209,7 +209,7 @@ class IqkSwitchLinear(nn.Module):
         the same split, with dequantize + ``gather_mm`` on the prefill side).
         ``iq1_s_r4`` has no grouped kernel and always takes the GEMV.
         """
-        pairs = int(np.prod(tuple(indices.shape))) if hasattr(indices, "shape") else \
+        pairs = indices.numel() if isinstance(indices, torch.Tensor) else \
             int(np.asarray(indices).size)
         if self.member in K.GROUPED_MEMBERS and (sorted_indices or pairs > DECODE_MAT_LIMIT):
             return self.grouped(x, indices)
