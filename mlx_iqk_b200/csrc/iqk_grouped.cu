@@ -635,6 +635,8 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
                     }
                     tc_fence_after();
                     const uint32_t st = smem_u + G.x + xs * x_slot_bytes(cap);
+                    // elect.sync needs the whole warp converged: one lane issues.
+                    __syncwarp();
                     if (elect_one()) {
 #pragma unroll
                         for (int kk = 0; kk < 8; ++kk) {
@@ -658,6 +660,7 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
                 __syncwarp();
             }
             if (!ok && lane == 0) give_up();
+            __syncwarp();
             // Every MMA issued must finish before tensor memory is freed.
             if (elect_one()) tc_commit(drain);
             __syncwarp();
