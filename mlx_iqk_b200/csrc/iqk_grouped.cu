@@ -80,7 +80,10 @@ constexpr int kMaxGroups = 4;
 constexpr int kTmemCols = 512;
 constexpr int kTok = 64;                             // tokens per work tile
 constexpr uint32_t kACol = 256;
-constexpr int kBarBytes = 8 * (2 * kMaxXSlots + 2 * kMaxCodeSlots + 2 * kMaxGroups + 3 + 4) + 16;
+// Barriers, the TMEM slot word and the abort flag; then the group tables.
+constexpr int kTabOff = 8 * (2 * kMaxXSlots + 2 * kMaxCodeSlots + 2 * kMaxGroups + 3 + 4) + 16;
+constexpr int kTabEntries = 64;  // IQ2_KS: (scale index + 16) | alphabet << 5; IQ2_K: idx + 8 | alpha << 4
+constexpr int kBarBytes = kTabOff + 8 * kTabEntries;
 constexpr int kSmemCap = 227 * 1024;
 
 // Per-item scale buffer: per (stage, row) scale words, transposed so that a
@@ -392,9 +395,16 @@ __device__ __forceinline__ void load_item_scales(const GroupedArgs &a, int4 tl, 
                 const uint32_t x32 = (c & 1) ? xb[c >> 1].y : xb[c >> 1].x;
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
+                    // stage 8c+j: groups 4(8c+j) .. +3, one byte each:
+                    // 5-bit scale (low nibble | high bit << 4) | alphabet << 5
                     const uint32_t lo = (sv[j >> 1] >> (16 * (j & 1))) & 0xffffu;
                     const uint32_t hi = (h32 >> (4 * j)) & 15u, al = (x32 >> (4 * j)) & 15u;
-                    sc[(8 * c + j) * rows + r] = lo | (hi << 16) | (al << 20);
+                    uint32_t packed = 0;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        packed |= (((lo >> (4 * q)) & 15u) | (((hi >> q) & 1u) << 4) |
+                                   (((al >> q) & 1u) << 5)) << (8 * q);
+                    sc[(8 * c + j) * rows + r] = packed;
                 }
             }
             rsc[r] = half_bits_to_float(dvb);
@@ -486,6 +496,10 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
     uint64_t *sempty = sfull + 2;  // [2]
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sempty + 2);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    // f16x2 pair tables of every (scale index, alphabet): {V0, V1} and {V2, V3}
+    // times the index (IQ2_KS), or times the index before the super-block
+    // scale (IQ2_K). Products of small integers: exact in f16.
+    uint2 *gtab = reinterpret_cast<uint2 *>(smem + G.bars + kTabOff);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int32_t *hdr = reinterpret_cast<const int32_t *>(a.ws + a.L.hdr);
@@ -517,6 +531,14 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
         }
         *abort_flag = 0;
         bar_fence_init();
+    }
+    if (threadIdx.x < kTabEntries) {
+        const int i = threadIdx.x;
+        const int idx = MEMBER == IQK_IQ2_KS ? (i & 31) - 16 : (i & 15) - 8;
+        const bool alpha = MEMBER == IQK_IQ2_KS ? (i >> 5) & 1 : (i >> 4) & 1;
+        const uint32_t hv = h2_bcast((float)idx);
+        gtab[i] = make_uint2(hmul2_bits(hv, alpha ? kV01a1 : kV01a0),
+                             hmul2_bits(hv, alpha ? kV23a1 : kV23a0));
     }
     if (warp == kTmemWarp) {
         tmem_alloc(tmem_slot, kTmemCols);
@@ -740,27 +762,22 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
                 tc_fence_after();
                 const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
                 const uint32_t taddr = tmem + lane_base + kACol + aslot;
-                float dsb = 0.f;
-                if (MEMBER == IQK_IQ2_K) dsb = __half2float(__ushort_as_half((uint16_t)(s1 >> 16)));
+                // IQ2_K: the super-block scale, f16 in both halves
+                const uint32_t dsb2 = MEMBER == IQK_IQ2_K ? (s1 >> 16) * 0x10001u : 0u;
                 uint32_t t01 = 0, t23 = 0;
 #pragma unroll
                 for (int wd = 0; wd < 8; ++wd) {
                     if (MEMBER == IQK_IQ2_KS) {
                         if ((wd & 1) == 0) {  // one 32-weight group per two words
-                            const int gq = wd >> 1;
-                            const int idx = (int)(((s0 >> (4 * gq)) & 15u) |
-                                                  (((s0 >> (16 + gq)) & 1u) << 4)) - 16;
-                            const bool alpha = (s0 >> (20 + gq)) & 1u;
-                            const uint32_t hv = h2_bcast((float)idx);
-                            t01 = hmul2_bits(hv, alpha ? kV01a1 : kV01a0);
-                            t23 = hmul2_bits(hv, alpha ? kV23a1 : kV23a0);
+                            const uint2 t = gtab[prmt(s0, 0u, 0x4440u + (uint32_t)(wd >> 1))];
+                            t01 = t.x;
+                            t23 = t.y;
                         }
                     } else {
-                        const int idx = (int)((s0 >> (4 * wd)) & 15u) - 8;
-                        const bool alpha = (s1 >> wd) & 1u;
-                        const uint32_t hv = h2_bcast(dsb * (float)idx);
-                        t01 = hmul2_bits(hv, alpha ? kV01a1 : kV01a0);
-                        t23 = hmul2_bits(hv, alpha ? kV23a1 : kV23a0);
+                        const uint32_t ti = ((s0 >> (4 * wd)) & 15u) | (((s1 >> wd) & 1u) << 4);
+                        const uint2 t = gtab[ti];
+                        t01 = hmul2_bits(t.x, dsb2);
+                        t23 = hmul2_bits(t.y, dsb2);
                     }
                     uint32_t r[8];
                     expand_word(words[wd], t01, t23, r);

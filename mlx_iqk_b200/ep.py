@@ -10,21 +10,26 @@ shard of the tokens. One forward:
 1. **dispatch** -- every token row goes once to every rank that holds at
    least one of its experts (deduplicated per (token, rank)), with the list
    of (row, local expert, router weight) pairs that need it:
-   ``all_to_all_single`` of the split counts, then of the rows (bf16) and the
-   pair records;
+   ``all_to_all_single`` of the split counts, then of the rows (bf16) and of
+   the pair records (one int64 record per pair, the weight as its f32 bits);
 2. **expert compute** on the receiving rank -- grouped GEMM of gate and up
    over the received pairs (``iqk_grouped_gemm`` with explicit rows),
-   SiLU(gate) * up, grouped GEMM of down, and the router-weighted sum of each
-   row's pairs;
+   SiLU(gate) * up scaled by the pair's router weight (the down projection
+   is linear, so the weight can go in before it), grouped GEMM of down, and
+   the sum of each row's pairs;
 3. **combine** -- one row per (token, rank) travels back the reverse way and
    is added into the token's output.
 
-No kernel reads another GPU's memory; the only data-path collectives are the
-three ``all_to_all_single`` exchanges, and every rank takes them in the same
-order. The expert computation is a parameter (``expert_fn``) only so that
-CPU tests can check the dispatch and combine logic on ``gloo`` ranks against
-a host stand-in; the default -- and the only product path -- is the CUDA
-grouped GEMM.
+All routing arithmetic runs on the device; the host reads the split counts
+once per call (that read also carries the out-of-range index check). With a
+single rank there is no exchange and no gather.
+
+No kernel reads another GPU's memory; the only collectives are the four
+``all_to_all_single`` exchanges (counts, rows, pair records, result rows),
+and every rank takes them in the same order. The expert computation is a
+parameter (``expert_fn``) only so that CPU tests can check the dispatch and
+combine logic on ``gloo`` ranks against a host stand-in; the default -- and
+the only product path -- is the CUDA grouped GEMM.
 """
 
 from __future__ import annotations
@@ -70,6 +75,7 @@ class ExpertParallelMoE:
             self.up = IqkSwitchLinear(u, self.local_experts, inter, hidden, device=self.device)
             self.down = IqkSwitchLinear(d, self.local_experts, hidden, inter, device=self.device)
         self.last_stats: dict = {}
+        self._tok_cache: dict = {}
 
     # -- expert compute --------------------------------------------------
 
@@ -98,77 +104,110 @@ class ExpertParallelMoE:
                       self.hidden, P, g, ws)
         K.grouped_run(self.up.member, self.up._streams(), self.local_experts, self.inter,
                       self.hidden, P, u, ws)
-        h = (torch.nn.functional.silu(g) * u).to(torch.bfloat16)
+        # SiLU(gate) * up, with the router weight folded in before the down
+        # projection (it is linear: w * (Wd h) == Wd (w * h)), so its output
+        # needs no weighted copy.
+        torch.nn.functional.silu(g, inplace=True)
+        g.mul_(u).mul_(pair_weight.to(device=g.device, dtype=torch.float32).unsqueeze(1))
+        h = g.to(torch.bfloat16)
+        del g, u
         y = torch.empty((P, self.hidden), dtype=torch.float32, device=rows.device)
         ws_d = torch.empty(K.grouped_workspace_bytes(self.inter, self.local_experts, P),
                            dtype=torch.uint8, device=rows.device)
         K.grouped(self.down.member, h, self.down._streams(), self.local_experts, self.hidden,
                   self.inter, sel, None, y, ws_d)
-        out.index_add_(0, pair_row.long(), y * pair_weight.to(torch.float32).unsqueeze(1))
+        out.index_add_(0, pair_row.long(), y)
         return out
 
     # -- dispatch / combine ----------------------------------------------
 
     def _exchange(self, send: torch.Tensor, send_counts: list[int], recv_counts: list[int]):
-        if self.world == 1:
-            return send
         recv = torch.empty((sum(recv_counts),) + tuple(send.shape[1:]), dtype=send.dtype,
                            device=send.device)
         dist.all_to_all_single(recv, send.contiguous(), recv_counts, send_counts,
                                group=self.group)
         return recv
 
+    def _token_index(self, T: int, k: int, dev) -> torch.Tensor:
+        """pair -> token for token-major [T, k] routing (cached per shape)."""
+        key = (T, k, str(dev))
+        t = self._tok_cache.get(key)
+        if t is None:
+            if len(self._tok_cache) >= 8:
+                self._tok_cache.clear()
+            t = torch.arange(T, device=dev).repeat_interleave(k)
+            self._tok_cache[key] = t
+        return t
+
     def forward(self, x: torch.Tensor, indices: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
         """``x [T, hidden]`` (this rank's tokens), ``indices [T, k]`` global expert
-        ids, ``weights [T, k]`` router weights -> ``[T, hidden]`` float32."""
-        T, k = indices.shape
-        G, El = self.world, self.local_experts
-        dev = x.device
-        idx = indices.to(device=dev, dtype=torch.int64)
-        if idx.numel() and (int(idx.min()) < 0 or int(idx.max()) >= self.num_experts):
-            raise K.IqkRuntimeError("expert index outside [0, num_experts)")
-        dest = idx // El                                        # [T, k]
-        # one row per (token, destination rank), destination-major
-        need = torch.zeros((G, T), dtype=torch.bool, device=dev)
-        need[dest.reshape(-1), torch.arange(T, device=dev).repeat_interleave(k)] = True
-        row_counts = need.sum(dim=1)                            # [G]
-        rank_in_dest = torch.cumsum(need.to(torch.int64), dim=1) - 1  # [G, T]
-        send_tok = need.nonzero(as_tuple=False)                 # [S, 2] (dest, token), sorted
-        send_rows = x.to(torch.bfloat16)[send_tok[:, 1]]
-        # pair records, destination-major (stable in token, then slot)
-        flat_dest = dest.reshape(-1)
-        order = torch.argsort(flat_dest, stable=True)
-        p_tok = torch.arange(T, device=dev).repeat_interleave(k)[order]
-        p_dest = flat_dest[order]
-        p_row = rank_in_dest[p_dest, p_tok]                     # row within its destination block
-        p_exp = (idx.reshape(-1)[order] - p_dest * El)
-        p_w = weights.to(device=dev, dtype=torch.float32).reshape(-1)[order]
-        pair_counts = torch.bincount(p_dest, minlength=G)
+        ids, ``weights [T, k]`` router weights -> ``[T, hidden]`` float32.
 
-        counts = torch.stack([row_counts, pair_counts]).to(torch.int64)   # [2, G]
-        if G > 1:
-            recv_c = torch.empty_like(counts.t().contiguous())
-            dist.all_to_all_single(recv_c, counts.t().contiguous(), group=self.group)
-            recv_c = recv_c.t()
-        else:
-            recv_c = counts
-        s_rows, s_pairs = counts[0].tolist(), counts[1].tolist()
-        r_rows, r_pairs = recv_c[0].tolist(), recv_c[1].tolist()
+        All routing arithmetic stays on the device; the host reads the split
+        counts (and whether any index was out of range) once per call.
+        """
+        T, k = indices.shape
+        G, El, E = self.world, self.local_experts, self.num_experts
+        dev = x.device
+        idx_in = indices.to(device=dev, dtype=torch.int64).reshape(-1)   # [T*k], token-major
+        idx = idx_in.clamp(0, E - 1)                                     # keeps every index in range
+        w = weights.to(device=dev, dtype=torch.float32).reshape(-1)
+        tok = self._token_index(T, k, dev)                               # pair -> token
+        if G == 1:
+            # every token's rows stay here: no dispatch gathers, no exchange
+            if bool((idx != idx_in).any()):
+                raise K.IqkRuntimeError("expert index outside [0, num_experts)")
+            y = self.local_experts_forward(x.to(torch.bfloat16), tok, idx, w)
+            self.last_stats = {"rows_sent": T, "pairs_sent": T * k, "rows_received": T,
+                               "pairs_received": T * k}
+            return y
+
+        dest = torch.div(idx, El, rounding_mode="floor")                 # [T*k]
+        # one row per (token, destination rank), destination-major
+        need = torch.zeros(G * T, dtype=torch.int64, device=dev)
+        need.index_fill_(0, dest * T + tok, 1)
+        rank_in_dest = need.view(G, T).cumsum(dim=1)                     # inclusive
+        # per destination: rows, pairs, and this rank's out-of-range flag
+        counts = torch.zeros((G, 3), dtype=torch.int64, device=dev)
+        counts[:, 0] = rank_in_dest[:, -1]
+        counts[:, 1].index_add_(0, dest, torch.ones_like(dest))
+        counts[:, 2] = (idx != idx_in).any()
+        recv_c = torch.empty_like(counts)
+        dist.all_to_all_single(recv_c, counts, group=self.group)
+        host = torch.cat([counts, recv_c]).tolist()                      # the one host read
+        if any(r[2] for r in host):
+            raise K.IqkRuntimeError("expert index outside [0, num_experts)")
+        s_rows, s_pairs = [r[0] for r in host[:G]], [r[1] for r in host[:G]]
+        r_rows, r_pairs = [r[0] for r in host[G:]], [r[1] for r in host[G:]]
+
+        # rows to send: slot of (g, t) = first slot of g's block + rank within
+        # it; unmarked (g, t) write a spare slot past the end
+        row_base = counts[:, 0].cumsum(0) - counts[:, 0]
+        slots = torch.where(need.view(G, T).bool(), rank_in_dest + (row_base - 1).unsqueeze(1),
+                            G * T)
+        send_tok = torch.empty(G * T + 1, dtype=torch.int64, device=dev)
+        send_tok.scatter_(0, slots.reshape(-1), self._token_index(T, 1, dev).repeat(G))
+        send_tok = send_tok[:sum(s_rows)]
+        send_rows = x.to(torch.bfloat16).index_select(0, send_tok)
+        # pair records (row in its destination block, local expert, weight
+        # bits), destination-major and stable in token, then slot
+        order = torch.argsort(dest, stable=True)
+        p_dest = dest[order]
+        recs = torch.stack([rank_in_dest.view(-1)[p_dest * T + tok[order]] - 1,
+                            idx[order] - p_dest * El,
+                            w[order].view(torch.int32).to(torch.int64)], dim=1)
 
         rows = self._exchange(send_rows, s_rows, r_rows)
-        recs = torch.stack([p_row.to(torch.int64), p_exp.to(torch.int64)], dim=1)
         recv_recs = self._exchange(recs, s_pairs, r_pairs)
-        recv_w = self._exchange(p_w, s_pairs, r_pairs)
         # pair rows are relative to the sender's block: add each block's offset
-        row_base = torch.cumsum(torch.tensor([0] + r_rows[:-1], device=dev), 0)
-        src_of_pair = torch.repeat_interleave(torch.arange(G, device=dev),
-                                              torch.tensor(r_pairs, device=dev))
-        pair_row = recv_recs[:, 0] + row_base[src_of_pair]
-        y_rows = self.local_experts_forward(rows, pair_row, recv_recs[:, 1], recv_w)
+        recv_base = recv_c[:, 0].cumsum(0) - recv_c[:, 0]
+        src = torch.repeat_interleave(recv_base, recv_c[:, 1], output_size=sum(r_pairs))
+        pair_w = recv_recs[:, 2].to(torch.int32).view(torch.float32)
+        y_rows = self.local_experts_forward(rows, recv_recs[:, 0] + src, recv_recs[:, 1], pair_w)
 
         back = self._exchange(y_rows.to(torch.bfloat16), r_rows, s_rows)
         out = torch.zeros((T, self.hidden), dtype=torch.float32, device=dev)
-        out.index_add_(0, send_tok[:, 1], back.to(torch.float32))
+        out.index_add_(0, send_tok, back.to(torch.float32))
         self.last_stats = {"rows_sent": int(sum(s_rows)), "pairs_sent": int(sum(s_pairs)),
                            "rows_received": int(sum(r_rows)), "pairs_received": int(sum(r_pairs))}
         return out
