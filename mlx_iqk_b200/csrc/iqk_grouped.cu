@@ -6,7 +6,8 @@
 // (src/mlx_iqk/nn.py:221-238): a full fp16 dequantization of the stacked
 // experts followed by mx.gather_mm over (optionally sorted) indices. Here the
 // weights are never materialised in HBM: each expert's relayout streams are
-// read once per 128-token tile and dequantized tile by tile straight into
+// read once per token tile (at most 64 tokens) and dequantized stage by stage
+// straight into
 // tensor memory, where they are the A operand of tcgen05.mma.
 //
 // Numerics. Activations are scaled per row by a power of two 2^S (so the row
@@ -18,23 +19,29 @@
 // the CPU's float weights. Products are exact and accumulate in f32.
 //
 // Preparation (two launches): a single-block routing kernel counting-sorts
-// the pairs by expert and cuts each expert's run into tiles of at most 128
+// the pairs by expert and cuts each expert's run into tiles of at most 64
 // tokens; a conversion kernel writes each routed pair's scaled, permuted f16
 // activation row in sorted order.
 //
-// GEMM kernel: persistent, one CTA per SM, 12 warps.
-//   warp 0      TMA producer: per 128-weight k-stage, the 128 x 32 B code tile
-//               (32-byte swizzle) and the tile's activation rows (two 64-wide
-//               k atoms in the 128-byte swizzle, 16-row boxes)
-//   warp 1      TMEM owner and MMA issuer (one thread): 8 x M128 N<=128 K16
-//               MMAs per stage, A from TMEM, B from shared memory
-//   warps 4-11  dequantize: two warps per TMEM lane quarter take alternate
-//               stages; each thread expands its row's 128 codes into 64 f16x2
-//               words with byte permutes on a per-group table of the four
-//               alphabet products, and stores them to TMEM (tcgen05.st);
-//               then the epilogue (tcgen05.ld of D, scale, store y)
-// Work items are (tile, 128-row block), expert-major, so CTAs running at the
-// same time share one expert's activation tile in L2.
+// GEMM kernel: persistent, one CTA per SM, 22 warps.
+//   warp 0      TMA producer of the activation stages (128 weights x the
+//               tile's tokens, two 64-wide k atoms, 128-byte swizzle)
+//   warp 1      TMEM owner (allocates 512 columns, frees them at exit)
+//   warps 2-3   scale loaders: per work item, every row's scale streams
+//               packed per 128-weight stage (one table index byte per
+//               group), the row factors and the tile's column table
+//   warps 4-19  dequantization: every stage, warp (q, j, kh) expands k
+//               slice kh of its 32 rows (lane quarter q of row half j) into
+//               f16x2 words with byte permutes on the group's table of the
+//               four alphabet products, and stores them into the stage's
+//               TMEM A buffer (tcgen05.st); then the epilogue (tcgen05.ld of
+//               D, row scale, 2^-S, store y)
+//   warp 20     TMA producer of the 2-bit code chunks (512 weights of every
+//               row of the item, 128-byte swizzle)
+//   warp 21     MMA issuer (one elected lane): per stage RB x 8
+//               M128 N<=64 K16 MMAs, A from TMEM, B from shared memory
+// Work items are (tile, 256- or 128-row block), expert-major, so CTAs running
+// at the same time share one expert's activation tile in L2.
 //
 // Operand order inside each 16-weight block: the TMEM word pair (c, c + 4)
 // of a code word (k = j and 4 + j, then 8 + j and 12 + j) is what one byte
@@ -57,9 +64,9 @@ namespace {
 
 using namespace dev;
 
-constexpr int kThreadsG = 800;                       // 25 warps
+constexpr int kThreadsG = 704;                       // 22 warps
 constexpr int kProducer = 0, kTmemWarp = 1, kLoader0 = 2, kDq0 = 4, kCodeWarp = 20,
-              kIssuer0 = 21;
+              kIssuer = 21;
 constexpr int kStageK = 128;                         // weights per k-stage (8 MMAs of K=16)
 constexpr int kMaxKS = 4096 / kStageK;               // k-stages of the widest row
 constexpr int kCodeK = 512;                          // weights per code load (4 stages)
@@ -67,21 +74,24 @@ constexpr int kCodeBox = kGroupRows * kCodeK / 4;    // 16 KB: 128 rows x 128 B,
 constexpr int kMaxCodeSlots = 4;
 constexpr int kMaxXSlots = 8;
 constexpr int kMinXSlots = 4;
-constexpr int kMaxGroups = 4;
+constexpr int kNumA = 3;  // A buffers in TMEM: the dequant runs up to two stages ahead
 // Work item = one token tile x RB*128 output rows (RB "halves" of 128 rows,
-// RB = 1 or 2). There are 4/RB dequant groups; group h takes the k-stages
-// g = h (mod 4/RB) for all RB halves, and its issuer warp runs their MMAs
-// (RB x 8 per stage, sharing one activation stage) into the group's RB
-// accumulators. TMEM columns, 64 each: accumulators (group h, half j) at
-// 64*(h*RB + j), then the A slots in the same order from column 256 -- 512
-// columns for either RB. Reusing a group's A slots waits on tfree[h], which
-// issuer h commits after each of the group's stages: its next phase needs
-// group h's own next stage, so it is never lapped while awaited.
+// RB = 1 or 2). Every k-stage (128 weights) goes through the same steps: the
+// 16 dequant warps write its A tile (f16, RB halves x 128 rows) into TMEM
+// buffer b = stage mod kNumA -- warp (q, j, kh) its lane quarter q of half j
+// and k slice kh -- and the issuer runs the stage's RB x 8 MMAs into the RB
+// accumulators, in stage order, then commits afree[b]. (One issuer measured
+// faster overall than one per half on B200: the dequantization bounds the
+// kernel, and a second issuer warp takes issue slots from it.) TMEM columns, 64
+// each: accumulator half j at 64*j, A buffer b half j at 64*(RB + b*RB + j):
+// 4*RB*64 <= 512 columns. A warp writes buffer b again for stage g + kNumA
+// only after afree[b] completes for stage g; that phase needs the issuer,
+// which in turn waits for every warp's aready[b] of stage g + kNumA before
+// committing the next phase, so no wait is ever lapped.
 constexpr int kTmemCols = 512;
 constexpr int kTok = 64;                             // tokens per work tile
-constexpr uint32_t kACol = 256;
 // Barriers, the TMEM slot word and the abort flag; then the group tables.
-constexpr int kTabOff = 8 * (2 * kMaxXSlots + 2 * kMaxCodeSlots + 2 * kMaxGroups + 3 + 4) + 16;
+constexpr int kTabOff = 8 * (2 * kMaxXSlots + 2 * kMaxCodeSlots + 2 * kNumA + 3 + 4) + 16;
 constexpr int kTabEntries = 64;  // IQ2_KS: (scale index + 16) | alphabet << 5; IQ2_K: idx + 8 | alpha << 4
 constexpr int kBarBytes = kTabOff + 8 * kTabEntries;
 constexpr int kSmemCap = 227 * 1024;
@@ -128,6 +138,11 @@ __device__ __forceinline__ void expand_word(uint32_t w, uint32_t t01, uint32_t t
     }
 }
 
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
 __device__ __forceinline__ uint4 lds128(uint32_t a) {
     uint4 v;
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
@@ -471,7 +486,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
 grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_map,
                     const __grid_constant__ XMaps x_maps) {
     constexpr int kRows = RB * kGroupRows;    // output rows per work item
-    constexpr int kNG = kMaxGroups / RB;      // dequant groups = issuers
+    constexpr uint32_t kACol = RB * 64u;      // first A-buffer column (after the accumulators)
     constexpr int kCodeSlot = RB * kCodeBox;  // codes of one 512-weight chunk, all rows
     extern __shared__ char smem_raw[];
     char *smem = smem_raw + ((1024u - (saddr(smem_raw) & 1023u)) & 1023u);
@@ -487,9 +502,9 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
     uint64_t *sdone = xfull + kMaxXSlots;
     uint64_t *cfull = sdone + kMaxXSlots;
     uint64_t *cempty = cfull + kMaxCodeSlots;
-    uint64_t *aready = cempty + kMaxCodeSlots;
-    uint64_t *tfree = aready + kMaxGroups;  // group h's A slots free again
-    uint64_t *dfull = tfree + kMaxGroups;
+    uint64_t *aready = cempty + kMaxCodeSlots;  // [kNumA] A buffer written (16 warps)
+    uint64_t *afree = aready + kNumA;           // [kNumA] A buffer read by its MMAs
+    uint64_t *dfull = afree + kNumA;
     uint64_t *dempty = dfull + 1;
     uint64_t *drain = dempty + 1;
     uint64_t *sfull = drain + 1;   // [2]
@@ -518,13 +533,13 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
             bar_init(&cfull[i], 1);
             bar_init(&cempty[i], 16);
         }
-        for (int i = 0; i < kNG; ++i) {
-            bar_init(&aready[i], 4 * RB);
-            bar_init(&tfree[i], 1);
+        for (int i = 0; i < kNumA; ++i) {
+            bar_init(&aready[i], 16);
+            bar_init(&afree[i], 1);
         }
-        bar_init(dfull, kNG);
+        bar_init(dfull, 1);
         bar_init(dempty, 16);
-        bar_init(drain, kNG);
+        bar_init(drain, 1);
         for (int i = 0; i < 2; ++i) {
             bar_init(&sfull[i], 64);
             bar_init(&sempty[i], 16);
@@ -629,64 +644,58 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
             }
         }
         __syncwarp();
-    } else if (warp >= kIssuer0) {
-        // MMA issuer of group h: the stages g = h (mod kNG), RB x 8 MMAs each.
-        // The whole warp runs the loop converged; one elected lane issues.
-        const int h = warp - kIssuer0;
-        if (h < kNG) {
-            int g = 0, item_i = 0;
-            bool ok = true;
-            for (int64_t it = blockIdx.x; ok && it < items && !*abort_flag;
-                 it += gridDim.x, ++item_i) {
-                const int4 tl = tiles[it / a.rblocks];
-                const int npad = (tl.z + 15) & ~15;
-                const uint32_t idesc = idesc_f16(kGroupRows, npad);
-                // the accumulators are free once the previous item's epilogue read them
-                if (item_i > 0 && !bar_wait(dempty, (uint32_t)(item_i - 1) & 1u, abort_flag)) {
+    } else if (warp == kIssuer) {
+        // The MMA issuer: per stage, RB x 8 MMAs (one activation stage, one A
+        // buffer) into the RB accumulators, in stage order. The whole warp
+        // runs the loop converged; one elected lane issues.
+        int g = 0, item_i = 0;
+        bool ok = true;
+        for (int64_t it = blockIdx.x; ok && it < items && !*abort_flag;
+             it += gridDim.x, ++item_i) {
+            const int4 tl = tiles[it / a.rblocks];
+            const int npad = (tl.z + 15) & ~15;
+            const uint32_t idesc = idesc_f16(kGroupRows, npad);
+            // the accumulators are free once the previous item's epilogue read them
+            if (item_i > 0 && !bar_wait(dempty, (uint32_t)(item_i - 1) & 1u, abort_flag)) {
+                ok = false;
+                break;
+            }
+            for (int ks = 0; ks < KS; ++ks, ++g) {
+                const int xs = g % XS, b = g % kNumA;
+                if (!bar_wait(&xfull[xs], (uint32_t)(g / XS) & 1u, abort_flag) ||
+                    !bar_wait(&aready[b], (uint32_t)(g / kNumA) & 1u, abort_flag)) {
                     ok = false;
                     break;
                 }
-                bool first = true;
-                for (int ks = 0; ks < KS; ++ks, ++g) {
-                    if (g % kNG != h) continue;
-                    const int xs = g % XS;
-                    if (!bar_wait(&xfull[xs], (uint32_t)(g / XS) & 1u, abort_flag) ||
-                        !bar_wait(&aready[h], (uint32_t)(g / kNG) & 1u, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t st = smem_u + G.x + xs * x_slot_bytes(cap);
-                    // elect.sync needs the whole warp converged: one lane issues.
-                    __syncwarp();
-                    if (elect_one()) {
+                tc_fence_after();
+                const uint32_t st = smem_u + G.x + xs * x_slot_bytes(cap);
+                // elect.sync needs the whole warp converged: one lane issues.
+                __syncwarp();
+                if (elect_one()) {
 #pragma unroll
-                        for (int kk = 0; kk < 8; ++kk) {
-                            const uint64_t bdesc = sw128_desc(st + (kk >> 2) * xatom + (kk & 3) * 32);
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint64_t bdesc = sw128_desc(st + (kk >> 2) * xatom + (kk & 3) * 32);
 #pragma unroll
-                            for (int j = 0; j < RB; ++j) {
-                                const uint32_t slot = (uint32_t)(h * RB + j) * 64u;
-                                tc_mma_ts(tmem + slot, tmem + kACol + slot + kk * 8, bdesc, idesc,
-                                          (first && kk == 0) ? 0u : 1u);
-                            }
-                        }
-                        tc_commit(&sdone[xs]);
-                        tc_commit(&tfree[h]);
+                        for (int j = 0; j < RB; ++j)
+                            tc_mma_ts(tmem + (uint32_t)j * 64u,
+                                      tmem + kACol + (uint32_t)(b * RB + j) * 64u + kk * 8, bdesc,
+                                      idesc, (ks == 0 && kk == 0) ? 0u : 1u);
                     }
-                    __syncwarp();
-                    first = false;
+                    tc_commit(&sdone[xs]);
+                    tc_commit(&afree[b]);
                 }
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) break;
-                if (elect_one()) tc_commit(dfull);
                 __syncwarp();
             }
-            if (!ok && lane == 0) give_up();
-            __syncwarp();
-            // Every MMA issued must finish before tensor memory is freed.
-            if (elect_one()) tc_commit(drain);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            if (elect_one()) tc_commit(dfull);
             __syncwarp();
         }
+        if (!ok && lane == 0) give_up();
+        __syncwarp();
+        // Every MMA issued must finish before tensor memory is freed.
+        if (elect_one()) tc_commit(drain);
+        __syncwarp();
     } else if (warp >= kLoader0 && warp < kDq0) {
         const int t = threadIdx.x - 32 * kLoader0;  // 0..63
         int item_i = 0;
@@ -706,14 +715,16 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
             bar_arrive(&sfull[buf]);
         }
     } else if (warp >= kDq0 && warp < kCodeWarp) {
-        // dequant warp: TMEM lane quarter q, group h, row half j
+        // dequant warp (q, j, kh): TMEM lane quarter q (fixed by the warp's
+        // index mod 4), row half j, and k slice kh -- WPW of the stage's 8
+        // code words (16 weights each) -- of every stage.
+        constexpr int KH = 4 / RB, WPW = 8 / KH;
         const int dq = warp - kDq0;
         const int q = warp & 3;
-        const int h = (dq >> 2) % kNG, j = (dq >> 2) / kNG;
+        const int j = (dq >> 2) % RB, kh = (dq >> 2) / RB;
         const int rloc = kGroupRows * j + 32 * q + lane;  // item-local row
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         const uint32_t rsw = (uint32_t)(rloc & 7);  // 128-byte swizzle of this code row
-        const uint32_t aslot = (uint32_t)(h * RB + j) * 64u;
         int g = 0, item_i = 0;
         for (int64_t it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++item_i) {
             const int4 tl = tiles[it / a.rblocks];
@@ -733,48 +744,57 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
             const int32_t *colp = reinterpret_cast<const int32_t *>(rsc + kRows);
             const float *colf = rsc + kRows + kTok;
             const float rscale = rsc[rloc];
+            bool ok = true;
             for (int ks = 0; ks < KS; ++ks, ++g) {
-                const int chunk = g >> 2, cs = chunk % CS, sub = g & 3;
-                if (g % kNG != h) {
-                    // still release the code chunk once this warp's stages in it are done
-                    continue;
-                }
+                const int chunk = g >> 2, cs = chunk % CS, sub = g & 3, ab = g % kNumA;
                 const uint32_t s0 = sc[ks * kRows + rloc];
                 const uint32_t s1 = scale_words(MEMBER) == 2 ? sc[(KS + ks) * kRows + rloc] : 0u;
                 if (!bar_wait(&cfull[cs], (uint32_t)(chunk / CS) & 1u, abort_flag)) {
-                    give_up();
+                    ok = false;
                     break;
                 }
-                // this stage's 32 code bytes: 16-byte chunks 2*sub, 2*sub+1 of the row
+                // this warp's code words of the stage: word w of the stage is
+                // word w % 4 of 16-byte chunk 2*sub + w / 4 of the row
                 const uint32_t code_u = smem_u + G.code + cs * kCodeSlot + rloc * 128;
-                const uint4 c0 = lds128(code_u + (((uint32_t)(2 * sub) ^ rsw) << 4));
-                const uint4 c1 = lds128(code_u + (((uint32_t)(2 * sub + 1) ^ rsw) << 4));
+                uint32_t words[WPW];
+                if (WPW == 4) {
+                    const uint4 c = lds128(code_u + (((uint32_t)(2 * sub + kh) ^ rsw) << 4));
+                    words[0] = c.x;
+                    words[1] = c.y;
+                    words[2 % WPW] = c.z;
+                    words[3 % WPW] = c.w;
+                } else {
+                    const uint2 c = lds64(code_u + (((uint32_t)(2 * sub + (kh >> 1)) ^ rsw) << 4) +
+                                          (uint32_t)(kh & 1) * 8u);
+                    words[0] = c.x;
+                    words[1] = c.y;
+                }
                 __syncwarp();
-                // the warp's last stage of this chunk releases it (RB = 1: one
-                // stage per chunk; RB = 2: stages sub = h and h + 2)
-                if (lane == 0 && sub + kNG >= 4) bar_arrive(&cempty[cs]);
-                // the group's A slots were last read by its previous stage
-                if (g >= kNG &&
-                    !bar_wait(&tfree[h], ((uint32_t)(g / kNG) & 1u) ^ 1u, abort_flag)) {
-                    give_up();
+                // every warp reads every stage: the chunk's last stage releases it
+                if (lane == 0 && sub == 3) bar_arrive(&cempty[cs]);
+                // A buffer ab was last read by the MMAs of stage g - kNumA
+                if (g >= kNumA &&
+                    !bar_wait(&afree[ab], ((uint32_t)(g / kNumA) & 1u) ^ 1u, abort_flag)) {
+                    ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-                const uint32_t taddr = tmem + lane_base + kACol + aslot;
+                const uint32_t taddr = tmem + lane_base + kACol + (uint32_t)(ab * RB + j) * 64u +
+                                       (uint32_t)(kh * WPW) * 8u;
                 // IQ2_K: the super-block scale, f16 in both halves
                 const uint32_t dsb2 = MEMBER == IQK_IQ2_K ? (s1 >> 16) * 0x10001u : 0u;
                 uint32_t t01 = 0, t23 = 0;
 #pragma unroll
-                for (int wd = 0; wd < 8; ++wd) {
+                for (int wd = 0; wd < WPW; ++wd) {
+                    const int wg = kh * WPW + wd;  // word of the stage
                     if (MEMBER == IQK_IQ2_KS) {
                         if ((wd & 1) == 0) {  // one 32-weight group per two words
-                            const uint2 t = gtab[prmt(s0, 0u, 0x4440u + (uint32_t)(wd >> 1))];
+                            const uint2 t = gtab[prmt(s0, 0u, 0x4440u + (uint32_t)(wg >> 1))];
                             t01 = t.x;
                             t23 = t.y;
                         }
                     } else {
-                        const uint32_t ti = ((s0 >> (4 * wd)) & 15u) | (((s1 >> wd) & 1u) << 4);
+                        const uint32_t ti = ((s0 >> (4 * wg)) & 15u) | (((s1 >> wg) & 1u) << 4);
                         const uint2 t = gtab[ti];
                         t01 = hmul2_bits(t.x, dsb2);
                         t23 = hmul2_bits(t.y, dsb2);
@@ -786,34 +806,30 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
                 tc_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) bar_arrive(&aready[h]);
+                if (lane == 0) bar_arrive(&aready[ab]);
+            }
+            if (!ok) {
+                give_up();
+                break;
             }
             if (*abort_flag) break;
             // Epilogue: D rows are this thread's output row, columns the tile's
-            // tokens; the kNG groups' accumulators of this half are summed in order.
+            // tokens; the KH warps of a (quarter, half) split the columns.
             if (!bar_wait(dfull, (uint32_t)item_i & 1u, abort_flag)) {
                 give_up();
                 break;
             }
             tc_fence_after();
-            for (int c = 8 * h; c < npad; c += 8 * kNG) {
-                float sum[8];
-#pragma unroll
-                for (int k = 0; k < 8; ++k) sum[k] = 0.f;
-#pragma unroll
-                for (int hh = 0; hh < kNG; ++hh) {
-                    uint32_t d[8];
-                    tmem_ld8(tmem + lane_base + (uint32_t)(hh * RB + j) * 64u + c, d);
-                    tc_wait_ld();
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) sum[k] += __uint_as_float(d[k]);
-                }
+            for (int c = 8 * kh; c < npad; c += 8 * KH) {
+                uint32_t d[8];
+                tmem_ld8(tmem + lane_base + (uint32_t)j * 64u + c, d);
+                tc_wait_ld();
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
                     const int col = c + k;
                     if (col < tl.z && row_ok) {
                         const int64_t o = (int64_t)colp[col] * out + rlocal;
-                        const float v = sum[k] * rscale * colf[col];
+                        const float v = __uint_as_float(d[k]) * rscale * colf[col];
                         if (a.y_dtype == IQK_F32) store_out<float>(a.y, o, v);
                         else if (a.y_dtype == IQK_F16) store_out<__half>(a.y, o, v);
                         else store_out<__nv_bfloat16>(a.y, o, v);

@@ -15,7 +15,7 @@ namespace iqk {
 struct GroupedLayout {
     size_t hdr, order, pscale, tiles, xs;
     int64_t max_tiles;
-    int tok_cap;  // tokens per work tile: 64 when experts average <= 80 pairs, else 128
+    int tok_cap;  // tokens per work tile (64: the MMA N and the accumulator width)
     size_t total;
 };
 
