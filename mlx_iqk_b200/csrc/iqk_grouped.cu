@@ -7,16 +7,16 @@
 // experts followed by mx.gather_mm over (optionally sorted) indices. Here the
 // weights are never materialised in HBM: each expert's relayout streams are
 // read once per token tile (at most 64 tokens) and dequantized stage by stage
-// straight into
-// tensor memory, where they are the A operand of tcgen05.mma.
+// straight into tensor memory, where they are the A operand of tcgen05.mma.
 //
 // Numerics. Activations are scaled per row by a power of two 2^S (so the row
 // maximum lies in [2^14, 2^15)) and converted to f16 -- exact for bf16 input.
 // IQ2_KS weights enter the MMA as the exact small integers idx * value
 // (|.| <= 496, exact in f16); the row's f16 scale is applied in the epilogue.
-// IQ2_K weights enter as f16(d_sb * 2^-E * idx) * value with E the row's
-// largest super-block exponent, so only two f16 roundings separate them from
-// the CPU's float weights. Products are exact and accumulate in f32.
+// IQ2_K weights enter as (idx * value) * f16(d_sb * 2^-E): the integer
+// product is exact and one f16 multiply applies the super-block scale (E, the
+// row's largest super-block exponent, goes back in the epilogue), so one f16
+// rounding separates them from the CPU's float weights. Products are exact and accumulate in f32.
 //
 // Preparation (two launches): a single-block routing kernel counting-sorts
 // the pairs by expert and cuts each expert's run into tiles of at most 64
