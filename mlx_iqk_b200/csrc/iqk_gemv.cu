@@ -71,6 +71,18 @@ __device__ __forceinline__ void mma_s8(int32_t d[4], const uint32_t a[4], uint32
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
 }
 
+// Programmatic dependent launch (PTX griddepcontrol). Both decode kernels are
+// launched with programmatic stream serialization: a kernel may start while
+// the previous kernel of the stream is still draining, does its shared-memory
+// set-up, then waits for that kernel's completion (and its memory) before it
+// reads or writes any global memory, and at once lets the next kernel start.
+__device__ __forceinline__ void grid_dep_wait() {
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_launch() {
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
 // ------------------------------------------------------------- prep kernel
 
 // One block per activation row: digit planes, block sums and the exponent.
@@ -282,6 +294,8 @@ __global__ void __launch_bounds__(256)
 gemv_prep_kernel(const XT *__restrict__ x, int n, int x_rows, const int32_t *__restrict__ sel,
                  const int32_t *__restrict__ tok, int pairs, int num_experts, GemvLayout L,
                  char *__restrict__ ws) {
+    grid_dep_wait();
+    grid_dep_launch();
     if ((int)blockIdx.x < x_rows) {
         prep_row<XT>(x, n, blockIdx.x, L, ws);
     } else {
@@ -319,8 +333,8 @@ template <int MEMBER> struct Geo {
 
 // The scale streams of one member at width N: bytes per row of stream si
 // (1 .. kCount-1, component order after qs) and each stream's offset inside
-// an item's scale slot (kItemRows rows of every stream, back to back).
-template <int MEMBER, int N> struct Streams {
+// an item's scale slot (ROWS rows of every stream, back to back).
+template <int MEMBER, int N, int ROWS = kItemRows> struct Streams {
     static constexpr int kCount = MEMBER == IQK_IQ2_KS ? 5 : MEMBER == IQK_IQ2_K ? 4 : 3;
     static constexpr __host__ __device__ int b(int si) {
         return MEMBER == IQK_IQ2_KS ? (si == 1 ? N / 64 : si == 4 ? 2 : N / 256)
@@ -328,29 +342,41 @@ template <int MEMBER, int N> struct Streams {
                                      : (si == 1 ? N / 16 : 2);
     }
     static constexpr __host__ __device__ int off(int si) {
-        return si <= 1 ? 0 : off(si - 1) + kItemRows * b(si - 1);
+        return si <= 1 ? 0 : off(si - 1) + ROWS * b(si - 1);
     }
     static constexpr int kSlot = off(kCount);
 };
 
-// Stage: [weights: kConsumers TMA boxes][activation slice], released every
-// round. An item's scale streams sit in one of two scale slots for the whole
-// item.
-template <int MEMBER> __host__ __device__ constexpr int stage_bytes() {
-    return (Geo<MEMBER>::kWBytes + Geo<MEMBER>::kXBlock + 1023) / 1024 * 1024;
+// Stage: [weights: kConsumers TMA boxes][activation slices of KQ chunks],
+// released every round. An item's scale streams sit in one of two scale
+// slots for the whole item.
+template <int MEMBER, int KQ = 1> __host__ __device__ constexpr int stage_bytes() {
+    return (Geo<MEMBER>::kWBytes + KQ * Geo<MEMBER>::kXBlock + 1023) / 1024 * 1024;
 }
-template <int MEMBER, int N> __host__ __device__ constexpr int sslot_bytes() {
-    return (Streams<MEMBER, N>::kSlot + 127) / 128 * 128;
+template <int MEMBER, int N, int ROWS = kItemRows> __host__ __device__ constexpr int sslot_bytes() {
+    return (Streams<MEMBER, N, ROWS>::kSlot + 127) / 128 * 128;
 }
 
-template <int MEMBER, int N> __host__ __device__ constexpr int gemv_smem_bytes() {
+// Two item shapes. Wide: 64 rows x all of k, each compute warp 16 rows x all
+// of k. Narrow (few items, e.g. one token): 16 rows x all of k, the four
+// compute warps take a quarter of every round's k each and their exact
+// partial sums meet in shared memory -- four times the items, so small
+// decode batches still reach every SM.
+template <int MEMBER, bool NARROW> struct Shape {
+    static constexpr int kRows = NARROW ? 16 : kItemRows;     // rows per item
+    static constexpr int KQ = NARROW ? kConsumers : 1;        // k chunks per round
+    static constexpr int kStages = NARROW ? 3 : Geo<MEMBER>::kStages;
+    static constexpr int kRedBytes = NARROW ? 2 * kConsumers * 32 * 16 : 0;
+};
+
+template <int MEMBER, int N, bool NARROW> __host__ __device__ constexpr int gemv_smem_bytes() {
     using G = Geo<MEMBER>;
-    constexpr int kStages = G::kStages;
-    return 1024 /* alignment slack */ + kStages * stage_bytes<MEMBER>() +
-           2 * sslot_bytes<MEMBER, N>() + 2 * kConsumers * G::kMetaBytes +
+    using SH = Shape<MEMBER, NARROW>;
+    return 1024 /* alignment slack */ + SH::kStages * stage_bytes<MEMBER, SH::KQ>() +
+           2 * sslot_bytes<MEMBER, N, SH::kRows>() + 2 * kConsumers * G::kMetaBytes +
            kMaxTiles * (int)sizeof(TileRef) + (MEMBER == IQK_IQ1_S_R4 ? 4096 : 0) +
-           (MEMBER == IQK_IQ2_K ? 256 : 0) + 2 * kStages * 8 + 4 * 8 + 16 +
-           kPairsPerRound * 192;
+           (MEMBER == IQK_IQ2_K ? 256 : 0) + 2 * SH::kStages * 8 + 8 * 8 + 16 +
+           kPairsPerRound * 192 + SH::kRedBytes;
 }
 
 struct GemvArgs {
@@ -467,16 +493,18 @@ __device__ __forceinline__ double pow2(int k) {
     return __longlong_as_double((long long)(k + 1023) << 52);
 }
 
-template <int MEMBER, int N>
+template <int MEMBER, int N, bool NARROW>
 __global__ void __launch_bounds__(kThreads, Geo<MEMBER>::kMinBlocks)
 gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     extern __shared__ char smem_raw[];
     using G = Geo<MEMBER>;
-    using SS = Streams<MEMBER, N>;
-    constexpr int kStages = G::kStages;
-    constexpr int CPW = N / kChunkK;  // rounds per item: 8 (n=4096) or 4 (2048)
-    constexpr int SSB = sslot_bytes<MEMBER, N>();
-    constexpr int STB = stage_bytes<MEMBER>();
+    using SH = Shape<MEMBER, NARROW>;
+    constexpr int kRows = SH::kRows, KQ = SH::KQ, kStages = SH::kStages;
+    using SS = Streams<MEMBER, N, kRows>;
+    constexpr int CPW = N / kChunkK;  // 512-weight chunks per row: 8 (n=4096) or 4 (2048)
+    constexpr int RPI = CPW / KQ;     // rounds per item
+    constexpr int SSB = sslot_bytes<MEMBER, N, kRows>();
+    constexpr int STB = stage_bytes<MEMBER, KQ>();
     char *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int out = a.out_features;
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -493,8 +521,11 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     uint64_t *empty = full + kStages;
     uint64_t *sfull = empty + kStages;  // [2] item scale slots
     uint64_t *sempty = sfull + 2;       // [2]
-    int *abort_flag = reinterpret_cast<int *>(sempty + 2);
+    uint64_t *rfull = sempty + 2;       // [2] narrow: warps 1-3 handed in their partials
+    uint64_t *rempty = rfull + 2;       // [2] narrow: warp 0 read them
+    int *abort_flag = reinterpret_cast<int *>(rempty + 2);
     char *zeros = reinterpret_cast<char *>(abort_flag) + 16;  // kPairsPerRound * 192 zero bytes
+    char *red = zeros + kPairsPerRound * 192;  // narrow: [2][kConsumers][32 lanes][16 B]
 
     const int32_t *hdr = reinterpret_cast<const int32_t *>(a.ws + a.L.hdr);
     const int32_t *order = reinterpret_cast<const int32_t *>(a.ws + a.L.order);
@@ -503,32 +534,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     const char *xbuf = a.ws + a.L.xbuf;
     const int64_t xrow = a.L.xrow_bytes;
 
-    const int ntiles = hdr[3];
-    const int rblocks = (out + kItemRows - 1) / kItemRows;
-    const int items = ntiles * rblocks;  // < 2^31 (checked by the C ABI)
-
-    if (blockIdx.x == 0) {
-        // zero the outputs of unroutable pairs (the tail of order)
-        const int elem = a.y_dtype == IQK_F32 ? 4 : 2;
-        const int row_words = out * elem / 4;
-        for (int q = ntiles; q < a.pairs; ++q) {
-            int32_t *yr = reinterpret_cast<int32_t *>(static_cast<char *>(a.y) +
-                                                      (int64_t)order[q] * out * elem);
-            for (int i = tid; i < row_words; i += blockDim.x) yr[i] = 0;
-        }
-    }
-    const int i0 = (int)((int64_t)items * blockIdx.x / gridDim.x);
-    const int i1 = (int)((int64_t)items * (blockIdx.x + 1) / gridDim.x);
-    if (i0 >= i1) return;  // uniform over the CTA
-    const int t0 = i0 / rblocks, t1 = (i1 - 1) / rblocks;
-    const bool cached = t1 - t0 < kMaxTiles;
-    auto load_tile = [&](int t) -> TileRef {
-        TileRef r = tlist[t];
-        r.sh0 = xscale[r.tok0];
-        return r;
-    };
-    if (cached)
-        for (int t = tid; t <= t1 - t0; t += blockDim.x) tcache[t] = load_tile(t0 + t);
+    // Shared-memory set-up first: it overlaps the previous kernel's drain.
     if (MEMBER == IQK_IQ1_S_R4)
         for (int i = tid; i < 2048; i += blockDim.x) grid[i] = g_iq1s_grid[i];
     if (MEMBER == IQK_IQ2_K && tid < 32) {
@@ -556,10 +562,42 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
         for (int s = 0; s < 2; ++s) {
             mbar_init(&sfull[s], 1);
             mbar_init(&sempty[s], kConsumers);
+            mbar_init(&rfull[s], kConsumers - 1);
+            mbar_init(&rempty[s], 1);
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
+    // From here on the workspace and the outputs: the previous kernel is done.
+    grid_dep_wait();
+    grid_dep_launch();
+
+    const int ntiles = hdr[3];
+    const int rblocks = (out + kRows - 1) / kRows;
+    const int items = ntiles * rblocks;  // < 2^31 (checked by the C ABI)
+
+    if (blockIdx.x == 0) {
+        // zero the outputs of unroutable pairs (the tail of order)
+        const int elem = a.y_dtype == IQK_F32 ? 4 : 2;
+        const int row_words = out * elem / 4;
+        for (int q = ntiles; q < a.pairs; ++q) {
+            int32_t *yr = reinterpret_cast<int32_t *>(static_cast<char *>(a.y) +
+                                                      (int64_t)order[q] * out * elem);
+            for (int i = tid; i < row_words; i += blockDim.x) yr[i] = 0;
+        }
+    }
+    const int i0 = (int)((int64_t)items * blockIdx.x / gridDim.x);
+    const int i1 = (int)((int64_t)items * (blockIdx.x + 1) / gridDim.x);
+    if (i0 >= i1) return;  // uniform over the CTA
+    const int t0 = i0 / rblocks, t1 = (i1 - 1) / rblocks;
+    const bool cached = t1 - t0 < kMaxTiles;
+    auto load_tile = [&](int t) -> TileRef {
+        TileRef r = tlist[t];
+        r.sh0 = xscale[r.tok0];
+        return r;
+    };
+    if (cached)
+        for (int t = tid; t <= t1 - t0; t += blockDim.x) tcache[t] = load_tile(t0 + t);
     __syncthreads();
     auto tile_of = [&](int t) -> TileRef { return cached ? tcache[t - t0] : load_tile(t); };
     const int n_items = i1 - i0;
@@ -574,43 +612,48 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
         const int s_rowb = si ? SS::b(si) : 0, s_off = si ? SS::off(si) : 0;
         for (int o = 0; o < n_items && ok; ++o) {
             const TileRef T = tile_of(ti);
-            const int r0 = rb * kItemRows;
-            const int rows_valid = min(kItemRows, out - r0);
+            const int r0 = rb * kRows;
+            const int rows_valid = min(kRows, out - r0);
             // the item's scale streams (all rows, all of k) into scale slot o % 2
             const int ss = o & 1;
             if (o >= 2 && !mbar_wait(&sempty[ss], ((o >> 1) & 1) ^ 1)) {
                 ok = false;
                 break;
             }
-            if (lane == 0) mbar_arrive_expect_tx(&sfull[ss], (uint32_t)(rows_valid * (SS::kSlot / kItemRows)));
+            if (lane == 0) mbar_arrive_expect_tx(&sfull[ss], (uint32_t)(rows_valid * (SS::kSlot / kRows)));
             __syncwarp();
             if (si)
                 bulk_load(sslots + ss * SSB + s_off,
                           static_cast<const char *>(a.s[si]) + ((int64_t)T.e * out + r0) * s_rowb,
                           (uint32_t)(rows_valid * s_rowb), &sfull[ss]);
             sissued = o + 1;
-            const int wrow = T.e * out + r0 + 16 * lane;
+            // wide: warp w's box is rows 16w.., chunk r; narrow: all warps the
+            // item's 16 rows, warp w chunk KQ*r + w
+            const int wrow = T.e * out + r0 + (NARROW ? 0 : 16 * lane);
             const char *xb = xbuf + T.tok0 * xrow;
-            for (int r = 0; r < CPW; ++r) {
-                const int j = o * CPW + r;
+            for (int r = 0; r < RPI; ++r) {
+                const int j = o * RPI + r;
                 const int slot = j % kStages;
                 if (j >= kStages && !mbar_wait(&empty[slot], ((j / kStages) & 1) ^ 1)) {
                     ok = false;
                     break;
                 }
                 char *st = stages + slot * STB;
-                if (lane == 0) mbar_arrive_expect_tx(&full[slot], (uint32_t)(G::kWBytes + G::kXBlock));
+                if (lane == 0) mbar_arrive_expect_tx(&full[slot], (uint32_t)(G::kWBytes + KQ * G::kXBlock));
                 __syncwarp();
                 if (lane < kConsumers) {
                     // weights: one 16-row x kRowChunk-byte box per compute warp
-                    tma_load_2d(st + lane * G::kWBox, &qs_map, r * G::kRowChunk, wrow, &full[slot]);
+                    tma_load_2d(st + lane * G::kWBox, &qs_map,
+                                (KQ * r + (NARROW ? lane : 0)) * G::kRowChunk, wrow, &full[slot]);
                 } else if (lane == kConsumers) {
-                    // activation digit planes (+ IQ1 block sums) of this round's k range
+                    // activation digit planes (+ IQ1 block sums) of this round's
+                    // KQ chunks: contiguous in the prepared row
                     char *xs = st + G::kWBytes;
-                    bulk_load(xs, xb + (int64_t)r * G::kXPlanes, G::kXPlanes, &full[slot]);
+                    bulk_load(xs, xb + (int64_t)r * KQ * G::kXPlanes, KQ * G::kXPlanes, &full[slot]);
                     if (G::kXSums)
-                        bulk_load(xs + G::kXPlanes, xb + 3 * (int64_t)N + (int64_t)r * G::kXSums,
-                                  G::kXSums, &full[slot]);
+                        bulk_load(xs + KQ * G::kXPlanes,
+                                  xb + 3 * (int64_t)N + (int64_t)r * KQ * G::kXSums,
+                                  KQ * G::kXSums, &full[slot]);
                 }
                 issued = j + 1;
             }
@@ -635,7 +678,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
 
     // ===================== compute warps
     const int g = lane >> 2, tig = lane & 3;
-    const int rt = wid;  // this warp's 16-row tile of the item
+    const int rbase = NARROW ? 0 : 16 * wid;  // first item-local row of this warp
     const uint32_t meta_u = smem_u32(metas + wid * 2 * G::kMetaBytes);  // two round buffers
     const int side = tig >> 1;             // which 32-weight group of an MMA pair
     int bplane;                            // activation plane of B column g (or -1)
@@ -651,7 +694,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     const uint32_t m30 = a.one << 30;  // mulhi(x, m30) == x >> 2
     // metadata lanes: (mg, mq) owns row pair (mg, mg + 8) and 128 weights a round
     const int mg = lane & 7, mq = lane >> 3;
-    const int mra = 16 * rt + mg;  // item-local row (and mra + 8)
+    const int mra = rbase + mg;  // item-local row (and mra + 8)
     // IQ2_KS group bits of (mg, mq) sit at bit msh of the sch / sex bytes
     const uint32_t msh = (uint32_t)(mq & 1) * 4u;
     const uint32_t hmask = 0xFu << msh;
@@ -661,12 +704,14 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
 
     // Group metadata of round r (this warp's 16 rows x 512 weights) into the
     // metadata buffer at mb.
-    auto build_meta = [&](const char *sd, int r, uint32_t mb) {
+    // this warp's 512-weight chunk of round r
+    auto chunk_of = [&](int r) { return KQ * r + (NARROW ? wid : 0); };
+    auto build_meta = [&](const char *sd, int c, uint32_t mb) {
         if (MEMBER == IQK_IQ2_KS) {
             // Four groups of rows mra and mra + 8 at once, one byte per
             // group: scale index (low nibble | high bit << 4) and the
             // alphabet mask (0x44 when the group uses the second one).
-            const int s0 = r * 16 + mq * 4;  // first of 4 groups (2 pairs)
+            const int s0 = c * 16 + mq * 4;  // first of 4 groups (2 pairs)
             const uint8_t *scl = reinterpret_cast<const uint8_t *>(sd);
             const uint8_t *sch = scl + SS::off(2) + (s0 >> 3);
             const uint8_t *sex = scl + SS::off(3) + (s0 >> 3);
@@ -691,7 +736,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                         (uint32_t)ib);
             }
         } else if (MEMBER == IQK_IQ2_K) {
-            const int b0 = r * 32 + mq * 8;  // first of 8 sub-blocks (2 pairs)
+            const int b0 = c * 32 + mq * 8;  // first of 8 sub-blocks (2 pairs)
             const uint8_t *scl = reinterpret_cast<const uint8_t *>(sd);
             const uint8_t *sex = scl + SS::off(2) + (b0 >> 3);
             scl += b0 >> 1;
@@ -707,7 +752,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                 st_s128(mb + pr * 512 + (mg * 4 + wd) * 16, ta.x, tb.x, ta.y, tb.y);
             }
         } else {
-            const int s0 = r * 16 + mq * 4;  // first of 4 blocks (2 pairs)
+            const int s0 = c * 16 + mq * 4;  // first of 4 blocks (2 pairs)
             const uint16_t *qh = reinterpret_cast<const uint16_t *>(sd) + s0;
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
@@ -724,8 +769,8 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     int ti = i0 / rblocks, rb = i0 % rblocks;
     for (int o = 0; o < n_items; ++o) {
         const TileRef T = tile_of(ti);
-        const int r0 = rb * kItemRows;
-        const bool live = 16 * rt < out - r0;  // this warp's row tile exists
+        const int r0 = rb * kRows;
+        const bool live = NARROW || rbase < out - r0;  // this warp's row tile exists
         const char *sd = sslots + (o & 1) * SSB;
         // the item's scale streams
         if (!mbar_wait(&sfull[o & 1], (o >> 1) & 1)) {
@@ -736,15 +781,15 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
             break;
         }
         if (*(volatile int *)abort_flag) break;
-        if (live) build_meta(sd, 0, meta_u);
+        if (live) build_meta(sd, chunk_of(0), meta_u);
         __syncwarp();
         int32_t tot[4] = {0, 0, 0, 0};
         int32_t acc1[4] = {0, 0, 0, 0}, acc2[4] = {0, 0, 0, 0};  // IQ2_K super-block sums
         double dacc[2] = {0.0, 0.0};                              // IQ2_K: rows g, g+8
         bool ok = true;
 #pragma unroll 1
-        for (int r = 0; r < CPW; ++r) {
-            const int j = o * CPW + r;
+        for (int r = 0; r < RPI; ++r) {
+            const int j = o * RPI + r;
             const int slot = j % kStages;
             if (!mbar_wait(&full[slot], (j / kStages) & 1)) {
                 ok = false;
@@ -755,7 +800,10 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                 // ---- 8 MMA pairs, all shared-memory addresses 32-bit and the
                 // per-pair offsets compile-time immediates.
                 const uint32_t wb_u = smem_u32(st + wid * G::kWBox);
-                const uint32_t xs_u = smem_u32(st + G::kWBytes);
+                // this warp's chunk: activation planes, and (IQ1) block sums
+                const uint32_t xs_u = smem_u32(st + G::kWBytes + (NARROW ? wid * G::kXPlanes : 0));
+                const uint32_t xsum_u = smem_u32(st + G::kWBytes + KQ * G::kXPlanes +
+                                                 (NARROW ? wid * G::kXSums : 0));
                 // B: live lanes read their plane's 16 bytes; the others a zero block
                 const uint32_t xl_u = bplane >= 0 ? xs_u + tig * 48 + bplane * 16 : zero_u;
                 const uint32_t mrow = meta_u + (r & 1) * G::kMetaBytes + moff;
@@ -820,14 +868,14 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                         if ((pr & 3) == 3) {
                             // end of a 256-weight super-block: fold in its fp16 scale.
                             // Lane tig 0 holds planes 0, 1 (cols 0, 1), tig 1 plane 2.
-                            const int sbi = (r * kChunkK + pr * 64) >> 8;
+                            const int sbi = (chunk_of(r) * kChunkK + pr * 64) >> 8;
                             const uint16_t *dvp = reinterpret_cast<const uint16_t *>(sd + SS::off(3));
                             const int32_t u0 = acc1[0] + 4 * acc2[0], u1 = acc1[1] + 4 * acc2[1];
                             const int32_t u2 = acc1[2] + 4 * acc2[2], u3 = acc1[3] + 4 * acc2[3];
                             const int32_t p2g = __shfl_down_sync(0xffffffffu, u0, 1);
                             const int32_t p2h = __shfl_down_sync(0xffffffffu, u2, 1);
                             if (tig == 0) {
-                                const int ra = 16 * rt + g;
+                                const int ra = rbase + g;
                                 const double Tg = (double)u0 * 65536.0 + (double)u1 * 256.0 + (double)p2g;
                                 const double Th = (double)u2 * 65536.0 + (double)u3 * 256.0 + (double)p2h;
                                 dacc[0] += (double)half_bits_to_float(dvp[ra * (N / 256) + sbi]) * Tg;
@@ -865,7 +913,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                         mma_s8_acc(d, A, bv.z, bv.w);
                         // block sums of this lane's two C columns (block 2*pr+side,
                         // planes 2*(tig&1) and +1; plane 3 reads the stored zero)
-                        const uint2 xsum = ld_s64(xs_u + G::kXPlanes + (pr * 2 + side) * 16 + hsel * 8);
+                        const uint2 xsum = ld_s64(xsum_u + (pr * 2 + side) * 16 + hsel * 8);
                         const int ma = (int)(m.w & 0xffffu), mb = (int)(m.w >> 16);
                         tot[0] += ma * 8 * d[0] + (int)m.y * (int)xsum.x;
                         tot[1] += ma * 8 * d[1] + (int)m.y * (int)xsum.y;
@@ -877,7 +925,8 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                 // loop in program order so its loads and arithmetic can fill
                 // the loop's latency gaps. (After an item's last round it reads
                 // other rows' bytes of the scale slot and is never used.)
-                build_meta(sd, r + 1, meta_u + ((r + 1) & 1) * G::kMetaBytes);
+                if (!NARROW || r + 1 < RPI)
+                    build_meta(sd, chunk_of(r + 1), meta_u + ((r + 1) & 1) * G::kMetaBytes);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);  // this round's stage
@@ -890,9 +939,58 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
             break;
         }
 
-        if (live) {
+        if (NARROW) {
+            // ---- combine the four k quarters in warp 0: warps 1-3 hand over
+            // their partials (exact integers; IQ2_K doubles, added in warp
+            // order), through a double-buffered exchange area per item parity.
+            const int rbuf = o & 1;
+            char *area = red + (rbuf * kConsumers * 32 + lane) * 16;  // + warp * 512
+            bool rok = true;
+            if (wid != 0) {
+                if (o >= 2 && !mbar_wait(&rempty[rbuf], ((o >> 1) & 1) ^ 1)) rok = false;
+                if (rok) {
+                    char *mine = area + wid * 32 * 16;
+                    if (MEMBER == IQK_IQ2_K)
+                        *reinterpret_cast<double2 *>(mine) = make_double2(dacc[0], dacc[1]);
+                    else
+                        *reinterpret_cast<int4 *>(mine) = make_int4(tot[0], tot[1], tot[2], tot[3]);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&rfull[rbuf]);
+                }
+            } else {
+                if (!mbar_wait(&rfull[rbuf], (o >> 1) & 1)) rok = false;
+                if (rok) {
+#pragma unroll
+                    for (int w = 1; w < kConsumers; ++w) {
+                        const char *theirs = area + w * 32 * 16;
+                        if (MEMBER == IQK_IQ2_K) {
+                            const double2 v = *reinterpret_cast<const double2 *>(theirs);
+                            dacc[0] += v.x;
+                            dacc[1] += v.y;
+                        } else {
+                            const int4 v = *reinterpret_cast<const int4 *>(theirs);
+                            tot[0] += v.x;
+                            tot[1] += v.y;
+                            tot[2] += v.z;
+                            tot[3] += v.w;
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&rempty[rbuf]);
+                }
+            }
+            if (!rok) {
+                if (lane == 0) {
+                    atomicOr(a.err, IQK_DEVERR_TIMEOUT);
+                    atomicExch(abort_flag, 1);
+                }
+                break;
+            }
+        }
+
+        if (live && (!NARROW || wid == 0)) {
             // ---- item end: this warp holds the whole k range of its 16 rows.
-            const int ra = 16 * rt + g;  // item-local row
+            const int ra = rbase + g;  // item-local row
             double yg, yg8;
             if (MEMBER == IQK_IQ2_K) {
                 yg = dacc[0];
@@ -969,16 +1067,47 @@ GemvLayout gemv_layout(int member, int64_t n, int64_t x_rows, int64_t pairs) {
     return L;
 }
 
-int gemv_smem_for(int member, int n) {
-    if (n == 2048) {
-        if (member == IQK_IQ2_KS) return gemv_smem_bytes<IQK_IQ2_KS, 2048>();
-        if (member == IQK_IQ2_K) return gemv_smem_bytes<IQK_IQ2_K, 2048>();
-        return gemv_smem_bytes<IQK_IQ1_S_R4, 2048>();
-    }
-    if (member == IQK_IQ2_KS) return gemv_smem_bytes<IQK_IQ2_KS, 4096>();
-    if (member == IQK_IQ2_K) return gemv_smem_bytes<IQK_IQ2_K, 4096>();
-    return gemv_smem_bytes<IQK_IQ1_S_R4, 4096>();
+using GemvFn = void (*)(GemvArgs, CUtensorMap);
+
+// The narrow shape exists at in_features 4096 only.
+static GemvFn gemv_fn(int member, int n, bool narrow) {
+#define IQK_FN(M, NN) (narrow ? (GemvFn)gemv_kernel<M, NN, true> : (GemvFn)gemv_kernel<M, NN, false>)
+    if (n == 2048)
+        return member == IQK_IQ2_KS ? (GemvFn)gemv_kernel<IQK_IQ2_KS, 2048, false>
+               : member == IQK_IQ2_K ? (GemvFn)gemv_kernel<IQK_IQ2_K, 2048, false>
+                                     : (GemvFn)gemv_kernel<IQK_IQ1_S_R4, 2048, false>;
+    return member == IQK_IQ2_KS ? IQK_FN(IQK_IQ2_KS, 4096)
+           : member == IQK_IQ2_K ? IQK_FN(IQK_IQ2_K, 4096) : IQK_FN(IQK_IQ1_S_R4, 4096);
+#undef IQK_FN
 }
+
+int gemv_smem_for(int member, int n, bool narrow) {
+#define IQK_SM(M, NN) (narrow ? gemv_smem_bytes<M, NN, true>() : gemv_smem_bytes<M, NN, false>())
+    if (n == 2048)
+        return member == IQK_IQ2_KS ? gemv_smem_bytes<IQK_IQ2_KS, 2048, false>()
+               : member == IQK_IQ2_K ? gemv_smem_bytes<IQK_IQ2_K, 2048, false>()
+                                     : gemv_smem_bytes<IQK_IQ1_S_R4, 2048, false>();
+    return member == IQK_IQ2_KS ? IQK_SM(IQK_IQ2_KS, 4096)
+           : member == IQK_IQ2_K ? IQK_SM(IQK_IQ2_K, 4096) : IQK_SM(IQK_IQ1_S_R4, 4096);
+#undef IQK_SM
+}
+
+// Launch configuration with programmatic stream serialization (the kernel
+// waits with griddepcontrol.wait before its first global-memory access).
+struct PdlLaunch {
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    PdlLaunch(unsigned grid, unsigned block, size_t smem, cudaStream_t stream) {
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(block);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream;
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+};
 
 cudaError_t launch_gemv_prepare(const void *x, int x_dtype, int64_t x_rows, int n,
                                 int64_t num_experts, const int32_t *sel, const int32_t *tok,
@@ -999,13 +1128,15 @@ cudaError_t launch_gemv_prepare(const void *x, int x_dtype, int64_t x_rows, int 
         if (err != cudaSuccess) return err;
     }
     const unsigned pblocks = (unsigned)x_rows + 1;
+    PdlLaunch pl(pblocks, 256, hist_bytes, stream);
 #define IQK_PREP(T)                                                                          \
-    gemv_prep_kernel<T><<<pblocks, 256, hist_bytes, stream>>>(                               \
-        static_cast<const T *>(x), n, (int)x_rows, sel, tok, (int)pairs, (int)num_experts, L, w)
+    err = cudaLaunchKernelEx(&pl.cfg, gemv_prep_kernel<T>, static_cast<const T *>(x), n,      \
+                             (int)x_rows, sel, tok, (int)pairs, (int)num_experts, L, w)
     if (x_dtype == IQK_F32) IQK_PREP(float);
     else if (x_dtype == IQK_F16) IQK_PREP(__half);
     else IQK_PREP(__nv_bfloat16);
 #undef IQK_PREP
+    if (err != cudaSuccess) return err;
     return cudaGetLastError();
 }
 
@@ -1056,49 +1187,54 @@ cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_
     cudaError_t err = encode_qs_map(&map, streams[0], num_experts * out_features,
                                     iq1 ? n / 8 : n / 4, iq1 ? 64 : 128, !iq1);
     if (err != cudaSuccess) return err;
-    const int smem = gemv_smem_for(member, n);
-    // Upper bound on CTA items: every pair its own tile of every row block.
-    const int64_t max_items = pairs * ((out_features + kItemRows - 1) / kItemRows);
     // One persistent wave: as many CTAs as fit on every SM at once (shared
-    // memory and registers decide; cached per member and width).
-    static std::atomic<int> resident[3][2];
-    // The shared-memory opt-in is a per-device function attribute: set once.
+    // memory and registers decide; cached per member, width and shape). The
+    // shared-memory opt-in is a per-device function attribute: set once.
+    static std::atomic<int> resident[3][2][2];
     static std::atomic<unsigned> attr_done[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = -1;
-    int64_t blocks = 1;
-#define IQK_GEMV(M, N)                                                                          \
-    do {                                                                                        \
-        const unsigned bit = 1u << ((M) * 2 + ((N) == 4096));                                   \
-        if (dev < 0 || !(attr_done[dev].load() & bit)) {                                        \
-            err = cudaFuncSetAttribute(gemv_kernel<M, N>,                                       \
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);      \
-            if (err != cudaSuccess) return err;                                                 \
-            if (dev >= 0) attr_done[dev].fetch_or(bit);                                         \
-        }                                                                                       \
-        std::atomic<int> &per_sm = resident[M][N == 4096];                                      \
-        if (per_sm.load() == 0) {                                                               \
-            int nb = 0;                                                                         \
-            err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, gemv_kernel<M, N>, kThreads, \
-                                                                smem);                          \
-            if (err != cudaSuccess) return err;                                                 \
-            per_sm.store(nb > 0 ? nb : 1);                                                      \
-        }                                                                                       \
-        const int64_t cap = (int64_t)num_sms * per_sm.load();                                   \
-        blocks = max_items < cap ? max_items : cap;                                             \
-        if (blocks < 1) blocks = 1;                                                             \
-        gemv_kernel<M, N><<<(unsigned)blocks, kThreads, smem, stream>>>(ga, map);               \
-    } while (0)
-    if (n == 2048) {
-        if (member == IQK_IQ2_KS) IQK_GEMV(IQK_IQ2_KS, 2048);
-        else if (member == IQK_IQ2_K) IQK_GEMV(IQK_IQ2_K, 2048);
-        else IQK_GEMV(IQK_IQ1_S_R4, 2048);
-    } else {
-        if (member == IQK_IQ2_KS) IQK_GEMV(IQK_IQ2_KS, 4096);
-        else if (member == IQK_IQ2_K) IQK_GEMV(IQK_IQ2_K, 4096);
-        else IQK_GEMV(IQK_IQ1_S_R4, 4096);
+    auto setup = [&](bool narrow, int &per_sm) -> cudaError_t {
+        const GemvFn fn = gemv_fn(member, n, narrow);
+        const int smem = gemv_smem_for(member, n, narrow);
+        const unsigned bit = 1u << ((member * 2 + (n == 4096)) * 2 + (narrow ? 1 : 0));
+        if (dev < 0 || !(attr_done[dev].load() & bit)) {
+            const cudaError_t e =
+                cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e != cudaSuccess) return e;
+            if (dev >= 0) attr_done[dev].fetch_or(bit);
+        }
+        std::atomic<int> &r = resident[member][n == 4096][narrow ? 1 : 0];
+        if (r.load() == 0) {
+            int nb = 0;
+            const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, kThreads, smem);
+            if (e != cudaSuccess) return e;
+            r.store(nb > 0 ? nb : 1);
+        }
+        per_sm = r.load();
+        return cudaSuccess;
+    };
+    int per_sm = 0;
+    err = setup(false, per_sm);
+    if (err != cudaSuccess) return err;
+    // Upper bound on items: every pair its own tile of every row block. Fewer
+    // wide items than resident CTAs (e.g. one token) take the narrow shape.
+    const int64_t wide_items = pairs * ((out_features + kItemRows - 1) / kItemRows);
+    // (At in_features 2048 an item is only four rounds wide already, and a
+    // narrow item's single round does not pay for its set-up: measured.)
+    const bool narrow = n == 4096 && wide_items < (int64_t)num_sms * per_sm;
+    if (narrow) {
+        err = setup(true, per_sm);
+        if (err != cudaSuccess) return err;
     }
-#undef IQK_GEMV
+    const int64_t rows = narrow ? 16 : kItemRows;
+    const int64_t max_items = pairs * ((out_features + rows - 1) / rows);
+    const int64_t cap = (int64_t)num_sms * per_sm;
+    int64_t blocks = max_items < cap ? max_items : cap;
+    if (blocks < 1) blocks = 1;
+    PdlLaunch pl((unsigned)blocks, kThreads, gemv_smem_for(member, n, narrow), stream);
+    err = cudaLaunchKernelEx(&pl.cfg, gemv_fn(member, n, narrow), ga, map);
+    if (err != cudaSuccess) return err;
     return cudaGetLastError();
 }
 

@@ -30,7 +30,7 @@ struct GemvLayout {
 };
 
 GemvLayout gemv_layout(int member, int64_t n, int64_t x_rows, int64_t pairs);
-int gemv_smem_for(int member, int n);
+int gemv_smem_for(int member, int n, bool narrow);
 cudaError_t launch_gemv_prepare(const void *x, int x_dtype, int64_t x_rows, int n,
                                 int64_t num_experts, const int32_t *sel, const int32_t *tok,
                                 int64_t pairs, void *ws, cudaStream_t stream);

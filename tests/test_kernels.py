@@ -240,6 +240,33 @@ def test_gemv_handles_many_pairs_per_expert(cuda, member):
     assert rel_err(got.cpu().numpy().reshape(want.shape), want) < GEMV_TOL
 
 
+@pytest.mark.parametrize("member", MEMBERS)
+@pytest.mark.parametrize("geom", [(2048, 4096), (4096, 2048)])
+@pytest.mark.parametrize("tokens", [1, 8])
+def test_full_geometry_both_item_shapes(cuda, member, geom, tokens):
+    """E=256 at the benchmark projection shapes. One token gives fewer 64-row
+    items than resident CTAs, so the run kernel takes its narrow shape (16-row
+    items, the four compute warps a quarter of k each); eight tokens take the
+    wide shape. Checked against float64 of the CPU-decoded selected experts."""
+    from mlx_iqk_b200.profile_cases import random_module
+    E = 256
+    out, n = geom
+    gen = torch.Generator(device=cuda).manual_seed(31 + tokens)
+    mod = random_module(member, E, out, n, cuda, gen)
+    rng = np.random.default_rng(40 + tokens)
+    idx = np.stack([rng.choice(E, 6, replace=False) for _ in range(tokens)])
+    x = torch.randn(tokens, 1, 1, n, generator=gen, device=cuda).to(torch.bfloat16)
+    got = mod.gemv(x, torch.from_numpy(idx).to(cuda)).cpu().numpy().reshape(tokens, 6, out)
+    xs = x.float().cpu().numpy().reshape(tokens, n).astype(np.float64)
+    for t in sorted({0, tokens - 1}):
+        for k in (0, 5):
+            e = int(idx[t, k])
+            st = {nm: getattr(mod, nm)[e].cpu().numpy().reshape(out, -1)
+                  for nm in mod.stream_names()}
+            want = oracle.decode(member, st, n).astype(np.float64) @ xs[t]
+            assert rel_err(got[t, k], want) < GEMV_TOL, (member, geom, tokens, t, k)
+
+
 def test_full_geometry_decode_sampled(cuda):
     """BASELINE config 2 geometry (E=256, gate 2048x4096), B=8, checked on the
     experts actually selected (size-independent sampling)."""
