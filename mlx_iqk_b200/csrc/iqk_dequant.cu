@@ -1,8 +1,10 @@
 // Bit-exact stacked dequantization of the IQ_K relayout streams.
 //
-// One thread reconstructs eight consecutive weights of one output row and
-// writes them with one 16-byte store (float16/bfloat16) or two (float32), so
-// a warp's stores cover 512 or 1024 contiguous bytes. The arithmetic is the
+// One thread reconstructs one 16-weight code word (2-bit members) or one
+// 32-weight block (IQ1_S_R4) of one output row and writes it with 16-byte
+// streaming stores. Every weight of a group (block) is one of the group's
+// four (three) float32 products, computed once per thread; 16-bit outputs
+// place them with byte permutes. The arithmetic is the
 // CPU dequantizer's float32 chain in its order
 // (vendor/ik_llama/iqk_iq2.cpp:502-562, vendor/ik_llama/iqk_iq1sr4.cpp:581-604;
 // the reference's Metal restatement is src/mlx_iqk/kernels.py:631-742):
@@ -17,66 +19,6 @@
 #include "iqk_tables.cuh"
 
 namespace iqk {
-
-// Decode the 8 weights of octet `oct` of source row `srow` into w[0..7].
-template <int MEMBER>
-__device__ __forceinline__ void decode_octet(const void *const *s, int64_t srow,
-                                             int oct, int n, const uint16_t *grid,
-                                             float w[8]) {
-    const int k0 = oct * 8;
-    if (MEMBER == IQK_IQ1_S_R4) {
-        const uint32_t *qs = static_cast<const uint32_t *>(s[0]);
-        const uint16_t *qh = static_cast<const uint16_t *>(s[1]);
-        const uint16_t *dv = static_cast<const uint16_t *>(s[2]);
-        const int b = k0 >> 5, i = (k0 >> 3) & 3;
-        const uint32_t qw = qs[srow * (n / 32) + b];
-        const uint32_t h = qh[srow * (n / 32) + b];
-        const float d = half_bits_to_float(dv[srow]);
-        const float dl = d * (float)(int)(2u * ((h >> 12) & 7u) + 1u);
-        const float shift = (h & 0x8000u) ? -0.125f : 0.125f;
-        const uint32_t idx = ((qw >> (8 * i)) & 0xffu) | (((h >> (3 * i)) & 7u) << 8);
-        const uint32_t code = grid[idx];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int g = (int)((code >> (2 * j)) & 3u) - 1;
-            w[j] = dl * ((float)g + shift);
-        }
-        return;
-    }
-    const uint32_t *qs = static_cast<const uint32_t *>(s[0]);
-    const uint32_t word = qs[srow * (n / 16) + (k0 >> 4)];
-    const uint32_t codes = word >> (2 * (k0 & 15));  // 8 codes in the low 16 bits
-    float dl;
-    int alpha;
-    if (MEMBER == IQK_IQ2_KS) {
-        const uint8_t *scl = static_cast<const uint8_t *>(s[1]);
-        const uint8_t *sch = static_cast<const uint8_t *>(s[2]);
-        const uint8_t *sex = static_cast<const uint8_t *>(s[3]);
-        const uint16_t *dv = static_cast<const uint16_t *>(s[4]);
-        const int g = k0 >> 5;
-        const int lo = (scl[srow * (n / 64) + (g >> 1)] >> (4 * (g & 1))) & 15;
-        const int hi = (sch[srow * (n / 256) + (g >> 3)] >> (g & 7)) & 1;
-        alpha = (sex[srow * (n / 256) + (g >> 3)] >> (g & 7)) & 1;
-        const float d = half_bits_to_float(dv[srow]);
-        dl = d * (float)((lo | (hi << 4)) - 16);
-    } else {
-        const uint8_t *scl = static_cast<const uint8_t *>(s[1]);
-        const uint8_t *sex = static_cast<const uint8_t *>(s[2]);
-        const uint16_t *dv = static_cast<const uint16_t *>(s[3]);
-        const int sb = k0 >> 4;
-        const int lo = (scl[srow * (n / 32) + (sb >> 1)] >> (4 * (sb & 1))) & 15;
-        alpha = (sex[srow * (n / 128) + (sb >> 3)] >> (sb & 7)) & 1;
-        const float d = half_bits_to_float(dv[srow * (n / 256) + (sb >> 4)]);
-        dl = d * (float)(lo - 8);
-    }
-    // The sub-block's four alphabet entries as int8 bytes of one register.
-    const uint32_t tab = alpha ? kIq2Tab1 : kIq2Tab0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const int v = (int)(int8_t)(tab >> (8 * ((codes >> (2 * j)) & 3u)));
-        w[j] = dl * (float)v;
-    }
-}
 
 struct StreamPtrs {
     const void *p[5];
@@ -136,6 +78,37 @@ __device__ __forceinline__ void store_word(OUT *out, uint32_t word, const float 
     }
 }
 
+// IQ1_S_R4, one 8-weight octet per thread: its 2-bit grid values (g + 1 in
+// bits 2j, 2j+1 of the 16-bit grid entry) pick one of the block's three
+// float32 products t[g + 1] = dl * (g + shift), computed once with the CPU's
+// chain -- so the result is the same bit for bit -- and placed like the low
+// half of a 2-bit code word.
+template <typename OUT>
+__device__ __forceinline__ void store_octet(OUT *out, uint32_t code, const float t[4]) {
+    if constexpr (sizeof(OUT) == 4) {
+        float w[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const uint32_t c = (code >> (2 * k)) & 3u;
+            w[k] = c == 0u ? t[0] : (c == 1u ? t[1] : t[2]);
+        }
+        float4 *o4 = reinterpret_cast<float4 *>(out);
+        IQK_DQ_ST(o4, make_float4(w[0], w[1], w[2], w[3]));
+        IQK_DQ_ST(o4 + 1, make_float4(w[4], w[5], w[6], w[7]));
+    } else {
+        const uint32_t t01 = pack2<OUT>(t[0], t[1]), t23 = pack2<OUT>(t[2], t[3]);
+        uint32_t r[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t m = (code >> (2 * j)) & 0x00000303u;  // codes j, 4+j
+            r[j] = prmt_dq(t01, t23, m * 0x22u + 0x10101010u);
+        }
+        IQK_DQ_ST(reinterpret_cast<uint4 *>(out),
+                  make_uint4(prmt_dq(r[0], r[1], 0x5410u), prmt_dq(r[2], r[3], 0x5410u),
+                             prmt_dq(r[0], r[1], 0x7632u), prmt_dq(r[2], r[3], 0x7632u)));
+    }
+}
+
 __device__ __forceinline__ void group_table(float dl, int alpha, float t[4]) {
     const uint32_t tab = alpha ? kIq2Tab1 : kIq2Tab0;
 #pragma unroll
@@ -181,37 +154,42 @@ dequant_words_kernel(StreamPtrs sp, uint32_t total_words, int log2_words, int n,
     }
 }
 
-template <int MEMBER, typename OUT>
+// IQ1_S_R4: one half block (16 weights, two octets: two grid bytes of the qs
+// word and their qh bits) per thread, so a thread writes 32 contiguous bytes
+// at 16-bit outputs -- the store pattern of the 2-bit word kernel.
+template <typename OUT>
 __global__ void __launch_bounds__(256)
-dequant_rows_kernel(StreamPtrs sp, uint32_t total_octets, int log2_octs,
-                    int n, int64_t out_features, int64_t row_start, uint32_t rows,
-                    OUT *__restrict__ dst) {
-    __shared__ uint16_t grid[MEMBER == IQK_IQ1_S_R4 ? 2048 : 1];
-    if (MEMBER == IQK_IQ1_S_R4) {
-        for (int i = threadIdx.x; i < 2048; i += blockDim.x) grid[i] = g_iq1s_grid[i];
-        __syncthreads();
-    }
+dequant_iq1_kernel(StreamPtrs sp, uint32_t total_halves, int log2_halves, int n,
+                   int64_t out_features, int64_t row_start, uint32_t rows,
+                   OUT *__restrict__ dst) {
+    __shared__ uint16_t grid[2048];
+    for (int i = threadIdx.x; i < 2048; i += blockDim.x) grid[i] = g_iq1s_grid[i];
+    __syncthreads();
+    const uint32_t *qs = static_cast<const uint32_t *>(sp.p[0]);
+    const uint16_t *qh = static_cast<const uint16_t *>(sp.p[1]);
+    const uint16_t *dv = static_cast<const uint16_t *>(sp.p[2]);
     const uint32_t stride = gridDim.x * blockDim.x;
-    for (uint32_t o = blockIdx.x * blockDim.x + threadIdx.x; o < total_octets; o += stride) {
-        const uint32_t lin = o >> log2_octs;  // [expert, local row]
-        const int oct = (int)(o & ((1u << log2_octs) - 1u));
-        const uint32_t e = lin / rows;
-        const int64_t srow = (int64_t)e * out_features + row_start + (lin - e * rows);
-        float w[8];
-        decode_octet<MEMBER>(sp.p, srow, oct, n, grid, w);
-        OUT *out = dst + (int64_t)lin * n + oct * 8;
-        if constexpr (sizeof(OUT) == 4) {
-            float4 *o4 = reinterpret_cast<float4 *>(out);
-            o4[0] = make_float4(w[0], w[1], w[2], w[3]);
-            o4[1] = make_float4(w[4], w[5], w[6], w[7]);
-        } else {
-            union {
-                OUT h[8];
-                uint4 u;
-            } pk;
+    const bool whole = rows == out_features;  // whole experts: source row == output row
+    for (uint32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < total_halves; u += stride) {
+        const uint32_t lin = u >> log2_halves;  // [expert, local row]
+        const int hb = (int)(u & ((1u << log2_halves) - 1u));
+        const int b = hb >> 1;
+        int64_t srow = lin;
+        if (!whole) {
+            const uint32_t e = lin / rows;
+            srow = (int64_t)e * out_features + row_start + (lin - e * rows);
+        }
+        const uint32_t qw = __ldg(qs + srow * (n / 32) + b);
+        const uint32_t h = __ldg(qh + srow * (n / 32) + b);
+        const float dl = half_bits_to_float(__ldg(dv + srow)) *
+                         (float)(int)(2u * ((h >> 12) & 7u) + 1u);
+        const float shift = (h & 0x8000u) ? -0.125f : 0.125f;
+        const float t[4] = {dl * (-1.0f + shift), dl * (0.0f + shift), dl * (1.0f + shift), 0.0f};
+        OUT *out = dst + (int64_t)lin * n + hb * 16;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) pk.h[j] = from_float<OUT>(w[j]);
-            *reinterpret_cast<uint4 *>(out) = pk.u;
+        for (int i = 2 * (hb & 1); i < 2 * (hb & 1) + 2; ++i) {
+            const uint32_t code = grid[((qw >> (8 * i)) & 0xffu) | (((h >> (3 * i)) & 7u) << 8)];
+            store_octet<OUT>(out + 8 * (i & 1), code, t);
         }
     }
 }
@@ -224,10 +202,9 @@ cudaError_t launch_dequant(int member, const void *const *streams, int64_t num_e
     const RowBytes rb = row_bytes(member, n);
     for (int i = 0; i < rb.count; ++i) sp.p[i] = streams[i];
     const int log2_octs = n == 4096 ? 9 : 8;  // n / 8 octets per row
-    const bool words = member != IQK_IQ1_S_R4;  // 2-bit members: one code word per thread
     const int elem = out_dtype == IQK_F32 ? 4 : 2;
-    // 32-bit octet indices: split the expert range so each launch stays below 2^31.
-    const int64_t per_expert = rows * (words ? n / 16 : n / 8);
+    // 32-bit unit indices: split the expert range so each launch stays below 2^31.
+    const int64_t per_expert = rows * (n / 16);  // 16-weight units of both kernels
     if (per_expert == 0 || num_experts == 0) return cudaSuccess;
     const int64_t chunk = ((int64_t)1 << 31) / per_expert;
     for (int64_t e0 = 0; e0 < num_experts; e0 += chunk) {
@@ -247,8 +224,8 @@ cudaError_t launch_dequant(int member, const void *const *streams, int64_t num_e
                 spc, total, log2_octs - 1, n, out_features, row_start, (uint32_t)rows, \
                 static_cast<T *>(dstc));                                              \
         else                                                                          \
-            dequant_rows_kernel<M, T><<<(unsigned)blocks, threads, 0, stream>>>(       \
-                spc, total, log2_octs, n, out_features, row_start, (uint32_t)rows,     \
+            dequant_iq1_kernel<T><<<(unsigned)blocks, threads, 0, stream>>>(           \
+                spc, total, log2_octs - 1, n, out_features, row_start, (uint32_t)rows, \
                 static_cast<T *>(dstc))
 #define IQK_DQ_MEMBER(M)                                             \
     do {                                                             \
