@@ -34,6 +34,22 @@ __device__ __forceinline__ uint32_t prmt_dq(uint32_t a, uint32_t b, uint32_t sel
     return d;
 }
 
+// A warp's 32 units are consecutive in one output row, CH 16-byte chunks each.
+// HBM writes run at full rate when every warp store instruction covers 512
+// contiguous bytes (measured on B200: 6.2 TB/s, against 3.5 TB/s for 32
+// bytes per thread in two stores), so a unit's chunks go through a per-warp
+// shared-memory stage and come out lane-contiguous.
+template <int CH>
+__device__ __forceinline__ void warp_store(uint4 *warp_out, const uint4 (&v)[CH], uint4 *stage,
+                                           int lane) {
+#pragma unroll
+    for (int c = 0; c < CH; ++c) stage[lane * CH + c] = v[c];
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < CH; ++c) IQK_DQ_ST(warp_out + 32 * c + lane, stage[32 * c + lane]);
+    __syncwarp();
+}
+
 template <typename OUT> __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     const OUT a = from_float<OUT>(lo), b = from_float<OUT>(hi);
     return (uint32_t)*reinterpret_cast<const uint16_t *>(&a) |
@@ -47,7 +63,8 @@ template <typename OUT> __device__ __forceinline__ uint32_t pack2(float lo, floa
 // pick entry c of the {T0,T1,T2,T3} table; pairs come out as (k, k+4) and
 // one more permute restores k order).
 template <typename OUT>
-__device__ __forceinline__ void store_word(OUT *out, uint32_t word, const float t[4]) {
+__device__ __forceinline__ void expand_word(uint32_t word, const float t[4],
+                                            uint4 (&v)[sizeof(OUT) == 4 ? 4 : 2]) {
     if constexpr (sizeof(OUT) == 4) {
         float w[16];
 #pragma unroll
@@ -56,10 +73,10 @@ __device__ __forceinline__ void store_word(OUT *out, uint32_t word, const float 
             const float lo2 = (c & 1u) ? t[1] : t[0], hi2 = (c & 1u) ? t[3] : t[2];
             w[k] = (c & 2u) ? hi2 : lo2;
         }
-        float4 *o4 = reinterpret_cast<float4 *>(out);
 #pragma unroll
         for (int q = 0; q < 4; ++q)
-            IQK_DQ_ST(o4 + q, make_float4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]));
+            v[q] = make_uint4(__float_as_uint(w[4 * q]), __float_as_uint(w[4 * q + 1]),
+                              __float_as_uint(w[4 * q + 2]), __float_as_uint(w[4 * q + 3]));
     } else {
         const uint32_t t01 = pack2<OUT>(t[0], t[1]), t23 = pack2<OUT>(t[2], t[3]);
         uint32_t r[8];
@@ -70,21 +87,19 @@ __device__ __forceinline__ void store_word(OUT *out, uint32_t word, const float 
             r[j] = prmt_dq(t01, t23, sel);
             r[4 + j] = prmt_dq(t01, t23, sel >> 16);
         }
-        uint4 *o4 = reinterpret_cast<uint4 *>(out);
-        IQK_DQ_ST(o4, make_uint4(prmt_dq(r[0], r[1], 0x5410u), prmt_dq(r[2], r[3], 0x5410u),
-                              prmt_dq(r[0], r[1], 0x7632u), prmt_dq(r[2], r[3], 0x7632u)));
-        IQK_DQ_ST(o4 + 1, make_uint4(prmt_dq(r[4], r[5], 0x5410u), prmt_dq(r[6], r[7], 0x5410u),
-                                  prmt_dq(r[4], r[5], 0x7632u), prmt_dq(r[6], r[7], 0x7632u)));
+        v[0] = make_uint4(prmt_dq(r[0], r[1], 0x5410u), prmt_dq(r[2], r[3], 0x5410u),
+                          prmt_dq(r[0], r[1], 0x7632u), prmt_dq(r[2], r[3], 0x7632u));
+        v[1] = make_uint4(prmt_dq(r[4], r[5], 0x5410u), prmt_dq(r[6], r[7], 0x5410u),
+                          prmt_dq(r[4], r[5], 0x7632u), prmt_dq(r[6], r[7], 0x7632u));
     }
 }
 
-// IQ1_S_R4, one 8-weight octet per thread: its 2-bit grid values (g + 1 in
-// bits 2j, 2j+1 of the 16-bit grid entry) pick one of the block's three
-// float32 products t[g + 1] = dl * (g + shift), computed once with the CPU's
-// chain -- so the result is the same bit for bit -- and placed like the low
-// half of a 2-bit code word.
+// IQ1_S_R4 octet: its 2-bit grid values (g + 1 in bits 2j, 2j+1 of the
+// 16-bit grid entry) pick one of the block's three float32 products
+// t[g + 1] = dl * (g + shift), computed once with the CPU's chain -- so the
+// result is the same bit for bit -- placed like the low half of a code word.
 template <typename OUT>
-__device__ __forceinline__ void store_octet(OUT *out, uint32_t code, const float t[4]) {
+__device__ __forceinline__ void expand_octet(uint32_t code, const float t[4], uint4 *v) {
     if constexpr (sizeof(OUT) == 4) {
         float w[8];
 #pragma unroll
@@ -92,9 +107,10 @@ __device__ __forceinline__ void store_octet(OUT *out, uint32_t code, const float
             const uint32_t c = (code >> (2 * k)) & 3u;
             w[k] = c == 0u ? t[0] : (c == 1u ? t[1] : t[2]);
         }
-        float4 *o4 = reinterpret_cast<float4 *>(out);
-        IQK_DQ_ST(o4, make_float4(w[0], w[1], w[2], w[3]));
-        IQK_DQ_ST(o4 + 1, make_float4(w[4], w[5], w[6], w[7]));
+        v[0] = make_uint4(__float_as_uint(w[0]), __float_as_uint(w[1]), __float_as_uint(w[2]),
+                          __float_as_uint(w[3]));
+        v[1] = make_uint4(__float_as_uint(w[4]), __float_as_uint(w[5]), __float_as_uint(w[6]),
+                          __float_as_uint(w[7]));
     } else {
         const uint32_t t01 = pack2<OUT>(t[0], t[1]), t23 = pack2<OUT>(t[2], t[3]);
         uint32_t r[4];
@@ -103,9 +119,8 @@ __device__ __forceinline__ void store_octet(OUT *out, uint32_t code, const float
             const uint32_t m = (code >> (2 * j)) & 0x00000303u;  // codes j, 4+j
             r[j] = prmt_dq(t01, t23, m * 0x22u + 0x10101010u);
         }
-        IQK_DQ_ST(reinterpret_cast<uint4 *>(out),
-                  make_uint4(prmt_dq(r[0], r[1], 0x5410u), prmt_dq(r[2], r[3], 0x5410u),
-                             prmt_dq(r[0], r[1], 0x7632u), prmt_dq(r[2], r[3], 0x7632u)));
+        v[0] = make_uint4(prmt_dq(r[0], r[1], 0x5410u), prmt_dq(r[2], r[3], 0x5410u),
+                          prmt_dq(r[0], r[1], 0x7632u), prmt_dq(r[2], r[3], 0x7632u));
     }
 }
 
@@ -120,8 +135,13 @@ __global__ void __launch_bounds__(256)
 dequant_words_kernel(StreamPtrs sp, uint32_t total_words, int log2_words, int n,
                      int64_t out_features, int64_t row_start, uint32_t rows,
                      OUT *__restrict__ dst) {
+    constexpr int CH = sizeof(OUT) == 4 ? 4 : 2;  // 16-byte chunks per word
+    __shared__ uint4 stage[256 / 32][32 * CH];
+    const int lane = threadIdx.x & 31;
+    uint4 *my_stage = stage[threadIdx.x >> 5];
     const uint32_t stride = gridDim.x * blockDim.x;
     const uint32_t *qs = static_cast<const uint32_t *>(sp.p[0]);
+    // total_words and stride are multiples of 32: every warp is all in or all out
     for (uint32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < total_words; u += stride) {
         const uint32_t lin = u >> log2_words;  // [expert, local row]
         const int wi = (int)(u & ((1u << log2_words) - 1u));
@@ -150,7 +170,10 @@ dequant_words_kernel(StreamPtrs sp, uint32_t total_words, int log2_words, int n,
             group_table(half_bits_to_float(__ldg(dv + srow * (n / 256) + (sb >> 4))) *
                             (float)(lo - 8), alpha, t);
         }
-        store_word<OUT>(dst + (int64_t)lin * n + wi * 16, word, t);
+        uint4 v[CH];
+        expand_word<OUT>(word, t, v);
+        warp_store<CH>(reinterpret_cast<uint4 *>(dst + (int64_t)lin * n + (wi - lane) * 16), v,
+                       my_stage, lane);
     }
 }
 
@@ -168,8 +191,13 @@ dequant_iq1_kernel(StreamPtrs sp, uint32_t total_halves, int log2_halves, int n,
     const uint32_t *qs = static_cast<const uint32_t *>(sp.p[0]);
     const uint16_t *qh = static_cast<const uint16_t *>(sp.p[1]);
     const uint16_t *dv = static_cast<const uint16_t *>(sp.p[2]);
+    constexpr int CH = sizeof(OUT) == 4 ? 4 : 2;  // 16-byte chunks per half block
+    __shared__ uint4 stage[256 / 32][32 * CH];
+    const int lane = threadIdx.x & 31;
+    uint4 *my_stage = stage[threadIdx.x >> 5];
     const uint32_t stride = gridDim.x * blockDim.x;
-    const bool whole = rows == out_features;  // whole experts: source row == output row
+    const bool whole = rows == out_features;
+    // total_halves and stride are multiples of 32: every warp is all in or all out  // whole experts: source row == output row
     for (uint32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < total_halves; u += stride) {
         const uint32_t lin = u >> log2_halves;  // [expert, local row]
         const int hb = (int)(u & ((1u << log2_halves) - 1u));
@@ -185,12 +213,15 @@ dequant_iq1_kernel(StreamPtrs sp, uint32_t total_halves, int log2_halves, int n,
                          (float)(int)(2u * ((h >> 12) & 7u) + 1u);
         const float shift = (h & 0x8000u) ? -0.125f : 0.125f;
         const float t[4] = {dl * (-1.0f + shift), dl * (0.0f + shift), dl * (1.0f + shift), 0.0f};
-        OUT *out = dst + (int64_t)lin * n + hb * 16;
+        uint4 v[CH];
 #pragma unroll
-        for (int i = 2 * (hb & 1); i < 2 * (hb & 1) + 2; ++i) {
+        for (int q = 0; q < 2; ++q) {
+            const int i = 2 * (hb & 1) + q;  // octet of the block
             const uint32_t code = grid[((qw >> (8 * i)) & 0xffu) | (((h >> (3 * i)) & 7u) << 8)];
-            store_octet<OUT>(out + 8 * (i & 1), code, t);
+            expand_octet<OUT>(code, t, v + q * (CH / 2));
         }
+        warp_store<CH>(reinterpret_cast<uint4 *>(dst + (int64_t)lin * n + (hb - lane) * 16), v,
+                       my_stage, lane);
     }
 }
 
