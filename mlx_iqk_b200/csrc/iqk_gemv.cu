@@ -375,7 +375,7 @@ template <int MEMBER, int N, bool NARROW> __host__ __device__ constexpr int gemv
     return 1024 /* alignment slack */ + SH::kStages * stage_bytes<MEMBER, SH::KQ>() +
            2 * sslot_bytes<MEMBER, N, SH::kRows>() + 2 * kConsumers * G::kMetaBytes +
            kMaxTiles * (int)sizeof(TileRef) + (MEMBER == IQK_IQ1_S_R4 ? 4096 : 0) +
-           (MEMBER == IQK_IQ2_K ? 256 : 0) + 2 * SH::kStages * 8 + 8 * 8 + 16 +
+           2 * SH::kStages * 8 + 8 * 8 + 16 +
            kPairsPerRound * 192 + SH::kRedBytes;
 }
 
@@ -515,9 +515,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     TileRef *tcache = reinterpret_cast<TileRef *>(metas + 2 * kConsumers * G::kMetaBytes);
     char *tail = reinterpret_cast<char *>(tcache + kMaxTiles);
     uint16_t *grid = reinterpret_cast<uint16_t *>(tail);   // IQ1_S_R4
-    uint2 *ktab = reinterpret_cast<uint2 *>(tail);         // IQ2_K: (alpha, idx) -> tables
-    uint64_t *full = reinterpret_cast<uint64_t *>(
-        tail + (MEMBER == IQK_IQ1_S_R4 ? 4096 : MEMBER == IQK_IQ2_K ? 256 : 0));
+    uint64_t *full = reinterpret_cast<uint64_t *>(tail + (MEMBER == IQK_IQ1_S_R4 ? 4096 : 0));
     uint64_t *empty = full + kStages;
     uint64_t *sfull = empty + kStages;  // [2] item scale slots
     uint64_t *sempty = sfull + 2;       // [2]
@@ -537,21 +535,6 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     // Shared-memory set-up first: it overlaps the previous kernel's drain.
     if (MEMBER == IQK_IQ1_S_R4)
         for (int i = tid; i < 2048; i += blockDim.x) grid[i] = g_iq1s_grid[i];
-    if (MEMBER == IQK_IQ2_K && tid < 32) {
-        // IQ2_K scale index idx = 4*hi + lo (hi = idx >> 2 in [-2, 1], lo = idx & 3):
-        // per (alphabet, idx) the two int8 tables V*lo and V*hi, so a sub-block's
-        // scale folds into its A operand and all sub-blocks share one accumulator.
-        const int alpha = tid >> 4, idx = (tid & 15) - 8;
-        const uint32_t tab = alpha ? kIq2Tab1 : kIq2Tab0;
-        uint32_t tlo = 0, thi = 0;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const int v = (int)(int8_t)(tab >> (8 * c));
-            tlo |= (uint32_t)(uint8_t)(int8_t)(v * (idx & 3)) << (8 * c);
-            thi |= (uint32_t)(uint8_t)(int8_t)(v * (idx >> 2)) << (8 * c);
-        }
-        ktab[tid] = make_uint2(tlo, thi);
-    }
     for (int i = tid; i < kPairsPerRound * 192 / 4; i += blockDim.x)
         reinterpret_cast<uint32_t *>(zeros)[i] = 0u;
     if (tid == 0) {
@@ -680,10 +663,20 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     const int g = lane >> 2, tig = lane & 3;
     const int rbase = NARROW ? 0 : 16 * wid;  // first item-local row of this warp
     const uint32_t meta_u = smem_u32(metas + wid * 2 * G::kMetaBytes);  // two round buffers
-    const int side = tig >> 1;             // which 32-weight group of an MMA pair
-    int bplane;                            // activation plane of B column g (or -1)
-    if (MEMBER == IQK_IQ2_K) bplane = g < 3 ? g : -1;
-    else bplane = ((g & 3) < 3 && (g >> 2) == side) ? (g & 3) : -1;
+    const int side = tig >> 1;  // IQ2_KS, IQ1_S_R4: which 32-weight group of an MMA pair
+    // Activation plane of B column g (or -1: a zero block). IQ2_KS and IQ1_S_R4
+    // have two sides (columns 4s .. 4s+2: planes 0-2 of side s, lanes tig >> 1
+    // == s supplying its k). IQ2_K has four, one per 16-weight sub-block = code
+    // word tig: product a, columns 2s and 2s+1 = planes 0 and 1 of side s;
+    // product b, column 2s = plane 2. Every column of a lane then belongs to
+    // its own sub-block and takes that sub-block's integer scale.
+    int bplane, bplane2 = -1;
+    if (MEMBER == IQK_IQ2_K) {
+        bplane = (g >> 1) == tig ? (g & 1) : -1;
+        bplane2 = g == 2 * tig ? 2 : -1;
+    } else {
+        bplane = ((g & 3) < 3 && (g >> 2) == side) ? (g & 3) : -1;
+    }
     // swizzled offsets of this lane's code words (rows g and g+8 of its box)
     uint32_t woff;
     if (MEMBER == IQK_IQ1_S_R4) woff = g * 64 + ((((uint32_t)g >> 1) & 3u) << 4) + side * 4;
@@ -736,20 +729,33 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                         (uint32_t)ib);
             }
         } else if (MEMBER == IQK_IQ2_K) {
+            // Eight 16-weight sub-blocks of rows mra and mra + 8, by byte
+            // permutes: the alphabet mask (0x44 per byte for the second
+            // alphabet; extra bit u spread to bit 7 of byte u & 3 by one
+            // multiply, then 0x80 -> 0x44 by mul.hi) and the scale
+            // 16 * (nibble - 8): nibble ^ 8 is nibble - 8 as a signed 4-bit
+            // value, moved to the top of a byte and sign-extended by the permute.
             const int b0 = c * 32 + mq * 8;  // first of 8 sub-blocks (2 pairs)
             const uint8_t *scl = reinterpret_cast<const uint8_t *>(sd);
             const uint8_t *sex = scl + SS::off(2) + (b0 >> 3);
             scl += b0 >> 1;
-            const uint32_t la = lds_u32(scl + mra * (N / 32));
-            const uint32_t lb = lds_u32(scl + (mra + 8) * (N / 32));
-            const uint32_t xa = sex[mra * (N / 128)];
-            const uint32_t xb = sex[(mra + 8) * (N / 128)];
+            const uint32_t la = lds_u32(scl + mra * (N / 32)) ^ 0x88888888u;
+            const uint32_t lb = lds_u32(scl + (mra + 8) * (N / 32)) ^ 0x88888888u;
+            const uint32_t xa = sex[mra * (N / 128)], xb = sex[(mra + 8) * (N / 128)];
+            const uint32_t ea[2] = {(la << 4) & 0xF0F0F0F0u, la & 0xF0F0F0F0u};  // even, odd u
+            const uint32_t eb[2] = {(lb << 4) & 0xF0F0F0F0u, lb & 0xF0F0F0F0u};
+            const uint32_t ma[2] = {mulhi(((xa & 0x0Fu) * 0x10204080u) & 0x80808080u, a44),
+                                    mulhi(((xa & 0xF0u) * 0x01020408u) & 0x80808080u, a44)};
+            const uint32_t mb2[2] = {mulhi(((xb & 0x0Fu) * 0x10204080u) & 0x80808080u, a44),
+                                     mulhi(((xb & 0xF0u) * 0x01020408u) & 0x80808080u, a44)};
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
-                const uint2 ta = ktab[((xa >> u) & 1u) * 16 + ((la >> (4 * u)) & 15u)];
-                const uint2 tb = ktab[((xb >> u) & 1u) * 16 + ((lb >> (4 * u)) & 15u)];
+                const uint32_t bsel = 0x1111u * (u & 3);                  // replicate byte
+                const uint32_t ssel = 0x8880u + 0x1111u * (u >> 1);       // sign-extend byte
                 const int pr = mq * 2 + (u >> 2), wd = u & 3;  // pair, word
-                st_s128(mb + pr * 512 + (mg * 4 + wd) * 16, ta.x, tb.x, ta.y, tb.y);
+                st_s128(mb + pr * 512 + (mg * 4 + wd) * 16, prmt(ma[u >> 2], 0u, bsel),
+                        prmt(mb2[u >> 2], 0u, bsel), prmt(ea[u & 1], 0u, ssel),
+                        prmt(eb[u & 1], 0u, ssel));
             }
         } else {
             const int s0 = c * 16 + mq * 4;  // first of 4 blocks (2 pairs)
@@ -784,8 +790,8 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
         if (live) build_meta(sd, chunk_of(0), meta_u);
         __syncwarp();
         int32_t tot[4] = {0, 0, 0, 0};
-        int32_t acc1[4] = {0, 0, 0, 0}, acc2[4] = {0, 0, 0, 0};  // IQ2_K super-block sums
-        double dacc[2] = {0.0, 0.0};                              // IQ2_K: rows g, g+8
+        int32_t tb[2] = {0, 0};        // IQ2_K: plane 2 (product b), rows g, g+8
+        double dacc[2] = {0.0, 0.0};  // IQ2_K: rows g, g+8, this lane's sub-blocks
         bool ok = true;
 #pragma unroll 1
         for (int r = 0; r < RPI; ++r) {
@@ -806,6 +812,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                                                  (NARROW ? wid * G::kXSums : 0));
                 // B: live lanes read their plane's 16 bytes; the others a zero block
                 const uint32_t xl_u = bplane >= 0 ? xs_u + tig * 48 + bplane * 16 : zero_u;
+                const uint32_t xl2_u = bplane2 >= 0 ? xs_u + tig * 48 + bplane2 * 16 : zero_u;
                 const uint32_t mrow = meta_u + (r & 1) * G::kMetaBytes + moff;
                 const uint32_t wl = wb_u | woff;  // box is 1024-aligned, woff < 1024
 #pragma unroll
@@ -840,49 +847,43 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                         const uint32_t wo = wl ^ (uint32_t)(pr << 4);
                         const uint32_t wg = ld_s32(wo);
                         const uint32_t wg8 = ld_s32(wo + 1024);
-                        const uint4 m = ld_s128(mrow + pr * 512);
-                        const uint32_t s0g = wg & 0x33333333u, s1g = shr2(wg, m30) & 0x33333333u;
-                        const uint32_t s0h = wg8 & 0x33333333u, s1h = shr2(wg8, m30) & 0x33333333u;
-                        const uint32_t s0gh = shr16(s0g), s1gh = shr16(s1g);
-                        const uint32_t s0hh = shr16(s0h), s1hh = shr16(s1h);
-                        A[0] = prmt(m.x, 0u, s0g);
-                        A[1] = prmt(m.y, 0u, s0h);
-                        A[2] = prmt(m.x, 0u, s1g);
-                        A[3] = prmt(m.y, 0u, s1h);
-                        mma_s8_acc(acc1, A, bv.x, bv.y);
-                        A[0] = prmt(m.x, 0u, s0gh);
-                        A[1] = prmt(m.y, 0u, s0hh);
-                        A[2] = prmt(m.x, 0u, s1gh);
-                        A[3] = prmt(m.y, 0u, s1hh);
-                        mma_s8_acc(acc1, A, bv.z, bv.w);
-                        A[0] = prmt(m.z, 0u, s0g);
-                        A[1] = prmt(m.w, 0u, s0h);
-                        A[2] = prmt(m.z, 0u, s1g);
-                        A[3] = prmt(m.w, 0u, s1h);
-                        mma_s8_acc(acc2, A, bv.x, bv.y);
-                        A[0] = prmt(m.z, 0u, s0gh);
-                        A[1] = prmt(m.w, 0u, s0hh);
-                        A[2] = prmt(m.z, 0u, s1gh);
-                        A[3] = prmt(m.w, 0u, s1hh);
-                        mma_s8_acc(acc2, A, bv.z, bv.w);
+                        const uint4 m = ld_s128(mrow + pr * 512);  // masks g, g+8; scales g, g+8
+                        const uint4 bw = ld_s128(xl2_u + pr * 192);
+                        const uint32_t s0g = (wg & 0x33333333u) | m.x;
+                        const uint32_t s1g = (shr2(wg, m30) & 0x33333333u) | m.x;
+                        const uint32_t s0h = (wg8 & 0x33333333u) | m.y;
+                        const uint32_t s1h = (shr2(wg8, m30) & 0x33333333u) | m.y;
+                        int32_t d[4], e[4];
+                        A[0] = prmt(kIq2Tab0, kIq2Tab1, s0g);
+                        A[1] = prmt(kIq2Tab0, kIq2Tab1, s0h);
+                        A[2] = prmt(kIq2Tab0, kIq2Tab1, s1g);
+                        A[3] = prmt(kIq2Tab0, kIq2Tab1, s1h);
+                        mma_s8(d, A, bv.x, bv.y);
+                        mma_s8(e, A, bw.x, bw.y);
+                        A[0] = prmt(kIq2Tab0, kIq2Tab1, shr16(s0g));
+                        A[1] = prmt(kIq2Tab0, kIq2Tab1, shr16(s0h));
+                        A[2] = prmt(kIq2Tab0, kIq2Tab1, shr16(s1g));
+                        A[3] = prmt(kIq2Tab0, kIq2Tab1, shr16(s1h));
+                        mma_s8_acc(d, A, bv.z, bv.w);
+                        mma_s8_acc(e, A, bw.z, bw.w);
+                        tot[0] += (int)m.z * d[0];
+                        tot[1] += (int)m.z * d[1];
+                        tot[2] += (int)m.w * d[2];
+                        tot[3] += (int)m.w * d[3];
+                        tb[0] += (int)m.z * e[0];
+                        tb[1] += (int)m.w * e[2];
                         if ((pr & 3) == 3) {
-                            // end of a 256-weight super-block: fold in its fp16 scale.
-                            // Lane tig 0 holds planes 0, 1 (cols 0, 1), tig 1 plane 2.
+                            // end of a 256-weight super-block: fold in its fp16
+                            // scale (exact products; |tot| < 2^26 per super-block)
                             const int sbi = (chunk_of(r) * kChunkK + pr * 64) >> 8;
                             const uint16_t *dvp = reinterpret_cast<const uint16_t *>(sd + SS::off(3));
-                            const int32_t u0 = acc1[0] + 4 * acc2[0], u1 = acc1[1] + 4 * acc2[1];
-                            const int32_t u2 = acc1[2] + 4 * acc2[2], u3 = acc1[3] + 4 * acc2[3];
-                            const int32_t p2g = __shfl_down_sync(0xffffffffu, u0, 1);
-                            const int32_t p2h = __shfl_down_sync(0xffffffffu, u2, 1);
-                            if (tig == 0) {
-                                const int ra = rbase + g;
-                                const double Tg = (double)u0 * 65536.0 + (double)u1 * 256.0 + (double)p2g;
-                                const double Th = (double)u2 * 65536.0 + (double)u3 * 256.0 + (double)p2h;
-                                dacc[0] += (double)half_bits_to_float(dvp[ra * (N / 256) + sbi]) * Tg;
-                                dacc[1] += (double)half_bits_to_float(dvp[(ra + 8) * (N / 256) + sbi]) * Th;
-                            }
-                            acc1[0] = acc1[1] = acc1[2] = acc1[3] = 0;
-                            acc2[0] = acc2[1] = acc2[2] = acc2[3] = 0;
+                            const int ra = rbase + g;
+                            const double Tg = (double)tot[0] * 65536.0 + (double)tot[1] * 256.0 + (double)tb[0];
+                            const double Th = (double)tot[2] * 65536.0 + (double)tot[3] * 256.0 + (double)tb[1];
+                            dacc[0] += (double)half_bits_to_float(dvp[ra * (N / 256) + sbi]) * Tg;
+                            dacc[1] += (double)half_bits_to_float(dvp[(ra + 8) * (N / 256) + sbi]) * Th;
+                            tot[0] = tot[1] = tot[2] = tot[3] = 0;
+                            tb[0] = tb[1] = 0;
                         }
                     } else {
                         // IQ1_S_R4: this lane covers sub-groups 2h, 2h+1 of block 2*pr+side
@@ -993,8 +994,11 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
             const int ra = rbase + g;  // item-local row
             double yg, yg8;
             if (MEMBER == IQK_IQ2_K) {
-                yg = dacc[0];
-                yg8 = dacc[1];
+                // the quad's four sub-block sides, in a fixed order
+                yg = dacc[0] + __shfl_xor_sync(0xffffffffu, dacc[0], 1);
+                yg8 = dacc[1] + __shfl_xor_sync(0xffffffffu, dacc[1], 1);
+                yg += __shfl_xor_sync(0xffffffffu, yg, 2);
+                yg8 += __shfl_xor_sync(0xffffffffu, yg8, 2);
             } else {
                 int32_t s4[4] = {tot[0], tot[1], tot[2], tot[3]};
                 // lanes tig 0/2 hold planes (0,1) of the two sides, 1/3 plane 2
@@ -1014,7 +1018,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                 if (S == kScaleNonFinite) {
                     vg = vg8 = __int_as_float(0x7fc00000);
                 } else {
-                    const double sc = pow2(-S - (MEMBER == IQK_IQ1_S_R4 ? 3 : 0));
+                    const double sc = pow2(-S - (MEMBER == IQK_IQ1_S_R4 ? 3 : MEMBER == IQK_IQ2_K ? 4 : 0));
                     vg = (float)(yg * sc);
                     vg8 = (float)(yg8 * sc);
                 }
