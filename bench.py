@@ -313,8 +313,9 @@ class PrefillLayer:
     """BASELINE config 5 on one GPU: one MoE layer, gate/up IQ2_KS and down
     IQ2_K over all 256 experts, T tokens routed top-6 by N(0,1) logits
     (mildly skewed load), sorted_indices=True, through the grouped GEMM.
-    Step = prepare(x) + gate + up + SiLU(gate)*up + prepare(h) + down +
-    router-weighted combine."""
+    Step = prepare(x) + gate + up + SiLU(gate)*up*router weight (one pass
+    over the routed pairs) + prepare(h) + down + each token's sum over its
+    slots -- the kernels ExpertParallelMoE runs on every rank."""
 
     def __init__(self, torch, K, dev, gen, tokens: int = PREFILL_TOKENS):
         from mlx_iqk_b200 import IqkSwitchLinear
@@ -327,7 +328,7 @@ class PrefillLayer:
                                             mod.member))
         logits = torch.randn((tokens, E), generator=gen, device=dev)
         top = torch.topk(logits, TOP_K, dim=-1)
-        self.weights = torch.softmax(top.values, dim=-1)
+        self.weights = torch.softmax(top.values, dim=-1).reshape(-1).contiguous()
         self.sel = top.indices.to(torch.int32).reshape(-1).contiguous()
         self.pairs = self.sel.numel()
         self.x = torch.randn((tokens, GATE_UP[1]), generator=gen, device=dev).to(torch.bfloat16)
@@ -359,13 +360,11 @@ class PrefillLayer:
                       self.ws_d)
 
     def step(self):
-        torch = self.torch
+        K = self.K
         self.gate_up()
-        torch.mul(torch.nn.functional.silu(self.yg), self.yu, out=self.yg)
-        self.h.copy_(self.yg)
+        K.pairs_swiglu(self.yg, self.yu, self.weights, GATE_UP[1], E, self.ws_gu, self.h)
         self.down_proj()
-        torch.sum(self.yd.view(self.T, TOP_K, DOWN[0]) * self.weights.unsqueeze(-1), dim=1,
-                  out=self.out)
+        K.pairs_combine(self.yd, self.sel, TOP_K, E, self.out)
 
 
 class DecodeCell:
@@ -556,7 +555,7 @@ def run_b200(args) -> None:
                    "value": round(PREFILL_TOKENS / (ep_ms * 1e-3), 1), "unit": "tokens/s",
                    "ms_per_step": round(ep_ms, 4), "tokens": PREFILL_TOKENS,
                    "scaling": "strong", "parallelism": f"ep{world}: {E // world} experts/rank, "
-                   "NCCL all_to_all dispatch/combine"}
+                   "NCCL all_gather dispatch, all_to_all combine"}
     if not args.no_prefill and world == 1:
         pl = PrefillLayer(torch, K, dev, gen)
         pl.step()

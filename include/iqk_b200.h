@@ -203,6 +203,41 @@ int iqk_grouped_run(int member, const void *const *streams, int64_t num_experts,
 int iqk_grouped_read_error(const void *workspace, int32_t *flags, iqk_stream_t stream);
 
 /*
+ * Expert-parallel helpers (no reference counterpart: the reference serves a
+ * whole layer on one device; these shard its SwitchGLU seam,
+ * src/mlx_iqk/nn.py:1-22, over ranks that each hold num_experts local
+ * experts and see every rank's pairs).
+ *
+ * iqk_grouped_prepare_shard: iqk_grouped_prepare, except that a pair whose
+ * expert index lies outside [0, num_experts) belongs to another rank: it is
+ * skipped without an error, and iqk_grouped_run leaves its output row
+ * untouched (an out-of-range row index is still an error).
+ *
+ * iqk_pairs_swiglu: for every pair q routed by a prepared workspace (same
+ * in_features, num_experts and pairs as the preparation),
+ * h[q, :] = bf16((silu(gate[q, :]) * up[q, :]) * weight[q]); other rows of h
+ * are not written. gate, up: float32 [pairs, inter]; h: bfloat16.
+ *
+ * iqk_pairs_combine: out[r, :] = sum over j < top_k, in order, of
+ * y[r * top_k + j, :] for the slots whose sel lies in [0, num_experts); rows
+ * without one are zeros. y: float32 [rows * top_k, hidden]; out: float32 or
+ * bfloat16 [rows, hidden]; hidden a multiple of 4.
+ */
+int iqk_grouped_prepare_shard(const void *x, int x_dtype, int64_t x_rows, int64_t in_features,
+                              int64_t num_experts, const int32_t *sel, const int32_t *tok,
+                              int64_t pairs, void *workspace, size_t workspace_bytes,
+                              iqk_stream_t stream);
+
+int iqk_pairs_swiglu(const float *gate, const float *up, const float *weight, int64_t inter,
+                     int64_t in_features, int64_t num_experts, int64_t pairs,
+                     const void *workspace, size_t workspace_bytes, void *h,
+                     iqk_stream_t stream);
+
+int iqk_pairs_combine(const float *y, const int32_t *sel, int64_t rows, int top_k,
+                      int64_t num_experts, int64_t hidden, void *out, int out_dtype,
+                      iqk_stream_t stream);
+
+/*
  * iqk_gemv without a workspace argument, for callers that cannot allocate
  * device memory where they launch (a runtime with a fixed memory plan, code
  * inside an allocator's own hooks, a binding without a device allocator).

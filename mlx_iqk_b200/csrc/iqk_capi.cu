@@ -208,6 +208,56 @@ int iqk_grouped_prepare(const void *x, int x_dtype, int64_t x_rows, int64_t in_f
                                               reinterpret_cast<cudaStream_t>(stream)));
 }
 
+int iqk_grouped_prepare_shard(const void *x, int x_dtype, int64_t x_rows, int64_t in_features,
+                              int64_t num_experts, const int32_t *sel, const int32_t *tok,
+                              int64_t pairs, void *workspace, size_t workspace_bytes,
+                              iqk_stream_t stream) {
+    int st = check_prepare(in_features, num_experts, x_rows, pairs, tok, x_dtype);
+    if (st != IQK_OK) return st;
+    if (pairs == 0) return IQK_OK;
+    if (!x || !sel || !workspace) return IQK_ERR_ARGUMENT;
+    if (!aligned(x, 16) || !aligned(workspace, 256)) return IQK_ERR_ALIGNMENT;
+    if (workspace_bytes < grouped_layout(in_features, num_experts, pairs).total)
+        return IQK_ERR_WORKSPACE;
+    return cuda_status(launch_grouped_prepare(x, x_dtype, x_rows, (int)in_features, num_experts,
+                                              sel, tok, pairs, workspace,
+                                              reinterpret_cast<cudaStream_t>(stream), true));
+}
+
+int iqk_pairs_swiglu(const float *gate, const float *up, const float *weight, int64_t inter,
+                     int64_t in_features, int64_t num_experts, int64_t pairs,
+                     const void *workspace, size_t workspace_bytes, void *h,
+                     iqk_stream_t stream) {
+    if (!width_ok(in_features)) return IQK_ERR_WIDTH;
+    if (num_experts <= 0 || num_experts > 4096) return IQK_ERR_GEOMETRY;
+    if (inter <= 0 || inter % 16 || inter > (1 << 20)) return IQK_ERR_GEOMETRY;
+    if (pairs < 0 || pairs > (1 << 24)) return IQK_ERR_GEOMETRY;
+    if (pairs == 0) return IQK_OK;
+    if (!gate || !up || !weight || !workspace || !h) return IQK_ERR_ARGUMENT;
+    if (!aligned(gate, 16) || !aligned(up, 16) || !aligned(h, 16) || !aligned(weight, 4) ||
+        !aligned(workspace, 256))
+        return IQK_ERR_ALIGNMENT;
+    if (workspace_bytes < grouped_layout(in_features, num_experts, pairs).total)
+        return IQK_ERR_WORKSPACE;
+    return cuda_status(launch_pairs_swiglu(gate, up, weight, (int)inter, (int)in_features,
+                                           num_experts, pairs, workspace, h,
+                                           reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int iqk_pairs_combine(const float *y, const int32_t *sel, int64_t rows, int top_k,
+                      int64_t num_experts, int64_t hidden, void *out, int out_dtype,
+                      iqk_stream_t stream) {
+    if (rows < 0 || rows > ((int64_t)1 << 31) - 1) return IQK_ERR_GEOMETRY;
+    if (top_k <= 0 || top_k > 64 || num_experts <= 0) return IQK_ERR_GEOMETRY;
+    if (hidden <= 0 || hidden % 4 || hidden > (1 << 20)) return IQK_ERR_GEOMETRY;
+    if (out_dtype != IQK_F32 && out_dtype != IQK_BF16) return IQK_ERR_ARGUMENT;
+    if (rows == 0) return IQK_OK;
+    if (!y || !sel || !out) return IQK_ERR_ARGUMENT;
+    if (!aligned(y, 16) || !aligned(sel, 4) || !aligned(out, 16)) return IQK_ERR_ALIGNMENT;
+    return cuda_status(launch_pairs_combine(y, sel, rows, top_k, num_experts, (int)hidden, out,
+                                            out_dtype, reinterpret_cast<cudaStream_t>(stream)));
+}
+
 int iqk_grouped_run(int member, const void *const *streams, int64_t num_experts,
                     int64_t out_features, int64_t in_features, int64_t pairs, void *y,
                     int y_dtype, const void *workspace, size_t workspace_bytes,

@@ -184,7 +184,7 @@ __device__ __forceinline__ int block_scan(int v, int *warp_tot, int *total) {
 // most L.tok_cap tokens. Shared memory: counts, then scatter cursors.
 __global__ void __launch_bounds__(1024)
 grouped_route_kernel(const int32_t *__restrict__ sel, const int32_t *__restrict__ tok, int pairs,
-                     int x_rows, int num_experts, GroupedLayout L, char *ws) {
+                     int x_rows, int num_experts, int shard, GroupedLayout L, char *ws) {
     const int cap = L.tok_cap;
     extern __shared__ int32_t cnt[];
     __shared__ int32_t warp_tot[33];
@@ -201,9 +201,13 @@ grouped_route_kernel(const int32_t *__restrict__ sel, const int32_t *__restrict_
     for (int p = tid; p < pairs; p += nt) {
         const int e = sel[p];
         const int t = tok ? tok[p] : p / dims;
-        if (e < 0 || e >= num_experts) err |= IQK_DEVERR_EXPERT;
-        else if (t < 0 || t >= x_rows) err |= IQK_DEVERR_TOKEN;
-        else atomicAdd(&cnt[e], 1);
+        if (e < 0 || e >= num_experts) {
+            if (!shard) err |= IQK_DEVERR_EXPERT;  // shard: another rank's expert
+        } else if (t < 0 || t >= x_rows) {
+            err |= IQK_DEVERR_TOKEN;
+        } else {
+            atomicAdd(&cnt[e], 1);
+        }
     }
     if (err) atomicOr(&s_bad, err);
     __syncthreads();
@@ -228,6 +232,7 @@ grouped_route_kernel(const int32_t *__restrict__ sel, const int32_t *__restrict_
         hdr[0] = s_bad;
         hdr[1] = n_tiles;
         hdr[2] = n_valid;
+        hdr[3] = shard;
         s_tail = n_valid;
     }
     __syncthreads();
@@ -560,9 +565,10 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
         tmem_relinquish();
         tc_fence_before();
     }
-    // Zero the outputs of unroutable pairs (bad expert or row index).
+    // Zero the outputs of unroutable pairs (bad expert or row index); a
+    // shard preparation leaves the rows of other ranks' pairs untouched.
     {
-        const int tail = a.pairs - n_valid;
+        const int tail = hdr[3] ? 0 : a.pairs - n_valid;
         const int64_t total = (int64_t)tail * out;
         for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
              i += (int64_t)gridDim.x * blockDim.x) {
@@ -903,7 +909,7 @@ GroupedLayout grouped_layout(int64_t n, int64_t num_experts, int64_t pairs) {
 
 cudaError_t launch_grouped_prepare(const void *x, int x_dtype, int64_t x_rows, int n,
                                    int64_t num_experts, const int32_t *sel, const int32_t *tok,
-                                   int64_t pairs, void *ws, cudaStream_t stream) {
+                                   int64_t pairs, void *ws, cudaStream_t stream, bool shard) {
     const GroupedLayout L = grouped_layout(n, num_experts, pairs);
     char *w = static_cast<char *>(ws);
     const size_t hist = sizeof(int32_t) * (size_t)num_experts;
@@ -914,7 +920,7 @@ cudaError_t launch_grouped_prepare(const void *x, int x_dtype, int64_t x_rows, i
         if (err != cudaSuccess) return err;
     }
     grouped_route_kernel<<<1, 1024, hist, stream>>>(sel, tok, (int)pairs, (int)x_rows,
-                                                    (int)num_experts, L, w);
+                                                    (int)num_experts, shard ? 1 : 0, L, w);
     if ((err = cudaGetLastError()) != cudaSuccess) return err;
     const unsigned blocks = (unsigned)pairs;
 #define IQK_CONV(T)                                                                         \

@@ -121,6 +121,12 @@ def library() -> ctypes.CDLL:
     lib.iqk_gemv_static.argtypes = [i32, vp, i32, i64, vp, i64, i64, i64, vp, vp, i64, vp, i32,
                                     vp]
     lib.iqk_gemv_static.restype = i32
+    lib.iqk_grouped_prepare_shard.argtypes = [vp, i32, i64, i64, i64, vp, vp, i64, vp, sz, vp]
+    lib.iqk_grouped_prepare_shard.restype = i32
+    lib.iqk_pairs_swiglu.argtypes = [vp, vp, vp, i64, i64, i64, i64, vp, sz, vp, vp]
+    lib.iqk_pairs_swiglu.restype = i32
+    lib.iqk_pairs_combine.argtypes = [vp, vp, i64, i32, i64, i64, vp, i32, vp]
+    lib.iqk_pairs_combine.restype = i32
     _LIB = lib
     return lib
 
@@ -131,7 +137,8 @@ def exported_symbols() -> list[str]:
             "iqk_gemv_workspace_bytes", "iqk_gemv", "iqk_gemv_prepare", "iqk_gemv_run",
             "iqk_read_error", "iqk_grouped_workspace_bytes", "iqk_grouped_gemm",
             "iqk_grouped_prepare", "iqk_grouped_run", "iqk_grouped_read_error",
-            "iqk_gemv_static_max_bytes", "iqk_gemv_static"]
+            "iqk_gemv_static_max_bytes", "iqk_gemv_static", "iqk_grouped_prepare_shard",
+            "iqk_pairs_swiglu", "iqk_pairs_combine"]
 
 
 def raise_for_status(status: int, what: str) -> None:
@@ -280,14 +287,19 @@ def grouped(member: str, x: torch.Tensor, streams, num_experts: int, out_feature
 
 
 def grouped_prepare(x: torch.Tensor, num_experts: int, in_features: int, sel: torch.Tensor,
-                    tok: torch.Tensor | None, workspace: torch.Tensor) -> torch.Tensor:
+                    tok: torch.Tensor | None, workspace: torch.Tensor,
+                    shard: bool = False) -> torch.Tensor:
+    """``iqk_grouped_prepare``; with ``shard`` ``iqk_grouped_prepare_shard``
+    (pairs whose expert lies outside [0, num_experts) are another rank's:
+    skipped, no error, their output rows left untouched)."""
     lib = library()
     check_device(workspace.device)
-    status = lib.iqk_grouped_prepare(
+    fn = lib.iqk_grouped_prepare_shard if shard else lib.iqk_grouped_prepare
+    status = fn(
         x.data_ptr(), DTYPE_IDS[x.dtype], x.shape[0], in_features, num_experts,
         sel.data_ptr(), None if tok is None else tok.data_ptr(), sel.numel(),
         workspace.data_ptr(), workspace.numel(), stream_handle(workspace.device))
-    raise_for_status(status, "iqk_grouped_prepare")
+    raise_for_status(status, "iqk_grouped_prepare_shard" if shard else "iqk_grouped_prepare")
     return workspace
 
 
@@ -300,6 +312,30 @@ def grouped_run(member: str, streams, num_experts: int, out_features: int, in_fe
         stream_handle(y.device))
     raise_for_status(status, "iqk_grouped_run")
     return y
+
+
+def pairs_swiglu(g: torch.Tensor, u: torch.Tensor, w: torch.Tensor, in_features: int,
+                 num_experts: int, workspace: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
+    """``iqk_pairs_swiglu``: h[q] = bf16((silu(g[q]) * u[q]) * w[q]) for the pairs
+    routed by ``workspace`` (prepared with ``in_features`` and ``num_experts``)."""
+    pairs, inter = g.shape
+    status = library().iqk_pairs_swiglu(
+        g.data_ptr(), u.data_ptr(), w.data_ptr(), inter, in_features, num_experts, pairs,
+        workspace.data_ptr(), workspace.numel(), h.data_ptr(), stream_handle(h.device))
+    raise_for_status(status, "iqk_pairs_swiglu")
+    return h
+
+
+def pairs_combine(y: torch.Tensor, sel: torch.Tensor, top_k: int, num_experts: int,
+                  out: torch.Tensor) -> torch.Tensor:
+    """``iqk_pairs_combine``: out[r] = sum_j y[r*k + j] over the slots of row r
+    whose sel lies in [0, num_experts)."""
+    rows, hidden = out.shape
+    status = library().iqk_pairs_combine(
+        y.data_ptr(), sel.data_ptr(), rows, top_k, num_experts, hidden, out.data_ptr(),
+        DTYPE_IDS[out.dtype], stream_handle(out.device))
+    raise_for_status(status, "iqk_pairs_combine")
+    return out
 
 
 def grouped_read_error(workspace: torch.Tensor) -> int:
