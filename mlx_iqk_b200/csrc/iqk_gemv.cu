@@ -694,6 +694,8 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     const uint32_t hmul = 0x02040810u >> msh;                 // bit msh+u -> bit 8u+4
     const uint32_t amul = msh ? 0x01020408u : 0x10204080u;    // bit msh+u -> bit 8u+7
     const uint32_t a44 = a.one * 0x88000000u;                 // mulhi: t>>1 | t>>5
+    // IQ1_S_R4 grid-index permute: bytes (qs 2h, high 2h, qs 2h+1, high 2h+1), h = tig & 1
+    const uint32_t isel = 0x5140u + 0x2222u * (uint32_t)(tig & 1);
 
     // Group metadata of round r (this warp's 16 rows x 512 weights) into the
     // metadata buffer at mb.
@@ -758,16 +760,22 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                         prmt(eb[u & 1], 0u, ssel));
             }
         } else {
+            // Per block and row: the four octets' 3-bit grid-index high parts
+            // spread to one byte each (fields 0, 2 and 1, 3 moved apart by
+            // one multiply each, no overlapping bits), and the signed shift
+            // term (sign of the block's delta) x its scale 2s+1.
             const int s0 = c * 16 + mq * 4;  // first of 4 blocks (2 pairs)
             const uint16_t *qh = reinterpret_cast<const uint16_t *>(sd) + s0;
+            auto spread3 = [](uint32_t h) {
+                return (((h & 0x1C7u) * 0x401u) & 0x00070007u) | (((h & 0xE38u) * 0x8020u) & 0x07000700u);
+            };
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 const uint32_t ha = qh[mra * (N / 32) + u], hb = qh[(mra + 8) * (N / 32) + u];
                 const int sa = 2 * (int)((ha >> 12) & 7u) + 1, sb = 2 * (int)((hb >> 12) & 7u) + 1;
                 const int pr = mq * 2 + (u >> 1), sd2 = u & 1;
-                st_s128(mb + pr * 256 + (mg * 2 + sd2) * 16, ha | (hb << 16),
-                        (uint32_t)((ha & 0x8000u) ? -sa : sa), (uint32_t)((hb & 0x8000u) ? -sb : sb),
-                        (uint32_t)(sa | (sb << 16)));
+                st_s128(mb + pr * 256 + (mg * 2 + sd2) * 16, spread3(ha), spread3(hb),
+                        (uint32_t)((ha & 0x8000u) ? -sa : sa), (uint32_t)((hb & 0x8000u) ? -sb : sb));
             }
         }
     };
@@ -891,14 +899,13 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                         const uint32_t wo = (wl ^ (uint32_t)((pr >> 1) << 4)) + (uint32_t)((pr & 1) << 3);
                         const uint32_t qg = ld_s32(wo);
                         const uint32_t qg8 = ld_s32(wo + 512);
-                        const uint4 m = ld_s128(mrow + pr * 256);
-                        const uint32_t hg = m.x & 0xffffu, hh = m.x >> 16;
-                        const uint32_t bg = qg >> (16 * hsel), bh = qg8 >> (16 * hsel);
-                        const uint32_t ga = grid[(bg & 0xffu) | (((hg >> (6 * hsel)) & 7u) << 8)];
-                        const uint32_t gb = grid[((bg >> 8) & 0xffu) | (((hg >> (6 * hsel + 3)) & 7u) << 8)];
-                        const uint32_t ha = grid[(bh & 0xffu) | (((hh >> (6 * hsel)) & 7u) << 8)];
-                        const uint32_t hb = grid[((bh >> 8) & 0xffu) | (((hh >> (6 * hsel + 3)) & 7u) << 8)];
-                        const uint32_t vg = ga | (gb << 16), vh = ha | (hb << 16);
+                        const uint4 m = ld_s128(mrow + pr * 256);  // high parts g, g+8; shift terms
+                        // both grid indices of a row (octets 2h, 2h+1: qs byte | high part << 8)
+                        // from one byte permute
+                        const uint32_t wig = prmt(qg, m.x, isel), wih = prmt(qg8, m.y, isel);
+                        const uint32_t ga = grid[wig & 0xffffu], gb = grid[wig >> 16];
+                        const uint32_t ha = grid[wih & 0xffffu], hb = grid[wih >> 16];
+                        const uint32_t vg = prmt(ga, gb, 0x5410u), vh = prmt(ha, hb, 0x5410u);
                         const uint32_t s0g = vg & 0x33333333u, s1g = shr2(vg, m30) & 0x33333333u;
                         const uint32_t s0h = vh & 0x33333333u, s1h = shr2(vh, m30) & 0x33333333u;
                         int32_t d[4];
@@ -915,11 +922,12 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                         // block sums of this lane's two C columns (block 2*pr+side,
                         // planes 2*(tig&1) and +1; plane 3 reads the stored zero)
                         const uint2 xsum = ld_s64(xsum_u + (pr * 2 + side) * 16 + hsel * 8);
-                        const int ma = (int)(m.w & 0xffffu), mb = (int)(m.w >> 16);
-                        tot[0] += ma * 8 * d[0] + (int)m.y * (int)xsum.x;
-                        tot[1] += ma * 8 * d[1] + (int)m.y * (int)xsum.y;
-                        tot[2] += mb * 8 * d[2] + (int)m.z * (int)xsum.x;
-                        tot[3] += mb * 8 * d[3] + (int)m.z * (int)xsum.y;
+                        const int sy = (int)m.z, sz = (int)m.w;  // +-(2s+1)
+                        const int ma = abs(sy), mb = abs(sz);
+                        tot[0] += ma * 8 * d[0] + sy * (int)xsum.x;
+                        tot[1] += ma * 8 * d[1] + sy * (int)xsum.y;
+                        tot[2] += mb * 8 * d[2] + sz * (int)xsum.x;
+                        tot[3] += mb * 8 * d[3] + sz * (int)xsum.y;
                     }
                 }
                 // Next round's metadata into the other buffer, after the pair
