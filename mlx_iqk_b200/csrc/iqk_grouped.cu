@@ -23,7 +23,7 @@
 // tokens; a conversion kernel writes each routed pair's scaled, permuted f16
 // activation row in sorted order.
 //
-// GEMM kernel: persistent, one CTA per SM, 22 warps.
+// GEMM kernel: persistent, one CTA per SM, 26 warps (72 registers each).
 //   warp 0      TMA producer of the activation stages (128 weights x the
 //               tile's tokens, two 64-wide k atoms, 128-byte swizzle)
 //   warp 1      TMEM owner (allocates 512 columns, frees them at exit)
@@ -34,12 +34,15 @@
 //               slice kh of its 32 rows (lane quarter q of row half j) into
 //               f16x2 words with byte permutes on the group's table of the
 //               four alphabet products, and stores them into the stage's
-//               TMEM A buffer (tcgen05.st); then the epilogue (tcgen05.ld of
-//               D, row scale, 2^-S, store y)
+//               TMEM A buffer (tcgen05.st)
 //   warp 20     TMA producer of the 2-bit code chunks (512 weights of every
 //               row of the item, 128-byte swizzle)
 //   warp 21     MMA issuer (one elected lane): per stage RB x 8
-//               M128 N<=64 K16 MMAs, A from TMEM, B from shared memory
+//               M128 N<=64 K16 MMAs, A from TMEM, B from shared memory,
+//               into the item's accumulator set (item parity)
+//   warps 22-25 epilogue, one per TMEM lane quarter: tcgen05.ld of the
+//               finished accumulators, row scale, 2^-S, store y -- while the
+//               other roles already run the next item
 // Work items are (tile, 256- or 128-row block), expert-major, so CTAs running
 // at the same time share one expert's activation tile in L2.
 //
@@ -64,9 +67,9 @@ namespace {
 
 using namespace dev;
 
-constexpr int kThreadsG = 704;                       // 22 warps
+constexpr int kThreadsG = 832;                       // 26 warps
 constexpr int kProducer = 0, kTmemWarp = 1, kLoader0 = 2, kDq0 = 4, kCodeWarp = 20,
-              kIssuer = 21;
+              kIssuer = 21, kEpi0 = 22;
 constexpr int kStageK = 128;                         // weights per k-stage (8 MMAs of K=16)
 constexpr int kMaxKS = 4096 / kStageK;               // k-stages of the widest row
 constexpr int kCodeK = 512;                          // weights per code load (4 stages)
@@ -74,26 +77,35 @@ constexpr int kCodeBox = kGroupRows * kCodeK / 4;    // 16 KB: 128 rows x 128 B,
 constexpr int kMaxCodeSlots = 4;
 constexpr int kMaxXSlots = 8;
 constexpr int kMinXSlots = 4;
-constexpr int kNumA = 3;  // A buffers in TMEM: the dequant runs up to two stages ahead
+constexpr int kNumA = 2;  // A buffers in TMEM: the dequant runs up to one stage ahead
 // Work item = one token tile x RB*128 output rows (RB "halves" of 128 rows,
 // RB = 1 or 2). Every k-stage (128 weights) goes through the same steps: the
 // 16 dequant warps write its A tile (f16, RB halves x 128 rows) into TMEM
 // buffer b = stage mod kNumA -- warp (q, j, kh) its lane quarter q of half j
-// and k slice kh -- and the issuer runs the stage's RB x 8 MMAs into the RB
-// accumulators, in stage order, then commits afree[b]. (One issuer measured
-// faster overall than one per half on B200: the dequantization bounds the
-// kernel, and a second issuer warp takes issue slots from it.) TMEM columns, 64
-// each: accumulator half j at 64*j, A buffer b half j at 64*(RB + b*RB + j):
-// 4*RB*64 <= 512 columns. A warp writes buffer b again for stage g + kNumA
-// only after afree[b] completes for stage g; that phase needs the issuer,
-// which in turn waits for every warp's aready[b] of stage g + kNumA before
-// committing the next phase, so no wait is ever lapped.
+// and k slice kh -- and the issuer runs the stage's RB x 8 MMAs into the
+// item's RB accumulators, in stage order, then commits afree[b]. (One issuer
+// measured faster overall than one per half on B200: the dequantization
+// bounds the kernel, and a second issuer warp takes issue slots from it.)
+// Accumulators are double-buffered by item parity, so the four epilogue
+// warps drain item i while the dequant warps and the issuer run item i + 1.
+// TMEM columns, 64 each: accumulator set s half j at 64*(s*RB + j), A buffer
+// b half j at 64*(2*RB + b*RB + j): 4*RB*64 <= 512 columns.
+// No wait is ever lapped: a warp writes A buffer b again for stage g + kNumA
+// only after afree[b] completes for stage g, which needs the issuer, which
+// in turn waits for every warp's aready[b] of stage g + kNumA before
+// committing the next phase; the issuer starts item i + 2 in accumulator set
+// s only after dempty[s] of item i, which needs item i's dfull[s].
 constexpr int kTmemCols = 512;
 constexpr int kTok = 64;                             // tokens per work tile
 // Barriers, the TMEM slot word and the abort flag; then the group tables.
-constexpr int kTabOff = 8 * (2 * kMaxXSlots + 2 * kMaxCodeSlots + 2 * kNumA + 3 + 4) + 16;
+constexpr int kTabOff = 8 * (2 * kMaxXSlots + 2 * kMaxCodeSlots + 2 * kNumA + 5 + 4) + 16;
 constexpr int kTabEntries = 64;  // IQ2_KS: (scale index + 16) | alphabet << 5; IQ2_K: idx + 8 | alpha << 4
-constexpr int kBarBytes = kTabOff + 8 * kTabEntries;
+// Per epilogue warp: the current item's column table {y offset of the
+// pair's row (int64), 2^-S (float), pad}, copied out of the scale buffer so
+// that the buffer is released before the accumulators are final.
+constexpr int kEcolOff = (kTabOff + 8 * kTabEntries + 15) & ~15;  // 16-byte entries
+constexpr int kBarBytes = kEcolOff + 4 * kTok * 16;
+static_assert(kEcolOff % 16 == 0 && kTabOff % 8 == 0, "barrier-region alignment");
 constexpr int kSmemCap = 227 * 1024;
 
 // Per-item scale buffer: per (stage, row) scale words, transposed so that a
@@ -491,7 +503,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
 grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_map,
                     const __grid_constant__ XMaps x_maps) {
     constexpr int kRows = RB * kGroupRows;    // output rows per work item
-    constexpr uint32_t kACol = RB * 64u;      // first A-buffer column (after the accumulators)
+    constexpr uint32_t kACol = 2 * RB * 64u;  // first A-buffer column (after both accumulator sets)
     constexpr int kCodeSlot = RB * kCodeBox;  // codes of one 512-weight chunk, all rows
     extern __shared__ char smem_raw[];
     char *smem = smem_raw + ((1024u - (saddr(smem_raw) & 1023u)) & 1023u);
@@ -509,9 +521,9 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
     uint64_t *cempty = cfull + kMaxCodeSlots;
     uint64_t *aready = cempty + kMaxCodeSlots;  // [kNumA] A buffer written (16 warps)
     uint64_t *afree = aready + kNumA;           // [kNumA] A buffer read by its MMAs
-    uint64_t *dfull = afree + kNumA;
-    uint64_t *dempty = dfull + 1;
-    uint64_t *drain = dempty + 1;
+    uint64_t *dfull = afree + kNumA;  // [2] an item's accumulators final (by parity)
+    uint64_t *dempty = dfull + 2;     // [2] the epilogue warps read them
+    uint64_t *drain = dempty + 2;
     uint64_t *sfull = drain + 1;   // [2]
     uint64_t *sempty = sfull + 2;  // [2]
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sempty + 2);
@@ -542,12 +554,14 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
             bar_init(&aready[i], 16);
             bar_init(&afree[i], 1);
         }
-        bar_init(dfull, 1);
-        bar_init(dempty, 16);
+        for (int i = 0; i < 2; ++i) {
+            bar_init(&dfull[i], 1);
+            bar_init(&dempty[i], 4);
+        }
         bar_init(drain, 1);
         for (int i = 0; i < 2; ++i) {
             bar_init(&sfull[i], 64);
-            bar_init(&sempty[i], 16);
+            bar_init(&sempty[i], 16 + 4);  // dequant warps, then the epilogue warps
         }
         *abort_flag = 0;
         bar_fence_init();
@@ -661,8 +675,12 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
             const int4 tl = tiles[it / a.rblocks];
             const int npad = (tl.z + 15) & ~15;
             const uint32_t idesc = idesc_f16(kGroupRows, npad);
-            // the accumulators are free once the previous item's epilogue read them
-            if (item_i > 0 && !bar_wait(dempty, (uint32_t)(item_i - 1) & 1u, abort_flag)) {
+            // accumulator set s (item parity) is free once the epilogue warps
+            // read item i - 2's results from it
+            const int sacc = item_i & 1;
+            const uint32_t acc = tmem + (uint32_t)(sacc * RB) * 64u;
+            if (item_i >= 2 &&
+                !bar_wait(&dempty[sacc], ((uint32_t)(item_i >> 1) & 1u) ^ 1u, abort_flag)) {
                 ok = false;
                 break;
             }
@@ -683,7 +701,7 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
                         const uint64_t bdesc = sw128_desc(st + (kk >> 2) * xatom + (kk & 3) * 32);
 #pragma unroll
                         for (int j = 0; j < RB; ++j)
-                            tc_mma_ts(tmem + (uint32_t)j * 64u,
+                            tc_mma_ts(acc + (uint32_t)j * 64u,
                                       tmem + kACol + (uint32_t)(b * RB + j) * 64u + kk * 8, bdesc,
                                       idesc, (ks == 0 && kk == 0) ? 0u : 1u);
                     }
@@ -694,7 +712,7 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
             }
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
-            if (elect_one()) tc_commit(dfull);
+            if (elect_one()) tc_commit(&dfull[sacc]);
             __syncwarp();
         }
         if (!ok && lane == 0) give_up();
@@ -733,23 +751,12 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
         const uint32_t rsw = (uint32_t)(rloc & 7);  // 128-byte swizzle of this code row
         int g = 0, item_i = 0;
         for (int64_t it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++item_i) {
-            const int4 tl = tiles[it / a.rblocks];
-            const int rb = (int)(it % a.rblocks);
-            const int npad = (tl.z + 15) & ~15;
-            const int64_t rlocal = (int64_t)rb * kRows + rloc;
-            const bool row_ok = rlocal < out;
             const int buf = item_i & 1;
             if (!bar_wait(&sfull[buf], (uint32_t)(item_i >> 1) & 1u, abort_flag)) {
                 give_up();
                 break;
             }
-            const char *b = sbuf + buf * G.sb;
-            const uint32_t *sc = reinterpret_cast<const uint32_t *>(b);
-            const float *rsc =
-                reinterpret_cast<const float *>(b + scale_words(MEMBER) * KS * kRows * 4);
-            const int32_t *colp = reinterpret_cast<const int32_t *>(rsc + kRows);
-            const float *colf = rsc + kRows + kTok;
-            const float rscale = rsc[rloc];
+            const uint32_t *sc = reinterpret_cast<const uint32_t *>(sbuf + buf * G.sb);
             bool ok = true;
             for (int ks = 0; ks < KS; ++ks, ++g) {
                 const int chunk = g >> 2, cs = chunk % CS, sub = g & 3, ab = g % kNumA;
@@ -819,35 +826,78 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
                 break;
             }
             if (*abort_flag) break;
-            // Epilogue: D rows are this thread's output row, columns the tile's
-            // tokens; the KH warps of a (quarter, half) split the columns.
-            if (!bar_wait(dfull, (uint32_t)item_i & 1u, abort_flag)) {
+            // this item's scale buffer is read (the epilogue warps release it too)
+            __syncwarp();
+            if (lane == 0) bar_arrive(&sempty[buf]);
+        }
+    } else if (warp >= kEpi0 && warp < kEpi0 + 4) {
+        // Epilogue warp: TMEM lane quarter q of both row halves. Per item: copy
+        // the column table and this thread's row scales out of the scale
+        // buffer and release it at once (the loader refills it for item i + 2
+        // during item i + 1); then, once the accumulators are final (dfull of
+        // the item's parity), D rows are this thread's output rows, columns
+        // the tile's tokens: row scale and 2^-S applied, stored to y; then the
+        // accumulator set is released.
+        const int q = warp & 3;
+        const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        uint4 *ecol = reinterpret_cast<uint4 *>(smem + G.bars + kEcolOff) + (warp - kEpi0) * kTok;
+        int item_i = 0;
+        for (int64_t it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++item_i) {
+            const int4 tl = tiles[it / a.rblocks];
+            const int rb = (int)(it % a.rblocks);
+            const int npad = (tl.z + 15) & ~15;
+            const int buf = item_i & 1, sacc = item_i & 1;
+            if (!bar_wait(&sfull[buf], (uint32_t)(item_i >> 1) & 1u, abort_flag)) {
+                give_up();
+                break;
+            }
+            const char *b = sbuf + buf * G.sb;
+            const float *rsc =
+                reinterpret_cast<const float *>(b + scale_words(MEMBER) * KS * kRows * 4);
+            const int32_t *colp = reinterpret_cast<const int32_t *>(rsc + kRows);
+            const float *colf = rsc + kRows + kTok;
+            float rscale[RB];
+#pragma unroll
+            for (int j = 0; j < RB; ++j) rscale[j] = rsc[kGroupRows * j + 32 * q + lane];
+#pragma unroll
+            for (int h = 0; h < kTok / 32; ++h) {
+                const int col = 32 * h + lane;
+                const int64_t off = col < tl.z ? (int64_t)colp[col] * out : 0;
+                ecol[col] = make_uint4((uint32_t)off, (uint32_t)(off >> 32),
+                                       __float_as_uint(colf[col]), 0u);
+            }
+            __syncwarp();
+            if (lane == 0) bar_arrive(&sempty[buf]);
+            if (!bar_wait(&dfull[sacc], (uint32_t)(item_i >> 1) & 1u, abort_flag)) {
                 give_up();
                 break;
             }
             tc_fence_after();
-            for (int c = 8 * kh; c < npad; c += 8 * KH) {
-                uint32_t d[8];
-                tmem_ld8(tmem + lane_base + (uint32_t)j * 64u + c, d);
-                tc_wait_ld();
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const int col = c + k;
-                    if (col < tl.z && row_ok) {
-                        const int64_t o = (int64_t)colp[col] * out + rlocal;
-                        const float v = __uint_as_float(d[k]) * rscale * colf[col];
-                        if (a.y_dtype == IQK_F32) store_out<float>(a.y, o, v);
-                        else if (a.y_dtype == IQK_F16) store_out<__half>(a.y, o, v);
-                        else store_out<__nv_bfloat16>(a.y, o, v);
+            for (int j = 0; j < RB; ++j) {
+                const int64_t rlocal = (int64_t)rb * kRows + kGroupRows * j + 32 * q + lane;
+                const bool row_ok = rlocal < out;
+                for (int c = 0; c < npad; c += 8) {
+                    uint32_t d[8];
+                    tmem_ld8(tmem + lane_base + (uint32_t)((sacc * RB + j) * 64 + c), d);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const int col = c + k;
+                        if (col < tl.z && row_ok) {
+                            const uint4 e = ecol[col];
+                            const int64_t o = (int64_t)(((uint64_t)e.y << 32) | e.x) + rlocal;
+                            const float v = __uint_as_float(d[k]) * rscale[j] * __uint_as_float(e.z);
+                            if (a.y_dtype == IQK_F32) store_out<float>(a.y, o, v);
+                            else if (a.y_dtype == IQK_F16) store_out<__half>(a.y, o, v);
+                            else store_out<__nv_bfloat16>(a.y, o, v);
+                        }
                     }
                 }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) {
-                bar_arrive(dempty);
-                bar_arrive(&sempty[buf]);
-            }
+            if (lane == 0) bar_arrive(&dempty[sacc]);
         }
     }
     __syncthreads();
