@@ -10,6 +10,7 @@ classes. The guard functions keep the reference's names and messages
 from __future__ import annotations
 
 import ctypes
+import functools
 import os
 from pathlib import Path
 
@@ -195,14 +196,16 @@ def dequant(member: str, streams, num_experts: int, out_features: int, in_featur
     return out
 
 
+@functools.lru_cache(maxsize=1024)
 def gemv_workspace_bytes(member: str, in_features: int, x_rows: int, pairs: int) -> int:
     return int(library().iqk_gemv_workspace_bytes(MEMBER_IDS[member], in_features, x_rows, pairs))
 
 
 def gemv(member: str, x: torch.Tensor, streams, num_experts: int, out_features: int,
          in_features: int, sel: torch.Tensor, tok: torch.Tensor | None, y: torch.Tensor,
-         workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """``iqk_gemv``: x [x_rows, in], sel/tok int32 [pairs], y [pairs, out]."""
+         workspace: torch.Tensor | None = None, stream: int | None = None) -> torch.Tensor:
+    """``iqk_gemv``: x [x_rows, in], sel/tok int32 [pairs], y [pairs, out]; on
+    ``stream`` (a CUDA stream handle), else the device's current stream."""
     lib = library()
     check_device(y.device)
     pairs = sel.numel()
@@ -214,7 +217,8 @@ def gemv(member: str, x: torch.Tensor, streams, num_experts: int, out_features: 
         MEMBER_IDS[member], x.data_ptr(), DTYPE_IDS[x.dtype], x_rows, ptr_array(streams),
         num_experts, out_features, in_features, sel.data_ptr(),
         None if tok is None else tok.data_ptr(), pairs, y.data_ptr(), DTYPE_IDS[y.dtype],
-        workspace.data_ptr(), workspace.numel(), stream_handle(y.device))
+        workspace.data_ptr(), workspace.numel(),
+        stream_handle(y.device) if stream is None else stream)
     raise_for_status(status, "iqk_gemv")
     return y
 

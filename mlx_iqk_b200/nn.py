@@ -96,6 +96,8 @@ class IqkSwitchLinear(nn.Module):
         for name, shape in shapes.items():
             self.register_buffer(
                 name, torch.zeros(shape, dtype=_TORCH_DTYPES[dtypes[name].name], device=dev))
+        self._names = tuple(shapes)           # kernel input order
+        self._ws_cache: dict[int, torch.Tensor] = {}  # decode scratch per CUDA stream
 
     # -- wire streams -------------------------------------------------------
 
@@ -105,7 +107,21 @@ class IqkSwitchLinear(nn.Module):
                                      self.in_features))
 
     def _streams(self) -> list[torch.Tensor]:
-        return [getattr(self, name) for name in self.stream_names()]
+        buffers = self._buffers
+        return [buffers[name] for name in self._names]
+
+    def _workspace(self, need: int, dev: torch.device, stream: int) -> torch.Tensor:
+        """Decode scratch reused across calls on one stream (stream order keeps a
+        call's kernels after the previous call's); fresh under graph capture."""
+        if torch.cuda.is_current_stream_capturing():
+            return torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
+        ws = self._ws_cache.get(stream)
+        if ws is None or ws.numel() < need or ws.device != dev:
+            if len(self._ws_cache) >= 8:
+                self._ws_cache.clear()
+            ws = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
+            self._ws_cache[stream] = ws
+        return ws
 
     @property
     def device(self) -> torch.device:
@@ -215,11 +231,12 @@ class IqkSwitchLinear(nn.Module):
             return self.grouped(x, indices)
         return self.gemv(x, indices)
 
-    def _prep(self, x: torch.Tensor) -> torch.Tensor:
+    def _prep(self, x: torch.Tensor, dev: torch.device | None = None) -> torch.Tensor:
+        dev = self.device if dev is None else dev
         if not isinstance(x, torch.Tensor):
             x = torch.as_tensor(np.asarray(x))
-        if x.device != self.device:
-            x = x.to(self.device)
+        if x.device != dev:
+            x = x.to(dev)
         if x.dtype not in K.DTYPE_IDS:
             x = x.to(torch.float32)
         return x.reshape(-1, self.in_features).contiguous()
@@ -232,18 +249,22 @@ class IqkSwitchLinear(nn.Module):
 
     def gemv(self, x, indices) -> torch.Tensor:
         """Fused dequant + GEMV over the selected experts; valid for any pair count."""
-        xt = self._prep(x)
+        dev = self.device
+        xt = self._prep(x, dev)
         idx_shape = tuple(indices.shape)
-        sel = self._idx(indices, self.device)
+        sel = self._idx(indices, dev)
         mats, rows = sel.numel(), xt.shape[0]
         if rows <= 0 or mats % rows:
             raise IqkRuntimeError(
                 f"{mats} token-expert pairs do not tile {rows} activation "
                 f"row(s); the operand and the routing disagree")
-        y = torch.empty((mats, self.out_features), dtype=torch.float32, device=self.device)
+        y = torch.empty((mats, self.out_features), dtype=torch.float32, device=dev)
+        stream = K.stream_handle(dev)
+        ws = self._workspace(K.gemv_workspace_bytes(self.member, self.in_features, rows, mats),
+                             dev, stream)
         K.gemv(self.member, xt, self._streams(), self.num_experts, self.out_features,
-               self.in_features, sel, None, y)
-        return y.reshape(*idx_shape, self.out_features).unsqueeze(-2)
+               self.in_features, sel, None, y, ws, stream=stream)
+        return y.view(idx_shape + (1, self.out_features))
 
     def grouped(self, x, indices) -> torch.Tensor:
         """Tensor-core grouped GEMM over the selected experts (the prefill route);

@@ -3,6 +3,12 @@
     python -m mlx_iqk_b200.profile_cases gemv    --member iq2_ks --batch 8   [--reps 20] [--graph]
     python -m mlx_iqk_b200.profile_cases grouped --member iq2_ks --tokens 2048
     python -m mlx_iqk_b200.profile_cases dequant --member iq2_ks [--experts 64]
+    python -m mlx_iqk_b200.profile_cases layer   --tokens 2048
+
+``layer`` is one config-5 MoE layer through ``ExpertParallelMoE`` on one GPU
+(gate/up IQ2_KS, down IQ2_K, top-6 of 256 experts): both preparations, the
+three grouped GEMMs, the SwiGLU and combine kernels, eager (the layer reads
+its index check on the host, so it is not captured in a graph).
 
 Each case builds random relayout streams for 256 experts (the benchmark
 geometry: [2048, 4096] for gate-shaped, [4096, 2048] for down-shaped
@@ -80,7 +86,7 @@ def timed(fn, reps: int, graph: bool = False) -> float:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=("gemv", "grouped", "dequant"))
+    ap.add_argument("case", choices=("gemv", "grouped", "dequant", "layer"))
     ap.add_argument("--member", default="iq2_ks")
     ap.add_argument("--batch", type=int, default=8, help="gemv: tokens (top-6 each)")
     ap.add_argument("--tokens", type=int, default=2048, help="grouped: tokens (top-6 each)")
@@ -95,6 +101,25 @@ def main() -> None:
     n = args.width
     out = 2048 if n == 4096 else 4096
     E = args.experts
+    if args.case == "layer":
+        from .ep import ExpertParallelMoE
+        T = args.tokens
+        layer = ExpertParallelMoE(E, 4096, 2048, members=("iq2_ks", "iq2_ks", "iq2_k"),
+                                  device=dev)
+        for name in ("gate", "up", "down"):
+            m = getattr(layer, name)
+            setattr(layer, name, random_module(m.member, E, m.out_features, m.in_features,
+                                               dev, gen))
+        x = torch.randn((T, 4096), generator=gen, device=dev).to(torch.bfloat16)
+        top = torch.topk(torch.randn((T, E), generator=gen, device=dev), 6, dim=-1)
+        w = torch.softmax(top.values, dim=-1)
+        ms = timed(lambda: layer(x, top.indices, w), args.reps)
+        P = T * 6
+        flops = 2.0 * P * (2 * 2048 * 4096 + 4096 * 2048)
+        print(json.dumps({"case": "layer", "experts": E, "tokens": T, "pairs": P,
+                          "us": round(ms * 1e3, 2), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+                          "tokens_per_s": round(T / (ms * 1e-3), 1)}))
+        return
     mod = random_module(args.member, E, out, n, dev, gen)
     rb = ROW_BYTES[args.member](n)
     line = {"case": args.case, "member": args.member, "experts": E, "out": out, "in": n}
