@@ -272,6 +272,7 @@ grouped_convert_kernel(const XT *__restrict__ x, const int32_t *__restrict__ tok
                        int x_rows, int n, GroupedLayout L, char *ws) {
     __shared__ float red[8];
     __shared__ int redb[8];
+    __shared__ uint4 stage[8][64];  // per warp: its 32 threads' 32-byte blocks, in order
     const int32_t *hdr = reinterpret_cast<const int32_t *>(ws + L.hdr);
     const int pos = blockIdx.x;
     if (pos >= hdr[2]) return;
@@ -332,6 +333,7 @@ grouped_convert_kernel(const XT *__restrict__ x, const int32_t *__restrict__ tok
         reinterpret_cast<int32_t *>(ws + L.pscale)[pos] = S;
         if (bad) atomicOr(reinterpret_cast<int32_t *>(ws + L.hdr), IQK_DEVERR_NONFINITE);
     }
+    // n / 16 is a multiple of 32 (n = 2048 or 4096): a warp is all in or all out
     if (tid < nblk) {
         float f[16];
 #pragma unroll
@@ -342,10 +344,15 @@ grouped_convert_kernel(const XT *__restrict__ x, const int32_t *__restrict__ tok
             const __half2 h2 = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
             w[i] = *reinterpret_cast<const uint32_t *>(&h2);
         }
+        // staged through shared memory so that each store instruction of the
+        // warp writes 512 contiguous bytes
+        stage[wid][2 * lane] = make_uint4(w[0], w[1], w[2], w[3]);
+        stage[wid][2 * lane + 1] = make_uint4(w[4], w[5], w[6], w[7]);
+        __syncwarp();
         uint4 *dst = reinterpret_cast<uint4 *>(
-            reinterpret_cast<__half *>(ws + L.xs) + (int64_t)pos * n + tid * 16);
-        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            reinterpret_cast<__half *>(ws + L.xs) + (int64_t)pos * n + (tid - lane) * 16);
+        dst[lane] = stage[wid][lane];
+        dst[32 + lane] = stage[wid][32 + lane];
     }
 }
 
