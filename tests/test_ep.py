@@ -1,7 +1,7 @@
 """Expert-parallel layer: dispatch / combine on gloo ranks (CPU) and the
 CUDA expert path on one GPU.
 
-The CPU tests run the real dispatch and combine code on world-size-2 gloo
+The CPU tests run the real dispatch and combine code on world-size-2 and -4 gloo
 process groups; the expert GEMMs there are a host stand-in (dense float
 matrices), injected through ``expert_fn`` by the test only.
 """
@@ -82,12 +82,18 @@ def _worker(rank, world, port, errq):
         if layer.last_stats["rows_gathered"] != world * 10:
             raise AssertionError(f"rank {rank}: {layer.last_stats}")
         # a second call reuses the group, with different token counts per rank
-        x2, idx2, w2 = tokens_for(rank, T=7 - 3 * rank, seed=200)
+        # (one rank of four has none)
+        T2 = (7, 4, 0, 6)[rank]
+        x2, idx2, w2 = tokens_for(rank, T=T2, seed=200)
         got2 = layer(x2, idx2, w2).double()
-        want2 = reference_layer(x2, idx2, w2, experts)
-        err2 = float((got2 - want2).abs().max() / want2.abs().max())
-        if err2 > 2e-2:
-            raise AssertionError(f"rank {rank}: second call rel err {err2}")
+        if T2 == 0:
+            if got2.shape != (0, H):
+                raise AssertionError(f"rank {rank}: empty call gave {tuple(got2.shape)}")
+        else:
+            want2 = reference_layer(x2, idx2, w2, experts)
+            err2 = float((got2 - want2).abs().max() / want2.abs().max())
+            if err2 > 2e-2:
+                raise AssertionError(f"rank {rank}: second call rel err {err2}")
         dist.barrier()
         dist.destroy_process_group()
         errq.put((rank, None))
@@ -101,11 +107,12 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def test_dispatch_combine_on_two_gloo_ranks():
+@pytest.mark.parametrize("world", [2, 4])
+def test_dispatch_combine_on_gloo_ranks(world):
     ctx = mp.get_context("spawn")
     errq = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, errq)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, errq)) for r in range(world)]
     for p in procs:
         p.start()
     results = [errq.get(timeout=120) for _ in procs]
