@@ -369,7 +369,10 @@ class PrefillLayer:
 
 class DecodeCell:
     """One batch size of the decode workload: a pool of rotating selections and
-    activations, preallocated workspaces and outputs, and the 5-launch step."""
+    activations, preallocated workspaces and outputs, and the 5-launch step.
+    Gate and up read the same prepared activations and nothing of each other,
+    so they run on two streams: the second fills the SMs the first's last wave
+    leaves idle. Down follows both, as SiLU(gate)*up would in a model."""
 
     def __init__(self, torch, K, mods, B: int, dev, gen, seed: int):
         self.torch, self.K, self.B = torch, K, B
@@ -396,14 +399,20 @@ class DecodeCell:
         self.yu = torch.empty((self.pairs, GATE_UP[0]), device=dev)
         self.yd = torch.empty((self.pairs, DOWN[0]), device=dev)
         self.sg, self.su, self.sd = self.gate._streams(), self.up._streams(), self.down._streams()
+        self.side = torch.cuda.Stream(dev)
 
     launches = 5
 
     def step(self, s: int) -> None:
         K, p, B, P = self.K, s % self.pool, self.B, self.pairs
+        torch = self.torch
         K.gemv_prepare(self.xs[p], E, GATE_UP[1], self.sels[p].reshape(-1), None, self.ws_gu)
+        main = torch.cuda.current_stream()
+        self.side.wait_stream(main)
         K.gemv_run(MEMBER, self.sg, E, GATE_UP[0], GATE_UP[1], B, P, self.yg, self.ws_gu)
-        K.gemv_run(MEMBER, self.su, E, GATE_UP[0], GATE_UP[1], B, P, self.yu, self.ws_gu)
+        with torch.cuda.stream(self.side):
+            K.gemv_run(MEMBER, self.su, E, GATE_UP[0], GATE_UP[1], B, P, self.yu, self.ws_gu)
+        main.wait_stream(self.side)
         K.gemv_prepare(self.xds[p], E, DOWN[1], self.sels[p].reshape(-1), None, self.ws_d)
         K.gemv_run(MEMBER, self.sd, E, DOWN[0], DOWN[1], P, P, self.yd, self.ws_d)
 
