@@ -341,17 +341,23 @@ class PrefillLayer:
         self.h = torch.empty((self.pairs, DOWN[1]), device=dev, dtype=torch.bfloat16)
         self.yd = torch.empty((self.pairs, DOWN[0]), device=dev)
         self.out = torch.empty((tokens, DOWN[0]), device=dev)
+        self.side = torch.cuda.Stream(dev)
         counts = torch.bincount(self.sel.long(), minlength=E).cpu()
         self.load = {"max_pairs_per_expert": int(counts.max()),
                      "min_pairs_per_expert": int(counts.min())}
 
     def gate_up(self):
-        K = self.K
+        K, torch = self.K, self.torch
         K.grouped_prepare(self.x, E, GATE_UP[1], self.sel, None, self.ws_gu)
+        # gate and up on two streams: the second fills the first's tail
+        main = torch.cuda.current_stream()
+        self.side.wait_stream(main)
         K.grouped_run("iq2_ks", self.gate._streams(), E, GATE_UP[0], GATE_UP[1], self.pairs,
                       self.yg, self.ws_gu)
-        K.grouped_run("iq2_ks", self.up._streams(), E, GATE_UP[0], GATE_UP[1], self.pairs,
-                      self.yu, self.ws_gu)
+        with torch.cuda.stream(self.side):
+            K.grouped_run("iq2_ks", self.up._streams(), E, GATE_UP[0], GATE_UP[1], self.pairs,
+                          self.yu, self.ws_gu)
+        main.wait_stream(self.side)
 
     def down_proj(self):
         K = self.K

@@ -80,6 +80,7 @@ class ExpertParallelMoE:
             self.up = IqkSwitchLinear(u, self.local_experts, inter, hidden, device=self.device)
             self.down = IqkSwitchLinear(d, self.local_experts, hidden, inter, device=self.device)
         self.last_stats: dict = {}
+        self._side: dict = {}  # per device: the stream the up GEMM runs on
 
     # -- expert compute --------------------------------------------------
 
@@ -108,9 +109,19 @@ class ExpertParallelMoE:
         K.grouped_prepare(rows.contiguous(), El, self.hidden, s, None, ws, shard=True)
         g = torch.empty((P, self.inter), dtype=torch.float32, device=rows.device)
         u = torch.empty_like(g)
+        # gate and up read only the prepared workspace: the up GEMM runs on a
+        # side stream, so it fills the SMs the gate GEMM's last wave leaves idle
+        main = torch.cuda.current_stream(rows.device)
+        side = self._side_stream(rows.device)
+        side.wait_stream(main)
         K.grouped_run(self.gate.member, self.gate._streams(), El, self.inter, self.hidden, P,
                       g, ws)
-        K.grouped_run(self.up.member, self.up._streams(), El, self.inter, self.hidden, P, u, ws)
+        with torch.cuda.stream(side):
+            K.grouped_run(self.up.member, self.up._streams(), El, self.inter, self.hidden, P,
+                          u, ws)
+            u.record_stream(side)
+            ws.record_stream(side)
+        main.wait_stream(side)
         h = torch.empty((P, self.inter), dtype=torch.bfloat16, device=rows.device)
         K.pairs_swiglu(g, u, w.reshape(-1).contiguous(), self.hidden, El, ws, h)
         del g, u
@@ -121,6 +132,12 @@ class ExpertParallelMoE:
         K.grouped_run(self.down.member, self.down._streams(), El, self.hidden, self.inter, P,
                       y, ws_d)
         return K.pairs_combine(y, s, k, El, out)
+
+    def _side_stream(self, dev) -> torch.cuda.Stream:
+        s = self._side.get(dev)
+        if s is None:
+            s = self._side[dev] = torch.cuda.Stream(dev)
+        return s
 
     # -- dispatch / combine ----------------------------------------------
 
