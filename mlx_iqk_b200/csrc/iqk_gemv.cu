@@ -503,6 +503,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     using SS = Streams<MEMBER, N, kRows>;
     constexpr int CPW = N / kChunkK;  // 512-weight chunks per row: 8 (n=4096) or 4 (2048)
     constexpr int RPI = CPW / KQ;     // rounds per item
+    static_assert(RPI % 2 == 0, "metadata buffers alternate by round parity");
     constexpr int SSB = sslot_bytes<MEMBER, N, kRows>();
     constexpr int STB = stage_bytes<MEMBER, KQ>();
     char *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -781,10 +782,16 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     };
 
     int ti = i0 / rblocks, rb = i0 % rblocks;
+    bool prebuilt = false;  // this item's first-round metadata was built during the last item
     for (int o = 0; o < n_items; ++o) {
         const TileRef T = tile_of(ti);
         const int r0 = rb * kRows;
         const bool live = NARROW || rbase < out - r0;  // this warp's row tile exists
+        // the next item's row tile, for building its first-round metadata early
+        // (wide items only: in a two-round narrow item the extra wait measured
+        // slower)
+        const bool nlive = !NARROW && o + 1 < n_items &&
+                           rbase < out - (rb + 1 == rblocks ? 0 : rb + 1) * kRows;
         const char *sd = sslots + (o & 1) * SSB;
         // the item's scale streams
         if (!mbar_wait(&sfull[o & 1], (o >> 1) & 1)) {
@@ -795,7 +802,8 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
             break;
         }
         if (*(volatile int *)abort_flag) break;
-        if (live) build_meta(sd, chunk_of(0), meta_u);
+        if (live && !prebuilt) build_meta(sd, chunk_of(0), meta_u);
+        prebuilt = false;
         __syncwarp();
         int32_t tot[4] = {0, 0, 0, 0};
         int32_t tb[2] = {0, 0};        // IQ2_K: plane 2 (product b), rows g, g+8
@@ -932,10 +940,15 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                 }
                 // Next round's metadata into the other buffer, after the pair
                 // loop in program order so its loads and arithmetic can fill
-                // the loop's latency gaps. (After an item's last round it reads
-                // other rows' bytes of the scale slot and is never used.)
-                if (!NARROW || r + 1 < RPI)
+                // the loop's latency gaps. After a wide item's last round: the
+                // next item's first round, from its scale slot, into buffer 0
+                // (RPI is even, so this round reads buffer 1).
+                if (r + 1 < RPI) {
                     build_meta(sd, chunk_of(r + 1), meta_u + ((r + 1) & 1) * G::kMetaBytes);
+                } else if (nlive && mbar_wait(&sfull[(o + 1) & 1], ((o + 1) >> 1) & 1)) {
+                    build_meta(sslots + ((o + 1) & 1) * SSB, chunk_of(0), meta_u);
+                    prebuilt = true;
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);  // this round's stage
