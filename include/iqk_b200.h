@@ -16,8 +16,12 @@
  *                 dv f16[E,o,n/256]}
  *   IQK_IQ1_S_R4 {qs u32[E,o,n/32], qh u16[E,o,n/32], dv f16[E,o]}
  *
- * Every entry point is stream-ordered on the caller's stream and reentrant;
- * the only library state is a read-only constant table per device.
+ * Every entry point is stream-ordered on the caller's stream. Library state
+ * is a read-only constant table per device, plus one exception: the
+ * writable static scratch array of iqk_gemv_static (one copy per CUDA
+ * context). Every other entry point is reentrant; iqk_gemv_static calls that
+ * are unordered with each other in one process's context on one device race
+ * on that array.
  */
 #ifndef IQK_B200_H
 #define IQK_B200_H
@@ -249,10 +253,17 @@ int iqk_pairs_combine(const float *y, const int32_t *sel, int64_t rows, int top_
  * in_features 4096). Nothing is allocated and no byte of the scratch has to
  * start at zero. The first call on each device looks up the array's address
  * (cudaGetSymbolAddress, which may load the library's device code); make that
- * first call outside any stream capture. All calls on one device share the
- * one array, so calls that overlap in time on that device -- different
- * streams, threads or processes' graphs without an ordering between them --
- * race on it; order them on one stream. Results equal iqk_gemv's.
+ * first call outside any stream capture. Each CUDA context that loads the
+ * library holds its own copy of the array (so separate processes never share
+ * one); the address is cached per device together with the context it was
+ * resolved in and looked up again when another context is current. All calls
+ * in one context on one device share the one array, so calls that overlap in
+ * time there -- different streams or threads without an ordering between
+ * them -- race on it; order them on one stream. Results equal iqk_gemv's.
+ *
+ * iqk_gemv_static_read_error: the device error bits (IQK_DEVERR_*) of the
+ * last iqk_gemv_static call of this geometry in the current context, as
+ * iqk_read_error gives them for a workspace; synchronises the stream.
  */
 size_t iqk_gemv_static_max_bytes(void);
 
@@ -260,6 +271,9 @@ int iqk_gemv_static(int member, const void *x, int x_dtype, int64_t x_rows,
                     const void *const *streams, int64_t num_experts, int64_t out_features,
                     int64_t in_features, const int32_t *sel, const int32_t *tok,
                     int64_t pairs, void *y, int y_dtype, iqk_stream_t stream);
+
+int iqk_gemv_static_read_error(int64_t in_features, int64_t x_rows, int64_t pairs,
+                               int32_t *flags, iqk_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -35,29 +35,61 @@ constexpr int kMaxDevices = 64;
 // activation planes) before the run kernel starts.
 __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
-std::atomic<void *> g_scratch_ptr[kMaxDevices];
+// The array's address belongs to one CUDA context: every context that loads
+// this library's device code gets its own copy. The cache therefore keeps,
+// per device ordinal, the context the address was resolved in, and resolves
+// again when a different context is current (a non-primary driver context,
+// or the primary context re-created after cudaDeviceReset).
+struct ScratchEntry {
+    void *ctx = nullptr;
+    void *ptr = nullptr;
+};
+ScratchEntry g_scratch[kMaxDevices];
 std::mutex g_scratch_mutex;
 
-// Address of this device's copy of g_static_scratch. The first call on a
-// device resolves it with cudaGetSymbolAddress, which may load the library's
-// device code onto that device; later calls read the cached pointer.
+// The current driver context, through the runtime's driver entry point (the
+// library does not link libcuda). nullptr when it cannot be queried.
+void *current_context() {
+    using GetCtxFn = int (*)(void **);
+    static std::atomic<GetCtxFn> fn{nullptr};
+    GetCtxFn f = fn.load(std::memory_order_acquire);
+    if (!f) {
+        void *sym = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &sym, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !sym)
+            return nullptr;
+        f = reinterpret_cast<GetCtxFn>(sym);
+        fn.store(f, std::memory_order_release);
+    }
+    void *ctx = nullptr;
+    return f(&ctx) == 0 ? ctx : nullptr;
+}
+
+// Address of the current context's copy of g_static_scratch. The first call
+// in a context resolves it with cudaGetSymbolAddress, which may load the
+// library's device code there; later calls in that context reuse it.
 cudaError_t scratch_for_current_device(void **out) {
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if (err != cudaSuccess) return err;
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-    void *p = g_scratch_ptr[dev].load(std::memory_order_acquire);
-    if (!p) {
-        std::lock_guard<std::mutex> lock(g_scratch_mutex);
-        p = g_scratch_ptr[dev].load(std::memory_order_relaxed);
-        if (!p) {
-            err = cudaGetSymbolAddress(&p, g_static_scratch);
-            if (err != cudaSuccess) return err;
-            if (!p) return cudaErrorInvalidSymbol;
-            g_scratch_ptr[dev].store(p, std::memory_order_release);
-        }
+    // No context may be current yet (nothing else has touched the device in
+    // this thread): then resolve, which makes the primary context current,
+    // and record the context that is current afterwards.
+    void *ctx = current_context();
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    ScratchEntry &e = g_scratch[dev];
+    if (!e.ptr || !ctx || e.ctx != ctx) {
+        void *p = nullptr;
+        err = cudaGetSymbolAddress(&p, g_static_scratch);
+        if (err != cudaSuccess) return err;
+        if (!p) return cudaErrorInvalidSymbol;
+        e.ptr = p;
+        e.ctx = current_context();
     }
-    *out = p;
+    *out = e.ptr;
     return cudaSuccess;
 }
 
@@ -91,6 +123,22 @@ int iqk_gemv_static(int member, const void *x, int x_dtype, int64_t x_rows,
     return iqk_gemv(member, x, x_dtype, x_rows, streams, num_experts, out_features,
                     in_features, sel, tok, pairs, y, y_dtype, scratch, kStaticScratchBytes,
                     stream);
+}
+
+int iqk_gemv_static_read_error(int64_t in_features, int64_t x_rows, int64_t pairs,
+                               int32_t *flags, iqk_stream_t stream) {
+    if (!flags) return IQK_ERR_ARGUMENT;
+    if (in_features != 2048 && in_features != 4096) return IQK_ERR_WIDTH;
+    if (x_rows < 0 || pairs < 0 || x_rows > (1 << 24) || pairs > (1 << 24))
+        return IQK_ERR_GEOMETRY;
+    if (gemv_layout(IQK_IQ2_KS, in_features, x_rows, pairs).total > kStaticScratchBytes)
+        return IQK_ERR_WORKSPACE;
+    void *scratch = nullptr;
+    if (scratch_for_current_device(&scratch) != cudaSuccess) {
+        cudaGetLastError();
+        return IQK_ERR_CUDA;
+    }
+    return iqk_read_error(scratch, in_features, x_rows, pairs, flags, stream);
 }
 
 }  // extern "C"

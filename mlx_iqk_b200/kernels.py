@@ -122,6 +122,8 @@ def library() -> ctypes.CDLL:
     lib.iqk_gemv_static.argtypes = [i32, vp, i32, i64, vp, i64, i64, i64, vp, vp, i64, vp, i32,
                                     vp]
     lib.iqk_gemv_static.restype = i32
+    lib.iqk_gemv_static_read_error.argtypes = [i64, i64, i64, ctypes.POINTER(ctypes.c_int32), vp]
+    lib.iqk_gemv_static_read_error.restype = i32
     lib.iqk_grouped_prepare_shard.argtypes = [vp, i32, i64, i64, i64, vp, vp, i64, vp, sz, vp]
     lib.iqk_grouped_prepare_shard.restype = i32
     lib.iqk_pairs_swiglu.argtypes = [vp, vp, vp, i64, i64, i64, i64, vp, sz, vp, vp]
@@ -138,7 +140,8 @@ def exported_symbols() -> list[str]:
             "iqk_gemv_workspace_bytes", "iqk_gemv", "iqk_gemv_prepare", "iqk_gemv_run",
             "iqk_read_error", "iqk_grouped_workspace_bytes", "iqk_grouped_gemm",
             "iqk_grouped_prepare", "iqk_grouped_run", "iqk_grouped_read_error",
-            "iqk_gemv_static_max_bytes", "iqk_gemv_static", "iqk_grouped_prepare_shard",
+            "iqk_gemv_static_max_bytes", "iqk_gemv_static", "iqk_gemv_static_read_error",
+            "iqk_grouped_prepare_shard",
             "iqk_pairs_swiglu", "iqk_pairs_combine"]
 
 
@@ -261,6 +264,19 @@ def gemv_static(member: str, x: torch.Tensor, streams, num_experts: int, out_fea
         stream_handle(y.device))
     raise_for_status(status, "iqk_gemv_static")
     return y
+
+
+def gemv_static_read_error(in_features: int, x_rows: int, pairs: int,
+                           device: torch.device | None = None) -> int:
+    """``iqk_gemv_static_read_error``: the device error bits of the last
+    ``iqk_gemv_static`` call of this geometry on the current device."""
+    flags = ctypes.c_int32(0)
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    raise_for_status(library().iqk_gemv_static_read_error(in_features, x_rows, pairs,
+                                                          ctypes.byref(flags),
+                                                          stream_handle(dev)),
+                     "iqk_gemv_static_read_error")
+    return int(flags.value)
 
 
 GROUPED_MEMBERS = ("iq2_ks", "iq2_k")

@@ -388,7 +388,7 @@ def load_ref(member: str):
         return _REF[lib_name]
     path = HERE / "_ref" / lib_name
     if not path.exists():
-        raise FileNotFoundError(f"{path} not built (make -C oracle ref)")
+        raise FileNotFoundError(f"{path} not built (make -C oracle ref IQK_REF=<checkout>)")
     lib = ctypes.CDLL(str(path))
     vp, i64 = ctypes.c_void_p, ctypes.c_int64
     members = ("iq1_s_r4",) if member == "iq1_s_r4" else ("iq2_k", "iq2_ks")

@@ -1,7 +1,7 @@
 """Generate the golden vectors the oracle is pinned against, from the reference.
 
 Runs in the build container only (the reference checkout and its compiled
-codec exist there; ``make -C oracle ref`` builds the codec). Writes
+codec exist there; ``make -C oracle ref IQK_REF=<checkout>`` builds the codec). Writes
 ``tests/golden/golden.npz``; the tests read that file and never the reference.
 
 Every expected output comes from the reference's own code on the same bytes:

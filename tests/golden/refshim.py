@@ -19,8 +19,20 @@ import sys
 import types
 from pathlib import Path
 
-REF = Path(os.environ.get("IQK_REF", "/root/reference"))
 REPO = Path(__file__).resolve().parents[2]
+
+
+def _reference() -> Path:
+    """``$IQK_REF``, else the ``reference_path`` recorded in ``BASELINE.json``."""
+    import json
+    cand = os.environ.get("IQK_REF") or json.loads(
+        (REPO / "BASELINE.json").read_text()).get("reference_path")
+    if not cand or not Path(cand).is_dir():
+        raise RuntimeError("set IQK_REF to the reference checkout")
+    return Path(cand)
+
+
+REF = _reference()
 REF_LIBS = REPO / "oracle" / "_ref"
 
 

@@ -84,3 +84,43 @@ def test_static_gemv_with_explicit_rows_and_no_new_device_memory(cuda):
     K.gemv(member, x, mod._streams(), mod.num_experts, out, n, sel, tok, y_ws)
     torch.cuda.synchronize()
     assert torch.equal(y_ws, y_st)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n,x_rows,pairs", [(4096, 64, 512), (2048, 128, 768)])
+def test_static_gemv_at_the_largest_geometry_that_fits(cuda, n, x_rows, pairs):
+    """The documented limit: scratch use within a few percent of the array,
+    explicit activation rows, equal to iqk_gemv bit for bit."""
+    member, experts, out = "iq2_ks", 16, 64
+    assert K.gemv_workspace_bytes(member, n, x_rows, pairs) > 0.85 * SCRATCH_BYTES
+    assert K.gemv_workspace_bytes(member, n, x_rows, pairs) <= SCRATCH_BYTES
+    mod, _, _ = make_module(member, n, seed=77 + n, experts=experts, out_features=out)
+    g = torch.Generator(device="cuda").manual_seed(n)
+    x = torch.randn((x_rows, n), generator=g, device="cuda").to(torch.bfloat16)
+    sel = torch.randint(0, experts, (pairs,), generator=g, device="cuda", dtype=torch.int32)
+    tok = torch.randint(0, x_rows, (pairs,), generator=g, device="cuda", dtype=torch.int32)
+    y_ws = torch.empty((pairs, out), device="cuda")
+    y_st = torch.full((pairs, out), float("nan"), device="cuda")
+    for _ in range(2):
+        K.gemv_static(member, x, mod._streams(), experts, out, n, sel, tok, y_st)
+    K.gemv(member, x, mod._streams(), experts, out, n, sel, tok, y_ws)
+    torch.cuda.synchronize()
+    assert torch.equal(y_ws, y_st)
+    assert K.gemv_static_read_error(n, x_rows, pairs) == 0
+
+
+@pytest.mark.gpu
+def test_static_gemv_reports_a_bad_expert_index(cuda):
+    """An out-of-range expert index made on the host: zeros for that pair and
+    IQK_DEVERR_EXPERT through iqk_gemv_static_read_error."""
+    member, n, experts, out = "iq2_k", 2048, 8, 32
+    mod, _, _ = make_module(member, n, seed=91, experts=experts, out_features=out)
+    x = torch.randn((2, n), device="cuda")
+    sel = torch.tensor([1, 99, 2, 3], dtype=torch.int32, device="cuda")
+    y = torch.full((4, out), 7.0, device="cuda")
+    K.gemv_static(member, x, mod._streams(), experts, out, n, sel, None, y)
+    assert K.gemv_static_read_error(n, 2, 4) & K.DEVERR_EXPERT
+    assert torch.all(y[1] == 0)
+    ok = torch.tensor([1, 2, 3, 0], dtype=torch.int32, device="cuda")
+    K.gemv_static(member, x, mod._streams(), experts, out, n, ok, None, y)
+    assert K.gemv_static_read_error(n, 2, 4) == 0
