@@ -1,28 +1,42 @@
-"""Routed-decode benchmark: IQ2_KS, 256 experts, top-6.
+"""Routed-expert benchmark (BASELINE config 2 headline, configs 1/3/4/5 as legs).
 
-One step = one MoE layer's routed projections for one decode step at each
-batch size of the configuration (B = 1, 4 and 8 tokens): gate and up
-([2048, 4096] per expert) and down ([4096, 2048] per expert), each through
-the fused dequant+GEMV kernels of libiqk_b200.so. The gate and up projections
-share one preparation (iqk_gemv_prepare), the down projection gets its own
-(one activation row per pair). Per-batch figures are reported under "sweep".
+Headline step = one MoE layer's routed projections for one decode step at each
+batch size B = 1, 4, 8: IQ2_KS gate and up
+([2048, 4096] per expert) and down ([4096, 2048] per expert), 256 experts,
+top-6, through the fused dequant+GEMV kernels of libiqk_b200.so. Gate and up
+share one preparation (iqk_gemv_prepare); down gets its own.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--batches 1,4,8] [--impl reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
 Metric: achieved GB/s of algorithmic bytes = the distinct (expert,
-projection) weight rows each step must stream (the reference's byte model,
+projection) weight rows a step must stream (the reference's byte model,
 bench/price.py:146, duplicates counted once) plus activations and outputs,
-divided by the device time of exactly K steps. Inputs: random IQ2_KS streams
-(uniform code/scale bytes, fp16 row scales at serving magnitudes, the
+over the device time of exactly K steps (CUDA graph replay, CUDA events,
+max over ranks). Inputs: random relayout streams at serving scales (the
 reference's own pricing inputs, bench/price.py:124), x ~ N(0,1) bf16, six
-distinct experts per token. Step selections rotate so no expert recurs within
-a window whose weight bytes exceed twice the 126 MB L2: no step can be served
-from L2. At N>1 every rank runs an independent replica (decode does not
-shard; weak scaling).
+distinct experts per token; selections rotate so that no expert recurs within
+a window whose weight bytes exceed twice the 126 MB L2.
 
-``--impl reference`` times the reference's own CPU path for the same step
-(vendored ik_llama dequantizer compiled from the reference's sources into
-oracle/_ref, then a numpy matvec) on all host cores.
+Legs on one GPU (each a line under its own key):
+  roofline   the gate GEMV at B=8 alone, beside its address floor
+             (iqk_gemv_floor_run: same copies, decode deleted -- the
+             reference's "vs own floor" ratio, bench/floors.py)
+  configs    config 1 (one IQ2_KS expert, fp32 x), config 3 (IQ2_K at
+             B = 1/16/64, unsorted and sorted), config 4 (IQ1_S_R4 at
+             B = 1..8), all through IqkSwitchLinear.__call__
+  dequant    the bit-exact dequantization of each member beside its floor
+  prefill    config 5 (one layer, gate/up IQ2_KS, down IQ2_K, 2048 tokens)
+             on one GPU and through the expert-parallel layer at every N,
+             with the expert-parallel output checked against the one-GPU
+             computation of the same tokens
+  e2e        the headline step through the public module API with pinned
+             host inputs and outputs copied inside the timed region
+At N>1 every rank runs an independent decode replica (weak scaling); the
+prefill layer shards experts and tokens (strong scaling).
+
+``--impl reference`` times the reference's own CPU path (the vendored
+ik_llama dequantizer compiled from the reference's sources into oracle/_ref,
+then a numpy matmul) on the host cores, one BLAS thread per worker.
 """
 
 from __future__ import annotations
@@ -35,7 +49,6 @@ import statistics
 import sys
 import threading
 import time
-from collections import deque
 from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
@@ -49,9 +62,8 @@ GATE_UP = (2048, 4096)   # out, in
 DOWN = (4096, 2048)
 MEMBER = "iq2_ks"
 L2_BYTES = 126 * 2 ** 20
-# dram__bytes_read.sum + dram__bytes_write.sum of one gate GEMV launch at B=8,
-# measured by ncu on this kernel build (reported as roofline.traffic).
-GATE_B8_DRAM_BYTES = 111.57e6
+# dram bytes of one gate GEMV launch at B=8 from the committed ncu capture
+TRAFFIC_FILE = REPO / "profiles" / "gemv_iq2ks_gate_b8_traffic.json"
 
 
 def row_bytes(member: str, n: int) -> int:
@@ -59,11 +71,15 @@ def row_bytes(member: str, n: int) -> int:
             "iq1_s_r4": 2 + 6 * (n // 32)}[member]
 
 
-def expert_bytes_per_step(batch: int) -> float:
+def layer_row_bytes(member: str) -> int:
+    """Weight bytes of one expert's gate + up + down."""
+    return 2 * GATE_UP[0] * row_bytes(member, GATE_UP[1]) + DOWN[0] * row_bytes(member, DOWN[1])
+
+
+def expert_bytes_per_step(batch: int, member: str = MEMBER) -> float:
     """Expected weight bytes of one step at uniform top-6 (planning only)."""
     distinct = E * (1 - ((E - TOP_K) / E) ** batch)
-    return distinct * (2 * GATE_UP[0] * row_bytes(MEMBER, GATE_UP[1])
-                       + DOWN[0] * row_bytes(MEMBER, DOWN[1]))
+    return distinct * layer_row_bytes(member)
 
 
 def make_selections(pool: int, batch: int, window: int, seed: int) -> np.ndarray:
@@ -91,6 +107,10 @@ def make_selections(pool: int, batch: int, window: int, seed: int) -> np.ndarray
         used[s] = set()
         draw(s)
     return sels
+
+
+def l2_window(batch: int, member: str = MEMBER) -> int:
+    return max(1, math.ceil(2 * L2_BYTES / expert_bytes_per_step(batch, member)))
 
 
 # --------------------------------------------------------------- clocks
@@ -152,15 +172,36 @@ class ClockSampler:
 
 # ---------------------------------------------------------- CPU baseline
 
-def cpu_path(batches, steps: int, seconds: float, seed: int) -> dict:
-    """The reference's CPU path on sampled decode steps: ik's dequantizer on
-    the selected experts' wire rows, then a float32 matvec, all host cores.
-    One step = one decode step at each batch size in `batches`."""
+def cpu_info() -> dict:
+    model = "unknown"
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle
+    return {"cpu_model": model, "host_cores": oracle.cpu_count()}
+
+
+def _oracle():
     sys.path.insert(0, str(REPO / "oracle"))
     import oracle
     kind = "reference" if oracle.ref_available() else "port"
     deq = oracle.ref_dequantize if kind == "reference" else oracle.dequant_wire
-    cores = oracle.cpu_count()
+    return oracle, kind, deq
+
+
+def cpu_decode(batches, steps: int, seconds: float, seed: int, workers: int) -> dict:
+    """The reference's CPU decode path on sampled decode steps: ik's
+    dequantizer on the selected experts' wire rows, then a float32 matmul.
+    ``workers`` threads over (projection, expert) jobs, each job's BLAS on one
+    thread (ik's dequantizer is single-threaded; the ctypes call and numpy
+    release the GIL), so ``workers`` is the core count used."""
+    from threadpoolctl import threadpool_limits
+    oracle, kind, deq = _oracle()
     cache: dict[tuple[str, int], np.ndarray] = {}
 
     def wire_for(proj: str, e: int) -> np.ndarray:
@@ -173,7 +214,6 @@ def cpu_path(batches, steps: int, seconds: float, seed: int) -> dict:
 
     sels_by_b = {b: make_selections(min(max(steps, 1), 64), b, 1, seed + b) for b in batches}
     rng = np.random.default_rng(seed + 1)
-    pool = ThreadPoolExecutor(max_workers=cores)
 
     def one(args):
         proj, e, xs = args
@@ -182,31 +222,92 @@ def cpu_path(batches, steps: int, seconds: float, seed: int) -> dict:
         return w @ xs.T
 
     done, total_bytes, t_all = 0, 0.0, 0.0
-    for s in range(steps):
-        for batch in batches:
-            sels = sels_by_b[batch]
-            sel_s = sels[s % sels.shape[0]]
-            experts = sorted(set(sel_s.ravel().tolist()))
-            for proj in ("gate", "up", "down"):
-                for e in experts:
-                    wire_for(proj, e)  # generation is input staging, not timed
-            x = rng.standard_normal((batch, GATE_UP[1])).astype(np.float32)
-            xd = rng.standard_normal((batch * TOP_K, DOWN[1])).astype(np.float32)
-            jobs = [(p, e, x) for p in ("gate", "up") for e in experts] + \
-                   [("down", e, xd[np.nonzero(sel_s.ravel() == e)[0]]) for e in experts]
-            t0 = time.perf_counter()
-            list(pool.map(one, jobs))
-            t_all += time.perf_counter() - t0
-            total_bytes += len(experts) * (2 * GATE_UP[0] * row_bytes(MEMBER, GATE_UP[1])
-                                           + DOWN[0] * row_bytes(MEMBER, DOWN[1]))
-        done += 1
-        if t_all > seconds:
-            break
-    pool.shutdown()
-    return {"value": total_bytes / t_all / 1e9, "unit": "GB/s", "cores": cores, "kind": kind,
+    with threadpool_limits(limits=1), ThreadPoolExecutor(max_workers=workers) as pool:
+        for s in range(steps):
+            for batch in batches:
+                sel_s = sels_by_b[batch][s % sels_by_b[batch].shape[0]]
+                experts = sorted(set(sel_s.ravel().tolist()))
+                for proj in ("gate", "up", "down"):
+                    for e in experts:
+                        wire_for(proj, e)  # generation is input staging, not timed
+                x = rng.standard_normal((batch, GATE_UP[1])).astype(np.float32)
+                xd = rng.standard_normal((batch * TOP_K, DOWN[1])).astype(np.float32)
+                jobs = [(p, e, x) for p in ("gate", "up") for e in experts] + \
+                       [("down", e, xd[np.nonzero(sel_s.ravel() == e)[0]]) for e in experts]
+                t0 = time.perf_counter()
+                list(pool.map(one, jobs))
+                t_all += time.perf_counter() - t0
+                total_bytes += len(experts) * layer_row_bytes(MEMBER)
+            done += 1
+            if t_all > seconds:
+                break
+    return {"value": total_bytes / t_all / 1e9, "unit": "GB/s", "cores": workers, "kind": kind,
             "sample": f"{done} decode steps at each B in {batches} (gate+up+down of the "
-                      f"selected experts): ik dequantize + float32 numpy matvec, {cores} threads",
-            "ms_per_step": 1e3 * t_all / max(done, 1)}
+                      f"selected experts): ik dequantize + float32 numpy matmul, {workers} "
+                      f"worker thread(s), one BLAS thread each",
+            "ms_per_step": 1e3 * t_all / max(done, 1), "steps": done}
+
+
+def cpu_prefill(seconds: float, workers: int, seed: int = 77) -> dict:
+    """Config 5 on the CPU, the reference's prefill path: per expert, ik's
+    dequantizer on gate, up (IQ2_KS) and down (IQ2_K), then the expert's
+    token group through silu(x Wg^T) * (x Wu^T) and down, float32 numpy.
+    A bounded sample of experts (48 tokens each, the config's mean load) is
+    timed with ``workers`` threads; the layer time is the sample's
+    per-expert throughput times 256 experts."""
+    from threadpoolctl import threadpool_limits
+    oracle, kind, deq = _oracle()
+    pool_n = max(4, workers)
+    wires = [(oracle.random_wire("iq2_ks", GATE_UP[0], GATE_UP[1], seed=seed + 3 * i,
+                                 scales="serving"),
+              oracle.random_wire("iq2_ks", GATE_UP[0], GATE_UP[1], seed=seed + 3 * i + 1,
+                                 scales="serving"),
+              oracle.random_wire("iq2_k", DOWN[0], DOWN[1], seed=seed + 3 * i + 2,
+                                 scales="serving")) for i in range(pool_n)]
+    rng = np.random.default_rng(seed)
+    tok = 2048 * TOP_K // E
+    xs = [rng.standard_normal((tok, GATE_UP[1])).astype(np.float32) for _ in range(pool_n)]
+
+    def one(i):
+        wg, wu, wd = wires[i % pool_n]
+        x = xs[i % pool_n]
+        g = x @ deq("iq2_ks", wg, GATE_UP[1]).T
+        u = x @ deq("iq2_ks", wu, GATE_UP[1]).T
+        h = g / (1.0 + np.exp(-g)) * u
+        return h @ deq("iq2_k", wd, DOWN[1]).T
+
+    done, t_all = 0, 0.0
+    with threadpool_limits(limits=1), ThreadPoolExecutor(max_workers=workers) as pool:
+        list(pool.map(one, range(workers)))  # warm
+        while t_all < seconds or done == 0:
+            t0 = time.perf_counter()
+            list(pool.map(one, range(done, done + workers)))
+            t_all += time.perf_counter() - t0
+            done += workers
+    layer_s = t_all / done * E
+    return {"value": round(2048 / layer_s, 2), "unit": "tokens/s", "cores": workers,
+            "kind": kind, "layer_ms": round(1e3 * layer_s, 1),
+            "sample": f"{done} experts x (gate+up+down) with {tok} tokens each: ik dequantize "
+                      f"+ float32 numpy, {workers} worker thread(s), one BLAS thread each; "
+                      f"layer = 256 experts at the sample's per-expert throughput"}
+
+
+def cpu_baselines(batches, seconds: float) -> dict:
+    """All-core decode (the headline cpu_baseline), plus single-core decode and
+    the prefill layer on all cores and on one, within about ``seconds``."""
+    info = cpu_info()
+    cores = info["host_cores"]
+    allc = cpu_decode(batches, 10 ** 6, 0.4 * seconds, seed=4321, workers=cores)
+    one = cpu_decode(batches, 10 ** 6, 0.2 * seconds, seed=4321, workers=1)
+    pre_all = cpu_prefill(0.25 * seconds, cores)
+    pre_one = cpu_prefill(0.15 * seconds, 1)
+    out = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in allc.items()
+           if k in ("value", "unit", "cores", "kind", "sample")}
+    out.update(info)
+    out["single_core"] = {"value": round(one["value"], 4), "unit": "GB/s", "cores": 1,
+                          "sample": one["sample"]}
+    out["prefill"] = {"all_cores": pre_all, "single_core": pre_one}
+    return out
 
 
 def run_reference(args) -> None:
@@ -214,17 +315,23 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     batches = [int(b) for b in args.batches.split(",")]
-    warm = cpu_path(batches, max(1, min(args.warmup, 2)), 1e9, seed=99)
-    del warm
-    res = cpu_path(batches, args.steps, args.cpu_seconds * 6, seed=1234)
+    info = cpu_info()
+    cores = info["host_cores"]
+    cpu_decode(batches, max(1, min(args.warmup, 2)), 1e9, seed=99, workers=cores)  # warm
+    res = cpu_decode(batches, args.steps, args.cpu_seconds * 6, seed=1234, workers=cores)
+    one = cpu_decode(batches, 10 ** 6, args.cpu_seconds, seed=1234, workers=1)
+    pre = cpu_prefill(args.cpu_seconds, cores)
     line = {
         "impl": "reference", "metric": metric_name(batches), "value": round(res["value"], 4),
         "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(res["ms_per_step"], 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32 dequant, f32 matvec",
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 dequant, f32 matmul",
         "data": "synthetic", "config": config(args, batches),
         "cpu_baseline": {"value": round(res["value"], 4), "unit": "GB/s", "cores": res["cores"],
-                         "kind": res["kind"], "sample": res["sample"]},
+                         "kind": res["kind"], "sample": res["sample"], **info,
+                         "single_core": {"value": round(one["value"], 4), "unit": "GB/s",
+                                         "cores": 1, "sample": one["sample"]},
+                         "prefill": pre},
         "e2e": {"value": round(res["value"], 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -248,158 +355,47 @@ def config(args, batches) -> dict:
             "parallelism": f"replicas x{args.gpus}"}
 
 
-def random_streams(torch, out: int, n: int, gen, dev, member: str = "iq2_ks",
-                   experts: int | None = None):
-    """Uniform random relayout streams on the device, serving scales."""
-    E = experts or globals()["E"]
-    def u8(count):
-        return torch.randint(0, 256, (count,), generator=gen, device=dev, dtype=torch.uint8)
-
-    def scales(shape):
-        mag = torch.rand(shape, generator=gen, device=dev) * 8e-4 + 2e-5
-        sign = torch.where(torch.rand(shape, generator=gen, device=dev) < 0.5, -1.0, 1.0)
-        return (mag * sign).to(torch.float16)
-
-    if member == "iq2_ks":
-        return {"qs": u8(E * out * n // 4).view(torch.uint32).reshape(E, out, n // 16),
-                "scl": u8(E * out * n // 64).reshape(E, out, n // 64),
-                "sch": u8(E * out * n // 256).reshape(E, out, n // 256),
-                "sex": u8(E * out * n // 256).reshape(E, out, n // 256),
-                "dv": scales((E, out))}
-    return {"qs": u8(E * out * n // 4).view(torch.uint32).reshape(E, out, n // 16),
-            "scl": u8(E * out * n // 32).reshape(E, out, n // 32),
-            "sex": u8(E * out * n // 128).reshape(E, out, n // 128),
-            "dv": scales((E, out, n // 256))}
-
-
-# ---------------------------------------------------------------- prefill
-
-PREFILL_TOKENS = 2048
-
-
-def prefill_flops(pairs: int) -> float:
-    return 2.0 * pairs * (2 * GATE_UP[0] * GATE_UP[1] + DOWN[0] * DOWN[1])
-
-
-def measure_ep_prefill(torch, dist, K, dev, world, rank, barrier, max_over_ranks, steps):
-    """Config 5 through ExpertParallelMoE: ms per layer step, max over ranks."""
-    from mlx_iqk_b200.ep import ExpertParallelMoE
-    gen = torch.Generator(device=dev).manual_seed(2000 + rank)
-    layer = ExpertParallelMoE(E, GATE_UP[1], GATE_UP[0], members=("iq2_ks", "iq2_ks", "iq2_k"),
-                              device=dev)
-    for mod in (layer.gate, layer.up, layer.down):
-        mod.load_streams(random_streams(torch, mod.out_features, mod.in_features, gen, dev,
-                                        mod.member, experts=layer.local_experts))
-    T = PREFILL_TOKENS // world
-    x = torch.randn((T, GATE_UP[1]), generator=gen, device=dev).to(torch.bfloat16)
-    logits = torch.randn((T, E), generator=gen, device=dev)
-    top = torch.topk(logits, TOP_K, dim=-1)
-    w = torch.softmax(top.values, dim=-1)
-    for _ in range(3):
-        layer(x, top.indices, w)
-    stream = torch.cuda.current_stream(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    e0.record(stream)
-    for _ in range(steps):
-        layer(x, top.indices, w)
-    e1.record(stream)
-    e1.synchronize()
-    barrier()
-    return max_over_ranks(e0.elapsed_time(e1) / steps)
-
-
-class PrefillLayer:
-    """BASELINE config 5 on one GPU: one MoE layer, gate/up IQ2_KS and down
-    IQ2_K over all 256 experts, T tokens routed top-6 by N(0,1) logits
-    (mildly skewed load), sorted_indices=True, through the grouped GEMM.
-    Step = prepare(x) + gate + up + SiLU(gate)*up*router weight (one pass
-    over the routed pairs) + prepare(h) + down + each token's sum over its
-    slots -- the kernels ExpertParallelMoE runs on every rank."""
-
-    def __init__(self, torch, K, dev, gen, tokens: int = PREFILL_TOKENS):
-        from mlx_iqk_b200 import IqkSwitchLinear
-        self.torch, self.K, self.T = torch, K, tokens
-        self.gate = IqkSwitchLinear("iq2_ks", E, *GATE_UP, device=dev)
-        self.up = IqkSwitchLinear("iq2_ks", E, *GATE_UP, device=dev)
-        self.down = IqkSwitchLinear("iq2_k", E, *DOWN, device=dev)
-        for mod in (self.gate, self.up, self.down):
-            mod.load_streams(random_streams(torch, mod.out_features, mod.in_features, gen, dev,
-                                            mod.member))
-        logits = torch.randn((tokens, E), generator=gen, device=dev)
-        top = torch.topk(logits, TOP_K, dim=-1)
-        self.weights = torch.softmax(top.values, dim=-1).reshape(-1).contiguous()
-        self.sel = top.indices.to(torch.int32).reshape(-1).contiguous()
-        self.pairs = self.sel.numel()
-        self.x = torch.randn((tokens, GATE_UP[1]), generator=gen, device=dev).to(torch.bfloat16)
-        self.ws_gu = torch.empty(K.grouped_workspace_bytes(GATE_UP[1], E, self.pairs),
-                                 dtype=torch.uint8, device=dev)
-        self.ws_d = torch.empty(K.grouped_workspace_bytes(DOWN[1], E, self.pairs),
-                                dtype=torch.uint8, device=dev)
-        self.yg = torch.empty((self.pairs, GATE_UP[0]), device=dev)
-        self.yu = torch.empty((self.pairs, GATE_UP[0]), device=dev)
-        self.h = torch.empty((self.pairs, DOWN[1]), device=dev, dtype=torch.bfloat16)
-        self.yd = torch.empty((self.pairs, DOWN[0]), device=dev)
-        self.out = torch.empty((tokens, DOWN[0]), device=dev)
-        self.side = torch.cuda.Stream(dev)
-        counts = torch.bincount(self.sel.long(), minlength=E).cpu()
-        self.load = {"max_pairs_per_expert": int(counts.max()),
-                     "min_pairs_per_expert": int(counts.min())}
-
-    def gate_up(self):
-        K, torch = self.K, self.torch
-        K.grouped_prepare(self.x, E, GATE_UP[1], self.sel, None, self.ws_gu)
-        # gate and up on two streams: the second fills the first's tail
-        main = torch.cuda.current_stream()
-        self.side.wait_stream(main)
-        K.grouped_run("iq2_ks", self.gate._streams(), E, GATE_UP[0], GATE_UP[1], self.pairs,
-                      self.yg, self.ws_gu)
-        with torch.cuda.stream(self.side):
-            K.grouped_run("iq2_ks", self.up._streams(), E, GATE_UP[0], GATE_UP[1], self.pairs,
-                          self.yu, self.ws_gu)
-        main.wait_stream(self.side)
-
-    def down_proj(self):
-        K = self.K
-        K.grouped_prepare(self.h, E, DOWN[1], self.sel, None, self.ws_d)
-        K.grouped_run("iq2_k", self.down._streams(), E, DOWN[0], DOWN[1], self.pairs, self.yd,
-                      self.ws_d)
-
-    def step(self):
-        K = self.K
-        self.gate_up()
-        K.pairs_swiglu(self.yg, self.yu, self.weights, GATE_UP[1], E, self.ws_gu, self.h)
-        self.down_proj()
-        K.pairs_combine(self.yd, self.sel, TOP_K, E, self.out)
+def layer_modules(torch, member: str, dev, gen, experts: int | None = None):
+    """gate, up ([2048, 4096]) and down ([4096, 2048]) of one member, random
+    relayout streams at serving scales."""
+    from mlx_iqk_b200 import IqkSwitchLinear
+    from mlx_iqk_b200.profile_cases import random_streams
+    ne = experts or E
+    mods = []
+    for out, n in (GATE_UP, GATE_UP, DOWN):
+        m = IqkSwitchLinear(member, ne, out, n, device=dev)
+        m.load_streams(random_streams(member, ne, out, n, dev, gen))
+        mods.append(m)
+    return mods
 
 
 class DecodeCell:
-    """One batch size of the decode workload: a pool of rotating selections and
-    activations, preallocated workspaces and outputs, and the 5-launch step.
-    Gate and up read the same prepared activations and nothing of each other,
-    so they run on two streams: the second fills the SMs the first's last wave
-    leaves idle. Down follows both, as SiLU(gate)*up would in a model."""
+    """One batch size of the headline decode step on the kernel entry points:
+    a pool of rotating selections and activations, preallocated workspaces
+    and outputs, and the 5-launch step. Gate and up read the same prepared
+    activations and nothing of each other, so they run on two streams: the
+    second fills the SMs the first's last wave leaves idle. Down follows
+    both, as SiLU(gate)*up would in a model."""
 
-    def __init__(self, torch, K, mods, B: int, dev, gen, seed: int):
-        self.torch, self.K, self.B = torch, K, B
+    launches = 5
+
+    def __init__(self, torch, K, mods, B: int, dev, gen, seed: int, member: str = MEMBER):
+        self.torch, self.K, self.B, self.member = torch, K, B, member
         self.gate, self.up, self.down = mods
-        window = max(1, math.ceil(2 * L2_BYTES / expert_bytes_per_step(B)))
         self.pool = 128
-        self.sels_np = make_selections(self.pool, B, window, seed=seed)
+        self.sels_np = make_selections(self.pool, B, l2_window(B, member), seed=seed)
         self.sels = torch.from_numpy(self.sels_np).to(dev, torch.int32)
         self.xs = torch.randn((self.pool, B, GATE_UP[1]), generator=gen, device=dev).to(torch.bfloat16)
         self.xds = torch.randn((self.pool, B * TOP_K, DOWN[1]), generator=gen, device=dev).to(torch.bfloat16)
-        rb_gu, rb_d = row_bytes(MEMBER, GATE_UP[1]), row_bytes(MEMBER, DOWN[1])
-        self.rb_gu = rb_gu
+        self.rb_gu = row_bytes(member, GATE_UP[1])
         act = (B * GATE_UP[1] * 2 + B * TOP_K * DOWN[1] * 2          # x, x_down (bf16)
                + B * TOP_K * (2 * GATE_UP[0] + DOWN[0]) * 4)          # y (f32)
-        self.step_bytes = [len(set(self.sels_np[s].ravel().tolist()))
-                           * (2 * GATE_UP[0] * rb_gu + DOWN[0] * rb_d) + act
-                           for s in range(self.pool)]
+        self.step_bytes = [len(set(self.sels_np[s].ravel().tolist())) * layer_row_bytes(member)
+                           + act for s in range(self.pool)]
         self.pairs = B * TOP_K
-        self.ws_gu = torch.empty(K.gemv_workspace_bytes(MEMBER, GATE_UP[1], B, self.pairs),
+        self.ws_gu = torch.empty(K.gemv_workspace_bytes(member, GATE_UP[1], B, self.pairs),
                                  dtype=torch.uint8, device=dev)
-        self.ws_d = torch.empty(K.gemv_workspace_bytes(MEMBER, DOWN[1], self.pairs, self.pairs),
+        self.ws_d = torch.empty(K.gemv_workspace_bytes(member, DOWN[1], self.pairs, self.pairs),
                                 dtype=torch.uint8, device=dev)
         self.yg = torch.empty((self.pairs, GATE_UP[0]), device=dev)
         self.yu = torch.empty((self.pairs, GATE_UP[0]), device=dev)
@@ -407,20 +403,55 @@ class DecodeCell:
         self.sg, self.su, self.sd = self.gate._streams(), self.up._streams(), self.down._streams()
         self.side = torch.cuda.Stream(dev)
 
-    launches = 5
-
     def step(self, s: int) -> None:
-        K, p, B, P = self.K, s % self.pool, self.B, self.pairs
+        K, p, B, P, M = self.K, s % self.pool, self.B, self.pairs, self.member
         torch = self.torch
         K.gemv_prepare(self.xs[p], E, GATE_UP[1], self.sels[p].reshape(-1), None, self.ws_gu)
         main = torch.cuda.current_stream()
         self.side.wait_stream(main)
-        K.gemv_run(MEMBER, self.sg, E, GATE_UP[0], GATE_UP[1], B, P, self.yg, self.ws_gu)
+        K.gemv_run(M, self.sg, E, GATE_UP[0], GATE_UP[1], B, P, self.yg, self.ws_gu)
         with torch.cuda.stream(self.side):
-            K.gemv_run(MEMBER, self.su, E, GATE_UP[0], GATE_UP[1], B, P, self.yu, self.ws_gu)
+            K.gemv_run(M, self.su, E, GATE_UP[0], GATE_UP[1], B, P, self.yu, self.ws_gu)
         main.wait_stream(self.side)
         K.gemv_prepare(self.xds[p], E, DOWN[1], self.sels[p].reshape(-1), None, self.ws_d)
-        K.gemv_run(MEMBER, self.sd, E, DOWN[0], DOWN[1], P, P, self.yd, self.ws_d)
+        K.gemv_run(M, self.sd, E, DOWN[0], DOWN[1], P, P, self.yd, self.ws_d)
+
+    def bytes(self, s: int) -> int:
+        return self.step_bytes[s % self.pool]
+
+
+class ModuleCell:
+    """One decode (or sorted) step of a member's layer through the public
+    module API, ``IqkSwitchLinear.__call__`` -- the route the drop-in takes:
+    gate(x), up(x) and down(x_down), each with the same routing. With
+    ``sorted_flat`` the flattened expert ids arrive in order and the call says
+    so (sorted_indices=True), as the reference's sorted dispatch does."""
+
+    def __init__(self, torch, mods, B: int, dev, gen, seed: int, member: str,
+                 sorted_flat: bool = False):
+        self.torch, self.B, self.sorted = torch, B, sorted_flat
+        self.gate, self.up, self.down = mods
+        self.pool = 64
+        sels = make_selections(self.pool, B, l2_window(B, member), seed=seed)
+        if sorted_flat:
+            sels = np.sort(sels.reshape(self.pool, -1), axis=1).reshape(sels.shape)
+        self.sels_np = sels
+        self.sels = torch.from_numpy(sels).to(dev, torch.int32)
+        self.xs = torch.randn((self.pool, B, 1, 1, GATE_UP[1]), generator=gen,
+                              device=dev).to(torch.bfloat16)
+        self.xds = torch.randn((self.pool, B, TOP_K, 1, DOWN[1]), generator=gen,
+                               device=dev).to(torch.bfloat16)
+        act = (B * GATE_UP[1] * 2 + B * TOP_K * DOWN[1] * 2
+               + B * TOP_K * (2 * GATE_UP[0] + DOWN[0]) * 4)
+        self.step_bytes = [len(set(sels[s].ravel().tolist())) * layer_row_bytes(member) + act
+                           for s in range(self.pool)]
+
+    def step(self, s: int) -> None:
+        p = s % self.pool
+        idx = self.sels[p]
+        self.gate(self.xs[p], idx, sorted_indices=self.sorted)
+        self.up(self.xs[p], idx, sorted_indices=self.sorted)
+        self.down(self.xds[p], idx, sorted_indices=self.sorted)
 
     def bytes(self, s: int) -> int:
         return self.step_bytes[s % self.pool]
@@ -436,11 +467,311 @@ class _Eager:
         self.fn()
 
 
+# ---------------------------------------------------------------- prefill
+
+PREFILL_TOKENS = 2048
+
+
+def prefill_flops(pairs: int) -> float:
+    return 2.0 * pairs * (2 * GATE_UP[0] * GATE_UP[1] + DOWN[0] * DOWN[1])
+
+
+def prefill_inputs(torch, dev, seed: int = 2024):
+    """Config 5 inputs, identical on every rank: x ~ N(0,1) bf16 [2048, 4096],
+    top-6 of N(0,1) router logits (mildly skewed load), softmax weights."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn((PREFILL_TOKENS, GATE_UP[1]), generator=g, device=dev).to(torch.bfloat16)
+    logits = torch.randn((PREFILL_TOKENS, E), generator=g, device=dev)
+    top = torch.topk(logits, TOP_K, dim=-1)
+    return x, top.indices.to(torch.int32), torch.softmax(top.values, dim=-1)
+
+
+class PrefillLayer:
+    """BASELINE config 5 on one GPU: one MoE layer (gate/up IQ2_KS, down
+    IQ2_K) over all of ``mods``' experts, tokens routed top-6,
+    sorted_indices=True, through the grouped GEMM. Step = prepare(x) + gate +
+    up + SiLU(gate)*up*router weight (one pass over the routed pairs) +
+    prepare(h) + down + each token's sum over its slots."""
+
+    def __init__(self, torch, K, dev, mods, x, sel, weights):
+        self.torch, self.K = torch, K
+        self.gate, self.up, self.down = mods
+        self.E = self.gate.num_experts
+        self.T = x.shape[0]
+        self.x = x
+        self.sel = sel.reshape(-1).contiguous()
+        self.weights = weights.reshape(-1).contiguous().float()
+        self.pairs = self.sel.numel()
+        self.ws_gu = torch.empty(K.grouped_workspace_bytes(GATE_UP[1], self.E, self.pairs),
+                                 dtype=torch.uint8, device=dev)
+        self.ws_d = torch.empty(K.grouped_workspace_bytes(DOWN[1], self.E, self.pairs),
+                                dtype=torch.uint8, device=dev)
+        self.yg = torch.empty((self.pairs, GATE_UP[0]), device=dev)
+        self.yu = torch.empty((self.pairs, GATE_UP[0]), device=dev)
+        self.h = torch.empty((self.pairs, DOWN[1]), device=dev, dtype=torch.bfloat16)
+        self.yd = torch.empty((self.pairs, DOWN[0]), device=dev)
+        self.out = torch.empty((self.T, DOWN[0]), device=dev)
+        self.side = torch.cuda.Stream(dev)
+        counts = torch.bincount(self.sel.long(), minlength=self.E).cpu()
+        self.load = {"max_pairs_per_expert": int(counts.max()),
+                     "min_pairs_per_expert": int(counts.min())}
+
+    def gate_up(self):
+        K, torch = self.K, self.torch
+        K.grouped_prepare(self.x, self.E, GATE_UP[1], self.sel, None, self.ws_gu)
+        main = torch.cuda.current_stream()
+        self.side.wait_stream(main)
+        K.grouped_run(self.gate.member, self.gate._streams(), self.E, GATE_UP[0], GATE_UP[1],
+                      self.pairs, self.yg, self.ws_gu)
+        with torch.cuda.stream(self.side):
+            K.grouped_run(self.up.member, self.up._streams(), self.E, GATE_UP[0], GATE_UP[1],
+                          self.pairs, self.yu, self.ws_gu)
+        main.wait_stream(self.side)
+
+    def down_proj(self):
+        K = self.K
+        K.grouped_prepare(self.h, self.E, DOWN[1], self.sel, None, self.ws_d)
+        K.grouped_run(self.down.member, self.down._streams(), self.E, DOWN[0], DOWN[1],
+                      self.pairs, self.yd, self.ws_d)
+
+    def step(self):
+        K = self.K
+        self.gate_up()
+        K.pairs_swiglu(self.yg, self.yu, self.weights, GATE_UP[1], self.E, self.ws_gu, self.h)
+        self.down_proj()
+        K.pairs_combine(self.yd, self.sel, TOP_K, self.E, self.out)
+        return self.out
+
+
+def config5_modules(torch, dev):
+    """The config-5 layer's full expert set, the same bytes on every rank
+    (one seeded generator), so any rank can compute any token's reference."""
+    from mlx_iqk_b200 import IqkSwitchLinear
+    from mlx_iqk_b200.profile_cases import random_streams
+    g = torch.Generator(device=dev).manual_seed(5005)
+    mods = []
+    for member, (out, n) in (("iq2_ks", GATE_UP), ("iq2_ks", GATE_UP), ("iq2_k", DOWN)):
+        m = IqkSwitchLinear(member, E, out, n, device=dev)
+        m.load_streams(random_streams(member, E, out, n, dev, g))
+        mods.append(m)
+    return mods
+
+
+def measure_ep_prefill(torch, K, dev, world, rank, barrier, max_over_ranks, steps, full):
+    """Config 5 through ExpertParallelMoE: ms per layer step (max over ranks),
+    and this rank's output checked against the one-GPU computation of its
+    tokens over the full expert set (max over ranks of the relative error)."""
+    from mlx_iqk_b200.ep import ExpertParallelMoE
+    T = PREFILL_TOKENS // world
+    layer = ExpertParallelMoE(E, GATE_UP[1], GATE_UP[0], members=("iq2_ks", "iq2_ks", "iq2_k"),
+                              device=dev, max_tokens=T)
+    lo, hi = layer.first_expert, layer.first_expert + layer.local_experts
+    for mine, whole in zip((layer.gate, layer.up, layer.down), full):
+        mine.load_streams({nm: getattr(whole, nm)[lo:hi] for nm in whole.stream_names()})
+    x_all, idx_all, w_all = prefill_inputs(torch, dev)
+    x, idx, w = (t[rank * T:(rank + 1) * T].contiguous() for t in (x_all, idx_all, w_all))
+    for _ in range(3):
+        out = layer(x, idx, w)
+    layer.check()
+    torch.cuda.synchronize()
+    # the check: the same tokens through the one-GPU layer over all experts
+    ref = PrefillLayer(torch, K, dev, full, x, idx, w).step().double()
+    got = out.double()
+    err = float((got - ref).abs().max() / ref.abs().max().clamp_min(1e-30))
+    rms = ref.pow(2).mean(dim=1, keepdim=True).sqrt()
+    per = float(((got - ref).abs() / torch.maximum(ref.abs(), rms)).max())
+    run = (lambda: layer(x, idx, w))
+    graph = None
+    if layer.capturable:
+        graph = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            run()
+            torch.cuda.synchronize()
+            with torch.cuda.graph(graph, stream=s):
+                for _ in range(steps):
+                    run()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        graph.replay()
+        torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    if graph is not None:
+        graph.replay()
+    else:
+        for _ in range(steps):
+            run()
+    e1.record(stream)
+    e1.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    layer.check()
+    phases = layer.profile_phases(x, idx, w) if hasattr(layer, "profile_phases") else None
+    del graph
+    check = {"max_rel_err": max_over_ranks(err), "per_output_err": max_over_ranks(per),
+             "tokens_checked_per_rank": T, "against": "one-GPU grouped-GEMM layer over all "
+             "256 experts on the same tokens (float32 out)"}
+    return ms, check, phases, layer
+
+
+# ------------------------------------------------------------------ legs
+
+class Timer:
+    """CUDA-graph capture and device timing shared by every leg."""
+
+    def __init__(self, torch, dev, world, eager: bool):
+        self.torch, self.dev, self.world, self.eager = torch, dev, world, eager
+        import torch.distributed as dist
+        self.dist = dist
+
+    def graph(self, fn):
+        if self.eager:
+            return _Eager(fn)
+        g = self.torch.cuda.CUDAGraph()
+        with self.torch.cuda.graph(g):
+            fn()
+        return g
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
+
+    def max_over_ranks(self, v: float) -> float:
+        t = self.torch.tensor([v], device=self.dev, dtype=self.torch.float64)
+        if self.world > 1:
+            self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(self, g) -> float:
+        """ms of one replay of ``g``, CUDA events on the current stream, max over ranks."""
+        torch = self.torch
+        stream = torch.cuda.current_stream(self.dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        self.barrier()
+        e0.record(stream)
+        g.replay()
+        e1.record(stream)
+        e1.synchronize()
+        self.barrier()
+        return self.max_over_ranks(e0.elapsed_time(e1))
+
+    def cell_rate(self, cell, steps: int, warm: int = 3) -> dict:
+        gw = self.graph(lambda: [cell.step(s) for s in range(warm)])
+        gt = self.graph(lambda: [cell.step(s) for s in range(warm, warm + steps)])
+        gw.replay()
+        ms = self.timed(gt)
+        by = sum(cell.bytes(s) for s in range(warm, warm + steps))
+        return {"GB/s": round(self.world * by / (ms * 1e-3) / 1e9, 2),
+                "us_per_step": round(1e3 * ms / steps, 3), "MB_per_step": round(by / steps / 1e6, 2)}
+
+
+def hbm_peak() -> tuple[float, str, dict]:
+    try:
+        peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
+    except Exception:  # noqa: BLE001
+        peaks = {}
+    hbm = peaks.get("hbm_gbs")
+    return (hbm or 6650.0), ("measured" if hbm else "fallback"), peaks
+
+
+def committed_traffic() -> dict | None:
+    """DRAM bytes per launch of the roofline kernel from the committed ncu
+    summary (profiles/), with the command that produced them."""
+    try:
+        return json.loads(TRAFFIC_FILE.read_text())
+    except (OSError, ValueError):
+        return None
+
+
+def gemv_floor_leg(tm, K, cell, proj: str, reps_target: int) -> dict:
+    """One projection's GEMV at the cell's batch, over pre-prepared rotating
+    routings, beside its address floor (same copies, decode deleted)."""
+    torch = tm.torch
+    n_in = GATE_UP[1] if proj != "down" else DOWN[1]
+    out = GATE_UP[0] if proj != "down" else DOWN[0]
+    x_rows = cell.B if proj != "down" else cell.pairs
+    streams = cell.sg if proj == "gate" else cell.sd
+    nr = min(cell.pool, 64)
+    wss = []
+    for i in range(nr):
+        ws = torch.empty(K.gemv_workspace_bytes(cell.member, n_in, x_rows, cell.pairs),
+                         dtype=torch.uint8, device=tm.dev)
+        xin = cell.xs[i] if proj != "down" else cell.xds[i]
+        K.gemv_prepare(xin, E, n_in, cell.sels[i].reshape(-1), None, ws)
+        wss.append(ws)
+    y = torch.empty((cell.pairs, out), device=tm.dev)
+    reps = max(2, reps_target // nr)
+    res = {}
+    for arm, fn in (("kernel", K.gemv_run), ("floor", K.gemv_floor_run)):
+        g = tm.graph(lambda fn=fn: [fn(cell.member, streams, E, out, n_in, x_rows, cell.pairs, y,
+                                       wss[i]) for _ in range(reps) for i in range(nr)])
+        g.replay()
+        res[arm] = tm.timed(g) / (reps * nr)
+        del g
+    rb = row_bytes(cell.member, n_in)
+    nbytes = float(np.mean([len(set(cell.sels_np[i].ravel().tolist())) * out * rb
+                            + x_rows * n_in * 2 + cell.pairs * out * 4 for i in range(nr)]))
+    return {"us": round(res["kernel"] * 1e3, 3), "floor_us": round(res["floor"] * 1e3, 3),
+            "vs_own_floor": round(res["kernel"] / res["floor"], 3),
+            "bytes_per_launch": int(nbytes),
+            "GB/s": round(nbytes / (res["kernel"] * 1e-3) / 1e9, 1),
+            "floor_GB/s": round(nbytes / (res["floor"] * 1e-3) / 1e9, 1)}
+
+
+def dequant_leg(tm, K, mod, hbm: float, experts: int = 32, reps: int = 4) -> dict:
+    """Stacked f16 dequantization of ``experts`` experts per call (rotating
+    expert ranges, 537 MB written per call at the gate shape) beside its
+    address floor."""
+    torch = tm.torch
+    out, n = mod.out_features, mod.in_features
+    dst = torch.empty((experts, out, n), dtype=torch.float16, device=tm.dev)
+    ranges = [(i * experts) % max(mod.num_experts - experts + 1, 1) for i in range(reps)]
+    streams = [[t[e0:e0 + experts] for t in mod._streams()] for e0 in ranges]
+    res = {}
+    for arm, fn in (("kernel", K.dequant), ("floor", K.dequant_floor)):
+        g = tm.graph(lambda fn=fn: [fn(mod.member, st, experts, out, n, 0, out, dst)
+                                    for st in streams])
+        g.replay()
+        res[arm] = tm.timed(g) / reps
+        del g
+    nbytes = experts * out * (row_bytes(mod.member, n) + n * 2)
+    gbs = nbytes / (res["kernel"] * 1e-3) / 1e9
+    return {"GB/s": round(gbs, 1), "frac": round(gbs / hbm, 4),
+            "floor_GB/s": round(nbytes / (res["floor"] * 1e-3) / 1e9, 1),
+            "vs_own_floor": round(res["kernel"] / res["floor"], 3),
+            "us": round(res["kernel"] * 1e3, 2), "bytes": nbytes,
+            "shape": f"{experts} x [{out}, {n}] -> f16"}
+
+
+def config1_leg(tm, dev, gen) -> dict:
+    """BASELINE config 1's call (one IQ2_KS [2048, 4096] expert, fp32 x, one
+    token) through the module; 128 copies of the expert rotate so that no
+    call is served from L2."""
+    torch = tm.torch
+    from mlx_iqk_b200 import IqkSwitchLinear
+    from mlx_iqk_b200.profile_cases import random_streams
+    copies = 128
+    mod = IqkSwitchLinear("iq2_ks", copies, *GATE_UP, device=dev)
+    mod.load_streams(random_streams("iq2_ks", copies, *GATE_UP, dev, gen))
+    x = torch.randn((copies, 1, 1, 1, GATE_UP[1]), generator=gen, device=dev)
+    idx = torch.arange(copies, device=dev, dtype=torch.int32).reshape(copies, 1, 1)
+    g = tm.graph(lambda: [mod(x[i], idx[i]) for i in range(copies)])
+    g.replay()
+    ms = tm.timed(g) / copies
+    nbytes = GATE_UP[0] * row_bytes("iq2_ks", GATE_UP[1]) + GATE_UP[1] * 4 + GATE_UP[0] * 4
+    del g
+    return {"us_per_call": round(ms * 1e3, 3), "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1),
+            "bytes": nbytes, "path": "IqkSwitchLinear.__call__ (decode GEMV), x float32"}
+
+
 def run_b200(args) -> None:
     import torch
     import torch.distributed as dist
 
-    from mlx_iqk_b200 import IqkSwitchLinear
     from mlx_iqk_b200 import kernels as K
 
     rank = int(os.environ.get("RANK", "0"))
@@ -451,183 +782,179 @@ def run_b200(args) -> None:
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    tm = Timer(torch, dev, world, args.eager)
+    hbm, peak_src, peaks = hbm_peak()
 
     gen = torch.Generator(device=dev).manual_seed(1000 + rank)
-    gate = IqkSwitchLinear(MEMBER, E, *GATE_UP, device=dev)
-    up = IqkSwitchLinear(MEMBER, E, *GATE_UP, device=dev)
-    down = IqkSwitchLinear(MEMBER, E, *DOWN, device=dev)
-    for mod in (gate, up, down):
-        mod.load_streams(random_streams(torch, mod.out_features, mod.in_features, gen, dev))
+    mods = layer_modules(torch, MEMBER, dev, gen)
     batches = [int(b) for b in args.batches.split(",")]
-    cells = [DecodeCell(torch, K, (gate, up, down), B, dev, gen, seed=7 + 31 * rank + B)
-             for B in batches]
+    cells = [DecodeCell(torch, K, mods, B, dev, gen, seed=7 + 31 * rank + B) for B in batches]
 
     def step(s: int) -> None:  # one decode step at every batch size of the sweep
         for c in cells:
             c.step(s)
 
-    def step_bytes(s: int) -> int:
-        return sum(c.bytes(s) for c in cells)
-
     launches_per_step = sum(c.launches for c in cells)
     step(0)
     torch.cuda.synchronize()
-
-    def graph(fn):
-        if args.eager:
-            return _Eager(fn)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            fn()
-        return g
-
     W, Kst = args.warmup, args.steps
-    g_warm = graph(lambda: [step(s) for s in range(W)])
-    g_time = graph(lambda: [step(s) for s in range(W, W + Kst)])
+    g_warm = tm.graph(lambda: [step(s) for s in range(W)])
+    g_time = tm.graph(lambda: [step(s) for s in range(W, W + Kst)])
     g_warm.replay()
     torch.cuda.synchronize()
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(ms: float) -> float:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    stream = torch.cuda.current_stream(dev)
-
-    def timed(g) -> float:
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier()
-        e0.record(stream)
-        g.replay()
-        e1.record(stream)
-        e1.synchronize()
-        barrier()
-        return max_over_ranks(e0.elapsed_time(e1))
-
     with ClockSampler(local) as clk:
-        ms_max = timed(g_time)
-    bytes_timed = sum(step_bytes(s) for s in range(W, W + Kst))
+        ms_max = tm.timed(g_time)
+    bytes_timed = sum(c.bytes(s) for c in cells for s in range(W, W + Kst))
     value = world * bytes_timed / (ms_max * 1e-3) / 1e9
+    del g_warm, g_time
 
-    # ---- per batch size (same launches, one cell at a time)
-    sweep = {}
-    for c in cells:
-        ks = max(50, Kst // 2)
-        gw = graph(lambda c=c: [c.step(s) for s in range(3)])
-        gt = graph(lambda c=c, ks=ks: [c.step(s) for s in range(3, 3 + ks)])
-        gw.replay()
-        ms_c = timed(gt)
-        by = sum(c.bytes(s) for s in range(3, 3 + ks))
-        sweep[f"B={c.B}"] = {"GB/s": round(world * by / (ms_c * 1e-3) / 1e9, 2),
-                             "us_per_step": round(1e3 * ms_c / ks, 3),
-                             "MB_per_step": round(by / ks / 1e6, 2)}
-        del gw, gt
+    sweep = {f"B={c.B}": tm.cell_rate(c, max(50, Kst // 2)) for c in cells}
 
-    # ---- kernel-only roofline: the gate GEMV at the largest batch, run over
-    # pre-prepared routings (rotating experts), CUDA events on its stream
-    c = cells[-1]
-    nr = min(c.pool, 64)
-    wss = [torch.empty_like(c.ws_gu) for _ in range(nr)]
-    for i in range(nr):
-        K.gemv_prepare(c.xs[i], E, GATE_UP[1], c.sels[i].reshape(-1), None, wss[i])
-    reps = max(2, Kst // nr)
-    gk = graph(lambda: [K.gemv_run(MEMBER, c.sg, E, GATE_UP[0], GATE_UP[1], c.B, c.pairs, c.yg,
-                                   wss[i]) for r in range(reps) for i in range(nr)])
-    gk.replay()
-    kms = timed(gk) / (reps * nr)
-    gate_bytes = np.mean([len(set(c.sels_np[i].ravel().tolist())) * GATE_UP[0] * c.rb_gu
-                          + c.B * GATE_UP[1] * 2 + c.pairs * GATE_UP[0] * 4 for i in range(nr)])
-    peaks = {}
-    try:
-        peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
-    except Exception:  # noqa: BLE001
-        pass
-    hbm = peaks.get("hbm_gbs")
-    peak_src = "measured" if hbm else "fallback"
-    hbm = hbm or 6650.0
-    achieved = gate_bytes / (kms * 1e-3) / 1e9
-    roofline = {"bound": "hbm", "kernel": f"gemv_kernel<IQ2_KS> (gate 2048x4096, B={c.B})",
-                "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+    # ---- kernel-only roofline: the gate GEMV at the largest batch, beside
+    # its address floor; down at the same batch as a second floor pair
+    c8 = cells[-1]
+    gate_leg = gemv_floor_leg(tm, K, c8, "gate", max(2 * Kst, 128))
+    down_leg = gemv_floor_leg(tm, K, c8, "down", max(2 * Kst, 128))
+    traffic = committed_traffic()
+    achieved = gate_leg["GB/s"]
+    roofline = {"bound": "hbm", "kernel": f"gemv_kernel<IQ2_KS> (gate 2048x4096, B={c8.B})",
+                "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4), "peak_source": peak_src,
-                "us_per_launch": round(kms * 1e3, 3), "bytes_per_launch": int(gate_bytes),
-                "traffic": args.traffic}
+                "us_per_launch": gate_leg["us"], "bytes_per_launch": gate_leg["bytes_per_launch"],
+                "traffic": traffic["dram_bytes_per_launch"] if traffic else None,
+                "traffic_source": traffic.get("source") if traffic else None,
+                "floor_us": gate_leg["floor_us"], "vs_own_floor": gate_leg["vs_own_floor"]}
+    floors = {f"gemv gate B={c8.B}": gate_leg, f"gemv down B={c8.B}": down_leg}
 
-    # ---- prefill (config 5): the expert-parallel layer over all ranks
-    # (experts sharded E/N per rank, the 2048 tokens sharded N ways: strong
-    # scaling), then at N=1 the grouped GEMMs timed alone.
-    prefill = None
-    if not args.no_prefill:
-        ep_ms = measure_ep_prefill(torch, dist, K, dev, world, rank, barrier, max_over_ranks,
-                                   steps=max(5, args.prefill_steps // 2))
-    if not args.no_prefill and world > 1:
-        prefill = {"metric": "prefill tokens/s (config 5 layer, expert-parallel)",
-                   "value": round(PREFILL_TOKENS / (ep_ms * 1e-3), 1), "unit": "tokens/s",
-                   "ms_per_step": round(ep_ms, 4), "tokens": PREFILL_TOKENS,
-                   "scaling": "strong", "parallelism": f"ep{world}: {E // world} experts/rank, "
-                   "NCCL all_gather dispatch, all_to_all combine"}
-    if not args.no_prefill and world == 1:
-        pl = PrefillLayer(torch, K, dev, gen)
-        pl.step()
-        torch.cuda.synchronize()
-        ps = max(5, args.prefill_steps)
-        gpw = graph(lambda: [pl.step() for _ in range(3)])
-        gpt = graph(lambda: [pl.step() for _ in range(ps)])
-        gpw.replay()
-        pms = timed(gpt) / ps
-        # kernel-level: each grouped GEMM alone, repeated (same routing)
-        reps = 10
-        gk_g = graph(lambda: [K.grouped_run("iq2_ks", pl.gate._streams(), E, GATE_UP[0],
-                                            GATE_UP[1], pl.pairs, pl.yg, pl.ws_gu)
-                              for _ in range(reps)])
-        gk_d = graph(lambda: [K.grouped_run("iq2_k", pl.down._streams(), E, DOWN[0], DOWN[1],
-                                            pl.pairs, pl.yd, pl.ws_d) for _ in range(reps)])
-        pl.gate_up()
-        pl.down_proj()
-        gk_g.replay()
-        gk_d.replay()
-        g_ms = timed(gk_g) / reps
-        d_ms = timed(gk_d) / reps
-        tf_peak = peaks.get("bf16_tflops") or 1590.0
-        g_fl = 2.0 * pl.pairs * GATE_UP[0] * GATE_UP[1]
-        d_fl = 2.0 * pl.pairs * DOWN[0] * DOWN[1]
-        layer_fl = prefill_flops(pl.pairs)
-        prefill = {
-            "metric": "prefill tokens/s (config 5 layer: gate/up IQ2_KS, down IQ2_K, "
-                      "256 experts top-6, sorted_indices=True)",
-            "value": round(world * pl.T / (pms * 1e-3), 1), "unit": "tokens/s",
-            "tokens_per_gpu": pl.T, "ms_per_step": round(pms, 4),
-            "ep_layer": {"value": round(PREFILL_TOKENS / (ep_ms * 1e-3), 1), "unit": "tokens/s",
-                         "ms_per_step": round(ep_ms, 4),
-                         "path": "ExpertParallelMoE.forward (dispatch, SwitchGLU, combine)"},
-            "layer_tflops": round(layer_fl / (pms * 1e-3) / 1e12, 1),
-            "load": pl.load,
-            "gemm": {
-                "gate_or_up_us": round(g_ms * 1e3, 2),
-                "gate_or_up_tflops": round(g_fl / (g_ms * 1e-3) / 1e12, 1),
-                "down_us": round(d_ms * 1e3, 2),
-                "down_tflops": round(d_fl / (d_ms * 1e-3) / 1e12, 1),
-                "bound": "tensor", "peak_tflops": tf_peak,
-                "peak_source": "measured" if peaks.get("bf16_tflops") else "fallback",
-                "frac_gate_or_up": round(g_fl / (g_ms * 1e-3) / 1e12 / tf_peak, 4),
-                "frac_down": round(d_fl / (d_ms * 1e-3) / 1e12 / tf_peak, 4),
-            },
-            "parallelism": f"replicas x{world}",
+    configs, dequant = None, None
+    if world == 1 and not args.no_legs:
+        configs = {"config1 (IQ2_KS one expert, fp32 x)": config1_leg(tm, dev, gen)}
+        for member, bs, sorts in (("iq2_k", (1, 16, 64), (False, True)),
+                                  ("iq1_s_r4", tuple(range(1, 9)), (False,))):
+            mm = layer_modules(torch, member, dev, gen)
+            leg = {}
+            for B in bs:
+                for srt in sorts:
+                    cell = ModuleCell(torch, mm, B, dev, gen, seed=900 + B, member=member,
+                                      sorted_flat=srt)
+                    key = f"B={B}" + (" sorted" if srt else "")
+                    leg[key] = tm.cell_rate(cell, 30)
+            name = ("config3 (IQ2_K, unsorted then sorted)" if member == "iq2_k"
+                    else "config4 (IQ1_S_R4)")
+            configs[name] = leg
+            if dequant is None:
+                dequant = {}
+            dequant[member] = dequant_leg(tm, K, mm[0], hbm)
+            del mm
+        dequant[MEMBER] = dequant_leg(tm, K, mods[0], hbm)
+        torch.cuda.empty_cache()
+
+    prefill = run_prefill(args, torch, K, dev, world, rank, tm, peaks)
+    e2e = run_e2e(args, torch, dev, mods, cells, tm)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baselines(batches, args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": metric_name(batches), "value": round(value, 2), "unit": "GB/s",
+            "n_gpus": world, "steps": Kst, "warmup": W,
+            "ms_per_step": round(ms_max / Kst, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "s8 x s8 -> s32 MMA, f64 epilogue (bf16 activations)",
+            "data": "synthetic: random IQ2_KS streams (serving scales), x~N(0,1) bf16",
+            "config": config(args, batches),
+            "sweep": sweep, "roofline": roofline, "floors": floors,
+            "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": launches_per_step * Kst,
+            "clocks": clk.summary(),
+            "hbm_frac_of_step": round(value / world / hbm, 4),
+            "configs": configs, "dequant": dequant, "prefill": prefill,
         }
-        del gpw, gpt, gk_g, gk_d, pl
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
-    # ---- end to end through the public module API, host buffers. Every step
-    # copies its inputs from pinned host memory and its results back; the
-    # copies run on two side streams (double-buffered device inputs), so step
-    # i+1's inputs upload and step i's results download while step i+1
-    # computes -- the pipelining a server does. The timed region runs from
-    # the first upload to the last download.
-    ne = min(Kst, 100)
+
+def run_prefill(args, torch, K, dev, world, rank, tm, peaks) -> dict | None:
+    """Config 5: the expert-parallel layer at every N (experts E/N per rank,
+    the 2048 tokens sharded N ways: strong scaling) with its output check,
+    and at N=1 the direct one-GPU layer and each grouped GEMM alone."""
+    if args.no_prefill:
+        return None
+    full = config5_modules(torch, dev)
+    ep_ms, check, phases, layer = measure_ep_prefill(
+        torch, K, dev, world, rank, tm.barrier, tm.max_over_ranks,
+        max(5, args.prefill_steps // 2), full)
+    ep = {"value": round(PREFILL_TOKENS / (ep_ms * 1e-3), 1), "unit": "tokens/s",
+          "ms_per_step": round(ep_ms, 4), "ep_check": check, "phases": phases,
+          "path": "ExpertParallelMoE.forward (all-to-all dispatch, SwitchGLU, combine)",
+          "graph": bool(layer.capturable)}
+    del layer
+    if world > 1:
+        return {"metric": "prefill tokens/s (config 5 layer, expert-parallel)",
+                "value": ep["value"], "unit": "tokens/s", "ms_per_step": ep["ms_per_step"],
+                "tokens": PREFILL_TOKENS, "scaling": "strong", "ep_check": check,
+                "phases": phases, "parallelism": f"ep{world}: {E // world} experts/rank, "
+                "NCCL all_to_all dispatch and combine"}
+    x, idx, w = prefill_inputs(torch, dev)
+    pl = PrefillLayer(torch, K, dev, full, x, idx, w)
+    pl.step()
+    torch.cuda.synchronize()
+    ps = max(5, args.prefill_steps)
+    gpw = tm.graph(lambda: [pl.step() for _ in range(3)])
+    gpt = tm.graph(lambda: [pl.step() for _ in range(ps)])
+    gpw.replay()
+    pms = tm.timed(gpt) / ps
+    reps = 10
+    g, u, d = full
+    gk_g = tm.graph(lambda: [K.grouped_run("iq2_ks", g._streams(), E, GATE_UP[0], GATE_UP[1],
+                                           pl.pairs, pl.yg, pl.ws_gu) for _ in range(reps)])
+    gk_d = tm.graph(lambda: [K.grouped_run("iq2_k", d._streams(), E, DOWN[0], DOWN[1],
+                                           pl.pairs, pl.yd, pl.ws_d) for _ in range(reps)])
+    pl.gate_up()
+    pl.down_proj()
+    gk_g.replay()
+    gk_d.replay()
+    g_ms = tm.timed(gk_g) / reps
+    d_ms = tm.timed(gk_d) / reps
+    tf_peak = peaks.get("bf16_tflops") or 1590.0
+    g_fl = 2.0 * pl.pairs * GATE_UP[0] * GATE_UP[1]
+    d_fl = 2.0 * pl.pairs * DOWN[0] * DOWN[1]
+    out = {
+        "metric": "prefill tokens/s (config 5 layer: gate/up IQ2_KS, down IQ2_K, "
+                  "256 experts top-6, sorted_indices=True)",
+        "value": round(pl.T / (pms * 1e-3), 1), "unit": "tokens/s",
+        "tokens_per_gpu": pl.T, "ms_per_step": round(pms, 4), "ep_layer": ep,
+        "layer_tflops": round(prefill_flops(pl.pairs) / (pms * 1e-3) / 1e12, 1),
+        "load": pl.load,
+        "gemm": {"gate_or_up_us": round(g_ms * 1e3, 2),
+                 "gate_or_up_tflops": round(g_fl / (g_ms * 1e-3) / 1e12, 1),
+                 "down_us": round(d_ms * 1e3, 2),
+                 "down_tflops": round(d_fl / (d_ms * 1e-3) / 1e12, 1),
+                 "bound": "tensor", "peak_tflops": tf_peak,
+                 "peak_source": "measured" if peaks.get("bf16_tflops") else "fallback",
+                 "frac_gate_or_up": round(g_fl / (g_ms * 1e-3) / 1e12 / tf_peak, 4),
+                 "frac_down": round(d_fl / (d_ms * 1e-3) / 1e12 / tf_peak, 4)},
+        "parallelism": "one GPU",
+    }
+    del gpw, gpt, gk_g, gk_d, pl, full
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_e2e(args, torch, dev, mods, cells, tm) -> dict:
+    """The headline step through the public module API with host buffers.
+    Every step copies its inputs from pinned host memory and its results
+    back; the copies run on two side streams (double-buffered device inputs),
+    so step i+1's inputs upload and step i's results download while step i+1
+    computes -- the pipelining a server does. The timed region runs from the
+    first upload to the last download."""
+    gate, up, down = mods
+    stream = torch.cuda.current_stream(dev)
+    ne = min(args.steps, 100)
     host, dbuf = [], []
     for c in cells:
         B = c.B
@@ -686,43 +1013,15 @@ def run_b200(args) -> None:
 
     e2e_run(3)
     torch.cuda.synchronize()
-    ems = timed(_Eager(lambda: e2e_run(ne)))
+    ems = tm.timed(_Eager(lambda: e2e_run(ne)))
     e_bytes = sum(c.bytes(i) for c in cells for i in range(ne))
     h2d = sum(c.B * GATE_UP[1] * 2 + c.B * TOP_K * DOWN[1] * 2 + c.B * TOP_K * 4 for c in cells)
     d2h = sum(c.B * TOP_K * (2 * GATE_UP[0] + DOWN[0]) * 4 for c in cells)
-    e2e = {"value": round(world * e_bytes / (ems * 1e-3) / 1e9, 2), "unit": "GB/s",
-           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-           "ms_per_step": round(ems / ne, 4), "steps": ne,
-           "path": "IqkSwitchLinear.__call__ (gate, up, down) per batch size, pinned host "
-                   "in/out; copies on two side streams overlapped with the next step"}
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        res = cpu_path(batches, 10 ** 6, args.cpu_seconds, seed=4321)
-        cpu = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in res.items()
-               if k in ("value", "unit", "cores", "kind", "sample")}
-
-    if rank == 0:
-        line = {
-            "metric": metric_name(batches), "value": round(value, 2), "unit": "GB/s",
-            "n_gpus": world, "steps": Kst, "warmup": W,
-            "ms_per_step": round(ms_max / Kst, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
-            "dtype": "s8 x s8 -> s32 MMA, f64 epilogue (bf16 activations)",
-            "data": "synthetic: random IQ2_KS streams (serving scales), x~N(0,1) bf16",
-            "config": config(args, batches),
-            "sweep": sweep,
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": launches_per_step * Kst,
-            "clocks": clk.summary(),
-            "hbm_frac_of_step": round(value / world / hbm, 4),
-            "prefill": prefill,
-        }
-        print(json.dumps(line), flush=True)
-    del g_warm, g_time, gk
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    return {"value": round(tm.world * e_bytes / (ems * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": round(ems / ne, 4), "steps": ne,
+            "path": "IqkSwitchLinear.__call__ (gate, up, down) per batch size, pinned host "
+                    "in/out; copies on two side streams overlapped with the next step"}
 
 
 def main() -> None:
@@ -735,14 +1034,14 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-legs", action="store_true",
+                    help="skip the config-1/3/4 and dequantization legs")
     ap.add_argument("--experts", type=int, default=256,
                     help="experts per projection (256 = the benchmark; fewer for profiling)")
     ap.add_argument("--eager", action="store_true",
                     help="launch kernels one by one instead of replaying CUDA graphs (profiling)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (config 5) leg")
     ap.add_argument("--prefill-steps", type=int, default=20)
-    ap.add_argument("--traffic", type=float, default=GATE_B8_DRAM_BYTES,
-                    help="dram bytes per GEMV launch from an ncu capture (reported as is)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     global E

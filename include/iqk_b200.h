@@ -100,6 +100,19 @@ int iqk_dequant(int member, const void *const *streams, int64_t num_experts,
                 int64_t rows, int out_dtype, void *dst, iqk_stream_t stream);
 
 /*
+ * Address floor of iqk_dequant: the same loads and the same stores with the
+ * decode deleted (the loaded words are folded into an integer, and that is
+ * what is stored, so nothing can be dropped). Same arguments; dst receives
+ * no weights. For the benchmark's "vs own floor" ratio only.
+ *
+ * Replaces the reference's dequant floor (bench/floors.py:186-220,
+ * dequant_floor_source), which prices its dequantization the same way.
+ */
+int iqk_dequant_floor(int member, const void *const *streams, int64_t num_experts,
+                      int64_t out_features, int64_t in_features, int64_t row_start,
+                      int64_t rows, int out_dtype, void *dst, iqk_stream_t stream);
+
+/*
  * Workspace bytes iqk_gemv needs for this member, width, activation-row
  * count and pair count (routing tables plus the prepared activations).
  */
@@ -157,6 +170,21 @@ int iqk_gemv_run(int member, const void *const *streams, int64_t num_experts,
                  int64_t out_features, int64_t in_features, int64_t x_rows, int64_t pairs,
                  void *y, int y_dtype, const void *workspace, size_t workspace_bytes,
                  iqk_stream_t stream);
+
+/*
+ * Address floor of iqk_gemv_run: the same launch, the same copies from HBM
+ * into shared memory and the same shared-memory reads of code words and
+ * activation planes, with the decode deleted (the words are folded into an
+ * integer that reaches y). Same arguments; y receives no projection. For the
+ * benchmark's "vs own floor" ratio only.
+ *
+ * Replaces the reference's GEMV floor (bench/floors.py:60-183,
+ * gemv_floor_source).
+ */
+int iqk_gemv_floor_run(int member, const void *const *streams, int64_t num_experts,
+                       int64_t out_features, int64_t in_features, int64_t x_rows,
+                       int64_t pairs, void *y, int y_dtype, const void *workspace,
+                       size_t workspace_bytes, iqk_stream_t stream);
 
 /*
  * Copy the device error bits of the last preparation in `workspace` (same

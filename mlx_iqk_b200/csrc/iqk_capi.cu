@@ -99,6 +99,25 @@ int iqk_dequant(int member, const void *const *streams, int64_t num_experts,
                                       num_sms_current()));
 }
 
+int iqk_dequant_floor(int member, const void *const *streams, int64_t num_experts,
+                      int64_t out_features, int64_t in_features, int64_t row_start,
+                      int64_t rows, int out_dtype, void *dst, iqk_stream_t stream) {
+    if (!member_ok(member)) return IQK_ERR_MEMBER;
+    if (!width_ok(in_features)) return IQK_ERR_WIDTH;
+    if (num_experts <= 0 || out_features <= 0) return IQK_ERR_GEOMETRY;
+    if (member == IQK_IQ1_S_R4 && out_features % 4) return IQK_ERR_GEOMETRY;
+    if (row_start < 0 || rows < 0 || row_start + rows > out_features) return IQK_ERR_GEOMETRY;
+    if (!dtype_ok(out_dtype) || !dst) return IQK_ERR_ARGUMENT;
+    if (!aligned(dst, 16)) return IQK_ERR_ALIGNMENT;
+    const int st = check_streams(member, streams);
+    if (st != IQK_OK) return st;
+    if (rows == 0) return IQK_OK;
+    return cuda_status(launch_dequant(member, streams, num_experts, out_features,
+                                      (int)in_features, row_start, rows, out_dtype, dst,
+                                      reinterpret_cast<cudaStream_t>(stream),
+                                      num_sms_current(), true));
+}
+
 size_t iqk_gemv_workspace_bytes(int member, int64_t in_features, int64_t x_rows,
                                 int64_t pairs) {
     if (!member_ok(member) || !width_ok(in_features) || x_rows < 0 || pairs < 0) return 0;
@@ -163,6 +182,31 @@ int iqk_gemv_run(int member, const void *const *streams, int64_t num_experts,
                                        pairs, y, y_dtype, workspace,
                                        reinterpret_cast<cudaStream_t>(stream),
                                        num_sms_current()));
+}
+
+int iqk_gemv_floor_run(int member, const void *const *streams, int64_t num_experts,
+                       int64_t out_features, int64_t in_features, int64_t x_rows, int64_t pairs,
+                       void *y, int y_dtype, const void *workspace, size_t workspace_bytes,
+                       iqk_stream_t stream) {
+    if (!member_ok(member)) return IQK_ERR_MEMBER;
+    if (!width_ok(in_features)) return IQK_ERR_WIDTH;
+    if (num_experts <= 0 || num_experts > 4096) return IQK_ERR_GEOMETRY;
+    if (out_features <= 0 || out_features % 16) return IQK_ERR_GEOMETRY;
+    if (!gemv_rows_ok(num_experts, out_features, pairs)) return IQK_ERR_GEOMETRY;
+    if (pairs < 0 || x_rows < 0 || pairs > (1 << 24) || x_rows > (1 << 24))
+        return IQK_ERR_GEOMETRY;
+    if (!dtype_ok(y_dtype)) return IQK_ERR_ARGUMENT;
+    if (pairs == 0) return IQK_OK;
+    if (!y || !workspace) return IQK_ERR_ARGUMENT;
+    if (!aligned(y, 4) || !aligned(workspace, 256)) return IQK_ERR_ALIGNMENT;
+    const int st = check_streams(member, streams);
+    if (st != IQK_OK) return st;
+    if (workspace_bytes < gemv_layout(member, in_features, x_rows, pairs).total)
+        return IQK_ERR_WORKSPACE;
+    return cuda_status(launch_gemv_run(member, streams, num_experts, out_features,
+                                       (int)in_features, x_rows, pairs, y, y_dtype, workspace,
+                                       reinterpret_cast<cudaStream_t>(stream),
+                                       num_sms_current(), true));
 }
 
 int iqk_gemv(int member, const void *x, int x_dtype, int64_t x_rows,

@@ -130,7 +130,18 @@ __device__ __forceinline__ void group_table(float dl, int alpha, float t[4]) {
     for (int c = 0; c < 4; ++c) t[c] = dl * (float)(int)(int8_t)(tab >> (8 * c));
 }
 
-template <int MEMBER, typename OUT>
+// FLOOR (both kernels): the address floor the reference prices its
+// dequantization against (bench/floors.py:1-17, dequant_floor_source): the
+// same loads and the same warp-staged stores, with the decode deleted -- the
+// loaded words are folded into an integer that is what gets stored. Only the
+// benchmark's floor entry point uses it.
+template <bool FLOOR, int CH>
+__device__ __forceinline__ void fold_store(uint32_t f, uint4 (&v)[CH]) {
+#pragma unroll
+    for (int c = 0; c < CH; ++c) v[c] = make_uint4(f, f + 1u, f + 2u, f + 3u);
+}
+
+template <int MEMBER, typename OUT, bool FLOOR = false>
 __global__ void __launch_bounds__(256)
 dequant_words_kernel(StreamPtrs sp, uint32_t total_words, int log2_words, int n,
                      int64_t out_features, int64_t row_start, uint32_t rows,
@@ -158,8 +169,13 @@ dequant_words_kernel(StreamPtrs sp, uint32_t total_words, int log2_words, int n,
             const int lo = (__ldg(scl + srow * (n / 64) + (g >> 1)) >> (4 * (g & 1))) & 15;
             const int hi = (__ldg(sch + srow * (n / 256) + (g >> 3)) >> (g & 7)) & 1;
             const int alpha = (__ldg(sex + srow * (n / 256) + (g >> 3)) >> (g & 7)) & 1;
-            group_table(half_bits_to_float(__ldg(dv + srow)) * (float)((lo | (hi << 4)) - 16),
-                        alpha, t);
+            if (FLOOR) {
+                t[0] = __uint_as_float(word + 3u * lo + 5u * hi + 7u * alpha +
+                                       11u * __ldg(dv + srow));
+            } else {
+                group_table(half_bits_to_float(__ldg(dv + srow)) *
+                                (float)((lo | (hi << 4)) - 16), alpha, t);
+            }
         } else {
             const uint8_t *scl = static_cast<const uint8_t *>(sp.p[1]);
             const uint8_t *sex = static_cast<const uint8_t *>(sp.p[2]);
@@ -167,11 +183,17 @@ dequant_words_kernel(StreamPtrs sp, uint32_t total_words, int log2_words, int n,
             const int sb = wi;
             const int lo = (__ldg(scl + srow * (n / 32) + (sb >> 1)) >> (4 * (sb & 1))) & 15;
             const int alpha = (__ldg(sex + srow * (n / 128) + (sb >> 3)) >> (sb & 7)) & 1;
-            group_table(half_bits_to_float(__ldg(dv + srow * (n / 256) + (sb >> 4))) *
-                            (float)(lo - 8), alpha, t);
+            if (FLOOR) {
+                t[0] = __uint_as_float(word + 3u * lo + 7u * alpha +
+                                       11u * __ldg(dv + srow * (n / 256) + (sb >> 4)));
+            } else {
+                group_table(half_bits_to_float(__ldg(dv + srow * (n / 256) + (sb >> 4))) *
+                                (float)(lo - 8), alpha, t);
+            }
         }
         uint4 v[CH];
-        expand_word<OUT>(word, t, v);
+        if (FLOOR) fold_store<FLOOR, CH>(__float_as_uint(t[0]), v);
+        else expand_word<OUT>(word, t, v);
         warp_store<CH>(reinterpret_cast<uint4 *>(dst + (int64_t)lin * n + (wi - lane) * 16), v,
                        my_stage, lane);
     }
@@ -180,7 +202,7 @@ dequant_words_kernel(StreamPtrs sp, uint32_t total_words, int log2_words, int n,
 // IQ1_S_R4: one half block (16 weights, two octets: two grid bytes of the qs
 // word and their qh bits) per thread, so a thread writes 32 contiguous bytes
 // at 16-bit outputs -- the store pattern of the 2-bit word kernel.
-template <typename OUT>
+template <typename OUT, bool FLOOR = false>
 __global__ void __launch_bounds__(256)
 dequant_iq1_kernel(StreamPtrs sp, uint32_t total_halves, int log2_halves, int n,
                    int64_t out_features, int64_t row_start, uint32_t rows,
@@ -214,11 +236,22 @@ dequant_iq1_kernel(StreamPtrs sp, uint32_t total_halves, int log2_halves, int n,
         const float shift = (h & 0x8000u) ? -0.125f : 0.125f;
         const float t[4] = {dl * (-1.0f + shift), dl * (0.0f + shift), dl * (1.0f + shift), 0.0f};
         uint4 v[CH];
+        if (FLOOR) {
+            // the grid gathers are addressing, not decode: kept
+            uint32_t f = qw + 3u * h + 5u * __ldg(dv + srow);
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-            const int i = 2 * (hb & 1) + q;  // octet of the block
-            const uint32_t code = grid[((qw >> (8 * i)) & 0xffu) | (((h >> (3 * i)) & 7u) << 8)];
-            expand_octet<OUT>(code, t, v + q * (CH / 2));
+            for (int q = 0; q < 2; ++q) {
+                const int i = 2 * (hb & 1) + q;
+                f += (7u + 4u * q) * grid[((qw >> (8 * i)) & 0xffu) | (((h >> (3 * i)) & 7u) << 8)];
+            }
+            fold_store<FLOOR, CH>(f, v);
+        } else {
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int i = 2 * (hb & 1) + q;  // octet of the block
+                const uint32_t code = grid[((qw >> (8 * i)) & 0xffu) | (((h >> (3 * i)) & 7u) << 8)];
+                expand_octet<OUT>(code, t, v + q * (CH / 2));
+            }
         }
         warp_store<CH>(reinterpret_cast<uint4 *>(dst + (int64_t)lin * n + (hb - lane) * 16), v,
                        my_stage, lane);
@@ -228,7 +261,7 @@ dequant_iq1_kernel(StreamPtrs sp, uint32_t total_halves, int log2_halves, int n,
 cudaError_t launch_dequant(int member, const void *const *streams, int64_t num_experts,
                            int64_t out_features, int n, int64_t row_start,
                            int64_t rows, int out_dtype, void *dst, cudaStream_t stream,
-                           int num_sms) {
+                           int num_sms, bool floor) {
     StreamPtrs sp{};
     const RowBytes rb = row_bytes(member, n);
     for (int i = 0; i < rb.count; ++i) sp.p[i] = streams[i];
@@ -249,15 +282,20 @@ cudaError_t launch_dequant(int member, const void *const *streams, int64_t num_e
         int64_t blocks = ((int64_t)total + threads - 1) / threads;
         const int64_t cap = (int64_t)num_sms * 8;  // resident blocks; grid-stride beyond
         if (blocks > cap) blocks = cap;
-#define IQK_DQ(M, T)                                                                  \
+#define IQK_DQF(M, T, F)                                                              \
         if (M != IQK_IQ1_S_R4)                                                        \
-            dequant_words_kernel<M, T><<<(unsigned)blocks, threads, 0, stream>>>(      \
+            dequant_words_kernel<M, T, F><<<(unsigned)blocks, threads, 0, stream>>>(   \
                 spc, total, log2_octs - 1, n, out_features, row_start, (uint32_t)rows, \
                 static_cast<T *>(dstc));                                              \
         else                                                                          \
-            dequant_iq1_kernel<T><<<(unsigned)blocks, threads, 0, stream>>>(           \
+            dequant_iq1_kernel<T, F><<<(unsigned)blocks, threads, 0, stream>>>(        \
                 spc, total, log2_octs - 1, n, out_features, row_start, (uint32_t)rows, \
                 static_cast<T *>(dstc))
+#define IQK_DQ(M, T)                                                   \
+        do {                                                           \
+            if (floor) { IQK_DQF(M, T, true); }                        \
+            else { IQK_DQF(M, T, false); }                             \
+        } while (0)
 #define IQK_DQ_MEMBER(M)                                             \
     do {                                                             \
         if (out_dtype == IQK_F32) IQK_DQ(M, float);                  \
@@ -269,6 +307,7 @@ cudaError_t launch_dequant(int member, const void *const *streams, int64_t num_e
         else IQK_DQ_MEMBER(IQK_IQ1_S_R4);
 #undef IQK_DQ_MEMBER
 #undef IQK_DQ
+#undef IQK_DQF
         cudaError_t err = cudaGetLastError();
         if (err != cudaSuccess) return err;
     }

@@ -493,7 +493,13 @@ __device__ __forceinline__ double pow2(int k) {
     return __longlong_as_double((long long)(k + 1023) << 52);
 }
 
-template <int MEMBER, int N, bool NARROW>
+// FLOOR: the address floor of this kernel (the reference's deleted-decode
+// floor, bench/floors.py:1-17): the same launch, producer and copies, so
+// the same bytes cross from HBM into shared memory, and the compute warps read
+// the same code words and activation planes, but fold them into an integer
+// accumulator instead of decoding; the folded value reaches y, so no copy
+// or read can be dropped. Only the benchmark's floor entry point uses it.
+template <int MEMBER, int N, bool NARROW, bool FLOOR = false>
 __global__ void __launch_bounds__(kThreads, Geo<MEMBER>::kMinBlocks)
 gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
     extern __shared__ char smem_raw[];
@@ -802,9 +808,10 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
             break;
         }
         if (*(volatile int *)abort_flag) break;
-        if (live && !prebuilt) build_meta(sd, chunk_of(0), meta_u);
+        if (!FLOOR && live && !prebuilt) build_meta(sd, chunk_of(0), meta_u);
         prebuilt = false;
         __syncwarp();
+        uint32_t facc = 0u;  // FLOOR: every word this warp would decode, folded
         int32_t tot[4] = {0, 0, 0, 0};
         int32_t tb[2] = {0, 0};        // IQ2_K: plane 2 (product b), rows g, g+8
         double dacc[2] = {0.0, 0.0};  // IQ2_K: rows g, g+8, this lane's sub-blocks
@@ -818,7 +825,33 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                 break;
             }
             const char *st = stages + slot * STB;
-            if (live) {
+            if (FLOOR && live) {
+                // the round's code words and activation planes (the loads of
+                // the MMA-pair loop) plus the scale-slot words its metadata
+                // reads, folded with distinct odd multipliers
+                const uint32_t wb_u = smem_u32(st + wid * G::kWBox);
+                const uint32_t xs_u = smem_u32(st + G::kWBytes + (NARROW ? wid * G::kXPlanes : 0));
+                const uint32_t wl = wb_u | woff;
+#pragma unroll
+                for (int pr = 0; pr < kPairsPerRound; ++pr) {
+                    uint32_t w0, w1;
+                    if (MEMBER == IQK_IQ1_S_R4) {
+                        const uint32_t wo = (wl ^ (uint32_t)((pr >> 1) << 4)) + (uint32_t)((pr & 1) << 3);
+                        w0 = ld_s32(wo);
+                        w1 = ld_s32(wo + 512);
+                        // the grid gathers are addressing, not decode: kept
+                        w0 += 131u * grid[w0 & 0x7ffu] + 137u * grid[(w1 >> 8) & 0x7ffu];
+                    } else {
+                        const uint32_t wo = wl ^ (uint32_t)(pr << 4);
+                        w0 = ld_s32(wo);
+                        w1 = ld_s32(wo + 1024);
+                    }
+                    const uint4 bv = ld_s128(xs_u + tig * 48 + pr * 192);
+                    facc += w0 + 3u * w1 + 5u * bv.x + 7u * bv.y + 11u * bv.z + 13u * bv.w;
+                }
+                const uint32_t* sw = reinterpret_cast<const uint32_t *>(sd);
+                facc += 17u * sw[(lane + 32 * (chunk_of(r) & 7)) % (SS::kSlot / 4)];
+            } else if (live) {
                 // ---- 8 MMA pairs, all shared-memory addresses 32-bit and the
                 // per-pair offsets compile-time immediates.
                 const uint32_t wb_u = smem_u32(st + wid * G::kWBox);
@@ -943,7 +976,8 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                 // the loop's latency gaps. After a wide item's last round: the
                 // next item's first round, from its scale slot, into buffer 0
                 // (RPI is even, so this round reads buffer 1).
-                if (r + 1 < RPI) {
+                if (FLOOR) {
+                } else if (r + 1 < RPI) {
                     build_meta(sd, chunk_of(r + 1), meta_u + ((r + 1) & 1) * G::kMetaBytes);
                 } else if (nlive && mbar_wait(&sfull[(o + 1) & 1], ((o + 1) >> 1) & 1)) {
                     build_meta(sslots + ((o + 1) & 1) * SSB, chunk_of(0), meta_u);
@@ -961,6 +995,12 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
             break;
         }
 
+        if (FLOOR) {
+            // the folds travel like the partial sums: through the narrow
+            // shape's exchange area to warp 0
+            tot[0] = (int32_t)facc;
+            dacc[0] = (double)facc;
+        }
         if (NARROW) {
             // ---- combine the four k quarters in warp 0: warps 1-3 hand over
             // their partials (exact integers; IQ2_K doubles, added in warp
@@ -1014,7 +1054,13 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
             // ---- item end: this warp holds the whole k range of its 16 rows.
             const int ra = rbase + g;  // item-local row
             double yg, yg8;
-            if (MEMBER == IQK_IQ2_K) {
+            if (FLOOR) {
+                uint32_t f = MEMBER == IQK_IQ2_K ? (uint32_t)(long long)dacc[0] : (uint32_t)tot[0];
+#pragma unroll
+                for (int o2 = 1; o2 < 32; o2 <<= 1) f += __shfl_xor_sync(0xffffffffu, f, o2);
+                yg = (double)(f & 0xffu);
+                yg8 = (double)((f >> 8) & 0xffu);
+            } else if (MEMBER == IQK_IQ2_K) {
                 // the quad's four sub-block sides, in a fixed order
                 yg = dacc[0] + __shfl_xor_sync(0xffffffffu, dacc[0], 1);
                 yg8 = dacc[1] + __shfl_xor_sync(0xffffffffu, dacc[1], 1);
@@ -1095,15 +1141,19 @@ GemvLayout gemv_layout(int member, int64_t n, int64_t x_rows, int64_t pairs) {
 using GemvFn = void (*)(GemvArgs, CUtensorMap);
 
 // The narrow shape exists at in_features 4096 only.
-static GemvFn gemv_fn(int member, int n, bool narrow) {
-#define IQK_FN(M, NN) (narrow ? (GemvFn)gemv_kernel<M, NN, true> : (GemvFn)gemv_kernel<M, NN, false>)
+template <bool FLOOR> static GemvFn gemv_fn_t(int member, int n, bool narrow) {
+#define IQK_FN(M, NN) (narrow ? (GemvFn)gemv_kernel<M, NN, true, FLOOR> \
+                              : (GemvFn)gemv_kernel<M, NN, false, FLOOR>)
     if (n == 2048)
-        return member == IQK_IQ2_KS ? (GemvFn)gemv_kernel<IQK_IQ2_KS, 2048, false>
-               : member == IQK_IQ2_K ? (GemvFn)gemv_kernel<IQK_IQ2_K, 2048, false>
-                                     : (GemvFn)gemv_kernel<IQK_IQ1_S_R4, 2048, false>;
+        return member == IQK_IQ2_KS ? (GemvFn)gemv_kernel<IQK_IQ2_KS, 2048, false, FLOOR>
+               : member == IQK_IQ2_K ? (GemvFn)gemv_kernel<IQK_IQ2_K, 2048, false, FLOOR>
+                                     : (GemvFn)gemv_kernel<IQK_IQ1_S_R4, 2048, false, FLOOR>;
     return member == IQK_IQ2_KS ? IQK_FN(IQK_IQ2_KS, 4096)
            : member == IQK_IQ2_K ? IQK_FN(IQK_IQ2_K, 4096) : IQK_FN(IQK_IQ1_S_R4, 4096);
 #undef IQK_FN
+}
+static GemvFn gemv_fn(int member, int n, bool narrow, bool floor) {
+    return floor ? gemv_fn_t<true>(member, n, narrow) : gemv_fn_t<false>(member, n, narrow);
 }
 
 int gemv_smem_for(int member, int n, bool narrow) {
@@ -1194,7 +1244,8 @@ static cudaError_t encode_qs_map(CUtensorMap *map, const void *qs, int64_t rows,
 
 cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_experts,
                             int64_t out_features, int n, int64_t x_rows, int64_t pairs, void *y,
-                            int y_dtype, const void *ws, cudaStream_t stream, int num_sms) {
+                            int y_dtype, const void *ws, cudaStream_t stream, int num_sms,
+                            bool floor) {
     const GemvLayout L = gemv_layout(member, n, x_rows, pairs);
     GemvArgs ga{};
     const RowBytes rb = row_bytes(member, n);
@@ -1215,21 +1266,27 @@ cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_
     // One persistent wave: as many CTAs as fit on every SM at once (shared
     // memory and registers decide; cached per member, width and shape). The
     // shared-memory opt-in is a per-device function attribute: set once.
-    static std::atomic<int> resident[3][2][2];
-    static std::atomic<unsigned> attr_done[64];
+    static std::atomic<int> resident[1][3][2][2];
+    static std::atomic<unsigned> attr_done[2][64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = -1;
+    // The floor variant runs with the decode kernel's grid (its own occupancy
+    // could differ), so the two launches issue the same copies from the same
+    // number of CTAs.
     auto setup = [&](bool narrow, int &per_sm) -> cudaError_t {
-        const GemvFn fn = gemv_fn(member, n, narrow);
         const int smem = gemv_smem_for(member, n, narrow);
         const unsigned bit = 1u << ((member * 2 + (n == 4096)) * 2 + (narrow ? 1 : 0));
-        if (dev < 0 || !(attr_done[dev].load() & bit)) {
-            const cudaError_t e =
-                cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            if (e != cudaSuccess) return e;
-            if (dev >= 0) attr_done[dev].fetch_or(bit);
+        for (int f = 0; f <= (floor ? 1 : 0); ++f) {
+            if (dev < 0 || !(attr_done[f][dev].load() & bit)) {
+                const cudaError_t e = cudaFuncSetAttribute(
+                    gemv_fn(member, n, narrow, f != 0), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                    smem);
+                if (e != cudaSuccess) return e;
+                if (dev >= 0) attr_done[f][dev].fetch_or(bit);
+            }
         }
-        std::atomic<int> &r = resident[member][n == 4096][narrow ? 1 : 0];
+        const GemvFn fn = gemv_fn(member, n, narrow, false);
+        std::atomic<int> &r = resident[0][member][n == 4096][narrow ? 1 : 0];
         if (r.load() == 0) {
             int nb = 0;
             const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, kThreads, smem);
@@ -1258,7 +1315,7 @@ cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_
     int64_t blocks = max_items < cap ? max_items : cap;
     if (blocks < 1) blocks = 1;
     PdlLaunch pl((unsigned)blocks, kThreads, gemv_smem_for(member, n, narrow), stream);
-    err = cudaLaunchKernelEx(&pl.cfg, gemv_fn(member, n, narrow), ga, map);
+    err = cudaLaunchKernelEx(&pl.cfg, gemv_fn(member, n, narrow, floor), ga, map);
     if (err != cudaSuccess) return err;
     return cudaGetLastError();
 }

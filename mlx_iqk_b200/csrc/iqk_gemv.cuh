@@ -36,10 +36,11 @@ cudaError_t launch_gemv_prepare(const void *x, int x_dtype, int64_t x_rows, int 
                                 int64_t pairs, void *ws, cudaStream_t stream);
 cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_experts,
                             int64_t out_features, int n, int64_t x_rows, int64_t pairs, void *y,
-                            int y_dtype, const void *ws, cudaStream_t stream, int num_sms);
+                            int y_dtype, const void *ws, cudaStream_t stream, int num_sms,
+                            bool floor = false);
 cudaError_t launch_dequant(int member, const void *const *streams, int64_t num_experts,
                            int64_t out_features, int n, int64_t row_start,
                            int64_t rows, int out_dtype, void *dst, cudaStream_t stream,
-                           int num_sms);
+                           int num_sms, bool floor = false);
 
 }  // namespace iqk

@@ -105,6 +105,10 @@ def library() -> ctypes.CDLL:
     lib.iqk_gemv_prepare.restype = i32
     lib.iqk_gemv_run.argtypes = [i32, vp, i64, i64, i64, i64, i64, vp, i32, vp, sz, vp]
     lib.iqk_gemv_run.restype = i32
+    lib.iqk_gemv_floor_run.argtypes = [i32, vp, i64, i64, i64, i64, i64, vp, i32, vp, sz, vp]
+    lib.iqk_gemv_floor_run.restype = i32
+    lib.iqk_dequant_floor.argtypes = [i32, vp, i64, i64, i64, i64, i64, i32, vp, vp]
+    lib.iqk_dequant_floor.restype = i32
     lib.iqk_read_error.argtypes = [vp, i64, i64, i64, ctypes.POINTER(ctypes.c_int32), vp]
     lib.iqk_read_error.restype = i32
     lib.iqk_grouped_workspace_bytes.argtypes = [i64, i64, i64]
@@ -142,7 +146,8 @@ def exported_symbols() -> list[str]:
             "iqk_grouped_prepare", "iqk_grouped_run", "iqk_grouped_read_error",
             "iqk_gemv_static_max_bytes", "iqk_gemv_static", "iqk_gemv_static_read_error",
             "iqk_grouped_prepare_shard",
-            "iqk_pairs_swiglu", "iqk_pairs_combine"]
+            "iqk_pairs_swiglu", "iqk_pairs_combine", "iqk_gemv_floor_run",
+            "iqk_dequant_floor"]
 
 
 def raise_for_status(status: int, what: str) -> None:
@@ -249,6 +254,29 @@ def gemv_run(member: str, streams, num_experts: int, out_features: int, in_featu
         stream_handle(y.device))
     raise_for_status(status, "iqk_gemv_run")
     return y
+
+
+def gemv_floor_run(member: str, streams, num_experts: int, out_features: int,
+                   in_features: int, x_rows: int, pairs: int, y: torch.Tensor,
+                   workspace: torch.Tensor) -> torch.Tensor:
+    """``iqk_gemv_floor_run``: the GEMV's address floor (benchmark only)."""
+    status = library().iqk_gemv_floor_run(
+        MEMBER_IDS[member], ptr_array(streams), num_experts, out_features, in_features, x_rows,
+        pairs, y.data_ptr(), DTYPE_IDS[y.dtype], workspace.data_ptr(), workspace.numel(),
+        stream_handle(y.device))
+    raise_for_status(status, "iqk_gemv_floor_run")
+    return y
+
+
+def dequant_floor(member: str, streams, num_experts: int, out_features: int, in_features: int,
+                  row_start: int, rows: int, out: torch.Tensor) -> torch.Tensor:
+    """``iqk_dequant_floor``: the dequantization's address floor (benchmark only)."""
+    status = library().iqk_dequant_floor(MEMBER_IDS[check_member(member)], ptr_array(streams),
+                                         num_experts, out_features, in_features, row_start,
+                                         rows, DTYPE_IDS[out.dtype], out.data_ptr(),
+                                         stream_handle(out.device))
+    raise_for_status(status, "iqk_dequant_floor")
+    return out
 
 
 def gemv_static(member: str, x: torch.Tensor, streams, num_experts: int, out_features: int,

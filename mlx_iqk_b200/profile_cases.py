@@ -34,8 +34,15 @@ ROW_BYTES = {"iq2_ks": lambda n: 2 + 70 * (n // 256), "iq2_k": lambda n: 76 * (n
              "iq1_s_r4": lambda n: 2 + 6 * (n // 32)}
 
 
-def random_module(member: str, experts: int, out: int, n: int, dev, gen) -> IqkSwitchLinear:
-    mod = IqkSwitchLinear(member, experts, out, n, device=dev)
+_STREAM_DTYPES = {"uint8": torch.uint8, "uint16": torch.uint16, "uint32": torch.uint32,
+                  "float16": torch.float16}
+
+
+def random_streams(member: str, experts: int, out: int, n: int, dev, gen) -> dict:
+    """Uniform random relayout streams on the device (every code, scale and
+    grid byte uniform), f16 scales at the magnitudes the codec produces."""
+    from .format import component_dtypes
+    dtypes = component_dtypes(member)
     streams = {}
     for name, shape in component_shapes(member, experts, out, n).items():
         if name == "dv":
@@ -43,14 +50,19 @@ def random_module(member: str, experts: int, out: int, n: int, dev, gen) -> IqkS
             sign = torch.where(torch.rand(shape, generator=gen, device=dev) < 0.5, -1.0, 1.0)
             streams[name] = (mag * sign).to(torch.float16)
             continue
-        dt = getattr(mod, name).dtype
+        dt = _STREAM_DTYPES[dtypes[name].name]
         count = 1
         for s in shape:
             count *= s
         raw = torch.randint(0, 256, (count * dt.itemsize,), generator=gen, device=dev,
                             dtype=torch.uint8)
         streams[name] = raw.view(dt).reshape(shape)
-    mod.load_streams(streams)
+    return streams
+
+
+def random_module(member: str, experts: int, out: int, n: int, dev, gen) -> IqkSwitchLinear:
+    mod = IqkSwitchLinear(member, experts, out, n, device=dev)
+    mod.load_streams(random_streams(member, experts, out, n, dev, gen))
     return mod
 
 

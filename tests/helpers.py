@@ -52,3 +52,33 @@ def ref_projection(ref, x, indices, paired: bool) -> np.ndarray:
 
 def to_np(t: torch.Tensor) -> np.ndarray:
     return t.detach().float().cpu().numpy() if t.dtype == torch.bfloat16 else t.detach().cpu().numpy()
+
+
+PREFILL_TOL = 2e-2
+"""Prefill (tensor-core grouped GEMM) bound: bf16-GEMM tolerance per output."""
+
+
+def per_output_err(got, want) -> float:
+    """max over outputs of |got - want| / max(|want|, rms(want's row)).
+
+    The per-output form of the prefill bound: each element against its own
+    magnitude, floored by its row's rms so that outputs near zero are judged
+    on the row's scale rather than on a vanishing denominator. Rows are the
+    last axis (one pair's output features)."""
+    got = np.asarray(got, dtype=np.float64)
+    want = np.asarray(want, dtype=np.float64)
+    want2 = want.reshape(-1, want.shape[-1])
+    rms = np.sqrt(np.mean(want2 * want2, axis=1, keepdims=True))
+    den = np.maximum(np.abs(want2), np.maximum(rms, 1e-300))
+    return float(np.max(np.abs(got.reshape(want2.shape) - want2) / den))
+
+
+def assert_prefill_close(got, want, what="") -> tuple[float, float]:
+    """Both prefill figures: the normwise max relative error and the
+    per-output one, each within the 2e-2 bound."""
+    norm = rel_err(got, want)
+    per = per_output_err(got, want)
+    print(f"prefill {what}: normwise {norm:.3e}, per-output {per:.3e}")
+    assert norm < PREFILL_TOL, (what, norm)
+    assert per < PREFILL_TOL, (what, per)
+    return norm, per

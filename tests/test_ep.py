@@ -78,8 +78,8 @@ def _worker(rank, world, port, errq):
         err = float((got - want).abs().max() / want.abs().max())
         if err > 2e-2:
             raise AssertionError(f"rank {rank}: rel err {err}")
-        # every rank saw every rank's rows, padded to the largest count
-        if layer.last_stats["rows_gathered"] != world * 10:
+        # every rank exchanged one chunk of the largest count with every rank
+        if layer.last_stats["rows_exchanged"] != world * 10:
             raise AssertionError(f"rank {rank}: {layer.last_stats}")
         # a second call reuses the group, with different token counts per rank
         # (one rank of four has none)
@@ -129,7 +129,7 @@ def test_single_rank_path_without_collectives():
     got = layer(x, idx, w).double()
     want = reference_layer(x, idx, w, experts)
     assert float((got - want).abs().max() / want.abs().max()) < 2e-2
-    assert layer.last_stats["rows_gathered"] == 12
+    assert layer.last_stats["rows_exchanged"] == 12
 
 
 def test_bad_expert_index_is_refused_before_any_exchange():
