@@ -235,6 +235,22 @@ int iqk_grouped_run(int member, const void *const *streams, int64_t num_experts,
 int iqk_grouped_read_error(const void *workspace, int32_t *flags, iqk_stream_t stream);
 
 /*
+ * iqk_grouped_run restricted to output rows [row_start, row_start + rows) of
+ * every expert: y is [pairs, rows]. Only those rows' weights are read and
+ * multiplied, and each output element is the same dot product as in the
+ * whole call, so range outputs concatenated along the feature axis equal
+ * iqk_grouped_run's bit for bit.
+ *
+ * Replaces the reference's bounded-liveness range route,
+ * IqkSwitchLinear.sorted_matmul_range (src/mlx_iqk/nn.py:203-217:
+ * dequantized_range + gather_mm over one out-row slice).
+ */
+int iqk_grouped_run_range(int member, const void *const *streams, int64_t num_experts,
+                          int64_t out_features, int64_t in_features, int64_t pairs,
+                          int64_t row_start, int64_t rows, void *y, int y_dtype,
+                          const void *workspace, size_t workspace_bytes, iqk_stream_t stream);
+
+/*
  * Expert-parallel helpers (no reference counterpart: the reference serves a
  * whole layer on one device; these shard its SwitchGLU seam,
  * src/mlx_iqk/nn.py:1-22, over ranks that each hold num_experts local

@@ -307,7 +307,7 @@ int iqk_grouped_run(int member, const void *const *streams, int64_t num_experts,
                     int y_dtype, const void *workspace, size_t workspace_bytes,
                     iqk_stream_t stream) {
     if (!member_ok(member)) return IQK_ERR_MEMBER;
-    if (member == IQK_IQ1_S_R4) return IQK_ERR_GEOMETRY;
+    if (member == IQK_IQ1_S_R4 && out_features % 4) return IQK_ERR_GEOMETRY;
     if (!width_ok(in_features)) return IQK_ERR_WIDTH;
     if (num_experts <= 0 || num_experts > 4096) return IQK_ERR_GEOMETRY;
     if (out_features <= 0 || out_features % 16) return IQK_ERR_GEOMETRY;
@@ -327,13 +327,39 @@ int iqk_grouped_run(int member, const void *const *streams, int64_t num_experts,
                                           num_sms_current()));
 }
 
+int iqk_grouped_run_range(int member, const void *const *streams, int64_t num_experts,
+                          int64_t out_features, int64_t in_features, int64_t pairs,
+                          int64_t row_start, int64_t rows, void *y, int y_dtype,
+                          const void *workspace, size_t workspace_bytes, iqk_stream_t stream) {
+    if (!member_ok(member)) return IQK_ERR_MEMBER;
+    if (member == IQK_IQ1_S_R4 && out_features % 4) return IQK_ERR_GEOMETRY;
+    if (!width_ok(in_features)) return IQK_ERR_WIDTH;
+    if (num_experts <= 0 || num_experts > 4096) return IQK_ERR_GEOMETRY;
+    if (out_features <= 0 || out_features % 16) return IQK_ERR_GEOMETRY;
+    if (num_experts * out_features > (int64_t)1 << 30) return IQK_ERR_GEOMETRY;
+    if (row_start < 0 || rows <= 0 || row_start + rows > out_features) return IQK_ERR_GEOMETRY;
+    if (pairs < 0 || pairs > (1 << 24)) return IQK_ERR_GEOMETRY;
+    if (!dtype_ok(y_dtype)) return IQK_ERR_ARGUMENT;
+    if (pairs == 0) return IQK_OK;
+    if (!y || !workspace) return IQK_ERR_ARGUMENT;
+    if (!aligned(y, 4) || !aligned(workspace, 256)) return IQK_ERR_ALIGNMENT;
+    const int st = check_streams(member, streams);
+    if (st != IQK_OK) return st;
+    if (workspace_bytes < grouped_layout(in_features, num_experts, pairs).total)
+        return IQK_ERR_WORKSPACE;
+    return cuda_status(launch_grouped_run(member, streams, num_experts, out_features,
+                                          (int)in_features, pairs, y, y_dtype, workspace,
+                                          reinterpret_cast<cudaStream_t>(stream),
+                                          num_sms_current(), row_start, rows));
+}
+
 int iqk_grouped_gemm(int member, const void *x, int x_dtype, int64_t x_rows,
                      const void *const *streams, int64_t num_experts, int64_t out_features,
                      int64_t in_features, const int32_t *sel, const int32_t *tok, int64_t pairs,
                      void *y, int y_dtype, void *workspace, size_t workspace_bytes,
                      iqk_stream_t stream) {
     if (!member_ok(member)) return IQK_ERR_MEMBER;
-    if (member == IQK_IQ1_S_R4) return IQK_ERR_GEOMETRY;
+    if (member == IQK_IQ1_S_R4 && out_features % 4) return IQK_ERR_GEOMETRY;
     int st = check_prepare(in_features, num_experts, x_rows, pairs, tok, x_dtype);
     if (st != IQK_OK) return st;
     if (out_features <= 0 || out_features % 16) return IQK_ERR_GEOMETRY;

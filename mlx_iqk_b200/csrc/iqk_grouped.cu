@@ -61,6 +61,7 @@
 #include "iqk_common.cuh"
 #include "iqk_grouped.cuh"
 #include "iqk_sync.cuh"
+#include "iqk_tables.cuh"
 
 namespace iqk {
 namespace {
@@ -74,6 +75,11 @@ constexpr int kStageK = 128;                         // weights per k-stage (8 M
 constexpr int kMaxKS = 4096 / kStageK;               // k-stages of the widest row
 constexpr int kCodeK = 512;                          // weights per code load (4 stages)
 constexpr int kCodeBox = kGroupRows * kCodeK / 4;    // 16 KB: 128 rows x 128 B, 128-byte swizzle
+// IQ1_S_R4 codes: 4 qs bytes (grid index low bytes) per 32 weights, so one
+// 512-weight chunk is 128 rows x 64 B (64-byte swizzle)
+__host__ __device__ constexpr int code_box(int member) {
+    return member == IQK_IQ1_S_R4 ? kGroupRows * kCodeK / 8 : kCodeBox;
+}
 constexpr int kMaxCodeSlots = 4;
 constexpr int kMaxXSlots = 8;
 constexpr int kMinXSlots = 4;
@@ -105,13 +111,20 @@ constexpr int kTabEntries = 64;  // IQ2_KS: (scale index + 16) | alphabet << 5; 
 // that the buffer is released before the accumulators are final.
 constexpr int kEcolOff = (kTabOff + 8 * kTabEntries + 15) & ~15;  // 16-byte entries
 constexpr int kBarBytes = kEcolOff + 4 * kTok * 16;
+// IQ1_S_R4: the 2048-entry grid (16-bit codes) after the barrier region
+__host__ __device__ constexpr int bar_bytes(int member) {
+    return kBarBytes + (member == IQK_IQ1_S_R4 ? 4096 : 0);
+}
 static_assert(kEcolOff % 16 == 0 && kTabOff % 8 == 0, "barrier-region alignment");
 constexpr int kSmemCap = 227 * 1024;
 
 // Per-item scale buffer: per (stage, row) scale words, transposed so that a
 // warp's 32 rows read 32 consecutive words; then row factors and the tile's
 // column table (pair index, 2^-S).
-__host__ __device__ constexpr int scale_words(int member) { return member == IQK_IQ2_K ? 2 : 1; }
+// Scale words per (stage, row): IQ2_KS one (four packed group bytes), IQ2_K
+// two (sub-block nibbles; alphabet bits and the f16 super-block scale),
+// IQ1_S_R4 two (the 16-bit qh of the stage's four blocks).
+__host__ __device__ constexpr int scale_words(int member) { return member == IQK_IQ2_KS ? 1 : 2; }
 __host__ __device__ constexpr int scale_buf_bytes(int member, int n, int rows) {
     return scale_words(member) * (n / kStageK) * rows * 4 + rows * 4 + 2 * kTok * 4;
 }
@@ -150,6 +163,11 @@ __device__ __forceinline__ void expand_word(uint32_t w, uint32_t t01, uint32_t t
     }
 }
 
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];\n" : "=r"(v) : "r"(a));
+    return v;
+}
 __device__ __forceinline__ uint2 lds64(uint32_t a) {
     uint2 v;
     asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "r"(a));
@@ -367,6 +385,9 @@ struct XMaps {
 struct GroupedArgs {
     const void *s[5];
     int64_t out_features;
+    // output-row window: rows [row0, row0 + rows_out) of every expert; y is
+    // [pairs, rows_out] (the whole projection: row0 = 0, rows_out = out)
+    int row0, rows_out;  // experts x out_features <= 2^30 (checked by the C ABI)
     int n, pairs, rblocks;
     int xslots, cslots, tok_cap;  // ring depths (activation, code), token cap
     const char *ws;
@@ -404,8 +425,8 @@ __device__ __forceinline__ void load_item_scales(const GroupedArgs &a, int4 tl, 
     }
 #pragma unroll 1
     for (int r = t; r < rows; r += 64) {
-        const int64_t rl = (int64_t)rb * rows + r;
-        const int64_t row = (int64_t)tl.x * out + (rl < out ? rl : 0);
+        const int64_t rl = (int64_t)rb * rows + r;  // window-local row
+        const int64_t row = (int64_t)tl.x * out + a.row0 + (rl < a.rows_out ? rl : 0);
         if (MEMBER == IQK_IQ2_KS) {
             // every load of the row is issued before any is used
             const uint8_t *scl = static_cast<const uint8_t *>(a.s[1]) + row * (n / 64);
@@ -447,6 +468,27 @@ __device__ __forceinline__ void load_item_scales(const GroupedArgs &a, int4 tl, 
                 }
             }
             rsc[r] = half_bits_to_float(dvb);
+        } else if (MEMBER == IQK_IQ1_S_R4) {
+            // qh u16[n/32] (n/16 bytes): stage ks = blocks 4ks .. 4ks+3 = words 2ks, 2ks+1
+            const uint8_t *qh = reinterpret_cast<const uint8_t *>(a.s[1]) + row * (n / 16);
+            const uint16_t dvb = static_cast<const uint16_t *>(a.s[2])[row];
+            // four 16-byte loads in flight at a time (eight stages)
+#pragma unroll 1
+            for (int i0 = 0; i0 < n / 256; i0 += 4) {
+                uint4 v[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) v[i] = ldg128(qh + 16 * (i0 + i));
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int ks = 2 * (i0 + i);
+                    sc[ks * rows + r] = v[i].x;
+                    sc[(KS + ks) * rows + r] = v[i].y;
+                    sc[(ks + 1) * rows + r] = v[i].z;
+                    sc[(KS + ks + 1) * rows + r] = v[i].w;
+                }
+            }
+            // the operand carries (2ls + 1) * 8 * (g + shift); d / 8 goes here
+            rsc[r] = half_bits_to_float(dvb) * 0.125f;
         } else {
             const uint8_t *scl = static_cast<const uint8_t *>(a.s[1]) + row * (n / 32);
             const uint8_t *sex = static_cast<const uint8_t *>(a.s[2]) + row * (n / 128);
@@ -499,7 +541,7 @@ __host__ __device__ inline GemmSmem gemm_smem(int member, int n, int rb_rows, in
     GemmSmem g;
     g.x = 0;
     g.code = (uint32_t)(xslots * x_slot_bytes(kTok));
-    g.sbuf = g.code + cslots * (rb_rows / kGroupRows) * kCodeBox;
+    g.sbuf = g.code + cslots * (rb_rows / kGroupRows) * code_box(member);
     g.sb = (scale_buf_bytes(member, n, rb_rows) + 15) & ~15;
     g.bars = g.sbuf + 2 * g.sb;
     return g;
@@ -511,7 +553,8 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
                     const __grid_constant__ XMaps x_maps) {
     constexpr int kRows = RB * kGroupRows;    // output rows per work item
     constexpr uint32_t kACol = 2 * RB * 64u;  // first A-buffer column (after both accumulator sets)
-    constexpr int kCodeSlot = RB * kCodeBox;  // codes of one 512-weight chunk, all rows
+    constexpr int kCodeSlot = RB * code_box(MEMBER);  // codes of one 512-weight chunk, all rows
+    constexpr uint32_t kCodeRow = MEMBER == IQK_IQ1_S_R4 ? 64u : 128u;  // code bytes per row
     extern __shared__ char smem_raw[];
     char *smem = smem_raw + ((1024u - (saddr(smem_raw) & 1023u)) & 1023u);
     const uint32_t smem_u = saddr(smem);
@@ -539,6 +582,7 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
     // times the index (IQ2_KS), or times the index before the super-block
     // scale (IQ2_K). Products of small integers: exact in f16.
     uint2 *gtab = reinterpret_cast<uint2 *>(smem + G.bars + kTabOff);
+    uint16_t *grid = reinterpret_cast<uint16_t *>(smem + G.bars + kBarBytes);  // IQ1_S_R4
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int32_t *hdr = reinterpret_cast<const int32_t *>(a.ws + a.L.hdr);
@@ -573,7 +617,20 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
         *abort_flag = 0;
         bar_fence_init();
     }
-    if (threadIdx.x < kTabEntries) {
+    if (MEMBER == IQK_IQ1_S_R4) {
+        for (int i = threadIdx.x; i < 2048; i += blockDim.x) grid[i] = g_iq1s_grid[i];
+    }
+    if (MEMBER == IQK_IQ1_S_R4 && threadIdx.x < 16) {
+        // block table (ls | sign << 3): {T0, T1}, {T2, 0} with
+        // T[c] = (2ls + 1) * (8 * (c - 1) + s), s = -1 for a set sign bit:
+        // small integers, exact in f16
+        const int i = threadIdx.x;
+        const float m = (float)(2 * (i & 7) + 1), sg = (i & 8) ? -1.f : 1.f;
+        const __half2 a01 = __floats2half2_rn(m * (sg - 8.f), m * sg);
+        const __half2 a23 = __floats2half2_rn(m * (sg + 8.f), 0.f);
+        gtab[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&a01),
+                             *reinterpret_cast<const uint32_t *>(&a23));
+    } else if (MEMBER != IQK_IQ1_S_R4 && threadIdx.x < kTabEntries) {
         const int i = threadIdx.x;
         const int idx = MEMBER == IQK_IQ2_KS ? (i & 31) - 16 : (i & 15) - 8;
         const bool alpha = MEMBER == IQK_IQ2_KS ? (i >> 5) & 1 : (i >> 4) & 1;
@@ -590,14 +647,15 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
     // shard preparation leaves the rows of other ranks' pairs untouched.
     {
         const int tail = hdr[3] ? 0 : a.pairs - n_valid;
-        const int64_t total = (int64_t)tail * out;
+        const int ro = a.rows_out;
+        const int64_t total = (int64_t)tail * ro;
         for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
              i += (int64_t)gridDim.x * blockDim.x) {
-            const int64_t p = order[n_valid + i / out];
-            const int64_t r = i % out;
-            if (a.y_dtype == IQK_F32) store_out<float>(a.y, p * out + r, 0.f);
-            else if (a.y_dtype == IQK_F16) store_out<__half>(a.y, p * out + r, 0.f);
-            else store_out<__nv_bfloat16>(a.y, p * out + r, 0.f);
+            const int64_t p = order[n_valid + i / ro];
+            const int64_t r = i % ro;
+            if (a.y_dtype == IQK_F32) store_out<float>(a.y, p * ro + r, 0.f);
+            else if (a.y_dtype == IQK_F16) store_out<__half>(a.y, p * ro + r, 0.f);
+            else store_out<__nv_bfloat16>(a.y, p * ro + r, 0.f);
         }
     }
     __syncthreads();
@@ -650,7 +708,7 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
             for (int64_t it = blockIdx.x; ok && it < items && !*abort_flag; it += gridDim.x) {
                 const int4 tl = tiles[it / a.rblocks];
                 const int rb = (int)(it % a.rblocks);
-                const int row0 = (int)((int64_t)tl.x * out + (int64_t)rb * kRows);
+                const int row0 = (int)((int64_t)tl.x * out + a.row0 + (int64_t)rb * kRows);
                 for (int c = 0; c < KS / 4; ++c, ++cchunk) {
                     const int cs = cchunk % CS;
                     if (!bar_wait(&cempty[cs], ((uint32_t)(cchunk / CS) & 1u) ^ 1u, abort_flag)) {
@@ -661,7 +719,7 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
 #pragma unroll
                     for (int j = 0; j < RB; ++j)
                         tma_2d(smem_u + G.code + cs * kCodeSlot + j * kCodeBox, &qs_map,
-                               c * (kCodeK / 4), row0 + j * kGroupRows, &cfull[cs]);
+                               c * (int)kCodeRow, row0 + j * kGroupRows, &cfull[cs]);
                 }
             }
             if (!ok) give_up();
@@ -775,9 +833,21 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
                 }
                 // this warp's code words of the stage: word w of the stage is
                 // word w % 4 of 16-byte chunk 2*sub + w / 4 of the row
-                const uint32_t code_u = smem_u + G.code + cs * kCodeSlot + rloc * 128;
+                const uint32_t code_u = smem_u + G.code + cs * kCodeSlot + rloc * kCodeRow;
                 uint32_t words[WPW];
-                if (WPW == 4) {
+                if (MEMBER == IQK_IQ1_S_R4) {
+                    // the stage's 16 qs bytes (4 blocks) are 16-byte chunk `sub`
+                    // of the row, 64-byte swizzled; this warp's code words
+                    // kh*WPW .. are blocks kh*WPW/2 ..: one qs word per block
+                    const uint32_t ch = code_u + (((uint32_t)sub ^ ((uint32_t)(rloc >> 1) & 3u)) << 4);
+                    if (WPW == 4) {
+                        const uint2 c = lds64(ch + (uint32_t)kh * 8u);
+                        words[0] = c.x;
+                        words[1] = c.y;
+                    } else {
+                        words[0] = lds32(ch + (uint32_t)kh * 4u);
+                    }
+                } else if (WPW == 4) {
                     const uint4 c = lds128(code_u + (((uint32_t)(2 * sub + kh) ^ rsw) << 4));
                     words[0] = c.x;
                     words[1] = c.y;
@@ -803,10 +873,31 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
                                        (uint32_t)(kh * WPW) * 8u;
                 // IQ2_K: the super-block scale, f16 in both halves
                 const uint32_t dsb2 = MEMBER == IQK_IQ2_K ? (s1 >> 16) * 0x10001u : 0u;
-                uint32_t t01 = 0, t23 = 0;
+                uint32_t t01 = 0, t23 = 0, hs = 0, qw = 0;
 #pragma unroll
                 for (int wd = 0; wd < WPW; ++wd) {
                     const int wg = kh * WPW + wd;  // word of the stage
+                    if (MEMBER == IQK_IQ1_S_R4) {
+                        if ((wd & 1) == 0) {  // one 32-weight block per two code words
+                            const int bl = wg >> 1;  // block of the stage
+                            const uint32_t h = (((bl & 2) ? s1 : s0) >> (16 * (bl & 1))) & 0xffffu;
+                            // the four 3-bit grid-index high parts, one per byte
+                            hs = (((h & 0x1C7u) * 0x401u) & 0x00070007u) |
+                                 (((h & 0xE38u) * 0x8020u) & 0x07000700u);
+                            const uint2 t = gtab[(h >> 12) & 15u];
+                            t01 = t.x;
+                            t23 = t.y;
+                            qw = words[wd >> 1];
+                        }
+                        // both grid indices of octets 2o, 2o+1: qs byte | high part << 8
+                        const uint32_t v = prmt(qw, hs, (wd & 1) ? 0x7362u : 0x5140u);
+                        const uint32_t cw = (uint32_t)grid[v & 0xffffu] |
+                                            ((uint32_t)grid[v >> 16] << 16);
+                        uint32_t r[8];
+                        expand_word(cw, t01, t23, r);
+                        tmem_st8(taddr + wd * 8, r);
+                        continue;
+                    }
                     if (MEMBER == IQK_IQ2_KS) {
                         if ((wd & 1) == 0) {  // one 32-weight group per two words
                             const uint2 t = gtab[prmt(s0, 0u, 0x4440u + (uint32_t)(wg >> 1))];
@@ -869,7 +960,7 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
 #pragma unroll
             for (int h = 0; h < kTok / 32; ++h) {
                 const int col = 32 * h + lane;
-                const int64_t off = col < tl.z ? (int64_t)colp[col] * out : 0;
+                const int64_t off = col < tl.z ? (int64_t)colp[col] * a.rows_out : 0;
                 ecol[col] = make_uint4((uint32_t)off, (uint32_t)(off >> 32),
                                        __float_as_uint(colf[col]), 0u);
             }
@@ -883,7 +974,7 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
 #pragma unroll
             for (int j = 0; j < RB; ++j) {
                 const int64_t rlocal = (int64_t)rb * kRows + kGroupRows * j + 32 * q + lane;
-                const bool row_ok = rlocal < out;
+                const bool row_ok = rlocal < a.rows_out;
                 for (int c = 0; c < npad; c += 8) {
                     uint32_t d[8];
                     tmem_ld8(tmem + lane_base + (uint32_t)((sacc * RB + j) * 64 + c), d);
@@ -992,12 +1083,15 @@ cudaError_t launch_grouped_prepare(const void *x, int x_dtype, int64_t x_rows, i
 
 cudaError_t launch_grouped_run(int member, const void *const *streams, int64_t num_experts,
                                int64_t out_features, int n, int64_t pairs, void *y, int y_dtype,
-                               const void *ws, cudaStream_t stream, int num_sms) {
+                               const void *ws, cudaStream_t stream, int num_sms,
+                               int64_t row_start, int64_t rows_out) {
     const GroupedLayout L = grouped_layout(n, num_experts, pairs);
     GroupedArgs ga{};
     const RowBytes rb = row_bytes(member, n);
     for (int i = 0; i < rb.count; ++i) ga.s[i] = streams[i];
     ga.out_features = out_features;
+    ga.row0 = (int)row_start;
+    ga.rows_out = (int)(rows_out < 0 ? out_features : rows_out);
     ga.n = n;
     ga.pairs = (int)pairs;
     ga.ws = static_cast<const char *>(ws);
@@ -1012,7 +1106,7 @@ cudaError_t launch_grouped_run(int member, const void *const *streams, int64_t n
     auto plan = [&](int rows, int &cslots, int &xslots, int &fixed) {
         for (cslots = kMaxCodeSlots; cslots >= 1; --cslots) {
             if (rows == 256 && cslots > 2) continue;
-            fixed = 1024 + (int)gemm_smem(member, n, rows, 0, cslots).bars + kBarBytes;
+            fixed = 1024 + (int)gemm_smem(member, n, rows, 0, cslots).bars + bar_bytes(member);
             xslots = (kSmemCap - fixed) / x_slot_bytes(L.tok_cap);
             if (xslots >= kMinXSlots) break;
         }
@@ -1024,16 +1118,20 @@ cudaError_t launch_grouped_run(int member, const void *const *streams, int64_t n
         rows = 128;
         if (!plan(128, cslots, xslots, fixed)) return cudaErrorInvalidConfiguration;
     }
-    ga.rblocks = (int)((out_features + rows - 1) / rows);
+    ga.rblocks = (int)((ga.rows_out + rows - 1) / rows);
     ga.xslots = xslots;
     ga.cslots = cslots;
     const int smem = fixed + xslots * x_slot_bytes(L.tok_cap);
     CUtensorMap qmap;
     XMaps xmap{};
-    // codes: [E * out rows, n / 4 bytes], 128 rows x 128 B boxes (512 weights), 128-byte swizzle
-    cudaError_t err = encode_map(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, streams[0], (uint64_t)n / 4,
-                                 (uint64_t)(num_experts * out_features), (uint64_t)n / 4,
-                                 kCodeK / 4, kGroupRows, CU_TENSOR_MAP_SWIZZLE_128B);
+    // codes: [E * out rows, n / 4 bytes], 128 rows x 128 B boxes (512 weights), 128-byte
+    // swizzle; IQ1_S_R4 [E * out rows, n / 8 bytes], 128 rows x 64 B, 64-byte swizzle
+    const bool iq1 = member == IQK_IQ1_S_R4;
+    const uint64_t qrow = iq1 ? (uint64_t)n / 8 : (uint64_t)n / 4;
+    cudaError_t err = encode_map(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, streams[0], qrow,
+                                 (uint64_t)(num_experts * out_features), qrow,
+                                 iq1 ? kCodeK / 8 : kCodeK / 4, kGroupRows,
+                                 iq1 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
     if (err != cudaSuccess) return err;
     // activations: [pairs rows, n] f16, boxes of 64 elements x (16 .. tok_cap) rows,
     // 128-byte swizzle
@@ -1070,7 +1168,8 @@ cudaError_t launch_grouped_run(int member, const void *const *streams, int64_t n
         if (rows == 256) IQK_GG(IQK_IQ2_K, 2);
         else IQK_GG(IQK_IQ2_K, 1);
     } else {
-        return cudaErrorInvalidValue;
+        if (rows == 256) IQK_GG(IQK_IQ1_S_R4, 2);
+        else IQK_GG(IQK_IQ1_S_R4, 1);
     }
 #undef IQK_GG
     return cudaGetLastError();

@@ -43,6 +43,7 @@ cudaError_t launch_pairs_combine(const float *y, const int32_t *sel, int64_t row
 
 cudaError_t launch_grouped_run(int member, const void *const *streams, int64_t num_experts,
                                int64_t out_features, int n, int64_t pairs, void *y, int y_dtype,
-                               const void *ws, cudaStream_t stream, int num_sms);
+                               const void *ws, cudaStream_t stream, int num_sms,
+                               int64_t row_start = 0, int64_t rows_out = -1);
 
 }  // namespace iqk

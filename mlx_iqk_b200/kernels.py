@@ -120,6 +120,9 @@ def library() -> ctypes.CDLL:
     lib.iqk_grouped_prepare.restype = i32
     lib.iqk_grouped_run.argtypes = [i32, vp, i64, i64, i64, i64, vp, i32, vp, sz, vp]
     lib.iqk_grouped_run.restype = i32
+    lib.iqk_grouped_run_range.argtypes = [i32, vp, i64, i64, i64, i64, i64, i64, vp, i32, vp,
+                                          sz, vp]
+    lib.iqk_grouped_run_range.restype = i32
     lib.iqk_grouped_read_error.argtypes = [vp, ctypes.POINTER(ctypes.c_int32), vp]
     lib.iqk_grouped_read_error.restype = i32
     lib.iqk_gemv_static_max_bytes.restype = sz
@@ -147,7 +150,7 @@ def exported_symbols() -> list[str]:
             "iqk_gemv_static_max_bytes", "iqk_gemv_static", "iqk_gemv_static_read_error",
             "iqk_grouped_prepare_shard",
             "iqk_pairs_swiglu", "iqk_pairs_combine", "iqk_gemv_floor_run",
-            "iqk_dequant_floor"]
+            "iqk_dequant_floor", "iqk_grouped_run_range"]
 
 
 def raise_for_status(status: int, what: str) -> None:
@@ -307,7 +310,7 @@ def gemv_static_read_error(in_features: int, x_rows: int, pairs: int,
     return int(flags.value)
 
 
-GROUPED_MEMBERS = ("iq2_ks", "iq2_k")
+GROUPED_MEMBERS = ("iq2_ks", "iq2_k", "iq1_s_r4")
 """Members the tensor-core grouped GEMM (prefill route) covers."""
 
 
@@ -359,6 +362,19 @@ def grouped_run(member: str, streams, num_experts: int, out_features: int, in_fe
         y.data_ptr(), DTYPE_IDS[y.dtype], workspace.data_ptr(), workspace.numel(),
         stream_handle(y.device))
     raise_for_status(status, "iqk_grouped_run")
+    return y
+
+
+def grouped_run_range(member: str, streams, num_experts: int, out_features: int,
+                      in_features: int, pairs: int, row_start: int, rows: int, y: torch.Tensor,
+                      workspace: torch.Tensor) -> torch.Tensor:
+    """``iqk_grouped_run_range``: output rows [row_start, row_start + rows) of
+    every expert over a prepared workspace into ``y`` [pairs, rows]."""
+    status = library().iqk_grouped_run_range(
+        MEMBER_IDS[member], ptr_array(streams), num_experts, out_features, in_features, pairs,
+        row_start, rows, y.data_ptr(), DTYPE_IDS[y.dtype], workspace.data_ptr(),
+        workspace.numel(), stream_handle(y.device))
+    raise_for_status(status, "iqk_grouped_run_range")
     return y
 
 

@@ -198,15 +198,39 @@ class IqkSwitchLinear(nn.Module):
                          self.in_features, start, rows, out)
 
     def sorted_matmul_range(self, x, indices, start: int, rows: int) -> torch.Tensor:
-        """The sorted projection restricted to out rows ``[start, start + rows)``.
+        """The sorted projection restricted to out rows ``[start, start + rows)``:
+        ``[..., top_k, 1, rows]``.
 
-        Concatenating range outputs along the feature axis reproduces the
-        unsplit call bit for bit (each output element is one dot product).
+        Only those rows of every selected expert are read and multiplied (the
+        reference bounds its live memory the same way,
+        ``src/mlx_iqk/nn.py:203-217``); each output element is the same dot
+        product as in the unsplit sorted call, so concatenating range outputs
+        along the feature axis reproduces it bit for bit. ``rows`` is a
+        positive power of two, as in the reference.
         """
-        full = self(x, indices, sorted_indices=True)
+        start, rows = int(start), int(rows)
         if rows <= 0 or rows & (rows - 1) or start < 0 or start + rows > self.out_features:
-            raise IqkRuntimeError(f"bad range [{start}, {start + rows})")
-        return full[..., start:start + rows].contiguous()
+            raise IqkRuntimeError(
+                f"range [{start}, {start + rows}) is not a power-of-two slice of "
+                f"out_features {self.out_features}")
+        if self.member not in K.GROUPED_MEMBERS:
+            full = self.gemv(x, indices)
+            return full[..., start:start + rows].contiguous()
+        xt = self._prep(x)
+        idx_shape = tuple(indices.shape)
+        sel = self._idx(indices, self.device)
+        mats, xrows = sel.numel(), xt.shape[0]
+        if xrows <= 0 or mats % xrows:
+            raise IqkRuntimeError(
+                f"{mats} token-expert pairs do not tile {xrows} activation "
+                f"row(s); the operand and the routing disagree")
+        ws = torch.empty(K.grouped_workspace_bytes(self.in_features, self.num_experts, mats),
+                         dtype=torch.uint8, device=self.device)
+        K.grouped_prepare(xt, self.num_experts, self.in_features, sel, None, ws)
+        y = torch.empty((mats, rows), dtype=torch.float32, device=self.device)
+        K.grouped_run_range(self.member, self._streams(), self.num_experts, self.out_features,
+                            self.in_features, mats, start, rows, y, ws)
+        return y.reshape(*idx_shape, rows).unsqueeze(-2)
 
     # -- call ---------------------------------------------------------------
 
@@ -223,7 +247,6 @@ class IqkSwitchLinear(nn.Module):
         fused dequant + GEMV; prefill-sized or ``sorted_indices=True`` calls
         run the tensor-core grouped GEMM (``src/mlx_iqk/nn.py:221-238`` makes
         the same split, with dequantize + ``gather_mm`` on the prefill side).
-        ``iq1_s_r4`` has no grouped kernel and always takes the GEMV.
         """
         pairs = indices.numel() if isinstance(indices, torch.Tensor) else \
             int(np.asarray(indices).size)

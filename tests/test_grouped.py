@@ -126,9 +126,8 @@ def test_module_routes_prefill_calls(cuda):
     assert torch.equal(mod(x[:2], few, sorted_indices=True), mod.grouped(x[:2], few))
     assert torch.equal(mod(x[:2], few), mod.gemv(x[:2], few))
     iq1, _, _ = make_module("iq1_s_r4", n, seed=12)
-    assert torch.equal(iq1(x, idx), iq1.gemv(x, idx))  # no grouped kernel for iq1_s_r4
-    with pytest.raises(K.IqkKernelError):
-        iq1.grouped(x, idx)
+    assert torch.equal(iq1(x, idx), iq1.grouped(x, idx))  # every member has the prefill route
+    assert torch.equal(iq1(x[:2], few), iq1.gemv(x[:2], few))
 
 
 def test_grouped_bad_index_and_nonfinite_row(cuda):
@@ -202,3 +201,50 @@ def test_grouped_repeated_calls_never_time_out(cuda):
     for _ in range(40):
         K.grouped_run("iq2_ks", mod._streams(), E, out, n, sel.numel(), y, ws)
     assert K.grouped_read_error(ws) & 8 == 0  # IQK_DEVERR_TIMEOUT
+
+
+@pytest.mark.parametrize("member", K.GROUPED_MEMBERS)
+@pytest.mark.parametrize("n", WIDTHS)
+def test_sorted_matmul_range_concat_matches_the_sorted_call(cuda, member, n):
+    """Range outputs concatenated along features equal the unsplit sorted
+    call bit for bit (the reference's gate, tests/test_nn.py:337-360), with
+    ranges that cut 128-row blocks and a range that ends at the last row."""
+    mod, _, _ = make_module(member, n, seed=oracle.seed_for(member, n, "nsplit"), experts=8,
+                            out_features=512)
+    rng = np.random.default_rng(67)
+    tokens, top_k = 24, 4
+    x = torch.from_numpy(rng.standard_normal((tokens, 1, 1, n)).astype(np.float32)).to(cuda)
+    idx = np.sort(rng.integers(0, 8, size=(tokens, top_k)), axis=None).reshape(tokens, top_k)
+    idx = torch.from_numpy(idx).to(cuda)
+    full = mod(x, idx, sorted_indices=True)
+    for cuts in ((0, 256, 512), (0, 64, 128, 256, 512), (0, 32, 64, 128, 256, 384, 448, 480, 512)):
+        parts = []
+        for a, b in zip(cuts, cuts[1:]):
+            part = mod.sorted_matmul_range(x, idx, a, b - a)
+            assert part.shape == (tokens, top_k, 1, b - a)
+            parts.append(part)
+        got = torch.cat(parts, dim=-1)
+        assert torch.equal(got.view(torch.int32), full.view(torch.int32)), cuts
+
+
+def test_sorted_matmul_range_refuses_a_bad_range(cuda):
+    mod, _, _ = make_module("iq2_ks", 2048, seed=61, experts=8, out_features=64)
+    x = torch.randn((2, 1, 1, 2048), device=cuda)
+    idx = torch.zeros((2, 2), dtype=torch.int64, device=cuda)
+    for start, rows in ((0, 0), (0, 12), (0, -8), (-8, 8), (60, 8), (0, 128)):
+        with pytest.raises(K.IqkRuntimeError):
+            mod.sorted_matmul_range(x, idx, start, rows)
+
+
+def test_sorted_matmul_range_at_full_geometry(cuda):
+    """E=256, gate [2048, 4096]: a 256-row slice of a 2048-token sorted
+    dispatch equals that slice of the unsplit call."""
+    from mlx_iqk_b200.profile_cases import random_module
+    gen = torch.Generator(device=cuda).manual_seed(99)
+    mod = random_module("iq2_k", 256, 2048, 4096, cuda, gen)
+    T = 512
+    idx = torch.topk(torch.randn((T, 256), generator=gen, device=cuda), 6, dim=-1).indices
+    x = torch.randn((T, 1, 1, 4096), generator=gen, device=cuda).to(torch.bfloat16)
+    full = mod(x, idx, sorted_indices=True)
+    part = mod.sorted_matmul_range(x, idx, 1024, 256)
+    assert torch.equal(part, full[..., 1024:1280])
