@@ -821,8 +821,14 @@ def run_b200(args) -> None:
                 "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4), "peak_source": peak_src,
                 "us_per_launch": gate_leg["us"], "bytes_per_launch": gate_leg["bytes_per_launch"],
-                "traffic": traffic["dram_bytes_per_launch"] if traffic else None,
-                "traffic_source": traffic.get("source") if traffic else None,
+                # the committed capture's DRAM bytes per algorithmic byte, on
+                # this launch's algorithmic bytes (its draw has other experts)
+                "traffic": (round(traffic["traffic_over_algorithmic"]
+                                  * gate_leg["bytes_per_launch"]) if traffic else None),
+                "traffic_capture": ({k: traffic[k] for k in ("dram_bytes_per_launch",
+                                                              "algorithmic_bytes_same_launch",
+                                                              "traffic_over_algorithmic",
+                                                              "command")} if traffic else None),
                 "floor_us": gate_leg["floor_us"], "vs_own_floor": gate_leg["vs_own_floor"]}
     floors = {f"gemv gate B={c8.B}": gate_leg, f"gemv down B={c8.B}": down_leg}
 

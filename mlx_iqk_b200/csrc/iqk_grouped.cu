@@ -718,7 +718,7 @@ grouped_gemm_kernel(const GroupedArgs a, const __grid_constant__ CUtensorMap qs_
                     bar_expect_tx(&cfull[cs], kCodeSlot);
 #pragma unroll
                     for (int j = 0; j < RB; ++j)
-                        tma_2d(smem_u + G.code + cs * kCodeSlot + j * kCodeBox, &qs_map,
+                        tma_2d(smem_u + G.code + cs * kCodeSlot + j * code_box(MEMBER), &qs_map,
                                c * (int)kCodeRow, row0 + j * kGroupRows, &cfull[cs]);
                 }
             }
