@@ -84,6 +84,19 @@ int iqk_abi_version(void);
 int iqk_check_device(void);
 
 /*
+ * On-device relayout of ik wire rows into the streams above: wire is
+ * [rows, ggml row bytes] (IQ2_KS 2 + 70*n/256, IQ2_K 76*n/256, IQ1_S_R4
+ * 2 + 6*n/32 -- for IQ1_S_R4 rows is a multiple of 4, the wire's row groups);
+ * streams[i] receives [rows, stream length] in component order, the same
+ * bits as the reference's host relayout. in_features a multiple of 256.
+ *
+ * Replaces format.pack (src/mlx_iqk/format.py:612-678, the numpy relayout
+ * the reference runs on the host before load_streams).
+ */
+int iqk_pack(int member, const void *wire, int64_t rows, int64_t in_features,
+             void *const *streams, iqk_stream_t stream);
+
+/*
  * Bit-exact stacked dequantization of out-rows [row_start, row_start + rows)
  * of every expert into dst[E, rows, in_features] (row-major), in float32,
  * float16 or bfloat16 (out_dtype). Every weight is the CPU dequantizer's

@@ -16,7 +16,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 SOURCES = ["iqk_capi.cu", "iqk_dequant.cu", "iqk_ep.cu", "iqk_gemv.cu", "iqk_grouped.cu",
-           "iqk_static.cu"]
+           "iqk_pack.cu", "iqk_static.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-shared",
          "--expt-relaxed-constexpr", "-diag-suppress", "177"]

@@ -118,6 +118,24 @@ int iqk_dequant_floor(int member, const void *const *streams, int64_t num_expert
                                       num_sms_current(), true));
 }
 
+int iqk_pack(int member, const void *wire, int64_t rows, int64_t in_features,
+             void *const *streams, iqk_stream_t stream) {
+    if (!member_ok(member)) return IQK_ERR_MEMBER;
+    if (in_features <= 0 || in_features % 256 || in_features > (1 << 20)) return IQK_ERR_WIDTH;
+    if (rows < 0 || rows > ((int64_t)1 << 31)) return IQK_ERR_GEOMETRY;
+    if (member == IQK_IQ1_S_R4 && rows % 4) return IQK_ERR_GEOMETRY;
+    if (rows == 0) return IQK_OK;
+    if (!wire || !streams) return IQK_ERR_ARGUMENT;
+    if (!aligned(wire, 16)) return IQK_ERR_ALIGNMENT;
+    const RowBytes rb = row_bytes(member, in_features);
+    for (int i = 0; i < rb.count; ++i) {
+        if (!streams[i]) return IQK_ERR_ARGUMENT;
+        if (!aligned(streams[i], 16)) return IQK_ERR_ALIGNMENT;
+    }
+    return cuda_status(launch_pack(member, wire, rows, (int)in_features, streams,
+                                   reinterpret_cast<cudaStream_t>(stream), num_sms_current()));
+}
+
 size_t iqk_gemv_workspace_bytes(int member, int64_t in_features, int64_t x_rows,
                                 int64_t pairs) {
     if (!member_ok(member) || !width_ok(in_features) || x_rows < 0 || pairs < 0) return 0;

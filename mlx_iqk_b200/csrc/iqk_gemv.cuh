@@ -38,6 +38,8 @@ cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_
                             int64_t out_features, int n, int64_t x_rows, int64_t pairs, void *y,
                             int y_dtype, const void *ws, cudaStream_t stream, int num_sms,
                             bool floor = false);
+cudaError_t launch_pack(int member, const void *wire, int64_t rows, int n,
+                        void *const *streams, cudaStream_t stream, int num_sms);
 cudaError_t launch_dequant(int member, const void *const *streams, int64_t num_experts,
                            int64_t out_features, int n, int64_t row_start,
                            int64_t rows, int out_dtype, void *dst, cudaStream_t stream,

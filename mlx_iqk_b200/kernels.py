@@ -96,6 +96,8 @@ def library() -> ctypes.CDLL:
     lib.iqk_check_device.restype = i32
     lib.iqk_dequant.argtypes = [i32, vp, i64, i64, i64, i64, i64, i32, vp, vp]
     lib.iqk_dequant.restype = i32
+    lib.iqk_pack.argtypes = [i32, vp, i64, i64, vp, vp]
+    lib.iqk_pack.restype = i32
     lib.iqk_gemv_workspace_bytes.argtypes = [i32, i64, i64, i64]
     lib.iqk_gemv_workspace_bytes.restype = sz
     lib.iqk_gemv.argtypes = [i32, vp, i32, i64, vp, i64, i64, i64, vp, vp, i64, vp, i32, vp,
@@ -150,7 +152,7 @@ def exported_symbols() -> list[str]:
             "iqk_gemv_static_max_bytes", "iqk_gemv_static", "iqk_gemv_static_read_error",
             "iqk_grouped_prepare_shard",
             "iqk_pairs_swiglu", "iqk_pairs_combine", "iqk_gemv_floor_run",
-            "iqk_dequant_floor", "iqk_grouped_run_range"]
+            "iqk_dequant_floor", "iqk_grouped_run_range", "iqk_pack"]
 
 
 def raise_for_status(status: int, what: str) -> None:
@@ -193,6 +195,16 @@ def ptr_array(tensors) -> ctypes.Array:
         arr = (ctypes.c_void_p * len(key))(*key)
         _PTR_ARRAYS[key] = arr
     return arr
+
+
+def pack(member: str, wire: torch.Tensor, in_features: int, streams) -> None:
+    """``iqk_pack``: ik wire rows [rows, ggml row bytes] (uint8, on the device)
+    into ``streams`` (component order, each [rows, length] viewed flat)."""
+    check_device(wire.device)
+    status = library().iqk_pack(MEMBER_IDS[check_member(member)], wire.data_ptr(),
+                                wire.shape[0], in_features, ptr_array(streams),
+                                stream_handle(wire.device))
+    raise_for_status(status, "iqk_pack")
 
 
 def dequant(member: str, streams, num_experts: int, out_features: int, in_features: int,

@@ -168,6 +168,27 @@ class IqkSwitchLinear(nn.Module):
         for name, t in staged.items():
             setattr(self, name, t)
 
+    def load_wire(self, wire) -> None:
+        """Install ik wire rows (``[E * out, ggml row bytes]`` uint8, e.g. the
+        tensor bytes of a GGUF file), relaid out on the device.
+
+        The same streams as ``load_streams(format.pack(member, wire, in))``
+        bit for bit; the relayout runs as one kernel (``iqk_pack``) where the
+        reference runs ``format.pack`` on the host (``src/mlx_iqk/format.py:612-678``).
+        """
+        from .format import ik_row_bytes
+        rb = ik_row_bytes(self.member, self.in_features)
+        rows = self.num_experts * self.out_features
+        if isinstance(wire, np.ndarray):
+            wire = torch.from_numpy(np.ascontiguousarray(wire, dtype=np.uint8))
+        if not isinstance(wire, torch.Tensor) or wire.element_size() != 1:
+            raise IqkRuntimeError("wire must be a uint8 array or tensor")
+        if wire.numel() != rows * rb:
+            raise IqkRuntimeError(
+                f"wire of {wire.numel()} bytes is not {rows} rows of {rb} bytes")
+        w = wire.reshape(rows, rb).to(self.device).contiguous()
+        K.pack(self.member, w.view(torch.uint8), self.in_features, self._streams())
+
     # -- dequantized route --------------------------------------------------
 
     def dequantized(self, dtype: torch.dtype = torch.float16) -> torch.Tensor:

@@ -107,6 +107,11 @@ def main() -> None:
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--graph", action="store_true",
                     help="time the calls replayed from one CUDA graph (no host launch cost)")
+    ap.add_argument("--floor", action="store_true",
+                    help="gemv / dequant: run the kernel's address floor instead")
+    ap.add_argument("--rotate", type=int, default=1,
+                    help="gemv: routings prepared up front and cycled, so that the weights "
+                         "do not stay in L2 across calls")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     gen = torch.Generator(device=dev).manual_seed(11)
@@ -137,18 +142,31 @@ def main() -> None:
     line = {"case": args.case, "member": args.member, "experts": E, "out": out, "in": n}
     if args.case == "gemv":
         B = args.batch
-        x = torch.randn((B, n), generator=gen, device=dev).to(torch.bfloat16)
-        sel = torch.stack([torch.randperm(E, generator=gen, device=dev)[:6] for _ in range(B)])
-        sel = sel.reshape(-1).to(torch.int32)
+        run = K.gemv_floor_run if args.floor else K.gemv_run
+        wss, distincts = [], []
+        for _ in range(max(1, args.rotate)):
+            x = torch.randn((B, n), generator=gen, device=dev).to(torch.bfloat16)
+            sel = torch.stack([torch.randperm(E, generator=gen, device=dev)[:6]
+                               for _ in range(B)])
+            sel = sel.reshape(-1).to(torch.int32)
+            ws = torch.empty(K.gemv_workspace_bytes(args.member, n, B, B * 6),
+                             dtype=torch.uint8, device=dev)
+            K.gemv_prepare(x, E, n, sel, None, ws)
+            wss.append(ws)
+            distincts.append(len(set(sel.tolist())))
         y = torch.empty((B * 6, out), device=dev)
-        ws = torch.empty(K.gemv_workspace_bytes(args.member, n, B, B * 6), dtype=torch.uint8,
-                         device=dev)
-        K.gemv_prepare(x, E, n, sel, None, ws)
-        ms = timed(lambda: K.gemv_run(args.member, mod._streams(), E, out, n, B, B * 6, y, ws),
-                   args.reps, args.graph)
-        distinct = len(set(sel.tolist()))
-        nbytes = distinct * out * rb + B * n * 2 + B * 6 * out * 4
-        line.update(batch=B, distinct_experts=distinct, us=round(ms * 1e3, 2),
+        calls = {"i": 0}
+
+        def one():
+            ws = wss[calls["i"] % len(wss)]
+            calls["i"] += 1
+            run(args.member, mod._streams(), E, out, n, B, B * 6, y, ws)
+
+        ms = timed(one, args.reps, args.graph)
+        distinct = sum(distincts) / len(distincts)
+        nbytes = int(distinct * out * rb + B * n * 2 + B * 6 * out * 4)
+        line.update(batch=B, distinct_experts=distinct, floor=args.floor, rotate=args.rotate,
+                    us=round(ms * 1e3, 2),
                     bytes=nbytes, GBps=round(nbytes / (ms * 1e-3) / 1e9, 1),
                     note="run kernel only (prepared once); weights are L2-hot across reps "
                          "when distinct experts x rows x row bytes < 126 MB")
@@ -168,7 +186,8 @@ def main() -> None:
                     tflops=round(flops / (ms * 1e-3) / 1e12, 1))
     else:
         y = torch.empty((E, out, n), dtype=torch.float16, device=dev)
-        ms = timed(lambda: K.dequant(args.member, mod._streams(), E, out, n, 0, out, y),
+        fn = K.dequant_floor if args.floor else K.dequant
+        ms = timed(lambda: fn(args.member, mod._streams(), E, out, n, 0, out, y),
                    args.reps, args.graph)
         nbytes = E * out * rb + E * out * n * 2
         line.update(us=round(ms * 1e3, 2), bytes=nbytes,
