@@ -200,6 +200,35 @@ int iqk_gemv_floor_run(int member, const void *const *streams, int64_t num_exper
                        size_t workspace_bytes, iqk_stream_t stream);
 
 /*
+ * A SwitchGLU's gate and up projections in one launch over a prepared
+ * workspace (iqk_gemv_prepare of the layer input): for every routed pair p
+ * and row r < out_features,
+ *   h[p, r] = silu(gate_p[r]) * up_p[r] * weight[p]     (float32)
+ * where gate_p / up_p are the two projections' decode GEMVs of the pair
+ * (the same per-element values iqk_gemv_run gives) and weight is the pair's
+ * router weight (NULL: 1). Both projections have member `member`; the down
+ * projection is linear, so folding the router weight into h makes the
+ * layer's output the plain sum over a token's pairs (iqk_pairs_combine).
+ * out_features a multiple of 32. Each CTA item covers 32 rows of one pair
+ * in both projections, so silu * up happens before anything leaves the SM.
+ *
+ * iqk_swiglu_rows: the same h from two finished float32 projections
+ * [rows, cols] (for a layer whose gate and up members differ).
+ *
+ * Replaces the caller's seam around the reference's projections
+ * (src/mlx_iqk/nn.py:1-22: gate and up IqkSwitchLinear on the token,
+ * SiLU(gate) * up, down); the reference runs them as separate dispatches.
+ */
+int iqk_gemv_glu_run(int member, const void *const *gate_streams,
+                     const void *const *up_streams, int64_t num_experts, int64_t out_features,
+                     int64_t in_features, int64_t x_rows, int64_t pairs, const float *weight,
+                     float *h, const void *workspace, size_t workspace_bytes,
+                     iqk_stream_t stream);
+
+int iqk_swiglu_rows(const float *gate, const float *up, const float *weight, int64_t rows,
+                    int64_t cols, float *h, iqk_stream_t stream);
+
+/*
  * Copy the device error bits of the last preparation in `workspace` (same
  * in_features / x_rows / pairs) into *flags (IQK_DEVERR_* bits),
  * synchronising the stream. No reference counterpart: the reference's

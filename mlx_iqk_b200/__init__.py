@@ -9,6 +9,8 @@ from . import format  # noqa: F401
 from .format import IqkFormatError
 from .kernels import IqkKernelError, IqkRuntimeError
 from .nn import DECODE_MAT_LIMIT, IqkSwitchLinear, grid_table, member_table, value_table
+from .glu import IqkSwitchGLU
 
 __all__ = ["DECODE_MAT_LIMIT", "IqkFormatError", "IqkKernelError", "IqkRuntimeError",
-           "IqkSwitchLinear", "format", "grid_table", "member_table", "value_table"]
+           "IqkSwitchGLU", "IqkSwitchLinear", "format", "grid_table", "member_table",
+           "value_table"]

@@ -227,6 +227,46 @@ int iqk_gemv_floor_run(int member, const void *const *streams, int64_t num_exper
                                        num_sms_current(), true));
 }
 
+int iqk_gemv_glu_run(int member, const void *const *gate_streams,
+                     const void *const *up_streams, int64_t num_experts, int64_t out_features,
+                     int64_t in_features, int64_t x_rows, int64_t pairs, const float *weight,
+                     float *h, const void *workspace, size_t workspace_bytes,
+                     iqk_stream_t stream) {
+    if (!member_ok(member)) return IQK_ERR_MEMBER;
+    if (!width_ok(in_features)) return IQK_ERR_WIDTH;
+    if (num_experts <= 0 || num_experts > 4096) return IQK_ERR_GEOMETRY;
+    if (out_features <= 0 || out_features % 32) return IQK_ERR_GEOMETRY;
+    if (!gemv_rows_ok(num_experts, out_features, pairs)) return IQK_ERR_GEOMETRY;
+    if (pairs < 0 || x_rows < 0 || pairs > (1 << 24) || x_rows > (1 << 24))
+        return IQK_ERR_GEOMETRY;
+    if (pairs == 0) return IQK_OK;
+    if (!h || !workspace) return IQK_ERR_ARGUMENT;
+    if (!aligned(h, 4) || !aligned(workspace, 256) || (weight && !aligned(weight, 4)))
+        return IQK_ERR_ALIGNMENT;
+    int st = check_streams(member, gate_streams);
+    if (st != IQK_OK) return st;
+    st = check_streams(member, up_streams);
+    if (st != IQK_OK) return st;
+    if (workspace_bytes < gemv_layout(member, in_features, x_rows, pairs).total)
+        return IQK_ERR_WORKSPACE;
+    return cuda_status(launch_gemv_run(member, gate_streams, num_experts, out_features,
+                                       (int)in_features, x_rows, pairs, h, IQK_F32, workspace,
+                                       reinterpret_cast<cudaStream_t>(stream), num_sms_current(),
+                                       false, up_streams, weight));
+}
+
+int iqk_swiglu_rows(const float *gate, const float *up, const float *weight, int64_t rows,
+                    int64_t cols, float *h, iqk_stream_t stream) {
+    if (rows < 0 || rows > ((int64_t)1 << 31) - 1) return IQK_ERR_GEOMETRY;
+    if (cols <= 0 || cols % 4 || cols > (1 << 20)) return IQK_ERR_GEOMETRY;
+    if (rows == 0) return IQK_OK;
+    if (!gate || !up || !h) return IQK_ERR_ARGUMENT;
+    if (!aligned(gate, 16) || !aligned(up, 16) || !aligned(h, 16) || (weight && !aligned(weight, 4)))
+        return IQK_ERR_ALIGNMENT;
+    return cuda_status(launch_rows_swiglu(gate, up, weight, rows, (int)cols, h,
+                                          reinterpret_cast<cudaStream_t>(stream)));
+}
+
 int iqk_gemv(int member, const void *x, int x_dtype, int64_t x_rows,
              const void *const *streams, int64_t num_experts, int64_t out_features,
              int64_t in_features, const int32_t *sel, const int32_t *tok, int64_t pairs,

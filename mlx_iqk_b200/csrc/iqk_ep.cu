@@ -79,7 +79,32 @@ pairs_combine_kernel(const float *__restrict__ y, const int32_t *__restrict__ se
     }
 }
 
+// h[r, c] = silu(g[r, c]) * u[r, c] * (w ? w[r] : 1), float32 rows: the
+// SwitchGLU step of a layer whose gate and up projections have different
+// members (one decode launch serves a same-member pair).
+__global__ void __launch_bounds__(256)
+rows_swiglu_kernel(const float *__restrict__ g, const float *__restrict__ u,
+                   const float *__restrict__ w, int cols, float *__restrict__ h) {
+    const int64_t r = blockIdx.x;
+    const float wr = w ? w[r] : 1.f;
+    const float4 *g4 = reinterpret_cast<const float4 *>(g + r * cols);
+    const float4 *u4 = reinterpret_cast<const float4 *>(u + r * cols);
+    float4 *h4 = reinterpret_cast<float4 *>(h + r * cols);
+    for (int i = threadIdx.x; i < cols / 4; i += blockDim.x) {
+        const float4 a = g4[i], b = u4[i];
+        h4[i] = make_float4(silu(a.x) * b.x * wr, silu(a.y) * b.y * wr, silu(a.z) * b.z * wr,
+                            silu(a.w) * b.w * wr);
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_rows_swiglu(const float *g, const float *u, const float *w, int64_t rows,
+                               int cols, float *h, cudaStream_t stream) {
+    if (rows == 0) return cudaSuccess;
+    rows_swiglu_kernel<<<(unsigned)rows, 256, 0, stream>>>(g, u, w, cols, h);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_pairs_swiglu(const float *g, const float *u, const float *w, int inter,
                                 int n, int64_t num_experts, int64_t pairs, const void *ws,

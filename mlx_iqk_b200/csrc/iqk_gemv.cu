@@ -362,18 +362,24 @@ template <int MEMBER, int N, int ROWS = kItemRows> __host__ __device__ constexpr
 // compute warps take a quarter of every round's k each and their exact
 // partial sums meet in shared memory -- four times the items, so small
 // decode batches still reach every SM.
-template <int MEMBER, bool NARROW> struct Shape {
-    static constexpr int kRows = NARROW ? 16 : kItemRows;     // rows per item
+// GLU (wide items only): a SwitchGLU's gate and up together -- an item is
+// 32 rows of one pair, warps 0-1 on the gate's rows, warps 2-3 on the same
+// rows of up; at item end the up warps hand their results to the gate warps,
+// which store h = silu(gate) * up * router weight.
+template <int MEMBER, bool NARROW, bool GLU = false> struct Shape {
+    static constexpr int kRows = NARROW ? 16 : GLU ? kItemRows / 2 : kItemRows;  // rows per item
     static constexpr int KQ = NARROW ? kConsumers : 1;        // k chunks per round
     static constexpr int kStages = NARROW ? 3 : Geo<MEMBER>::kStages;
-    static constexpr int kRedBytes = NARROW ? 2 * kConsumers * 32 * 16 : 0;
+    static constexpr int kRedBytes = NARROW ? 2 * kConsumers * 32 * 16 : GLU ? 2 * 2 * 8 * 8 : 0;
+    static constexpr int kProj = GLU ? 2 : 1;  // projections whose scale streams fill a slot
 };
 
-template <int MEMBER, int N, bool NARROW> __host__ __device__ constexpr int gemv_smem_bytes() {
+template <int MEMBER, int N, bool NARROW, bool GLU = false>
+__host__ __device__ constexpr int gemv_smem_bytes() {
     using G = Geo<MEMBER>;
-    using SH = Shape<MEMBER, NARROW>;
+    using SH = Shape<MEMBER, NARROW, GLU>;
     return 1024 /* alignment slack */ + SH::kStages * stage_bytes<MEMBER, SH::KQ>() +
-           2 * sslot_bytes<MEMBER, N, SH::kRows>() + 2 * kConsumers * G::kMetaBytes +
+           2 * SH::kProj * sslot_bytes<MEMBER, N, SH::kRows>() + 2 * kConsumers * G::kMetaBytes +
            kMaxTiles * (int)sizeof(TileRef) + (MEMBER == IQK_IQ1_S_R4 ? 4096 : 0) +
            2 * SH::kStages * 8 + 8 * 8 + 16 +
            kPairsPerRound * 192 + SH::kRedBytes;
@@ -381,6 +387,8 @@ template <int MEMBER, int N, bool NARROW> __host__ __device__ constexpr int gemv
 
 struct GemvArgs {
     const void *s[5];
+    const void *s2[5];  // GLU: the up projection's streams
+    const float *rw;    // GLU: router weight per pair, or null (1)
     int out_features;  // experts x out_features <= 2^30 (checked by the C ABI)
     int pairs;
     uint32_t one;      // 1: source of the mul.hi shift multipliers (see below)
@@ -499,12 +507,14 @@ __device__ __forceinline__ double pow2(int k) {
 // the same code words and activation planes, but fold them into an integer
 // accumulator instead of decoding; the folded value reaches y, so no copy
 // or read can be dropped. Only the benchmark's floor entry point uses it.
-template <int MEMBER, int N, bool NARROW, bool FLOOR = false>
+template <int MEMBER, int N, bool NARROW, bool FLOOR = false, bool GLU = false>
 __global__ void __launch_bounds__(kThreads, Geo<MEMBER>::kMinBlocks)
-gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
+gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
+            const __grid_constant__ CUtensorMap qs_map2) {
     extern __shared__ char smem_raw[];
     using G = Geo<MEMBER>;
-    using SH = Shape<MEMBER, NARROW>;
+    using SH = Shape<MEMBER, NARROW, GLU>;
+    static_assert(!(GLU && (NARROW || FLOOR)), "the GLU shape is wide and decodes");
     constexpr int kRows = SH::kRows, KQ = SH::KQ, kStages = SH::kStages;
     using SS = Streams<MEMBER, N, kRows>;
     constexpr int CPW = N / kChunkK;  // 512-weight chunks per row: 8 (n=4096) or 4 (2048)
@@ -518,7 +528,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
 
     char *stages = smem;
     char *sslots = stages + kStages * STB;  // two item scale slots
-    char *metas = sslots + 2 * SSB;
+    char *metas = sslots + 2 * SH::kProj * SSB;  // slot o: projection q at (o * kProj + q) * SSB
     TileRef *tcache = reinterpret_cast<TileRef *>(metas + 2 * kConsumers * G::kMetaBytes);
     char *tail = reinterpret_cast<char *>(tcache + kMaxTiles);
     uint16_t *grid = reinterpret_cast<uint16_t *>(tail);   // IQ1_S_R4
@@ -552,8 +562,8 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
         for (int s = 0; s < 2; ++s) {
             mbar_init(&sfull[s], 1);
             mbar_init(&sempty[s], kConsumers);
-            mbar_init(&rfull[s], kConsumers - 1);
-            mbar_init(&rempty[s], 1);
+            mbar_init(&rfull[s], GLU ? 2 : kConsumers - 1);
+            mbar_init(&rempty[s], GLU ? 2 : 1);
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -597,9 +607,13 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
         int ti = i0 / rblocks, rb = i0 % rblocks;
         int issued = 0, sissued = 0;
         bool ok = true;
-        // this lane's scale stream (lanes 1 .. kCount-1): bytes per row, slot offset
-        const int si = lane >= 1 && lane < SS::kCount ? lane : 0;
-        const int s_rowb = si ? SS::b(si) : 0, s_off = si ? SS::off(si) : 0;
+        // this lane's scale stream (lanes 1 .. kCount-1; GLU: lanes 17 .. for
+        // up's): bytes per row, slot offset
+        const int sproj = GLU && lane >= 16 ? 1 : 0;
+        const int sl = lane - 16 * sproj;
+        const int si = sl >= 1 && sl < SS::kCount ? sl : 0;
+        const int s_rowb = si ? SS::b(si) : 0, s_off = si ? sproj * SSB + SS::off(si) : 0;
+        const void *const *sstreams = sproj ? a.s2 : a.s;
         for (int o = 0; o < n_items && ok; ++o) {
             const TileRef T = tile_of(ti);
             const int r0 = rb * kRows;
@@ -610,16 +624,18 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                 ok = false;
                 break;
             }
-            if (lane == 0) mbar_arrive_expect_tx(&sfull[ss], (uint32_t)(rows_valid * (SS::kSlot / kRows)));
+            if (lane == 0)
+                mbar_arrive_expect_tx(&sfull[ss],
+                                      (uint32_t)(SH::kProj * rows_valid * (SS::kSlot / kRows)));
             __syncwarp();
             if (si)
-                bulk_load(sslots + ss * SSB + s_off,
-                          static_cast<const char *>(a.s[si]) + ((int64_t)T.e * out + r0) * s_rowb,
+                bulk_load(sslots + ss * SH::kProj * SSB + s_off,
+                          static_cast<const char *>(sstreams[si]) + ((int64_t)T.e * out + r0) * s_rowb,
                           (uint32_t)(rows_valid * s_rowb), &sfull[ss]);
             sissued = o + 1;
             // wide: warp w's box is rows 16w.., chunk r; narrow: all warps the
             // item's 16 rows, warp w chunk KQ*r + w
-            const int wrow = T.e * out + r0 + (NARROW ? 0 : 16 * lane);
+            const int wrow = T.e * out + r0 + (NARROW ? 0 : 16 * (GLU ? (lane & 1) : lane));
             const char *xb = xbuf + T.tok0 * xrow;
             for (int r = 0; r < RPI; ++r) {
                 const int j = o * RPI + r;
@@ -633,7 +649,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                 __syncwarp();
                 if (lane < kConsumers) {
                     // weights: one 16-row x kRowChunk-byte box per compute warp
-                    tma_load_2d(st + lane * G::kWBox, &qs_map,
+                    tma_load_2d(st + lane * G::kWBox, GLU && lane >= 2 ? &qs_map2 : &qs_map,
                                 (KQ * r + (NARROW ? lane : 0)) * G::kRowChunk, wrow, &full[slot]);
                 } else if (lane == kConsumers) {
                     // activation digit planes (+ IQ1 block sums) of this round's
@@ -668,7 +684,9 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
 
     // ===================== compute warps
     const int g = lane >> 2, tig = lane & 3;
-    const int rbase = NARROW ? 0 : 16 * wid;  // first item-local row of this warp
+    // first item-local row of this warp (GLU: within its projection)
+    const int rbase = NARROW ? 0 : 16 * (GLU ? (wid & 1) : wid);
+    const int proj = GLU ? (wid >> 1) : 0;  // GLU: 0 gate, 1 up
     const uint32_t meta_u = smem_u32(metas + wid * 2 * G::kMetaBytes);  // two round buffers
     const int side = tig >> 1;  // IQ2_KS, IQ1_S_R4: which 32-weight group of an MMA pair
     // Activation plane of B column g (or -1: a zero block). IQ2_KS and IQ1_S_R4
@@ -798,7 +816,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
         // slower)
         const bool nlive = !NARROW && o + 1 < n_items &&
                            rbase < out - (rb + 1 == rblocks ? 0 : rb + 1) * kRows;
-        const char *sd = sslots + (o & 1) * SSB;
+        const char *sd = sslots + ((o & 1) * SH::kProj + proj) * SSB;
         // the item's scale streams
         if (!mbar_wait(&sfull[o & 1], (o >> 1) & 1)) {
             if (lane == 0) {
@@ -980,7 +998,8 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                 } else if (r + 1 < RPI) {
                     build_meta(sd, chunk_of(r + 1), meta_u + ((r + 1) & 1) * G::kMetaBytes);
                 } else if (nlive && mbar_wait(&sfull[(o + 1) & 1], ((o + 1) >> 1) & 1)) {
-                    build_meta(sslots + ((o + 1) & 1) * SSB, chunk_of(0), meta_u);
+                    build_meta(sslots + (((o + 1) & 1) * SH::kProj + proj) * SSB, chunk_of(0),
+                               meta_u);
                     prebuilt = true;
                 }
             }
@@ -1079,9 +1098,11 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                 yg = (double)half_bits_to_float(dvp[ra]) * Tg;
                 yg8 = (double)half_bits_to_float(dvp[ra + 8]) * Tg8;
             }
+            float vg = 0.f, vg8 = 0.f;
+            const int64_t o0 = (int64_t)T.pair0 * out + r0 + ra;
+            const bool ok8 = r0 + ra + 8 < out;
             if (tig == 0) {
                 const int S = T.sh0;
-                float vg, vg8;
                 if (S == kScaleNonFinite) {
                     vg = vg8 = __int_as_float(0x7fc00000);
                 } else {
@@ -1089,8 +1110,40 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map) {
                     vg = (float)(yg * sc);
                     vg8 = (float)(yg8 * sc);
                 }
-                const int64_t o0 = (int64_t)T.pair0 * out + r0 + ra;
-                const bool ok8 = r0 + ra + 8 < out;
+            }
+            if (GLU) {
+                // up warps hand rows (g, g + 8) of their row pair to the gate
+                // warp of the same rows through a double-buffered exchange
+                // (by item parity); the gate warp stores
+                // h = silu(gate) * up * router weight
+                const int rbuf = o & 1;
+                float2 *xa = reinterpret_cast<float2 *>(red) + (rbuf * 2 + (wid & 1)) * 8;
+                bool gok = true;
+                if (proj == 1) {
+                    if (o >= 2 && !mbar_wait(&rempty[rbuf], ((o >> 1) & 1) ^ 1)) gok = false;
+                    if (gok && tig == 0) xa[g] = make_float2(vg, vg8);
+                    __syncwarp();
+                    if (gok && lane == 0) mbar_arrive(&rfull[rbuf]);
+                } else {
+                    if (!mbar_wait(&rfull[rbuf], (o >> 1) & 1)) gok = false;
+                    if (gok && tig == 0) {
+                        const float2 u = xa[g];
+                        const float w = a.rw ? a.rw[T.pair0] : 1.f;
+                        float *y = static_cast<float *>(a.y);
+                        y[o0] = vg / (1.0f + expf(-vg)) * u.x * w;
+                        if (ok8) y[o0 + 8] = vg8 / (1.0f + expf(-vg8)) * u.y * w;
+                    }
+                    __syncwarp();
+                    if (gok && lane == 0) mbar_arrive(&rempty[rbuf]);
+                }
+                if (!gok) {
+                    if (lane == 0) {
+                        atomicOr(a.err, IQK_DEVERR_TIMEOUT);
+                        atomicExch(abort_flag, 1);
+                    }
+                    break;
+                }
+            } else if (tig == 0) {
                 if (a.y_dtype == IQK_F32) {
                     float *y = static_cast<float *>(a.y);
                     y[o0] = vg;
@@ -1138,34 +1191,40 @@ GemvLayout gemv_layout(int member, int64_t n, int64_t x_rows, int64_t pairs) {
     return L;
 }
 
-using GemvFn = void (*)(GemvArgs, CUtensorMap);
+using GemvFn = void (*)(GemvArgs, CUtensorMap, CUtensorMap);
 
-// The narrow shape exists at in_features 4096 only.
-template <bool FLOOR> static GemvFn gemv_fn_t(int member, int n, bool narrow) {
-#define IQK_FN(M, NN) (narrow ? (GemvFn)gemv_kernel<M, NN, true, FLOOR> \
-                              : (GemvFn)gemv_kernel<M, NN, false, FLOOR>)
+// Kernel variants: the decode, its address floor, and the SwitchGLU pair.
+enum GemvVariant { kVarDecode = 0, kVarFloor = 1, kVarGlu = 2 };
+
+// The narrow shape exists at in_features 4096 only (decode and floor).
+template <bool FLOOR, bool GLU> static GemvFn gemv_fn_t(int member, int n, bool narrow) {
+#define IQK_FN(M, NN) (narrow && !GLU ? (GemvFn)gemv_kernel<M, NN, true, FLOOR, false> \
+                                      : (GemvFn)gemv_kernel<M, NN, false, FLOOR, GLU>)
     if (n == 2048)
-        return member == IQK_IQ2_KS ? (GemvFn)gemv_kernel<IQK_IQ2_KS, 2048, false, FLOOR>
-               : member == IQK_IQ2_K ? (GemvFn)gemv_kernel<IQK_IQ2_K, 2048, false, FLOOR>
-                                     : (GemvFn)gemv_kernel<IQK_IQ1_S_R4, 2048, false, FLOOR>;
+        return member == IQK_IQ2_KS ? (GemvFn)gemv_kernel<IQK_IQ2_KS, 2048, false, FLOOR, GLU>
+               : member == IQK_IQ2_K ? (GemvFn)gemv_kernel<IQK_IQ2_K, 2048, false, FLOOR, GLU>
+                                     : (GemvFn)gemv_kernel<IQK_IQ1_S_R4, 2048, false, FLOOR, GLU>;
     return member == IQK_IQ2_KS ? IQK_FN(IQK_IQ2_KS, 4096)
            : member == IQK_IQ2_K ? IQK_FN(IQK_IQ2_K, 4096) : IQK_FN(IQK_IQ1_S_R4, 4096);
 #undef IQK_FN
 }
-static GemvFn gemv_fn(int member, int n, bool narrow, bool floor) {
-    return floor ? gemv_fn_t<true>(member, n, narrow) : gemv_fn_t<false>(member, n, narrow);
+static GemvFn gemv_fn(int member, int n, bool narrow, int variant) {
+    return variant == kVarFloor ? gemv_fn_t<true, false>(member, n, narrow)
+           : variant == kVarGlu ? gemv_fn_t<false, true>(member, n, false)
+                                : gemv_fn_t<false, false>(member, n, narrow);
 }
 
-int gemv_smem_for(int member, int n, bool narrow) {
-#define IQK_SM(M, NN) (narrow ? gemv_smem_bytes<M, NN, true>() : gemv_smem_bytes<M, NN, false>())
+static int gemv_smem_for(int member, int n, bool narrow, bool glu) {
+#define IQK_SM(M, NN) (glu ? gemv_smem_bytes<M, NN, false, true>()                 \
+                           : narrow ? gemv_smem_bytes<M, NN, true>() : gemv_smem_bytes<M, NN, false>())
     if (n == 2048)
-        return member == IQK_IQ2_KS ? gemv_smem_bytes<IQK_IQ2_KS, 2048, false>()
-               : member == IQK_IQ2_K ? gemv_smem_bytes<IQK_IQ2_K, 2048, false>()
-                                     : gemv_smem_bytes<IQK_IQ1_S_R4, 2048, false>();
+        return member == IQK_IQ2_KS ? IQK_SM(IQK_IQ2_KS, 2048)
+               : member == IQK_IQ2_K ? IQK_SM(IQK_IQ2_K, 2048) : IQK_SM(IQK_IQ1_S_R4, 2048);
     return member == IQK_IQ2_KS ? IQK_SM(IQK_IQ2_KS, 4096)
            : member == IQK_IQ2_K ? IQK_SM(IQK_IQ2_K, 4096) : IQK_SM(IQK_IQ1_S_R4, 4096);
 #undef IQK_SM
 }
+int gemv_smem_for(int member, int n, bool narrow) { return gemv_smem_for(member, n, narrow, false); }
 
 // Launch configuration with programmatic stream serialization (the kernel
 // waits with griddepcontrol.wait before its first global-memory access).
@@ -1245,11 +1304,16 @@ static cudaError_t encode_qs_map(CUtensorMap *map, const void *qs, int64_t rows,
 cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_experts,
                             int64_t out_features, int n, int64_t x_rows, int64_t pairs, void *y,
                             int y_dtype, const void *ws, cudaStream_t stream, int num_sms,
-                            bool floor) {
+                            bool floor, const void *const *up_streams, const float *router_weight) {
+    const int variant = up_streams ? kVarGlu : floor ? kVarFloor : kVarDecode;
     const GemvLayout L = gemv_layout(member, n, x_rows, pairs);
     GemvArgs ga{};
     const RowBytes rb = row_bytes(member, n);
-    for (int i = 0; i < rb.count; ++i) ga.s[i] = streams[i];
+    for (int i = 0; i < rb.count; ++i) {
+        ga.s[i] = streams[i];
+        ga.s2[i] = up_streams ? up_streams[i] : streams[i];
+    }
+    ga.rw = router_weight;
     ga.out_features = (int)out_features;
     ga.pairs = (int)pairs;
     ga.one = 1u;
@@ -1258,35 +1322,43 @@ cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_
     ga.err = reinterpret_cast<int32_t *>(const_cast<char *>(ga.ws) + L.hdr);
     ga.y = y;
     ga.y_dtype = y_dtype;
-    CUtensorMap map;
+    CUtensorMap map, map2;
     const bool iq1 = member == IQK_IQ1_S_R4;
     cudaError_t err = encode_qs_map(&map, streams[0], num_experts * out_features,
                                     iq1 ? n / 8 : n / 4, iq1 ? 64 : 128, !iq1);
     if (err != cudaSuccess) return err;
+    map2 = map;
+    if (up_streams) {
+        err = encode_qs_map(&map2, up_streams[0], num_experts * out_features, iq1 ? n / 8 : n / 4,
+                            iq1 ? 64 : 128, !iq1);
+        if (err != cudaSuccess) return err;
+    }
     // One persistent wave: as many CTAs as fit on every SM at once (shared
     // memory and registers decide; cached per member, width and shape). The
     // shared-memory opt-in is a per-device function attribute: set once.
-    static std::atomic<int> resident[1][3][2][2];
-    static std::atomic<unsigned> attr_done[2][64];
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = -1;
     // The floor variant runs with the decode kernel's grid (its own occupancy
     // could differ), so the two launches issue the same copies from the same
-    // number of CTAs.
+    // number of CTAs; the GLU variant has its own.
+    static std::atomic<int> resident[2][3][2][2];
+    static std::atomic<unsigned> attr_done[3][64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = -1;
+    const bool glu = variant == kVarGlu;
     auto setup = [&](bool narrow, int &per_sm) -> cudaError_t {
-        const int smem = gemv_smem_for(member, n, narrow);
+        const int smem = gemv_smem_for(member, n, narrow, glu);
         const unsigned bit = 1u << ((member * 2 + (n == 4096)) * 2 + (narrow ? 1 : 0));
-        for (int f = 0; f <= (floor ? 1 : 0); ++f) {
-            if (dev < 0 || !(attr_done[f][dev].load() & bit)) {
+        for (int v = 0; v < 3; ++v) {
+            if (v != kVarDecode && v != variant) continue;
+            if (dev < 0 || !(attr_done[v][dev].load() & bit)) {
                 const cudaError_t e = cudaFuncSetAttribute(
-                    gemv_fn(member, n, narrow, f != 0), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                    smem);
+                    gemv_fn(member, n, narrow, v), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                    gemv_smem_for(member, n, narrow, v == kVarGlu));
                 if (e != cudaSuccess) return e;
-                if (dev >= 0) attr_done[f][dev].fetch_or(bit);
+                if (dev >= 0) attr_done[v][dev].fetch_or(bit);
             }
         }
-        const GemvFn fn = gemv_fn(member, n, narrow, false);
-        std::atomic<int> &r = resident[0][member][n == 4096][narrow ? 1 : 0];
+        const GemvFn fn = gemv_fn(member, n, narrow, glu ? kVarGlu : kVarDecode);
+        std::atomic<int> &r = resident[glu][member][n == 4096][narrow ? 1 : 0];
         if (r.load() == 0) {
             int nb = 0;
             const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, kThreads, smem);
@@ -1304,18 +1376,18 @@ cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_
     const int64_t wide_items = pairs * ((out_features + kItemRows - 1) / kItemRows);
     // (At in_features 2048 an item is only four rounds wide already, and a
     // narrow item's single round does not pay for its set-up: measured.)
-    const bool narrow = n == 4096 && wide_items < (int64_t)num_sms * per_sm;
+    const bool narrow = !glu && n == 4096 && wide_items < (int64_t)num_sms * per_sm;
     if (narrow) {
         err = setup(true, per_sm);
         if (err != cudaSuccess) return err;
     }
-    const int64_t rows = narrow ? 16 : kItemRows;
+    const int64_t rows = narrow ? 16 : glu ? kItemRows / 2 : kItemRows;
     const int64_t max_items = pairs * ((out_features + rows - 1) / rows);
     const int64_t cap = (int64_t)num_sms * per_sm;
     int64_t blocks = max_items < cap ? max_items : cap;
     if (blocks < 1) blocks = 1;
-    PdlLaunch pl((unsigned)blocks, kThreads, gemv_smem_for(member, n, narrow), stream);
-    err = cudaLaunchKernelEx(&pl.cfg, gemv_fn(member, n, narrow, floor), ga, map);
+    PdlLaunch pl((unsigned)blocks, kThreads, gemv_smem_for(member, n, narrow, glu), stream);
+    err = cudaLaunchKernelEx(&pl.cfg, gemv_fn(member, n, narrow, variant), ga, map, map2);
     if (err != cudaSuccess) return err;
     return cudaGetLastError();
 }

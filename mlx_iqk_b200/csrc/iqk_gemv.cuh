@@ -37,7 +37,8 @@ cudaError_t launch_gemv_prepare(const void *x, int x_dtype, int64_t x_rows, int 
 cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_experts,
                             int64_t out_features, int n, int64_t x_rows, int64_t pairs, void *y,
                             int y_dtype, const void *ws, cudaStream_t stream, int num_sms,
-                            bool floor = false);
+                            bool floor = false, const void *const *up_streams = nullptr,
+                            const float *router_weight = nullptr);
 cudaError_t launch_pack(int member, const void *wire, int64_t rows, int n,
                         void *const *streams, cudaStream_t stream, int num_sms);
 cudaError_t launch_dequant(int member, const void *const *streams, int64_t num_experts,

@@ -37,6 +37,8 @@ cudaError_t launch_grouped_prepare(const void *x, int x_dtype, int64_t x_rows, i
 cudaError_t launch_pairs_swiglu(const float *g, const float *u, const float *w, int inter,
                                 int n, int64_t num_experts, int64_t pairs, const void *ws,
                                 void *h, cudaStream_t stream);
+cudaError_t launch_rows_swiglu(const float *g, const float *u, const float *w, int64_t rows,
+                               int cols, float *h, cudaStream_t stream);
 cudaError_t launch_pairs_combine(const float *y, const int32_t *sel, int64_t rows, int top_k,
                                  int64_t num_experts, int hidden, void *out, int out_dtype,
                                  cudaStream_t stream);

@@ -109,6 +109,10 @@ def library() -> ctypes.CDLL:
     lib.iqk_gemv_run.restype = i32
     lib.iqk_gemv_floor_run.argtypes = [i32, vp, i64, i64, i64, i64, i64, vp, i32, vp, sz, vp]
     lib.iqk_gemv_floor_run.restype = i32
+    lib.iqk_gemv_glu_run.argtypes = [i32, vp, vp, i64, i64, i64, i64, i64, vp, vp, vp, sz, vp]
+    lib.iqk_gemv_glu_run.restype = i32
+    lib.iqk_swiglu_rows.argtypes = [vp, vp, vp, i64, i64, vp, vp]
+    lib.iqk_swiglu_rows.restype = i32
     lib.iqk_dequant_floor.argtypes = [i32, vp, i64, i64, i64, i64, i64, i32, vp, vp]
     lib.iqk_dequant_floor.restype = i32
     lib.iqk_read_error.argtypes = [vp, i64, i64, i64, ctypes.POINTER(ctypes.c_int32), vp]
@@ -152,7 +156,8 @@ def exported_symbols() -> list[str]:
             "iqk_gemv_static_max_bytes", "iqk_gemv_static", "iqk_gemv_static_read_error",
             "iqk_grouped_prepare_shard",
             "iqk_pairs_swiglu", "iqk_pairs_combine", "iqk_gemv_floor_run",
-            "iqk_dequant_floor", "iqk_grouped_run_range", "iqk_pack"]
+            "iqk_dequant_floor", "iqk_grouped_run_range", "iqk_pack",
+            "iqk_gemv_glu_run", "iqk_swiglu_rows"]
 
 
 def raise_for_status(status: int, what: str) -> None:
@@ -269,6 +274,29 @@ def gemv_run(member: str, streams, num_experts: int, out_features: int, in_featu
         stream_handle(y.device))
     raise_for_status(status, "iqk_gemv_run")
     return y
+
+
+def gemv_glu_run(member: str, gate_streams, up_streams, num_experts: int, out_features: int,
+                 in_features: int, x_rows: int, pairs: int, weight: torch.Tensor | None,
+                 h: torch.Tensor, workspace: torch.Tensor) -> torch.Tensor:
+    """``iqk_gemv_glu_run``: h [pairs, out] float32 = silu(gate) * up * weight."""
+    status = library().iqk_gemv_glu_run(
+        MEMBER_IDS[member], ptr_array(gate_streams), ptr_array(up_streams), num_experts,
+        out_features, in_features, x_rows, pairs,
+        None if weight is None else weight.data_ptr(), h.data_ptr(), workspace.data_ptr(),
+        workspace.numel(), stream_handle(h.device))
+    raise_for_status(status, "iqk_gemv_glu_run")
+    return h
+
+
+def swiglu_rows(g: torch.Tensor, u: torch.Tensor, weight: torch.Tensor | None,
+                h: torch.Tensor) -> torch.Tensor:
+    """``iqk_swiglu_rows``: h = silu(g) * u * weight[row], float32 [rows, cols]."""
+    status = library().iqk_swiglu_rows(
+        g.data_ptr(), u.data_ptr(), None if weight is None else weight.data_ptr(), g.shape[0],
+        g.shape[1], h.data_ptr(), stream_handle(h.device))
+    raise_for_status(status, "iqk_swiglu_rows")
+    return h
 
 
 def gemv_floor_run(member: str, streams, num_experts: int, out_features: int,
