@@ -855,8 +855,12 @@ def run_b200(args) -> None:
         dequant[MEMBER] = dequant_leg(tm, K, mods[0], hbm)
         torch.cuda.empty_cache()
 
+    # the same decode steps through the fused layer module, device-timed
+    layer = glu_layer(torch, dev, mods)
+    gcells = [GluCell(torch, layer, c, gen, dev) for c in cells]
+    switchglu = {f"B={g.B}": tm.cell_rate(g, max(50, Kst // 2)) for g in gcells}
     prefill = run_prefill(args, torch, K, dev, world, rank, tm, peaks)
-    e2e = run_e2e(args, torch, dev, mods, cells, tm)
+    e2e = run_e2e(args, torch, dev, layer, cells, tm)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -871,7 +875,7 @@ def run_b200(args) -> None:
             "dtype": "s8 x s8 -> s32 MMA, f64 epilogue (bf16 activations)",
             "data": "synthetic: random IQ2_KS streams (serving scales), x~N(0,1) bf16",
             "config": config(args, batches),
-            "sweep": sweep, "roofline": roofline, "floors": floors,
+            "sweep": sweep, "switchglu_sweep": switchglu, "roofline": roofline, "floors": floors,
             "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": launches_per_step * Kst,
             "clocks": clk.summary(),
@@ -951,31 +955,55 @@ def run_prefill(args, torch, K, dev, world, rank, tm, peaks) -> dict | None:
     return out
 
 
-def run_e2e(args, torch, dev, mods, cells, tm) -> dict:
-    """The headline step through the public module API with host buffers.
-    Every step copies its inputs from pinned host memory and its results
-    back; the copies run on two side streams (double-buffered device inputs),
-    so step i+1's inputs upload and step i's results download while step i+1
+def glu_layer(torch, dev, mods):
+    """The headline layer's projections as one IqkSwitchGLU (shared streams)."""
+    from mlx_iqk_b200 import IqkSwitchGLU
+    layer = IqkSwitchGLU((MEMBER, MEMBER, MEMBER), E, GATE_UP[1], GATE_UP[0], device=dev)
+    layer.gate, layer.up, layer.down = mods
+    return layer
+
+
+class GluCell:
+    """One decode step of the whole SwitchGLU layer through the public module
+    (IqkSwitchGLU: gate and up in one launch, SiLU * up * router weight, down,
+    the router-weighted top-k sum), on a DecodeCell's rotating selections."""
+
+    def __init__(self, torch, layer, cell, gen, dev):
+        self.layer, self.cell, self.B = layer, cell, cell.B
+        self.scores = torch.softmax(torch.randn((cell.pool, cell.B, TOP_K), generator=gen,
+                                                device=dev), dim=-1)
+
+    def step(self, s: int) -> None:
+        p = s % self.cell.pool
+        self.layer(self.cell.xs[p], self.cell.sels[p], self.scores[p])
+
+    def bytes(self, s: int) -> int:
+        return self.cell.bytes(s)
+
+
+def run_e2e(args, torch, dev, layer, cells, tm) -> dict:
+    """The headline step through the public API with host buffers: one
+    IqkSwitchGLU call per batch size (the layer's gate, up, down and the
+    router-weighted sum). Every step copies its inputs (activations, routing
+    ids, router weights) from pinned host memory and the layer output back;
+    the copies run on two side streams (double-buffered device inputs), so
+    step i+1's inputs upload and step i's output downloads while step i+1
     computes -- the pipelining a server does. The timed region runs from the
     first upload to the last download."""
-    gate, up, down = mods
     stream = torch.cuda.current_stream(dev)
     ne = min(args.steps, 100)
     host, dbuf = [], []
     for c in cells:
         B = c.B
         host.append({
-            "x": torch.randn((ne, B, 1, 1, GATE_UP[1])).to(torch.bfloat16).pin_memory(),
-            "xd": torch.randn((ne, B, TOP_K, 1, DOWN[1])).to(torch.bfloat16).pin_memory(),
+            "x": torch.randn((ne, B, GATE_UP[1])).to(torch.bfloat16).pin_memory(),
             # int32 routing indices, as the reference's router emits 32-bit ids
             "idx": torch.from_numpy(c.sels_np[np.arange(ne) % c.pool].astype(np.int32)).pin_memory(),
-            "yg": torch.empty((ne, B, TOP_K, 1, GATE_UP[0])).pin_memory(),
-            "yu": torch.empty((ne, B, TOP_K, 1, GATE_UP[0])).pin_memory(),
-            "yd": torch.empty((ne, B, TOP_K, 1, DOWN[0])).pin_memory()})
-        dbuf.append([{"dx": torch.empty((B, 1, 1, GATE_UP[1]), device=dev, dtype=torch.bfloat16),
-                      "dxd": torch.empty((B, TOP_K, 1, DOWN[1]), device=dev, dtype=torch.bfloat16),
-                      "didx": torch.empty((B, TOP_K), device=dev, dtype=torch.int32)}
-                     for _ in range(2)])
+            "w": torch.softmax(torch.randn((ne, B, TOP_K)), dim=-1).pin_memory(),
+            "y": torch.empty((ne, B, DOWN[0])).pin_memory()})
+        dbuf.append([{"dx": torch.empty((B, GATE_UP[1]), device=dev, dtype=torch.bfloat16),
+                      "didx": torch.empty((B, TOP_K), device=dev, dtype=torch.int32),
+                      "dw": torch.empty((B, TOP_K), device=dev)} for _ in range(2)])
     up_s, down_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     in_ev = [torch.cuda.Event() for _ in range(2)]    # inputs of buffer set b landed
     free_ev = [torch.cuda.Event() for _ in range(2)]  # buffer set b's step computed
@@ -988,8 +1016,8 @@ def run_e2e(args, torch, dev, mods, cells, tm) -> dict:
                 up_s.wait_event(free_ev[b])
             for h, d in zip(host, dbuf):
                 d[b]["dx"].copy_(h["x"][i], non_blocking=True)
-                d[b]["dxd"].copy_(h["xd"][i], non_blocking=True)
                 d[b]["didx"].copy_(h["idx"][i], non_blocking=True)
+                d[b]["dw"].copy_(h["w"][i], non_blocking=True)
             in_ev[b].record(up_s)
 
     def e2e_run(n: int):
@@ -1000,20 +1028,14 @@ def run_e2e(args, torch, dev, mods, cells, tm) -> dict:
             if i + 1 < n:
                 upload(i + 1)
             stream.wait_event(in_ev[b])
-            outs = []
-            for d in dbuf:
-                outs.append((gate(d[b]["dx"], d[b]["didx"]), up(d[b]["dx"], d[b]["didx"]),
-                             down(d[b]["dxd"], d[b]["didx"])))
+            outs = [layer(d[b]["dx"], d[b]["didx"], d[b]["dw"]) for d in dbuf]
             free_ev[b].record(stream)
             out_ev.record(stream)
             with torch.cuda.stream(down_s):
                 down_s.wait_event(out_ev)
-                for h, (yg, yu, yd) in zip(host, outs):
-                    for t in (yg, yu, yd):
-                        t.record_stream(down_s)
-                    h["yg"][i].copy_(yg, non_blocking=True)
-                    h["yu"][i].copy_(yu, non_blocking=True)
-                    h["yd"][i].copy_(yd, non_blocking=True)
+                for h, y in zip(host, outs):
+                    y.record_stream(down_s)
+                    h["y"][i].copy_(y, non_blocking=True)
         stream.wait_stream(down_s)
         stream.wait_stream(up_s)
 
@@ -1021,13 +1043,14 @@ def run_e2e(args, torch, dev, mods, cells, tm) -> dict:
     torch.cuda.synchronize()
     ems = tm.timed(_Eager(lambda: e2e_run(ne)))
     e_bytes = sum(c.bytes(i) for c in cells for i in range(ne))
-    h2d = sum(c.B * GATE_UP[1] * 2 + c.B * TOP_K * DOWN[1] * 2 + c.B * TOP_K * 4 for c in cells)
-    d2h = sum(c.B * TOP_K * (2 * GATE_UP[0] + DOWN[0]) * 4 for c in cells)
+    h2d = sum(c.B * GATE_UP[1] * 2 + c.B * TOP_K * 4 + c.B * TOP_K * 4 for c in cells)
+    d2h = sum(c.B * DOWN[0] * 4 for c in cells)
     return {"value": round(tm.world * e_bytes / (ems * 1e-3) / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": round(ems / ne, 4), "steps": ne,
-            "path": "IqkSwitchLinear.__call__ (gate, up, down) per batch size, pinned host "
-                    "in/out; copies on two side streams overlapped with the next step"}
+            "path": "IqkSwitchGLU.__call__ (gate+up in one launch, SiLU*up*router weight, "
+                    "down, top-k sum) per batch size, pinned host in/out; copies on two side "
+                    "streams overlapped with the next step"}
 
 
 def main() -> None:

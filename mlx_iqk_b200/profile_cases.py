@@ -98,7 +98,7 @@ def timed(fn, reps: int, graph: bool = False) -> float:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=("gemv", "grouped", "dequant", "layer"))
+    ap.add_argument("case", choices=("gemv", "grouped", "dequant", "layer", "step"))
     ap.add_argument("--member", default="iq2_ks")
     ap.add_argument("--batch", type=int, default=8, help="gemv: tokens (top-6 each)")
     ap.add_argument("--tokens", type=int, default=2048, help="grouped: tokens (top-6 each)")
@@ -136,6 +136,34 @@ def main() -> None:
         print(json.dumps({"case": "layer", "experts": E, "tokens": T, "pairs": P,
                           "us": round(ms * 1e3, 2), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
                           "tokens_per_s": round(T / (ms * 1e-3), 1)}))
+        return
+    if args.case == "step":
+        # one SwitchGLU decode step (gate, up, SiLU * up * weight, down, top-k
+        # sum) through IqkSwitchGLU, routings rotated so weights leave L2
+        from .glu import IqkSwitchGLU
+        B, m = args.batch, args.member
+        layer = IqkSwitchGLU((m, m, m), E, 4096, 2048, device=dev)
+        for mm in (layer.gate, layer.up, layer.down):
+            mm.load_streams(random_streams(m, E, mm.out_features, mm.in_features, dev, gen))
+        R = max(1, args.rotate)
+        xs = torch.randn((R, B, 4096), generator=gen, device=dev).to(torch.bfloat16)
+        sels = torch.stack([torch.stack([torch.randperm(E, generator=gen, device=dev)[:6]
+                                         for _ in range(B)]) for _ in range(R)])
+        ws_ = torch.softmax(torch.randn((R, B, 6), generator=gen, device=dev), dim=-1)
+        calls = {"i": 0}
+
+        def one():
+            i = calls["i"] % R
+            calls["i"] += 1
+            layer(xs[i], sels[i], ws_[i])
+
+        ms = timed(one, args.reps, args.graph)
+        distinct = sum(len(set(sels[i].reshape(-1).tolist())) for i in range(R)) / R
+        rbm = ROW_BYTES[m]
+        nbytes = int(distinct * (2 * 2048 * rbm(4096) + 4096 * rbm(2048)))
+        print(json.dumps({"case": "step", "member": m, "batch": B, "distinct_experts": distinct,
+                          "us": round(ms * 1e3, 2), "bytes": nbytes,
+                          "GBps": round(nbytes / (ms * 1e-3) / 1e9, 1)}))
         return
     mod = random_module(args.member, E, out, n, dev, gen)
     rb = ROW_BYTES[args.member](n)
