@@ -581,19 +581,28 @@ def measure_ep_prefill(torch, K, dev, world, rank, barrier, max_over_ranks, step
     rms = ref.pow(2).mean(dim=1, keepdim=True).sqrt()
     per = float(((got - ref).abs() / torch.maximum(ref.abs(), rms)).max())
     run = (lambda: layer(x, idx, w))
-    graph = None
-    if layer.capturable:
-        graph = torch.cuda.CUDAGraph()
-        s = torch.cuda.Stream(dev)
-        s.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(s):
-            run()
-            torch.cuda.synchronize()
-            with torch.cuda.graph(graph, stream=s):
-                for _ in range(steps):
-                    run()
-        torch.cuda.current_stream(dev).wait_stream(s)
-        graph.replay()
+    graph, capture_error = None, None
+    if layer.capturable and not os.environ.get("IQK_EP_EAGER"):
+        # every rank captures (collectives included) or none does
+        try:
+            graph = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream(dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s):
+                run()
+                torch.cuda.synchronize()
+                with torch.cuda.graph(graph, stream=s):
+                    for _ in range(steps):
+                        run()
+            torch.cuda.current_stream(dev).wait_stream(s)
+        except Exception as exc:  # noqa: BLE001 - time eagerly instead
+            graph, capture_error = None, repr(exc)[:200]
+        ok = max_over_ranks(0.0 if graph is not None else 1.0) == 0.0
+        if not ok:
+            graph = None
+        barrier()
+        if graph is not None:
+            graph.replay()
         torch.cuda.synchronize()
     stream = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -614,6 +623,7 @@ def measure_ep_prefill(torch, K, dev, world, rank, barrier, max_over_ranks, step
     check = {"max_rel_err": max_over_ranks(err), "per_output_err": max_over_ranks(per),
              "tokens_checked_per_rank": T, "against": "one-GPU grouped-GEMM layer over all "
              "256 experts on the same tokens (float32 out)"}
+    layer.timing = {"graph": graph is not None, "capture_error": capture_error}
     return ms, check, phases, layer
 
 
@@ -901,14 +911,15 @@ def run_prefill(args, torch, K, dev, world, rank, tm, peaks) -> dict | None:
     ep = {"value": round(PREFILL_TOKENS / (ep_ms * 1e-3), 1), "unit": "tokens/s",
           "ms_per_step": round(ep_ms, 4), "ep_check": check, "phases": phases,
           "path": "ExpertParallelMoE.forward (all-to-all dispatch, SwitchGLU, combine)",
-          "graph": bool(layer.capturable)}
+          **layer.timing}
+    ep_timing = layer.timing
     del layer
     if world > 1:
         return {"metric": "prefill tokens/s (config 5 layer, expert-parallel)",
                 "value": ep["value"], "unit": "tokens/s", "ms_per_step": ep["ms_per_step"],
                 "tokens": PREFILL_TOKENS, "scaling": "strong", "ep_check": check,
-                "phases": phases, "parallelism": f"ep{world}: {E // world} experts/rank, "
-                "NCCL all_to_all dispatch and combine"}
+                "phases": phases, **ep_timing, "parallelism": f"ep{world}: {E // world} "
+                "experts/rank, NCCL all_to_all dispatch and combine"}
     x, idx, w = prefill_inputs(torch, dev)
     pl = PrefillLayer(torch, K, dev, full, x, idx, w)
     pl.step()
