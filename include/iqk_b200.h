@@ -84,6 +84,16 @@ int iqk_abi_version(void);
 int iqk_check_device(void);
 
 /*
+ * Failure-detection check of the kernels' bounded waits: one warp waits on a
+ * shared-memory mbarrier that nothing arrives on, with the same bounded-wait
+ * code the decode kernels use and a limit of limit_ns (at most 2 s), then
+ * ORs IQK_DEVERR_TIMEOUT into the device word *flags (caller-owned, zeroed
+ * by the caller). The kernel returns normally, so the context stays usable.
+ * No reference counterpart: the reference's kernels have no bounded waits.
+ */
+int iqk_check_bounded_wait(int64_t limit_ns, int32_t *flags, iqk_stream_t stream);
+
+/*
  * On-device relayout of ik wire rows into the streams above: wire is
  * [rows, ggml row bytes] (IQ2_KS 2 + 70*n/256, IQ2_K 76*n/256, IQ1_S_R4
  * 2 + 6*n/32 -- for IQ1_S_R4 rows is a multiple of 4, the wire's row groups);

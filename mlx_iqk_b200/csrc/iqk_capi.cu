@@ -71,6 +71,14 @@ const char *iqk_status_string(int status) {
 
 int iqk_abi_version(void) { return 1; }
 
+int iqk_check_bounded_wait(int64_t limit_ns, int32_t *flags, iqk_stream_t stream) {
+    if (limit_ns < 0 || limit_ns > 2000000000LL) return IQK_ERR_ARGUMENT;
+    if (!flags) return IQK_ERR_ARGUMENT;
+    if (!aligned(flags, 4)) return IQK_ERR_ALIGNMENT;
+    return cuda_status(launch_bounded_wait_check(limit_ns, flags,
+                                                 reinterpret_cast<cudaStream_t>(stream)));
+}
+
 int iqk_check_device(void) {
     int dev = 0, major = 0, minor = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return cuda_status(cudaErrorNoDevice);

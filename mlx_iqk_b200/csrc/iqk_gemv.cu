@@ -476,12 +476,29 @@ __device__ __forceinline__ unsigned long long global_ns() {
     return t;
 }
 // Wait for a phase with a wall-clock bound; false means it timed out.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = global_ns();
     while (!mbar_try_wait(bar, parity))
-        if (global_ns() - t0 > kWaitLimitNs) return false;
+        if (global_ns() - t0 > limit_ns) return false;
     return true;
+}
+
+// The expiry path of the bounded wait above, on demand: one warp waits on a
+// shared-memory mbarrier that nothing ever arrives on, with the given limit,
+// and records IQK_DEVERR_TIMEOUT when the wait gives up. No copy is in
+// flight and nothing else waits, so the kernel simply returns.
+__global__ void __launch_bounds__(32) bounded_wait_check_kernel(unsigned long long limit_ns,
+                                                              int32_t *flags) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    __syncwarp();
+    const bool ok = mbar_wait(&bar, 0, limit_ns);
+    if (!ok && threadIdx.x == 0) atomicOr(flags, IQK_DEVERR_TIMEOUT);
 }
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
                                             uint64_t *bar) {
@@ -1171,6 +1188,11 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
 
 
 // ------------------------------------------------------------------- host
+
+cudaError_t launch_bounded_wait_check(int64_t limit_ns, int32_t *flags, cudaStream_t stream) {
+    bounded_wait_check_kernel<<<1, 32, 0, stream>>>((unsigned long long)limit_ns, flags);
+    return cudaGetLastError();
+}
 
 GemvLayout gemv_layout(int member, int64_t n, int64_t x_rows, int64_t pairs) {
     GemvLayout L{};

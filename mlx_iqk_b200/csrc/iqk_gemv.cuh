@@ -39,6 +39,7 @@ cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_
                             int y_dtype, const void *ws, cudaStream_t stream, int num_sms,
                             bool floor = false, const void *const *up_streams = nullptr,
                             const float *router_weight = nullptr);
+cudaError_t launch_bounded_wait_check(int64_t limit_ns, int32_t *flags, cudaStream_t stream);
 cudaError_t launch_pack(int member, const void *wire, int64_t rows, int n,
                         void *const *streams, cudaStream_t stream, int num_sms);
 cudaError_t launch_dequant(int member, const void *const *streams, int64_t num_experts,

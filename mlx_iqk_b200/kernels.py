@@ -34,7 +34,7 @@ _STATUS_NAMES = {
     1: "IQK_ERR_MEMBER", 2: "IQK_ERR_WIDTH", 3: "IQK_ERR_GEOMETRY", 4: "IQK_ERR_ARGUMENT",
     5: "IQK_ERR_ALIGNMENT", 6: "IQK_ERR_WORKSPACE", 7: "IQK_ERR_CUDA", 8: "IQK_ERR_DEVICE",
 }
-DEVERR_EXPERT, DEVERR_TOKEN, DEVERR_NONFINITE = 1, 2, 4
+DEVERR_EXPERT, DEVERR_TOKEN, DEVERR_NONFINITE, DEVERR_TIMEOUT = 1, 2, 4, 8
 DTYPE_IDS = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 
 
@@ -94,6 +94,8 @@ def library() -> ctypes.CDLL:
     lib.iqk_status_string.restype = ctypes.c_char_p
     lib.iqk_abi_version.restype = i32
     lib.iqk_check_device.restype = i32
+    lib.iqk_check_bounded_wait.argtypes = [i64, vp, vp]
+    lib.iqk_check_bounded_wait.restype = i32
     lib.iqk_dequant.argtypes = [i32, vp, i64, i64, i64, i64, i64, i32, vp, vp]
     lib.iqk_dequant.restype = i32
     lib.iqk_pack.argtypes = [i32, vp, i64, i64, vp, vp]
@@ -157,7 +159,17 @@ def exported_symbols() -> list[str]:
             "iqk_grouped_prepare_shard",
             "iqk_pairs_swiglu", "iqk_pairs_combine", "iqk_gemv_floor_run",
             "iqk_dequant_floor", "iqk_grouped_run_range", "iqk_pack",
-            "iqk_gemv_glu_run", "iqk_swiglu_rows"]
+            "iqk_gemv_glu_run", "iqk_swiglu_rows", "iqk_check_bounded_wait"]
+
+
+def check_bounded_wait(limit_ns: int, device: torch.device) -> int:
+    """``iqk_check_bounded_wait``: the device error bits a wait that nothing
+    satisfies leaves after ``limit_ns`` (IQK_DEVERR_TIMEOUT expected)."""
+    flags = torch.zeros(1, dtype=torch.int32, device=device)
+    raise_for_status(library().iqk_check_bounded_wait(limit_ns, flags.data_ptr(),
+                                                      stream_handle(device)),
+                     "iqk_check_bounded_wait")
+    return int(flags.item())
 
 
 def raise_for_status(status: int, what: str) -> None:

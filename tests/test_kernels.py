@@ -295,3 +295,19 @@ def test_full_geometry_decode_sampled(cuda):
             w = oracle.decode(member, st, n)
             want = w.astype(np.float64) @ xs[t]
             assert rel_err(got[t, k], want) < GEMV_TOL, (t, k)
+
+
+def test_an_expired_bounded_wait_reports_and_the_context_survives(cuda):
+    """A wait that nothing satisfies gives up after its limit with
+    IQK_DEVERR_TIMEOUT (the same bounded-wait code the decode kernels use),
+    and the next kernels in the same context run normally."""
+    import time
+    t0 = time.perf_counter()
+    assert K.check_bounded_wait(5_000_000, cuda) == K.DEVERR_TIMEOUT  # 5 ms limit
+    assert time.perf_counter() - t0 < 5.0
+    n = 2048
+    mod, ref, _ = make_module("iq2_ks", n, seed=8)
+    x = torch.randn(1, 1, 1, n, device=cuda)
+    y = mod.gemv(x, torch.tensor([[3]], device=cuda)).cpu().numpy().reshape(-1)
+    want = ref[3].astype(np.float64) @ x.double().cpu().numpy().reshape(-1)
+    assert rel_err(y, want) < GEMV_TOL
