@@ -619,11 +619,12 @@ def measure_ep_prefill(torch, K, dev, world, rank, barrier, max_over_ranks, step
     ms = max_over_ranks(e0.elapsed_time(e1) / steps)
     layer.check()
     phases = layer.profile_phases(x, idx, w) if hasattr(layer, "profile_phases") else None
-    del graph
+    graphed = graph is not None
+    del graph  # a graph holding NCCL calls goes before the process group does
     check = {"max_rel_err": max_over_ranks(err), "per_output_err": max_over_ranks(per),
              "tokens_checked_per_rank": T, "against": "one-GPU grouped-GEMM layer over all "
              "256 experts on the same tokens (float32 out)"}
-    layer.timing = {"graph": graph is not None, "capture_error": capture_error}
+    layer.timing = {"graph": graphed, "capture_error": capture_error}
     return ms, check, phases, layer
 
 
