@@ -214,6 +214,7 @@ class ExpertParallelMoE:
         idx = torch.where(bad, torch.full_like(idx, -1), idx)
         self.last_stats = {"capacity": C, "rows_exchanged": G * C, "slots": G * C * k}
         if G == 1:
+            mark("experts")
             return self.local_experts_forward(x.to(torch.bfloat16), idx, w.contiguous())
         if C == 0:
             return torch.zeros((T, H), dtype=torch.float32, device=dev)
@@ -262,6 +263,8 @@ class ExpertParallelMoE:
         max over ranks (collective: every rank calls it)."""
         if self.device.type != "cuda":
             return None
+        self._forward(x, indices, weights, None)  # warm: workspaces, first-call set-up
+        torch.cuda.synchronize(self.device)
         marks = []
 
         def mark(name):
