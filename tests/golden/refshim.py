@@ -56,6 +56,7 @@ def load():
     codec = mods[2]
     codec.library_path = lambda: REF_LIBS / "libiqk_iq2.so"
     codec.iq1sr4_library_path = lambda: REF_LIBS / "libiqk_iq1sr4.so"
+    codec.dense_library_path = lambda: REF_LIBS / "libiqk_dense.so"
     if str(REF / "tests") not in sys.path:
         sys.path.insert(0, str(REF / "tests"))
     import wirepack  # the reference's independent block packers
