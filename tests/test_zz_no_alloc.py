@@ -25,12 +25,15 @@ def test_static_scratch_limit_is_stated_and_enforced_on_the_host():
     # 80 rows at in_features 4096 need more than 1 MiB: refused before any
     # device call, so this needs no GPU.
     rows = 80
-    assert K.gemv_workspace_bytes("iq2_ks", 4096, rows, rows) > SCRATCH_BYTES
+    assert K.gemv_workspace_min_bytes("iq2_ks", 4096, rows, rows) > SCRATCH_BYTES
     fake = (torch.zeros(1, dtype=torch.int64),) * 5
     status = lib.iqk_gemv_static(0, 16, 2, rows, K.ptr_array(fake), 8, 32, 4096, 16, None,
                                  rows, 16, 0, None)
     assert status == 6  # IQK_ERR_WORKSPACE
-    assert K.gemv_workspace_bytes("iq2_ks", 4096, 64, 512) <= SCRATCH_BYTES
+    # the static entry needs the smallest accepted workspace (no split slots)
+    assert K.gemv_workspace_min_bytes("iq2_ks", 4096, 64, 512) <= SCRATCH_BYTES
+    assert (K.gemv_workspace_min_bytes("iq2_ks", 4096, 64, 512)
+            < K.gemv_workspace_bytes("iq2_ks", 4096, 64, 512))
 
 
 def _case(member, n, tokens, top_k, paired, seed, experts=16, out=64):
@@ -92,8 +95,8 @@ def test_static_gemv_at_the_largest_geometry_that_fits(cuda, n, x_rows, pairs):
     """The documented limit: scratch use within a few percent of the array,
     explicit activation rows, equal to iqk_gemv bit for bit."""
     member, experts, out = "iq2_ks", 16, 64
-    assert K.gemv_workspace_bytes(member, n, x_rows, pairs) > 0.85 * SCRATCH_BYTES
-    assert K.gemv_workspace_bytes(member, n, x_rows, pairs) <= SCRATCH_BYTES
+    assert K.gemv_workspace_min_bytes(member, n, x_rows, pairs) > 0.85 * SCRATCH_BYTES
+    assert K.gemv_workspace_min_bytes(member, n, x_rows, pairs) <= SCRATCH_BYTES
     mod, _, _ = make_module(member, n, seed=77 + n, experts=experts, out_features=out)
     g = torch.Generator(device="cuda").manual_seed(n)
     x = torch.randn((x_rows, n), generator=g, device="cuda").to(torch.bfloat16)
