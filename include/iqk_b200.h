@@ -36,11 +36,16 @@ extern "C" {
 /* Same object as cudaStream_t; NULL is the legacy default stream. */
 typedef struct CUstream_st *iqk_stream_t;
 
-/* Members (src/mlx_iqk/format.py:116 MEMBERS). */
+/* Members (src/mlx_iqk/format.py:116 MEMBERS) and the dense members
+ * (format.py:120 DENSE_MEMBERS), which only the iqk_dense_* entries take. */
 enum {
     IQK_IQ2_KS = 0,
     IQK_IQ2_K = 1,
-    IQK_IQ1_S_R4 = 2
+    IQK_IQ1_S_R4 = 2,
+    IQK_IQ4_KS = 3,
+    IQK_IQ4_K = 4,
+    IQK_IQ5_K = 5,
+    IQK_IQ6_K = 6
 };
 
 /* Element types of activations and outputs. */
@@ -56,8 +61,8 @@ enum {
  * src/mlx_iqk/kernels.py:86, src/mlx_iqk/nn.py:97. */
 enum {
     IQK_OK = 0,
-    IQK_ERR_MEMBER = 1,      /* member not one of the three */
-    IQK_ERR_WIDTH = 2,       /* in_features not a sized width (2048, 4096) */
+    IQK_ERR_MEMBER = 1,      /* member not one an entry point takes */
+    IQK_ERR_WIDTH = 2,       /* in_features not a sized width (2048, 4096; dense 1024-8192) */
     IQK_ERR_GEOMETRY = 3,    /* out_features / experts / row range / pairs */
     IQK_ERR_ARGUMENT = 4,    /* null pointer, bad dtype, negative count */
     IQK_ERR_ALIGNMENT = 5,   /* a pointer lacks the alignment a kernel needs */
@@ -137,10 +142,18 @@ int iqk_dequant_floor(int member, const void *const *streams, int64_t num_expert
 
 /*
  * Workspace bytes iqk_gemv needs for this member, width, activation-row
- * count and pair count (routing tables plus the prepared activations).
+ * count and pair count (routing tables plus the prepared activations), with
+ * the split slots at the end: with them a wide decode grid divides its work
+ * by rounds and cuts an item between two CTAs where that evens out the load
+ * (IQ2_KS and IQ1_S_R4, whose sums are exact: the output is the same bit for
+ * bit). iqk_gemv_workspace_min_bytes is the smallest workspace the GEMV
+ * entries accept: the same minus the slots, dividing whole items. Prepare and
+ * run must be given the same workspace size.
  */
 size_t iqk_gemv_workspace_bytes(int member, int64_t in_features, int64_t x_rows,
                                 int64_t pairs);
+size_t iqk_gemv_workspace_min_bytes(int member, int64_t in_features, int64_t x_rows,
+                                    int64_t pairs);
 
 /*
  * Fused dequant + GEMV over token-expert pairs:
@@ -370,6 +383,41 @@ int iqk_gemv_static(int member, const void *x, int x_dtype, int64_t x_rows,
 
 int iqk_gemv_static_read_error(int64_t in_features, int64_t x_rows, int64_t pairs,
                                int32_t *flags, iqk_stream_t stream);
+
+/*
+ * Dense members: one [out_features, in_features] matrix of IQ4_KS, IQ4_K,
+ * IQ5_K or IQ6_K rows, streams in the reference's dense component order
+ * (src/mlx_iqk/format.py:898-915):
+ *
+ *   IQK_IQ4_KS {qs u32[o,n/8], scl u8[o,n/32], dv f32[o]}
+ *   IQK_IQ4_K  {qs u32[o,n/8], scl u8[o,n/32], sch u8[o,n/64], sex u8[o,n/128],
+ *               dv f16[o,n/256]}
+ *   IQK_IQ5_K  {qs u32[o,n/8], qh u32[o,n/32], scl u8[o,n/32], sch u8[o,n/64],
+ *               sex u8[o,n/128], dv f16[o,n/256]}
+ *   IQK_IQ6_K  {qs u32[o,n/8], qh u32[o,n/16], scl u8[o,n/16], sex u8[o,n/128],
+ *               dv f16[o,n/256]}
+ *
+ * in_features is 1024, 2048, 4096 or 8192 (src/mlx_iqk/dense_kernels.py:56).
+ * qs must be 16-byte aligned, qh 8-byte aligned.
+ *
+ * iqk_dense_dequant: rows [row_start, row_start + rows) into dst[rows, n] in
+ * f32, f16 or bf16, bit for bit the reference decode rounded once
+ * (src/mlx_iqk/dense.py:145-189, dense_dequantized / _range; the reference
+ * stores fp16).
+ *
+ * iqk_dense_gemv: y[tokens, out] = x[tokens, n] W^T for f16 x (the
+ * reference's call seam casts to fp16, src/mlx_iqk/dense.py:107-112), y in
+ * f16 (the reference's output) or f32; out_features a multiple of 16
+ * (src/mlx_iqk/dense_kernels.py:70-81). Replaces dense_gemv
+ * (src/mlx_iqk/dense.py:116-142): each sub-block's scale is applied to its
+ * own float32 partial sum.
+ */
+int iqk_dense_dequant(int member, const void *const *streams, int64_t out_features,
+                      int64_t in_features, int64_t row_start, int64_t rows, int out_dtype,
+                      void *dst, iqk_stream_t stream);
+int iqk_dense_gemv(int member, const void *x, int64_t tokens, const void *const *streams,
+                   int64_t out_features, int64_t in_features, void *y, int y_dtype,
+                   iqk_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -15,8 +15,8 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
-SOURCES = ["iqk_capi.cu", "iqk_dequant.cu", "iqk_ep.cu", "iqk_gemv.cu", "iqk_grouped.cu",
-           "iqk_pack.cu", "iqk_static.cu"]
+SOURCES = ["iqk_capi.cu", "iqk_dense.cu", "iqk_dequant.cu", "iqk_ep.cu", "iqk_gemv.cu",
+           "iqk_grouped.cu", "iqk_pack.cu", "iqk_static.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-shared",
          "--expt-relaxed-constexpr", "-diag-suppress", "177"]
@@ -32,8 +32,8 @@ def nvcc() -> str:
 def build(verbose: bool = False) -> Path:
     out = HERE / "libiqk_b200.so"
     srcs = [str(CSRC / s) for s in SOURCES]
-    deps = srcs + [str(p) for p in CSRC.glob("*.cuh")] + [str(CSRC / "iq1s_grid.h"),
-                                                          str(HERE.parent / "include" / "iqk_b200.h")]
+    deps = (srcs + [str(p) for p in CSRC.glob("*.cuh")] + [str(p) for p in CSRC.glob("*.h")]
+            + [str(HERE.parent / "include" / "iqk_b200.h")])
     if out.exists() and all(out.stat().st_mtime >= Path(d).stat().st_mtime for d in deps):
         return out
     tmp = out.with_suffix(".so.tmp")

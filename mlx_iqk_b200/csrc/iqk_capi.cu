@@ -9,6 +9,7 @@
 
 #include "iqk_common.cuh"
 #include "iqk_gemv.cuh"
+#include "iqk_dense.cuh"
 #include "iqk_grouped.cuh"
 
 namespace {
@@ -44,6 +45,25 @@ int check_streams(int member, const void *const *streams) {
     return IQK_OK;
 }
 
+bool dense_member_ok(int m) {
+    return m == IQK_IQ4_KS || m == IQK_IQ4_K || m == IQK_IQ5_K || m == IQK_IQ6_K;
+}
+bool dense_width_ok(int64_t n) { return n == 1024 || n == 2048 || n == 4096 || n == 8192; }
+
+// Dense streams: present; qs 16-byte aligned (the kernels read four code words
+// at once), qh 8-byte aligned, the rest at their element size.
+int check_dense_streams(int member, const void *const *streams) {
+    if (!streams) return IQK_ERR_ARGUMENT;
+    const int count = member == IQK_IQ4_KS ? 3 : member == IQK_IQ5_K ? 6 : 5;
+    for (int i = 0; i < count; ++i)
+        if (!streams[i]) return IQK_ERR_ARGUMENT;
+    if (!aligned(streams[0], 16)) return IQK_ERR_ALIGNMENT;
+    if ((member == IQK_IQ5_K || member == IQK_IQ6_K) && !aligned(streams[1], 8))
+        return IQK_ERR_ALIGNMENT;
+    if (!aligned(streams[count - 1], member == IQK_IQ4_KS ? 4 : 2)) return IQK_ERR_ALIGNMENT;
+    return IQK_OK;
+}
+
 int cuda_status(cudaError_t err) {
     if (err == cudaSuccess) return IQK_OK;
     cudaGetLastError();  // clear a sticky launch error for the caller
@@ -70,6 +90,43 @@ const char *iqk_status_string(int status) {
 }
 
 int iqk_abi_version(void) { return 1; }
+
+int iqk_dense_dequant(int member, const void *const *streams, int64_t out_features,
+                      int64_t in_features, int64_t row_start, int64_t rows, int out_dtype,
+                      void *dst, iqk_stream_t stream) {
+    if (!dense_member_ok(member)) return IQK_ERR_MEMBER;
+    if (!dense_width_ok(in_features)) return IQK_ERR_WIDTH;
+    if (out_features <= 0 || out_features > ((int64_t)1 << 31)) return IQK_ERR_GEOMETRY;
+    if (row_start < 0 || rows < 0 || row_start + rows > out_features) return IQK_ERR_GEOMETRY;
+    if (!dtype_ok(out_dtype)) return IQK_ERR_ARGUMENT;
+    if (rows == 0) return IQK_OK;
+    if (!dst) return IQK_ERR_ARGUMENT;
+    if (!aligned(dst, 16)) return IQK_ERR_ALIGNMENT;
+    const int st = check_dense_streams(member, streams);
+    if (st != IQK_OK) return st;
+    return cuda_status(launch_dense_dequant(member, streams, (int)in_features, row_start, rows,
+                                            dst, out_dtype, reinterpret_cast<cudaStream_t>(stream),
+                                            num_sms_current()));
+}
+
+int iqk_dense_gemv(int member, const void *x, int64_t tokens, const void *const *streams,
+                   int64_t out_features, int64_t in_features, void *y, int y_dtype,
+                   iqk_stream_t stream) {
+    if (!dense_member_ok(member)) return IQK_ERR_MEMBER;
+    if (!dense_width_ok(in_features)) return IQK_ERR_WIDTH;
+    if (out_features <= 0 || out_features % 16 || out_features > ((int64_t)1 << 30))
+        return IQK_ERR_GEOMETRY;
+    if (tokens < 0 || tokens > (1 << 24)) return IQK_ERR_GEOMETRY;
+    if (y_dtype != IQK_F16 && y_dtype != IQK_F32) return IQK_ERR_ARGUMENT;
+    if (tokens == 0) return IQK_OK;
+    if (!x || !y) return IQK_ERR_ARGUMENT;
+    if (!aligned(x, 4) || !aligned(y, 4)) return IQK_ERR_ALIGNMENT;
+    const int st = check_dense_streams(member, streams);
+    if (st != IQK_OK) return st;
+    return cuda_status(launch_dense_gemv(member, streams, (int)in_features, (int)out_features, x,
+                                         (int)tokens, y, y_dtype,
+                                         reinterpret_cast<cudaStream_t>(stream)));
+}
 
 int iqk_check_bounded_wait(int64_t limit_ns, int32_t *flags, iqk_stream_t stream) {
     if (limit_ns < 0 || limit_ns > 2000000000LL) return IQK_ERR_ARGUMENT;
@@ -150,6 +207,12 @@ size_t iqk_gemv_workspace_bytes(int member, int64_t in_features, int64_t x_rows,
     return gemv_layout(member, in_features, x_rows, pairs).total;
 }
 
+size_t iqk_gemv_workspace_min_bytes(int member, int64_t in_features, int64_t x_rows,
+                                    int64_t pairs) {
+    if (!member_ok(member) || !width_ok(in_features) || x_rows < 0 || pairs < 0) return 0;
+    return gemv_layout(member, in_features, x_rows, pairs).total_nosplit;
+}
+
 // The GEMV addresses weight rows (expert * out_features + row) with 32-bit
 // tensor-map coordinates and counts its work items (pair x 64-row block) in
 // 32 bits.
@@ -178,11 +241,12 @@ int iqk_gemv_prepare(const void *x, int x_dtype, int64_t x_rows, int64_t in_feat
     if (pairs == 0) return IQK_OK;
     if (!x || !sel || !workspace) return IQK_ERR_ARGUMENT;
     if (!aligned(x, 16) || !aligned(workspace, 256)) return IQK_ERR_ALIGNMENT;
-    if (workspace_bytes < gemv_layout(0, in_features, x_rows, pairs).total)
-        return IQK_ERR_WORKSPACE;
+    const GemvLayout L = gemv_layout(0, in_features, x_rows, pairs);
+    if (workspace_bytes < L.total_nosplit) return IQK_ERR_WORKSPACE;
     return cuda_status(launch_gemv_prepare(x, x_dtype, x_rows, (int)in_features, num_experts,
                                            sel, tok, pairs, workspace,
-                                           reinterpret_cast<cudaStream_t>(stream)));
+                                           reinterpret_cast<cudaStream_t>(stream),
+                                           workspace_bytes >= L.total));
 }
 
 int iqk_gemv_run(int member, const void *const *streams, int64_t num_experts,
@@ -202,12 +266,13 @@ int iqk_gemv_run(int member, const void *const *streams, int64_t num_experts,
     if (!aligned(y, 4) || !aligned(workspace, 256)) return IQK_ERR_ALIGNMENT;
     const int st = check_streams(member, streams);
     if (st != IQK_OK) return st;
-    if (workspace_bytes < gemv_layout(member, in_features, x_rows, pairs).total)
-        return IQK_ERR_WORKSPACE;
+    const GemvLayout L = gemv_layout(member, in_features, x_rows, pairs);
+    if (workspace_bytes < L.total_nosplit) return IQK_ERR_WORKSPACE;
     return cuda_status(launch_gemv_run(member, streams, num_experts, out_features, (int)in_features, x_rows,
                                        pairs, y, y_dtype, workspace,
                                        reinterpret_cast<cudaStream_t>(stream),
-                                       num_sms_current()));
+                                       num_sms_current(), false, nullptr, nullptr,
+                                       workspace_bytes >= L.total));
 }
 
 int iqk_gemv_floor_run(int member, const void *const *streams, int64_t num_experts,
@@ -227,12 +292,13 @@ int iqk_gemv_floor_run(int member, const void *const *streams, int64_t num_exper
     if (!aligned(y, 4) || !aligned(workspace, 256)) return IQK_ERR_ALIGNMENT;
     const int st = check_streams(member, streams);
     if (st != IQK_OK) return st;
-    if (workspace_bytes < gemv_layout(member, in_features, x_rows, pairs).total)
-        return IQK_ERR_WORKSPACE;
+    const GemvLayout L = gemv_layout(member, in_features, x_rows, pairs);
+    if (workspace_bytes < L.total_nosplit) return IQK_ERR_WORKSPACE;
     return cuda_status(launch_gemv_run(member, streams, num_experts, out_features,
                                        (int)in_features, x_rows, pairs, y, y_dtype, workspace,
                                        reinterpret_cast<cudaStream_t>(stream),
-                                       num_sms_current(), true));
+                                       num_sms_current(), true, nullptr, nullptr,
+                                       workspace_bytes >= L.total));
 }
 
 int iqk_gemv_glu_run(int member, const void *const *gate_streams,
@@ -255,7 +321,7 @@ int iqk_gemv_glu_run(int member, const void *const *gate_streams,
     if (st != IQK_OK) return st;
     st = check_streams(member, up_streams);
     if (st != IQK_OK) return st;
-    if (workspace_bytes < gemv_layout(member, in_features, x_rows, pairs).total)
+    if (workspace_bytes < gemv_layout(member, in_features, x_rows, pairs).total_nosplit)
         return IQK_ERR_WORKSPACE;
     return cuda_status(launch_gemv_run(member, gate_streams, num_experts, out_features,
                                        (int)in_features, x_rows, pairs, h, IQK_F32, workspace,

@@ -16,7 +16,8 @@ from pathlib import Path
 
 import torch
 
-from .format import MEMBER_IDS, IqkFormatError, check_member, check_row_width
+from .format import (DENSE_MEMBER_IDS, MEMBER_IDS, IqkFormatError, check_dense_member,
+                     check_member, check_row_width)
 
 ROWS_PER_TG = 16
 """Output rows one decode work unit (a warp) covers; out_features must tile it."""
@@ -98,10 +99,16 @@ def library() -> ctypes.CDLL:
     lib.iqk_check_bounded_wait.restype = i32
     lib.iqk_dequant.argtypes = [i32, vp, i64, i64, i64, i64, i64, i32, vp, vp]
     lib.iqk_dequant.restype = i32
+    lib.iqk_dense_dequant.argtypes = [i32, vp, i64, i64, i64, i64, i32, vp, vp]
+    lib.iqk_dense_dequant.restype = i32
+    lib.iqk_dense_gemv.argtypes = [i32, vp, i64, vp, i64, i64, vp, i32, vp]
+    lib.iqk_dense_gemv.restype = i32
     lib.iqk_pack.argtypes = [i32, vp, i64, i64, vp, vp]
     lib.iqk_pack.restype = i32
     lib.iqk_gemv_workspace_bytes.argtypes = [i32, i64, i64, i64]
     lib.iqk_gemv_workspace_bytes.restype = sz
+    lib.iqk_gemv_workspace_min_bytes.argtypes = [i32, i64, i64, i64]
+    lib.iqk_gemv_workspace_min_bytes.restype = sz
     lib.iqk_gemv.argtypes = [i32, vp, i32, i64, vp, i64, i64, i64, vp, vp, i64, vp, i32, vp,
                              sz, vp]
     lib.iqk_gemv.restype = i32
@@ -152,14 +159,16 @@ def library() -> ctypes.CDLL:
 def exported_symbols() -> list[str]:
     """C ABI entry points declared in include/iqk_b200.h."""
     return ["iqk_status_string", "iqk_abi_version", "iqk_check_device", "iqk_dequant",
-            "iqk_gemv_workspace_bytes", "iqk_gemv", "iqk_gemv_prepare", "iqk_gemv_run",
+            "iqk_gemv_workspace_bytes", "iqk_gemv_workspace_min_bytes", "iqk_gemv",
+            "iqk_gemv_prepare", "iqk_gemv_run",
             "iqk_read_error", "iqk_grouped_workspace_bytes", "iqk_grouped_gemm",
             "iqk_grouped_prepare", "iqk_grouped_run", "iqk_grouped_read_error",
             "iqk_gemv_static_max_bytes", "iqk_gemv_static", "iqk_gemv_static_read_error",
             "iqk_grouped_prepare_shard",
             "iqk_pairs_swiglu", "iqk_pairs_combine", "iqk_gemv_floor_run",
             "iqk_dequant_floor", "iqk_grouped_run_range", "iqk_pack",
-            "iqk_gemv_glu_run", "iqk_swiglu_rows", "iqk_check_bounded_wait"]
+            "iqk_gemv_glu_run", "iqk_swiglu_rows", "iqk_check_bounded_wait",
+            "iqk_dense_dequant", "iqk_dense_gemv"]
 
 
 def check_bounded_wait(limit_ns: int, device: torch.device) -> int:
@@ -236,9 +245,43 @@ def dequant(member: str, streams, num_experts: int, out_features: int, in_featur
     return out
 
 
+def dense_dequant(member: str, streams, out_features: int, in_features: int, row_start: int,
+                  rows: int, out: torch.Tensor) -> torch.Tensor:
+    """``iqk_dense_dequant``: rows [row_start, row_start + rows) of a dense
+    matrix into ``out`` [rows, in] (f32, f16 or bf16)."""
+    check_device(out.device)
+    status = library().iqk_dense_dequant(DENSE_MEMBER_IDS[check_dense_member(member)],
+                                         ptr_array(streams), out_features, in_features,
+                                         row_start, rows, DTYPE_IDS[out.dtype], out.data_ptr(),
+                                         stream_handle(out.device))
+    raise_for_status(status, "iqk_dense_dequant")
+    return out
+
+
+def dense_gemv(member: str, x: torch.Tensor, streams, out_features: int, in_features: int,
+               y: torch.Tensor) -> torch.Tensor:
+    """``iqk_dense_gemv``: ``y [T, out] = x [T, in] W^T`` for f16 ``x``; ``y``
+    f16 or f32."""
+    check_device(y.device)
+    if x.dtype != torch.float16 or not x.is_contiguous():
+        raise IqkRuntimeError("the dense gemv takes contiguous fp16 activations")
+    status = library().iqk_dense_gemv(DENSE_MEMBER_IDS[check_dense_member(member)],
+                                      x.data_ptr(), x.shape[0], ptr_array(streams),
+                                      out_features, in_features, y.data_ptr(),
+                                      DTYPE_IDS[y.dtype], stream_handle(y.device))
+    raise_for_status(status, "iqk_dense_gemv")
+    return y
+
+
 @functools.lru_cache(maxsize=1024)
 def gemv_workspace_bytes(member: str, in_features: int, x_rows: int, pairs: int) -> int:
     return int(library().iqk_gemv_workspace_bytes(MEMBER_IDS[member], in_features, x_rows, pairs))
+
+
+def gemv_workspace_min_bytes(member: str, in_features: int, x_rows: int, pairs: int) -> int:
+    """The smallest workspace the GEMV accepts (no split slots: whole items)."""
+    return int(library().iqk_gemv_workspace_min_bytes(MEMBER_IDS[member], in_features, x_rows,
+                                                      pairs))
 
 
 def gemv(member: str, x: torch.Tensor, streams, num_experts: int, out_features: int,
