@@ -25,6 +25,8 @@ Legs on one GPU (each a line under its own key):
              B = 1/16/64, unsorted and sorted), config 4 (IQ1_S_R4 at
              B = 1..8), all through IqkSwitchLinear.__call__
   dequant    the bit-exact dequantization of each member beside its floor
+  dense      the dense members (IQ4_KS, IQ4_K, IQ5_K, IQ6_K): the decode GEMV
+             at the lm_head shape [129280, 4096] and the fp16 dequantization
   prefill    config 5 (one layer, gate/up IQ2_KS, down IQ2_K, 2048 tokens)
              on one GPU and through the expert-parallel layer at every N,
              with the expert-parallel output checked against the one-GPU
@@ -758,6 +760,47 @@ def dequant_leg(tm, K, mod, hbm: float, experts: int = 32, reps: int = 4) -> dic
             "shape": f"{experts} x [{out}, {n}] -> f16"}
 
 
+def dense_leg(tm, K, dev, gen, hbm: float) -> dict:
+    """The dense members (the survey's next row): the decode GEMV at the
+    lm_head shape [129280, 4096] (1 and 8 tokens; the matrix is 280-440 MB,
+    larger than L2, so every call streams it from HBM) and the fp16
+    dequantization of 16384 of its rows, per member."""
+    torch = tm.torch
+    from mlx_iqk_b200 import dense as dn
+    from mlx_iqk_b200.format import DENSE_MEMBERS, ik_row_bytes
+    from mlx_iqk_b200.profile_cases import random_dense_streams
+    out, n, rows = 129280, 4096, 16384
+    res = {}
+    for member in DENSE_MEMBERS:
+        st = dn.check_dense_streams(member, random_dense_streams(member, out, n, dev, gen), out, n)
+        wbytes = out * ik_row_bytes(member, n)
+        leg = {"weights_MB": round(wbytes / 1e6, 1)}
+        for T in (1, 8):
+            x = torch.randn((T, n), generator=gen, device=dev).half()
+            y = torch.empty((T, out), dtype=torch.float16, device=dev)
+            g = tm.graph(lambda: [K.dense_gemv(member, x, st, out, n, y) for _ in range(4)])
+            g.replay()
+            ms = tm.timed(g) / 4
+            del g
+            gbs = wbytes / (ms * 1e-3) / 1e9
+            leg[f"gemv T={T}"] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1),
+                                  "frac": round(gbs / hbm, 4)}
+        dst = torch.empty((rows, n), dtype=torch.float16, device=dev)
+        starts = [0, 40960, 81920, 112896]
+        g = tm.graph(lambda: [K.dense_dequant(member, st, out, n, s0, rows, dst) for s0 in starts])
+        g.replay()
+        ms = tm.timed(g) / len(starts)
+        del g
+        nb = rows * (ik_row_bytes(member, n) + 2 * n)
+        leg["dequant"] = {"us": round(ms * 1e3, 2), "GB/s": round(nb / (ms * 1e-3) / 1e9, 1),
+                          "frac": round(nb / (ms * 1e-3) / 1e9 / hbm, 4),
+                          "shape": f"[{rows}, {n}] -> f16"}
+        res[member] = leg
+        del st, dst
+        torch.cuda.empty_cache()
+    return res
+
+
 def config1_leg(tm, dev, gen) -> dict:
     """BASELINE config 1's call (one IQ2_KS [2048, 4096] expert, fp32 x, one
     token) through the module; 128 copies of the expert rotate so that no
@@ -843,7 +886,7 @@ def run_b200(args) -> None:
                 "floor_us": gate_leg["floor_us"], "vs_own_floor": gate_leg["vs_own_floor"]}
     floors = {f"gemv gate B={c8.B}": gate_leg, f"gemv down B={c8.B}": down_leg}
 
-    configs, dequant = None, None
+    configs, dequant, dense = None, None, None
     if world == 1 and not args.no_legs:
         configs = {"config1 (IQ2_KS one expert, fp32 x)": config1_leg(tm, dev, gen)}
         for member, bs, sorts in (("iq2_k", (1, 16, 64), (False, True)),
@@ -865,6 +908,7 @@ def run_b200(args) -> None:
             del mm
         dequant[MEMBER] = dequant_leg(tm, K, mods[0], hbm)
         torch.cuda.empty_cache()
+        dense = dense_leg(tm, K, dev, gen, hbm)
 
     # the same decode steps through the fused layer module, device-timed
     layer = glu_layer(torch, dev, mods)
@@ -891,7 +935,7 @@ def run_b200(args) -> None:
             "gpu_launches": launches_per_step * Kst,
             "clocks": clk.summary(),
             "hbm_frac_of_step": round(value / world / hbm, 4),
-            "configs": configs, "dequant": dequant, "prefill": prefill,
+            "configs": configs, "dequant": dequant, "dense": dense, "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

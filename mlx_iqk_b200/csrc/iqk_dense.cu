@@ -186,37 +186,203 @@ __device__ __forceinline__ void mma_f16_acc(float d[4], const uint32_t a[4], uin
 constexpr int kDenseWarps = 4;
 constexpr int kDenseRows = 16;
 
-// Table entry e of lane l at word 32 e + l: the value as f16 in the low half
-// and, for IQ6_K, the f16 residual (float32 value - hi) in the high half.
+// GEMV value table in shared memory, one copy per lane (entry e of lane l at
+// word 32 e + l, so every lookup is conflict-free whatever the codes).
+//   IQ4_KS / IQ4_K: pair entries, index alphabet << 8 | code byte: the f16
+//     values of the byte's two weights (low nibble first), which is exactly
+//     one A-fragment register.
+//   IQ5_K / IQ6_K: single entries, index alphabet << W | code: the f16 value
+//     in the low half (IQ6_K: the f16 residual of the float32 value in the
+//     high half, for the second MMA).
+template <int M> struct GemvTab {
+    static constexpr bool kPair = M == IQK_IQ4_KS || M == IQK_IQ4_K;
+    static constexpr int kEntries = kPair ? 512 : DenseGeo<M>::kEntries;
+    static constexpr int kBytes = kEntries * 32 * 4;
+};
+
 template <int M> __device__ __forceinline__ uint32_t gemv_entry(int e) {
+    if (GemvTab<M>::kPair) {
+        const int a = e >> 8;
+        const __half v0 = __float2half_rn(table_value(M, (a << 4) | (e & 15)));
+        const __half v1 = __float2half_rn(table_value(M, (a << 4) | ((e >> 4) & 15)));
+        return (uint32_t)__half_as_ushort(v0) | ((uint32_t)__half_as_ushort(v1) << 16);
+    }
     const float v = table_value(M, e);
     const __half hi = __float2half_rn(v);
     const __half lo = M == IQK_IQ6_K ? __float2half_rn(v - __half2float(hi)) : __float2half_rn(0.f);
     return (uint32_t)__half_as_ushort(hi) | ((uint32_t)__half_as_ushort(lo) << 16);
 }
 
-// NT token tiles of 8 per pass (tokens t0 .. t0 + 8 NT - 1).
-template <int M, int NT>
-__global__ void __launch_bounds__(kDenseWarps * 32)
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];\n" : "=r"(v) : "r"(a));
+    return v;
+}
+
+__device__ __forceinline__ void cp_async(uint32_t dst, const void *src, int bytes) {
+    if (bytes == 16)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src));
+    else if (bytes == 8)
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst), "l"(src));
+    else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(dst), "l"(src));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds8(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u8 %0, [%1];\n" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u16 %0, [%1];\n" : "=r"(v) : "r"(a));
+    return v;
+}
+
+// Geometry of the GEMV's staging. A CTA has 8 warps; KW of them (4, or 2 at
+// in_features 1024) split one 16-row tile's k range, so a CTA iteration
+// covers 8 / KW row tiles. Each warp streams its rows x k range in 64-weight
+// steps through its own ring of D shared-memory slots (cp.async: code words,
+// high bits), D - 1 steps ahead, and the scale bytes of its rows x k range
+// per row tile through two buffers, issued with the tile's first step.
+template <int M> struct DenseStage {
+    static constexpr int kQs = 16 * 32;                                  // qs bytes per step
+    static constexpr int kQh = M == IQK_IQ6_K ? 16 * 16 : M == IQK_IQ5_K ? 16 * 8 : 0;
+    static constexpr int kSlot = kQs + kQh;
+};
+// scale bytes per row of each stream over a k range of kq weights
+struct ScaleRows {
+    int scl, sch, sex, dv;  // bytes per row
+    int off_sch, off_sex, off_dv, total;  // region offsets in a buffer (16 rows each)
+};
+__host__ __device__ inline ScaleRows scale_rows(int member, int kq) {
+    ScaleRows r{};
+    if (member == IQK_IQ4_KS) {
+        r.scl = kq / 32;
+        r.dv = 0;  // the f32 row scale is read once per row tile
+    } else {
+        r.scl = member == IQK_IQ6_K ? kq / 16 : kq / 32;
+        r.sch = (member == IQK_IQ4_K || member == IQK_IQ5_K) ? kq / 64 : 0;
+        r.sex = kq / 128;
+        r.dv = 2 * (kq / 256);
+    }
+    r.off_sch = 16 * r.scl;
+    r.off_sex = r.off_sch + 16 * r.sch;
+    r.off_dv = r.off_sex + 16 * r.sex;
+    r.total = (r.off_dv + 16 * r.dv + 15) / 16 * 16;
+    return r;
+}
+
+template <int M>
+__host__ __device__ inline int dense_gemv_smem(int n, int D) {
+    const int KW = n >= 2048 ? 4 : 2;
+    const ScaleRows sr = scale_rows(M, n / KW);
+    return GemvTab<M>::kBytes + 8 * (D * DenseStage<M>::kSlot + 2 * sr.total);
+}
+
+// NT token tiles of 8 per pass (tokens t0 .. t0 + 8 NT - 1); D ring slots.
+template <int M, int NT, int D>
+__global__ void __launch_bounds__(256, 2)
 dense_gemv_kernel(DenseStreams st, int n, int out, const __half *__restrict__ x, int tokens,
                   void *__restrict__ y, int y_dtype) {
     using DG = DenseGeo<M>;
-    __shared__ uint32_t tab[DG::kEntries * 32];
-    __shared__ float red[kDenseWarps - 1][32][NT * 4];
+    using TB = GemvTab<M>;
+    using SG = DenseStage<M>;
+    extern __shared__ __align__(16) uint32_t dsm[];
+    __shared__ float red[8][32][NT * 4];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    for (int i = threadIdx.x; i < DG::kEntries * 32; i += blockDim.x) tab[i] = gemv_entry<M>(i >> 5);
+    const int KW = n >= 2048 ? 4 : 2, RT = 8 / KW;
+    const int rt = wid / KW, kw = wid % KW;  // this warp's row tile in the iteration, k part
+    const int kq = n / KW, kbeg = kw * kq, steps = kq / 64;
+    const ScaleRows sr = scale_rows(M, kq);
+    for (int i = threadIdx.x; i < TB::kEntries * 32; i += blockDim.x) dsm[i] = gemv_entry<M>(i >> 5);
+    const uint32_t smem0 = (uint32_t)__cvta_generic_to_shared(dsm);
+    const uint32_t tab_u = smem0 + 4u * lane;
+    const uint32_t ring = smem0 + TB::kBytes + (uint32_t)wid * (D * SG::kSlot + 2 * sr.total);
+    const uint32_t scb = ring + D * SG::kSlot;  // two scale buffers
     __syncthreads();
-    const uint32_t *mytab = tab + lane;
-    const int r0 = blockIdx.x * kDenseRows;
-    const int64_t ra = r0 + g, rb = r0 + g + 8;
-    const int kq = n / kDenseWarps;       // this warp's k range: [wid * kq, (wid + 1) * kq)
-    const int kbeg = wid * kq;
+
+    const int tiles = out / kDenseRows;
+    const int groups = (tiles + RT - 1) / RT;  // row-tile groups: one per CTA iteration
+    const int iters = (int)blockIdx.x < groups ? (groups - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int total = iters * steps;  // this warp's steps
+    auto tile_of = [&](int it) { return ((int)blockIdx.x + it * (int)gridDim.x) * RT + rt; };
+    // issue the copies of step f: its code words and high bits into slot f % D,
+    // and at a row tile's first step that tile's scale bytes into buffer it & 1
+    auto issue = [&](int f) {
+        const int it = f / steps, sidx = f - it * steps;
+        const int tile = tile_of(it);
+        if (tile >= tiles) return;
+        const int64_t r0 = (int64_t)tile * kDenseRows;
+        const int k0 = kbeg + 64 * sidx;
+        const uint32_t slot = ring + (uint32_t)(f % D) * SG::kSlot;
+        {
+            const int row = lane >> 1, half = lane & 1;
+            cp_async(slot + (uint32_t)(row * 32 + half * 16),
+                     st.qs + (r0 + row) * (n / 8) + (k0 >> 3) + 4 * half, 16);
+        }
+        if (M == IQK_IQ5_K && lane < 16)
+            cp_async(slot + SG::kQs + lane * 8, st.qh + (r0 + lane) * (n / 32) + (k0 >> 5), 8);
+        if (M == IQK_IQ6_K && lane < 16)
+            cp_async(slot + SG::kQs + lane * 16, st.qh + (r0 + lane) * (n / 16) + (k0 >> 4), 16);
+        if (sidx == 0 && lane < 16) {
+            const uint32_t b = scb + (uint32_t)(it & 1) * sr.total;
+            const int64_t row = r0 + lane;
+            auto piece = [&](uint32_t dst, const uint8_t *src, int bytes) {
+                for (int o = 0; o < bytes; o += 16)
+                    cp_async(dst + o, src + o, bytes - o >= 16 ? 16 : bytes - o);
+            };
+            if (M == IQK_IQ6_K)
+                piece(b + lane * sr.scl, st.scl + row * (n / 16) + kbeg / 16, sr.scl);
+            else
+                piece(b + lane * sr.scl, st.scl + row * (n / 32) + kbeg / 32, sr.scl);
+            if (sr.sch) piece(b + sr.off_sch + lane * sr.sch, st.sch + row * (n / 64) + kbeg / 64, sr.sch);
+            if (sr.sex) piece(b + sr.off_sex + lane * sr.sex, st.sex + row * (n / 128) + kbeg / 128, sr.sex);
+            if (sr.dv)
+                piece(b + sr.off_dv + lane * sr.dv,
+                      reinterpret_cast<const uint8_t *>(static_cast<const uint16_t *>(st.dv) + row * (n / 256) + kbeg / 256),
+                      sr.dv);
+        }
+    };
+    // dl of local sub-block `ls` of row `lr` (0..15) of the scale buffer `b`,
+    // the alphabet bit in the lowest mantissa bit (at most one float32 ulp)
+    auto scale_of = [&](uint32_t b, int lr, int ls, float drow) -> float {
+        int index, alpha;
+        float d;
+        if (M == IQK_IQ4_KS) {
+            const uint32_t v = lds8(b + lr * sr.scl + ls);
+            index = (int)(v & 254u) - 127;
+            alpha = (int)(v & 1u);
+            d = drow;
+        } else {
+            if (M == IQK_IQ6_K) {
+                index = (int)(int8_t)lds8(b + lr * sr.scl + ls);
+            } else {
+                const int lo = (int)((lds8(b + lr * sr.scl + (ls >> 1)) >> (4 * (ls & 1))) & 15u);
+                const int hi = (int)((lds8(b + sr.off_sch + lr * sr.sch + (ls >> 2)) >> (2 * (ls & 3))) & 3u);
+                index = (lo | (hi << 4)) - 32;
+            }
+            alpha = (int)((lds8(b + sr.off_sex + lr * sr.sex + (ls >> 3)) >> (ls & 7)) & 1u);
+            d = __half2float(__ushort_as_half((unsigned short)lds16(b + sr.off_dv + lr * sr.dv + 2 * (ls >> 4))));
+        }
+        const float dl = __fmul_rn(d, (float)index);
+        return __int_as_float((__float_as_int(dl) & ~1) | alpha);
+    };
+    // pairs: byte t of a word to bits 7..14 (entry index * 128 bytes) by one rotate
+    const uint32_t prot = (uint32_t)(8 * t - 7) & 31u;
+    constexpr uint32_t kAlphaShift = TB::kPair ? 15 : DG::kW + 7;
+
     for (int t0 = 0; t0 < tokens; t0 += 8 * NT) {
-        float acc[NT][4];
-#pragma unroll
-        for (int q = 0; q < NT; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
-        // B rows: token t0 + 8 q + g (zero past the last token)
         const __half *xb[NT];
         bool xok[NT];
 #pragma unroll
@@ -225,116 +391,154 @@ dense_gemv_kernel(DenseStreams st, int n, int out, const __half *__restrict__ x,
             xok[q] = tk < tokens;
             xb[q] = x + (int64_t)(xok[q] ? tk : 0) * n + 2 * t;
         }
+        float acc[NT][4];
+#pragma unroll
+        for (int q = 0; q < NT; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
+        // prologue: D - 1 steps in flight
 #pragma unroll 1
-        for (int k0 = kbeg; k0 < kbeg + kq; k0 += 32) {
-            // two 16-weight tiles: code words k0/8 .. k0/8 + 3 of rows ra, rb
-            const uint4 wa = *reinterpret_cast<const uint4 *>(st.qs + ra * (n / 8) + (k0 >> 3));
-            const uint4 wb = *reinterpret_cast<const uint4 *>(st.qs + rb * (n / 8) + (k0 >> 3));
-            uint32_t ha = 0, hb = 0;  // high bits of this lane's weights, both tiles
-            if (M == IQK_IQ5_K) {
-                ha = st.qh[ra * (n / 32) + (k0 >> 5)];
-                hb = st.qh[rb * (n / 32) + (k0 >> 5)];
-            }
-            uint2 qa = make_uint2(0, 0), qb = make_uint2(0, 0);
-            if (M == IQK_IQ6_K) {
-                qa = *reinterpret_cast<const uint2 *>(st.qh + ra * (n / 16) + (k0 >> 4));
-                qb = *reinterpret_cast<const uint2 *>(st.qh + rb * (n / 16) + (k0 >> 4));
-            }
-            int al_a, al_b;
-            float dla[2], dlb[2];
-            if (M == IQK_IQ4_KS) {
-                dla[0] = dla[1] = sub_scale<M>(st, n, ra, k0 >> 5, al_a);
-                dlb[0] = dlb[1] = sub_scale<M>(st, n, rb, k0 >> 5, al_b);
-            }
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {  // tile h: k0 + 16 h
-                const uint32_t w0a = h ? wa.z : wa.x, w1a = h ? wa.w : wa.y;
-                const uint32_t w0b = h ? wb.z : wb.x, w1b = h ? wb.w : wb.y;
-                int aa = al_a, ab = al_b;
-                if (M != IQK_IQ4_KS) {
-                    dla[h] = sub_scale<M>(st, n, ra, (k0 >> 4) + h, aa);
-                    dlb[h] = sub_scale<M>(st, n, rb, (k0 >> 4) + h, ab);
+        for (int f = 0; f < D - 1; ++f) {
+            if (f < total) issue(f);
+            cp_async_commit();
+        }
+        float dra = 0.f, drb = 0.f;
+#pragma unroll 1
+        for (int f = 0; f < total; ++f) {
+            const int it = f / steps, sidx = f - it * steps;
+            const int tile = tile_of(it);
+            const bool live = tile < tiles;
+            const int64_t ra = (int64_t)tile * kDenseRows + g, rb = ra + 8;
+            // the slot of step f - 1 is free again: refill it with step f + D - 1
+            __syncwarp();
+            if (f + D - 1 < total) issue(f + D - 1);
+            cp_async_commit();
+            cp_async_wait<D - 1>();
+            __syncwarp();
+            if (live) {
+                if (M == IQK_IQ4_KS && sidx == 0) {
+                    dra = __ldg(static_cast<const float *>(st.dv) + ra);
+                    drb = __ldg(static_cast<const float *>(st.dv) + rb);
                 }
-                // codes of k = 16h + {2t, 2t+1} (word w0) and {8+2t, 9+2t} (word w1)
-                int ca[4], cb[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int sh = 4 * (2 * t + (i & 1));
-                    ca[i] = (int)(((i < 2 ? w0a : w1a) >> sh) & 15u);
-                    cb[i] = (int)(((i < 2 ? w0b : w1b) >> sh) & 15u);
-                    const int kk = 16 * h + 2 * t + (i & 1) + 8 * (i >> 1);  // weight within k0 .. k0+31
-                    if (M == IQK_IQ5_K) {
-                        ca[i] |= (int)((ha >> kk) & 1u) << 4;
-                        cb[i] |= (int)((hb >> kk) & 1u) << 4;
-                    }
-                    if (M == IQK_IQ6_K) {
-                        const uint32_t wa2 = kk < 16 ? qa.x : qa.y, wb2 = kk < 16 ? qb.x : qb.y;
-                        ca[i] |= (int)((wa2 >> (2 * (kk & 15))) & 3u) << 4;
-                        cb[i] |= (int)((wb2 >> (2 * (kk & 15))) & 3u) << 4;
-                    }
+                const uint32_t slot = ring + (uint32_t)(f % D) * SG::kSlot;
+                const uint32_t b = scb + (uint32_t)(it & 1) * sr.total;
+                const int ls = M == IQK_IQ4_KS ? 2 * sidx + (t >> 1) : 4 * sidx + t;
+                const float dla_m = scale_of(b, g, ls, dra);
+                const float dlb_m = scale_of(b, g + 8, ls, drb);
+                const uint4 qa0 = lds128(slot + g * 32), qa1 = lds128(slot + g * 32 + 16);
+                const uint4 qb0 = lds128(slot + (g + 8) * 32), qb1 = lds128(slot + (g + 8) * 32 + 16);
+                uint4 ha = make_uint4(0, 0, 0, 0), hb = make_uint4(0, 0, 0, 0);
+                if (M == IQK_IQ5_K) {
+                    const uint32_t h = slot + SG::kQs;
+                    ha.x = lds32(h + g * 8);
+                    ha.y = lds32(h + g * 8 + 4);
+                    hb.x = lds32(h + (g + 8) * 8);
+                    hb.y = lds32(h + (g + 8) * 8 + 4);
                 }
-                uint32_t ea[4], eb[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    ea[i] = mytab[((aa << DG::kW) | ca[i]) * 32];
-                    eb[i] = mytab[((ab << DG::kW) | cb[i]) * 32];
-                }
-                // A: a0 = row g (k 2t, 2t+1), a1 = row g+8, a2 = row g (k 8+2t, 9+2t), a3 = row g+8
-                uint32_t A[4] = {__byte_perm(ea[0], ea[1], 0x5410), __byte_perm(eb[0], eb[1], 0x5410),
-                                 __byte_perm(ea[2], ea[3], 0x5410), __byte_perm(eb[2], eb[3], 0x5410)};
-                uint32_t L[4];
                 if (M == IQK_IQ6_K) {
-                    L[0] = __byte_perm(ea[0], ea[1], 0x7632);
-                    L[1] = __byte_perm(eb[0], eb[1], 0x7632);
-                    L[2] = __byte_perm(ea[2], ea[3], 0x7632);
-                    L[3] = __byte_perm(eb[2], eb[3], 0x7632);
+                    ha = lds128(slot + SG::kQs + g * 16);
+                    hb = lds128(slot + SG::kQs + (g + 8) * 16);
                 }
+                const int k0 = kbeg + 64 * sidx;
 #pragma unroll
-                for (int q = 0; q < NT; ++q) {
-                    const int kx = k0 + 16 * h;
-                    const uint32_t b0 = xok[q] ? __ldg(reinterpret_cast<const unsigned int *>(xb[q] + kx)) : 0u;
-                    const uint32_t b1 = xok[q] ? __ldg(reinterpret_cast<const unsigned int *>(xb[q] + kx + 8)) : 0u;
-                    float d[4];
-                    mma_f16(d, A, b0, b1);
-                    if (M == IQK_IQ6_K) mma_f16_acc(d, L, b0, b1);
-                    // this tile's partial sums, scaled by its sub-block's dl (rows g, g+8)
-                    acc[q][0] = fmaf(dla[h], d[0], acc[q][0]);
-                    acc[q][1] = fmaf(dla[h], d[1], acc[q][1]);
-                    acc[q][2] = fmaf(dlb[h], d[2], acc[q][2]);
-                    acc[q][3] = fmaf(dlb[h], d[3], acc[q][3]);
+                for (int tt = 0; tt < 4; ++tt) {
+                    const float dla = __shfl_sync(0xffffffffu, dla_m, (lane & ~3) | tt);
+                    const float dlb = __shfl_sync(0xffffffffu, dlb_m, (lane & ~3) | tt);
+                    const uint32_t offa = tab_u + (((uint32_t)__float_as_int(dla) & 1u) << kAlphaShift);
+                    const uint32_t offb = tab_u + (((uint32_t)__float_as_int(dlb) & 1u) << kAlphaShift);
+                    const uint4 &qa4 = tt < 2 ? qa0 : qa1;
+                    const uint4 &qb4 = tt < 2 ? qb0 : qb1;
+                    const uint32_t w0a = (tt & 1) ? qa4.z : qa4.x, w1a = (tt & 1) ? qa4.w : qa4.y;
+                    const uint32_t w0b = (tt & 1) ? qb4.z : qb4.x, w1b = (tt & 1) ? qb4.w : qb4.y;
+                    uint32_t A[4], L[4];
+                    if (TB::kPair) {
+                        A[0] = lds32(offa + (__funnelshift_r(w0a, w0a, prot) & 0x7f80u));
+                        A[1] = lds32(offb + (__funnelshift_r(w0b, w0b, prot) & 0x7f80u));
+                        A[2] = lds32(offa + (__funnelshift_r(w1a, w1a, prot) & 0x7f80u));
+                        A[3] = lds32(offb + (__funnelshift_r(w1b, w1b, prot) & 0x7f80u));
+                    } else {
+                        // single entries: weights 16 tt + {2t, 2t+1, 8+2t, 9+2t} of the step
+                        uint32_t e[2][4];
+#pragma unroll
+                        for (int r = 0; r < 2; ++r) {
+                            const uint32_t w0 = r ? w0b : w0a, w1 = r ? w1b : w1a;
+                            const uint4 &h4 = r ? hb : ha;
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const uint32_t w = i < 2 ? w0 : w1;
+                                const int kk = 16 * tt + 2 * t + (i & 1) + 8 * (i >> 1);
+                                uint32_t c = (w >> (4 * (2 * t + (i & 1)))) & 15u;
+                                if (M == IQK_IQ5_K) {
+                                    const uint32_t hw = kk < 32 ? h4.x : h4.y;
+                                    c |= ((hw >> (kk & 31)) & 1u) << 4;
+                                } else {
+                                    const uint32_t hw = (kk >> 4) == 0 ? h4.x : (kk >> 4) == 1 ? h4.y
+                                                        : (kk >> 4) == 2 ? h4.z : h4.w;
+                                    c |= ((hw >> (2 * (kk & 15))) & 3u) << 4;
+                                }
+                                e[r][i] = lds32((r ? offb : offa) + (c << 7));
+                            }
+                        }
+                        A[0] = __byte_perm(e[0][0], e[0][1], 0x5410);
+                        A[1] = __byte_perm(e[1][0], e[1][1], 0x5410);
+                        A[2] = __byte_perm(e[0][2], e[0][3], 0x5410);
+                        A[3] = __byte_perm(e[1][2], e[1][3], 0x5410);
+                        if (M == IQK_IQ6_K) {
+                            L[0] = __byte_perm(e[0][0], e[0][1], 0x7632);
+                            L[1] = __byte_perm(e[1][0], e[1][1], 0x7632);
+                            L[2] = __byte_perm(e[0][2], e[0][3], 0x7632);
+                            L[3] = __byte_perm(e[1][2], e[1][3], 0x7632);
+                        }
+                    }
+                    const int kx = k0 + 16 * tt;
+#pragma unroll
+                    for (int q = 0; q < NT; ++q) {
+                        const uint32_t b0 = xok[q] ? __ldg(reinterpret_cast<const unsigned int *>(xb[q] + kx)) : 0u;
+                        const uint32_t b1 = xok[q] ? __ldg(reinterpret_cast<const unsigned int *>(xb[q] + kx + 8)) : 0u;
+                        float d[4];
+                        mma_f16(d, A, b0, b1);
+                        if (M == IQK_IQ6_K) mma_f16_acc(d, L, b0, b1);
+                        acc[q][0] = fmaf(dla, d[0], acc[q][0]);
+                        acc[q][1] = fmaf(dla, d[1], acc[q][1]);
+                        acc[q][2] = fmaf(dlb, d[2], acc[q][2]);
+                        acc[q][3] = fmaf(dlb, d[3], acc[q][3]);
+                    }
                 }
             }
-        }
-        // the four k quarters meet in warp 0, added in warp order
-        if (wid > 0) {
-#pragma unroll
-            for (int q = 0; q < NT; ++q)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) red[wid - 1][lane][q * 4 + i] = acc[q][i];
-        }
-        __syncthreads();
-        if (wid == 0) {
-#pragma unroll
-            for (int w = 0; w < kDenseWarps - 1; ++w)
+            if (sidx + 1 < steps) continue;
+            // end of the iteration's row tiles: each tile's KW k parts meet in
+            // its first warp, added in k order
+            if (kw > 0) {
 #pragma unroll
                 for (int q = 0; q < NT; ++q)
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) acc[q][i] += red[w][lane][q * 4 + i];
-            // D fragment: d0 = (row g, token 2t), d1 = (row g, 2t+1), d2/d3 rows g+8
+                    for (int i = 0; i < 4; ++i) red[wid][lane][q * 4 + i] = acc[q][i];
+            }
+            __syncthreads();
+            if (kw == 0 && live) {
+                for (int w = 1; w < KW; ++w)
 #pragma unroll
-            for (int q = 0; q < NT; ++q) {
+                    for (int q = 0; q < NT; ++q)
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int tk = t0 + 8 * q + 2 * t + (i & 1);
-                    const int64_t row = (i < 2) ? ra : rb;
-                    if (tk < tokens) {
-                        const int64_t o = (int64_t)tk * out + row;
-                        if (y_dtype == IQK_F32) static_cast<float *>(y)[o] = acc[q][i];
-                        else static_cast<__half *>(y)[o] = __float2half_rn(acc[q][i]);
+                        for (int i = 0; i < 4; ++i) acc[q][i] += red[wid + w][lane][q * 4 + i];
+                // D fragment: d0 = (row g, token 2t), d1 = (row g, 2t+1), d2/d3 rows g+8
+#pragma unroll
+                for (int q = 0; q < NT; ++q) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int tk = t0 + 8 * q + 2 * t + (i & 1);
+                        const int64_t row = (i < 2) ? ra : rb;
+                        if (tk < tokens) {
+                            const int64_t o = (int64_t)tk * out + row;
+                            if (y_dtype == IQK_F32) static_cast<float *>(y)[o] = acc[q][i];
+                            else static_cast<__half *>(y)[o] = __float2half_rn(acc[q][i]);
+                        }
                     }
                 }
             }
+            __syncthreads();
+#pragma unroll
+            for (int q = 0; q < NT; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
         }
+        cp_async_wait<0>();
         __syncthreads();
     }
 }
@@ -371,17 +575,48 @@ cudaError_t dequant_m(const void *const *s, int n, int64_t row_start, int64_t ro
     return cudaGetLastError();
 }
 
+template <int M, int NT, int D>
+cudaError_t gemv_launch(const DenseStreams &st, int n, int out, const __half *xh, int tokens,
+                        void *y, int y_dtype, cudaStream_t stream, int dev) {
+    const int smem = dense_gemv_smem<M>(n, D);
+    // per (device, n) shared-memory opt-in and resident CTAs, queried once
+    static int per_sm[64][4] = {};
+    const int wi = n == 1024 ? 0 : n == 2048 ? 1 : n == 4096 ? 2 : 3;
+    int &ps = per_sm[dev & 63][wi];
+    if (ps == 0) {
+        cudaError_t e = cudaFuncSetAttribute(dense_gemv_kernel<M, NT, D>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        int nb = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, dense_gemv_kernel<M, NT, D>, 256, smem);
+        if (e != cudaSuccess) return e;
+        ps = nb > 0 ? nb : 1;
+    }
+    int sms = 148;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
+    const int RT = n >= 2048 ? 2 : 4;
+    const int groups = (out / kDenseRows + RT - 1) / RT;
+    const int grid = groups < sms * ps ? groups : sms * ps;
+    dense_gemv_kernel<M, NT, D><<<grid, 256, smem, stream>>>(st, n, out, xh, tokens, y, y_dtype);
+    return cudaGetLastError();
+}
+
 template <int M>
 cudaError_t gemv_m(const void *const *s, int n, int out, const void *x, int tokens, void *y,
                    int y_dtype, cudaStream_t stream) {
     const DenseStreams st = dense_streams<M>(s);
-    const unsigned blocks = (unsigned)(out / kDenseRows);
     const __half *xh = static_cast<const __half *>(x);
-    if (tokens <= 8)
-        dense_gemv_kernel<M, 1><<<blocks, kDenseWarps * 32, 0, stream>>>(st, n, out, xh, tokens, y, y_dtype);
-    else
-        dense_gemv_kernel<M, 2><<<blocks, kDenseWarps * 32, 0, stream>>>(st, n, out, xh, tokens, y, y_dtype);
-    return cudaGetLastError();
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+    // the deepest ring (8, 6 or 4 slots a warp) at which two CTAs still fit
+    // on an SM (228 KB: the dynamic part, the 8 KB reduction buffer, 1 KB
+    // reserved per CTA)
+    constexpr int kBudget = 104 * 1024;
+    const int D = dense_gemv_smem<M>(n, 8) <= kBudget ? 8 : dense_gemv_smem<M>(n, 6) <= kBudget ? 6 : 4;
+#define IQK_DG(NT_, D_) gemv_launch<M, NT_, D_>(st, n, out, xh, tokens, y, y_dtype, stream, dev)
+    if (tokens <= 8) return D == 8 ? IQK_DG(1, 8) : D == 6 ? IQK_DG(1, 6) : IQK_DG(1, 4);
+    return D == 8 ? IQK_DG(2, 8) : D == 6 ? IQK_DG(2, 6) : IQK_DG(2, 4);
+#undef IQK_DG
 }
 
 }  // namespace

@@ -60,6 +60,27 @@ def random_streams(member: str, experts: int, out: int, n: int, dev, gen) -> dic
     return streams
 
 
+def random_dense_streams(member: str, out: int, n: int, dev, gen) -> dict:
+    """Uniform random dense-member streams on the device, block scales at
+    serving magnitudes (float32 row scale for ``iq4_ks``)."""
+    from .format import dense_component_shapes
+    streams = {}
+    for name, shape in dense_component_shapes(member, out, n).items():
+        if name == "dv":
+            mag = torch.rand(shape, generator=gen, device=dev) * 8e-4 + 2e-5
+            sign = torch.where(torch.rand(shape, generator=gen, device=dev) < 0.5, -1.0, 1.0)
+            streams[name] = (mag * sign).to(torch.float32 if member == "iq4_ks" else torch.float16)
+            continue
+        dt = torch.uint32 if name in ("qs", "qh") else torch.uint8
+        count = 1
+        for s_ in shape:
+            count *= s_
+        raw = torch.randint(0, 256, (count * dt.itemsize,), generator=gen, device=dev,
+                            dtype=torch.uint8)
+        streams[name] = raw.view(dt).reshape(shape)
+    return streams
+
+
 def random_module(member: str, experts: int, out: int, n: int, dev, gen) -> IqkSwitchLinear:
     mod = IqkSwitchLinear(member, experts, out, n, device=dev)
     mod.load_streams(random_streams(member, experts, out, n, dev, gen))
@@ -98,7 +119,7 @@ def timed(fn, reps: int, graph: bool = False) -> float:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=("gemv", "grouped", "dequant", "layer", "step"))
+    ap.add_argument("case", choices=("gemv", "grouped", "dequant", "layer", "step", "dense"))
     ap.add_argument("--member", default="iq2_ks")
     ap.add_argument("--batch", type=int, default=8, help="gemv: tokens (top-6 each)")
     ap.add_argument("--tokens", type=int, default=2048, help="grouped: tokens (top-6 each)")
@@ -136,6 +157,21 @@ def main() -> None:
         print(json.dumps({"case": "layer", "experts": E, "tokens": T, "pairs": P,
                           "us": round(ms * 1e3, 2), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
                           "tokens_per_s": round(T / (ms * 1e-3), 1)}))
+        return
+    if args.case == "dense":
+        # the dense decode GEMV at the lm_head shape ([129280, 4096], --batch
+        # tokens) for --member (a dense member)
+        from . import dense as dn
+        from .format import ik_row_bytes
+        m, out_d, n_d = args.member, 129280, 4096
+        st = dn.check_dense_streams(m, random_dense_streams(m, out_d, n_d, dev, gen), out_d, n_d)
+        x = torch.randn((args.batch, n_d), generator=gen, device=dev).half()
+        y = torch.empty((args.batch, out_d), dtype=torch.float16, device=dev)
+        ms = timed(lambda: K.dense_gemv(m, x, st, out_d, n_d, y), args.reps, args.graph)
+        nbytes = out_d * ik_row_bytes(m, n_d)
+        print(json.dumps({"case": "dense", "member": m, "out": out_d, "in": n_d,
+                          "tokens": args.batch, "us": round(ms * 1e3, 2), "bytes": nbytes,
+                          "GBps": round(nbytes / (ms * 1e-3) / 1e9, 1)}))
         return
     if args.case == "step":
         # one SwitchGLU decode step (gate, up, SiLU * up * weight, down, top-k

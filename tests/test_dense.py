@@ -263,7 +263,11 @@ def test_gemv_at_the_lm_head_shape(cuda, member):
     x = np.random.default_rng(37).standard_normal((1, n)).astype(np.float16)
     got = dn.dense_gemv(member, torch.from_numpy(x).to(cuda), streams, out, n).cpu().numpy()[0]
     rows = np.sort(np.random.default_rng(38).choice(out, 512, replace=False))
-    sub = {k: v[rows.tolist()].cpu().numpy() for k, v in streams.items()}
+    idx = torch.from_numpy(rows).to(cuda)
+    sub = {}
+    for k, v in streams.items():  # (uint32 tensors have no gather: index their int32 view)
+        picked = (v.view(torch.int32) if v.dtype == torch.uint32 else v).index_select(0, idx)
+        sub[k] = picked.cpu().numpy().view(np.uint32) if v.dtype == torch.uint32 else picked.cpu().numpy()
     weights = D.decode(member, sub, n)
     want = weights.astype(np.float64) @ x[0].astype(np.float64)
     rel = np.max(np.abs(got[rows].astype(np.float64) - want)) / np.max(np.abs(want))
