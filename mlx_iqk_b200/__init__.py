@@ -9,8 +9,8 @@ from . import format  # noqa: F401
 from .format import IqkFormatError
 from .kernels import IqkKernelError, IqkRuntimeError
 from .nn import DECODE_MAT_LIMIT, IqkSwitchLinear, grid_table, member_table, value_table
-from .glu import IqkSwitchGLU
+from .glu import GraphedSwitchGLU, IqkSwitchGLU
 
 __all__ = ["DECODE_MAT_LIMIT", "IqkFormatError", "IqkKernelError", "IqkRuntimeError",
-           "IqkSwitchGLU", "IqkSwitchLinear", "format", "grid_table", "member_table",
+           "GraphedSwitchGLU", "IqkSwitchGLU", "IqkSwitchLinear", "format", "grid_table", "member_table",
            "value_table"]

@@ -74,6 +74,11 @@ class IqkSwitchGLU(nn.Module):
     def __call__(self, x, indices, scores=None, sorted_indices=False):
         return self.forward(x, indices, scores, sorted_indices)
 
+    def graphed(self, batch: int, top_k: int, dtype: torch.dtype = torch.bfloat16) -> "GraphedSwitchGLU":
+        """This layer's decode step for ``batch`` tokens captured in a CUDA
+        graph over static input / output tensors (see :class:`GraphedSwitchGLU`)."""
+        return GraphedSwitchGLU(self, batch, top_k, dtype)
+
     def forward(self, x, indices, scores=None, sorted_indices=False) -> torch.Tensor:
         """``x [..., hidden]``, ``indices [..., top_k]``, ``scores [..., top_k]``
         -> ``[..., hidden]`` float32 (or ``[..., top_k, hidden]`` when
@@ -152,4 +157,38 @@ class IqkSwitchGLU(nn.Module):
         return yd
 
 
-__all__ = ["IqkSwitchGLU"]
+class GraphedSwitchGLU:
+    """One decode step of an ``IqkSwitchGLU`` for a fixed batch, captured in a
+    CUDA graph: the static device tensors ``x [batch, hidden]``, ``indices
+    [batch, top_k]`` (int32) and ``scores [batch, top_k]`` (float32) are the
+    inputs, ``out [batch, hidden]`` (float32) the output. A server copies the
+    step's inputs into them (from pinned host memory, on any stream it orders
+    before the replay), calls :meth:`replay` on the current stream and reads
+    ``out`` -- the layer's launches then cost one graph launch instead of
+    their host-side set-up. Built by :meth:`IqkSwitchGLU.graphed`."""
+
+    def __init__(self, layer: "IqkSwitchGLU", batch: int, top_k: int,
+                 dtype: torch.dtype = torch.bfloat16):
+        dev = layer.device
+        self.layer, self.batch, self.top_k = layer, int(batch), int(top_k)
+        self.x = torch.zeros((batch, layer.hidden), dtype=dtype, device=dev)
+        # distinct valid experts per token for the capture's warm-up
+        ids = torch.arange(batch * top_k, device=dev, dtype=torch.int32) % layer.num_experts
+        self.indices = ids.reshape(batch, top_k).contiguous()
+        self.scores = torch.full((batch, top_k), 1.0 / top_k, device=dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            layer(self.x, self.indices, self.scores)  # first-call set-up outside capture
+            torch.cuda.synchronize(dev)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, stream=side):
+                self.out = layer(self.x, self.indices, self.scores)
+        torch.cuda.current_stream(dev).wait_stream(side)
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.out
+
+
+__all__ = ["GraphedSwitchGLU", "IqkSwitchGLU"]

@@ -154,3 +154,27 @@ def test_full_geometry_decode_step(cuda):
             h = a / (1 + np.exp(-a)) * (w_of(layer.up, e) @ xs[t]) * float(scores[t, j])
             want += w_of(layer.down, e) @ h
         assert rel_err(got[t], want) < 1e-4, t
+
+
+@pytest.mark.parametrize("tokens", [1, 8])
+def test_graphed_step_equals_the_eager_call(cuda, tokens):
+    """IqkSwitchGLU.graphed: the captured decode step over static inputs gives
+    the eager call's output bit for bit, replay after replay with new inputs."""
+    from mlx_iqk_b200 import GraphedSwitchGLU
+    E, k = 16, 6
+    layer, _ = make_layer(("iq2_ks", "iq2_ks", "iq2_ks"), E, cuda, seed=5)
+    step = layer.graphed(tokens, k)
+    assert isinstance(step, GraphedSwitchGLU)
+    rng = np.random.default_rng(90 + tokens)
+    for r in range(3):
+        idx = torch.from_numpy(np.stack([rng.choice(E, k, replace=False) for _ in range(tokens)])
+                               .astype(np.int32)).to(cuda)
+        w = torch.from_numpy(rng.dirichlet(np.ones(k), size=tokens).astype(np.float32)).to(cuda)
+        x = torch.randn((tokens, H), device=cuda).to(torch.bfloat16)
+        step.x.copy_(x)
+        step.indices.copy_(idx)
+        step.scores.copy_(w)
+        got = step.replay().clone()
+        want = layer(x, idx, w)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want), r
