@@ -145,8 +145,8 @@ int iqk_dequant_floor(int member, const void *const *streams, int64_t num_expert
  * count and pair count (routing tables plus the prepared activations), with
  * the split slots at the end: with them a wide decode grid divides its work
  * by rounds and cuts an item between two CTAs where that evens out the load
- * (IQ2_KS and IQ1_S_R4, whose sums are exact: the output is the same bit for
- * bit). iqk_gemv_workspace_min_bytes is the smallest workspace the GEMV
+ * (IQ1_S_R4, whose sums are exact: the output is the same bit for bit).
+ * iqk_gemv_workspace_min_bytes is the smallest workspace the GEMV
  * entries accept: the same minus the slots, dividing whole items. Prepare and
  * run must be given the same workspace size.
  */

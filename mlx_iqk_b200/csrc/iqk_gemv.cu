@@ -612,16 +612,20 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
             for (int i = tid; i < row_words; i += blockDim.x) yr[i] = 0;
         }
     }
-    // Work division. Whole items in general; for the members whose partial
-    // sums are exact integers (so the sum over a cut item does not depend on
-    // where it is cut), a wide grid of at most kMaxSplit CTAs with at least
-    // one item per CTA divides the rounds evenly instead: a CTA's first item
-    // may start mid-way (its tail part) and its last end mid-way (its head
-    // part), and the two parts of a cut item meet in split slot blockIdx.x
-    // (tail) == blockIdx.x + 1 of the CTA before (head). Rounds per CTA are
-    // then items * RPI / grid, within one round of each other, instead of
-    // whole items (3 or 4 of them at B = 8: a quarter idle).
-    constexpr bool kSplittable = !NARROW && !GLU && MEMBER != IQK_IQ2_K;
+    // Work division. Whole items in general; for IQ1_S_R4 (exact integer
+    // partial sums, so the sum over a cut item does not depend on where it is
+    // cut) a wide grid of at most kMaxSplit CTAs with at least one item per
+    // CTA divides the rounds evenly instead: a CTA's first item may start
+    // mid-way (its tail part) and its last end mid-way (its head part), and
+    // the two parts of a cut item meet in split slot blockIdx.x (tail) ==
+    // blockIdx.x + 1 of the CTA before (head). Rounds per CTA are then
+    // items * RPI / grid, within one round of each other, instead of whole
+    // items (3 or 4 of them at B = 8). Measured: IQ1_S_R4 B = 8 70 -> 65.6
+    // us; IQ2_KS (also exact) 38.0 -> 38.7 us at B = 8 and 21.5 -> 23.5 at
+    // B = 4 -- its warps' pace varies more than whole items do, and the cut
+    // items' extra scale-slot loads cost more than the balance gains -- so
+    // IQ2_KS keeps whole items.
+    constexpr bool kSplittable = !NARROW && !GLU && MEMBER == IQK_IQ1_S_R4;
     const bool split = kSplittable && a.split && hdr[6] == 1 && items >= (int)gridDim.x;
     const int64_t work = split ? (int64_t)items * RPI : items;
     const int64_t g0 = work * blockIdx.x / gridDim.x, g1 = work * (blockIdx.x + 1) / gridDim.x;
