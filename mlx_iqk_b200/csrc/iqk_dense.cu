@@ -122,23 +122,35 @@ dense_dequant_kernel(DenseStreams st, int n, int64_t row_start, int64_t rows,
     const int upr = n / 16;  // units per row (a power of two, >= 64)
     const int64_t total = rows * upr;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    // total and stride are multiples of 32: every warp is all in or all out
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
-        const int64_t lr = i / upr;
-        const int u = (int)(i - lr * upr);
-        const int64_t row = row_start + lr;
+    // one unit's inputs: its two code words, high bits and scale
+    struct Unit {
+        uint2 w;
+        uint32_t hi;
+        float dl;
+        int base;
+        int64_t lr;
+        int u;
+    };
+    auto load = [&](int64_t i) {
+        Unit U;
+        U.lr = i / upr;
+        U.u = (int)(i - U.lr * upr);
+        const int64_t row = row_start + U.lr;
         int alpha;
-        const float dl = sub_scale<M>(st, n, row, M == IQK_IQ4_KS ? u >> 1 : u, alpha);
-        const uint2 w = *reinterpret_cast<const uint2 *>(st.qs + row * (n / 8) + 2 * u);
-        const uint32_t hi = unit_high<M>(st, n, row, u);
-        const int base = alpha << DG::kW;
+        U.dl = sub_scale<M>(st, n, row, M == IQK_IQ4_KS ? U.u >> 1 : U.u, alpha);
+        U.w = *reinterpret_cast<const uint2 *>(st.qs + row * (n / 8) + 2 * U.u);
+        U.hi = unit_high<M>(st, n, row, U.u);
+        U.base = alpha << DG::kW;
+        return U;
+    };
+    auto emit = [&](const Unit &U) {
         float v[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-            int c = (int)(((j < 8 ? w.x : w.y) >> (4 * (j & 7))) & 15u);
-            if (M == IQK_IQ5_K) c |= (int)((hi >> j) & 1u) << 4;
-            if (M == IQK_IQ6_K) c |= (int)((hi >> (2 * j)) & 3u) << 4;
-            v[j] = __fmul_rn(dl, mytab[(base | c) * 32]);
+            int c = (int)(((j < 8 ? U.w.x : U.w.y) >> (4 * (j & 7))) & 15u);
+            if (M == IQK_IQ5_K) c |= (int)((U.hi >> j) & 1u) << 4;
+            if (M == IQK_IQ6_K) c |= (int)((U.hi >> (2 * j)) & 3u) << 4;
+            v[j] = __fmul_rn(U.dl, mytab[(U.base | c) * 32]);
         }
         uint4 out[CH];
         if constexpr (sizeof(OUT) == 4) {
@@ -158,10 +170,21 @@ dense_dequant_kernel(DenseStreams st, int n, int64_t row_start, int64_t rows,
 #pragma unroll
         for (int c = 0; c < CH; ++c) my_stage[lane * CH + c] = out[c];
         __syncwarp();
-        uint4 *wout = reinterpret_cast<uint4 *>(dst + lr * n + (int64_t)(u - lane) * 16);
+        uint4 *wout = reinterpret_cast<uint4 *>(dst + U.lr * n + (int64_t)(U.u - lane) * 16);
 #pragma unroll
         for (int c = 0; c < CH; ++c) __stcs(wout + 32 * c + lane, my_stage[32 * c + lane]);
         __syncwarp();
+    };
+    // total and stride are multiples of 32: every warp is all in or all out of
+    // each unit; two units per pass, both units' loads issued before either
+    // is decoded (twice the reads in flight)
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += 2 * stride) {
+        const bool two = i + stride < total;
+        const Unit a = load(i);
+        Unit b{};
+        if (two) b = load(i + stride);
+        emit(a);
+        if (two) emit(b);
     }
 }
 
