@@ -374,12 +374,14 @@ def layer_modules(torch, member: str, dev, gen, experts: int | None = None):
 class DecodeCell:
     """One batch size of the headline decode step on the kernel entry points:
     a pool of rotating selections and activations, preallocated workspaces
-    and outputs, and the 5-launch step. Gate and up read the same prepared
-    activations and nothing of each other, so they run on two streams: the
-    second fills the SMs the first's last wave leaves idle. Down follows
-    both, as SiLU(gate)*up would in a model."""
+    and outputs, and the 6-launch step: gate and up each prepared into its
+    own workspace and run on its own stream (the run kernels claim their items
+    from a counter in their workspace, so runs on one workspace are
+    stream-ordered, and two concurrent runs take two workspaces); the second
+    fills the SMs the first's tail leaves idle. Down follows both, as
+    SiLU(gate)*up would feed it in a model."""
 
-    launches = 5
+    launches = 6
 
     def __init__(self, torch, K, mods, B: int, dev, gen, seed: int, member: str = MEMBER):
         self.torch, self.K, self.B, self.member = torch, K, B, member
@@ -397,6 +399,7 @@ class DecodeCell:
         self.pairs = B * TOP_K
         self.ws_gu = torch.empty(K.gemv_workspace_bytes(member, GATE_UP[1], B, self.pairs),
                                  dtype=torch.uint8, device=dev)
+        self.ws_up = torch.empty_like(self.ws_gu)
         self.ws_d = torch.empty(K.gemv_workspace_bytes(member, DOWN[1], self.pairs, self.pairs),
                                 dtype=torch.uint8, device=dev)
         self.yg = torch.empty((self.pairs, GATE_UP[0]), device=dev)
@@ -408,12 +411,13 @@ class DecodeCell:
     def step(self, s: int) -> None:
         K, p, B, P, M = self.K, s % self.pool, self.B, self.pairs, self.member
         torch = self.torch
-        K.gemv_prepare(self.xs[p], E, GATE_UP[1], self.sels[p].reshape(-1), None, self.ws_gu)
         main = torch.cuda.current_stream()
         self.side.wait_stream(main)
+        K.gemv_prepare(self.xs[p], E, GATE_UP[1], self.sels[p].reshape(-1), None, self.ws_gu)
         K.gemv_run(M, self.sg, E, GATE_UP[0], GATE_UP[1], B, P, self.yg, self.ws_gu)
         with torch.cuda.stream(self.side):
-            K.gemv_run(M, self.su, E, GATE_UP[0], GATE_UP[1], B, P, self.yu, self.ws_gu)
+            K.gemv_prepare(self.xs[p], E, GATE_UP[1], self.sels[p].reshape(-1), None, self.ws_up)
+            K.gemv_run(M, self.su, E, GATE_UP[0], GATE_UP[1], B, P, self.yu, self.ws_up)
         main.wait_stream(self.side)
         K.gemv_prepare(self.xds[p], E, DOWN[1], self.sels[p].reshape(-1), None, self.ws_d)
         K.gemv_run(M, self.sd, E, DOWN[0], DOWN[1], P, P, self.yd, self.ws_d)

@@ -148,7 +148,12 @@ int iqk_dequant_floor(int member, const void *const *streams, int64_t num_expert
  * (IQ1_S_R4, whose sums are exact: the output is the same bit for bit).
  * iqk_gemv_workspace_min_bytes is the smallest workspace the GEMV
  * entries accept: the same minus the slots, dividing whole items. Prepare and
- * run must be given the same workspace size.
+ * run must be given the same workspace size. The run kernels keep their
+ * work-distribution counters in the workspace (CTAs claim items from it, the
+ * last one done resets it; the prepare zeroes it), so runs over one
+ * workspace must be ordered (one stream, or events): two projections that
+ * share a preparation run one after the other, or each over its own
+ * prepared workspace.
  */
 size_t iqk_gemv_workspace_bytes(int member, int64_t in_features, int64_t x_rows,
                                 int64_t pairs);

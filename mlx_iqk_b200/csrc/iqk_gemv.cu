@@ -305,7 +305,12 @@ gemv_prep_kernel(const XT *__restrict__ x, int n, int x_rows, const int32_t *__r
             int32_t *cnt = reinterpret_cast<int32_t *>(ws + L.split_cnt);
             for (int i = threadIdx.x; i < kMaxSplit * 4; i += blockDim.x) cnt[i] = 0;
         }
-        if (threadIdx.x == 0) reinterpret_cast<int32_t *>(ws + L.hdr)[6] = with_split;
+        if (threadIdx.x == 0) {
+            int32_t *h = reinterpret_cast<int32_t *>(ws + L.hdr);
+            h[6] = with_split;
+            h[8] = 0;  // the run kernels' work counter (items claimed)
+            h[9] = 0;  // and the count of their CTAs done (the last one resets both)
+        }
         route_pairs(sel, tok, pairs, x_rows, num_experts, L, ws);
     }
 }
@@ -403,6 +408,7 @@ struct GemvArgs {
     const char *ws;
     int32_t *err;  // device error word (workspace header)
     int split;     // 1: the grid fits the split slots (kMaxSplit)
+    int dynamic;   // 1: CTAs claim whole items from the workspace's work counter
     void *y;
     int y_dtype;
 };
@@ -625,17 +631,38 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
     // B = 4 -- its warps' pace varies more than whole items do, and the cut
     // items' extra scale-slot loads cost more than the balance gains -- so
     // IQ2_KS keeps whole items.
+    // Every other launch claims whole items dynamically: each CTA's producer
+    // takes the next item from a counter in the workspace header and hands it
+    // to the compute warps with the item's scale slot. The schedulers favour
+    // low warp slots (measured: warps in slots 0-3 run a round in 0.89 us,
+    // slots 12-15 in 1.17 us), so a static division leaves the slow CTAs
+    // finishing alone; claimed items keep every CTA busy until the work runs
+    // out. The last CTA to finish resets the counter for the next run on the
+    // workspace (runs on one workspace are stream-ordered).
     constexpr bool kSplittable = !NARROW && !GLU && MEMBER == IQK_IQ1_S_R4;
     const bool split = kSplittable && a.split && hdr[6] == 1 && items >= (int)gridDim.x;
+    // (more items than CTAs only: the first item of CTA b is item b, claims
+    // start after the first wave, so no claim sits before a CTA's first copy)
+    const bool dyn = !split && a.dynamic && items > (int)gridDim.x;
+    int32_t *work_ctr = reinterpret_cast<int32_t *>(const_cast<char *>(a.ws) + a.L.hdr) + 8;
+    int32_t *done_ctr = work_ctr + 1;
+    int *sitem = abort_flag + 1;  // [2] the item of scale slot 0 / 1 (-1: no more)
     const int64_t work = split ? (int64_t)items * RPI : items;
-    const int64_t g0 = work * blockIdx.x / gridDim.x, g1 = work * (blockIdx.x + 1) / gridDim.x;
-    if (g0 >= g1) return;  // uniform over the CTA
+    const int64_t g0 = dyn ? 0 : work * blockIdx.x / gridDim.x;
+    const int64_t g1 = dyn ? work : work * (blockIdx.x + 1) / gridDim.x;
+    if (g0 >= g1) {  // uniform over the CTA
+        if (dyn && tid == 0 && atomicAdd(done_ctr, 1) == (int)gridDim.x - 1) {
+            atomicExch(work_ctr, 0);
+            atomicExch(done_ctr, 0);
+        }
+        return;
+    }
     const int i0 = (int)(split ? g0 / RPI : g0);
     const int i1 = (int)(split ? (g1 - 1) / RPI + 1 : g1);
     const int r_first = split ? (int)(g0 % RPI) : 0;           // first item's first round
     const int r_last = split ? (int)((g1 - 1) % RPI) + 1 : RPI;  // last item's round end
     const int t0 = i0 / rblocks, t1 = (i1 - 1) / rblocks;
-    const bool cached = t1 - t0 < kMaxTiles;
+    const bool cached = !dyn && t1 - t0 < kMaxTiles;
     auto load_tile = [&](int t) -> TileRef {
         TileRef r = tlist[t];
         r.sh0 = xscale[r.tok0];
@@ -663,16 +690,40 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
         const int si = sl >= 1 && sl < SS::kCount ? sl : 0;
         const int s_rowb = si ? SS::b(si) : 0, s_off = si ? sproj * SSB + SS::off(si) : 0;
         const void *const *sstreams = sproj ? a.s2 : a.s;
-        for (int o = 0; o < n_items && ok; ++o) {
-            const TileRef T = tile_of(ti);
-            const int r0 = rb * kRows;
-            const int rows_valid = min(kRows, out - r0);
+        for (int o = 0; ok; ++o) {
+            int item;
+            if (dyn) {
+                if (o == 0) {
+                    item = (int)blockIdx.x;
+                } else {
+                    if (lane == 0) item = (int)gridDim.x + atomicAdd(work_ctr, 1);
+                    item = __shfl_sync(0xffffffffu, item, 0);
+                }
+            } else {
+                if (o >= n_items) break;
+                item = i0 + o;
+            }
             // the item's scale streams (all rows, all of k) into scale slot o % 2
             const int ss = o & 1;
             if (o >= 2 && !mbar_wait(&sempty[ss], ((o >> 1) & 1) ^ 1)) {
                 ok = false;
                 break;
             }
+            if (dyn && item >= items) {
+                // no more work: the compute warps learn it from the slot
+                if (lane == 0) {
+                    sitem[ss] = -1;
+                    mbar_arrive(&sfull[ss]);
+                }
+                sissued = o + 1;
+                break;
+            }
+            if (dyn && lane == 0) sitem[ss] = item;
+            ti = item / rblocks;
+            rb = item - ti * rblocks;
+            const TileRef T = tile_of(ti);
+            const int r0 = rb * kRows;
+            const int rows_valid = min(kRows, out - r0);
             if (lane == 0)
                 mbar_arrive_expect_tx(&sfull[ss],
                                       (uint32_t)(SH::kProj * rows_valid * (SS::kSlot / kRows)));
@@ -713,10 +764,6 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
                 }
                 issued = j + 1;
             }
-            if (++rb == rblocks) {
-                rb = 0;
-                ++ti;
-            }
         }
         if (!ok && lane == 0) {
             atomicOr(a.err, IQK_DEVERR_TIMEOUT);
@@ -729,6 +776,15 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
             mbar_wait(&full[j % kStages], (j / kStages) & 1);
         for (int q = sissued - 1; q >= 0 && q >= sissued - 2; --q)
             mbar_wait(&sfull[q & 1], (q >> 1) & 1);
+        if (dyn && lane == 0) {
+            // the last CTA done resets the counters (every CTA has claimed its
+            // last item before it counts itself done)
+            __threadfence();
+            if (atomicAdd(done_ctr, 1) == (int)gridDim.x - 1) {
+                atomicExch(work_ctr, 0);
+                atomicExch(done_ctr, 0);
+            }
+        }
         return;
     }
 
@@ -858,17 +914,8 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
     int ti = i0 / rblocks, rb = i0 % rblocks;
     int jr = 0;             // rounds consumed so far (the producer's ring order)
     bool prebuilt = false;  // this item's first-round metadata was built during the last item
-    for (int o = 0; o < n_items; ++o) {
-        const TileRef T = tile_of(ti);
-        const int r0 = rb * kRows;
-        const bool live = NARROW || rbase < out - r0;  // this warp's row tile exists
-        // the next item's row tile, for building its first-round metadata early
-        // (wide items only: in a two-round narrow item the extra wait measured
-        // slower)
-        const bool nlive = !NARROW && o + 1 < n_items &&
-                           rbase < out - (rb + 1 == rblocks ? 0 : rb + 1) * kRows;
-        const char *sd = sslots + ((o & 1) * SH::kProj + proj) * SSB;
-        // the item's scale streams
+    for (int o = 0; dyn || o < n_items; ++o) {
+        // the item's scale streams (and, claimed dynamically, the item itself)
         if (!mbar_wait(&sfull[o & 1], (o >> 1) & 1)) {
             if (lane == 0) {
                 atomicOr(a.err, IQK_DEVERR_TIMEOUT);
@@ -877,6 +924,19 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
             break;
         }
         if (*(volatile int *)abort_flag) break;
+        const int item = dyn ? *(volatile int *)&sitem[o & 1] : i0 + o;
+        if (item < 0) break;  // no more work
+        ti = item / rblocks;
+        rb = item - ti * rblocks;
+        const TileRef T = tile_of(ti);
+        const int r0 = rb * kRows;
+        const bool live = NARROW || rbase < out - r0;  // this warp's row tile exists
+        // the next item's row tile, for building its first-round metadata early
+        // (wide items only: in a two-round narrow item the extra wait measured
+        // slower); claimed dynamically, it is known once its slot is full
+        const bool nlive = !NARROW && (dyn || (o + 1 < n_items &&
+                           rbase < out - (rb + 1 == rblocks ? 0 : rb + 1) * kRows));
+        const char *sd = sslots + ((o & 1) * SH::kProj + proj) * SSB;
         const int rs = round_begin(o), re = round_end(o);
         // metadata buffer of round r: r & 1
         if (!FLOOR && live && !prebuilt) build_meta(sd, chunk_of(rs), meta_u + (rs & 1) * G::kMetaBytes);
@@ -1052,9 +1112,12 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
                 } else if (r + 1 < re) {
                     build_meta(sd, chunk_of(r + 1), meta_u + ((r + 1) & 1) * G::kMetaBytes);
                 } else if (nlive && (r & 1) && mbar_wait(&sfull[(o + 1) & 1], ((o + 1) >> 1) & 1)) {
-                    build_meta(sslots + (((o + 1) & 1) * SH::kProj + proj) * SSB, chunk_of(0),
-                               meta_u);
-                    prebuilt = true;
+                    const int nitem = dyn ? *(volatile int *)&sitem[(o + 1) & 1] : item + 1;
+                    if (nitem >= 0 && rbase < out - (nitem % rblocks) * kRows) {
+                        build_meta(sslots + (((o + 1) & 1) * SH::kProj + proj) * SSB, chunk_of(0),
+                                   meta_u);
+                        prebuilt = true;
+                    }
                 }
             }
             __syncwarp();
@@ -1263,10 +1326,6 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sempty[o & 1]);  // the item's scale slot
-        if (++rb == rblocks) {
-            rb = 0;
-            ++ti;
-        }
     }
 }
 
@@ -1499,6 +1558,7 @@ cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_
     int64_t blocks = max_items < cap ? max_items : cap;
     if (blocks < 1) blocks = 1;
     ga.split = allow_split && blocks <= kMaxSplit ? 1 : 0;  // one split slot per CTA boundary
+    ga.dynamic = 1;
     PdlLaunch pl((unsigned)blocks, kThreads, gemv_smem_for(member, n, narrow, glu), stream);
     err = cudaLaunchKernelEx(&pl.cfg, gemv_fn(member, n, narrow, variant), ga, map, map2);
     if (err != cudaSuccess) return err;
