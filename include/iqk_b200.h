@@ -142,15 +142,11 @@ int iqk_dequant_floor(int member, const void *const *streams, int64_t num_expert
 
 /*
  * Workspace bytes iqk_gemv needs for this member, width, activation-row
- * count and pair count (routing tables plus the prepared activations), with
- * the split slots at the end: with them a wide decode grid divides its work
- * by rounds and cuts an item between two CTAs where that evens out the load
- * (IQ1_S_R4, whose sums are exact: the output is the same bit for bit).
- * iqk_gemv_workspace_min_bytes is the smallest workspace the GEMV
- * entries accept: the same minus the slots, dividing whole items. Prepare and
- * run must be given the same workspace size. The run kernels keep their
- * work-distribution counters in the workspace (CTAs claim items from it, the
- * last one done resets it; the prepare zeroes it), so runs over one
+ * count and pair count (routing tables plus the prepared activations).
+ * iqk_gemv_workspace_min_bytes is the smallest workspace the GEMV entries
+ * accept (today the same figure). The run kernels keep their
+ * work-distribution counters in the workspace header (CTAs claim items from
+ * it, the last one done resets it; the prepare zeroes it), so runs over one
  * workspace must be ordered (one stream, or events): two projections that
  * share a preparation run one after the other, or each over its own
  * prepared workspace.

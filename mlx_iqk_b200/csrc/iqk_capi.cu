@@ -210,7 +210,7 @@ size_t iqk_gemv_workspace_bytes(int member, int64_t in_features, int64_t x_rows,
 size_t iqk_gemv_workspace_min_bytes(int member, int64_t in_features, int64_t x_rows,
                                     int64_t pairs) {
     if (!member_ok(member) || !width_ok(in_features) || x_rows < 0 || pairs < 0) return 0;
-    return gemv_layout(member, in_features, x_rows, pairs).total_nosplit;
+    return gemv_layout(member, in_features, x_rows, pairs).total;
 }
 
 // The GEMV addresses weight rows (expert * out_features + row) with 32-bit
@@ -241,12 +241,11 @@ int iqk_gemv_prepare(const void *x, int x_dtype, int64_t x_rows, int64_t in_feat
     if (pairs == 0) return IQK_OK;
     if (!x || !sel || !workspace) return IQK_ERR_ARGUMENT;
     if (!aligned(x, 16) || !aligned(workspace, 256)) return IQK_ERR_ALIGNMENT;
-    const GemvLayout L = gemv_layout(0, in_features, x_rows, pairs);
-    if (workspace_bytes < L.total_nosplit) return IQK_ERR_WORKSPACE;
+    if (workspace_bytes < gemv_layout(0, in_features, x_rows, pairs).total)
+        return IQK_ERR_WORKSPACE;
     return cuda_status(launch_gemv_prepare(x, x_dtype, x_rows, (int)in_features, num_experts,
                                            sel, tok, pairs, workspace,
-                                           reinterpret_cast<cudaStream_t>(stream),
-                                           workspace_bytes >= L.total));
+                                           reinterpret_cast<cudaStream_t>(stream)));
 }
 
 int iqk_gemv_run(int member, const void *const *streams, int64_t num_experts,
@@ -266,13 +265,12 @@ int iqk_gemv_run(int member, const void *const *streams, int64_t num_experts,
     if (!aligned(y, 4) || !aligned(workspace, 256)) return IQK_ERR_ALIGNMENT;
     const int st = check_streams(member, streams);
     if (st != IQK_OK) return st;
-    const GemvLayout L = gemv_layout(member, in_features, x_rows, pairs);
-    if (workspace_bytes < L.total_nosplit) return IQK_ERR_WORKSPACE;
+    if (workspace_bytes < gemv_layout(member, in_features, x_rows, pairs).total)
+        return IQK_ERR_WORKSPACE;
     return cuda_status(launch_gemv_run(member, streams, num_experts, out_features, (int)in_features, x_rows,
                                        pairs, y, y_dtype, workspace,
                                        reinterpret_cast<cudaStream_t>(stream),
-                                       num_sms_current(), false, nullptr, nullptr,
-                                       workspace_bytes >= L.total));
+                                       num_sms_current()));
 }
 
 int iqk_gemv_floor_run(int member, const void *const *streams, int64_t num_experts,
@@ -292,13 +290,12 @@ int iqk_gemv_floor_run(int member, const void *const *streams, int64_t num_exper
     if (!aligned(y, 4) || !aligned(workspace, 256)) return IQK_ERR_ALIGNMENT;
     const int st = check_streams(member, streams);
     if (st != IQK_OK) return st;
-    const GemvLayout L = gemv_layout(member, in_features, x_rows, pairs);
-    if (workspace_bytes < L.total_nosplit) return IQK_ERR_WORKSPACE;
+    if (workspace_bytes < gemv_layout(member, in_features, x_rows, pairs).total)
+        return IQK_ERR_WORKSPACE;
     return cuda_status(launch_gemv_run(member, streams, num_experts, out_features,
                                        (int)in_features, x_rows, pairs, y, y_dtype, workspace,
                                        reinterpret_cast<cudaStream_t>(stream),
-                                       num_sms_current(), true, nullptr, nullptr,
-                                       workspace_bytes >= L.total));
+                                       num_sms_current(), true));
 }
 
 int iqk_gemv_glu_run(int member, const void *const *gate_streams,
@@ -321,7 +318,7 @@ int iqk_gemv_glu_run(int member, const void *const *gate_streams,
     if (st != IQK_OK) return st;
     st = check_streams(member, up_streams);
     if (st != IQK_OK) return st;
-    if (workspace_bytes < gemv_layout(member, in_features, x_rows, pairs).total_nosplit)
+    if (workspace_bytes < gemv_layout(member, in_features, x_rows, pairs).total)
         return IQK_ERR_WORKSPACE;
     return cuda_status(launch_gemv_run(member, gate_streams, num_experts, out_features,
                                        (int)in_features, x_rows, pairs, h, IQK_F32, workspace,

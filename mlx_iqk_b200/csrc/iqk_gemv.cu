@@ -293,21 +293,14 @@ template <typename XT>
 __global__ void __launch_bounds__(256)
 gemv_prep_kernel(const XT *__restrict__ x, int n, int x_rows, const int32_t *__restrict__ sel,
                  const int32_t *__restrict__ tok, int pairs, int num_experts, GemvLayout L,
-                 char *__restrict__ ws, int with_split) {
+                 char *__restrict__ ws) {
     grid_dep_wait();
     grid_dep_launch();
     if ((int)blockIdx.x < x_rows) {
         prep_row<XT>(x, n, blockIdx.x, L, ws);
     } else {
-        // The run kernels cut items only over counters that start from zero:
-        // zeroed here when the workspace holds them, and header word 6 says so.
-        if (with_split) {
-            int32_t *cnt = reinterpret_cast<int32_t *>(ws + L.split_cnt);
-            for (int i = threadIdx.x; i < kMaxSplit * 4; i += blockDim.x) cnt[i] = 0;
-        }
         if (threadIdx.x == 0) {
             int32_t *h = reinterpret_cast<int32_t *>(ws + L.hdr);
-            h[6] = with_split;
             h[8] = 0;  // the run kernels' work counter (items claimed)
             h[9] = 0;  // and the count of their CTAs done (the last one resets both)
         }
@@ -407,7 +400,6 @@ struct GemvArgs {
     GemvLayout L;
     const char *ws;
     int32_t *err;  // device error word (workspace header)
-    int split;     // 1: the grid fits the split slots (kMaxSplit)
     int dynamic;   // 1: CTAs claim whole items from the workspace's work counter
     void *y;
     int y_dtype;
@@ -618,49 +610,26 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
             for (int i = tid; i < row_words; i += blockDim.x) yr[i] = 0;
         }
     }
-    // Work division. Whole items in general; for IQ1_S_R4 (exact integer
-    // partial sums, so the sum over a cut item does not depend on where it is
-    // cut) a wide grid of at most kMaxSplit CTAs with at least one item per
-    // CTA divides the rounds evenly instead: a CTA's first item may start
-    // mid-way (its tail part) and its last end mid-way (its head part), and
-    // the two parts of a cut item meet in split slot blockIdx.x (tail) ==
-    // blockIdx.x + 1 of the CTA before (head). Rounds per CTA are then
-    // items * RPI / grid, within one round of each other, instead of whole
-    // items (3 or 4 of them at B = 8). Measured: IQ1_S_R4 B = 8 70 -> 65.6
-    // us; IQ2_KS (also exact) 38.0 -> 38.7 us at B = 8 and 21.5 -> 23.5 at
-    // B = 4 -- its warps' pace varies more than whole items do, and the cut
-    // items' extra scale-slot loads cost more than the balance gains -- so
-    // IQ2_KS keeps whole items.
-    // Every other launch claims whole items dynamically: each CTA's producer
-    // takes the next item from a counter in the workspace header and hands it
-    // to the compute warps with the item's scale slot. The schedulers favour
-    // low warp slots (measured: warps in slots 0-3 run a round in 0.89 us,
-    // slots 12-15 in 1.17 us), so a static division leaves the slow CTAs
-    // finishing alone; claimed items keep every CTA busy until the work runs
-    // out. The last CTA to finish resets the counter for the next run on the
-    // workspace (runs on one workspace are stream-ordered).
-    constexpr bool kSplittable = !NARROW && !GLU && MEMBER == IQK_IQ1_S_R4;
-    const bool split = kSplittable && a.split && hdr[6] == 1 && items >= (int)gridDim.x;
-    // (more items than CTAs only: the first item of CTA b is item b, claims
-    // start after the first wave, so no claim sits before a CTA's first copy)
-    const bool dyn = !split && a.dynamic && items > (int)gridDim.x;
+    // Work division: whole items. With more than two items per CTA they are
+    // claimed dynamically: CTA b takes item b, then its producer claims the next one
+    // from a counter in the workspace header and hands it to the compute warps
+    // beside the item's scale slot. The schedulers favour low warp slots
+    // (measured: warps in slots 0-3 run a round in 0.89 us, slots 12-15 in
+    // 1.17 us), so a static division leaves the CTAs on high slots finishing
+    // alone (30 % after the rest); claimed items keep every CTA busy until the
+    // work runs out. The last CTA to finish resets the counter for the next
+    // run on the workspace (runs on one workspace are stream-ordered). Each
+    // item's rows are computed by one CTA with exact integer sums, so the
+    // output does not depend on which CTA ran it.
+    // (claiming pays for itself only with several items per CTA: with one or
+    // two, every CTA's closing claim and count would only lengthen the launch)
+    const bool dyn = a.dynamic && items > 2 * (int)gridDim.x;
     int32_t *work_ctr = reinterpret_cast<int32_t *>(const_cast<char *>(a.ws) + a.L.hdr) + 8;
     int32_t *done_ctr = work_ctr + 1;
     int *sitem = abort_flag + 1;  // [2] the item of scale slot 0 / 1 (-1: no more)
-    const int64_t work = split ? (int64_t)items * RPI : items;
-    const int64_t g0 = dyn ? 0 : work * blockIdx.x / gridDim.x;
-    const int64_t g1 = dyn ? work : work * (blockIdx.x + 1) / gridDim.x;
-    if (g0 >= g1) {  // uniform over the CTA
-        if (dyn && tid == 0 && atomicAdd(done_ctr, 1) == (int)gridDim.x - 1) {
-            atomicExch(work_ctr, 0);
-            atomicExch(done_ctr, 0);
-        }
-        return;
-    }
-    const int i0 = (int)(split ? g0 / RPI : g0);
-    const int i1 = (int)(split ? (g1 - 1) / RPI + 1 : g1);
-    const int r_first = split ? (int)(g0 % RPI) : 0;           // first item's first round
-    const int r_last = split ? (int)((g1 - 1) % RPI) + 1 : RPI;  // last item's round end
+    const int i0 = dyn ? 0 : (int)((int64_t)items * blockIdx.x / gridDim.x);
+    const int i1 = dyn ? items : (int)((int64_t)items * (blockIdx.x + 1) / gridDim.x);
+    if (i0 >= i1) return;  // uniform over the CTA (a dynamic launch has items > 0)
     const int t0 = i0 / rblocks, t1 = (i1 - 1) / rblocks;
     const bool cached = !dyn && t1 - t0 < kMaxTiles;
     auto load_tile = [&](int t) -> TileRef {
@@ -673,15 +642,11 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
     __syncthreads();
     auto tile_of = [&](int t) -> TileRef { return cached ? tcache[t - t0] : load_tile(t); };
     const int n_items = i1 - i0;
-    // rounds [round_begin(o), round_end(o)) of the CTA's item ordinal o
-    auto round_begin = [&](int o) { return o == 0 ? r_first : 0; };
-    auto round_end = [&](int o) { return o == n_items - 1 ? r_last : RPI; };
 
     if (wid == kConsumers) {
         // ================= producer warp: TMA / bulk copies into the ring
         int ti = i0 / rblocks, rb = i0 % rblocks;
         int issued = 0, sissued = 0;
-        int jr = 0;  // rounds issued so far: ring slot jr % kStages, phase jr / kStages
         bool ok = true;
         // this lane's scale stream (lanes 1 .. kCount-1; GLU: lanes 17 .. for
         // up's): bytes per row, slot offset
@@ -737,9 +702,8 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
             // item's 16 rows, warp w chunk KQ*r + w
             const int wrow = T.e * out + r0 + (NARROW ? 0 : 16 * (GLU ? (lane & 1) : lane));
             const char *xb = xbuf + T.tok0 * xrow;
-            const int re = round_end(o);
-            for (int r = round_begin(o); r < re; ++r) {
-                const int j = kSplittable ? jr++ : o * RPI + r;
+            for (int r = 0; r < RPI; ++r) {
+                const int j = o * RPI + r;
                 const int slot = j % kStages;
                 if (j >= kStages && !mbar_wait(&empty[slot], ((j / kStages) & 1) ^ 1)) {
                     ok = false;
@@ -912,7 +876,6 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
     };
 
     int ti = i0 / rblocks, rb = i0 % rblocks;
-    int jr = 0;             // rounds consumed so far (the producer's ring order)
     bool prebuilt = false;  // this item's first-round metadata was built during the last item
     for (int o = 0; dyn || o < n_items; ++o) {
         // the item's scale streams (and, claimed dynamically, the item itself)
@@ -937,9 +900,8 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
         const bool nlive = !NARROW && (dyn || (o + 1 < n_items &&
                            rbase < out - (rb + 1 == rblocks ? 0 : rb + 1) * kRows));
         const char *sd = sslots + ((o & 1) * SH::kProj + proj) * SSB;
-        const int rs = round_begin(o), re = round_end(o);
         // metadata buffer of round r: r & 1
-        if (!FLOOR && live && !prebuilt) build_meta(sd, chunk_of(rs), meta_u + (rs & 1) * G::kMetaBytes);
+        if (!FLOOR && live && !prebuilt) build_meta(sd, chunk_of(0), meta_u);
         prebuilt = false;
         __syncwarp();
         uint32_t facc = 0u;  // FLOOR: every word this warp would decode, folded
@@ -948,8 +910,8 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
         double dacc[2] = {0.0, 0.0};  // IQ2_K: rows g, g+8, this lane's sub-blocks
         bool ok = true;
 #pragma unroll 1
-        for (int r = rs; r < re; ++r) {
-            const int j = kSplittable ? jr++ : o * RPI + r;
+        for (int r = 0; r < RPI; ++r) {
+            const int j = o * RPI + r;
             const int slot = j % kStages;
             if (!mbar_wait(&full[slot], (j / kStages) & 1)) {
                 ok = false;
@@ -1106,10 +1068,9 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
                 // loop in program order so its loads and arithmetic can fill
                 // the loop's latency gaps. After a wide item's last round: the
                 // next item's first round, from its scale slot, into buffer 0
-                // (RPI is even and a cut item is never followed by one in
-                // its CTA unless it ends at RPI, so this round reads buffer 1).
+                // (RPI is even, so this round reads buffer 1).
                 if (FLOOR) {
-                } else if (r + 1 < re) {
+                } else if (r + 1 < RPI) {
                     build_meta(sd, chunk_of(r + 1), meta_u + ((r + 1) & 1) * G::kMetaBytes);
                 } else if (nlive && (r & 1) && mbar_wait(&sfull[(o + 1) & 1], ((o + 1) >> 1) & 1)) {
                     const int nitem = dyn ? *(volatile int *)&sitem[(o + 1) & 1] : item + 1;
@@ -1190,78 +1151,31 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
             // ---- item end: this warp holds the whole k range of its 16 rows.
             const int ra = rbase + g;  // item-local row
             double yg, yg8;
-            bool finish = true;  // false: the other part of a cut item stores the rows
-            if (MEMBER == IQK_IQ2_K && !FLOOR) {
+            if (FLOOR) {
+                uint32_t f = MEMBER == IQK_IQ2_K ? (uint32_t)(long long)dacc[0] : (uint32_t)tot[0];
+#pragma unroll
+                for (int o2 = 1; o2 < 32; o2 <<= 1) f += __shfl_xor_sync(0xffffffffu, f, o2);
+                yg = (double)(f & 0xffu);
+                yg8 = (double)((f >> 8) & 0xffu);
+            } else if (MEMBER == IQK_IQ2_K) {
                 // the quad's four sub-block sides, in a fixed order
                 yg = dacc[0] + __shfl_xor_sync(0xffffffffu, dacc[0], 1);
                 yg8 = dacc[1] + __shfl_xor_sync(0xffffffffu, dacc[1], 1);
                 yg += __shfl_xor_sync(0xffffffffu, yg, 2);
                 yg8 += __shfl_xor_sync(0xffffffffu, yg8, 2);
             } else {
-                // exact integer sums of rows g and g + 8 (as doubles, < 2^53),
-                // complete on the lanes with tig == 0
-                double Tg, Tg8;
-                if (FLOOR) {
-                    uint32_t f = MEMBER == IQK_IQ2_K ? (uint32_t)(long long)dacc[0] : (uint32_t)tot[0];
+                int32_t s4[4] = {tot[0], tot[1], tot[2], tot[3]};
+                // lanes tig 0/2 hold planes (0,1) of the two sides, 1/3 plane 2
 #pragma unroll
-                    for (int o2 = 1; o2 < 32; o2 <<= 1) f += __shfl_xor_sync(0xffffffffu, f, o2);
-                    Tg = (double)f;
-                    Tg8 = 0.0;
-                } else {
-                    int32_t s4[4] = {tot[0], tot[1], tot[2], tot[3]};
-                    // lanes tig 0/2 hold planes (0,1) of the two sides, 1/3 plane 2
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) s4[k] += __shfl_down_sync(0xffffffffu, s4[k], 2);
-                    const int32_t n0 = __shfl_down_sync(0xffffffffu, s4[0], 1);
-                    const int32_t n2 = __shfl_down_sync(0xffffffffu, s4[2], 1);
-                    Tg = (double)s4[0] * 65536.0 + (double)s4[1] * 256.0 + (double)n0;
-                    Tg8 = (double)s4[2] * 65536.0 + (double)s4[3] * 256.0 + (double)n2;
-                }
-                if (split && (rs > 0 || re < RPI)) {
-                    // A cut item: both parts leave their rows' sums in the
-                    // slot, then count themselves in; the second to arrive
-                    // adds the other part's sums (exact, so the order of
-                    // arrival cannot change a bit) and stores the rows. No
-                    // part waits for the other.
-                    const bool tail = rs > 0;
-                    const int si = (int)blockIdx.x + (tail ? 0 : 1);
-                    double *slot = reinterpret_cast<double *>(const_cast<char *>(a.ws) + a.L.split) +
-                                   (size_t)si * (2 * kConsumers * 16);
-                    double *mine = slot + ((tail ? 1 : 0) * kConsumers + wid) * 16;
-                    const double *theirs = slot + ((tail ? 0 : 1) * kConsumers + wid) * 16;
-                    int32_t *cnt = reinterpret_cast<int32_t *>(const_cast<char *>(a.ws) + a.L.split_cnt) +
-                                   si * kConsumers + wid;
-                    if (tig == 0) {
-                        __stcg(mine + g, Tg);
-                        __stcg(mine + g + 8, Tg8);
-                    }
-                    __threadfence();
-                    __syncwarp();
-                    int before = 0;
-                    if (lane == 0) before = atomicAdd(cnt, 1);
-                    before = __shfl_sync(0xffffffffu, before, 0);
-                    if (before == 0) {
-                        finish = false;
-                    } else {
-                        __threadfence();
-                        if (tig == 0) {
-                            Tg += __ldcg(theirs + g);
-                            Tg8 += __ldcg(theirs + g + 8);
-                        }
-                        if (lane == 0) atomicExch(cnt, 0);  // ready for the next run on this workspace
-                    }
-                }
-                if (FLOOR) {
-                    const uint32_t f = (uint32_t)(unsigned long long)(long long)Tg;
-                    yg = (double)(f & 0xffu);
-                    yg8 = (double)((f >> 8) & 0xffu);
-                } else {
-                    const uint16_t *dvp = reinterpret_cast<const uint16_t *>(sd + SS::off(SS::kCount - 1));
-                    yg = (double)half_bits_to_float(dvp[ra]) * Tg;
-                    yg8 = (double)half_bits_to_float(dvp[ra + 8]) * Tg8;
-                }
+                for (int k = 0; k < 4; ++k) s4[k] += __shfl_down_sync(0xffffffffu, s4[k], 2);
+                const int32_t n0 = __shfl_down_sync(0xffffffffu, s4[0], 1);
+                const int32_t n2 = __shfl_down_sync(0xffffffffu, s4[2], 1);
+                const double Tg = (double)s4[0] * 65536.0 + (double)s4[1] * 256.0 + (double)n0;
+                const double Tg8 = (double)s4[2] * 65536.0 + (double)s4[3] * 256.0 + (double)n2;
+                const uint16_t *dvp = reinterpret_cast<const uint16_t *>(sd + SS::off(SS::kCount - 1));
+                yg = (double)half_bits_to_float(dvp[ra]) * Tg;
+                yg8 = (double)half_bits_to_float(dvp[ra + 8]) * Tg8;
             }
-            if (finish) {
             float vg = 0.f, vg8 = 0.f;
             const int64_t o0 = (int64_t)T.pair0 * out + r0 + ra;
             const bool ok8 = r0 + ra + 8 < out;
@@ -1322,7 +1236,6 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
                     if (ok8) y[o0 + 8] = __float2bfloat16_rn(vg8);
                 }
             }
-            }  // finish
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sempty[o & 1]);  // the item's scale slot
@@ -1353,9 +1266,6 @@ GemvLayout gemv_layout(int member, int64_t n, int64_t x_rows, int64_t pairs) {
     L.xscale = take(sizeof(int32_t) * (x_rows + 1));
     L.xrow_bytes = 3 * n + n / 2;  // planes [n/64][4][3][16] + block sums [n/32][4] int32
     L.xbuf = take((size_t)(x_rows * L.xrow_bytes));
-    L.total_nosplit = off;
-    L.split = take(sizeof(double) * kMaxSplit * 2 * 4 * 16);
-    L.split_cnt = take(sizeof(int32_t) * kMaxSplit * 4);
     L.total = off;
     return L;
 }
@@ -1414,7 +1324,7 @@ struct PdlLaunch {
 
 cudaError_t launch_gemv_prepare(const void *x, int x_dtype, int64_t x_rows, int n,
                                 int64_t num_experts, const int32_t *sel, const int32_t *tok,
-                                int64_t pairs, void *ws, cudaStream_t stream, bool with_split) {
+                                int64_t pairs, void *ws, cudaStream_t stream) {
     const GemvLayout L = gemv_layout(0, n, x_rows, pairs);
     char *w = static_cast<char *>(ws);
     const size_t hist_bytes = sizeof(int32_t) * (size_t)num_experts;
@@ -1434,8 +1344,7 @@ cudaError_t launch_gemv_prepare(const void *x, int x_dtype, int64_t x_rows, int 
     PdlLaunch pl(pblocks, 256, hist_bytes, stream);
 #define IQK_PREP(T)                                                                          \
     err = cudaLaunchKernelEx(&pl.cfg, gemv_prep_kernel<T>, static_cast<const T *>(x), n,      \
-                             (int)x_rows, sel, tok, (int)pairs, (int)num_experts, L, w,     \
-                             with_split ? 1 : 0)
+                             (int)x_rows, sel, tok, (int)pairs, (int)num_experts, L, w)
     if (x_dtype == IQK_F32) IQK_PREP(float);
     else if (x_dtype == IQK_F16) IQK_PREP(__half);
     else IQK_PREP(__nv_bfloat16);
@@ -1474,8 +1383,7 @@ static cudaError_t encode_qs_map(CUtensorMap *map, const void *qs, int64_t rows,
 cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_experts,
                             int64_t out_features, int n, int64_t x_rows, int64_t pairs, void *y,
                             int y_dtype, const void *ws, cudaStream_t stream, int num_sms,
-                            bool floor, const void *const *up_streams, const float *router_weight,
-                            bool allow_split) {
+                            bool floor, const void *const *up_streams, const float *router_weight) {
     const int variant = up_streams ? kVarGlu : floor ? kVarFloor : kVarDecode;
     const GemvLayout L = gemv_layout(member, n, x_rows, pairs);
     GemvArgs ga{};
@@ -1557,7 +1465,6 @@ cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_
     const int64_t cap = (int64_t)num_sms * per_sm;
     int64_t blocks = max_items < cap ? max_items : cap;
     if (blocks < 1) blocks = 1;
-    ga.split = allow_split && blocks <= kMaxSplit ? 1 : 0;  // one split slot per CTA boundary
     ga.dynamic = 1;
     PdlLaunch pl((unsigned)blocks, kThreads, gemv_smem_for(member, n, narrow, glu), stream);
     err = cudaLaunchKernelEx(&pl.cfg, gemv_fn(member, n, narrow, variant), ga, map, map2);

@@ -18,23 +18,15 @@ struct TileRef {
 static_assert(sizeof(TileRef) == 32, "TileRef is 32 bytes");
 
 // Byte offsets inside the caller's workspace (all 256-byte aligned).
-// A wide decode grid of at most this many CTAs divides its work by rounds, so
-// one item can be cut between two neighbouring CTAs; each cut has one slot.
-constexpr int kMaxSplit = 448;
-
 struct GemvLayout {
-    size_t hdr;     // int32[16]: [0] error bits, [3] routable pairs (work tiles)
+    size_t hdr;     // int32[16]: [0] error bits, [3] routable pairs (work tiles),
+                    //   [8] items claimed, [9] CTAs done (the run kernels' counters)
     size_t order;   // int32[P]      pair ids bucketed by expert, unroutable ones last
     size_t ptok;    // int32[P]      activation row of each pair
     size_t tiles1;  // TileRef[P]    one work tile per routable pair, grouped by expert
     size_t xscale;  // int32[x_rows] power-of-two exponent S of each row
     size_t xbuf;    // per row: int8 planes [n/32][3][4][8], int32 block sums [n/32][4]
-    // Optional tail (a workspace may end before it; the run then divides
-    // whole items): the split slots of a wide decode grid.
-    size_t split;   // double[kMaxSplit][2 halves][4 warps][16 rows]  cut items' row sums
-    size_t split_cnt;  // int32[kMaxSplit][4 warps]  parts arrived (zeroed by the prepare)
     int64_t xrow_bytes;
-    size_t total_nosplit;  // bytes without the split slots
     size_t total;
 };
 
@@ -42,13 +34,12 @@ GemvLayout gemv_layout(int member, int64_t n, int64_t x_rows, int64_t pairs);
 int gemv_smem_for(int member, int n, bool narrow);
 cudaError_t launch_gemv_prepare(const void *x, int x_dtype, int64_t x_rows, int n,
                                 int64_t num_experts, const int32_t *sel, const int32_t *tok,
-                                int64_t pairs, void *ws, cudaStream_t stream,
-                                bool with_split = false);
+                                int64_t pairs, void *ws, cudaStream_t stream);
 cudaError_t launch_gemv_run(int member, const void *const *streams, int64_t num_experts,
                             int64_t out_features, int n, int64_t x_rows, int64_t pairs, void *y,
                             int y_dtype, const void *ws, cudaStream_t stream, int num_sms,
                             bool floor = false, const void *const *up_streams = nullptr,
-                            const float *router_weight = nullptr, bool allow_split = false);
+                            const float *router_weight = nullptr);
 cudaError_t launch_bounded_wait_check(int64_t limit_ns, int32_t *flags, cudaStream_t stream);
 cudaError_t launch_pack(int member, const void *wire, int64_t rows, int n,
                         void *const *streams, cudaStream_t stream, int num_sms);

@@ -110,7 +110,7 @@ int iqk_gemv_static(int member, const void *x, int x_dtype, int64_t x_rows,
         return IQK_ERR_GEOMETRY;
     // Checked before anything touches the device, so an oversized call fails
     // the same way on every device and never resolves the scratch.
-    if (gemv_layout(member, in_features, x_rows, pairs).total_nosplit > kStaticScratchBytes)
+    if (gemv_layout(member, in_features, x_rows, pairs).total > kStaticScratchBytes)
         return IQK_ERR_WORKSPACE;
     if (pairs == 0) return iqk_gemv(member, x, x_dtype, x_rows, streams, num_experts,
                                     out_features, in_features, sel, tok, pairs, y, y_dtype,
@@ -131,7 +131,7 @@ int iqk_gemv_static_read_error(int64_t in_features, int64_t x_rows, int64_t pair
     if (in_features != 2048 && in_features != 4096) return IQK_ERR_WIDTH;
     if (x_rows < 0 || pairs < 0 || x_rows > (1 << 24) || pairs > (1 << 24))
         return IQK_ERR_GEOMETRY;
-    if (gemv_layout(IQK_IQ2_KS, in_features, x_rows, pairs).total_nosplit > kStaticScratchBytes)
+    if (gemv_layout(IQK_IQ2_KS, in_features, x_rows, pairs).total > kStaticScratchBytes)
         return IQK_ERR_WORKSPACE;
     void *scratch = nullptr;
     if (scratch_for_current_device(&scratch) != cudaSuccess) {
