@@ -342,8 +342,9 @@ dense_gemv_kernel(DenseStreams st, int n, int out, const __half *__restrict__ x,
     auto tile_of = [&](int it) { return ((int)blockIdx.x + it * (int)gridDim.x) * RT + rt; };
     // issue the copies of step f: its code words and high bits into slot f % D,
     // and at a row tile's first step that tile's scale bytes into buffer it & 1
-    auto issue = [&](int f) {
-        const int it = f / steps, sidx = f - it * steps;
+    // (step f = it * steps + sidx; both walks below advance (it, sidx) by
+    // one step at a time instead of dividing)
+    auto issue = [&](int f, int it, int sidx) {
         const int tile = tile_of(it);
         if (tile >= tiles) return;
         const int64_t r0 = (int64_t)tile * kDenseRows;
@@ -419,21 +420,34 @@ dense_gemv_kernel(DenseStreams st, int n, int out, const __half *__restrict__ x,
         for (int q = 0; q < NT; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
         // prologue: D - 1 steps in flight
 #pragma unroll 1
+        int iit = 0, isidx = 0;  // the issue walk: the next step to copy
         for (int f = 0; f < D - 1; ++f) {
-            if (f < total) issue(f);
+            if (f < total) issue(f, iit, isidx);
             cp_async_commit();
+            if (++isidx == steps) {
+                isidx = 0;
+                ++iit;
+            }
         }
         float dra = 0.f, drb = 0.f;
 #pragma unroll 1
+        int it = 0, sidx = -1;  // the compute walk
         for (int f = 0; f < total; ++f) {
-            const int it = f / steps, sidx = f - it * steps;
+            if (++sidx == steps) {
+                sidx = 0;
+                ++it;
+            }
             const int tile = tile_of(it);
             const bool live = tile < tiles;
             const int64_t ra = (int64_t)tile * kDenseRows + g, rb = ra + 8;
             // the slot of step f - 1 is free again: refill it with step f + D - 1
             __syncwarp();
-            if (f + D - 1 < total) issue(f + D - 1);
+            if (f + D - 1 < total) issue(f + D - 1, iit, isidx);
             cp_async_commit();
+            if (++isidx == steps) {
+                isidx = 0;
+                ++iit;
+            }
             cp_async_wait<D - 1>();
             __syncwarp();
             if (live) {
