@@ -206,7 +206,6 @@ __device__ __forceinline__ void mma_f16_acc(float d[4], const uint32_t a[4], uin
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-constexpr int kDenseWarps = 4;
 constexpr int kDenseRows = 16;
 
 // GEMV value table in shared memory, one copy per lane (entry e of lane l at
@@ -419,8 +418,8 @@ dense_gemv_kernel(DenseStreams st, int n, int out, const __half *__restrict__ x,
 #pragma unroll
         for (int q = 0; q < NT; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
         // prologue: D - 1 steps in flight
-#pragma unroll 1
         int iit = 0, isidx = 0;  // the issue walk: the next step to copy
+#pragma unroll 1
         for (int f = 0; f < D - 1; ++f) {
             if (f < total) issue(f, iit, isidx);
             cp_async_commit();
@@ -430,8 +429,8 @@ dense_gemv_kernel(DenseStreams st, int n, int out, const __half *__restrict__ x,
             }
         }
         float dra = 0.f, drb = 0.f;
-#pragma unroll 1
         int it = 0, sidx = -1;  // the compute walk
+#pragma unroll 1
         for (int f = 0; f < total; ++f) {
             if (++sidx == steps) {
                 sidx = 0;
