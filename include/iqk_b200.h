@@ -399,7 +399,7 @@ int iqk_gemv_static_read_error(int64_t in_features, int64_t x_rows, int64_t pair
  *               dv f16[o,n/256]}
  *
  * in_features is 1024, 2048, 4096 or 8192 (src/mlx_iqk/dense_kernels.py:56).
- * qs must be 16-byte aligned, qh 8-byte aligned.
+ * Every stream and the GEMV's x must be 16-byte aligned (IQK_ERR_ALIGNMENT).
  *
  * iqk_dense_dequant: rows [row_start, row_start + rows) into dst[rows, n] in
  * f32, f16 or bf16, bit for bit the reference decode rounded once

@@ -50,17 +50,16 @@ bool dense_member_ok(int m) {
 }
 bool dense_width_ok(int64_t n) { return n == 1024 || n == 2048 || n == 4096 || n == 8192; }
 
-// Dense streams: present; qs 16-byte aligned (the kernels read four code words
-// at once), qh 8-byte aligned, the rest at their element size.
+// Dense streams: present and 16-byte aligned (the GEMV stages every stream's
+// rows with 16-byte asynchronous copies; rows of every width are whole
+// 16-byte multiples, so aligned bases keep every copy aligned).
 int check_dense_streams(int member, const void *const *streams) {
     if (!streams) return IQK_ERR_ARGUMENT;
     const int count = member == IQK_IQ4_KS ? 3 : member == IQK_IQ5_K ? 6 : 5;
-    for (int i = 0; i < count; ++i)
+    for (int i = 0; i < count; ++i) {
         if (!streams[i]) return IQK_ERR_ARGUMENT;
-    if (!aligned(streams[0], 16)) return IQK_ERR_ALIGNMENT;
-    if ((member == IQK_IQ5_K || member == IQK_IQ6_K) && !aligned(streams[1], 8))
-        return IQK_ERR_ALIGNMENT;
-    if (!aligned(streams[count - 1], member == IQK_IQ4_KS ? 4 : 2)) return IQK_ERR_ALIGNMENT;
+        if (!aligned(streams[i], 16)) return IQK_ERR_ALIGNMENT;
+    }
     return IQK_OK;
 }
 
@@ -120,7 +119,7 @@ int iqk_dense_gemv(int member, const void *x, int64_t tokens, const void *const 
     if (y_dtype != IQK_F16 && y_dtype != IQK_F32) return IQK_ERR_ARGUMENT;
     if (tokens == 0) return IQK_OK;
     if (!x || !y) return IQK_ERR_ARGUMENT;
-    if (!aligned(x, 4) || !aligned(y, 4)) return IQK_ERR_ALIGNMENT;
+    if (!aligned(x, 16) || !aligned(y, 4)) return IQK_ERR_ALIGNMENT;  // x: 8-byte fragment loads
     const int st = check_dense_streams(member, streams);
     if (st != IQK_OK) return st;
     return cuda_status(launch_dense_gemv(member, streams, (int)in_features, (int)out_features, x,

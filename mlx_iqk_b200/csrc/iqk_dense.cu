@@ -579,6 +579,319 @@ dense_gemv_kernel(DenseStreams st, int n, int out, const __half *__restrict__ x,
     }
 }
 
+// ---- IQ4 members: the pair table at a fixed shared-window address.
+//
+// IQ4_KS and IQ4_K look up one f16 pair per code byte. With the table's
+// 64 KB at shared address 64 KB, entry (code byte c, alphabet a) of lane l
+// sits at 64 KB | c << 8 | a << 7 | l << 2, so one byte permute of the code
+// word with a per-lane base word forms each lookup address. That fixes the
+// CTA: one per SM, 16 warps, the code rings below 64 KB, the table at
+// [64 KB, 128 KB), the scale buffers and the k-part reduction area above.
+//
+// Each warp walks 16-row tiles over 1024 weights of k (KW = n / 1024 warps
+// share a tile, RT = 16 / KW tiles per CTA iteration) in 64-weight steps. In
+// one MMA a lane takes two code bytes of a row, so the MMA's logical k pairs
+// (2t, 2t+1) and (2t+8, 2t+9) map to four consecutive weights of the step:
+//   IQ4_KS  MMA (s, m) of 32-weight sub-block s: bytes 2m, 2m+1 of word
+//           4s + t, weights 32s + 8t + 4m .. + 3 (two MMAs per scale);
+//   IQ4_K   MMA s of 16-weight sub-block s: bytes 2(t&1), 2(t&1)+1 of word
+//           2s + (t>>1), weights 16s + 4t .. + 3 (one MMA per scale);
+// so a lane's activation fragment is one 8-byte load.
+constexpr uint32_t kPairTab = 65536;  // shared-window address of the pair table
+constexpr int kP4Warps = 16;
+constexpr int kP4Steps = 16;  // 64-weight steps of a warp's 1024-weight k part
+
+template <int M, int NT> __host__ __device__ inline int p4_tail_bytes(int n) {
+    const ScaleRows sr = scale_rows(M, 1024);
+    return kP4Warps * 2 * sr.total + (n > 1024 ? 2 * kP4Warps * 32 * NT * 16 : 0);
+}
+
+__device__ __forceinline__ void sts32(uint32_t a, uint32_t v) {
+    asm volatile("st.shared.u32 [%0], %1;\n" ::"r"(a), "r"(v));
+}
+__device__ __forceinline__ void sts128(uint32_t a, float4 v) {
+    asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};\n" ::"r"(a), "f"(v.x), "f"(v.y), "f"(v.z),
+                 "f"(v.w));
+}
+__device__ __forceinline__ float4 lds128f(uint32_t a) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void bar_tile(int id, int threads) {
+    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory");
+}
+// the lookup address of code byte j of word w: 64 KB | byte << 8 | base byte 0
+__device__ __forceinline__ uint32_t pair_addr(uint32_t w, uint32_t base, uint32_t sel) {
+    return __byte_perm(w, base, sel);
+}
+
+template <int M, int NT, int D>
+__global__ void __launch_bounds__(kP4Warps * 32, 1)
+dense_gemv_p4_kernel(DenseStreams st, int n, int out, const __half *__restrict__ x, int tokens,
+                     void *__restrict__ y, int y_dtype) {
+    static_assert(M == IQK_IQ4_KS || M == IQK_IQ4_K, "pair-table members only");
+    extern __shared__ __align__(128) uint8_t p4sm[];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int KW = n >> 10, RT = kP4Warps / KW;
+    const int rt = wid / KW, kw = wid % KW;
+    const int kbeg = kw * 1024;
+    const ScaleRows sr = scale_rows(M, 1024);
+    const uint32_t s0 = (uint32_t)__cvta_generic_to_shared(p4sm);
+    uint32_t dyn;
+    asm("mov.u32 %0, %%dynamic_smem_size;\n" : "=r"(dyn));
+    const uint32_t ring0 = (s0 + 127u) & ~127u;
+    const uint32_t tail = kPairTab + 65536u;
+    // the rings must end below the table and the tail lie inside the
+    // allocation (the host sizes it so); otherwise the outputs are NaN
+    if (ring0 + (uint32_t)(kP4Warps * D * 512) > kPairTab ||
+        s0 + dyn < tail + (uint32_t)p4_tail_bytes<M, NT>(n)) {
+        const int64_t total = (int64_t)tokens * out;
+        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+             i += (int64_t)gridDim.x * blockDim.x) {
+            if (y_dtype == IQK_F32) static_cast<float *>(y)[i] = __int_as_float(0x7fc00000);
+            else static_cast<__half *>(y)[i] = __ushort_as_half((unsigned short)0x7e00u);
+        }
+        return;
+    }
+    // the table: word i is entry (code byte i >> 6, alphabet (i >> 5) & 1), lane i & 31
+    for (int i = threadIdx.x; i < 16384; i += kP4Warps * 32) {
+        const int c = i >> 6, a = (i >> 5) & 1;
+        const __half v0 = __float2half_rn((float)c_iq4k[(a << 4) | (c & 15)]);
+        const __half v1 = __float2half_rn((float)c_iq4k[(a << 4) | (c >> 4)]);
+        sts32(kPairTab + 4u * (uint32_t)i,
+              (uint32_t)__half_as_ushort(v0) | ((uint32_t)__half_as_ushort(v1) << 16));
+    }
+    const uint32_t ring = ring0 + (uint32_t)wid * (D * 512);
+    const uint32_t scb = tail + (uint32_t)wid * 2 * sr.total;  // two scale buffers
+    const uint32_t red0 = tail + (uint32_t)(kP4Warps * 2 * sr.total);
+    const uint32_t lbase = kPairTab | ((uint32_t)lane << 2);
+    // code words of rows g, g+8 in a slot: row r's 16-byte halves swapped when
+    // (r >> 2) is odd, so the eight rows a load touches fall in distinct banks
+    const uint32_t sw = (uint32_t)((g >> 2) & 1);
+    __syncthreads();
+
+    const int tiles = out / kDenseRows;
+    const int groups = (tiles + RT - 1) / RT;
+    const int iters = (int)blockIdx.x < groups ? (groups - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int total = iters * kP4Steps;
+    auto tile_of = [&](int it) { return ((int)blockIdx.x + it * (int)gridDim.x) * RT + rt; };
+    auto issue = [&](int f, int it, int sidx) {
+        const int tile = tile_of(it);
+        if (tile >= tiles) return;
+        const int64_t r0 = (int64_t)tile * kDenseRows;
+        const int k0 = kbeg + 64 * sidx;
+        const uint32_t slot = ring + (uint32_t)(f % D) * 512u;
+        {
+            const int row = lane >> 1, half = lane & 1;
+            cp_async(slot + (uint32_t)(row * 32 + ((half ^ ((row >> 2) & 1)) * 16)),
+                     st.qs + (r0 + row) * (n / 8) + (k0 >> 3) + 4 * half, 16);
+        }
+        if (sidx == 0 && lane < 16) {
+            const uint32_t b = scb + (uint32_t)(it & 1) * sr.total;
+            const int64_t row = r0 + lane;
+            auto piece = [&](uint32_t dst, const uint8_t *src, int bytes) {
+                for (int o = 0; o < bytes; o += 16)
+                    cp_async(dst + o, src + o, bytes - o >= 16 ? 16 : bytes - o);
+            };
+            piece(b + lane * sr.scl, st.scl + row * (n / 32) + kbeg / 32, sr.scl);
+            if (M == IQK_IQ4_K) {
+                piece(b + sr.off_sch + lane * sr.sch, st.sch + row * (n / 64) + kbeg / 64, sr.sch);
+                piece(b + sr.off_sex + lane * sr.sex, st.sex + row * (n / 128) + kbeg / 128, sr.sex);
+                piece(b + sr.off_dv + lane * sr.dv,
+                      reinterpret_cast<const uint8_t *>(static_cast<const uint16_t *>(st.dv) +
+                                                        row * (n / 256) + kbeg / 256),
+                      sr.dv);
+            }
+        }
+    };
+
+    for (int t0 = 0; t0 < tokens; t0 += 8 * NT) {
+        // B column g of token tile q: token t0 + 8q + g (clamped: columns
+        // past the last token are computed and never stored)
+        const __half *xq[NT];
+#pragma unroll
+        for (int q = 0; q < NT; ++q) {
+            const int tk = min(t0 + 8 * q + g, tokens - 1);
+            xq[q] = x + (int64_t)tk * n + kbeg + (M == IQK_IQ4_KS ? 8 * t : 4 * t);
+        }
+        float acc[NT][4];
+#pragma unroll
+        for (int q = 0; q < NT; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
+        int iit = 0, isidx = 0;  // the issue walk
+#pragma unroll 1
+        for (int f = 0; f < D - 1; ++f) {
+            if (f < total) issue(f, iit, isidx);
+            cp_async_commit();
+            if (++isidx == kP4Steps) {
+                isidx = 0;
+                ++iit;
+            }
+        }
+        float drow = 0.f;  // IQ4_KS: the row scale of row lane & 15
+        int it = 0, sidx = -1;  // the compute walk
+#pragma unroll 1
+        for (int f = 0; f < total; ++f) {
+            if (++sidx == kP4Steps) {
+                sidx = 0;
+                ++it;
+            }
+            const int tile = tile_of(it);
+            const bool live = tile < tiles;
+            const int64_t r0 = (int64_t)tile * kDenseRows;
+            __syncwarp();
+            if (f + D - 1 < total) issue(f + D - 1, iit, isidx);
+            cp_async_commit();
+            if (++isidx == kP4Steps) {
+                isidx = 0;
+                ++iit;
+            }
+            cp_async_wait<D - 1>();
+            __syncwarp();
+            if (live) {
+                const uint32_t slot = ring + (uint32_t)(f % D) * 512u;
+                const uint32_t b = scb + (uint32_t)(it & 1) * sr.total;
+                const int lr = lane & 15, hs = lane >> 4;  // scale lane: row, sub-block parity
+                const int kx = 64 * sidx;
+                if (M == IQK_IQ4_KS) {
+                    if (sidx == 0) drow = __ldg(static_cast<const float *>(st.dv) + r0 + lr);
+                    // dl of (row lr, sub-block hs), alphabet bit in the lowest mantissa bit
+                    const uint32_t v = lds8(b + lr * sr.scl + 2 * sidx + hs);
+                    const float dl = __fmul_rn(drow, (float)((int)(v & 254u) - 127));
+                    const float dm = __int_as_float((__float_as_int(dl) & ~1) | (int)(v & 1u));
+                    const uint32_t ra = slot + (uint32_t)g * 32u + 4u * (uint32_t)t;
+                    const uint32_t wa[2] = {lds32(ra + 16u * sw), lds32(ra + 16u * (sw ^ 1u))};
+                    const uint32_t wb[2] = {lds32(ra + 256u + 16u * sw), lds32(ra + 256u + 16u * (sw ^ 1u))};
+#pragma unroll
+                    for (int s = 0; s < 2; ++s) {
+                        const float dla = __shfl_sync(0xffffffffu, dm, 16 * s + g);
+                        const float dlb = __shfl_sync(0xffffffffu, dm, 16 * s + 8 + g);
+                        const uint32_t la = lbase | (((uint32_t)__float_as_int(dla) & 1u) << 7);
+                        const uint32_t lb = lbase | (((uint32_t)__float_as_int(dlb) & 1u) << 7);
+                        float d[NT][4];
+#pragma unroll
+                        for (int m = 0; m < 2; ++m) {
+                            uint32_t A[4];
+                            A[0] = lds32(pair_addr(wa[s], la, 0x7604u | (2u * m) << 4));
+                            A[1] = lds32(pair_addr(wb[s], lb, 0x7604u | (2u * m) << 4));
+                            A[2] = lds32(pair_addr(wa[s], la, 0x7604u | (2u * m + 1u) << 4));
+                            A[3] = lds32(pair_addr(wb[s], lb, 0x7604u | (2u * m + 1u) << 4));
+#pragma unroll
+                            for (int q = 0; q < NT; ++q) {
+                                const uint2 bx = __ldg(reinterpret_cast<const uint2 *>(xq[q] + kx + 32 * s + 4 * m));
+                                if (m == 0) {
+                                    d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0.f;
+                                    mma_f16(d[q], A, bx.x, bx.y);
+                                } else {
+                                    mma_f16_acc(d[q], A, bx.x, bx.y);
+                                }
+                            }
+                        }
+#pragma unroll
+                        for (int q = 0; q < NT; ++q) {
+                            acc[q][0] = fmaf(dla, d[q][0], acc[q][0]);
+                            acc[q][1] = fmaf(dla, d[q][1], acc[q][1]);
+                            acc[q][2] = fmaf(dlb, d[q][2], acc[q][2]);
+                            acc[q][3] = fmaf(dlb, d[q][3], acc[q][3]);
+                        }
+                    }
+                } else {
+                    // dl of (row lr, sub-blocks hs and 2 + hs of the step)
+                    const uint32_t lo2 = lds16(b + lr * sr.scl + 2 * sidx);  // sub-blocks 4sidx .. +3
+                    const uint32_t hi = lds8(b + sr.off_sch + lr * sr.sch + sidx);
+                    const uint32_t ex = lds8(b + sr.off_sex + lr * sr.sex + (sidx >> 1)) >> (4 * (sidx & 1));
+                    const float d0 = __half2float(__ushort_as_half(
+                        (unsigned short)lds16(b + sr.off_dv + lr * sr.dv + 2 * (sidx >> 2))));
+                    float dm[2];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const int ls = 2 * u + hs;  // sub-block of the step
+                        const int idx = (int)(((lo2 >> (4 * ls)) & 15u) | (((hi >> (2 * ls)) & 3u) << 4)) - 32;
+                        const float dl = __fmul_rn(d0, (float)idx);
+                        dm[u] = __int_as_float((__float_as_int(dl) & ~1) | (int)((ex >> ls) & 1u));
+                    }
+                    const uint32_t ra = slot + (uint32_t)g * 32u + 4u * (uint32_t)(t >> 1);
+                    const uint32_t sel0 = 0x7604u | ((uint32_t)(2 * (t & 1)) << 4);
+                    const uint32_t sel1 = sel0 + 0x10u;
+#pragma unroll
+                    for (int s = 0; s < 4; ++s) {
+                        // word 2s + (t >> 1) of rows g, g + 8
+                        const uint32_t wo = 16u * ((uint32_t)(s >> 1) ^ sw) + 8u * (uint32_t)(s & 1);
+                        const uint32_t wa = lds32(ra + wo), wb = lds32(ra + 256u + wo);
+                        const float dla = __shfl_sync(0xffffffffu, dm[s >> 1], 16 * (s & 1) + g);
+                        const float dlb = __shfl_sync(0xffffffffu, dm[s >> 1], 16 * (s & 1) + 8 + g);
+                        const uint32_t la = lbase | (((uint32_t)__float_as_int(dla) & 1u) << 7);
+                        const uint32_t lb = lbase | (((uint32_t)__float_as_int(dlb) & 1u) << 7);
+                        uint32_t A[4];
+                        A[0] = lds32(pair_addr(wa, la, sel0));
+                        A[1] = lds32(pair_addr(wb, lb, sel0));
+                        A[2] = lds32(pair_addr(wa, la, sel1));
+                        A[3] = lds32(pair_addr(wb, lb, sel1));
+#pragma unroll
+                        for (int q = 0; q < NT; ++q) {
+                            const uint2 bx = __ldg(reinterpret_cast<const uint2 *>(xq[q] + kx + 16 * s));
+                            float d[4] = {0.f, 0.f, 0.f, 0.f};
+                            mma_f16(d, A, bx.x, bx.y);
+                            acc[q][0] = fmaf(dla, d[0], acc[q][0]);
+                            acc[q][1] = fmaf(dla, d[1], acc[q][1]);
+                            acc[q][2] = fmaf(dlb, d[2], acc[q][2]);
+                            acc[q][3] = fmaf(dlb, d[3], acc[q][3]);
+                        }
+                    }
+                }
+            }
+            if (sidx + 1 < kP4Steps) continue;
+            // end of the iteration's row tiles: each tile's KW k parts meet in
+            // its first warp, added in k order (reduction area by iteration
+            // parity, so one barrier per iteration suffices)
+            if (KW > 1) {
+                const uint32_t rp = red0 + (uint32_t)((it & 1) * kP4Warps) * (32u * NT * 16u);
+                if (kw > 0) {
+#pragma unroll
+                    for (int q = 0; q < NT; ++q)
+                        sts128(rp + ((uint32_t)wid * 32u + lane) * (NT * 16u) + 16u * q,
+                               make_float4(acc[q][0], acc[q][1], acc[q][2], acc[q][3]));
+                }
+                bar_tile(1 + rt, KW * 32);
+                if (kw == 0 && live) {
+                    for (int w = 1; w < KW; ++w) {
+#pragma unroll
+                        for (int q = 0; q < NT; ++q) {
+                            const float4 v = lds128f(rp + ((uint32_t)(wid + w) * 32u + lane) * (NT * 16u) + 16u * q);
+                            acc[q][0] += v.x;
+                            acc[q][1] += v.y;
+                            acc[q][2] += v.z;
+                            acc[q][3] += v.w;
+                        }
+                    }
+                }
+            }
+            if (kw == 0 && live) {
+                // D fragment: d0 = (row g, token 2t), d1 = (row g, 2t+1), d2/d3 rows g+8
+#pragma unroll
+                for (int q = 0; q < NT; ++q) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int tk = t0 + 8 * q + 2 * t + (i & 1);
+                        const int64_t row = r0 + g + (i < 2 ? 0 : 8);
+                        if (tk < tokens) {
+                            const int64_t o = (int64_t)tk * out + row;
+                            if (y_dtype == IQK_F32) static_cast<float *>(y)[o] = acc[q][i];
+                            else static_cast<__half *>(y)[o] = __float2half_rn(acc[q][i]);
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < NT; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
+        }
+        cp_async_wait<0>();
+        __syncthreads();
+    }
+}
+
 template <int M> DenseStreams dense_streams(const void *const *s) {
     DenseStreams st{};
     st.qs = static_cast<const uint32_t *>(s[0]);
@@ -637,6 +950,35 @@ cudaError_t gemv_launch(const DenseStreams &st, int n, int out, const __half *xh
     return cudaGetLastError();
 }
 
+template <int M, int NT>
+cudaError_t p4_launch(const DenseStreams &st, int n, int out, const __half *xh, int tokens,
+                      void *y, int y_dtype, cudaStream_t stream, int dev) {
+    constexpr int D = 7;  // ring slots a warp: 16 x 7 x 512 B end below the table
+    // per device: the shared memory reserved below a CTA's own (+1; 0 = not
+    // yet queried), which places the dynamic allocation in the window
+    static int reserved[64] = {};
+    int &rs = reserved[dev & 63];
+    if (rs == 0) {
+        int v = 0;
+        cudaError_t e = cudaDeviceGetAttribute(&v, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(dense_gemv_p4_kernel<M, NT, D>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(kPairTab + 65536u) + p4_tail_bytes<M, NT>(8192) - v);
+        if (e != cudaSuccess) return e;
+        rs = v + 1;
+    }
+    const int smem = (int)(kPairTab + 65536u) + p4_tail_bytes<M, NT>(n) - (rs - 1);
+    int sms = 148;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
+    const int RT = kP4Warps / (n >> 10);
+    const int groups = (out / kDenseRows + RT - 1) / RT;
+    const int grid = groups < sms ? groups : sms;
+    dense_gemv_p4_kernel<M, NT, D><<<grid, kP4Warps * 32, smem, stream>>>(st, n, out, xh, tokens, y,
+                                                                          y_dtype);
+    return cudaGetLastError();
+}
+
 template <int M>
 cudaError_t gemv_m(const void *const *s, int n, int out, const void *x, int tokens, void *y,
                    int y_dtype, cudaStream_t stream) {
@@ -644,15 +986,20 @@ cudaError_t gemv_m(const void *const *s, int n, int out, const void *x, int toke
     const __half *xh = static_cast<const __half *>(x);
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
-    // the deepest ring (8, 6 or 4 slots a warp) at which two CTAs still fit
-    // on an SM (228 KB: the dynamic part, the 8 KB reduction buffer, 1 KB
-    // reserved per CTA)
-    constexpr int kBudget = 104 * 1024;
-    const int D = dense_gemv_smem<M>(n, 8) <= kBudget ? 8 : dense_gemv_smem<M>(n, 6) <= kBudget ? 6 : 4;
+    if constexpr (M == IQK_IQ4_KS || M == IQK_IQ4_K) {
+        return tokens <= 8 ? p4_launch<M, 1>(st, n, out, xh, tokens, y, y_dtype, stream, dev)
+                           : p4_launch<M, 2>(st, n, out, xh, tokens, y, y_dtype, stream, dev);
+    } else {
+        // the deepest ring (8, 6 or 4 slots a warp) at which two CTAs still fit
+        // on an SM (228 KB: the dynamic part, the 8 KB reduction buffer, 1 KB
+        // reserved per CTA)
+        constexpr int kBudget = 104 * 1024;
+        const int D = dense_gemv_smem<M>(n, 8) <= kBudget ? 8 : dense_gemv_smem<M>(n, 6) <= kBudget ? 6 : 4;
 #define IQK_DG(NT_, D_) gemv_launch<M, NT_, D_>(st, n, out, xh, tokens, y, y_dtype, stream, dev)
-    if (tokens <= 8) return D == 8 ? IQK_DG(1, 8) : D == 6 ? IQK_DG(1, 6) : IQK_DG(1, 4);
-    return D == 8 ? IQK_DG(2, 8) : D == 6 ? IQK_DG(2, 6) : IQK_DG(2, 4);
+        if (tokens <= 8) return D == 8 ? IQK_DG(1, 8) : D == 6 ? IQK_DG(1, 6) : IQK_DG(1, 4);
+        return D == 8 ? IQK_DG(2, 8) : D == 6 ? IQK_DG(2, 6) : IQK_DG(2, 4);
 #undef IQK_DG
+    }
 }
 
 }  // namespace

@@ -129,6 +129,8 @@ def check_dense_streams(member: str, streams: dict, out_features: int,
             raise IqkDenseError(f"stream {name} must be {dtypes[name].name}, got {value.dtype}")
         if not value.is_contiguous():
             raise IqkDenseError(f"stream {name} must be contiguous")
+        if value.data_ptr() % 16:
+            raise IqkDenseError(f"stream {name} must start on a 16-byte boundary")
         if dev is None:
             dev = value.device
         elif value.device != dev:
@@ -141,7 +143,10 @@ def _tokens_view(x: torch.Tensor, in_features: int) -> torch.Tensor:
     xt = x.reshape(-1, in_features)
     if xt.dtype != torch.float16:
         xt = xt.to(torch.float16)
-    return xt.contiguous()
+    xt = xt.contiguous()
+    if xt.data_ptr() % 16:  # the C ABI takes 16-byte aligned activations
+        xt = xt.clone()
+    return xt
 
 
 def dense_gemv(member: str, x: torch.Tensor, streams: dict, out_features: int,

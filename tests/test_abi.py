@@ -66,6 +66,28 @@ def test_host_side_rejections_need_no_device():
     assert lib.iqk_gemv_prepare(None, 9, 1, 2048, 8, None, None, 6, None, 0, None) == 4
 
 
+
+def test_dense_alignment_rejections_need_no_device():
+    """Every dense stream and the GEMV's activations must start on a 16-byte
+    boundary (the GEMV stages stream rows with 16-byte asynchronous copies and
+    loads 8-byte activation fragments); the ABI refuses others before any
+    CUDA call."""
+    lib = K.library()
+    ok = [0x10000 * (i + 1) for i in range(5)]  # aligned stand-ins, never dereferenced
+
+    def gemv(x, streams, member=4):
+        arr = (ctypes.c_void_p * 5)(*streams)
+        return lib.iqk_dense_gemv(member, x, 1, arr, 16, 1024, 0x90000, 1, None)
+
+    assert gemv(0x80008, ok) == 5  # x 8-byte aligned only
+    for i in range(5):  # IQ4_K has five streams: qs, scl, sch, sex, dv
+        bad = list(ok)
+        bad[i] += 8
+        assert gemv(0x80000, bad) == 5, i
+        arr = (ctypes.c_void_p * 5)(*bad)
+        assert lib.iqk_dense_dequant(4, arr, 16, 1024, 0, 16, 1, 0x90000, None) == 5, i
+
+
 # -- Python layer: geometry guards and the stream contract (CPU tensors) -----
 
 
