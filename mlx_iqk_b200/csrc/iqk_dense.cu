@@ -26,14 +26,18 @@
 // word 32 e + l: no bank conflicts whatever the codes), 16-byte chunks staged
 // per warp so each store instruction writes 512 contiguous bytes.
 //
-// GEMV: a CTA owns 16 rows, its four warps a quarter of k each. Per 16-weight
-// k tile a lane needs rows g and g + 8 at k = 2t, 2t + 1, 8 + 2t, 9 + 2t (the
-// f16 m16n8k16 A fragment): byte t of two consecutive code words, so each
-// weight is one table lookup of its f16 value (IQ6_K: an f16 pair hi + lo
-// whose sum is the float32 value to 2^-22, through two MMAs). The tokens (up
-// to 16 per pass, f16 as at the reference's call seam) are the N dimension;
-// each sub-block's float32 partial sum is scaled by its dl into the float32
-// accumulators, the four warps' sums meet in shared memory in a fixed order.
+// GEMV: f16 m16n8k16 MMAs whose A fragments (rows g and g + 8, two weights
+// per register) come from lane-replicated value tables in shared memory; the
+// tokens (up to 16 per pass, f16 as at the reference's call seam) are the N
+// dimension; each sub-block's float32 partial sum is scaled by its dl into
+// float32 accumulators, and the warps sharing a row tile's k range add their
+// sums in a fixed order.
+//   IQ4_KS / IQ4_K (dense_gemv_p4_kernel): one f16 pair per code byte from a
+//     table at a fixed shared address, so one byte permute forms each lookup
+//     address; one 16-warp CTA per SM.
+//   IQ5_K / IQ6_K (dense_gemv_kernel): one f16 value per code (IQ6_K: an f16
+//     pair hi + lo whose sum is the float32 value to 2^-22, through two MMAs);
+//     persistent CTAs of 8 warps, two per SM.
 #include "iqk_common.cuh"
 #include "iqk_dense_tables.h"
 
@@ -47,7 +51,6 @@ __constant__ uint32_t c_iq6k[128] = {IQK_IQ6K_BITS};
 template <int M> struct DenseGeo {
     static constexpr int kW = M == IQK_IQ5_K ? 5 : M == IQK_IQ6_K ? 6 : 4;  // code bits
     static constexpr int kEntries = 2 << kW;                                // both alphabets
-    static constexpr int kSub = M == IQK_IQ4_KS ? 32 : 16;                  // weights per scale
 };
 
 struct DenseStreams {
@@ -678,34 +681,48 @@ dense_gemv_p4_kernel(DenseStreams st, int n, int out, const __half *__restrict__
     const int iters = (int)blockIdx.x < groups ? (groups - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
     const int total = iters * kP4Steps;
     auto tile_of = [&](int it) { return ((int)blockIdx.x + it * (int)gridDim.x) * RT + rt; };
-    auto issue = [&](int f, int it, int sidx) {
-        const int tile = tile_of(it);
-        if (tile >= tiles) return;
-        const int64_t r0 = (int64_t)tile * kDenseRows;
-        const int k0 = kbeg + 64 * sidx;
-        const uint32_t slot = ring + (uint32_t)(f % D) * 512u;
-        {
-            const int row = lane >> 1, half = lane & 1;
-            cp_async(slot + (uint32_t)(row * 32 + ((half ^ ((row >> 2) & 1)) * 16)),
-                     st.qs + (r0 + row) * (n / 8) + (k0 >> 3) + 4 * half, 16);
-        }
-        if (sidx == 0 && lane < 16) {
-            const uint32_t b = scb + (uint32_t)(it & 1) * sr.total;
-            const int64_t row = r0 + lane;
-            auto piece = [&](uint32_t dst, const uint8_t *src, int bytes) {
-                for (int o = 0; o < bytes; o += 16)
-                    cp_async(dst + o, src + o, bytes - o >= 16 ? 16 : bytes - o);
-            };
-            piece(b + lane * sr.scl, st.scl + row * (n / 32) + kbeg / 32, sr.scl);
-            if (M == IQK_IQ4_K) {
-                piece(b + sr.off_sch + lane * sr.sch, st.sch + row * (n / 64) + kbeg / 64, sr.sch);
-                piece(b + sr.off_sex + lane * sr.sex, st.sex + row * (n / 128) + kbeg / 128, sr.sex);
-                piece(b + sr.off_dv + lane * sr.dv,
-                      reinterpret_cast<const uint8_t *>(static_cast<const uint16_t *>(st.dv) +
-                                                        row * (n / 256) + kbeg / 256),
-                      sr.dv);
+    // Copy walk: the next step to issue, this lane's 16-byte source and the
+    // ring slot, advanced one step at a time (a tile's first step recomputes
+    // the row pointer and sends the tile's scale bytes to buffer it & 1).
+    const uint32_t dsto = (uint32_t)((lane >> 1) * 32 + (((lane & 1) ^ ((lane >> 3) & 1)) * 16));
+    int iit = 0, isidx = 0, ileft = 0, islot = 0;
+    const uint32_t *iq = st.qs;
+    auto issue_next = [&]() {
+        if (ileft > 0) {
+            --ileft;
+            const int tile = tile_of(iit);
+            if (tile < tiles) {
+                if (isidx == 0) {
+                    const int64_t r0 = (int64_t)tile * kDenseRows;
+                    iq = st.qs + (r0 + (lane >> 1)) * (n / 8) + (kbeg >> 3) + 4 * (lane & 1);
+                    if (lane < 16) {
+                        const uint32_t b = scb + (uint32_t)(iit & 1) * sr.total;
+                        const int64_t row = r0 + lane;
+                        auto piece = [&](uint32_t dst, const uint8_t *src, int bytes) {
+                            for (int o = 0; o < bytes; o += 16)
+                                cp_async(dst + o, src + o, bytes - o >= 16 ? 16 : bytes - o);
+                        };
+                        piece(b + lane * sr.scl, st.scl + row * (n / 32) + kbeg / 32, sr.scl);
+                        if (M == IQK_IQ4_K) {
+                            piece(b + sr.off_sch + lane * sr.sch, st.sch + row * (n / 64) + kbeg / 64, sr.sch);
+                            piece(b + sr.off_sex + lane * sr.sex, st.sex + row * (n / 128) + kbeg / 128, sr.sex);
+                            piece(b + sr.off_dv + lane * sr.dv,
+                                  reinterpret_cast<const uint8_t *>(static_cast<const uint16_t *>(st.dv) +
+                                                                    row * (n / 256) + kbeg / 256),
+                                  sr.dv);
+                        }
+                    }
+                }
+                cp_async(ring + (uint32_t)islot * 512u + dsto, iq, 16);
+                iq += 8;  // the row's next 64 codes
+            }
+            if (++isidx == kP4Steps) {
+                isidx = 0;
+                ++iit;
             }
         }
+        cp_async_commit();
+        islot = islot + 1 == D ? 0 : islot + 1;
     };
 
     for (int t0 = 0; t0 < tokens; t0 += 8 * NT) {
@@ -720,129 +737,152 @@ dense_gemv_p4_kernel(DenseStreams st, int n, int out, const __half *__restrict__
         float acc[NT][4];
 #pragma unroll
         for (int q = 0; q < NT; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
-        int iit = 0, isidx = 0;  // the issue walk
+        iit = 0;
+        isidx = 0;
+        ileft = total;
+        islot = 0;
+        // D - 2 steps in flight ahead of the pair of steps being computed
 #pragma unroll 1
-        for (int f = 0; f < D - 1; ++f) {
-            if (f < total) issue(f, iit, isidx);
-            cp_async_commit();
-            if (++isidx == kP4Steps) {
-                isidx = 0;
-                ++iit;
-            }
-        }
+        for (int f = 0; f < D - 2; ++f) issue_next();
         float drow = 0.f;  // IQ4_KS: the row scale of row lane & 15
-        int it = 0, sidx = -1;  // the compute walk
+        int it = 0, sidx = 0, cslot = 0;
+        const int lr = lane & 15, hs = lane >> 4;  // scale lane: row, sub-block parity
 #pragma unroll 1
-        for (int f = 0; f < total; ++f) {
-            if (++sidx == kP4Steps) {
-                sidx = 0;
-                ++it;
-            }
+        for (int f = 0; f < total; f += 2) {
             const int tile = tile_of(it);
             const bool live = tile < tiles;
             const int64_t r0 = (int64_t)tile * kDenseRows;
+            // the slots of steps f - 2, f - 1 are free again
             __syncwarp();
-            if (f + D - 1 < total) issue(f + D - 1, iit, isidx);
-            cp_async_commit();
-            if (++isidx == kP4Steps) {
-                isidx = 0;
-                ++iit;
-            }
-            cp_async_wait<D - 1>();
+            issue_next();
+            issue_next();
+            cp_async_wait<D - 2>();
             __syncwarp();
             if (live) {
-                const uint32_t slot = ring + (uint32_t)(f % D) * 512u;
                 const uint32_t b = scb + (uint32_t)(it & 1) * sr.total;
-                const int lr = lane & 15, hs = lane >> 4;  // scale lane: row, sub-block parity
-                const int kx = 64 * sidx;
                 if (M == IQK_IQ4_KS) {
                     if (sidx == 0) drow = __ldg(static_cast<const float *>(st.dv) + r0 + lr);
-                    // dl of (row lr, sub-block hs), alphabet bit in the lowest mantissa bit
-                    const uint32_t v = lds8(b + lr * sr.scl + 2 * sidx + hs);
-                    const float dl = __fmul_rn(drow, (float)((int)(v & 254u) - 127));
-                    const float dm = __int_as_float((__float_as_int(dl) & ~1) | (int)(v & 1u));
-                    const uint32_t ra = slot + (uint32_t)g * 32u + 4u * (uint32_t)t;
-                    const uint32_t wa[2] = {lds32(ra + 16u * sw), lds32(ra + 16u * (sw ^ 1u))};
-                    const uint32_t wb[2] = {lds32(ra + 256u + 16u * sw), lds32(ra + 256u + 16u * (sw ^ 1u))};
+                    // scale bytes of sub-blocks 2 sidx .. 2 sidx + 3 (this pair of steps)
+                    const uint32_t v4 = lds32(b + lr * sr.scl + 2 * sidx);
+                    // both steps' code words first: rows g, g + 8, words t and 4 + t
+                    uint32_t wa[2][2], wb[2][2];
 #pragma unroll
-                    for (int s = 0; s < 2; ++s) {
-                        const float dla = __shfl_sync(0xffffffffu, dm, 16 * s + g);
-                        const float dlb = __shfl_sync(0xffffffffu, dm, 16 * s + 8 + g);
-                        const uint32_t la = lbase | (((uint32_t)__float_as_int(dla) & 1u) << 7);
-                        const uint32_t lb = lbase | (((uint32_t)__float_as_int(dlb) & 1u) << 7);
-                        float d[NT][4];
+                    for (int h = 0; h < 2; ++h) {
+                        const uint32_t ra = ring + (uint32_t)cslot * 512u + (uint32_t)g * 32u + 4u * (uint32_t)t;
+                        cslot = cslot + 1 == D ? 0 : cslot + 1;
+                        wa[h][0] = lds32(ra + 16u * sw);
+                        wa[h][1] = lds32(ra + 16u * (sw ^ 1u));
+                        wb[h][0] = lds32(ra + 256u + 16u * sw);
+                        wb[h][1] = lds32(ra + 256u + 16u * (sw ^ 1u));
+                    }
 #pragma unroll
-                        for (int m = 0; m < 2; ++m) {
-                            uint32_t A[4];
-                            A[0] = lds32(pair_addr(wa[s], la, 0x7604u | (2u * m) << 4));
-                            A[1] = lds32(pair_addr(wb[s], lb, 0x7604u | (2u * m) << 4));
-                            A[2] = lds32(pair_addr(wa[s], la, 0x7604u | (2u * m + 1u) << 4));
-                            A[3] = lds32(pair_addr(wb[s], lb, 0x7604u | (2u * m + 1u) << 4));
+                    for (int h = 0; h < 2; ++h) {
+                        const int kx = 64 * (sidx + h);
+                        // dl of (row lr, sub-block hs), alphabet bit in the lowest mantissa bit
+                        const uint32_t v = (v4 >> (8 * (2 * h + hs))) & 255u;
+                        const float dl = __fmul_rn(drow, (float)((int)(v & 254u) - 127));
+                        const float dm = __int_as_float((__float_as_int(dl) & ~1) | (int)(v & 1u));
 #pragma unroll
-                            for (int q = 0; q < NT; ++q) {
-                                const uint2 bx = __ldg(reinterpret_cast<const uint2 *>(xq[q] + kx + 32 * s + 4 * m));
-                                if (m == 0) {
-                                    d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0.f;
-                                    mma_f16(d[q], A, bx.x, bx.y);
-                                } else {
-                                    mma_f16_acc(d[q], A, bx.x, bx.y);
+                        for (int s = 0; s < 2; ++s) {
+                            const float dla = __shfl_sync(0xffffffffu, dm, 16 * s + g);
+                            const float dlb = __shfl_sync(0xffffffffu, dm, 16 * s + 8 + g);
+                            const uint32_t la = lbase | (((uint32_t)__float_as_int(dla) & 1u) << 7);
+                            const uint32_t lb = lbase | (((uint32_t)__float_as_int(dlb) & 1u) << 7);
+                            uint4 bx[NT];
+#pragma unroll
+                            for (int q = 0; q < NT; ++q)
+                                bx[q] = __ldg(reinterpret_cast<const uint4 *>(xq[q] + kx + 32 * s));
+                            float d[NT][4];
+#pragma unroll
+                            for (int m = 0; m < 2; ++m) {
+                                uint32_t A[4];
+                                A[0] = lds32(pair_addr(wa[h][s], la, 0x7604u | (2u * m) << 4));
+                                A[1] = lds32(pair_addr(wb[h][s], lb, 0x7604u | (2u * m) << 4));
+                                A[2] = lds32(pair_addr(wa[h][s], la, 0x7604u | (2u * m + 1u) << 4));
+                                A[3] = lds32(pair_addr(wb[h][s], lb, 0x7604u | (2u * m + 1u) << 4));
+#pragma unroll
+                                for (int q = 0; q < NT; ++q) {
+                                    if (m == 0) {
+                                        d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0.f;
+                                        mma_f16(d[q], A, bx[q].x, bx[q].y);
+                                    } else {
+                                        mma_f16_acc(d[q], A, bx[q].z, bx[q].w);
+                                    }
                                 }
                             }
-                        }
 #pragma unroll
-                        for (int q = 0; q < NT; ++q) {
-                            acc[q][0] = fmaf(dla, d[q][0], acc[q][0]);
-                            acc[q][1] = fmaf(dla, d[q][1], acc[q][1]);
-                            acc[q][2] = fmaf(dlb, d[q][2], acc[q][2]);
-                            acc[q][3] = fmaf(dlb, d[q][3], acc[q][3]);
+                            for (int q = 0; q < NT; ++q) {
+                                acc[q][0] = fmaf(dla, d[q][0], acc[q][0]);
+                                acc[q][1] = fmaf(dla, d[q][1], acc[q][1]);
+                                acc[q][2] = fmaf(dlb, d[q][2], acc[q][2]);
+                                acc[q][3] = fmaf(dlb, d[q][3], acc[q][3]);
+                            }
                         }
                     }
                 } else {
-                    // dl of (row lr, sub-blocks hs and 2 + hs of the step)
-                    const uint32_t lo2 = lds16(b + lr * sr.scl + 2 * sidx);  // sub-blocks 4sidx .. +3
-                    const uint32_t hi = lds8(b + sr.off_sch + lr * sr.sch + sidx);
-                    const uint32_t ex = lds8(b + sr.off_sex + lr * sr.sex + (sidx >> 1)) >> (4 * (sidx & 1));
+                    // scale parts of sub-blocks 4 sidx .. 4 sidx + 7 (this pair of steps)
+                    const uint32_t lo4 = lds32(b + lr * sr.scl + 2 * sidx);
+                    const uint32_t hi2 = lds16(b + sr.off_sch + lr * sr.sch + sidx);
+                    const uint32_t ex = lds8(b + sr.off_sex + lr * sr.sex + (sidx >> 1));
                     const float d0 = __half2float(__ushort_as_half(
                         (unsigned short)lds16(b + sr.off_dv + lr * sr.dv + 2 * (sidx >> 2))));
-                    float dm[2];
+                    // both steps' code words first: word 2s + (t >> 1) of rows g, g + 8
+                    uint32_t wa[2][4], wb[2][4];
 #pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const int ls = 2 * u + hs;  // sub-block of the step
-                        const int idx = (int)(((lo2 >> (4 * ls)) & 15u) | (((hi >> (2 * ls)) & 3u) << 4)) - 32;
-                        const float dl = __fmul_rn(d0, (float)idx);
-                        dm[u] = __int_as_float((__float_as_int(dl) & ~1) | (int)((ex >> ls) & 1u));
+                    for (int h = 0; h < 2; ++h) {
+                        const uint32_t ra = ring + (uint32_t)cslot * 512u + (uint32_t)g * 32u + 4u * (uint32_t)(t >> 1);
+                        cslot = cslot + 1 == D ? 0 : cslot + 1;
+#pragma unroll
+                        for (int s = 0; s < 4; ++s) {
+                            const uint32_t wo = 16u * ((uint32_t)(s >> 1) ^ sw) + 8u * (uint32_t)(s & 1);
+                            wa[h][s] = lds32(ra + wo);
+                            wb[h][s] = lds32(ra + 256u + wo);
+                        }
                     }
-                    const uint32_t ra = slot + (uint32_t)g * 32u + 4u * (uint32_t)(t >> 1);
-                    const uint32_t sel0 = 0x7604u | ((uint32_t)(2 * (t & 1)) << 4);
-                    const uint32_t sel1 = sel0 + 0x10u;
 #pragma unroll
-                    for (int s = 0; s < 4; ++s) {
-                        // word 2s + (t >> 1) of rows g, g + 8
-                        const uint32_t wo = 16u * ((uint32_t)(s >> 1) ^ sw) + 8u * (uint32_t)(s & 1);
-                        const uint32_t wa = lds32(ra + wo), wb = lds32(ra + 256u + wo);
-                        const float dla = __shfl_sync(0xffffffffu, dm[s >> 1], 16 * (s & 1) + g);
-                        const float dlb = __shfl_sync(0xffffffffu, dm[s >> 1], 16 * (s & 1) + 8 + g);
-                        const uint32_t la = lbase | (((uint32_t)__float_as_int(dla) & 1u) << 7);
-                        const uint32_t lb = lbase | (((uint32_t)__float_as_int(dlb) & 1u) << 7);
-                        uint32_t A[4];
-                        A[0] = lds32(pair_addr(wa, la, sel0));
-                        A[1] = lds32(pair_addr(wb, lb, sel0));
-                        A[2] = lds32(pair_addr(wa, la, sel1));
-                        A[3] = lds32(pair_addr(wb, lb, sel1));
+                    for (int h = 0; h < 2; ++h) {
+                        const int kx = 64 * (sidx + h);
+                        // dl of (row lr, sub-blocks hs and 2 + hs of step h)
+                        float dm[2];
 #pragma unroll
-                        for (int q = 0; q < NT; ++q) {
-                            const uint2 bx = __ldg(reinterpret_cast<const uint2 *>(xq[q] + kx + 16 * s));
-                            float d[4] = {0.f, 0.f, 0.f, 0.f};
-                            mma_f16(d, A, bx.x, bx.y);
-                            acc[q][0] = fmaf(dla, d[0], acc[q][0]);
-                            acc[q][1] = fmaf(dla, d[1], acc[q][1]);
-                            acc[q][2] = fmaf(dlb, d[2], acc[q][2]);
-                            acc[q][3] = fmaf(dlb, d[3], acc[q][3]);
+                        for (int u = 0; u < 2; ++u) {
+                            const int ls = 4 * h + 2 * u + hs;  // sub-block of the pair of steps
+                            const int idx = (int)(((lo4 >> (4 * ls)) & 15u) | (((hi2 >> (2 * ls)) & 3u) << 4)) - 32;
+                            const float dl = __fmul_rn(d0, (float)idx);
+                            dm[u] = __int_as_float((__float_as_int(dl) & ~1) | (int)((ex >> ls) & 1u));
+                        }
+                        const uint32_t sel0 = 0x7604u | ((uint32_t)(2 * (t & 1)) << 4);
+                        const uint32_t sel1 = sel0 + 0x10u;
+#pragma unroll
+                        for (int s = 0; s < 4; ++s) {
+                            const float dla = __shfl_sync(0xffffffffu, dm[s >> 1], 16 * (s & 1) + g);
+                            const float dlb = __shfl_sync(0xffffffffu, dm[s >> 1], 16 * (s & 1) + 8 + g);
+                            const uint32_t la = lbase | (((uint32_t)__float_as_int(dla) & 1u) << 7);
+                            const uint32_t lb = lbase | (((uint32_t)__float_as_int(dlb) & 1u) << 7);
+                            uint32_t A[4];
+                            A[0] = lds32(pair_addr(wa[h][s], la, sel0));
+                            A[1] = lds32(pair_addr(wb[h][s], lb, sel0));
+                            A[2] = lds32(pair_addr(wa[h][s], la, sel1));
+                            A[3] = lds32(pair_addr(wb[h][s], lb, sel1));
+#pragma unroll
+                            for (int q = 0; q < NT; ++q) {
+                                const uint2 bx = __ldg(reinterpret_cast<const uint2 *>(xq[q] + kx + 16 * s));
+                                float d[4] = {0.f, 0.f, 0.f, 0.f};
+                                mma_f16(d, A, bx.x, bx.y);
+                                acc[q][0] = fmaf(dla, d[0], acc[q][0]);
+                                acc[q][1] = fmaf(dla, d[1], acc[q][1]);
+                                acc[q][2] = fmaf(dlb, d[2], acc[q][2]);
+                                acc[q][3] = fmaf(dlb, d[3], acc[q][3]);
+                            }
                         }
                     }
                 }
+            } else {
+                cslot = cslot + 2 >= D ? cslot + 2 - D : cslot + 2;
             }
-            if (sidx + 1 < kP4Steps) continue;
+            sidx += 2;
+            if (sidx < kP4Steps) continue;
+            sidx = 0;
             // end of the iteration's row tiles: each tile's KW k parts meet in
             // its first warp, added in k order (reduction area by iteration
             // parity, so one barrier per iteration suffices)
@@ -886,6 +926,7 @@ dense_gemv_p4_kernel(DenseStreams st, int n, int out, const __half *__restrict__
             }
 #pragma unroll
             for (int q = 0; q < NT; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
+            ++it;
         }
         cp_async_wait<0>();
         __syncthreads();
