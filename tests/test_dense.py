@@ -243,6 +243,37 @@ def test_linear_routes_agree(cuda, member):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("member", MEMBERS)
+@pytest.mark.parametrize("n", (1024, 8192))
+@pytest.mark.parametrize("tokens", (1, 9))
+def test_gemv_over_several_waves_of_row_tiles(cuda, member, n, tokens):
+    """Heights of two and a bit CTA waves (every CTA walks several row-tile
+    groups, the last one partial), every output row checked: the reference is
+    a float64 matmul of the f32 dequantization, itself bit-exact to the
+    oracle (test_dequant_is_bit_identical)."""
+    from mlx_iqk_b200.profile_cases import random_dense_streams
+    sms = torch.cuda.get_device_properties(cuda).multi_processor_count
+    # rows one CTA iteration covers: IQ4 members 16 warps / (n / 1024) k parts
+    # of 16-row tiles; IQ5_K / IQ6_K 8 warps / (4 or 2) k parts, two CTAs per SM
+    if member in ("iq4_ks", "iq4_k"):
+        rows_per_group, ctas = 16 * (16 // (n // 1024)), sms
+    else:
+        rows_per_group, ctas = 16 * (8 // (4 if n >= 2048 else 2)), 2 * sms
+    out = rows_per_group * (2 * ctas + 1) + 48
+    gen = torch.Generator(device=cuda).manual_seed(n + tokens)
+    st = dn.check_dense_streams(member, random_dense_streams(member, out, n, cuda, gen), out, n)
+    w = torch.empty((out, n), dtype=torch.float32, device=cuda)
+    K.dense_dequant(member, st, out, n, 0, out, w)
+    x = torch.randn((tokens, n), generator=gen, device=cuda).half()
+    y = torch.empty((tokens, out), dtype=torch.float32, device=cuda)
+    K.dense_gemv(member, x, st, out, n, y)
+    want = x.double() @ w.double().t()
+    rel = float((y.double() - want).abs().max()) / float(want.abs().max())
+    assert rel < 1e-4, rel
+    del w
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("member", ("iq4_ks", "iq6_k"))
 def test_gemv_at_the_lm_head_shape(cuda, member):
     """One token through a 129280 x 4096 head (random streams made on the
