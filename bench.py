@@ -950,7 +950,8 @@ def run_b200(args) -> None:
 def run_prefill(args, torch, K, dev, world, rank, tm, peaks) -> dict | None:
     """Config 5: the expert-parallel layer at every N (experts E/N per rank,
     the 2048 tokens sharded N ways: strong scaling) with its output check,
-    and at N=1 the direct one-GPU layer and each grouped GEMM alone."""
+    and at N=1 the direct one-GPU layer and each grouped GEMM alone (IQ2_KS at
+    the gate shape, IQ2_K at the down shape, IQ1_S_R4 at the gate shape)."""
     if args.no_prefill:
         return None
     full = config5_modules(torch, dev)
@@ -990,6 +991,19 @@ def run_prefill(args, torch, K, dev, world, rank, tm, peaks) -> dict | None:
     gk_d.replay()
     g_ms = tm.timed(gk_g) / reps
     d_ms = tm.timed(gk_d) / reps
+    # IQ1_S_R4 experts of the gate shape over the same routed pairs and the
+    # same prepared activations (the grouped workspace is member-independent)
+    from mlx_iqk_b200 import IqkSwitchLinear
+    from mlx_iqk_b200.profile_cases import random_streams
+    iq1 = IqkSwitchLinear("iq1_s_r4", E, *GATE_UP, device=dev)
+    iq1.load_streams(random_streams("iq1_s_r4", E, *GATE_UP, dev,
+                                    torch.Generator(device=dev).manual_seed(5006)))
+    gk_1 = tm.graph(lambda: [K.grouped_run("iq1_s_r4", iq1._streams(), E, GATE_UP[0],
+                                           GATE_UP[1], pl.pairs, pl.yg, pl.ws_gu)
+                             for _ in range(reps)])
+    pl.gate_up()
+    gk_1.replay()
+    i_ms = tm.timed(gk_1) / reps
     tf_peak = peaks.get("bf16_tflops") or 1590.0
     g_fl = 2.0 * pl.pairs * GATE_UP[0] * GATE_UP[1]
     d_fl = 2.0 * pl.pairs * DOWN[0] * DOWN[1]
@@ -1007,10 +1021,13 @@ def run_prefill(args, torch, K, dev, world, rank, tm, peaks) -> dict | None:
                  "bound": "tensor", "peak_tflops": tf_peak,
                  "peak_source": "measured" if peaks.get("bf16_tflops") else "fallback",
                  "frac_gate_or_up": round(g_fl / (g_ms * 1e-3) / 1e12 / tf_peak, 4),
-                 "frac_down": round(d_fl / (d_ms * 1e-3) / 1e12 / tf_peak, 4)},
+                 "frac_down": round(d_fl / (d_ms * 1e-3) / 1e12 / tf_peak, 4),
+                 "iq1_s_r4_gate_shape_us": round(i_ms * 1e3, 2),
+                 "iq1_s_r4_gate_shape_tflops": round(g_fl / (i_ms * 1e-3) / 1e12, 1),
+                 "frac_iq1_s_r4": round(g_fl / (i_ms * 1e-3) / 1e12 / tf_peak, 4)},
         "parallelism": "one GPU",
     }
-    del gpw, gpt, gk_g, gk_d, pl, full
+    del gpw, gpt, gk_g, gk_d, gk_1, iq1, pl, full
     torch.cuda.empty_cache()
     return out
 
