@@ -1,10 +1,11 @@
-"""Routed-expert benchmark (BASELINE config 2 headline, configs 1/3/4/5 as legs).
+"""Routed-expert benchmark: the routed decode headline, the other configurations as legs.
 
 Headline step = one MoE layer's routed projections for one decode step at each
-batch size B = 1, 4, 8 (BASELINE configs[1]): IQ2_KS gate and up
+batch size B = 1, 4, 8: IQ2_KS gate and up
 ([2048, 4096] per expert) and down ([4096, 2048] per expert), 256 experts,
 top-6, through the fused dequant+GEMV kernels of libiqk_b200.so. Gate and up
-share one preparation (iqk_gemv_prepare); down gets its own.
+run on two streams, each prepared into its own workspace (the decode kernels
+claim items from a counter there); down follows with its own preparation.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
@@ -493,7 +494,7 @@ def prefill_inputs(torch, dev, seed: int = 2024):
 
 
 class PrefillLayer:
-    """BASELINE config 5 on one GPU: one MoE layer (gate/up IQ2_KS, down
+    """Config 5 (prefill) on one GPU: one MoE layer (gate/up IQ2_KS, down
     IQ2_K) over all of ``mods``' experts, tokens routed top-6,
     sorted_indices=True, through the grouped GEMM. Step = prepare(x) + gate +
     up + SiLU(gate)*up*router weight (one pass over the routed pairs) +
@@ -765,7 +766,7 @@ def dequant_leg(tm, K, mod, hbm: float, experts: int = 32, reps: int = 4) -> dic
 
 
 def dense_leg(tm, K, dev, gen, hbm: float) -> dict:
-    """The dense members (the survey's next row): the decode GEMV at the
+    """The dense members: the decode GEMV at the
     lm_head shape [129280, 4096] (1 and 8 tokens; the matrix is 280-440 MB,
     larger than L2, so every call streams it from HBM) and the fp16
     dequantization of 16384 of its rows, per member."""
