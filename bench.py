@@ -807,7 +807,7 @@ def dense_leg(tm, K, dev, gen, hbm: float) -> dict:
 
 
 def config1_leg(tm, dev, gen) -> dict:
-    """BASELINE config 1's call (one IQ2_KS [2048, 4096] expert, fp32 x, one
+    """Config 1's call (one IQ2_KS [2048, 4096] expert, fp32 x, one
     token) through the module; 128 copies of the expert rotate so that no
     call is served from L2."""
     torch = tm.torch

@@ -83,7 +83,7 @@ def main() -> None:
         want = codec.dequantize(member, wire, 256)
         out[f"exhaustive/{member}/wire"] = wire
         out[f"exhaustive/{member}/sha256"] = np.array(digest(want))
-    # one IQ2_KS expert [2048, 4096], N(0, 0.02^2) rows,
+    # config 1: one IQ2_KS expert [2048, 4096], N(0, 0.02^2) rows,
     # U(0.1, 1) imatrix, codec-quantized. The first 64 rows are stored; the
     # whole tensor is pinned by digest (regenerated where the codec is built).
     rng = np.random.default_rng(wirepack.seed_for("config1", "iq2_ks"))

@@ -147,7 +147,7 @@ def test_gemv_reads_the_expert_the_index_names(cuda, member):
 
 
 def test_config1_expert_gemv(cuda, golden):
-    """BASELINE config 1 head rows: the reference-quantized expert, fp32 x."""
+    """Config 1 head rows: the reference-quantized expert, fp32 x."""
     wire = golden["config1/wire_head"]  # 64 rows of the 2048-row expert
     mod, ref, _ = make_module("iq2_ks", 4096, seed=0, experts=1, out_features=64, wire=wire)
     x = golden["config1/x"]
@@ -268,7 +268,7 @@ def test_full_geometry_both_item_shapes(cuda, member, geom, tokens):
 
 
 def test_full_geometry_decode_sampled(cuda):
-    """BASELINE config 2 geometry (E=256, gate 2048x4096), B=8, checked on the
+    """Config 2 geometry (E=256, gate 2048x4096), B=8, checked on the
     experts actually selected (size-independent sampling)."""
     member, E, out, n = "iq2_ks", 256, 2048, 4096
     gen = torch.Generator(device=cuda).manual_seed(7)
