@@ -323,8 +323,11 @@ constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // bounded mbarrier 
 // from one 32-bit code word per lane and row.
 template <int MEMBER> struct Geo {
     // Four-stage rings; three CTAs per SM (two for IQ2_K, whose scale
-    // streams and metadata are twice as large).
-    static constexpr int kStages = 4;
+    // streams and metadata are twice as large). IQ1_S_R4, whose scale slots
+    // are the largest and whose grid table also sits in shared memory, takes
+    // three stages and a 32-entry tile cache, so that three CTAs fit.
+    static constexpr int kStages = MEMBER == IQK_IQ1_S_R4 ? 3 : 4;
+    static constexpr int kTileCache = MEMBER == IQK_IQ1_S_R4 ? 32 : kMaxTiles;
     static constexpr int kMinBlocks = MEMBER == IQK_IQ2_K ? 2 : 3;
     static constexpr int kRowChunk = MEMBER == IQK_IQ1_S_R4 ? 64 : 128;   // qs bytes per round
     static constexpr int kWBox = 16 * kRowChunk;                         // one warp's TMA box
@@ -385,7 +388,7 @@ __host__ __device__ constexpr int gemv_smem_bytes() {
     using SH = Shape<MEMBER, NARROW, GLU>;
     return 1024 /* alignment slack */ + SH::kStages * stage_bytes<MEMBER, SH::KQ>() +
            2 * SH::kProj * sslot_bytes<MEMBER, N, SH::kRows>() + 2 * kConsumers * G::kMetaBytes +
-           kMaxTiles * (int)sizeof(TileRef) + (MEMBER == IQK_IQ1_S_R4 ? 8192 : 0) +
+           G::kTileCache * (int)sizeof(TileRef) + (MEMBER == IQK_IQ1_S_R4 ? 4096 : 0) +
            2 * SH::kStages * 8 + 8 * 8 + 16 +
            kPairsPerRound * 192 + SH::kRedBytes;
 }
@@ -554,12 +557,9 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
     char *sslots = stages + kStages * STB;  // two item scale slots
     char *metas = sslots + 2 * SH::kProj * SSB;  // slot o: projection q at (o * kProj + q) * SSB
     TileRef *tcache = reinterpret_cast<TileRef *>(metas + 2 * kConsumers * G::kMetaBytes);
-    char *tail = reinterpret_cast<char *>(tcache + kMaxTiles);
-    // IQ1_S_R4: the ternary grid as byte-permute selectors, entry i holding
-    // grid word i's even codes (low half) and odd codes (high half), one per
-    // nibble's low two bits -- each half selects four codes' values
-    uint32_t *gridEO = reinterpret_cast<uint32_t *>(tail);
-    uint64_t *full = reinterpret_cast<uint64_t *>(tail + (MEMBER == IQK_IQ1_S_R4 ? 8192 : 0));
+    char *tail = reinterpret_cast<char *>(tcache + G::kTileCache);
+    uint16_t *grid = reinterpret_cast<uint16_t *>(tail);   // IQ1_S_R4
+    uint64_t *full = reinterpret_cast<uint64_t *>(tail + (MEMBER == IQK_IQ1_S_R4 ? 4096 : 0));
     uint64_t *empty = full + kStages;
     uint64_t *sfull = empty + kStages;  // [2] item scale slots
     uint64_t *sempty = sfull + 2;       // [2]
@@ -578,10 +578,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
 
     // Shared-memory set-up first: it overlaps the previous kernel's drain.
     if (MEMBER == IQK_IQ1_S_R4)
-        for (int i = tid; i < 2048; i += blockDim.x) {
-            const uint32_t gw = g_iq1s_grid[i];
-            gridEO[i] = (gw & 0x3333u) | (((gw >> 2) & 0x3333u) << 16);
-        }
+        for (int i = tid; i < 2048; i += blockDim.x) grid[i] = g_iq1s_grid[i];
     for (int i = tid; i < kPairsPerRound * 192 / 4; i += blockDim.x)
         reinterpret_cast<uint32_t *>(zeros)[i] = 0u;
     if (tid == 0) {
@@ -637,7 +634,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
     const int i1 = dyn ? items : (int)((int64_t)items * (blockIdx.x + 1) / gridDim.x);
     if (i0 >= i1) return;  // uniform over the CTA (a dynamic launch has items > 0)
     const int t0 = i0 / rblocks, t1 = (i1 - 1) / rblocks;
-    const bool cached = !dyn && t1 - t0 < kMaxTiles;
+    const bool cached = !dyn && t1 - t0 < G::kTileCache;
     auto load_tile = [&](int t) -> TileRef {
         TileRef r = tlist[t];
         r.sh0 = xscale[r.tok0];
@@ -939,7 +936,7 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
                         w0 = ld_s32(wo);
                         w1 = ld_s32(wo + 512);
                         // the grid gathers are addressing, not decode: kept
-                        w0 += 131u * gridEO[w0 & 0x7ffu] + 137u * gridEO[(w1 >> 8) & 0x7ffu];
+                        w0 += 131u * grid[w0 & 0x7ffu] + 137u * grid[(w1 >> 8) & 0x7ffu];
                     } else {
                         const uint32_t wo = wl ^ (uint32_t)(pr << 4);
                         w0 = ld_s32(wo);
@@ -1043,21 +1040,21 @@ gemv_kernel(GemvArgs a, const __grid_constant__ CUtensorMap qs_map,
                         // both grid indices of a row (octets 2h, 2h+1: qs byte | high part << 8)
                         // from one byte permute
                         const uint32_t wig = prmt(qg, m.x, isel), wih = prmt(qg8, m.y, isel);
-                        const uint32_t ia = wig & 0xffffu, ib = wig >> 16;
-                        const uint32_t ja = wih & 0xffffu, jb = wih >> 16;
-                        const uint32_t ea = gridEO[ia], eb = gridEO[ib];
-                        const uint32_t fa = gridEO[ja], fb = gridEO[jb];
-                        // octet a's codes (rows g, g + 8), then octet b's
+                        const uint32_t ga = grid[wig & 0xffffu], gb = grid[wig >> 16];
+                        const uint32_t ha = grid[wih & 0xffffu], hb = grid[wih >> 16];
+                        const uint32_t vg = prmt(ga, gb, 0x5410u), vh = prmt(ha, hb, 0x5410u);
+                        const uint32_t s0g = vg & 0x33333333u, s1g = shr2(vg, m30) & 0x33333333u;
+                        const uint32_t s0h = vh & 0x33333333u, s1h = shr2(vh, m30) & 0x33333333u;
                         int32_t d[4];
-                        A[0] = prmt(kTernTab, 0u, ea);
-                        A[1] = prmt(kTernTab, 0u, fa);
-                        A[2] = prmt(kTernTab, 0u, shr16(ea));
-                        A[3] = prmt(kTernTab, 0u, shr16(fa));
+                        A[0] = prmt(kTernTab, 0u, s0g);
+                        A[1] = prmt(kTernTab, 0u, s0h);
+                        A[2] = prmt(kTernTab, 0u, s1g);
+                        A[3] = prmt(kTernTab, 0u, s1h);
                         mma_s8(d, A, bv.x, bv.y);
-                        A[0] = prmt(kTernTab, 0u, eb);
-                        A[1] = prmt(kTernTab, 0u, fb);
-                        A[2] = prmt(kTernTab, 0u, shr16(eb));
-                        A[3] = prmt(kTernTab, 0u, shr16(fb));
+                        A[0] = prmt(kTernTab, 0u, shr16(s0g));
+                        A[1] = prmt(kTernTab, 0u, shr16(s0h));
+                        A[2] = prmt(kTernTab, 0u, shr16(s1g));
+                        A[3] = prmt(kTernTab, 0u, shr16(s1h));
                         mma_s8_acc(d, A, bv.z, bv.w);
                         // block sums of this lane's two C columns (block 2*pr+side,
                         // planes 2*(tig&1) and +1; plane 3 reads the stored zero)
