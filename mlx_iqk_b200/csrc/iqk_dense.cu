@@ -622,6 +622,11 @@ __device__ __forceinline__ float4 lds128f(uint32_t a) {
                  : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
     return v;
 }
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
 __device__ __forceinline__ void bar_tile(int id, int threads) {
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory");
 }
@@ -630,7 +635,9 @@ __device__ __forceinline__ uint32_t pair_addr(uint32_t w, uint32_t base, uint32_
     return __byte_perm(w, base, sel);
 }
 
-template <int M, int NT, int D>
+// XS: the pass's activation rows are staged in shared memory after the tail
+// (when they fit), so the fragment loads are shared-memory broadcasts.
+template <int M, int NT, int D, bool XS>
 __global__ void __launch_bounds__(kP4Warps * 32, 1)
 dense_gemv_p4_kernel(DenseStreams st, int n, int out, const __half *__restrict__ x, int tokens,
                      void *__restrict__ y, int y_dtype) {
@@ -650,7 +657,8 @@ dense_gemv_p4_kernel(DenseStreams st, int n, int out, const __half *__restrict__
     // the rings must end below the table and the tail lie inside the
     // allocation (the host sizes it so); otherwise the outputs are NaN
     if (ring0 + (uint32_t)(kP4Warps * D * 512) > kPairTab ||
-        s0 + dyn < tail + (uint32_t)p4_tail_bytes<M, NT>(n)) {
+        s0 + dyn < tail + (uint32_t)p4_tail_bytes<M, NT>(n) +
+                       (XS ? (uint32_t)(min(tokens, 8 * NT) * n * 2) : 0u)) {
         const int64_t total = (int64_t)tokens * out;
         for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
              i += (int64_t)gridDim.x * blockDim.x) {
@@ -725,14 +733,29 @@ dense_gemv_p4_kernel(DenseStreams st, int n, int out, const __half *__restrict__
         islot = islot + 1 == D ? 0 : islot + 1;
     };
 
+    const uint32_t xsm = tail + (uint32_t)p4_tail_bytes<M, NT>(n);  // XS: staged rows
     for (int t0 = 0; t0 < tokens; t0 += 8 * NT) {
+        if (XS) {
+            // this pass's rows t0 .. t0 + rows - 1, contiguous as in x
+            const int rows = min(8 * NT, tokens - t0);
+            const uint4 *src = reinterpret_cast<const uint4 *>(x + (int64_t)t0 * n);
+            for (int i = threadIdx.x; i < rows * n / 8; i += kP4Warps * 32) {
+                const uint4 v = __ldg(src + i);
+                asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(xsm + 16u * (uint32_t)i),
+                             "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w));
+            }
+            __syncthreads();
+        }
         // B column g of token tile q: token t0 + 8q + g (clamped: columns
         // past the last token are computed and never stored)
         const __half *xq[NT];
+        uint32_t xs[NT];
 #pragma unroll
         for (int q = 0; q < NT; ++q) {
             const int tk = min(t0 + 8 * q + g, tokens - 1);
-            xq[q] = x + (int64_t)tk * n + kbeg + (M == IQK_IQ4_KS ? 8 * t : 4 * t);
+            const int kk = kbeg + (M == IQK_IQ4_KS ? 8 * t : 4 * t);
+            xq[q] = x + (int64_t)tk * n + kk;
+            xs[q] = xsm + 2u * (uint32_t)((tk - t0) * n + kk);
         }
         float acc[NT][4];
 #pragma unroll
@@ -791,7 +814,8 @@ dense_gemv_p4_kernel(DenseStreams st, int n, int out, const __half *__restrict__
                             uint4 bx[NT];
 #pragma unroll
                             for (int q = 0; q < NT; ++q)
-                                bx[q] = __ldg(reinterpret_cast<const uint4 *>(xq[q] + kx + 32 * s));
+                                bx[q] = XS ? lds128(xs[q] + 2u * (uint32_t)(kx + 32 * s))
+                                           : __ldg(reinterpret_cast<const uint4 *>(xq[q] + kx + 32 * s));
                             float d[NT][4];
 #pragma unroll
                             for (int m = 0; m < 2; ++m) {
@@ -866,7 +890,8 @@ dense_gemv_p4_kernel(DenseStreams st, int n, int out, const __half *__restrict__
                             A[3] = lds32(pair_addr(wb[h][s], lb, sel1));
 #pragma unroll
                             for (int q = 0; q < NT; ++q) {
-                                const uint2 bx = __ldg(reinterpret_cast<const uint2 *>(xq[q] + kx + 16 * s));
+                                const uint2 bx = XS ? lds64(xs[q] + 2u * (uint32_t)(kx + 16 * s))
+                                                    : __ldg(reinterpret_cast<const uint2 *>(xq[q] + kx + 16 * s));
                                 float d[4] = {0.f, 0.f, 0.f, 0.f};
                                 mma_f16(d, A, bx.x, bx.y);
                                 acc[q][0] = fmaf(dla, d[0], acc[q][0]);
@@ -997,26 +1022,39 @@ cudaError_t p4_launch(const DenseStreams &st, int n, int out, const __half *xh, 
     constexpr int D = 7;  // ring slots a warp: 16 x 7 x 512 B end below the table
     // per device: the shared memory reserved below a CTA's own (+1; 0 = not
     // yet queried), which places the dynamic allocation in the window
-    static int reserved[64] = {};
+    static int reserved[64] = {}, optin[64] = {};
     int &rs = reserved[dev & 63];
     if (rs == 0) {
-        int v = 0;
+        int v = 0, o = 0;
         cudaError_t e = cudaDeviceGetAttribute(&v, cudaDevAttrReservedSharedMemoryPerBlock, dev);
         if (e != cudaSuccess) return e;
-        e = cudaFuncSetAttribute(dense_gemv_p4_kernel<M, NT, D>,
+        e = cudaDeviceGetAttribute(&o, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(dense_gemv_p4_kernel<M, NT, D, false>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)(kPairTab + 65536u) + p4_tail_bytes<M, NT>(8192) - v);
         if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(dense_gemv_p4_kernel<M, NT, D, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, o);
+        if (e != cudaSuccess) return e;
+        optin[dev & 63] = o;
         rs = v + 1;
     }
     const int smem = (int)(kPairTab + 65536u) + p4_tail_bytes<M, NT>(n) - (rs - 1);
+    // stage the activation rows when they fit in the opt-in shared memory
+    const int xs_bytes = (tokens < 8 * NT ? tokens : 8 * NT) * n * 2;
+    const bool xs = smem + xs_bytes <= optin[dev & 63];
     int sms = 148;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
     const int RT = kP4Warps / (n >> 10);
     const int groups = (out / kDenseRows + RT - 1) / RT;
     const int grid = groups < sms ? groups : sms;
-    dense_gemv_p4_kernel<M, NT, D><<<grid, kP4Warps * 32, smem, stream>>>(st, n, out, xh, tokens, y,
-                                                                          y_dtype);
+    if (xs)
+        dense_gemv_p4_kernel<M, NT, D, true><<<grid, kP4Warps * 32, smem + xs_bytes, stream>>>(
+            st, n, out, xh, tokens, y, y_dtype);
+    else
+        dense_gemv_p4_kernel<M, NT, D, false><<<grid, kP4Warps * 32, smem, stream>>>(
+            st, n, out, xh, tokens, y, y_dtype);
     return cudaGetLastError();
 }
 
